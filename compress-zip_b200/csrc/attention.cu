@@ -1,0 +1,202 @@
+// attention.cu -- exact causal integer attention for whole chunks.
+//
+// Reference: gqa_attention_mqa_i8, rust/src/attention.rs:162-289, called for
+// positions 0..n-1 of a chunk (rust/src/main.rs:212-217).  For query position p
+// and head h the reference walks keys t = 0..p *in order* with an online softmax:
+// when a score beats the running max m, the running sums are rescaled by
+// exp(m - score) with rounding, so the result depends on where the prefix-max
+// "records" fall.  Between records the weights w_t = exp(score_t - m) and the
+// sums s += w, vacc += w * v are plain integer additions (u64 and wrapping i32),
+// hence associative.  This kernel therefore:
+//   * scores 32 keys at a time, one key per lane;
+//   * finds the prefix max of the block with a warp scan (records = lanes whose
+//     score beats the max of everything before them);
+//   * adds record-free blocks in any order, and replays blocks that contain a
+//     record key by key, applying each rescale where the reference does.
+// Output: clamp(round_half_even(vacc / s)) per dimension (attention.rs:279-284).
+//
+// One CTA per chunk.  The chunk's rotated keys and values (kv rows, 128 B per
+// position) are staged in shared memory when they fit.  Warps take (position,
+// head) tasks longest-first from a shared counter.  Lane l owns output
+// dimensions 2l and 2l+1.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace czg {
+namespace {
+
+constexpr int ATT_THREADS = 512;
+constexpr int ATT_WARPS = ATT_THREADS / 32;
+constexpr int SMEM_KV_MAX = 1024;   // positions staged in shared memory
+
+__device__ __forceinline__ int score_of(const uint32_t (&q)[16], const int8_t *krow, int mult) {
+    const uint4 *k4 = reinterpret_cast<const uint4 *>(krow);
+    int dot = 0;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        uint4 kw = k4[i];
+        dot = __dp4a((int)q[4 * i + 0], (int)kw.x, dot);
+        dot = __dp4a((int)q[4 * i + 1], (int)kw.y, dot);
+        dot = __dp4a((int)q[4 * i + 2], (int)kw.z, dot);
+        dot = __dp4a((int)q[4 * i + 3], (int)kw.w, dot);
+    }
+    // attention.rs:236-245: round(dot >> 2), times score_mult (i64), round(>> 15)
+    return sra_rne64_to32((long long)sra_rne32(dot, 2) * (long long)mult, 15);
+}
+
+template <bool KV_SMEM>
+__global__ void __launch_bounds__(ATT_THREADS, 1)
+k_attention(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restrict__ kv_g,
+            const int *__restrict__ chunk_row0, const int *__restrict__ chunk_len, int n_heads,
+            const int32_t *__restrict__ score_mult, const int8_t *__restrict__ sink_key,
+            const int16_t *__restrict__ rope_cos, const int16_t *__restrict__ rope_sin,
+            const uint16_t *__restrict__ lut_g, int8_t *__restrict__ out, int ldo) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ uint16_t lut[256];
+    __shared__ int task_ctr;
+    __shared__ __align__(16) int8_t qbuf[ATT_WARPS][64];
+
+    const int c = blockIdx.x;
+    const int r0 = chunk_row0[c], n = chunk_len[c];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t coef = 378194u;   // ATTN_COEF_Q24, attention.rs:14-19
+    for (int i = tid; i < 256; i += ATT_THREADS) lut[i] = lut_g[i];
+    if (tid == 0) task_ctr = 0;
+
+    const int8_t *kv;
+    if (KV_SMEM) {
+        uint4 *dst = reinterpret_cast<uint4 *>(smem);
+        const uint4 *src = reinterpret_cast<const uint4 *>(kv_g + (size_t)r0 * 128);
+        for (int i = tid; i < n * 8; i += ATT_THREADS) dst[i] = src[i];
+        kv = reinterpret_cast<const int8_t *>(smem);
+    } else {
+        kv = kv_g + (size_t)r0 * 128;
+    }
+    __syncthreads();
+
+    const int n_tasks = n * n_heads;
+    for (;;) {
+        int task = 0;
+        if (lane == 0) task = atomicAdd(&task_ctr, 1);
+        task = __shfl_sync(0xffffffffu, task, 0);
+        if (task >= n_tasks) break;
+        const int p = n - 1 - task / n_heads;   // longest first
+        const int h = task % n_heads;
+        const int mult = score_mult[h];
+
+        // Q of head h at position p with RoPE and the NET_SHIFT rounding (attention.rs:53-83)
+        {
+            const int8_t *qr = qkv + (size_t)(r0 + p) * ldq + h * 64;
+            int x = qr[lane], y = qr[lane + 32];
+            int cs = rope_cos[p * kHalfDim + lane], sn = rope_sin[p * kHalfDim + lane];
+            qbuf[warp][lane] = (int8_t)clamp127(sra_rne32(sra_rne32(x * cs - y * sn, 15), 1));
+            qbuf[warp][lane + 32] = (int8_t)clamp127(sra_rne32(sra_rne32(x * sn + y * cs, 15), 1));
+        }
+        __syncwarp();
+        uint32_t q[16];
+        {
+            const uint4 *q4 = reinterpret_cast<const uint4 *>(qbuf[warp]);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                uint4 w = q4[i];
+                q[4 * i] = w.x; q[4 * i + 1] = w.y; q[4 * i + 2] = w.z; q[4 * i + 3] = w.w;
+            }
+        }
+        __syncwarp();
+
+        int m = INT32_MIN;
+        unsigned long long s = 0;
+        uint32_t va0 = 0, va1 = 0;   // wrapping i32 accumulators of dims 2*lane, 2*lane+1
+        if (sink_key != nullptr) {   // attention.rs:211-224: sink score is the first max
+            m = score_of(q, sink_key, mult);
+            s = 65535ull;
+        }
+
+        for (int kb = 0; kb <= p; kb += 32) {
+            const int t = kb + lane;
+            const bool valid = t <= p;
+            const int sc = valid ? score_of(q, kv + (size_t)t * 128, mult) : INT32_MIN;
+            int incl = sc;   // inclusive prefix max over the block, in key order
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                int u = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl = max(incl, u);
+            }
+            incl = max(incl, m);
+            int prev = __shfl_up_sync(0xffffffffu, incl, 1);
+            if (lane == 0) prev = m;
+            const bool rec = valid && sc > prev;
+            // weight against the max in force after this key (attention.rs:266-268)
+            const uint32_t w = valid ? exp_q16((int)((uint32_t)sc - (uint32_t)incl), lut, coef) : 0u;
+            // rescale factor applied at this key when it sets a new max (attention.rs:248-263)
+            const uint32_t e = (rec && prev != INT32_MIN)
+                                   ? exp_q16((int)((uint32_t)prev - (uint32_t)sc), lut, coef) : 0u;
+            const uint32_t recs = __ballot_sync(0xffffffffu, rec);
+            const int nvalid = min(32, p - kb + 1);
+            const int8_t *vbase = kv + (size_t)kb * 128 + 64 + 2 * lane;
+            if (recs == 0) {
+                uint32_t ws = w;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) ws += __shfl_xor_sync(0xffffffffu, ws, o);
+                s += ws;
+                for (int j = 0; j < nvalid; j++) {
+                    uint32_t wj = __shfl_sync(0xffffffffu, w, j);
+                    uint32_t vv = *reinterpret_cast<const uint16_t *>(vbase + (size_t)j * 128);
+                    va0 += wj * (uint32_t)sext8(vv, 0);
+                    va1 += wj * (uint32_t)sext8(vv, 1);
+                }
+            } else {
+                for (int j = 0; j < nvalid; j++) {
+                    uint32_t wj = __shfl_sync(0xffffffffu, w, j);
+                    uint32_t ej = __shfl_sync(0xffffffffu, e, j);
+                    if (((recs >> j) & 1u) && ej != 0u) {
+                        s = (s * ej + 0x8000ull) >> 16;
+                        long long p0 = (long long)(int)va0 * (long long)ej;
+                        long long p1 = (long long)(int)va1 * (long long)ej;
+                        p0 += p0 >= 0 ? (1ll << 15) : -(1ll << 15);
+                        p1 += p1 >= 0 ? (1ll << 15) : -(1ll << 15);
+                        va0 = (uint32_t)(int)(p0 >> 16);
+                        va1 = (uint32_t)(int)(p1 >> 16);
+                    }
+                    s += wj;
+                    uint32_t vv = *reinterpret_cast<const uint16_t *>(vbase + (size_t)j * 128);
+                    va0 += wj * (uint32_t)sext8(vv, 0);
+                    va1 += wj * (uint32_t)sext8(vv, 1);
+                }
+            }
+            m = __shfl_sync(0xffffffffu, incl, 31);
+        }
+        const unsigned long long den = s == 0 ? 1ull : s;
+        int8_t *o = out + (size_t)(r0 + p) * ldo + h * 64 + 2 * lane;
+        uint16_t pk = (uint16_t)(uint8_t)clamp127(div_rne_s32_u64((int)va0, den)) |
+                      ((uint16_t)(uint8_t)clamp127(div_rne_s32_u64((int)va1, den)) << 8);
+        *reinterpret_cast<uint16_t *>(o) = pk;
+    }
+}
+
+}  // namespace
+
+void attention_init() {
+    cudaFuncSetAttribute(k_attention<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         SMEM_KV_MAX * 128);
+}
+
+void launch_attention(const int8_t *qkv, int ldq, const int8_t *kv, const int *chunk_row0,
+                      const int *chunk_len, int n_chunks, int max_len, int n_heads,
+                      const int32_t *score_mult, const int8_t *sink_key, const int16_t *rope_cos,
+                      const int16_t *rope_sin, const uint16_t *lut, int8_t *out, int ldo,
+                      cudaStream_t st) {
+    if (n_chunks == 0) return;
+    if (max_len <= SMEM_KV_MAX) {
+        size_t smem = (size_t)max_len * 128;
+        k_attention<true><<<n_chunks, ATT_THREADS, smem, st>>>(
+            qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
+            lut, out, ldo);
+    } else {
+        k_attention<false><<<n_chunks, ATT_THREADS, 0, st>>>(
+            qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
+            lut, out, ldo);
+    }
+}
+
+}  // namespace czg

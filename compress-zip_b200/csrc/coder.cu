@@ -1,0 +1,183 @@
+// coder.cu -- integer softmax -> CDF and the 32-bit arithmetic encoder.
+//
+// CDF: rust/src/softmax_cdf.rs:85-139.  For one row of int32 logits:
+//   max and first argmax; e_i = exp_q16(l_i - max) (coef from the model file);
+//   S = sum e_i; freq_i = 1 + floor(e_i * (T - V) / S); the argmax also takes
+//   T - sum freq; cum = inclusive prefix sum.
+// The encoder only needs the symbol's interval, so the compress path reduces
+// the row to (sym_low, sym_high) = (cum[sym-1], cum[sym]) without storing cum.
+// The division by the row-invariant S uses a 64-bit reciprocal with one
+// correction step (exact, see udiv_by_inv).
+//
+// Encoder: rust/src/arith_coder.rs:8-136, one thread per chunk: interval update
+// (80-98), E1/E2/E3 renormalisation with pending bits (101-119), MSB-first bit
+// packing (51-62), finish = one '1' bit and a zero-padded last byte (122-130).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace czg {
+namespace {
+
+// one warp per row
+__global__ void k_cdf_lohi(const int32_t *__restrict__ logits, int V, int ld,
+                           const uint32_t *__restrict__ sym, const uint16_t *__restrict__ lut_g,
+                           uint32_t coef, uint32_t total, int M, uint2 *__restrict__ lohi) {
+    __shared__ uint16_t lut[256];
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) lut[i] = lut_g[i];
+    __syncthreads();
+    const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= M) return;
+    const int32_t *lg = logits + (size_t)row * ld;
+
+    // max and its first index (argmax_deterministic, primitives.rs:278-295)
+    int mx = INT32_MIN, am = 0x7fffffff;
+    for (int i = lane; i < V; i += 32) {
+        int v = lg[i];
+        if (v > mx) { mx = v; am = i; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        int om = __shfl_xor_sync(0xffffffffu, mx, o);
+        int oa = __shfl_xor_sync(0xffffffffu, am, o);
+        if (om > mx || (om == mx && oa < am)) { mx = om; am = oa; }
+    }
+    // S = sum of exp weights (<= 65535 * V, fits 32 bits for V <= 65536)
+    uint32_t S = 0;
+    for (int i = lane; i < V; i += 32)
+        S += exp_q16((int)((uint32_t)lg[i] - (uint32_t)mx), lut, coef);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
+
+    const unsigned long long R = (unsigned long long)(total - (uint32_t)V);
+    const unsigned long long inv = 0xFFFFFFFFFFFFFFFFull / S;
+    const uint32_t sy = sym[row];
+    uint32_t f_all = 0, f_below = 0, f_sym = 0;
+    for (int i = lane; i < V; i += 32) {
+        uint32_t e = exp_q16((int)((uint32_t)lg[i] - (uint32_t)mx), lut, coef);
+        uint32_t f = 1u + (uint32_t)udiv_by_inv((unsigned long long)e * R, S, inv);
+        f_all += f;
+        if ((uint32_t)i < sy) f_below += f;
+        if ((uint32_t)i == sy) f_sym = f;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        f_all += __shfl_xor_sync(0xffffffffu, f_all, o);
+        f_below += __shfl_xor_sync(0xffffffffu, f_below, o);
+        f_sym += __shfl_xor_sync(0xffffffffu, f_sym, o);
+    }
+    if (lane == 0) {
+        uint32_t rem = total - f_all;   // goes to the argmax (softmax_cdf.rs:125-127)
+        uint32_t lo = f_below + ((uint32_t)am < sy ? rem : 0u);
+        uint32_t hi = lo + f_sym + ((uint32_t)am == sy ? rem : 0u);
+        lohi[row] = make_uint2(lo, hi);
+    }
+}
+
+struct BitSink {
+    uint8_t *out;
+    uint32_t cap, len;
+    unsigned long long acc;   // pending bits, right-aligned
+    int n;                    // number of pending bits (< 8 between calls)
+    bool overflow;
+
+    __device__ __forceinline__ void push(uint32_t bits, int count) {   // count <= 32
+        acc = (acc << count) | bits;
+        n += count;
+        while (n >= 8) {
+            n -= 8;
+            uint8_t b = (uint8_t)(acc >> n);
+            if (len < cap) out[len] = b; else overflow = true;
+            len++;
+        }
+        acc &= (1ull << n) - 1ull;
+    }
+    // one bit followed by `run` copies of its complement (arith_coder.rs:66-73)
+    __device__ __forceinline__ void bit_plus_pending(uint32_t bit, uint32_t run) {
+        push(bit, 1);
+        uint32_t fill = bit ? 0u : 0xFFFFFFFFu;
+        while (run > 0) {
+            int c = run > 32 ? 32 : (int)run;
+            push(c == 32 ? fill : (fill & ((1u << c) - 1u)), c);
+            run -= c;
+        }
+    }
+};
+
+// one thread per chunk
+__global__ void k_encode(const uint2 *__restrict__ lohi, const int *__restrict__ chunk_row0,
+                         const int *__restrict__ chunk_len, int n_chunks, uint32_t total,
+                         unsigned long long inv_total, uint8_t *__restrict__ slots,
+                         const uint64_t *__restrict__ slot_off, uint32_t *__restrict__ lens,
+                         int *__restrict__ err) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= n_chunks) return;
+    const unsigned long long HALF = 1ull << 31, QUARTER = 1ull << 30, MASK = 0xFFFFFFFFull;
+    const int r0 = chunk_row0[c], n = chunk_len[c];
+    BitSink bs;
+    bs.out = slots + slot_off[c];
+    bs.cap = (uint32_t)(slot_off[c + 1] - slot_off[c]);
+    bs.len = 0; bs.acc = 0; bs.n = 0; bs.overflow = false;
+    unsigned long long low = 0, high = MASK;
+    uint32_t pending = 0;
+    for (int i = 0; i < n; i++) {
+        uint2 lh = lohi[r0 + i];
+        unsigned long long range = high - low + 1;
+        high = low + udiv_by_inv((unsigned long long)lh.y * range, total, inv_total) - 1;
+        low = low + udiv_by_inv((unsigned long long)lh.x * range, total, inv_total);
+        for (;;) {
+            if (((low ^ high) & HALF) == 0) {
+                bs.bit_plus_pending((uint32_t)((low >> 31) & 1ull), pending);
+                pending = 0;
+                low = (low << 1) & MASK;
+                high = ((high << 1) & MASK) | 1ull;
+            } else if ((low & ~high & QUARTER) != 0) {
+                pending++;
+                low = ((low << 1) ^ HALF) & MASK;
+                high = (((high ^ HALF) << 1) | HALF | 1ull) & MASK;
+            } else {
+                break;
+            }
+        }
+    }
+    bs.push(1u, 1);   // finish: terminating '1', then pad the partial byte
+    if (bs.n > 0) bs.push(0u, 8 - bs.n);
+    lens[c] = bs.len;
+    if (bs.overflow) atomicOr(err, kErrOverflow);
+}
+
+// one CTA per chunk: slot bytes -> packed position
+__global__ void k_pack(const uint8_t *__restrict__ slots, const uint64_t *__restrict__ slot_off,
+                       const uint32_t *__restrict__ lens, const uint64_t *__restrict__ pack_off,
+                       uint8_t *__restrict__ packed) {
+    const int c = blockIdx.x;
+    const uint8_t *src = slots + slot_off[c];
+    uint8_t *dst = packed + pack_off[c];
+    const uint32_t n = lens[c];
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
+}
+
+}  // namespace
+
+void launch_cdf_lohi(const int32_t *logits, int V, int ld, const uint32_t *sym, const uint16_t *lut,
+                     uint32_t coef, uint32_t total, int M, uint2 *lohi, cudaStream_t st) {
+    if (M == 0) return;
+    k_cdf_lohi<<<(M + 7) / 8, 256, 0, st>>>(logits, V, ld, sym, lut, coef, total, M, lohi);
+}
+
+void launch_encode(const uint2 *lohi, const int *chunk_row0, const int *chunk_len, int n_chunks,
+                   uint32_t total, uint8_t *slots, const uint64_t *slot_off, uint32_t *lens,
+                   int *err, cudaStream_t st) {
+    if (n_chunks == 0) return;
+    unsigned long long inv = 0xFFFFFFFFFFFFFFFFull / total;
+    k_encode<<<(n_chunks + 127) / 128, 128, 0, st>>>(lohi, chunk_row0, chunk_len, n_chunks, total,
+                                                      inv, slots, slot_off, lens, err);
+}
+
+void launch_pack(const uint8_t *slots, const uint64_t *slot_off, const uint32_t *lens,
+                 const uint64_t *pack_off, int n_chunks, uint8_t *packed, cudaStream_t st) {
+    if (n_chunks == 0) return;
+    k_pack<<<n_chunks, 128, 0, st>>>(slots, slot_off, lens, pack_off, packed);
+}
+
+}  // namespace czg

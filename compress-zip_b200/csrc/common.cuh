@@ -1,0 +1,135 @@
+// common.cuh -- device integer arithmetic shared by the sm_100a kernels.
+//
+// Every helper reproduces the exact integer semantics of the reference crate
+// (carsonpo/compress-zip, rust/src), cited per function; Rust release builds
+// wrap on overflow, so accumulators that may wrap are kept in uint32_t.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace czg {
+
+constexpr int kHeadDim = 64;
+constexpr int kHalfDim = 32;
+constexpr uint32_t kBos = 1022u;   // rust/src/main.rs:214
+
+// primitives.rs:9-11
+__device__ __forceinline__ int clamp127(int x) { return min(127, max(-127, x)); }
+
+// primitives.rs:18-42.  Round-half-even is symmetric, so flooring the signed
+// value and rounding the remainder equals the reference's sign-magnitude form.
+__device__ __forceinline__ int sra_rne32(int v, int sh) {
+    if (sh == 0) return v;
+    int q = v >> sh;
+    uint32_t r = (uint32_t)v & ((1u << sh) - 1u);
+    uint32_t half = 1u << (sh - 1);
+    q += (r > half) | ((r == half) & (q & 1));
+    return q;
+}
+
+// primitives.rs:49-73 (result saturated to the int32 range)
+__device__ __forceinline__ int sra_rne64_to32(long long v, int sh) {
+    long long q = v;
+    if (sh > 0) {
+        q = v >> sh;
+        unsigned long long r = (unsigned long long)v & ((1ull << sh) - 1ull);
+        unsigned long long half = 1ull << (sh - 1);
+        q += (r > half) | ((r == half) & (q & 1));
+    }
+    q = q < -2147483648ll ? -2147483648ll : q;
+    q = q > 2147483647ll ? 2147483647ll : q;
+    return (int)q;
+}
+
+// model.rs:280-300 -- requantise an int32 accumulator to int8
+__device__ __forceinline__ int requant(int acc, int mult, int shift) {
+    long long p = (long long)acc * (long long)mult;
+    if (shift <= 0) {
+        p = p < -127 ? -127 : (p > 127 ? 127 : p);
+        return (int)p;
+    }
+    return clamp127(sra_rne64_to32(p, shift));
+}
+
+// lut.rs:213-235 == softmax_cdf.rs:55-77: Q16 weight of a non-positive difference
+__device__ __forceinline__ uint32_t exp_q16(int neg_x, const uint16_t *lut, uint32_t coef) {
+    if (neg_x >= 0) return 65535u;
+    uint32_t neg = 0u - (uint32_t)neg_x;
+    uint32_t t256 = (uint32_t)(((unsigned long long)neg * coef + (1ull << 23)) >> 24);
+    uint32_t ip = t256 >> 8;
+    if (ip >= 31) return 1u;
+    uint32_t out = (((1u << 16) >> ip) * (uint32_t)lut[t256 & 255u] + 0x8000u) >> 16;
+    return min(65535u, max(1u, out));
+}
+
+// primitives.rs:192-213 -- restoring integer square root
+__device__ __forceinline__ uint32_t isqrt32(uint32_t x) {
+    uint32_t op = x, res = 0, one = 1u << 30;
+    while (one > op) one >>= 2;
+    while (one != 0) {
+        if (op >= res + one) {
+            op -= res + one;
+            res = (res >> 1) + one;
+        } else {
+            res >>= 1;
+        }
+        one >>= 2;
+    }
+    return res;
+}
+
+// primitives.rs:80-97 -- ties to even only when 2r == d exactly
+__device__ __forceinline__ uint32_t udiv_rne32(uint32_t n, uint32_t d) {
+    if (d == 0) return 0;
+    uint32_t q = n / d, r = n - q * d, tr = r << 1;
+    if (tr > d) return q + 1;
+    if (tr == d) return q + (q & 1u);
+    return q;
+}
+
+// rmsnorm.rs:14-30 with mean_sq = floor(sum_sq / d) + eps (rmsnorm.rs:53-58)
+__device__ __forceinline__ int inv_rms_q15(uint32_t sum_sq, int d, int eps) {
+    int mean_sq = (int)(sum_sq / (uint32_t)d) + eps;
+    uint32_t ms = mean_sq > 0 ? (uint32_t)mean_sq : 1u;
+    uint32_t inv = udiv_rne32(8388608u, isqrt32(ms << 16));
+    return (int)min(32768u, max(1u, inv));
+}
+
+// primitives.rs:163-185; the final `(q as i32) * sign` wraps like Rust release
+__device__ __forceinline__ int div_rne_s32_u64(int num, unsigned long long den) {
+    if (den == 0) return 0;
+    bool neg = num < 0;
+    uint32_t an = neg ? 0u - (uint32_t)num : (uint32_t)num;
+    unsigned long long q, r;
+    if (den <= 0xFFFFFFFFull) {
+        uint32_t d32 = (uint32_t)den;
+        uint32_t q32 = an / d32;
+        q = q32;
+        r = an - q32 * d32;
+    } else {
+        q = 0;
+        r = an;
+    }
+    unsigned long long tr = r << 1;
+    if (tr > den) q += 1;
+    else if (tr == den) q += (q & 1ull);
+    uint32_t q32 = (uint32_t)q;
+    return (int)(neg ? 0u - q32 : q32);
+}
+
+// floor(a / d) for a < 2^62 and d > 0 given inv = floor((2^64 - 1) / d):
+// the estimate umulhi(a, inv) is at most one below the quotient.
+__device__ __forceinline__ unsigned long long udiv_by_inv(unsigned long long a,
+                                                          unsigned long long d,
+                                                          unsigned long long inv) {
+    unsigned long long q = __umul64hi(a, inv);
+    unsigned long long r = a - q * d;
+    if (r >= d) q += 1;
+    return q;
+}
+
+__device__ __forceinline__ int sext8(uint32_t w, int byte) {
+    return (int)(int8_t)((w >> (8 * byte)) & 0xFFu);
+}
+
+}  // namespace czg

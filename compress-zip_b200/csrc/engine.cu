@@ -1,0 +1,663 @@
+// engine.cu -- the C-ABI context: model upload, wave scheduling of chunk
+// batches through the sm_100a kernels, statistics.  Declared in include/czg.h.
+//
+// A compress call (the chunk loop of rust/src/main.rs:206-238 for all chunks at
+// once) runs in waves of consecutive chunks.  Rows of a wave are the wave's
+// tokens in input order, so chunk c of the wave owns rows
+// [starts[c] - starts[c0], starts[c+1] - starts[c0]).  Per wave:
+//   rows -> embed+norm1 -> per layer {QKV GEMM+requant -> K RoPE/V stage ->
+//   exact attention -> O GEMM+requant -> norm3+residual+norm2 -> up GEMM+requant
+//   +ReGLU -> down GEMM+requant -> norm4+residual+next norm} -> LM head GEMM
+//   (int32 logits) -> CDF reduced to the coder interval -> one encoder thread per
+//   chunk -> pack.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "czg.h"
+#include "czm_parse.h"
+#include "kernels.h"
+
+using namespace czg;
+
+void czg::kernels_init() { attention_init(); }
+
+namespace {
+
+enum KernelClass {
+    kRows = 0, kEmbedNorm, kGemmQkv, kKvPrep, kAttention, kGemmO, kResidualNorm, kGemmUp,
+    kGemmDown, kGemmHead, kCdf, kEncode, kPack, kNumClasses
+};
+const char *kClassNames[kNumClasses] = {
+    "rows", "embed_norm", "gemm_qkv", "kv_prep", "attention", "gemm_o", "residual_norm",
+    "gemm_up_reglu", "gemm_down", "gemm_head", "cdf", "encode", "pack"};
+
+thread_local std::string g_create_error;
+
+struct LayerDev {
+    int8_t *attn_norm = nullptr, *post_attn_norm = nullptr, *ffn_norm = nullptr,
+           *post_ffn_norm = nullptr;
+    int8_t *qkv_w = nullptr, *out_w = nullptr, *up_w = nullptr, *down_w = nullptr;
+    int32_t *score_mult = nullptr;
+    int8_t *sink_key = nullptr;
+    int qkv_mult = 1, out_mult = 1, up_mult = 1, down_mult = 1;
+    int qkv_shift = 0, out_shift = 0, up_shift = 0, down_shift = 0;
+};
+
+struct EvPair {
+    cudaEvent_t a, b;
+    int cls;
+};
+
+}  // namespace
+
+struct czg_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    std::string err;
+    czg_model_info info{};
+    int eps = 1;
+    int vpad = 0;           // vocab rounded up to the GEMM tile (extra head rows are zero)
+    int8_t *embed = nullptr, *final_norm = nullptr, *head_w = nullptr;
+    uint16_t *lut = nullptr;
+    int16_t *rope_cos = nullptr, *rope_sin = nullptr;
+    std::vector<LayerDev> layers;
+    std::vector<void *> allocs;
+
+    // wave workspace
+    int cap_rows = 0, cap_chunks = 0;
+    uint32_t *tokens = nullptr, *tok_in = nullptr, *tok_out = nullptr;
+    int *pos = nullptr, *x_res = nullptr, *err_flag = nullptr;
+    int8_t *xn = nullptr, *qkv = nullptr, *kv = nullptr, *attn = nullptr, *o8 = nullptr, *hbuf = nullptr;
+    int32_t *logits = nullptr;
+    uint2 *lohi = nullptr;
+    uint8_t *slots = nullptr, *packed = nullptr;
+    uint32_t *lens = nullptr;
+    uint64_t *slot_off = nullptr, *pack_off = nullptr, *chunk_tok0 = nullptr;
+    int *chunk_row0 = nullptr, *chunk_len = nullptr;
+    // pinned host staging
+    uint8_t *h_meta = nullptr;
+    size_t h_meta_bytes = 0;
+
+    // statistics
+    czg_stats stats{};
+    std::vector<EvPair> evs;
+    size_t ev_used = 0;
+    cudaEvent_t ev_begin = nullptr, ev_end = nullptr;
+};
+
+namespace {
+
+int fail(czg_ctx *c, int code, const std::string &msg) {
+    if (c) c->err = msg;
+    else g_create_error = msg;
+    return code;
+}
+
+bool cuda_ok(czg_ctx *c, cudaError_t e, const char *what) {
+    if (e == cudaSuccess) return true;
+    c->err = std::string(what) + ": " + cudaGetErrorString(e);
+    return false;
+}
+
+template <class T>
+bool dalloc(czg_ctx *c, T **p, size_t n) {
+    void *q = nullptr;
+    cudaError_t e = cudaMalloc(&q, std::max<size_t>(n, 16) * sizeof(T));
+    if (e != cudaSuccess) {
+        c->err = std::string("cudaMalloc: ") + cudaGetErrorString(e);
+        return false;
+    }
+    c->allocs.push_back(q);
+    *p = static_cast<T *>(q);
+    return true;
+}
+
+template <class T>
+bool upload(czg_ctx *c, T **p, const void *src, size_t bytes) {
+    if (!dalloc(c, reinterpret_cast<uint8_t **>(p), bytes)) return false;
+    return cuda_ok(c, cudaMemcpy(*p, src, bytes, cudaMemcpyHostToDevice), "upload");
+}
+
+EvPair &next_ev(czg_ctx *c, int cls) {
+    if (c->ev_used == c->evs.size()) {
+        EvPair e;
+        cudaEventCreate(&e.a);
+        cudaEventCreate(&e.b);
+        c->evs.push_back(e);
+    }
+    EvPair &e = c->evs[c->ev_used++];
+    e.cls = cls;
+    return e;
+}
+
+template <class F>
+void timed(czg_ctx *c, int cls, F &&f) {
+    EvPair &e = next_ev(c, cls);
+    cudaEventRecord(e.a, c->stream);
+    f();
+    cudaEventRecord(e.b, c->stream);
+    c->stats.launches[cls]++;
+}
+
+// Accumulate the recorded event pairs (class -1 = H2D copy, -2 = D2H copy).
+void collect_events(czg_ctx *c) {
+    for (size_t i = 0; i < c->ev_used; i++) {
+        float ms = 0;
+        if (cudaEventElapsedTime(&ms, c->evs[i].a, c->evs[i].b) != cudaSuccess) continue;
+        int cls = c->evs[i].cls;
+        if (cls == -1) c->stats.h2d_ms += ms;
+        else if (cls == -2) c->stats.d2h_ms += ms;
+        else c->stats.kernel_ms[cls] += ms;
+    }
+    c->ev_used = 0;
+}
+
+// ---- model loading --------------------------------------------------------
+
+int meta_int(const CzmFile &f, const char *key, int dflt) {
+    auto it = f.metadata.find(key);
+    if (it == f.metadata.end()) return dflt;
+    const std::string &s = it->second;
+    if (s.empty()) return dflt;
+    char *endp = nullptr;
+    long long v = strtoll(s.c_str(), &endp, 10);
+    if (*endp != '\0' || v < 0 || v > 0x7fffffff) return dflt;   // usize parse failure
+    return (int)v;
+}
+
+const TensorRef *find(const CzmFile &f, const std::string &name) {
+    auto it = f.tensors.find(name);
+    return it == f.tensors.end() ? nullptr : &it->second;
+}
+
+int need(czg_ctx *c, const CzmFile &f, const std::string &name, const char *dtype, int64_t numel,
+         const TensorRef **out) {
+    const TensorRef *t = find(f, name);
+    if (!t) return fail(c, CZG_E_MODEL, "Missing tensor: " + name);
+    if (t->dtype != dtype) return fail(c, CZG_E_MODEL, "tensor " + name + " has dtype " + t->dtype +
+                                              ", expected " + dtype);
+    size_t esz = t->dtype == "I8" || t->dtype == "U8" ? 1 : (t->dtype == "I16" || t->dtype == "U16" ? 2 : 4);
+    if (t->numel() < numel || (size_t)t->numel() * esz > t->nbytes)
+        return fail(c, CZG_E_MODEL, "tensor " + name + " is too small");
+    *out = t;
+    return CZG_OK;
+}
+
+// model.rs:157-170: a missing *.mult reads as 1, a missing *.shift as 0
+int scalar_i32(czg_ctx *c, const CzmFile &f, const std::string &name, int dflt, int *out) {
+    const TensorRef *t = find(f, name);
+    if (!t) { *out = dflt; return CZG_OK; }
+    if (t->dtype != "I32" || t->nbytes < 4) return fail(c, CZG_E_MODEL, "tensor " + name + " is not I32");
+    int32_t v;
+    memcpy(&v, t->data, 4);
+    *out = v;
+    return CZG_OK;
+}
+
+int scalar_i8(czg_ctx *c, const CzmFile &f, const std::string &name, int dflt, int *out) {
+    const TensorRef *t = find(f, name);
+    if (!t) { *out = dflt; return CZG_OK; }
+    if (t->dtype != "I8" || t->nbytes < 1) return fail(c, CZG_E_MODEL, "tensor " + name + " is not I8");
+    *out = (int8_t)t->data[0];
+    return CZG_OK;
+}
+
+int load_model(czg_ctx *c, const uint8_t *bytes, size_t len) {
+    CzmFile f;
+    std::string perr = parse_czm(bytes, len, f);
+    if (!perr.empty()) return fail(c, CZG_E_MODEL, "Failed to load safetensors: " + perr);
+    czg_model_info &m = c->info;
+    // model.rs:113-145
+    int ctx = meta_int(f, "context_length", -1);
+    if (ctx < 0) {
+        int l2 = meta_int(f, "context_length_log2", -1);
+        ctx = l2 >= 0 && l2 < 31 ? (1 << l2) : meta_int(f, "max_seq_len", 64);
+    }
+    m.vocab_size = meta_int(f, "vocab_size", 1024);
+    m.n_layers = meta_int(f, "n_layers", 1);
+    m.n_heads = meta_int(f, "n_heads", 6);
+    m.n_kv_heads = meta_int(f, "n_kv_heads", 1);
+    m.d_model = meta_int(f, "d_model", 384);
+    m.d_ff = meta_int(f, "d_ff", 1024);
+    m.head_dim = meta_int(f, "head_dim", 64);
+    m.max_seq_len = meta_int(f, "max_seq_len", 64);
+    m.context_length = ctx;
+    const int d = m.d_model, V = m.vocab_size, H = m.n_heads, dff = m.d_ff;
+    // shapes the reference runs without panicking (attention.rs:172-176, main.rs:214)
+    if (!(H == 4 || H == 6 || H == 8)) return fail(c, CZG_E_UNSUPPORTED, "n_heads must be 4, 6 or 8");
+    if (m.head_dim != 64 || d != H * 64) return fail(c, CZG_E_UNSUPPORTED, "head_dim must be 64 and d_model = 64 * n_heads");
+    if (m.n_kv_heads < 1 || (d + 2 * 64 * m.n_kv_heads) / (d + 128) != 1)
+        return fail(c, CZG_E_UNSUPPORTED, "n_kv_heads gives a KV batch other than 1");
+    if (V <= 1022 || V > 65536) return fail(c, CZG_E_UNSUPPORTED, "vocab_size must be in 1023..65536");
+    if (m.n_layers < 1 || m.n_layers > 256) return fail(c, CZG_E_UNSUPPORTED, "n_layers out of range");
+    if (dff < 64 || dff % 64 != 0 || dff > 16384) return fail(c, CZG_E_UNSUPPORTED, "d_ff must be a multiple of 64");
+    if (ctx < 1 || ctx > 65536) return fail(c, CZG_E_UNSUPPORTED, "context_length out of range");
+    const int qkv_rows = d + 2 * 64 * m.n_kv_heads;
+    int st;
+    const TensorRef *t;
+    if ((st = need(c, f, "embed.weight", "I8", (int64_t)V * d, &t))) return st;
+    if (!upload(c, &c->embed, t->data, (size_t)V * d)) return CZG_E_DEVICE;
+    if ((st = need(c, f, "norm.weight", "I8", d, &t))) return st;
+    if (!upload(c, &c->final_norm, t->data, d)) return CZG_E_DEVICE;
+    if ((st = need(c, f, "head.weight", "I8", (int64_t)V * d, &t))) return st;
+    c->vpad = (V + 127) / 128 * 128;
+    {
+        std::vector<int8_t> hp((size_t)c->vpad * d, 0);
+        memcpy(hp.data(), t->data, (size_t)V * d);
+        if (!upload(c, &c->head_w, hp.data(), hp.size())) return CZG_E_DEVICE;
+    }
+    if ((st = need(c, f, "lut.exp2", "U16", 256, &t))) return st;
+    if (t->numel() != 256) return fail(c, CZG_E_MODEL, "Exp2 LUT must have exactly 256 entries");
+    if (!upload(c, &c->lut, t->data, 512)) return CZG_E_DEVICE;
+    for (int k = 0; k < 2; k++) {
+        const char *nm = k ? "lut.rope_sin" : "lut.rope_cos";
+        if ((st = need(c, f, nm, "I16", (int64_t)ctx * 32, &t))) return st;
+        if (t->numel() != (int64_t)ctx * 32)   // model.rs:325-333 (from_arrays_with_dims)
+            return fail(c, CZG_E_MODEL, "RoPE LUT arrays size mismatch with max_seq_len * half_dim");
+        if (!upload(c, k ? &c->rope_sin : &c->rope_cos, t->data, (size_t)ctx * 64)) return CZG_E_DEVICE;
+    }
+    // softmax constants (model.rs:255-262, fallbacks softmax_cdf.rs:23-46)
+    const TensorRef *tc = find(f, "softmax.coef_q24"), *tt = find(f, "softmax.target_total");
+    if (tc && (tc->dtype != "U32" || tc->nbytes < 4)) return fail(c, CZG_E_MODEL, "softmax.coef_q24 is not U32");
+    if (tt && (tt->dtype != "U32" || tt->nbytes < 4)) return fail(c, CZG_E_MODEL, "softmax.target_total is not U32");
+    if (tc) memcpy(&m.coef_q24, tc->data, 4);
+    else m.coef_q24 = (uint32_t)std::max(1.0, std::round((0.1 * 1.4426950408889634) / 64.0 * 16777216.0));
+    if (tt) memcpy(&m.target_total, tt->data, 4);
+    else {
+        uint32_t q = 1u << 30, vs = (uint32_t)V;
+        uint32_t tgt = q > vs ? q - vs : 0;
+        tgt = tgt > 1024 ? tgt - 1024 : 0;
+        m.target_total = std::max(tgt, vs + 1);
+    }
+    if (m.target_total <= (uint32_t)V || m.target_total >= (1u << 30))
+        return fail(c, CZG_E_UNSUPPORTED, "softmax.target_total must lie in (vocab_size, 2^30)");
+
+    c->layers.resize(m.n_layers);
+    for (int i = 0; i < m.n_layers; i++) {
+        LayerDev &L = c->layers[i];
+        std::string p = "layers." + std::to_string(i) + ".";
+        struct { const char *nm; int8_t **dst; } norms[4] = {
+            {"attn_norm.weight", &L.attn_norm}, {"post_attn_norm.weight", &L.post_attn_norm},
+            {"ffn_norm.weight", &L.ffn_norm}, {"post_ffn_norm.weight", &L.post_ffn_norm}};
+        for (auto &nw : norms) {
+            if ((st = need(c, f, p + nw.nm, "I8", d, &t))) return st;
+            if (!upload(c, nw.dst, t->data, d)) return CZG_E_DEVICE;
+        }
+        if ((st = need(c, f, p + "attn.qkv.weight", "I8", (int64_t)qkv_rows * d, &t))) return st;
+        // only rows [0, d + 128) are read: q, then the single K and V the reference uses
+        if (!upload(c, &L.qkv_w, t->data, (size_t)(d + 128) * d)) return CZG_E_DEVICE;
+        if ((st = need(c, f, p + "attn.out.weight", "I8", (int64_t)d * d, &t))) return st;
+        if (!upload(c, &L.out_w, t->data, (size_t)d * d)) return CZG_E_DEVICE;
+        if ((st = need(c, f, p + "ffn.up.weight", "I8", (int64_t)2 * dff * d, &t))) return st;
+        {   // interleave gate row j and up row j so the GEMM epilogue sees both
+            std::vector<int8_t> il((size_t)2 * dff * d);
+            for (int j = 0; j < dff; j++) {
+                memcpy(&il[(size_t)(2 * j) * d], t->data + (size_t)j * d, d);
+                memcpy(&il[(size_t)(2 * j + 1) * d], t->data + (size_t)(dff + j) * d, d);
+            }
+            if (!upload(c, &L.up_w, il.data(), il.size())) return CZG_E_DEVICE;
+        }
+        if ((st = need(c, f, p + "ffn.down.weight", "I8", (int64_t)d * dff, &t))) return st;
+        if (!upload(c, &L.down_w, t->data, (size_t)d * dff)) return CZG_E_DEVICE;
+        if ((st = need(c, f, p + "attn.score_mult", "I32", H, &t))) return st;
+        if (!upload(c, &L.score_mult, t->data, (size_t)H * 4)) return CZG_E_DEVICE;
+        if (const TensorRef *sk = find(f, p + "attn.sink_key")) {
+            if (sk->dtype != "I8" || sk->numel() < 64 || sk->nbytes < 64)
+                return fail(c, CZG_E_MODEL, "attn.sink_key must be I8[64]");
+            if (!upload(c, &L.sink_key, sk->data, 64)) return CZG_E_DEVICE;
+        }
+        if ((st = scalar_i32(c, f, p + "attn.qkv.mult", 1, &L.qkv_mult))) return st;
+        if ((st = scalar_i32(c, f, p + "attn.out.mult", 1, &L.out_mult))) return st;
+        if ((st = scalar_i32(c, f, p + "ffn.up.mult", 1, &L.up_mult))) return st;
+        if ((st = scalar_i32(c, f, p + "ffn.down.mult", 1, &L.down_mult))) return st;
+        if ((st = scalar_i8(c, f, p + "attn.qkv.shift", 0, &L.qkv_shift))) return st;
+        if ((st = scalar_i8(c, f, p + "attn.out.shift", 0, &L.out_shift))) return st;
+        if ((st = scalar_i8(c, f, p + "ffn.up.shift", 0, &L.up_shift))) return st;
+        if ((st = scalar_i8(c, f, p + "ffn.down.shift", 0, &L.down_shift))) return st;
+    }
+    return CZG_OK;
+}
+
+int alloc_workspace(czg_ctx *c, int rows, int chunks) {
+    const czg_model_info &m = c->info;
+    const int d = m.d_model;
+    size_t R = (size_t)(rows + 127) / 128 * 128 + 128;
+    c->cap_rows = rows;
+    c->cap_chunks = chunks;
+    bool ok = dalloc(c, &c->tokens, R) && dalloc(c, &c->tok_in, R) && dalloc(c, &c->tok_out, R) &&
+              dalloc(c, &c->pos, R) && dalloc(c, &c->x_res, R * d) && dalloc(c, &c->xn, R * d) &&
+              dalloc(c, &c->qkv, R * (d + 128)) && dalloc(c, &c->kv, R * 128) &&
+              dalloc(c, &c->attn, R * d) && dalloc(c, &c->o8, R * d) &&
+              dalloc(c, &c->hbuf, R * m.d_ff) && dalloc(c, &c->logits, R * c->vpad) &&
+              dalloc(c, &c->lohi, R) && dalloc(c, &c->slots, 4 * R + 8 * (size_t)chunks + 64) &&
+              dalloc(c, &c->packed, 4 * R + 8 * (size_t)chunks + 64) &&
+              dalloc(c, &c->lens, (size_t)chunks) && dalloc(c, &c->slot_off, (size_t)chunks + 1) &&
+              dalloc(c, &c->pack_off, (size_t)chunks + 1) && dalloc(c, &c->chunk_tok0, (size_t)chunks) &&
+              dalloc(c, &c->chunk_row0, (size_t)chunks) && dalloc(c, &c->chunk_len, (size_t)chunks) &&
+              dalloc(c, &c->err_flag, 1);
+    if (!ok) return CZG_E_DEVICE;
+    c->h_meta_bytes = (size_t)chunks * 32 + 64;
+    if (!cuda_ok(c, cudaMallocHost(&c->h_meta, c->h_meta_bytes), "cudaMallocHost")) return CZG_E_DEVICE;
+    return CZG_OK;
+}
+
+struct Trace {
+    int32_t *logits = nullptr;
+    uint32_t *lohi = nullptr;
+    int8_t *attn = nullptr;
+    int8_t *final_in = nullptr;
+};
+
+// Run the model + CDF + encoder for chunks [c0, c1); rows are the wave's tokens.
+// d_tok: device pointer to the wave's first token.  Results stay on device.
+int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t c0, uint32_t c1,
+             const Trace *tr) {
+    const czg_model_info &m = c->info;
+    const int d = m.d_model, dff = m.d_ff, V = m.vocab_size, H = m.n_heads;
+    const int nc = (int)(c1 - c0);
+    const int M = (int)(starts[c1] - starts[c0]);
+    cudaStream_t st = c->stream;
+    // chunk metadata: row0 / len / token offset / slot offsets
+    int *h_row0 = reinterpret_cast<int *>(c->h_meta);
+    int *h_len = h_row0 + nc;
+    uint64_t *h_tok0 = reinterpret_cast<uint64_t *>(h_len + nc + (nc & 1));
+    uint64_t *h_slot = h_tok0 + nc;
+    int max_len = 0;
+    h_slot[0] = 0;
+    for (int i = 0; i < nc; i++) {
+        h_row0[i] = (int)(starts[c0 + i] - starts[c0]);
+        h_len[i] = (int)(starts[c0 + i + 1] - starts[c0 + i]);
+        h_tok0[i] = (uint64_t)h_row0[i];
+        h_slot[i + 1] = h_slot[i] + 4ull * (uint64_t)h_len[i] + 8ull;
+        max_len = std::max(max_len, h_len[i]);
+    }
+    cudaMemcpyAsync(c->chunk_row0, h_row0, sizeof(int) * nc, cudaMemcpyHostToDevice, st);
+    cudaMemcpyAsync(c->chunk_len, h_len, sizeof(int) * nc, cudaMemcpyHostToDevice, st);
+    cudaMemcpyAsync(c->chunk_tok0, h_tok0, sizeof(uint64_t) * nc, cudaMemcpyHostToDevice, st);
+    cudaMemcpyAsync(c->slot_off, h_slot, sizeof(uint64_t) * (nc + 1), cudaMemcpyHostToDevice, st);
+    cudaMemsetAsync(c->err_flag, 0, sizeof(int), st);
+
+    timed(c, kRows, [&] {
+        launch_rows(d_tok, c->chunk_row0, c->chunk_len, c->chunk_tok0, nc, V, c->tok_in, c->tok_out,
+                    c->pos, c->err_flag, st);
+    });
+    timed(c, kEmbedNorm, [&] {
+        launch_embed_norm(c->tok_in, c->embed, c->layers[0].attn_norm, M, d, c->eps, c->x_res, c->xn, st);
+    });
+    for (int l = 0; l < m.n_layers; l++) {
+        const LayerDev &L = c->layers[l];
+        timed(c, kGemmQkv, [&] {
+            launch_gemm(c->xn, L.qkv_w, M, d + 128, d, kEpiRequant, L.qkv_mult, L.qkv_shift, c->qkv,
+                        d + 128, st);
+        });
+        timed(c, kKvPrep, [&] {
+            launch_kv_prep(c->qkv, d + 128, d, c->pos, c->rope_cos, c->rope_sin, M, c->kv, st);
+        });
+        timed(c, kAttention, [&] {
+            launch_attention(c->qkv, d + 128, c->kv, c->chunk_row0, c->chunk_len, nc, max_len, H,
+                             L.score_mult, L.sink_key, c->rope_cos, c->rope_sin, c->lut, c->attn, d, st);
+        });
+        if (tr && tr->attn)
+            cudaMemcpy2DAsync(tr->attn + (size_t)l * d, (size_t)m.n_layers * d, c->attn, d, d, M,
+                              cudaMemcpyDeviceToHost, st);
+        timed(c, kGemmO, [&] {
+            launch_gemm(c->attn, L.out_w, M, d, d, kEpiRequant, L.out_mult, L.out_shift, c->o8, d, st);
+        });
+        timed(c, kResidualNorm, [&] {
+            launch_residual_norm(c->o8, L.ffn_norm, L.post_attn_norm, M, d, c->eps, c->x_res, c->xn, st);
+        });
+        timed(c, kGemmUp, [&] {
+            launch_gemm(c->xn, L.up_w, M, 2 * dff, d, kEpiReglu, L.up_mult, L.up_shift, c->hbuf, dff, st);
+        });
+        timed(c, kGemmDown, [&] {
+            launch_gemm(c->hbuf, L.down_w, M, d, dff, kEpiRequant, L.down_mult, L.down_shift, c->o8, d, st);
+        });
+        const int8_t *next = l + 1 < m.n_layers ? c->layers[l + 1].attn_norm : c->final_norm;
+        timed(c, kResidualNorm, [&] {
+            launch_residual_norm(c->o8, L.post_ffn_norm, next, M, d, c->eps, c->x_res, c->xn, st);
+        });
+    }
+    if (tr && tr->final_in)
+        cudaMemcpyAsync(tr->final_in, c->xn, (size_t)M * d, cudaMemcpyDeviceToHost, st);
+    timed(c, kGemmHead, [&] {
+        launch_gemm(c->xn, c->head_w, M, c->vpad, d, kEpiInt32, 1, 0, c->logits, c->vpad, st);
+    });
+    if (tr && tr->logits)
+        cudaMemcpy2DAsync(tr->logits, (size_t)V * 4, c->logits, (size_t)c->vpad * 4, (size_t)V * 4, M,
+                          cudaMemcpyDeviceToHost, st);
+    timed(c, kCdf, [&] {
+        launch_cdf_lohi(c->logits, V, c->vpad, c->tok_out, c->lut, m.coef_q24, m.target_total, M,
+                        c->lohi, st);
+    });
+    if (tr && tr->lohi)
+        cudaMemcpyAsync(tr->lohi, c->lohi, (size_t)M * 8, cudaMemcpyDeviceToHost, st);
+    timed(c, kEncode, [&] {
+        launch_encode(c->lohi, c->chunk_row0, c->chunk_len, nc, m.target_total, c->slots, c->slot_off,
+                      c->lens, c->err_flag, st);
+    });
+    if (!cuda_ok(c, cudaGetLastError(), "kernel launch")) return CZG_E_DEVICE;
+    return CZG_OK;
+}
+
+struct WavePlan {
+    uint32_t c0, c1;
+};
+
+std::vector<WavePlan> plan_waves(const czg_ctx *c, const uint64_t *starts, uint32_t n) {
+    std::vector<WavePlan> w;
+    uint32_t c0 = 0;
+    while (c0 < n) {
+        uint32_t c1 = c0;
+        while (c1 < n && (c1 - c0) < (uint32_t)c->cap_chunks &&
+               starts[c1 + 1] - starts[c0] <= (uint64_t)c->cap_rows)
+            c1++;
+        w.push_back({c0, c1});
+        c0 = c1;
+    }
+    return w;
+}
+
+void stats_begin(czg_ctx *c) {
+    memset(&c->stats, 0, sizeof(c->stats));
+    c->stats.n_classes = kNumClasses;
+    c->ev_used = 0;
+    cudaEventRecord(c->ev_begin, c->stream);
+}
+
+void stats_end(czg_ctx *c) {
+    cudaEventRecord(c->ev_end, c->stream);
+    cudaEventSynchronize(c->ev_end);
+    float ms = 0;
+    cudaEventElapsedTime(&ms, c->ev_begin, c->ev_end);
+    c->stats.total_ms = ms;
+}
+
+int compress_impl(czg_ctx *c, const uint32_t *tokens, bool device_tokens, const uint64_t *starts,
+                  uint32_t n_chunks, uint8_t *out, uint64_t out_cap, uint32_t *out_lens,
+                  uint64_t *out_needed) {
+    if (!c) return CZG_E_ARG;
+    if ((!starts && n_chunks) || (n_chunks && !tokens)) return fail(c, CZG_E_ARG, "null input pointer");
+    uint64_t ntok = n_chunks ? starts[n_chunks] - starts[0] : 0;
+    const int limit = std::min(c->info.context_length, c->info.max_seq_len);
+    for (uint32_t i = 0; i < n_chunks; i++) {
+        if (starts[i + 1] < starts[i]) return fail(c, CZG_E_ARG, "chunk_starts must be non-decreasing");
+        if (starts[i + 1] - starts[i] > (uint64_t)limit)
+            return fail(c, CZG_E_CHUNK, "chunk " + std::to_string(i) + " is longer than the model's context");
+    }
+    uint64_t bound = czg_compress_bound(ntok, n_chunks);
+    if (!out) {
+        if (out_needed) *out_needed = bound;
+        return CZG_OK;
+    }
+    if (!out_lens) return fail(c, CZG_E_ARG, "out_lens is null");
+    if (!cuda_ok(c, cudaSetDevice(c->device), "cudaSetDevice")) return CZG_E_DEVICE;
+    stats_begin(c);
+    c->stats.n_tokens = ntok;
+    c->stats.n_chunks = n_chunks;
+    uint64_t total = 0;
+    int status = CZG_OK;
+    for (const WavePlan &w : plan_waves(c, starts, n_chunks)) {
+        const uint64_t t0 = starts[w.c0], nt = starts[w.c1] - t0;
+        const uint32_t *d_tok;
+        if (device_tokens) {
+            d_tok = tokens + t0;
+        } else {
+            EvPair &e = next_ev(c, -1);
+            cudaEventRecord(e.a, c->stream);
+            cudaMemcpyAsync(c->tokens, tokens + t0, nt * 4, cudaMemcpyHostToDevice, c->stream);
+            cudaEventRecord(e.b, c->stream);
+            c->stats.h2d_bytes += nt * 4;
+            d_tok = c->tokens;
+        }
+        int st = run_wave(c, d_tok, starts, w.c0, w.c1, nullptr);
+        if (st) return st;
+        const int nc = (int)(w.c1 - w.c0);
+        // lengths -> packed offsets on the host, then pack and copy out
+        int err = 0;
+        cudaMemcpyAsync(out_lens + w.c0, c->lens, sizeof(uint32_t) * nc, cudaMemcpyDeviceToHost, c->stream);
+        cudaMemcpyAsync(&err, c->err_flag, sizeof(int), cudaMemcpyDeviceToHost, c->stream);
+        if (!cuda_ok(c, cudaStreamSynchronize(c->stream), "wave")) return CZG_E_DEVICE;
+        c->stats.d2h_bytes += sizeof(uint32_t) * nc;
+        if (err & kErrToken) return fail(c, CZG_E_TOKEN, "token id >= vocab_size");
+        if (err & kErrOverflow) return fail(c, CZG_E_DEVICE, "encoder slot overflow");
+        uint64_t *h_pack = reinterpret_cast<uint64_t *>(c->h_meta);
+        h_pack[0] = 0;
+        for (int i = 0; i < nc; i++) h_pack[i + 1] = h_pack[i] + out_lens[w.c0 + i];
+        const uint64_t wave_bytes = h_pack[nc];
+        if (total + wave_bytes <= out_cap) {
+            cudaMemcpyAsync(c->pack_off, h_pack, sizeof(uint64_t) * (nc + 1), cudaMemcpyHostToDevice, c->stream);
+            timed(c, kPack, [&] {
+                launch_pack(c->slots, c->slot_off, c->lens, c->pack_off, nc, c->packed, c->stream);
+            });
+            EvPair &e = next_ev(c, -2);
+            cudaEventRecord(e.a, c->stream);
+            cudaMemcpyAsync(out + total, c->packed, wave_bytes, cudaMemcpyDeviceToHost, c->stream);
+            cudaEventRecord(e.b, c->stream);
+            c->stats.d2h_bytes += wave_bytes;
+        } else {
+            status = CZG_E_CAPACITY;
+        }
+        total += wave_bytes;
+        if (!cuda_ok(c, cudaStreamSynchronize(c->stream), "wave copy-out")) return CZG_E_DEVICE;
+        collect_events(c);
+    }
+    stats_end(c);
+    if (out_needed) *out_needed = total;
+    if (status == CZG_E_CAPACITY) return fail(c, CZG_E_CAPACITY, "output buffer too small");
+    return CZG_OK;
+}
+
+}  // namespace
+
+// ---- C ABI ------------------------------------------------------------------
+
+extern "C" {
+
+int czg_ctx_create(int device, const uint8_t *czm, size_t czm_len, czg_ctx **out) {
+    if (!out || !czm) return fail(nullptr, CZG_E_ARG, "null argument");
+    *out = nullptr;
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev)
+        return fail(nullptr, CZG_E_DEVICE, "no such CUDA device");
+    czg_ctx *c = new czg_ctx();
+    c->device = device;
+    int st = CZG_OK;
+    if (cudaSetDevice(device) != cudaSuccess || cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        st = fail(c, CZG_E_DEVICE, "cannot initialise the device");
+    }
+    if (!st) st = load_model(c, czm, czm_len);
+    int wave = 262144;
+    if (const char *e = getenv("CZG_WAVE_TOKENS")) wave = std::max(4096, atoi(e));
+    if (!st) st = alloc_workspace(c, wave, std::max(1024, wave / 16));
+    if (!st) {
+        cudaEventCreate(&c->ev_begin);
+        cudaEventCreate(&c->ev_end);
+        kernels_init();
+        if (!cuda_ok(c, cudaDeviceSynchronize(), "init")) st = CZG_E_DEVICE;
+    }
+    if (st) {
+        g_create_error = c->err;
+        czg_ctx_destroy(c);
+        return st;
+    }
+    *out = c;
+    return CZG_OK;
+}
+
+void czg_ctx_destroy(czg_ctx *c) {
+    if (!c) return;
+    cudaSetDevice(c->device);
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    for (void *p : c->allocs) cudaFree(p);
+    if (c->h_meta) cudaFreeHost(c->h_meta);
+    for (auto &e : c->evs) { cudaEventDestroy(e.a); cudaEventDestroy(e.b); }
+    if (c->ev_begin) cudaEventDestroy(c->ev_begin);
+    if (c->ev_end) cudaEventDestroy(c->ev_end);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    delete c;
+}
+
+const char *czg_last_error(const czg_ctx *c) { return c ? c->err.c_str() : g_create_error.c_str(); }
+
+int czg_model_info_get(const czg_ctx *c, czg_model_info *out) {
+    if (!c || !out) return CZG_E_ARG;
+    *out = c->info;
+    return CZG_OK;
+}
+
+uint64_t czg_compress_bound(uint64_t n_tokens, uint64_t n_chunks) { return 4 * n_tokens + 8 * n_chunks; }
+
+int czg_compress_chunks(czg_ctx *c, const uint32_t *tokens, const uint64_t *starts, uint32_t n_chunks,
+                        uint8_t *out, uint64_t out_cap, uint32_t *out_lens, uint64_t *out_needed) {
+    return compress_impl(c, tokens, false, starts, n_chunks, out, out_cap, out_lens, out_needed);
+}
+
+int czg_compress_chunks_device(czg_ctx *c, const uint32_t *d_tokens, const uint64_t *starts,
+                               uint32_t n_chunks, uint8_t *out, uint64_t out_cap, uint32_t *out_lens,
+                               uint64_t *out_needed) {
+    return compress_impl(c, d_tokens, true, starts, n_chunks, out, out_cap, out_lens, out_needed);
+}
+
+int czg_decompress_chunks(czg_ctx *c, const uint8_t *, const uint64_t *, const uint32_t *, uint32_t,
+                          uint32_t *) {
+    return fail(c, CZG_E_UNSUPPORTED, "decompression is not built yet");
+}
+
+int czg_last_stats(const czg_ctx *c, czg_stats *out) {
+    if (!c || !out) return CZG_E_ARG;
+    *out = c->stats;
+    return CZG_OK;
+}
+
+const char *czg_kernel_name(uint32_t k) { return k < kNumClasses ? kClassNames[k] : ""; }
+
+int czg_debug_trace(czg_ctx *c, const uint32_t *tokens, uint32_t n, int32_t *logits, uint32_t *lohi,
+                    int8_t *attn, int8_t *final_in) {
+    if (!c || (!tokens && n)) return CZG_E_ARG;
+    const int limit = std::min(c->info.context_length, c->info.max_seq_len);
+    if ((int64_t)n > limit) return fail(c, CZG_E_CHUNK, "chunk longer than the model's context");
+    if (n == 0) return CZG_OK;
+    if (!cuda_ok(c, cudaSetDevice(c->device), "cudaSetDevice")) return CZG_E_DEVICE;
+    stats_begin(c);
+    uint64_t starts[2] = {0, n};
+    cudaMemcpyAsync(c->tokens, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, c->stream);
+    Trace tr{logits, lohi, attn, final_in};
+    int st = run_wave(c, c->tokens, starts, 0, 1, &tr);
+    if (st) return st;
+    int err = 0;
+    cudaMemcpyAsync(&err, c->err_flag, sizeof(int), cudaMemcpyDeviceToHost, c->stream);
+    if (!cuda_ok(c, cudaStreamSynchronize(c->stream), "trace")) return CZG_E_DEVICE;
+    collect_events(c);
+    stats_end(c);
+    if (err & kErrToken) return fail(c, CZG_E_TOKEN, "token id >= vocab_size");
+    return CZG_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,54 @@
+// kernels.h -- host-side launchers of the sm_100a kernels (one per file).
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace czg {
+
+// bits of the device error word
+constexpr int kErrToken = 1;     // token id >= vocab
+constexpr int kErrOverflow = 2;  // an encoded chunk outgrew its slot
+constexpr int kErrTimeout = 4;   // a bounded device wait gave up
+
+// per-device one-time set-up (shared-memory opt-ins); call with the device current
+void kernels_init();
+
+// rows.cu
+void launch_rows(const uint32_t *tokens, const int *chunk_row0, const int *chunk_len,
+                 const uint64_t *chunk_tok0, int n_chunks, int vocab, uint32_t *tok_in,
+                 uint32_t *tok_out, int *pos, int *err, cudaStream_t st);
+void launch_embed_norm(const uint32_t *tok_in, const int8_t *embed, const int8_t *norm_w, int M,
+                       int d, int eps, int *x_res, int8_t *xn, cudaStream_t st);
+void launch_residual_norm(const int8_t *o, const int8_t *post_w, const int8_t *next_w, int M, int d,
+                          int eps, int *x_res, int8_t *xn, cudaStream_t st);
+void launch_kv_prep(const int8_t *qkv, int ldq, int d, const int *pos, const int16_t *rope_cos,
+                    const int16_t *rope_sin, int M, int8_t *kv, cudaStream_t st);
+
+// gemm_mma.cu: C[M,N] = A[M,K] . B[N,K]^T in int8 -> int32 with an epilogue.
+// A must hold ceil(M/128)*128 readable rows; N % 128 == 0; K % 64 == 0.
+enum GemmEpilogue {
+    kEpiRequant = 0,   // out int8 [M][ldo] = requant(acc)
+    kEpiReglu = 1,     // B rows interleaved (gate_j, up_j): out int8 [M][ldo], column j
+    kEpiInt32 = 2      // out int32 [M][ldo]
+};
+void launch_gemm(const int8_t *A, const int8_t *B, int M, int N, int K, int epi, int mult,
+                 int shift, void *out, int ldo, cudaStream_t st);
+
+void attention_init();
+// attention.cu: one CTA per chunk; rows of chunk c are chunk_row0[c] ..+chunk_len[c]
+void launch_attention(const int8_t *qkv, int ldq, const int8_t *kv, const int *chunk_row0,
+                      const int *chunk_len, int n_chunks, int max_len, int n_heads,
+                      const int32_t *score_mult, const int8_t *sink_key, const int16_t *rope_cos,
+                      const int16_t *rope_sin, const uint16_t *lut, int8_t *out, int ldo,
+                      cudaStream_t st);
+
+// coder.cu
+void launch_cdf_lohi(const int32_t *logits, int V, int ld, const uint32_t *sym, const uint16_t *lut,
+                     uint32_t coef, uint32_t total, int M, uint2 *lohi, cudaStream_t st);
+void launch_encode(const uint2 *lohi, const int *chunk_row0, const int *chunk_len, int n_chunks,
+                   uint32_t total, uint8_t *slots, const uint64_t *slot_off, uint32_t *lens,
+                   int *err, cudaStream_t st);
+void launch_pack(const uint8_t *slots, const uint64_t *slot_off, const uint32_t *lens,
+                 const uint64_t *pack_off, int n_chunks, uint8_t *packed, cudaStream_t st);
+
+}  // namespace czg

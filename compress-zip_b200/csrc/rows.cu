@@ -1,0 +1,191 @@
+// rows.cu -- per-token row kernels: row set-up, embedding + RMSNorm, and the
+// fused "post-norm, residual add, next pre-norm" step that follows the O and
+// down projections.  One warp per token row; d_model must be a multiple of 128.
+//
+// Reference: the residual stream and sandwich norms of rust/src/model.rs:362-480,
+// RMSNorm of rust/src/rmsnorm.rs:40-75.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace czg {
+
+// One CTA per chunk: token ids into the forward (BOS at position 0, else the
+// previous token, rust/src/main.rs:212-214), the symbol to encode, the position.
+__global__ void k_rows(const uint32_t *__restrict__ tokens, const int *__restrict__ chunk_row0,
+                       const int *__restrict__ chunk_len, const uint64_t *__restrict__ chunk_tok0,
+                       int vocab, uint32_t *__restrict__ tok_in, uint32_t *__restrict__ tok_out,
+                       int *__restrict__ pos, int *__restrict__ err) {
+    int c = blockIdx.x;
+    int r0 = chunk_row0[c], n = chunk_len[c];
+    const uint32_t *src = tokens + chunk_tok0[c];
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        uint32_t t = src[i];
+        uint32_t prev = i == 0 ? kBos : src[i - 1];
+        if (t >= (uint32_t)vocab) atomicOr(err, kErrToken);
+        tok_in[r0 + i] = min(prev, (uint32_t)(vocab - 1));   // kept in bounds; the error flag reports it
+        tok_out[r0 + i] = min(t, (uint32_t)(vocab - 1));
+        pos[r0 + i] = i;
+    }
+}
+
+// Warp-level RMSNorm of one row held as D/128 words of 4 int8 per lane
+// (lane owns bytes [4*lane + 128*j, +4)).  rmsnorm.rs:40-75.
+template <int NW>
+__device__ __forceinline__ void rmsnorm_words(const uint32_t (&x)[NW], const uint32_t (&w)[NW],
+                                              int d, int eps, uint32_t (&y)[NW]) {
+    uint32_t ss = 0;
+#pragma unroll
+    for (int j = 0; j < NW; j++)
+#pragma unroll
+        for (int b = 0; b < 4; b++) {
+            int v = sext8(x[j], b);
+            ss += (uint32_t)(v * v);
+        }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    int inv = inv_rms_q15(ss, d, eps);
+#pragma unroll
+    for (int j = 0; j < NW; j++) {
+        uint32_t out = 0;
+#pragma unroll
+        for (int b = 0; b < 4; b++) {
+            int t = (sext8(x[j], b) * sext8(w[j], b)) * inv;
+            out |= ((uint32_t)(uint8_t)(int8_t)clamp127(sra_rne32(t, 15))) << (8 * b);
+        }
+        y[j] = out;
+    }
+}
+
+// x_res[r] = embed[tok_in[r]] (int32 residual), xn[r] = norm(clamp(x_res[r]))
+template <int NW>
+__global__ void k_embed_norm(const uint32_t *__restrict__ tok_in, const int8_t *__restrict__ embed,
+                             const int8_t *__restrict__ norm_w, int M, int eps,
+                             int *__restrict__ x_res, int8_t *__restrict__ xn) {
+    constexpr int D = NW * 128;
+    int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    if (warp >= M) return;
+    const uint32_t *e = reinterpret_cast<const uint32_t *>(embed + (size_t)tok_in[warp] * D);
+    const uint32_t *wv = reinterpret_cast<const uint32_t *>(norm_w);
+    uint32_t x[NW], w[NW], y[NW];
+#pragma unroll
+    for (int j = 0; j < NW; j++) {
+        x[j] = __ldg(e + lane + 32 * j);
+        w[j] = __ldg(wv + lane + 32 * j);
+    }
+    int4 *xr = reinterpret_cast<int4 *>(x_res + (size_t)warp * D);
+#pragma unroll
+    for (int j = 0; j < NW; j++)
+        xr[lane + 32 * j] = make_int4(sext8(x[j], 0), sext8(x[j], 1), sext8(x[j], 2), sext8(x[j], 3));
+#pragma unroll
+    for (int j = 0; j < NW; j++) {   // clamp_i8 before the norm: -128 becomes -127
+        uint32_t c = 0;
+#pragma unroll
+        for (int b = 0; b < 4; b++) c |= (uint32_t)(uint8_t)clamp127(sext8(x[j], b)) << (8 * b);
+        x[j] = c;
+    }
+    rmsnorm_words<NW>(x, w, D, eps, y);
+    uint32_t *yo = reinterpret_cast<uint32_t *>(xn + (size_t)warp * D);
+#pragma unroll
+    for (int j = 0; j < NW; j++) yo[lane + 32 * j] = y[j];
+}
+
+// o_n = norm(o, post_w); x_res += o_n (int32, never clamped: model.rs:432-434);
+// xn = norm(clamp(x_res), next_w)
+template <int NW>
+__global__ void k_residual_norm(const int8_t *__restrict__ o, const int8_t *__restrict__ post_w,
+                                const int8_t *__restrict__ next_w, int M, int eps,
+                                int *__restrict__ x_res, int8_t *__restrict__ xn) {
+    constexpr int D = NW * 128;
+    int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    if (warp >= M) return;
+    const uint32_t *ov = reinterpret_cast<const uint32_t *>(o + (size_t)warp * D);
+    const uint32_t *pw = reinterpret_cast<const uint32_t *>(post_w);
+    const uint32_t *nw = reinterpret_cast<const uint32_t *>(next_w);
+    uint32_t x[NW], w[NW], y[NW];
+#pragma unroll
+    for (int j = 0; j < NW; j++) {
+        x[j] = ov[lane + 32 * j];
+        w[j] = __ldg(pw + lane + 32 * j);
+    }
+    rmsnorm_words<NW>(x, w, D, eps, y);
+    int4 *xr = reinterpret_cast<int4 *>(x_res + (size_t)warp * D);
+#pragma unroll
+    for (int j = 0; j < NW; j++) {
+        int4 r = xr[lane + 32 * j];
+        r.x = (int)((uint32_t)r.x + (uint32_t)sext8(y[j], 0));
+        r.y = (int)((uint32_t)r.y + (uint32_t)sext8(y[j], 1));
+        r.z = (int)((uint32_t)r.z + (uint32_t)sext8(y[j], 2));
+        r.w = (int)((uint32_t)r.w + (uint32_t)sext8(y[j], 3));
+        xr[lane + 32 * j] = r;
+        x[j] = (uint32_t)(uint8_t)clamp127(r.x) | ((uint32_t)(uint8_t)clamp127(r.y) << 8) |
+               ((uint32_t)(uint8_t)clamp127(r.z) << 16) | ((uint32_t)(uint8_t)clamp127(r.w) << 24);
+        w[j] = __ldg(nw + lane + 32 * j);
+    }
+    rmsnorm_words<NW>(x, w, D, eps, y);
+    uint32_t *yo = reinterpret_cast<uint32_t *>(xn + (size_t)warp * D);
+#pragma unroll
+    for (int j = 0; j < NW; j++) yo[lane + 32 * j] = y[j];
+}
+
+// K rotated with RoPE at the row's position and V copied, into kv[row] =
+// [k_rot (64) | v (64)].  The reference reads K at qkv[d..d+64) and V at
+// qkv[d+64..d+128) whatever n_kv_heads is (rust/src/attention.rs:174-194).
+__global__ void k_kv_prep(const int8_t *__restrict__ qkv, int ldq, int d, const int *__restrict__ pos,
+                          const int16_t *__restrict__ rope_cos, const int16_t *__restrict__ rope_sin,
+                          int M, int8_t *__restrict__ kv) {
+    int gid = blockIdx.x * blockDim.x + threadIdx.x;
+    int row = gid >> 5, i = gid & 31;
+    if (row >= M) return;
+    const int8_t *k = qkv + (size_t)row * ldq + d;
+    int p = pos[row];
+    int x = k[i], y = k[i + kHalfDim];
+    int c = rope_cos[p * kHalfDim + i], s = rope_sin[p * kHalfDim + i];
+    int8_t *dst = kv + (size_t)row * 128;
+    dst[i] = (int8_t)clamp127(sra_rne32(x * c - y * s, 15));            // attention.rs:29-50
+    dst[i + kHalfDim] = (int8_t)clamp127(sra_rne32(x * s + y * c, 15));
+    reinterpret_cast<uint16_t *>(dst + 64)[i] = reinterpret_cast<const uint16_t *>(k + 64)[i];
+}
+
+// ---- host launchers -------------------------------------------------------
+
+void launch_rows(const uint32_t *tokens, const int *chunk_row0, const int *chunk_len,
+                 const uint64_t *chunk_tok0, int n_chunks, int vocab, uint32_t *tok_in,
+                 uint32_t *tok_out, int *pos, int *err, cudaStream_t st) {
+    if (n_chunks == 0) return;
+    k_rows<<<n_chunks, 256, 0, st>>>(tokens, chunk_row0, chunk_len, chunk_tok0, vocab, tok_in,
+                                     tok_out, pos, err);
+}
+
+void launch_embed_norm(const uint32_t *tok_in, const int8_t *embed, const int8_t *norm_w, int M,
+                       int d, int eps, int *x_res, int8_t *xn, cudaStream_t st) {
+    int blocks = (M + 7) / 8;
+    switch (d / 128) {
+        case 2: k_embed_norm<2><<<blocks, 256, 0, st>>>(tok_in, embed, norm_w, M, eps, x_res, xn); break;
+        case 3: k_embed_norm<3><<<blocks, 256, 0, st>>>(tok_in, embed, norm_w, M, eps, x_res, xn); break;
+        case 4: k_embed_norm<4><<<blocks, 256, 0, st>>>(tok_in, embed, norm_w, M, eps, x_res, xn); break;
+        default: break;
+    }
+}
+
+void launch_residual_norm(const int8_t *o, const int8_t *post_w, const int8_t *next_w, int M, int d,
+                          int eps, int *x_res, int8_t *xn, cudaStream_t st) {
+    int blocks = (M + 7) / 8;
+    switch (d / 128) {
+        case 2: k_residual_norm<2><<<blocks, 256, 0, st>>>(o, post_w, next_w, M, eps, x_res, xn); break;
+        case 3: k_residual_norm<3><<<blocks, 256, 0, st>>>(o, post_w, next_w, M, eps, x_res, xn); break;
+        case 4: k_residual_norm<4><<<blocks, 256, 0, st>>>(o, post_w, next_w, M, eps, x_res, xn); break;
+        default: break;
+    }
+}
+
+void launch_kv_prep(const int8_t *qkv, int ldq, int d, const int *pos, const int16_t *rope_cos,
+                    const int16_t *rope_sin, int M, int8_t *kv, cudaStream_t st) {
+    if (M == 0) return;
+    long long threads = (long long)M * 32;
+    k_kv_prep<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(qkv, ldq, d, pos, rope_cos, rope_sin,
+                                                                 M, kv);
+}
+
+}  // namespace czg

@@ -1,0 +1,122 @@
+/*
+ * czg.h -- C ABI of the B200 (sm_100a) compress-zip engine: the model forward,
+ * the integer CDF and the arithmetic coder, batched over many chunks.
+ *
+ * It replaces the per-chunk loops of the reference CLI
+ * (rust/src/main.rs:206-238 compress, rust/src/main.rs:377-396 decompress) and
+ * the crate API those loops drive:
+ *   Model::new / Model::forward / Model::get_cumfreqs   rust/src/model.rs:315,362,483
+ *   ArithEncoder::{new, encode_symbol, finish}           rust/src/arith_coder.rs:28,80,122
+ *   ArithDecoder::{new, decode_symbol}                   rust/src/arith_coder.rs:153,195
+ * The tokenizer, the CZIPv1 container and the brotli/zstd outer layer stay on
+ * the host.  Output is bit-identical to the reference crate.
+ *
+ * Conventions: plain pointers and sizes; caller-owned buffers; every entry point
+ * returns an int status (CZG_OK = 0); nothing panics or aborts across the ABI.
+ * One context per device.  Calls on one context are serialised by the caller
+ * (the context runs its work on its own CUDA stream).  Multi-GPU use = one
+ * context per device, each driven by its own host thread.
+ */
+#ifndef CZG_H
+#define CZG_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct czg_ctx czg_ctx;
+
+enum czg_status {
+    CZG_OK = 0,
+    CZG_E_ARG = 1,          /* null pointer, inconsistent sizes                         */
+    CZG_E_MODEL = 2,        /* .czm bytes malformed, tensor missing or of the wrong dtype */
+    CZG_E_UNSUPPORTED = 3,  /* a shape the reference cannot run (it would panic)        */
+    CZG_E_CAPACITY = 4,     /* output buffer too small; *out_needed holds the size      */
+    CZG_E_DEVICE = 5,       /* CUDA error (message in czg_last_error)                   */
+    CZG_E_TIMEOUT = 6,      /* a bounded device-side wait expired                       */
+    CZG_E_TOKEN = 7,        /* token id >= vocab_size (the reference would panic)       */
+    CZG_E_CHUNK = 8         /* chunk longer than the model's context / KV cache         */
+};
+
+/* Model facts a host driver needs (rust/src/model.rs:19-46). */
+typedef struct {
+    int32_t vocab_size, n_layers, n_heads, n_kv_heads, d_model, d_ff, head_dim;
+    int32_t max_seq_len, context_length;
+    uint32_t coef_q24, target_total;
+} czg_model_info;
+
+/* Device-side timing of the last compress/decompress call, from CUDA events on
+ * the context's stream.  kernel_ms[i] is the summed duration of kernel class i
+ * (names from czg_kernel_name), launches[i] its launch count. */
+#define CZG_MAX_KERNEL_CLASSES 16
+typedef struct {
+    double total_ms;                 /* first launch to last completion, device clock */
+    double h2d_ms, d2h_ms;           /* copies inside the call                        */
+    uint64_t h2d_bytes, d2h_bytes;
+    uint64_t n_tokens, n_chunks;
+    uint32_t n_classes;
+    double kernel_ms[CZG_MAX_KERNEL_CLASSES];
+    uint64_t launches[CZG_MAX_KERNEL_CLASSES];
+} czg_stats;
+
+/* Load a .czm model (safetensors bytes, rust/src/model.rs:108-274 and
+ * rust/src/safetensors.rs:287-376) onto `device` and make a context
+ * (Model::new, rust/src/model.rs:315-351). */
+int czg_ctx_create(int device, const uint8_t *czm, size_t czm_len, czg_ctx **out);
+void czg_ctx_destroy(czg_ctx *ctx);
+
+/* Message of the last failed call on ctx (or of the last failed czg_ctx_create
+ * in this thread when ctx is NULL).  Valid until the next call on ctx. */
+const char *czg_last_error(const czg_ctx *ctx);
+
+int czg_model_info_get(const czg_ctx *ctx, czg_model_info *out);
+
+/* Upper bound of the compressed bytes of n_chunks chunks holding n_tokens
+ * tokens in total (at most 32 renormalisation bits per symbol plus the final
+ * bit, rust/src/arith_coder.rs:101-130). */
+uint64_t czg_compress_bound(uint64_t n_tokens, uint64_t n_chunks);
+
+/* Compress chunks (the loop body of rust/src/main.rs:206-238 for every chunk).
+ * tokens: host array; chunk i is tokens[chunk_starts[i] .. chunk_starts[i+1])
+ * (chunk_starts has n_chunks+1 entries).  Each chunk starts from BOS 1022 at
+ * position 0 with an empty KV cache.  The encoded chunks are written to `out`
+ * back to back in chunk order, chunk i's length to out_lens[i].
+ * out == NULL: only *out_needed = czg_compress_bound(...) is returned.
+ * out_cap too small: CZG_E_CAPACITY with *out_needed = the exact total. */
+int czg_compress_chunks(czg_ctx *ctx, const uint32_t *tokens, const uint64_t *chunk_starts,
+                        uint32_t n_chunks, uint8_t *out, uint64_t out_cap, uint32_t *out_lens,
+                        uint64_t *out_needed);
+
+/* As czg_compress_chunks with the token ids already in device memory
+ * (d_tokens on this context's device).  The encoded bytes and lengths are still
+ * returned in host memory. */
+int czg_compress_chunks_device(czg_ctx *ctx, const uint32_t *d_tokens,
+                               const uint64_t *chunk_starts, uint32_t n_chunks, uint8_t *out,
+                               uint64_t out_cap, uint32_t *out_lens, uint64_t *out_needed);
+
+/* Decompress chunks (the loop body of rust/src/main.rs:377-396 for every chunk).
+ * data: host bytes, chunk i is data[data_starts[i] .. data_starts[i+1]);
+ * n_tokens[i] tokens are decoded for it (reads past its end see zero bits,
+ * rust/src/arith_coder.rs:176-190).  Tokens of chunk i land at
+ * out_tokens + sum(n_tokens[0..i)). */
+int czg_decompress_chunks(czg_ctx *ctx, const uint8_t *data, const uint64_t *data_starts,
+                          const uint32_t *n_tokens, uint32_t n_chunks, uint32_t *out_tokens);
+
+/* Statistics of the last compress/decompress call on ctx. */
+int czg_last_stats(const czg_ctx *ctx, czg_stats *out);
+const char *czg_kernel_name(uint32_t kernel_class);
+
+/* Per-position intermediates of one chunk computed on the GPU, for parity
+ * localisation against the CPU oracle.  Any output may be NULL.
+ * logits: [n][vocab] int32; lohi: [n][2] (sym_low, sym_high of the coder);
+ * attn: [n][n_layers][d_model] attention outputs; final_in: [n][d_model]. */
+int czg_debug_trace(czg_ctx *ctx, const uint32_t *tokens, uint32_t n, int32_t *logits,
+                    uint32_t *lohi, int8_t *attn, int8_t *final_in);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

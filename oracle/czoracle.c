@@ -256,63 +256,88 @@ void czo_build_cumfreqs(const int32_t *logits, int V, const uint16_t *lut, uint3
 /* attention (attention.rs:162-289)                                          */
 /* ------------------------------------------------------------------------ */
 
-/* qkv holds [q (n_heads*64) | k (64) | v (64)] as the reference's single-KV-head
- * attention reads it (attention.rs:174-194).  kc/vc: [max_seq_len][64]. */
+/* One query head at position `step` over cached rotated keys kc[0..step] and
+ * values vc[0..step] ([t][64] each): the ordered online softmax of
+ * attention.rs:199-284, with the optional sink key of attention.rs:211-224. */
+static void attn_one_head(const int8_t *q_in, const int8_t *kc, const int8_t *vc, int step,
+                          int32_t mult, const int8_t *sink_key, const int16_t *cos_t,
+                          const int16_t *sin_t, const uint16_t *lut, int8_t *out) {
+    const int D = 64;
+    const uint32_t coef = czo_attn_coef_q24();
+    int8_t q[64];
+    memcpy(q, q_in, 64);
+    czo_rope_q(q, cos_t, sin_t, step);
+    int32_t mrun = INT32_MIN;
+    uint64_t s = 0;
+    uint32_t vacc[64];   /* i32 with wrapping adds */
+    memset(vacc, 0, sizeof(vacc));
+    if (sink_key) {
+        int32_t dot = 0;
+        for (int i = 0; i < D; i++) dot += (int32_t)q[i] * (int32_t)sink_key[i];
+        int32_t du = czo_sra_rne_s32(dot, 2);
+        mrun = czo_sra_rne_s64_to_s32((int64_t)du * (int64_t)mult, 15);
+        s = czo_exp_q16(0, lut, coef);
+    }
+    for (int t = 0; t <= step; t++) {
+        const int8_t *k = kc + (size_t)t * D;
+        int32_t dot = 0;
+        for (int i = 0; i < D; i++) dot += (int32_t)q[i] * (int32_t)k[i];
+        int32_t du = czo_sra_rne_s32(dot, 2);
+        int32_t score = czo_sra_rne_s64_to_s32((int64_t)du * (int64_t)mult, 15);
+        if (score > mrun) {
+            if (mrun != INT32_MIN) {
+                int32_t diff = (int32_t)((uint32_t)mrun - (uint32_t)score);
+                uint16_t so = czo_exp_q16(diff, lut, coef);
+                s = (s * so + 0x8000ull) >> 16;
+                for (int i = 0; i < D; i++) {
+                    int64_t p = (int64_t)(int32_t)vacc[i] * (int64_t)so;
+                    int64_t adj = p >= 0 ? p + (1ll << 15) : p - (1ll << 15);
+                    vacc[i] = (uint32_t)(int32_t)(adj >> 16);
+                }
+            }
+            mrun = score;
+        }
+        int32_t diff = (int32_t)((uint32_t)score - (uint32_t)mrun);
+        uint16_t w = czo_exp_q16(diff, lut, coef);
+        s += w;
+        const int8_t *v = vc + (size_t)t * D;
+        for (int i = 0; i < D; i++) vacc[i] += (uint32_t)((int32_t)w * (int32_t)v[i]);
+    }
+    uint64_t den = s == 0 ? 1 : s;
+    for (int i = 0; i < D; i++) out[i] = czo_clamp_i8(czo_div_rne_s32_by_u64((int32_t)vacc[i], den));
+}
+
+/* attention.rs:162-289.  qkv holds [q (n_heads*64) | k (64) | v (64) ...] as the
+ * reference's single-KV-head attention reads it (attention.rs:174-194).
+ * kc/vc: [max_seq_len][64]. */
 static void attention_step(const czo_model *m, const czo_layer *L, const int8_t *qkv,
                            int8_t *kc, int8_t *vc, int step, int8_t *out) {
-    const int H = m->n_heads, D = 64;
-    const int d = H * D;
-    const uint32_t coef = czo_attn_coef_q24();
+    const int H = m->n_heads, D = 64, d = H * D;
     int8_t krot[64];
     memcpy(krot, qkv + d, 64);
     czo_rope_k(krot, m->rope_cos, m->rope_sin, step);
     memcpy(kc + (size_t)step * D, krot, 64);
     memcpy(vc + (size_t)step * D, qkv + d + 64, 64);
-    for (int h = 0; h < H; h++) {
-        int8_t q[64];
-        memcpy(q, qkv + h * D, 64);
-        czo_rope_q(q, m->rope_cos, m->rope_sin, step);
-        int32_t mrun = INT32_MIN;
-        uint64_t s = 0;
-        uint32_t vacc[64];   /* i32 with wrapping adds */
-        memset(vacc, 0, sizeof(vacc));
-        int32_t mult = L->score_mult[h];
-        if (L->sink_key) {   /* attention.rs:211-224 */
-            int32_t dot = 0;
-            for (int i = 0; i < D; i++) dot += (int32_t)q[i] * (int32_t)L->sink_key[i];
-            int32_t du = czo_sra_rne_s32(dot, 2);
-            mrun = czo_sra_rne_s64_to_s32((int64_t)du * (int64_t)mult, 15);
-            s = czo_exp_q16(0, m->exp2_lut, coef);
-        }
-        for (int t = 0; t <= step; t++) {
-            const int8_t *k = kc + (size_t)t * D;
-            int32_t dot = 0;
-            for (int i = 0; i < D; i++) dot += (int32_t)q[i] * (int32_t)k[i];
-            int32_t du = czo_sra_rne_s32(dot, 2);
-            int32_t score = czo_sra_rne_s64_to_s32((int64_t)du * (int64_t)mult, 15);
-            if (score > mrun) {
-                if (mrun != INT32_MIN) {
-                    int32_t diff = (int32_t)((uint32_t)mrun - (uint32_t)score);
-                    uint16_t so = czo_exp_q16(diff, m->exp2_lut, coef);
-                    s = (s * so + 0x8000ull) >> 16;
-                    for (int i = 0; i < D; i++) {
-                        int64_t p = (int64_t)(int32_t)vacc[i] * (int64_t)so;
-                        int64_t adj = p >= 0 ? p + (1ll << 15) : p - (1ll << 15);
-                        vacc[i] = (uint32_t)(int32_t)(adj >> 16);
-                    }
-                }
-                mrun = score;
-            }
-            int32_t diff = (int32_t)((uint32_t)score - (uint32_t)mrun);
-            uint16_t w = czo_exp_q16(diff, m->exp2_lut, coef);
-            s += w;
-            const int8_t *v = vc + (size_t)t * D;
-            for (int i = 0; i < D; i++) vacc[i] += (uint32_t)((int32_t)w * (int32_t)v[i]);
-        }
-        uint64_t den = s == 0 ? 1 : s;
-        for (int i = 0; i < D; i++)
-            out[h * D + i] = czo_clamp_i8(czo_div_rne_s32_by_u64((int32_t)vacc[i], den));
+    for (int h = 0; h < H; h++)
+        attn_one_head(qkv + h * D, kc, vc, step, L->score_mult[h], L->sink_key, m->rope_cos,
+                      m->rope_sin, m->exp2_lut, out + h * D);
+}
+
+void czo_attention_seq(const int8_t *q, const int8_t *k, const int8_t *v, int n, int H,
+                       const int32_t *score_mult, const int8_t *sink_key, const int16_t *cos_t,
+                       const int16_t *sin_t, const uint16_t *lut, int8_t *out) {
+    int8_t *kc = (int8_t *)malloc((size_t)n * 64 + 64);
+    int8_t *vc = (int8_t *)malloc((size_t)n * 64 + 64);
+    for (int t = 0; t < n; t++) {
+        memcpy(kc + (size_t)t * 64, k + (size_t)t * 64, 64);
+        czo_rope_k(kc + (size_t)t * 64, cos_t, sin_t, t);
+        memcpy(vc + (size_t)t * 64, v + (size_t)t * 64, 64);
+        for (int h = 0; h < H; h++)
+            attn_one_head(q + ((size_t)t * H + h) * 64, kc, vc, t, score_mult[h], sink_key, cos_t,
+                          sin_t, lut, out + ((size_t)t * H + h) * 64);
     }
+    free(kc);
+    free(vc);
 }
 
 /* ------------------------------------------------------------------------ */

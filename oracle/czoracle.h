@@ -47,6 +47,13 @@ void czo_rope_k(int8_t *x, const int16_t *cos_t, const int16_t *sin_t, int pos);
 void czo_rope_q(int8_t *x, const int16_t *cos_t, const int16_t *sin_t, int pos); /* attention.rs:53-83 */
 uint32_t czo_attn_coef_q24(void);                             /* attention.rs:17-19 */
 
+/* Attention of one chunk's positions 0..n-1, H query heads sharing one K/V
+ * head (attention.rs:162-289 run for pos = 0..n-1).  q: [n][H][64] and k: [n][64]
+ * before RoPE, v: [n][64]; out: [n][H][64].  sink_key may be NULL. */
+void czo_attention_seq(const int8_t *q, const int8_t *k, const int8_t *v, int n, int H,
+                       const int32_t *score_mult, const int8_t *sink_key, const int16_t *cos_t,
+                       const int16_t *sin_t, const uint16_t *lut, int8_t *out);
+
 /* softmax -> inclusive cumulative frequencies (softmax_cdf.rs:85-139) */
 void czo_build_cumfreqs(const int32_t *logits, int V, const uint16_t *lut,
                         uint32_t coef_q24, uint32_t target_total, uint32_t *cum);

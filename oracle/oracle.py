@@ -115,6 +115,7 @@ def _declare(L: C.CDLL) -> None:
         "czo_compress_chunks": (C.c_int, [P, P, P, C.c_uint32, P, C.c_uint64, P, C.c_int]),
         "czo_decompress_chunks": (C.c_int, [P, P, P, P, C.c_uint32, P, C.c_int]),
         "czo_chunk_trace": (None, [P, P, C.c_int, P, P, P, P]),
+        "czo_attention_seq": (None, [P, P, P, C.c_int, C.c_int, P, P, P, P, P, P]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -317,4 +318,22 @@ def decode_symbols(data: bytes, cum_rows) -> list[int]:
     for row in cum_rows:
         row = np.ascontiguousarray(row, dtype=np.uint32)
         out.append(L.czo_dec_decode(C.byref(d), ptr(row), len(row)))
+    return out
+
+
+def attention_seq(q: np.ndarray, k: np.ndarray, v: np.ndarray, score_mult, cos, sin, lut,
+                  sink_key=None) -> np.ndarray:
+    """q: [n][H][64], k/v: [n][64] (k, q before RoPE) -> out [n][H][64]."""
+    q = np.ascontiguousarray(q, dtype=np.int8)
+    k = np.ascontiguousarray(k, dtype=np.int8)
+    v = np.ascontiguousarray(v, dtype=np.int8)
+    n, H = q.shape[0], q.shape[1]
+    sm = np.ascontiguousarray(score_mult, dtype=np.int32)
+    cos = np.ascontiguousarray(cos, dtype=np.int16)
+    sin = np.ascontiguousarray(sin, dtype=np.int16)
+    lut = np.ascontiguousarray(lut, dtype=np.uint16)
+    sk = None if sink_key is None else np.ascontiguousarray(sink_key, dtype=np.int8)
+    out = np.zeros((n, H, 64), dtype=np.int8)
+    lib().czo_attention_seq(ptr(q), ptr(k), ptr(v), n, H, ptr(sm), None if sk is None else ptr(sk),
+                            ptr(cos), ptr(sin), ptr(lut), ptr(out))
     return out

@@ -1,0 +1,132 @@
+"""GPU parity: the CUDA path (through the C ABI) against the CPU oracle.
+
+Bit-exact on every intermediate exposed by the debug trace (attention output
+per layer, final-norm output, int32 logits, coder interval) and on the encoded
+chunk bytes.  Inputs: seeded synthetic text through the model's own tokenizer,
+plus random token ids for edge cases.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def shipped_engine(shipped_path):
+    from compress_zip_b200.engine import Engine
+
+    eng = Engine.from_file(shipped_path, 0)
+    yield eng
+    eng.close()
+
+
+@pytest.fixture(scope="module")
+def shipped_tokens(shipped_path):
+    from compress_zip_b200 import czm, synth
+
+    tok = czm.ModelFile.load(shipped_path).tokenizer()
+    return np.array(tok.encode_with_special_tokens(synth.document(0, 15000)), dtype=np.uint32)
+
+
+def _starts(n, C):
+    return np.array(list(range(0, n, C)) + [n], dtype=np.uint64)
+
+
+def _trace_equal(eng, om, oracle_mod, toks):
+    g = eng.debug_trace(toks)
+    o = oracle_mod.chunk_trace(om, toks)
+    for k in ("attn", "final_in", "logits", "lohi"):
+        if not np.array_equal(g[k], o[k]):
+            bad = np.argwhere(g[k] != o[k])
+            raise AssertionError(f"{k} differs at {len(bad)} places, first {bad[:5].tolist()}")
+
+
+@pytest.mark.parametrize("n", [1, 2, 33, 64, 300])
+def test_trace_shipped(shipped_engine, shipped_oracle, oracle_mod, shipped_tokens, n):
+    _trace_equal(shipped_engine, shipped_oracle, oracle_mod, shipped_tokens[:n])
+
+
+def test_trace_shipped_full_context(shipped_engine, shipped_oracle, oracle_mod, shipped_tokens):
+    _trace_equal(shipped_engine, shipped_oracle, oracle_mod, shipped_tokens[1000:2024])
+
+
+def test_trace_random_tokens(shipped_engine, shipped_oracle, oracle_mod):
+    rng = np.random.default_rng(5)
+    toks = rng.integers(0, 1024, 200).astype(np.uint32)
+    _trace_equal(shipped_engine, shipped_oracle, oracle_mod, toks)
+
+
+@pytest.mark.parametrize("C", [64, 1024])
+def test_compress_bytes_match_oracle(shipped_engine, shipped_oracle, oracle_mod, shipped_tokens, C):
+    starts = _starts(len(shipped_tokens), C)
+    got = shipped_engine.compress_chunks(shipped_tokens, starts)
+    want = oracle_mod.compress_chunks(shipped_oracle, shipped_tokens, starts)
+    assert len(got) == len(want)
+    for i, (a, b) in enumerate(zip(got, want)):
+        assert a == b, f"chunk {i} differs"
+
+
+def test_compress_many_docs(shipped_engine, shipped_oracle, oracle_mod, shipped_path):
+    """Several documents with ragged last chunks in one call."""
+    from compress_zip_b200 import czm, synth
+
+    tok = czm.ModelFile.load(shipped_path).tokenizer()
+    toks, starts = [], [0]
+    for seed in (1, 2, 3):
+        ids = tok.encode_with_special_tokens(synth.document(seed, 3000 + 700 * seed))
+        base = sum(len(t) for t in toks)
+        for s in range(0, len(ids), 256):
+            starts.append(base + min(s + 256, len(ids)))
+        toks.append(ids)
+    tokens = np.concatenate([np.array(t, np.uint32) for t in toks])
+    starts = np.array(starts, np.uint64)
+    got = shipped_engine.compress_chunks(tokens, starts)
+    want = oracle_mod.compress_chunks(shipped_oracle, tokens, starts)
+    assert got == want
+
+
+def test_edge_cases(shipped_engine, shipped_oracle, oracle_mod):
+    from compress_zip_b200.engine import CzgError
+
+    # no chunks
+    packed, lens = shipped_engine.compress_packed(np.zeros(0, np.uint32), np.zeros(1, np.uint64))
+    assert len(packed) == 0 and len(lens) == 0
+    # one-token chunks and an empty chunk
+    toks = np.array([5, 1023, 0, 1022], np.uint32)
+    starts = np.array([0, 1, 2, 2, 4], np.uint64)
+    assert shipped_engine.compress_chunks(toks, starts) == \
+        oracle_mod.compress_chunks(shipped_oracle, toks, starts)
+    # token id out of range: the reference would panic, the ABI reports it
+    with pytest.raises(CzgError) as ei:
+        shipped_engine.compress_chunks(np.array([1, 1024], np.uint32), np.array([0, 2], np.uint64))
+    assert ei.value.status == 7
+    # chunk longer than the model context
+    with pytest.raises(CzgError) as ei:
+        shipped_engine.compress_chunks(np.zeros(1025, np.uint32), np.array([0, 1025], np.uint64))
+    assert ei.value.status == 8
+    # the context still works after errors
+    assert shipped_engine.compress_chunks(toks, starts) == \
+        oracle_mod.compress_chunks(shipped_oracle, toks, starts)
+
+
+@pytest.fixture(scope="module")
+def arch2(tmp_path_factory, shipped_path):
+    from compress_zip_b200 import czm, synth
+    from compress_zip_b200.engine import Engine
+
+    data = synth.arch2_model(czm.ModelFile.load(shipped_path), 512)
+    p = tmp_path_factory.mktemp("m") / "arch2_512.czm"
+    p.write_bytes(data)
+    eng = Engine(data, 0)
+    yield eng, str(p)
+    eng.close()
+
+
+def test_arch2_trace_and_bytes(arch2, oracle_mod, shipped_tokens):
+    eng, path = arch2
+    om = oracle_mod.load_model(path)
+    assert om.check() == 0
+    _trace_equal(eng, om, oracle_mod, shipped_tokens[:200])
+    toks = shipped_tokens[:1500]
+    starts = _starts(len(toks), 512)
+    assert eng.compress_chunks(toks, starts) == oracle_mod.compress_chunks(om, toks, starts)
