@@ -1,0 +1,399 @@
+#!/usr/bin/env python
+"""Benchmark of the compress-zip model-plus-coder path on B200.
+
+Workload: the shipped model v001_eng.czm at
+level L5 (context 1024), batch compression of 1,024 synthetic 15,000-byte
+documents (seeds 1..1024 on rank 0; rank r uses seeds r*1024+1..).  A step is
+one compression of the whole batch: every chunk of every document through the
+model, the CDF and the arithmetic coder (the loop of rust/src/main.rs:206-238).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line (rank 0).  ``value`` is measured with the token ids already
+resident in HBM (czg_compress_chunks_device); ``e2e`` is the same work through
+the host-buffer C-ABI call (czg_compress_chunks), with the host->device copy of
+the tokens and the device->host copy of the encoded bytes inside the timed
+region.  Per-step times come from CUDA events on the stream the engine runs on;
+L2 is flushed (a 256 MiB write) before every timed step, outside the timing.
+The reference arm times the CPU oracle (a C restatement of the reference's Rust
+path) on the host cores over a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+from __graft_entry__ import load_package  # noqa: E402
+
+load_package()
+from compress_zip_b200 import czm, synth  # noqa: E402
+
+METRIC = "compress tokens/s & MB/s at L5 ctx1024, 1/2/4/8 B200; batched decode tok/s"
+MODEL = os.path.join(ROOT, "models", "v001_eng.czm")
+DOC_BYTES = 15000
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--docs", type=int, default=1024)
+    ap.add_argument("--ctx", type=int, default=1024)
+    ap.add_argument("--cpu-sample-docs", type=int, default=32)
+    return ap.parse_args()
+
+
+def workload(mf, seeds, ctx):
+    tok = mf.tokenizer()
+    docs = synth.documents(seeds, DOC_BYTES)
+    ids = tok.encode_batch(docs, num_threads=min(16, os.cpu_count() or 1))
+    starts = [0]
+    base = 0
+    for t in ids:
+        for s in range(0, len(t), ctx):
+            starts.append(base + min(s + ctx, len(t)))
+        base += len(t)
+    tokens = np.concatenate([np.asarray(t, dtype=np.uint32) for t in ids])
+    return tokens, np.asarray(starts, dtype=np.uint64), sum(len(d.encode()) for d in docs)
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.rows = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) == 7:
+                self.rows.append(parts)
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=5)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            try:
+                sm.append(float(r[0]))
+                mx.append(float(r[1]))
+            except ValueError:
+                continue
+            for name, v in zip(names, r[3:]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), float(d["bf16_tflops_sustained"]), \
+            "of measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, 1590.0, 1400.0, "of fallback"
+
+
+def traffic_per_token():
+    """dram bytes per token of each kernel class from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "dram_bytes_per_token.json")
+    try:
+        with open(p) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
+
+
+def algorithmic(kernel: str, info: dict, tokens_per_launch: float):
+    """(bound, algorithmic amount per launch, unit) of a kernel class."""
+    d, dff, V, L = info["d_model"], info["d_ff"], info["vocab_size"], info["n_layers"]
+    if kernel == "attention":
+        # per token and layer: K/V row (128 B) + Q row (d) read once, output (d) written once
+        return "hbm", (128 + 2 * d) * tokens_per_launch, "GB/s"
+    if kernel == "cdf":
+        return "hbm", (4 * V + 4 + 8) * tokens_per_launch, "GB/s"
+    if kernel == "encode":
+        return "hbm", 8.0 * tokens_per_launch + 1.2 * tokens_per_launch, "GB/s"
+    macs = {"gemm_qkv": (d + 128) * d, "gemm_o": d * d, "gemm_up_reglu": 2 * dff * d,
+            "gemm_down": d * dff, "gemm_head": V * d}.get(kernel)
+    if macs is not None:
+        return "tensor", 2.0 * macs * tokens_per_launch, "TFLOP/s"
+    return "hbm", 0.0, "GB/s"
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    mf = czm.ModelFile.load(MODEL)
+    if args.impl == "reference":
+        return run_reference(args, mf, rank, world)
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    from compress_zip_b200.engine import Engine
+
+    seeds = range(rank * args.docs + 1, rank * args.docs + args.docs + 1)
+    tokens, starts, nbytes = workload(mf, seeds, args.ctx)
+    n_tok, n_chunks = int(len(tokens)), int(len(starts) - 1)
+
+    eng = Engine(mf.raw, local)
+    stream = torch.cuda.current_stream()
+    eng.set_stream(stream.cuda_stream)
+    d_tokens = torch.from_numpy(tokens.view(np.int32)).to(f"cuda:{local}")
+    bound = 4 * n_tok + 8 * n_chunks
+    out = np.empty(bound, dtype=np.uint8)
+    lens = np.empty(n_chunks, dtype=np.uint32)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=f"cuda:{local}")
+
+    def step_device():
+        return eng.compress_device(d_tokens.data_ptr(), starts, out, lens)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        step_device()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    times, launches, kern_ms, kern_n = [], 0, {}, {}
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    for _ in range(args.steps):
+        flush.zero_()
+        ev0.record(stream)
+        nout = step_device()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        times.append(ev0.elapsed_time(ev1))
+        st = eng.last_stats()
+        for k, v in st["kernels"].items():
+            kern_ms[k] = kern_ms.get(k, 0.0) + v["ms"]
+            kern_n[k] = kern_n.get(k, 0) + v["launches"]
+            launches += v["launches"]
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    t_rank = sum(times)
+
+    # end to end through the host-buffer ABI call (pinned host memory)
+    h_tokens = torch.from_numpy(tokens.view(np.int32)).pin_memory()
+    h_out = torch.empty(bound, dtype=torch.uint8).pin_memory()
+    h_tok_np = h_tokens.numpy().view(np.uint32)
+    h_out_np = h_out.numpy()
+    import ctypes as C
+    from compress_zip_b200 import engine as E
+
+    def step_host():
+        need = C.c_uint64(0)
+        stt = E.lib().czg_compress_chunks(eng._h, h_tok_np.ctypes.data, starts.ctypes.data,
+                                          n_chunks, h_out_np.ctypes.data, bound,
+                                          lens.ctypes.data, C.byref(need))
+        eng._check(stt)
+        return need.value
+
+    step_host()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_times = []
+    for _ in range(args.steps):
+        flush.zero_()
+        ev0.record(stream)
+        nout_h = step_host()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        e2e_times.append(ev0.elapsed_time(ev1))
+    barrier()
+    t_e2e = sum(e2e_times)
+    parity = bytes(h_out_np[:nout_h]) == bytes(out[:nout])
+
+    if world > 1:
+        t = torch.tensor([t_rank, t_e2e], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_max, t_e2e_max = float(t[0]), float(t[1])
+        tot = torch.tensor([n_tok, nbytes], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(tot)
+        all_tok, all_bytes = float(tot[0]), float(tot[1])
+    else:
+        t_max, t_e2e_max, all_tok, all_bytes = t_rank, t_e2e, float(n_tok), float(nbytes)
+
+    if rank == 0:
+        K = args.steps
+        value = all_tok * K / (t_max / 1e3)
+        e2e_value = all_tok * K / (t_e2e_max / 1e3)
+        hbm, bf16, bf16_sus, basis = peaks()
+        dom = max(kern_ms, key=kern_ms.get)
+        per_launch_ms = kern_ms[dom] / max(1, kern_n[dom])
+        tok_per_launch = n_tok * K / max(1, kern_n[dom])
+        if dom.startswith("gemm") or dom == "attention":
+            tok_per_launch *= 1  # one launch per layer per wave
+        bound, amount, unit = algorithmic(dom, eng.info, tok_per_launch)
+        achieved = amount / (per_launch_ms / 1e3) / (1e9 if unit == "GB/s" else 1e12)
+        peak = hbm if bound == "hbm" else 2.0 * bf16_sus
+        tpt = traffic_per_token().get(dom)
+        roofline = {"kernel": dom, "bound": bound, "achieved": round(achieved, 3), "peak": peak,
+                    "unit": unit, "frac": round(achieved / peak, 5),
+                    "traffic": None if tpt is None else round(tpt * tok_per_launch),
+                    "peak_basis": (f"hbm_gbs {basis}" if bound == "hbm" else
+                                   f"2 x bf16_tflops_sustained {basis} (dense int8 = 2 x bf16)")}
+        cpu = cpu_baseline(mf, args) if world == 1 else None
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+            "steps": K, "warmup": args.warmup, "ms_per_step": round(t_max / K, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic (seeded Zipf lexicon text, BASELINE config 1 shapes)",
+            "mb_per_s": round(all_bytes * K / (t_max / 1e3) / 1e6, 3),
+            "config": {"workload": "config1: shipped v001_eng.czm, L5 ctx 1024, "
+                                   f"{args.docs} docs x {DOC_BYTES} B per GPU",
+                       "model": "v001_eng.czm (d384, 1 layer, 6 heads, MQA, d_ff 1024, V 1024)",
+                       "ctx_len": args.ctx, "docs_per_gpu": args.docs,
+                       "tokens_per_gpu": n_tok, "chunks_per_gpu": n_chunks,
+                       "input_bytes_per_gpu": nbytes, "parallelism": f"dp{world} (documents)",
+                       "l2": "flushed before each timed step (256 MiB write, untimed)"},
+            "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": 4 * n_tok,
+                    "d2h_bytes_per_step": int(nout_h + 4 * n_chunks),
+                    "mb_per_s": round(all_bytes * K / (t_e2e_max / 1e3) / 1e6, 3),
+                    "bytes_identical_to_device_path": parity},
+            "roofline": roofline,
+            "kernels_ms_per_step": {k: round(v / K, 3) for k, v in kern_ms.items()},
+            "gpu_launches": int(launches),
+            "clocks": clk,
+            "compressed_bytes_per_gpu": int(nout),
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def _oracle_sample(mf, ndocs, ctx):
+    tokens, starts, nbytes = workload(mf, range(1, ndocs + 1), ctx)
+    return tokens, starts, nbytes
+
+
+def cpu_baseline(mf, args):
+    """The C oracle (port of the reference's Rust path) on all host cores over the
+    first --cpu-sample-docs documents of the workload."""
+    from oracle import oracle as O
+
+    om = O.load_model(MODEL)
+    tokens, starts, nbytes = _oracle_sample(mf, args.cpu_sample_docs, args.ctx)
+    cores = os.cpu_count() or 1
+    t0 = time.perf_counter()
+    O.compress_chunks(om, tokens, starts, nthreads=cores, variant="avx2")
+    dt = time.perf_counter() - t0
+    # the same source built for the generic x86-64 target (the reference's release profile)
+    g_docs = max(1, args.cpu_sample_docs // 4)
+    g_end = int(np.searchsorted(starts, starts[-1] * g_docs / args.cpu_sample_docs))
+    g_starts = starts[: g_end + 1]
+    t1 = time.perf_counter()
+    O.compress_chunks(om, tokens[: int(g_starts[-1])], g_starts, nthreads=cores, variant="generic")
+    dg = time.perf_counter() - t1
+    return {"value": round(len(tokens) / dt, 1), "unit": "tokens/s", "cores": cores,
+            "kind": "port", "mb_per_s": round(nbytes / dt / 1e6, 4),
+            "value_generic_x86_64": round(int(g_starts[-1]) / dg, 1),
+            "sample": f"{args.cpu_sample_docs} docs x {DOC_BYTES} B (seeds 1..{args.cpu_sample_docs}), "
+                      f"{len(tokens)} tokens, ctx {args.ctx}, {dt:.1f} s; C restatement of the "
+                      "reference Rust path built for x86-64-v3 (value) and for generic x86-64 "
+                      "(value_generic_x86_64, first quarter of the sample)"}
+
+
+def run_reference(args, mf, rank, world):
+    if rank != 0:
+        return 0
+    from oracle import oracle as O
+
+    om = O.load_model(MODEL)
+    ndocs = 8
+    tokens, starts, nbytes = _oracle_sample(mf, ndocs, args.ctx)
+    cores = os.cpu_count() or 1
+    for _ in range(args.warmup):
+        O.compress_chunks(om, tokens, starts, nthreads=cores, variant="avx2")
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        O.compress_chunks(om, tokens, starts, nthreads=cores, variant="avx2")
+        times.append(time.perf_counter() - t0)
+    t = sum(times)
+    value = len(tokens) * args.steps / t
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * t / args.steps, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic (seeded Zipf lexicon text, BASELINE config 1 shapes)",
+        "impl": "reference",
+        "mb_per_s": round(nbytes * args.steps / t / 1e6, 4),
+        "config": {"workload": "config1: shipped v001_eng.czm, L5 ctx 1024; each step a bounded "
+                               f"sample of {ndocs} docs x {DOC_BYTES} B",
+                   "model": "v001_eng.czm", "ctx_len": args.ctx, "tokens_per_step": int(len(tokens))},
+        "cpu_baseline": {"value": round(value, 1), "unit": "tokens/s", "cores": cores,
+                         "kind": "port",
+                         "sample": f"{ndocs} docs (seeds 1..{ndocs}), {len(tokens)} tokens per step; "
+                                   "C restatement of the reference Rust path built for x86-64-v3 "
+                                   "(cargo is absent, the Rust crate cannot be built)"},
+        "e2e": {"value": round(value, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main() or 0)

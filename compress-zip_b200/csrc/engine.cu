@@ -59,7 +59,8 @@ struct EvPair {
 
 struct czg_ctx {
     int device = 0;
-    cudaStream_t stream = nullptr;
+    cudaStream_t stream = nullptr;       // stream all work runs on
+    cudaStream_t own_stream = nullptr;   // the context's own stream
     std::string err;
     czg_model_info info{};
     int eps = 1;
@@ -569,9 +570,11 @@ int czg_ctx_create(int device, const uint8_t *czm, size_t czm_len, czg_ctx **out
     czg_ctx *c = new czg_ctx();
     c->device = device;
     int st = CZG_OK;
-    if (cudaSetDevice(device) != cudaSuccess || cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
+    if (cudaSetDevice(device) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking) != cudaSuccess) {
         st = fail(c, CZG_E_DEVICE, "cannot initialise the device");
     }
+    c->stream = c->own_stream;
     if (!st) st = load_model(c, czm, czm_len);
     int wave = 262144;
     if (const char *e = getenv("CZG_WAVE_TOKENS")) wave = std::max(4096, atoi(e));
@@ -595,12 +598,13 @@ void czg_ctx_destroy(czg_ctx *c) {
     if (!c) return;
     cudaSetDevice(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
+    if (c->own_stream && c->own_stream != c->stream) cudaStreamSynchronize(c->own_stream);
     for (void *p : c->allocs) cudaFree(p);
     if (c->h_meta) cudaFreeHost(c->h_meta);
     for (auto &e : c->evs) { cudaEventDestroy(e.a); cudaEventDestroy(e.b); }
     if (c->ev_begin) cudaEventDestroy(c->ev_begin);
     if (c->ev_end) cudaEventDestroy(c->ev_end);
-    if (c->stream) cudaStreamDestroy(c->stream);
+    if (c->own_stream) cudaStreamDestroy(c->own_stream);
     delete c;
 }
 
@@ -628,6 +632,14 @@ int czg_compress_chunks_device(czg_ctx *c, const uint32_t *d_tokens, const uint6
 int czg_decompress_chunks(czg_ctx *c, const uint8_t *, const uint64_t *, const uint32_t *, uint32_t,
                           uint32_t *) {
     return fail(c, CZG_E_UNSUPPORTED, "decompression is not built yet");
+}
+
+int czg_set_stream(czg_ctx *c, void *stream) {
+    if (!c) return CZG_E_ARG;
+    if (!cuda_ok(c, cudaSetDevice(c->device), "cudaSetDevice")) return CZG_E_DEVICE;
+    if (!cuda_ok(c, cudaStreamSynchronize(c->stream), "cudaStreamSynchronize")) return CZG_E_DEVICE;
+    c->stream = stream ? static_cast<cudaStream_t>(stream) : c->own_stream;
+    return CZG_OK;
 }
 
 int czg_last_stats(const czg_ctx *c, czg_stats *out) {

@@ -21,7 +21,8 @@ MAX_KERNEL_CLASSES = 16
 # The exported symbols of include/czg.h, checked by the CPU test suite.
 EXPORTS = ["czg_ctx_create", "czg_ctx_destroy", "czg_last_error", "czg_model_info_get",
            "czg_compress_bound", "czg_compress_chunks", "czg_compress_chunks_device",
-           "czg_decompress_chunks", "czg_last_stats", "czg_kernel_name", "czg_debug_trace"]
+           "czg_decompress_chunks", "czg_last_stats", "czg_kernel_name", "czg_debug_trace",
+           "czg_set_stream"]
 
 
 class CzgError(RuntimeError):
@@ -75,6 +76,8 @@ def lib() -> C.CDLL:
         L.czg_kernel_name.restype = C.c_char_p
         L.czg_debug_trace.argtypes = [P, P, C.c_uint32, P, P, P, P]
         L.czg_debug_trace.restype = C.c_int
+        L.czg_set_stream.argtypes = [P, P]
+        L.czg_set_stream.restype = C.c_int
         _lib = L
     return _lib
 
@@ -168,6 +171,10 @@ class Engine:
         starts[1:] = np.cumsum([len(c) for c in chunks])
         self._check(lib().czg_decompress_chunks(self._h, _p(data), _p(starts), _p(nt), n, _p(out)))
         return out[: int(nt.sum())]
+
+    def set_stream(self, stream_handle: int | None) -> None:
+        """Run subsequent work on a caller's cudaStream_t (None: the own stream)."""
+        self._check(lib().czg_set_stream(self._h, C.c_void_p(stream_handle or 0)))
 
     # ---- diagnostics -----------------------------------------------------------
     def last_stats(self) -> dict:

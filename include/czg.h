@@ -105,6 +105,12 @@ int czg_compress_chunks_device(czg_ctx *ctx, const uint32_t *d_tokens,
 int czg_decompress_chunks(czg_ctx *ctx, const uint8_t *data, const uint64_t *data_starts,
                           const uint32_t *n_tokens, uint32_t n_chunks, uint32_t *out_tokens);
 
+/* Run this context's work on `stream` (a cudaStream_t of the context's device;
+ * NULL restores the context's own stream).  Lets a caller order the engine's
+ * kernels with its own work and time them with events on its stream.  (No
+ * counterpart in the reference, which has no device streams.) */
+int czg_set_stream(czg_ctx *ctx, void *stream);
+
 /* Statistics of the last compress/decompress call on ctx. */
 int czg_last_stats(const czg_ctx *ctx, czg_stats *out);
 const char *czg_kernel_name(uint32_t kernel_class);

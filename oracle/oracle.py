@@ -17,7 +17,8 @@ import subprocess
 import numpy as np
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-_LIB_PATH = os.path.join(_HERE, "libczoracle.so")
+_LIB_PATHS = {"generic": os.path.join(_HERE, "libczoracle.so"),
+              "avx2": os.path.join(_HERE, "libczoracle_avx2.so")}
 MAX_LAYERS = 64
 BOS = 1022
 
@@ -25,20 +26,22 @@ BOS = 1022
 def build() -> str:
     """Compile the oracle with its Makefile (checker build, not the product)."""
     subprocess.run(["make", "-s", "-C", _HERE], check=True)
-    return _LIB_PATH
+    return _LIB_PATHS["generic"]
 
 
-_lib = None
+_libs: dict = {}
 
 
-def lib() -> C.CDLL:
-    global _lib
-    if _lib is None:
-        if not os.path.exists(_LIB_PATH):
+def lib(variant: str = "generic") -> C.CDLL:
+    """The oracle library: "generic" (default x86-64 target) or "avx2" (x86-64-v3)."""
+    if variant not in _libs:
+        path = _LIB_PATHS[variant]
+        if not os.path.exists(path):
             build()
-        _lib = C.CDLL(_LIB_PATH)
-        _declare(_lib)
-    return _lib
+        L = C.CDLL(path)
+        _declare(L)
+        _libs[variant] = L
+    return _libs[variant]
 
 
 class Layer(C.Structure):
@@ -240,7 +243,7 @@ def slot_cap(n_tokens: int) -> int:
 
 
 def compress_chunks(model: OracleModel, tokens: np.ndarray, chunk_starts: np.ndarray,
-                    nthreads: int | None = None) -> list[bytes]:
+                    nthreads: int | None = None, variant: str = "generic") -> list[bytes]:
     tokens = np.ascontiguousarray(tokens, dtype=np.uint32)
     starts = np.ascontiguousarray(chunk_starts, dtype=np.uint64)
     n = len(starts) - 1
@@ -250,15 +253,15 @@ def compress_chunks(model: OracleModel, tokens: np.ndarray, chunk_starts: np.nda
     out = np.zeros(n * cap, dtype=np.uint8)
     lens = np.zeros(n, dtype=np.uint32)
     nt = nthreads or os.cpu_count() or 1
-    st = lib().czo_compress_chunks(model.ref, ptr(tokens), ptr(starts), n, ptr(out), cap,
-                                   ptr(lens), nt)
+    st = lib(variant).czo_compress_chunks(model.ref, ptr(tokens), ptr(starts), n, ptr(out), cap,
+                                          ptr(lens), nt)
     if st != 0:
         raise ValueError(f"oracle compress failed ({st})")
     return [out[i * cap: i * cap + int(lens[i])].tobytes() for i in range(n)]
 
 
 def decompress_chunks(model: OracleModel, chunks: list[bytes], n_tokens,
-                      nthreads: int | None = None) -> np.ndarray:
+                      nthreads: int | None = None, variant: str = "generic") -> np.ndarray:
     n = len(chunks)
     if n == 0:
         return np.zeros(0, dtype=np.uint32)
@@ -267,8 +270,8 @@ def decompress_chunks(model: OracleModel, chunks: list[bytes], n_tokens,
     starts[1:] = np.cumsum([len(c) for c in chunks])
     nt_arr = np.ascontiguousarray(n_tokens, dtype=np.uint32)
     out = np.zeros(int(nt_arr.sum()), dtype=np.uint32)
-    st = lib().czo_decompress_chunks(model.ref, ptr(data), ptr(starts), ptr(nt_arr), n,
-                                     ptr(out), nthreads or os.cpu_count() or 1)
+    st = lib(variant).czo_decompress_chunks(model.ref, ptr(data), ptr(starts), ptr(nt_arr), n,
+                                            ptr(out), nthreads or os.cpu_count() or 1)
     if st != 0:
         raise ValueError(f"oracle decompress failed ({st})")
     return out
