@@ -26,7 +26,10 @@
 
 using namespace czg;
 
-void czg::kernels_init() { attention_init(); }
+void czg::kernels_init() {
+    attention_init();
+    attention_mma_init();
+}
 
 namespace {
 
@@ -64,9 +67,11 @@ struct czg_ctx {
     std::string err;
     czg_model_info info{};
     int eps = 1;
+    bool scalar_attention = false;   // CZG_SCALAR_ATTENTION=1 selects the CUDA-core kernel
     int vpad = 0;           // vocab rounded up to the GEMM tile (extra head rows are zero)
     int8_t *embed = nullptr, *final_norm = nullptr, *head_w = nullptr;
     uint16_t *lut = nullptr;
+    uint16_t *lut4k = nullptr;   // exp_q16 by t256 < 4096 (lut.rs:213-235 unrolled over ip)
     int16_t *rope_cos = nullptr, *rope_sin = nullptr;
     std::vector<LayerDev> layers;
     std::vector<void *> allocs;
@@ -257,6 +262,16 @@ int load_model(czg_ctx *c, const uint8_t *bytes, size_t len) {
     if ((st = need(c, f, "lut.exp2", "U16", 256, &t))) return st;
     if (t->numel() != 256) return fail(c, CZG_E_MODEL, "Exp2 LUT must have exactly 256 entries");
     if (!upload(c, &c->lut, t->data, 512)) return CZG_E_DEVICE;
+    {   // t256 -> clamp(((65536 >> (t256 >> 8)) * lut[t256 & 255] + 2^15) >> 16, 1, 65535)
+        uint16_t lut8[256];
+        memcpy(lut8, t->data, 512);
+        std::vector<uint16_t> l4(4096);
+        for (uint32_t tt = 0; tt < 4096; tt++) {
+            uint32_t o = (((1u << 16) >> (tt >> 8)) * (uint32_t)lut8[tt & 255] + 0x8000u) >> 16;
+            l4[tt] = (uint16_t)std::min(65535u, std::max(1u, o));
+        }
+        if (!upload(c, &c->lut4k, l4.data(), 8192)) return CZG_E_DEVICE;
+    }
     for (int k = 0; k < 2; k++) {
         const char *nm = k ? "lut.rope_sin" : "lut.rope_cos";
         if ((st = need(c, f, nm, "I16", (int64_t)ctx * 32, &t))) return st;
@@ -402,8 +417,13 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
             launch_kv_prep(c->qkv, d + 128, d, c->pos, c->rope_cos, c->rope_sin, M, c->kv, st);
         });
         timed(c, kAttention, [&] {
-            launch_attention(c->qkv, d + 128, c->kv, c->chunk_row0, c->chunk_len, nc, max_len, H,
-                             L.score_mult, L.sink_key, c->rope_cos, c->rope_sin, c->lut, c->attn, d, st);
+            if (attention_mma_fits(max_len) && !c->scalar_attention)
+                launch_attention_mma(c->qkv, d + 128, c->kv, c->chunk_row0, c->chunk_len, nc, max_len, H,
+                                     L.score_mult, L.sink_key, c->rope_cos, c->rope_sin, c->lut4k,
+                                     c->attn, d, st);
+            else
+                launch_attention(c->qkv, d + 128, c->kv, c->chunk_row0, c->chunk_len, nc, max_len, H,
+                                 L.score_mult, L.sink_key, c->rope_cos, c->rope_sin, c->lut, c->attn, d, st);
         });
         if (tr && tr->attn)
             cudaMemcpy2DAsync(tr->attn + (size_t)l * d, (size_t)m.n_layers * d, c->attn, d, d, M,
@@ -576,6 +596,7 @@ int czg_ctx_create(int device, const uint8_t *czm, size_t czm_len, czg_ctx **out
     }
     c->stream = c->own_stream;
     if (!st) st = load_model(c, czm, czm_len);
+    c->scalar_attention = getenv("CZG_SCALAR_ATTENTION") && atoi(getenv("CZG_SCALAR_ATTENTION")) != 0;
     int wave = 262144;
     if (const char *e = getenv("CZG_WAVE_TOKENS")) wave = std::max(4096, atoi(e));
     if (!st) st = alloc_workspace(c, wave, std::max(1024, wave / 16));

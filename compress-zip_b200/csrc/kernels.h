@@ -35,6 +35,15 @@ void launch_gemm(const int8_t *A, const int8_t *B, int M, int N, int K, int epi,
                  int shift, void *out, int ldo, cudaStream_t st);
 
 void attention_init();
+// attention_mma.cu: tensor-core version for chunks of at most 1024 positions;
+// lut4k = exp_q16 for t256 < 4096 (see exp4k_table)
+bool attention_mma_fits(int max_len);
+void attention_mma_init();
+void launch_attention_mma(const int8_t *qkv, int ldq, const int8_t *kv, const int *chunk_row0,
+                          const int *chunk_len, int n_chunks, int max_len, int n_heads,
+                          const int32_t *score_mult, const int8_t *sink_key, const int16_t *rope_cos,
+                          const int16_t *rope_sin, const uint16_t *lut4k, int8_t *out, int ldo,
+                          cudaStream_t st);
 // attention.cu: one CTA per chunk; rows of chunk c are chunk_row0[c] ..+chunk_len[c]
 void launch_attention(const int8_t *qkv, int ldq, const int8_t *kv, const int *chunk_row0,
                       const int *chunk_len, int n_chunks, int max_len, int n_heads,

@@ -130,3 +130,55 @@ def test_arch2_trace_and_bytes(arch2, oracle_mod, shipped_tokens):
     toks = shipped_tokens[:1500]
     starts = _starts(len(toks), 512)
     assert eng.compress_chunks(toks, starts) == oracle_mod.compress_chunks(om, toks, starts)
+
+
+def _variant_model(shipped_path, tmp_path, sink=False, score_mult=None):
+    """The shipped model with an attention sink key and/or other score multipliers."""
+    from compress_zip_b200 import czm
+
+    mf = czm.ModelFile.load(shipped_path)
+    t = {k: np.array(v) for k, v in mf.tensors.items()}
+    rng = np.random.default_rng(11)
+    if sink:
+        t["layers.0.attn.sink_key"] = rng.integers(-127, 128, 64).astype(np.int8)
+    if score_mult is not None:
+        t["layers.0.attn.score_mult"] = np.asarray(score_mult, np.int32)
+    data = czm.write_safetensors(t, mf.metadata)
+    p = tmp_path / "variant.czm"
+    p.write_bytes(data)
+    return data, str(p)
+
+
+@pytest.mark.parametrize("sink,score_mult", [
+    (True, None),
+    (False, [1 << 20, 1 << 24, 2147483647, -2147483647, 3, -60000]),   # record-heavy, clamped scores
+    (True, [400000, 1, 70000, 58218, -58218, 900000]),
+])
+def test_attention_edge_models(shipped_path, tmp_path, oracle_mod, shipped_tokens, sink, score_mult):
+    from compress_zip_b200.engine import Engine
+
+    data, path = _variant_model(shipped_path, tmp_path, sink, score_mult)
+    om = oracle_mod.load_model(path)
+    eng = Engine(data, 0)
+    try:
+        _trace_equal(eng, om, oracle_mod, shipped_tokens[:700])
+        toks = shipped_tokens[:2100]
+        starts = _starts(len(toks), 1024)
+        assert eng.compress_chunks(toks, starts) == oracle_mod.compress_chunks(om, toks, starts)
+    finally:
+        eng.close()
+
+
+def test_scalar_attention_kernel(shipped_path, shipped_oracle, oracle_mod, shipped_tokens, monkeypatch):
+    """The CUDA-core attention kernel (used beyond 1024 positions) on short chunks too."""
+    from compress_zip_b200.engine import Engine
+
+    monkeypatch.setenv("CZG_SCALAR_ATTENTION", "1")
+    eng = Engine.from_file(shipped_path, 0)
+    try:
+        _trace_equal(eng, shipped_oracle, oracle_mod, shipped_tokens[:300])
+        starts = _starts(len(shipped_tokens), 1024)
+        assert eng.compress_chunks(shipped_tokens, starts) == \
+            oracle_mod.compress_chunks(shipped_oracle, shipped_tokens, starts)
+    finally:
+        eng.close()
