@@ -597,7 +597,7 @@ int czg_ctx_create(int device, const uint8_t *czm, size_t czm_len, czg_ctx **out
     c->stream = c->own_stream;
     if (!st) st = load_model(c, czm, czm_len);
     c->scalar_attention = getenv("CZG_SCALAR_ATTENTION") && atoi(getenv("CZG_SCALAR_ATTENTION")) != 0;
-    int wave = 262144;
+    int wave = 1 << 20;
     if (const char *e = getenv("CZG_WAVE_TOKENS")) wave = std::max(4096, atoi(e));
     if (!st) st = alloc_workspace(c, wave, std::max(1024, wave / 16));
     if (!st) {
