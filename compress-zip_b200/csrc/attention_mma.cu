@@ -18,9 +18,12 @@
 // exactly sum(byte * v) and never overflows (|sum| <= 255*127*4096), so
 // vacc = 256*Hi + Lo (mod 2^32) equals the reference's wrapping i32 sum.
 // A tile whose rows contain records is replayed in passes: pass q adds the keys
-// of segment q (segment = run of keys between records), and before pass q every
-// row with a q-th record folds its state exactly as the reference rescales at
-// that key: state = R(state + 256*Hi + Lo, e), s = ((s + seg_sum) * e + 2^15) >> 16.
+// of segment q (segment = run of keys between records).  Before pass q every
+// row with a q-th record in the tile folds its state exactly as the reference
+// rescales at that key: state = R(state + 256*Hi + Lo, e),
+// s = ((s + seg_sum) * e + 2^15) >> 16.  The folded state of a warp's 16 rows
+// lives in shared memory as [row][dim] so that all 32 lanes fold one row
+// together (2 dims each).
 #include "common.cuh"
 #include "kernels.h"
 
@@ -30,6 +33,7 @@ namespace {
 constexpr int AM_THREADS = 256;
 constexpr int AM_WARPS = AM_THREADS / 32;
 constexpr int AM_MAX_KEYS = 1024;
+constexpr int AM_WARP_SMEM = 16 * 64 * 4 * 2 + 16 * 32 * 4 + 16 * 4 * 2;   // vst, segbuf, rec_e, nrec, s
 
 __device__ __forceinline__ void mma_s8s8(int (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
     asm volatile(
@@ -47,6 +51,12 @@ __device__ __forceinline__ void mma_u8s8(int (&c)[4], const uint32_t (&a)[4], ui
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
 // exp_q16 with the attention coefficient via a 4096-entry table indexed by
 // t256 (entries for t256 >= 4096 are all 1, whatever the exp2 LUT holds).
 // t256 = floor((neg * coef + 2^23) / 2^24) = hi + (lo >= 2^31) of neg * (coef << 8).
@@ -57,34 +67,115 @@ __device__ __forceinline__ uint32_t exp_attn(int diff, const uint16_t *lut4k, ui
     return t < 4096u ? (uint32_t)lut4k[t] : 1u;
 }
 
+// score = round_even(round_even(dot / 4) * mult / 2^15) saturated to int32
+// (attention.rs:236-245).  round_even(x / 2^s) = (x + 2^(s-1) - 1 + ((x >> s) & 1)) >> s.
+template <bool WIDE>
 __device__ __forceinline__ int score_from_dot(int dot, int mult) {
-    return sra_rne64_to32((long long)sra_rne32(dot, 2) * (long long)mult, 15);
+    const int du = (dot + 1 + ((dot >> 2) & 1)) >> 2;
+    const long long p = (long long)du * (long long)mult;
+    long long s = (p + 16383 + ((p >> 15) & 1)) >> 15;
+    if (WIDE) {   // |mult| >= 2^28: the result may leave the int32 range
+        s = s < -2147483648ll ? -2147483648ll : (s > 2147483647ll ? 2147483647ll : s);
+    }
+    return (int)s;
 }
 
-// quad (4 lanes with equal lane>>2) helpers
-__device__ __forceinline__ uint32_t quad_or(uint32_t v) {
-    v |= __shfl_xor_sync(0xffffffffu, v, 1);
-    v |= __shfl_xor_sync(0xffffffffu, v, 2);
-    return v;
-}
 __device__ __forceinline__ uint32_t quad_sum(uint32_t v) {
     v += __shfl_xor_sync(0xffffffffu, v, 1);
     v += __shfl_xor_sync(0xffffffffu, v, 2);
     return v;
 }
 
-// key of accumulator column n = 8j + 2t + e in the QK product (and of B row n = 8j + g)
+// key (within a 32-key tile) of QK accumulator column / B row n = 8j + r
 __device__ __forceinline__ int perm_key(int n) {
     int j = n >> 3, r = n & 7;
     return 16 * (j >> 1) + 4 * (r >> 1) + 2 * (j & 1) + (r & 1);
 }
 
-// K rows: 64 bytes, 16-byte chunks XOR-swizzled by (key >> 2) & 3
-__device__ __forceinline__ uint32_t k_word(const uint8_t *ks, int key, int dim) {
-    int chunk = (dim >> 4) ^ ((key >> 2) & 3);
-    return *reinterpret_cast<const uint32_t *>(ks + key * 64 + chunk * 16 + (dim & 15));
+struct Tile {
+    // per row half: weights, record factor flags, segment of each entry
+    uint32_t w[2][8];
+    uint32_t ef[2][8];
+    int seg[2][8];
+    int nrec[2];
+};
+
+// Scores, prefix max, records, weights and segments of one 32-key tile.
+// Entry i of a row half is key kb + 16*(i>>2) + 4t + (i&3).
+template <bool MASKED, bool WIDE>
+__device__ __forceinline__ void tile_softmax(const int (&sacc)[4][4], int kb, const int (&prow)[2], int n,
+                                             int mult, int t, int lane, int (&m)[2],
+                                             const uint16_t *lut4k, uint32_t c8, Tile &T) {
+#pragma unroll
+    for (int hr = 0; hr < 2; hr++) {
+        int sc[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int q = i >> 2, b = i & 3;
+            const int j = 2 * q + (b >> 1), e = b & 1;
+            bool valid = true;
+            if (MASKED) valid = kb + 16 * q + 4 * t + b <= prow[hr] && prow[hr] < n;
+            sc[i] = valid ? score_from_dot<WIDE>(sacc[j][2 * hr + e], mult) : INT32_MIN;
+        }
+        int run = m[hr];
+        int cnt_before = 0;
+#pragma unroll
+        for (int q = 0; q < 2; q++) {
+            int L[4];
+            L[0] = sc[4 * q];
+#pragma unroll
+            for (int b = 1; b < 4; b++) L[b] = max(L[b - 1], sc[4 * q + b]);
+            int inc = L[3];
+            int u = __shfl_up_sync(0xffffffffu, inc, 1, 4);
+            if (t >= 1) inc = max(inc, u);
+            u = __shfl_up_sync(0xffffffffu, inc, 2, 4);
+            if (t >= 2) inc = max(inc, u);
+            const int excl = __shfl_up_sync(0xffffffffu, inc, 1, 4);
+            const int base = t == 0 ? run : max(run, excl);
+            int prevmax = base;
+            int lrec = 0;
+#pragma unroll
+            for (int b = 0; b < 4; b++) {
+                const int i = 4 * q + b;
+                bool valid = true;
+                if (MASKED) valid = kb + 16 * q + 4 * t + b <= prow[hr] && prow[hr] < n;
+                const int pm = max(base, L[b]);
+                const bool rec = valid && sc[i] > prevmax;
+                T.w[hr][i] = valid ? exp_attn((int)((uint32_t)sc[i] - (uint32_t)pm), lut4k, c8) : 0u;
+                uint32_t f = 0;
+                if (rec) {
+                    // 0x10000 | factor, or 0x20000 while the previous max is still INT32_MIN:
+                    // the reference then keeps its sums unscaled (attention.rs:248-250)
+                    f = prevmax == INT32_MIN
+                            ? 0x20000u
+                            : 0x10000u | exp_attn((int)((uint32_t)prevmax - (uint32_t)sc[i]), lut4k, c8);
+                    lrec++;
+                }
+                T.ef[hr][i] = f;
+                prevmax = pm;
+            }
+            int cinc = lrec;
+            int cu = __shfl_up_sync(0xffffffffu, cinc, 1, 4);
+            if (t >= 1) cinc += cu;
+            cu = __shfl_up_sync(0xffffffffu, cinc, 2, 4);
+            if (t >= 2) cinc += cu;
+            const int cex = __shfl_up_sync(0xffffffffu, cinc, 1, 4);
+            int sidx = cnt_before + (t == 0 ? 0 : cex);
+#pragma unroll
+            for (int b = 0; b < 4; b++) {
+                const int i = 4 * q + b;
+                sidx += T.ef[hr][i] != 0u;
+                T.seg[hr][i] = sidx;
+            }
+            cnt_before += __shfl_sync(0xffffffffu, cinc, (lane & ~3) | 3);
+            run = max(run, __shfl_sync(0xffffffffu, inc, (lane & ~3) | 3));
+        }
+        m[hr] = run;
+        T.nrec[hr] = cnt_before;
+    }
 }
 
+template <bool WIDE>
 __global__ void __launch_bounds__(AM_THREADS, 1)
 k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restrict__ kv_g,
                 const int *__restrict__ chunk_row0, const int *__restrict__ chunk_len, int n_heads,
@@ -96,28 +187,38 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
     const int c = blockIdx.x;
     const int r0 = chunk_row0[c], n = chunk_len[c];
     const int npad = (n + 31) & ~31;
-    const int vt_ld = npad + 16;   // V^T row stride: 16-byte pad spreads the 8 dims of a fragment over banks
-    uint8_t *ks = smem;                                   // [npad][64] swizzled
-    uint8_t *vt = smem + npad * 64;                       // [64][vt_ld]
+    const int vt_ld = ((npad + 127) & ~127) + 32;   // 8 dims of a fragment land on distinct banks
+    uint8_t *ks = smem;                              // [npad][64], dims permuted per thread quarter
+    uint8_t *vt = ks + npad * 64;                    // [64][vt_ld], keys permuted per 32-key tile
     uint16_t *lut4k = reinterpret_cast<uint16_t *>(vt + 64 * vt_ld);
+    uint8_t *wsm = reinterpret_cast<uint8_t *>(lut4k + 4096);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, t = lane & 3;
+    int *vst = reinterpret_cast<int *>(wsm + warp * AM_WARP_SMEM);   // [16][64] folded state
+    int *segbuf = vst + 16 * 64;                                     // [16][64] segment sums
+    uint32_t *rec_e = reinterpret_cast<uint32_t *>(segbuf + 16 * 64);  // [16][32]
+    int *nrec_s = reinterpret_cast<int *>(rec_e + 16 * 32);          // [16]
+    uint32_t *s_s = reinterpret_cast<uint32_t *>(nrec_s + 16);       // [16] final s (low 32 bits)
 
     for (int i = tid; i < 4096 / 8; i += AM_THREADS)
         reinterpret_cast<uint4 *>(lut4k)[i] = reinterpret_cast<const uint4 *>(lut4k_g)[i];
-    // K (rotated) rows -> swizzled smem; V -> transposed smem.  Rows >= n are zero.
-    for (int i = tid; i < npad * 4; i += AM_THREADS) {
-        int key = i >> 2, ch = i & 3;
-        uint4 kw = make_uint4(0, 0, 0, 0);
-        if (key < n) kw = *reinterpret_cast<const uint4 *>(kv_g + (size_t)(r0 + key) * 128 + ch * 16);
-        *reinterpret_cast<uint4 *>(ks + key * 64 + ((ch ^ ((key >> 2) & 3)) * 16)) = kw;
-    }
+    // K row layout: bytes [16t' + 4k + b] = dim 16k + 4t' + b, so thread t reads its
+    // four B words (dims 4t, 16+4t, 32+4t, 48+4t) as one 16-byte load.
     for (int i = tid; i < npad * 16; i += AM_THREADS) {
-        int key = i >> 4, q4 = i & 15;   // dims 4*q4 .. 4*q4+3 of key
-        uint32_t v = 0;
-        if (key < n) v = *reinterpret_cast<const uint32_t *>(kv_g + (size_t)(r0 + key) * 128 + 64 + 4 * q4);
+        const int key = i >> 4, wk = i & 15;   // source word: dims 4*wk .. 4*wk+3
+        uint32_t v = 0, kw = 0;
+        if (key < n) {
+            const int8_t *src = kv_g + (size_t)(r0 + key) * 128;
+            kw = *reinterpret_cast<const uint32_t *>(src + 4 * wk);
+            v = *reinterpret_cast<const uint32_t *>(src + 64 + 4 * wk);
+        }
+        const int kq = wk >> 2, tq = wk & 3;   // dims 16*kq + 4*tq ..
+        *reinterpret_cast<uint32_t *>(ks + key * 64 + 16 * tq + 4 * kq) = kw;
+        // V^T: tile position of key: keys 4u..4u+3 -> 8u + 0..3, keys 16+4u.. -> 8u + 4..7
+        const int kt = key & 31;
+        const int pos = (key & ~31) + 8 * ((kt & 15) >> 2) + 4 * (kt >> 4) + (kt & 3);
 #pragma unroll
-        for (int b = 0; b < 4; b++) vt[(4 * q4 + b) * vt_ld + key] = (uint8_t)(v >> (8 * b));
+        for (int b = 0; b < 4; b++) vt[(4 * wk + b) * vt_ld + pos] = (uint8_t)(v >> (8 * b));
     }
     if (tid == 0) task_ctr = 0;
     __syncthreads();
@@ -135,6 +236,7 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
         const int p0 = rb * 16;
         const int prow[2] = {p0 + g, p0 + g + 8};
         const int p_last = min(p0 + 15, n - 1);
+        const bool full_rows = p0 + 15 < n;
         const int mult = score_mult[h];
 
         // Q fragments with RoPE (attention.rs:53-83); pairs (i, i+32) live in kk = 0 / 1
@@ -162,19 +264,17 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
                     lo[k] |= (uint32_t)(uint8_t)xr << (8 * b);
                     hi[k] |= (uint32_t)(uint8_t)yr << (8 * b);
                 }
-            // kk = 0: dims 0..31 -> a0/a1 = dims 4t.., a2/a3 = dims 16+4t..; kk = 1: +32
             qa[0][hr] = lo[0];
             qa[0][hr + 2] = lo[1];
             qa[1][hr] = hi[0];
             qa[1][hr + 2] = hi[1];
         }
 
-        // per-row state, replicated over the quad
+        // per-row running max and weight sums, replicated over the quad
         int m[2] = {INT32_MIN, INT32_MIN};
         unsigned long long s_state[2] = {0, 0};
         uint32_t s_seg[2] = {0, 0};
         if (sink_key != nullptr) {   // attention.rs:211-224
-            // sink score of each row: dot(q_rot, sink) via the same fragments
             int accs[4] = {0, 0, 0, 0};
 #pragma unroll
             for (int kk = 0; kk < 2; kk++) {
@@ -182,150 +282,93 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
                 uint32_t b1 = *reinterpret_cast<const uint32_t *>(sink_key + 32 * kk + 16 + 4 * t);
                 mma_s8s8(accs, qa[kk], b0, b1);   // every B column is the sink key
             }
-            m[0] = score_from_dot(accs[0], mult);
-            m[1] = score_from_dot(accs[2], mult);
+            m[0] = score_from_dot<true>(accs[0], mult);
+            m[1] = score_from_dot<true>(accs[2], mult);
             s_state[0] = s_state[1] = 65535ull;
         }
-        uint32_t vst[2][8][2];
+        for (int i = lane; i < 16 * 64; i += 32) vst[i] = 0;
         int hiacc[8][4], loacc[8][4];
 #pragma unroll
         for (int jd = 0; jd < 8; jd++)
 #pragma unroll
             for (int k = 0; k < 4; k++) { hiacc[jd][k] = 0; loacc[jd][k] = 0; }
-#pragma unroll
-        for (int hr = 0; hr < 2; hr++)
-#pragma unroll
-            for (int jd = 0; jd < 8; jd++) { vst[hr][jd][0] = 0; vst[hr][jd][1] = 0; }
 
         for (int kb = 0; kb <= p_last; kb += 32) {
             // ---- S = Q K^T over 32 keys (permuted columns) ----
             int sacc[4][4];
 #pragma unroll
-            for (int j = 0; j < 4; j++)
-#pragma unroll
-                for (int k = 0; k < 4; k++) sacc[j][k] = 0;
-#pragma unroll
-            for (int kk = 0; kk < 2; kk++)
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    const int key = kb + perm_key(8 * j + g);
-                    uint32_t b0 = k_word(ks, key, 32 * kk + 4 * t);
-                    uint32_t b1 = k_word(ks, key, 32 * kk + 16 + 4 * t);
-                    mma_s8s8(sacc[j], qa[kk], b0, b1);
-                }
-            // V^T fragments for this tile (reused by every pass)
-            uint32_t bv[8][2];
-#pragma unroll
-            for (int jd = 0; jd < 8; jd++) {
-                const uint8_t *row = vt + (8 * jd + g) * vt_ld + kb + 4 * t;
-                bv[jd][0] = *reinterpret_cast<const uint32_t *>(row);
-                bv[jd][1] = *reinterpret_cast<const uint32_t *>(row + 16);
+            for (int j = 0; j < 4; j++) {
+                sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0;
+                const uint4 kw = *reinterpret_cast<const uint4 *>(ks + (kb + perm_key(8 * j + g)) * 64 + 16 * t);
+                mma_s8s8(sacc[j], qa[0], kw.x, kw.y);
+                mma_s8s8(sacc[j], qa[1], kw.z, kw.w);
             }
+            uint2 bv[8];
+#pragma unroll
+            for (int jd = 0; jd < 8; jd++)
+                bv[jd] = *reinterpret_cast<const uint2 *>(vt + (8 * jd + g) * vt_ld + kb + 8 * t);
 
-            // ---- scores, prefix max, records, weights (entry i: key kb + 16*(i>>2) + 4t + (i&3)) ----
-            uint32_t w[2][8], ef[2][8];
-            uint32_t recmask[2] = {0, 0};
-            int seg[2][8];
-            int nrec[2];
+            Tile T;
+            if (!full_rows || kb + 31 > p0)
+                tile_softmax<true, WIDE>(sacc, kb, prow, n, mult, t, lane, m, lut4k, c8, T);
+            else
+                tile_softmax<false, WIDE>(sacc, kb, prow, n, mult, t, lane, m, lut4k, c8, T);
+            const int maxrec = (int)__reduce_max_sync(0xffffffffu, (unsigned)max(T.nrec[0], T.nrec[1]));
+            if (maxrec > 0) {
+                // publish each row's record factors by segment, and its record count
 #pragma unroll
-            for (int hr = 0; hr < 2; hr++) {
-                int sc[8];
+                for (int hr = 0; hr < 2; hr++) {
+                    const int row = g + 8 * hr;
 #pragma unroll
-                for (int i = 0; i < 8; i++) {
-                    const int q = i >> 2, b = i & 3;
-                    const int j = 2 * q + (b >> 1), e = b & 1;
-                    const int key = kb + 16 * q + 4 * t + b;
-                    const bool valid = key <= prow[hr] && prow[hr] < n;
-                    sc[i] = valid ? score_from_dot(sacc[j][2 * hr + e], mult) : INT32_MIN;
+                    for (int i = 0; i < 8; i++)
+                        if (T.ef[hr][i]) rec_e[row * 32 + T.seg[hr][i] - 1] = T.ef[hr][i];
+                    if (t == 0) nrec_s[row] = T.nrec[hr];
                 }
-                int run = m[hr];
-                int cnt_before = 0;
-#pragma unroll
-                for (int q = 0; q < 2; q++) {
-                    int L[4];
-                    L[0] = sc[4 * q];
-#pragma unroll
-                    for (int b = 1; b < 4; b++) L[b] = max(L[b - 1], sc[4 * q + b]);
-                    int inc = L[3];
-                    int u = __shfl_up_sync(0xffffffffu, inc, 1, 4);
-                    if (t >= 1) inc = max(inc, u);
-                    u = __shfl_up_sync(0xffffffffu, inc, 2, 4);
-                    if (t >= 2) inc = max(inc, u);
-                    int excl = __shfl_up_sync(0xffffffffu, inc, 1, 4);
-                    const int base = t == 0 ? run : max(run, excl);
-                    int prevmax = base;
-                    int lrec = 0;
-#pragma unroll
-                    for (int b = 0; b < 4; b++) {
-                        const int i = 4 * q + b;
-                        const int key = kb + 16 * q + 4 * t + b;
-                        const bool valid = key <= prow[hr] && prow[hr] < n;
-                        const int pm = max(base, L[b]);
-                        const bool rec = valid && sc[i] > prevmax;
-                        w[hr][i] = valid ? exp_attn((int)((uint32_t)sc[i] - (uint32_t)pm), lut4k, c8) : 0u;
-                        // record flag 0x10000 | rescale factor, or 0x20000 when the previous max
-                        // is still INT32_MIN: the reference then keeps its sums unscaled
-                        ef[hr][i] = !rec ? 0u
-                                    : prevmax == INT32_MIN
-                                        ? 0x20000u
-                                        : 0x10000u | exp_attn((int)((uint32_t)prevmax - (uint32_t)sc[i]), lut4k, c8);
-                        if (rec) { recmask[hr] |= 1u << i; lrec++; }
-                        prevmax = pm;
-                    }
-                    // segment index of each entry: records at or before it in this tile
-                    int cinc = lrec;
-                    int cu = __shfl_up_sync(0xffffffffu, cinc, 1, 4);
-                    if (t >= 1) cinc += cu;
-                    cu = __shfl_up_sync(0xffffffffu, cinc, 2, 4);
-                    if (t >= 2) cinc += cu;
-                    int cex = __shfl_up_sync(0xffffffffu, cinc, 1, 4);
-                    int sidx = cnt_before + (t == 0 ? 0 : cex);
-#pragma unroll
-                    for (int b = 0; b < 4; b++) {
-                        const int i = 4 * q + b;
-                        if ((recmask[hr] >> i) & 1u) sidx++;
-                        seg[hr][i] = sidx;
-                    }
-                    cnt_before += __shfl_sync(0xffffffffu, cinc, (lane & ~3) | 3);
-                    run = max(run, __shfl_sync(0xffffffffu, inc, (lane & ~3) | 3));
-                }
-                m[hr] = run;
-                nrec[hr] = cnt_before;
+                __syncwarp();
             }
-            const int passes = 1 + __reduce_max_sync(0xffffffffu, (unsigned)max(nrec[0], nrec[1]));
-
-            for (int pass = 0; pass < passes; pass++) {
+            for (int pass = 0; pass <= maxrec; pass++) {
                 if (pass > 0) {
+                    // rows with a pass-th record: hand their segment sums to the warp
 #pragma unroll
                     for (int hr = 0; hr < 2; hr++) {
-                        uint32_t cand = 0;
-#pragma unroll
-                        for (int i = 0; i < 8; i++)
-                            if (((recmask[hr] >> i) & 1u) && seg[hr][i] == pass) cand = ef[hr][i];
-                        cand = quad_or(cand);
-                        if (cand) {   // fold exactly as the reference rescales (attention.rs:248-263)
-                            const bool scale = (cand & 0x20000u) == 0;
-                            const unsigned long long e = cand & 0xFFFFu;
+                        if (T.nrec[hr] >= pass) {
+                            const int row = g + 8 * hr;
+                            const uint32_t f = rec_e[row * 32 + pass - 1];
                             const unsigned long long stot = s_state[hr] + s_seg[hr];
-                            s_state[hr] = scale ? (stot * e + 0x8000ull) >> 16 : stot;
+                            s_state[hr] = (f & 0x20000u) ? stot : (stot * (f & 0xFFFFu) + 0x8000ull) >> 16;
                             s_seg[hr] = 0;
 #pragma unroll
-                            for (int jd = 0; jd < 8; jd++)
-#pragma unroll
-                                for (int k = 0; k < 2; k++) {
-                                    uint32_t x = vst[hr][jd][k] + ((uint32_t)hiacc[jd][2 * hr + k] << 8) +
-                                                 (uint32_t)loacc[jd][2 * hr + k];
-                                    if (scale) {
-                                        long long pr = (long long)(int)x * (long long)e;
-                                        pr += pr >= 0 ? (1ll << 15) : -(1ll << 15);
-                                        x = (uint32_t)(int)(pr >> 16);
-                                    }
-                                    vst[hr][jd][k] = x;
-                                    hiacc[jd][2 * hr + k] = 0;
-                                    loacc[jd][2 * hr + k] = 0;
-                                }
+                            for (int jd = 0; jd < 8; jd++) {
+                                int2 v2;
+                                v2.x = (int)(((uint32_t)hiacc[jd][2 * hr] << 8) + (uint32_t)loacc[jd][2 * hr]);
+                                v2.y = (int)(((uint32_t)hiacc[jd][2 * hr + 1] << 8) + (uint32_t)loacc[jd][2 * hr + 1]);
+                                *reinterpret_cast<int2 *>(segbuf + row * 64 + 8 * jd + 2 * t) = v2;
+                                hiacc[jd][2 * hr] = hiacc[jd][2 * hr + 1] = 0;
+                                loacc[jd][2 * hr] = loacc[jd][2 * hr + 1] = 0;
+                            }
                         }
                     }
+                    __syncwarp();
+                    // the whole warp folds each such row, 2 dims per lane (attention.rs:252-263)
+                    for (int row = 0; row < 16; row++) {
+                        if (nrec_s[row] < pass) continue;
+                        const uint32_t f = rec_e[row * 32 + pass - 1];
+                        const long long e = f & 0xFFFFu;
+                        int2 sv = *reinterpret_cast<int2 *>(vst + row * 64 + 2 * lane);
+                        const int2 gv = *reinterpret_cast<const int2 *>(segbuf + row * 64 + 2 * lane);
+                        uint32_t x0 = (uint32_t)sv.x + (uint32_t)gv.x, x1 = (uint32_t)sv.y + (uint32_t)gv.y;
+                        if (!(f & 0x20000u)) {
+                            long long p0_ = (long long)(int)x0 * e, p1_ = (long long)(int)x1 * e;
+                            p0_ += p0_ >= 0 ? (1ll << 15) : -(1ll << 15);
+                            p1_ += p1_ >= 0 ? (1ll << 15) : -(1ll << 15);
+                            x0 = (uint32_t)(int)(p0_ >> 16);
+                            x1 = (uint32_t)(int)(p1_ >> 16);
+                        }
+                        sv.x = (int)x0;
+                        sv.y = (int)x1;
+                        *reinterpret_cast<int2 *>(vst + row * 64 + 2 * lane) = sv;
+                    }
+                    __syncwarp();
                 }
                 // P fragments of this pass: weights of keys in segment `pass`
                 uint32_t ahi[4], alo[4];
@@ -334,24 +377,24 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
                     uint32_t ssum = 0;
 #pragma unroll
                     for (int q = 0; q < 2; q++) {
-                        uint32_t ph = 0, pl = 0;
+                        uint32_t wv[4];
 #pragma unroll
                         for (int b = 0; b < 4; b++) {
                             const int i = 4 * q + b;
-                            const uint32_t wv = seg[hr][i] == pass ? w[hr][i] : 0u;
-                            ssum += wv;
-                            pl |= (wv & 0xFFu) << (8 * b);
-                            ph |= (wv >> 8) << (8 * b);
+                            wv[b] = (maxrec == 0 || T.seg[hr][i] == pass) ? T.w[hr][i] : 0u;
+                            ssum += wv[b];
                         }
-                        alo[hr + 2 * q] = pl;
-                        ahi[hr + 2 * q] = ph;
+                        const uint32_t x01 = prmt(wv[0], wv[1], 0x5140u);   // lo0 lo1 hi0 hi1
+                        const uint32_t x23 = prmt(wv[2], wv[3], 0x5140u);
+                        alo[hr + 2 * q] = prmt(x01, x23, 0x5410u);
+                        ahi[hr + 2 * q] = prmt(x01, x23, 0x7632u);
                     }
                     s_seg[hr] += quad_sum(ssum);
                 }
 #pragma unroll
                 for (int jd = 0; jd < 8; jd++) {
-                    mma_u8s8(hiacc[jd], ahi, bv[jd][0], bv[jd][1]);
-                    mma_u8s8(loacc[jd], alo, bv[jd][0], bv[jd][1]);
+                    mma_u8s8(hiacc[jd], ahi, bv[jd].x, bv[jd].y);
+                    mma_u8s8(loacc[jd], alo, bv[jd].x, bv[jd].y);
                 }
             }
         }
@@ -359,46 +402,68 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
         // output: clamp(round_half_even(vacc / s)) (attention.rs:279-284)
 #pragma unroll
         for (int hr = 0; hr < 2; hr++) {
-            const int p = prow[hr];
-            if (p >= n) continue;
-            const unsigned long long s = s_state[hr] + s_seg[hr];
-            const unsigned long long den = s == 0 ? 1ull : s;
-            int8_t *o = out + (size_t)(r0 + p) * ldo + h * 64 + 2 * t;
+            const int row = g + 8 * hr;
 #pragma unroll
             for (int jd = 0; jd < 8; jd++) {
-                uint32_t x0 = vst[hr][jd][0] + ((uint32_t)hiacc[jd][2 * hr] << 8) + (uint32_t)loacc[jd][2 * hr];
-                uint32_t x1 = vst[hr][jd][1] + ((uint32_t)hiacc[jd][2 * hr + 1] << 8) + (uint32_t)loacc[jd][2 * hr + 1];
-                uint16_t pk = (uint16_t)(uint8_t)clamp127(div_rne_s32_u64((int)x0, den)) |
-                              ((uint16_t)(uint8_t)clamp127(div_rne_s32_u64((int)x1, den)) << 8);
-                *reinterpret_cast<uint16_t *>(o + 8 * jd) = pk;
+                int2 v2;
+                v2.x = (int)(((uint32_t)hiacc[jd][2 * hr] << 8) + (uint32_t)loacc[jd][2 * hr]);
+                v2.y = (int)(((uint32_t)hiacc[jd][2 * hr + 1] << 8) + (uint32_t)loacc[jd][2 * hr + 1]);
+                *reinterpret_cast<int2 *>(segbuf + row * 64 + 8 * jd + 2 * t) = v2;
+            }
+            if (t == 0) {
+                const unsigned long long s = s_state[hr] + s_seg[hr];
+                s_s[row] = s == 0 ? 1u : (uint32_t)min(s, 0xFFFFFFFFull);
+                nrec_s[row] = s > 0xFFFFFFFFull;   // s beyond 32 bits: every quotient is 0
             }
         }
+        __syncwarp();
+        for (int row = 0; row < 16; row++) {
+            const int p = p0 + row;
+            if (p >= n) break;
+            const int2 sv = *reinterpret_cast<const int2 *>(vst + row * 64 + 2 * lane);
+            const int2 gv = *reinterpret_cast<const int2 *>(segbuf + row * 64 + 2 * lane);
+            const unsigned long long den = nrec_s[row] ? 0x100000000ull : s_s[row];
+            const int x0 = (int)((uint32_t)sv.x + (uint32_t)gv.x), x1 = (int)((uint32_t)sv.y + (uint32_t)gv.y);
+            const uint16_t pk = (uint16_t)(uint8_t)clamp127(div_rne_s32_u64(x0, den)) |
+                                ((uint16_t)(uint8_t)clamp127(div_rne_s32_u64(x1, den)) << 8);
+            *reinterpret_cast<uint16_t *>(out + (size_t)(r0 + p) * ldo + h * 64 + 2 * lane) = pk;
+        }
+        __syncwarp();
     }
 }
 
 }  // namespace
 
 size_t attention_mma_smem(int max_len) {
-    int npad = (max_len + 31) & ~31;
-    return (size_t)npad * 64 + (size_t)64 * (npad + 16) + 4096 * 2;
+    const int npad = (max_len + 31) & ~31;
+    const int vt_ld = ((npad + 127) & ~127) + 32;
+    return (size_t)npad * 64 + (size_t)64 * vt_ld + 4096 * 2 + (size_t)AM_WARPS * AM_WARP_SMEM;
 }
 
 bool attention_mma_fits(int max_len) { return max_len <= AM_MAX_KEYS; }
 
 void attention_mma_init() {
-    cudaFuncSetAttribute(k_attention_mma, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(k_attention_mma<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)attention_mma_smem(AM_MAX_KEYS));
+    cudaFuncSetAttribute(k_attention_mma<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)attention_mma_smem(AM_MAX_KEYS));
 }
 
 void launch_attention_mma(const int8_t *qkv, int ldq, const int8_t *kv, const int *chunk_row0,
                           const int *chunk_len, int n_chunks, int max_len, int n_heads,
                           const int32_t *score_mult, const int8_t *sink_key, const int16_t *rope_cos,
-                          const int16_t *rope_sin, const uint16_t *lut4k, int8_t *out, int ldo,
-                          cudaStream_t st) {
+                          const int16_t *rope_sin, const uint16_t *lut4k, bool wide_mult, int8_t *out,
+                          int ldo, cudaStream_t st) {
     if (n_chunks == 0) return;
-    k_attention_mma<<<n_chunks, AM_THREADS, attention_mma_smem(max_len), st>>>(
-        qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin, lut4k,
-        out, ldo);
+    const size_t smem = attention_mma_smem(max_len);
+    if (wide_mult)
+        k_attention_mma<true><<<n_chunks, AM_THREADS, smem, st>>>(
+            qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
+            lut4k, out, ldo);
+    else
+        k_attention_mma<false><<<n_chunks, AM_THREADS, smem, st>>>(
+            qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
+            lut4k, out, ldo);
 }
 
 }  // namespace czg

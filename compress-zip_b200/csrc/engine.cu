@@ -49,6 +49,7 @@ struct LayerDev {
     int8_t *qkv_w = nullptr, *out_w = nullptr, *up_w = nullptr, *down_w = nullptr;
     int32_t *score_mult = nullptr;
     int8_t *sink_key = nullptr;
+    bool wide_mult = false;   // some |score_mult| >= 2^28: scores may saturate int32
     int qkv_mult = 1, out_mult = 1, up_mult = 1, down_mult = 1;
     int qkv_shift = 0, out_shift = 0, up_shift = 0, down_shift = 0;
 };
@@ -324,6 +325,11 @@ int load_model(czg_ctx *c, const uint8_t *bytes, size_t len) {
         if (!upload(c, &L.down_w, t->data, (size_t)d * dff)) return CZG_E_DEVICE;
         if ((st = need(c, f, p + "attn.score_mult", "I32", H, &t))) return st;
         if (!upload(c, &L.score_mult, t->data, (size_t)H * 4)) return CZG_E_DEVICE;
+        for (int hh = 0; hh < H; hh++) {
+            int32_t sm;
+            memcpy(&sm, t->data + 4 * hh, 4);
+            if (sm >= (1 << 28) || sm <= -(1 << 28)) L.wide_mult = true;
+        }
         if (const TensorRef *sk = find(f, p + "attn.sink_key")) {
             if (sk->dtype != "I8" || sk->numel() < 64 || sk->nbytes < 64)
                 return fail(c, CZG_E_MODEL, "attn.sink_key must be I8[64]");
@@ -420,7 +426,7 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
             if (attention_mma_fits(max_len) && !c->scalar_attention)
                 launch_attention_mma(c->qkv, d + 128, c->kv, c->chunk_row0, c->chunk_len, nc, max_len, H,
                                      L.score_mult, L.sink_key, c->rope_cos, c->rope_sin, c->lut4k,
-                                     c->attn, d, st);
+                                     L.wide_mult, c->attn, d, st);
             else
                 launch_attention(c->qkv, d + 128, c->kv, c->chunk_row0, c->chunk_len, nc, max_len, H,
                                  L.score_mult, L.sink_key, c->rope_cos, c->rope_sin, c->lut, c->attn, d, st);

@@ -42,8 +42,8 @@ void attention_mma_init();
 void launch_attention_mma(const int8_t *qkv, int ldq, const int8_t *kv, const int *chunk_row0,
                           const int *chunk_len, int n_chunks, int max_len, int n_heads,
                           const int32_t *score_mult, const int8_t *sink_key, const int16_t *rope_cos,
-                          const int16_t *rope_sin, const uint16_t *lut4k, int8_t *out, int ldo,
-                          cudaStream_t st);
+                          const int16_t *rope_sin, const uint16_t *lut4k, bool wide_mult, int8_t *out,
+                          int ldo, cudaStream_t st);
 // attention.cu: one CTA per chunk; rows of chunk c are chunk_row0[c] ..+chunk_len[c]
 void launch_attention(const int8_t *qkv, int ldq, const int8_t *kv, const int *chunk_row0,
                       const int *chunk_len, int n_chunks, int max_len, int n_heads,
