@@ -33,7 +33,8 @@ namespace {
 constexpr int AM_THREADS = 256;
 constexpr int AM_WARPS = AM_THREADS / 32;
 constexpr int AM_MAX_KEYS = 1024;
-constexpr int AM_WARP_SMEM = 16 * 64 * 4 * 2 + 16 * 32 * 4 + 16 * 4 * 2;   // vst, segbuf, rec_e, nrec, s
+constexpr int AM_ROW = 72;   // words per row of the per-warp state buffers (bank-spread)
+constexpr int AM_WARP_SMEM = 16 * AM_ROW * 4 * 2 + 16 * 32 * 4 + 16 * 4 * 2;   // vst, segbuf, rec_e, nrec, s
 
 __device__ __forceinline__ void mma_s8s8(int (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
     asm volatile(
@@ -64,7 +65,9 @@ __device__ __forceinline__ uint32_t exp_attn(int diff, const uint16_t *lut4k, ui
     if (diff >= 0) return 65535u;
     uint32_t neg = 0u - (uint32_t)diff;
     uint32_t t = __umulhi(neg, c8) + ((neg * c8) >> 31);
-    return t < 4096u ? (uint32_t)lut4k[t] : 1u;
+    uint32_t w = 1u;
+    if (t < 4096u) w = __ldg(lut4k + t);   // only lanes near the running max touch the table
+    return w;
 }
 
 // score = round_even(round_even(dot / 4) * mult / 2^15) saturated to int32
@@ -80,12 +83,6 @@ __device__ __forceinline__ int score_from_dot(int dot, int mult) {
     return (int)s;
 }
 
-__device__ __forceinline__ uint32_t quad_sum(uint32_t v) {
-    v += __shfl_xor_sync(0xffffffffu, v, 1);
-    v += __shfl_xor_sync(0xffffffffu, v, 2);
-    return v;
-}
-
 // key (within a 32-key tile) of QK accumulator column / B row n = 8j + r
 __device__ __forceinline__ int perm_key(int n) {
     int j = n >> 3, r = n & 7;
@@ -93,14 +90,13 @@ __device__ __forceinline__ int perm_key(int n) {
 }
 
 struct Tile {
-    // per row half: weights, record factor flags, segment of each entry
-    uint32_t w[2][8];
-    uint32_t ef[2][8];
-    int seg[2][8];
-    int nrec[2];
+    uint32_t w[2][8];     // weights of each row half's 8 entries
+    uint32_t ef[2][8];    // 0, or record flag | rescale factor
+    int lrec[2][2];       // records of this thread per row half and 16-key half
+    int nrec[2];          // records of the row in this tile (quad total)
 };
 
-// Scores, prefix max, records, weights and segments of one 32-key tile.
+// Scores, prefix max, records and weights of one 32-key tile.
 // Entry i of a row half is key kb + 16*(i>>2) + 4t + (i&3).
 template <bool MASKED, bool WIDE>
 __device__ __forceinline__ void tile_softmax(const int (&sacc)[4][4], int kb, const int (&prow)[2], int n,
@@ -118,7 +114,7 @@ __device__ __forceinline__ void tile_softmax(const int (&sacc)[4][4], int kb, co
             sc[i] = valid ? score_from_dot<WIDE>(sacc[j][2 * hr + e], mult) : INT32_MIN;
         }
         int run = m[hr];
-        int cnt_before = 0;
+        int total = 0;
 #pragma unroll
         for (int q = 0; q < 2; q++) {
             int L[4];
@@ -154,25 +150,56 @@ __device__ __forceinline__ void tile_softmax(const int (&sacc)[4][4], int kb, co
                 T.ef[hr][i] = f;
                 prevmax = pm;
             }
-            int cinc = lrec;
+            T.lrec[hr][q] = lrec;
+            total += lrec;
+            run = max(run, __shfl_sync(0xffffffffu, inc, (lane & ~3) | 3));
+        }
+        m[hr] = run;
+        total += __shfl_xor_sync(0xffffffffu, total, 1);
+        total += __shfl_xor_sync(0xffffffffu, total, 2);
+        T.nrec[hr] = total;
+    }
+}
+
+// Segment of each entry (records at or before it in key order within the tile),
+// packed one byte per entry in A-fragment word order (word hr + 2q, byte b); the
+// record factors are published to rec_e[row][segment - 1].
+__device__ __forceinline__ void tile_segments(const Tile &T, int t, int g, uint32_t *rec_e, int *nrec_s,
+                                              uint32_t (&segw)[4]) {
+#pragma unroll
+    for (int hr = 0; hr < 2; hr++) {
+        const int row = g + 8 * hr;
+        int before = 0;
+#pragma unroll
+        for (int q = 0; q < 2; q++) {
+            int cinc = T.lrec[hr][q];
             int cu = __shfl_up_sync(0xffffffffu, cinc, 1, 4);
             if (t >= 1) cinc += cu;
             cu = __shfl_up_sync(0xffffffffu, cinc, 2, 4);
             if (t >= 2) cinc += cu;
-            const int cex = __shfl_up_sync(0xffffffffu, cinc, 1, 4);
-            int sidx = cnt_before + (t == 0 ? 0 : cex);
+            int sidx = before + cinc - T.lrec[hr][q];
+            uint32_t word = 0;
 #pragma unroll
             for (int b = 0; b < 4; b++) {
                 const int i = 4 * q + b;
-                sidx += T.ef[hr][i] != 0u;
-                T.seg[hr][i] = sidx;
+                if (T.ef[hr][i]) {
+                    sidx++;
+                    rec_e[row * 32 + sidx - 1] = T.ef[hr][i];
+                }
+                word |= (uint32_t)sidx << (8 * b);
             }
-            cnt_before += __shfl_sync(0xffffffffu, cinc, (lane & ~3) | 3);
-            run = max(run, __shfl_sync(0xffffffffu, inc, (lane & ~3) | 3));
+            segw[hr + 2 * q] = word;
+            before += __shfl_sync(0xffffffffu, cinc, (threadIdx.x & 31 & ~3) | 3);
         }
-        m[hr] = run;
-        T.nrec[hr] = cnt_before;
+        if (t == 0) nrec_s[row] = T.nrec[hr];
     }
+}
+
+// 0xFF in each byte of x equal to q, else 0
+__device__ __forceinline__ uint32_t bytes_equal(uint32_t x, uint32_t q) {
+    const uint32_t y = x ^ (q * 0x01010101u);
+    const uint32_t nz = ((y & 0x7F7F7F7Fu) + 0x7F7F7F7Fu) | y;   // bit 7 set in non-zero bytes
+    return prmt(~nz & 0x80808080u, 0u, 0xBA98u);                    // replicate bit 7 over the byte
 }
 
 template <bool WIDE>
@@ -190,18 +217,16 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
     const int vt_ld = ((npad + 127) & ~127) + 32;   // 8 dims of a fragment land on distinct banks
     uint8_t *ks = smem;                              // [npad][64], dims permuted per thread quarter
     uint8_t *vt = ks + npad * 64;                    // [64][vt_ld], keys permuted per 32-key tile
-    uint16_t *lut4k = reinterpret_cast<uint16_t *>(vt + 64 * vt_ld);
-    uint8_t *wsm = reinterpret_cast<uint8_t *>(lut4k + 4096);
+    uint8_t *wsm = vt + 64 * vt_ld;
+    const uint16_t *lut4k = lut4k_g;   // 8 KB, stays in L1
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, t = lane & 3;
-    int *vst = reinterpret_cast<int *>(wsm + warp * AM_WARP_SMEM);   // [16][64] folded state
-    int *segbuf = vst + 16 * 64;                                     // [16][64] segment sums
-    uint32_t *rec_e = reinterpret_cast<uint32_t *>(segbuf + 16 * 64);  // [16][32]
+    int *vst = reinterpret_cast<int *>(wsm + warp * AM_WARP_SMEM);   // [16][AM_ROW] folded state
+    int *segbuf = vst + 16 * AM_ROW;                                 // [16][AM_ROW] segment sums
+    uint32_t *rec_e = reinterpret_cast<uint32_t *>(segbuf + 16 * AM_ROW);  // [16][32]
     int *nrec_s = reinterpret_cast<int *>(rec_e + 16 * 32);          // [16]
     uint32_t *s_s = reinterpret_cast<uint32_t *>(nrec_s + 16);       // [16] final s (low 32 bits)
 
-    for (int i = tid; i < 4096 / 8; i += AM_THREADS)
-        reinterpret_cast<uint4 *>(lut4k)[i] = reinterpret_cast<const uint4 *>(lut4k_g)[i];
     // K row layout: bytes [16t' + 4k + b] = dim 16k + 4t' + b, so thread t reads its
     // four B words (dims 4t, 16+4t, 32+4t, 48+4t) as one 16-byte load.
     for (int i = tid; i < npad * 16; i += AM_THREADS) {
@@ -273,7 +298,7 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
         // per-row running max and weight sums, replicated over the quad
         int m[2] = {INT32_MIN, INT32_MIN};
         unsigned long long s_state[2] = {0, 0};
-        uint32_t s_seg[2] = {0, 0};
+        int sh[4] = {0, 0, 0, 0}, sl[4] = {0, 0, 0, 0};   // weight sums since the last fold
         if (sink_key != nullptr) {   // attention.rs:211-224
             int accs[4] = {0, 0, 0, 0};
 #pragma unroll
@@ -286,7 +311,7 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
             m[1] = score_from_dot<true>(accs[2], mult);
             s_state[0] = s_state[1] = 65535ull;
         }
-        for (int i = lane; i < 16 * 64; i += 32) vst[i] = 0;
+        for (int i = lane; i < 16 * AM_ROW; i += 32) vst[i] = 0;
         int hiacc[8][4], loacc[8][4];
 #pragma unroll
         for (int jd = 0; jd < 8; jd++)
@@ -313,49 +338,61 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
                 tile_softmax<true, WIDE>(sacc, kb, prow, n, mult, t, lane, m, lut4k, c8, T);
             else
                 tile_softmax<false, WIDE>(sacc, kb, prow, n, mult, t, lane, m, lut4k, c8, T);
-            const int maxrec = (int)__reduce_max_sync(0xffffffffu, (unsigned)max(T.nrec[0], T.nrec[1]));
-            if (maxrec > 0) {
-                // publish each row's record factors by segment, and its record count
+            // full P fragments (u8 halves of the weights)
+            uint32_t phi[4], plo[4];
 #pragma unroll
-                for (int hr = 0; hr < 2; hr++) {
-                    const int row = g + 8 * hr;
+            for (int hr = 0; hr < 2; hr++)
 #pragma unroll
-                    for (int i = 0; i < 8; i++)
-                        if (T.ef[hr][i]) rec_e[row * 32 + T.seg[hr][i] - 1] = T.ef[hr][i];
-                    if (t == 0) nrec_s[row] = T.nrec[hr];
+                for (int q = 0; q < 2; q++) {
+                    const uint32_t *wq = &T.w[hr][4 * q];
+                    const uint32_t x01 = prmt(wq[0], wq[1], 0x5140u);   // lo0 lo1 hi0 hi1
+                    const uint32_t x23 = prmt(wq[2], wq[3], 0x5140u);
+                    plo[hr + 2 * q] = prmt(x01, x23, 0x5410u);
+                    phi[hr + 2 * q] = prmt(x01, x23, 0x7632u);
                 }
+            const int maxrec = (int)__reduce_max_sync(0xffffffffu, (unsigned)max(T.nrec[0], T.nrec[1]));
+            uint32_t segw[4] = {0, 0, 0, 0};
+            if (maxrec > 0) {
+                tile_segments(T, t, g, rec_e, nrec_s, segw);
                 __syncwarp();
             }
             for (int pass = 0; pass <= maxrec; pass++) {
                 if (pass > 0) {
-                    // rows with a pass-th record: hand their segment sums to the warp
+                    // rows with a pass-th record hand their segment sums to the warp
 #pragma unroll
                     for (int hr = 0; hr < 2; hr++) {
                         if (T.nrec[hr] >= pass) {
                             const int row = g + 8 * hr;
                             const uint32_t f = rec_e[row * 32 + pass - 1];
-                            const unsigned long long stot = s_state[hr] + s_seg[hr];
+                            const unsigned long long stot = s_state[hr] +
+                                256ull * (uint32_t)sh[2 * hr] + (unsigned long long)(uint32_t)sl[2 * hr];
                             s_state[hr] = (f & 0x20000u) ? stot : (stot * (f & 0xFFFFu) + 0x8000ull) >> 16;
-                            s_seg[hr] = 0;
+                            sh[2 * hr] = sh[2 * hr + 1] = sl[2 * hr] = sl[2 * hr + 1] = 0;
 #pragma unroll
                             for (int jd = 0; jd < 8; jd++) {
                                 int2 v2;
                                 v2.x = (int)(((uint32_t)hiacc[jd][2 * hr] << 8) + (uint32_t)loacc[jd][2 * hr]);
                                 v2.y = (int)(((uint32_t)hiacc[jd][2 * hr + 1] << 8) + (uint32_t)loacc[jd][2 * hr + 1]);
-                                *reinterpret_cast<int2 *>(segbuf + row * 64 + 8 * jd + 2 * t) = v2;
+                                *reinterpret_cast<int2 *>(segbuf + row * AM_ROW + 8 * jd + 2 * t) = v2;
                                 hiacc[jd][2 * hr] = hiacc[jd][2 * hr + 1] = 0;
                                 loacc[jd][2 * hr] = loacc[jd][2 * hr + 1] = 0;
                             }
                         }
                     }
+                    const uint32_t fold0 = __ballot_sync(0xffffffffu, t == 0 && T.nrec[0] >= pass);
+                    const uint32_t fold1 = __ballot_sync(0xffffffffu, t == 0 && T.nrec[1] >= pass);
                     __syncwarp();
                     // the whole warp folds each such row, 2 dims per lane (attention.rs:252-263)
-                    for (int row = 0; row < 16; row++) {
-                        if (nrec_s[row] < pass) continue;
+                    uint32_t rows = 0;
+#pragma unroll
+                    for (int k = 0; k < 8; k++) rows |= (((fold0 >> (4 * k)) & 1u) << k) | (((fold1 >> (4 * k)) & 1u) << (k + 8));
+                    while (rows) {
+                        const int row = __ffs(rows) - 1;
+                        rows &= rows - 1;
                         const uint32_t f = rec_e[row * 32 + pass - 1];
                         const long long e = f & 0xFFFFu;
-                        int2 sv = *reinterpret_cast<int2 *>(vst + row * 64 + 2 * lane);
-                        const int2 gv = *reinterpret_cast<const int2 *>(segbuf + row * 64 + 2 * lane);
+                        int2 sv = *reinterpret_cast<int2 *>(vst + row * AM_ROW + 2 * lane);
+                        const int2 gv = *reinterpret_cast<const int2 *>(segbuf + row * AM_ROW + 2 * lane);
                         uint32_t x0 = (uint32_t)sv.x + (uint32_t)gv.x, x1 = (uint32_t)sv.y + (uint32_t)gv.y;
                         if (!(f & 0x20000u)) {
                             long long p0_ = (long long)(int)x0 * e, p1_ = (long long)(int)x1 * e;
@@ -366,31 +403,25 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
                         }
                         sv.x = (int)x0;
                         sv.y = (int)x1;
-                        *reinterpret_cast<int2 *>(vst + row * 64 + 2 * lane) = sv;
+                        *reinterpret_cast<int2 *>(vst + row * AM_ROW + 2 * lane) = sv;
                     }
                     __syncwarp();
                 }
-                // P fragments of this pass: weights of keys in segment `pass`
+                // P fragments of this pass: bytes of entries in segment `pass`
                 uint32_t ahi[4], alo[4];
+                if (maxrec == 0) {
 #pragma unroll
-                for (int hr = 0; hr < 2; hr++) {
-                    uint32_t ssum = 0;
+                    for (int a = 0; a < 4; a++) { ahi[a] = phi[a]; alo[a] = plo[a]; }
+                } else {
 #pragma unroll
-                    for (int q = 0; q < 2; q++) {
-                        uint32_t wv[4];
-#pragma unroll
-                        for (int b = 0; b < 4; b++) {
-                            const int i = 4 * q + b;
-                            wv[b] = (maxrec == 0 || T.seg[hr][i] == pass) ? T.w[hr][i] : 0u;
-                            ssum += wv[b];
-                        }
-                        const uint32_t x01 = prmt(wv[0], wv[1], 0x5140u);   // lo0 lo1 hi0 hi1
-                        const uint32_t x23 = prmt(wv[2], wv[3], 0x5140u);
-                        alo[hr + 2 * q] = prmt(x01, x23, 0x5410u);
-                        ahi[hr + 2 * q] = prmt(x01, x23, 0x7632u);
+                    for (int a = 0; a < 4; a++) {
+                        const uint32_t mk = bytes_equal(segw[a], (uint32_t)pass);
+                        ahi[a] = phi[a] & mk;
+                        alo[a] = plo[a] & mk;
                     }
-                    s_seg[hr] += quad_sum(ssum);
                 }
+                mma_u8s8(sh, ahi, 0x01010101u, 0x01010101u);   // weight sums (all-ones column)
+                mma_u8s8(sl, alo, 0x01010101u, 0x01010101u);
 #pragma unroll
                 for (int jd = 0; jd < 8; jd++) {
                     mma_u8s8(hiacc[jd], ahi, bv[jd].x, bv[jd].y);
@@ -408,10 +439,11 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
                 int2 v2;
                 v2.x = (int)(((uint32_t)hiacc[jd][2 * hr] << 8) + (uint32_t)loacc[jd][2 * hr]);
                 v2.y = (int)(((uint32_t)hiacc[jd][2 * hr + 1] << 8) + (uint32_t)loacc[jd][2 * hr + 1]);
-                *reinterpret_cast<int2 *>(segbuf + row * 64 + 8 * jd + 2 * t) = v2;
+                *reinterpret_cast<int2 *>(segbuf + row * AM_ROW + 8 * jd + 2 * t) = v2;
             }
             if (t == 0) {
-                const unsigned long long s = s_state[hr] + s_seg[hr];
+                const unsigned long long s = s_state[hr] + 256ull * (uint32_t)sh[2 * hr] +
+                                             (unsigned long long)(uint32_t)sl[2 * hr];
                 s_s[row] = s == 0 ? 1u : (uint32_t)min(s, 0xFFFFFFFFull);
                 nrec_s[row] = s > 0xFFFFFFFFull;   // s beyond 32 bits: every quotient is 0
             }
@@ -420,8 +452,8 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
         for (int row = 0; row < 16; row++) {
             const int p = p0 + row;
             if (p >= n) break;
-            const int2 sv = *reinterpret_cast<const int2 *>(vst + row * 64 + 2 * lane);
-            const int2 gv = *reinterpret_cast<const int2 *>(segbuf + row * 64 + 2 * lane);
+            const int2 sv = *reinterpret_cast<const int2 *>(vst + row * AM_ROW + 2 * lane);
+            const int2 gv = *reinterpret_cast<const int2 *>(segbuf + row * AM_ROW + 2 * lane);
             const unsigned long long den = nrec_s[row] ? 0x100000000ull : s_s[row];
             const int x0 = (int)((uint32_t)sv.x + (uint32_t)gv.x), x1 = (int)((uint32_t)sv.y + (uint32_t)gv.y);
             const uint16_t pk = (uint16_t)(uint8_t)clamp127(div_rne_s32_u64(x0, den)) |
@@ -437,7 +469,7 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
 size_t attention_mma_smem(int max_len) {
     const int npad = (max_len + 31) & ~31;
     const int vt_ld = ((npad + 127) & ~127) + 32;
-    return (size_t)npad * 64 + (size_t)64 * vt_ld + 4096 * 2 + (size_t)AM_WARPS * AM_WARP_SMEM;
+    return (size_t)npad * 64 + (size_t)64 * vt_ld + (size_t)AM_WARPS * AM_WARP_SMEM;
 }
 
 bool attention_mma_fits(int max_len) { return max_len <= AM_MAX_KEYS; }
