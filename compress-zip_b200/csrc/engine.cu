@@ -29,6 +29,7 @@ using namespace czg;
 void czg::kernels_init() {
     attention_init();
     attention_mma_init();
+    gemm_tc_init();
 }
 
 namespace {
@@ -52,6 +53,7 @@ struct LayerDev {
     bool wide_mult = false;   // some |score_mult| >= 2^28: scores may saturate int32
     int qkv_mult = 1, out_mult = 1, up_mult = 1, down_mult = 1;
     int qkv_shift = 0, out_shift = 0, up_shift = 0, down_shift = 0;
+    TcMatrix tm_qkv, tm_out, tm_up, tm_down;   // TMA descriptors of the weights
 };
 
 struct EvPair {
@@ -88,6 +90,9 @@ struct czg_ctx {
     uint32_t *lens = nullptr;
     uint64_t *slot_off = nullptr, *pack_off = nullptr, *chunk_tok0 = nullptr;
     int *chunk_row0 = nullptr, *chunk_len = nullptr;
+    // tcgen05 path: TMA descriptors of the GEMM A operands (wave buffers) and the head
+    bool use_tc = false;
+    TcMatrix tm_xn, tm_attn, tm_h, tm_head;
     // pinned host staging
     uint8_t *h_meta = nullptr;
     size_t h_meta_bytes = 0;
@@ -365,9 +370,32 @@ int alloc_workspace(czg_ctx *c, int rows, int chunks) {
               dalloc(c, &c->chunk_row0, (size_t)chunks) && dalloc(c, &c->chunk_len, (size_t)chunks) &&
               dalloc(c, &c->err_flag, 1);
     if (!ok) return CZG_E_DEVICE;
+    // tcgen05 GEMMs need K % 128 == 0 and N % 128 == 0 for every projection
+    const char *ge = getenv("CZG_GEMM");
+    c->use_tc = !(ge && std::string(ge) == "mma") && d % 128 == 0 && m.d_ff % 128 == 0 &&
+                tc_bn_for(d + 128) && tc_bn_for(d) && tc_bn_for(2 * m.d_ff) && tc_bn_for(c->vpad);
+    if (c->use_tc) {
+        bool ok = tc_make_matrix(c->tm_xn, c->xn, R, d, 128) && tc_make_matrix(c->tm_attn, c->attn, R, d, 128) &&
+                  tc_make_matrix(c->tm_h, c->hbuf, R, m.d_ff, 128) &&
+                  tc_make_matrix(c->tm_head, c->head_w, c->vpad, d, tc_bn_for(c->vpad));
+        for (auto &L : c->layers) {
+            ok = ok && tc_make_matrix(L.tm_qkv, L.qkv_w, d + 128, d, tc_bn_for(d + 128)) &&
+                 tc_make_matrix(L.tm_out, L.out_w, d, d, tc_bn_for(d)) &&
+                 tc_make_matrix(L.tm_up, L.up_w, 2 * m.d_ff, d, tc_bn_for(2 * m.d_ff)) &&
+                 tc_make_matrix(L.tm_down, L.down_w, d, m.d_ff, tc_bn_for(d));
+        }
+        if (!ok) c->use_tc = false;
+    }
     c->h_meta_bytes = (size_t)chunks * 32 + 64;
     if (!cuda_ok(c, cudaMallocHost(&c->h_meta, c->h_meta_bytes), "cudaMallocHost")) return CZG_E_DEVICE;
     return CZG_OK;
+}
+
+// One projection: tcgen05 path when available, else the mma.sync kernel.
+void gemm(czg_ctx *c, const TcMatrix &ta, const TcMatrix &tb, const int8_t *A, const int8_t *B, int M, int N,
+          int K, int epi, int mult, int shift, void *out, int ldo) {
+    if (c->use_tc) launch_gemm_tc(ta, tb, M, N, K, epi, mult, shift, out, ldo, c->err_flag, c->stream);
+    else launch_gemm(A, B, M, N, K, epi, mult, shift, out, ldo, c->stream);
 }
 
 struct Trace {
@@ -416,8 +444,8 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
     for (int l = 0; l < m.n_layers; l++) {
         const LayerDev &L = c->layers[l];
         timed(c, kGemmQkv, [&] {
-            launch_gemm(c->xn, L.qkv_w, M, d + 128, d, kEpiRequant, L.qkv_mult, L.qkv_shift, c->qkv,
-                        d + 128, st);
+            gemm(c, c->tm_xn, L.tm_qkv, c->xn, L.qkv_w, M, d + 128, d, kEpiRequant, L.qkv_mult, L.qkv_shift,
+                 c->qkv, d + 128);
         });
         timed(c, kKvPrep, [&] {
             launch_kv_prep(c->qkv, d + 128, d, c->pos, c->rope_cos, c->rope_sin, M, c->kv, st);
@@ -435,16 +463,19 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
             cudaMemcpy2DAsync(tr->attn + (size_t)l * d, (size_t)m.n_layers * d, c->attn, d, d, M,
                               cudaMemcpyDeviceToHost, st);
         timed(c, kGemmO, [&] {
-            launch_gemm(c->attn, L.out_w, M, d, d, kEpiRequant, L.out_mult, L.out_shift, c->o8, d, st);
+            gemm(c, c->tm_attn, L.tm_out, c->attn, L.out_w, M, d, d, kEpiRequant, L.out_mult, L.out_shift,
+                 c->o8, d);
         });
         timed(c, kResidualNorm, [&] {
             launch_residual_norm(c->o8, L.ffn_norm, L.post_attn_norm, M, d, c->eps, c->x_res, c->xn, st);
         });
         timed(c, kGemmUp, [&] {
-            launch_gemm(c->xn, L.up_w, M, 2 * dff, d, kEpiReglu, L.up_mult, L.up_shift, c->hbuf, dff, st);
+            gemm(c, c->tm_xn, L.tm_up, c->xn, L.up_w, M, 2 * dff, d, kEpiReglu, L.up_mult, L.up_shift,
+                 c->hbuf, dff);
         });
         timed(c, kGemmDown, [&] {
-            launch_gemm(c->hbuf, L.down_w, M, d, dff, kEpiRequant, L.down_mult, L.down_shift, c->o8, d, st);
+            gemm(c, c->tm_h, L.tm_down, c->hbuf, L.down_w, M, d, dff, kEpiRequant, L.down_mult,
+                 L.down_shift, c->o8, d);
         });
         const int8_t *next = l + 1 < m.n_layers ? c->layers[l + 1].attn_norm : c->final_norm;
         timed(c, kResidualNorm, [&] {
@@ -454,7 +485,7 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
     if (tr && tr->final_in)
         cudaMemcpyAsync(tr->final_in, c->xn, (size_t)M * d, cudaMemcpyDeviceToHost, st);
     timed(c, kGemmHead, [&] {
-        launch_gemm(c->xn, c->head_w, M, c->vpad, d, kEpiInt32, 1, 0, c->logits, c->vpad, st);
+        gemm(c, c->tm_xn, c->tm_head, c->xn, c->head_w, M, c->vpad, d, kEpiInt32, 1, 0, c->logits, c->vpad);
     });
     if (tr && tr->logits)
         cudaMemcpy2DAsync(tr->logits, (size_t)V * 4, c->logits, (size_t)c->vpad * 4, (size_t)V * 4, M,
@@ -554,6 +585,7 @@ int compress_impl(czg_ctx *c, const uint32_t *tokens, bool device_tokens, const 
         c->stats.d2h_bytes += sizeof(uint32_t) * nc;
         if (err & kErrToken) return fail(c, CZG_E_TOKEN, "token id >= vocab_size");
         if (err & kErrOverflow) return fail(c, CZG_E_DEVICE, "encoder slot overflow");
+        if (err & kErrTimeout) return fail(c, CZG_E_TIMEOUT, "a bounded device wait expired");
         uint64_t *h_pack = reinterpret_cast<uint64_t *>(c->h_meta);
         h_pack[0] = 0;
         for (int i = 0; i < nc; i++) h_pack[i + 1] = h_pack[i] + out_lens[w.c0 + i];
@@ -696,6 +728,7 @@ int czg_debug_trace(czg_ctx *c, const uint32_t *tokens, uint32_t n, int32_t *log
     collect_events(c);
     stats_end(c);
     if (err & kErrToken) return fail(c, CZG_E_TOKEN, "token id >= vocab_size");
+    if (err & kErrTimeout) return fail(c, CZG_E_TIMEOUT, "a bounded device wait expired");
     return CZG_OK;
 }
 
