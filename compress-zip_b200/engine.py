@@ -15,14 +15,15 @@ LIB_PATH = os.path.join(_HERE, "libczg.so")
 
 CZG_OK = 0
 STATUS_NAMES = {1: "CZG_E_ARG", 2: "CZG_E_MODEL", 3: "CZG_E_UNSUPPORTED", 4: "CZG_E_CAPACITY",
-                5: "CZG_E_DEVICE", 6: "CZG_E_TIMEOUT", 7: "CZG_E_TOKEN", 8: "CZG_E_CHUNK"}
+                5: "CZG_E_DEVICE", 6: "CZG_E_TIMEOUT", 7: "CZG_E_TOKEN", 8: "CZG_E_CHUNK",
+                9: "CZG_E_LIMIT"}
 MAX_KERNEL_CLASSES = 16
 
 # The exported symbols of include/czg.h, checked by the CPU test suite.
 EXPORTS = ["czg_ctx_create", "czg_ctx_destroy", "czg_last_error", "czg_model_info_get",
            "czg_compress_bound", "czg_compress_chunks", "czg_compress_chunks_device",
            "czg_decompress_chunks", "czg_last_stats", "czg_kernel_name", "czg_debug_trace",
-           "czg_set_stream"]
+           "czg_set_stream", "czg_encode_intervals_static"]
 
 
 class CzgError(RuntimeError):
@@ -78,6 +79,9 @@ def lib() -> C.CDLL:
         L.czg_debug_trace.restype = C.c_int
         L.czg_set_stream.argtypes = [P, P]
         L.czg_set_stream.restype = C.c_int
+        L.czg_encode_intervals_static.argtypes = [P, P, C.c_uint32, C.c_uint64, C.c_uint32, P,
+                                                   C.c_uint64, P, C.POINTER(C.c_uint64), P]
+        L.czg_encode_intervals_static.restype = C.c_int
         _lib = L
     return _lib
 

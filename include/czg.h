@@ -38,7 +38,8 @@ enum czg_status {
     CZG_E_DEVICE = 5,       /* CUDA error (message in czg_last_error)                   */
     CZG_E_TIMEOUT = 6,      /* a bounded device-side wait expired                       */
     CZG_E_TOKEN = 7,        /* token id >= vocab_size (the reference would panic)       */
-    CZG_E_CHUNK = 8         /* chunk longer than the model's context / KV cache         */
+    CZG_E_CHUNK = 8,        /* chunk longer than the model's context / KV cache         */
+    CZG_E_LIMIT = 9         /* request beyond a fixed size limit of the entry point      */
 };
 
 /* Model facts a host driver needs (rust/src/model.rs:19-46). */
@@ -121,6 +122,38 @@ const char *czg_kernel_name(uint32_t kernel_class);
  * attn: [n][n_layers][d_model] attention outputs; final_in: [n][d_model]. */
 int czg_debug_trace(czg_ctx *ctx, const uint32_t *tokens, uint32_t n, int32_t *logits,
                     uint32_t *lohi, int8_t *attn, int8_t *final_in);
+
+/* Allocation-free encoder: intervals -> packed chunk bytes.  (No counterpart in
+ * the reference; it is the encoder of the compress path, rust/src/arith_coder.rs
+ * run per chunk, for callers that may not allocate device memory.)
+ *
+ * Some callers cannot call cudaMalloc/cudaFree: their device memory belongs to
+ * another allocator (a framework's caching allocator or a fixed arena sized at
+ * start-up) that must stay the only owner, so the library may not grow its own
+ * allocations behind it.  This entry point takes every input and output in
+ * device memory the caller already owns, and keeps its working storage in one
+ * fixed array inside the library (12 MiB of device memory per GPU that loads
+ * the library, held until the process exits).  It calls no allocating routine.
+ *
+ * d_lohi: device array of n_tokens (sym_low, sym_high) pairs, chunk by chunk;
+ * d_chunk_len: device array of n_chunks token counts (summing to n_tokens);
+ * target_total: the model's target total (czg_model_info.target_total).
+ * Encoded chunks are packed back to back into d_out (out_cap bytes), chunk i's
+ * length goes to d_out_lens[i], the packed size to *out_bytes.  Runs on
+ * `stream` and waits for it before returning.
+ * Limits: n_chunks <= CZG_STATIC_MAX_CHUNKS, n_tokens <= CZG_STATIC_MAX_TOKENS
+ * (else CZG_E_LIMIT); a too small out_cap gives CZG_E_CAPACITY with the needed
+ * size in *out_bytes.
+ * The first call on a device looks up the array's device address (with that
+ * device current); make that first call before any stream capture.  All calls
+ * share the array and each call clears what must start at zero; calls whose
+ * work overlaps on the GPU race on it and must be serialised by the caller. */
+#define CZG_STATIC_MAX_CHUNKS 16384
+#define CZG_STATIC_MAX_TOKENS 2097152
+int czg_encode_intervals_static(const uint32_t *d_lohi, const uint32_t *d_chunk_len,
+                                uint32_t n_chunks, uint64_t n_tokens, uint32_t target_total,
+                                uint8_t *d_out, uint64_t out_cap, uint32_t *d_out_lens,
+                                uint64_t *out_bytes, void *stream);
 
 #ifdef __cplusplus
 }
