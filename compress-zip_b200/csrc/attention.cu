@@ -44,6 +44,103 @@ __device__ __forceinline__ int score_of(const uint32_t (&q)[16], const int8_t *k
     return sra_rne64_to32((long long)sra_rne32(dot, 2) * (long long)mult, 15);
 }
 
+// One warp: the query of head (qr = its 64 raw bytes) at position p against
+// the keys 0..p of kv (rows of [k_rot 64 | v 64]); writes the 64 output bytes.
+__device__ __forceinline__ void attend_query(const int8_t *__restrict__ qr, int p, int mult,
+                                             const int8_t *__restrict__ sink_key,
+                                             const int16_t *__restrict__ rope_cos,
+                                             const int16_t *__restrict__ rope_sin,
+                                             const uint16_t *lut, int8_t *qb, const int8_t *kv,
+                                             int8_t *__restrict__ o) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t coef = 378194u;   // ATTN_COEF_Q24, attention.rs:14-19
+    // Q with RoPE and the NET_SHIFT rounding (attention.rs:53-83)
+    {
+        int x = qr[lane], y = qr[lane + 32];
+        int cs = rope_cos[p * kHalfDim + lane], sn = rope_sin[p * kHalfDim + lane];
+        qb[lane] = (int8_t)clamp127(sra_rne32(sra_rne32(x * cs - y * sn, 15), 1));
+        qb[lane + 32] = (int8_t)clamp127(sra_rne32(sra_rne32(x * sn + y * cs, 15), 1));
+    }
+    __syncwarp();
+    uint32_t q[16];
+    {
+        const uint4 *q4 = reinterpret_cast<const uint4 *>(qb);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            uint4 w = q4[i];
+            q[4 * i] = w.x; q[4 * i + 1] = w.y; q[4 * i + 2] = w.z; q[4 * i + 3] = w.w;
+        }
+    }
+    __syncwarp();
+
+    int m = INT32_MIN;
+    unsigned long long s = 0;
+    uint32_t va0 = 0, va1 = 0;   // wrapping i32 accumulators of dims 2*lane, 2*lane+1
+    if (sink_key != nullptr) {   // attention.rs:211-224: sink score is the first max
+        m = score_of(q, sink_key, mult);
+        s = 65535ull;
+    }
+
+    for (int kb = 0; kb <= p; kb += 32) {
+        const int t = kb + lane;
+        const bool valid = t <= p;
+        const int sc = valid ? score_of(q, kv + (size_t)t * 128, mult) : INT32_MIN;
+        int incl = sc;   // inclusive prefix max over the block, in key order
+#pragma unroll
+        for (int o2 = 1; o2 < 32; o2 <<= 1) {
+            int u = __shfl_up_sync(0xffffffffu, incl, o2);
+            if (lane >= o2) incl = max(incl, u);
+        }
+        incl = max(incl, m);
+        int prev = __shfl_up_sync(0xffffffffu, incl, 1);
+        if (lane == 0) prev = m;
+        const bool rec = valid && sc > prev;
+        // weight against the max in force after this key (attention.rs:266-268)
+        const uint32_t w = valid ? exp_q16((int)((uint32_t)sc - (uint32_t)incl), lut, coef) : 0u;
+        // rescale factor applied at this key when it sets a new max (attention.rs:248-263)
+        const uint32_t e = (rec && prev != INT32_MIN)
+                               ? exp_q16((int)((uint32_t)prev - (uint32_t)sc), lut, coef) : 0u;
+        const uint32_t recs = __ballot_sync(0xffffffffu, rec);
+        const int nvalid = min(32, p - kb + 1);
+        const int8_t *vbase = kv + (size_t)kb * 128 + 64 + 2 * lane;
+        if (recs == 0) {
+            uint32_t ws = w;
+#pragma unroll
+            for (int o2 = 16; o2 > 0; o2 >>= 1) ws += __shfl_xor_sync(0xffffffffu, ws, o2);
+            s += ws;
+            for (int j = 0; j < nvalid; j++) {
+                uint32_t wj = __shfl_sync(0xffffffffu, w, j);
+                uint32_t vv = *reinterpret_cast<const uint16_t *>(vbase + (size_t)j * 128);
+                va0 += wj * (uint32_t)sext8(vv, 0);
+                va1 += wj * (uint32_t)sext8(vv, 1);
+            }
+        } else {
+            for (int j = 0; j < nvalid; j++) {
+                uint32_t wj = __shfl_sync(0xffffffffu, w, j);
+                uint32_t ej = __shfl_sync(0xffffffffu, e, j);
+                if (((recs >> j) & 1u) && ej != 0u) {
+                    s = (s * ej + 0x8000ull) >> 16;
+                    long long p0 = (long long)(int)va0 * (long long)ej;
+                    long long p1 = (long long)(int)va1 * (long long)ej;
+                    p0 += p0 >= 0 ? (1ll << 15) : -(1ll << 15);
+                    p1 += p1 >= 0 ? (1ll << 15) : -(1ll << 15);
+                    va0 = (uint32_t)(int)(p0 >> 16);
+                    va1 = (uint32_t)(int)(p1 >> 16);
+                }
+                s += wj;
+                uint32_t vv = *reinterpret_cast<const uint16_t *>(vbase + (size_t)j * 128);
+                va0 += wj * (uint32_t)sext8(vv, 0);
+                va1 += wj * (uint32_t)sext8(vv, 1);
+            }
+        }
+        m = __shfl_sync(0xffffffffu, incl, 31);
+    }
+    const unsigned long long den = s == 0 ? 1ull : s;
+    uint16_t pk = (uint16_t)(uint8_t)clamp127(div_rne_s32_u64((int)va0, den)) |
+                  ((uint16_t)(uint8_t)clamp127(div_rne_s32_u64((int)va1, den)) << 8);
+    *reinterpret_cast<uint16_t *>(o + 2 * lane) = pk;
+}
+
 template <bool KV_SMEM>
 __global__ void __launch_bounds__(ATT_THREADS, 1)
 k_attention(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restrict__ kv_g,
@@ -59,7 +156,6 @@ k_attention(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restrict__ 
     const int c = blockIdx.x;
     const int r0 = chunk_row0[c], n = chunk_len[c];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const uint32_t coef = 378194u;   // ATTN_COEF_Q24, attention.rs:14-19
     for (int i = tid; i < 256; i += ATT_THREADS) lut[i] = lut_g[i];
     if (tid == 0) task_ctr = 0;
 
@@ -82,99 +178,42 @@ k_attention(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restrict__ 
         if (task >= n_tasks) break;
         const int p = n - 1 - task / n_heads;   // longest first
         const int h = task % n_heads;
-        const int mult = score_mult[h];
-
-        // Q of head h at position p with RoPE and the NET_SHIFT rounding (attention.rs:53-83)
-        {
-            const int8_t *qr = qkv + (size_t)(r0 + p) * ldq + h * 64;
-            int x = qr[lane], y = qr[lane + 32];
-            int cs = rope_cos[p * kHalfDim + lane], sn = rope_sin[p * kHalfDim + lane];
-            qbuf[warp][lane] = (int8_t)clamp127(sra_rne32(sra_rne32(x * cs - y * sn, 15), 1));
-            qbuf[warp][lane + 32] = (int8_t)clamp127(sra_rne32(sra_rne32(x * sn + y * cs, 15), 1));
-        }
-        __syncwarp();
-        uint32_t q[16];
-        {
-            const uint4 *q4 = reinterpret_cast<const uint4 *>(qbuf[warp]);
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                uint4 w = q4[i];
-                q[4 * i] = w.x; q[4 * i + 1] = w.y; q[4 * i + 2] = w.z; q[4 * i + 3] = w.w;
-            }
-        }
-        __syncwarp();
-
-        int m = INT32_MIN;
-        unsigned long long s = 0;
-        uint32_t va0 = 0, va1 = 0;   // wrapping i32 accumulators of dims 2*lane, 2*lane+1
-        if (sink_key != nullptr) {   // attention.rs:211-224: sink score is the first max
-            m = score_of(q, sink_key, mult);
-            s = 65535ull;
-        }
-
-        for (int kb = 0; kb <= p; kb += 32) {
-            const int t = kb + lane;
-            const bool valid = t <= p;
-            const int sc = valid ? score_of(q, kv + (size_t)t * 128, mult) : INT32_MIN;
-            int incl = sc;   // inclusive prefix max over the block, in key order
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                int u = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o) incl = max(incl, u);
-            }
-            incl = max(incl, m);
-            int prev = __shfl_up_sync(0xffffffffu, incl, 1);
-            if (lane == 0) prev = m;
-            const bool rec = valid && sc > prev;
-            // weight against the max in force after this key (attention.rs:266-268)
-            const uint32_t w = valid ? exp_q16((int)((uint32_t)sc - (uint32_t)incl), lut, coef) : 0u;
-            // rescale factor applied at this key when it sets a new max (attention.rs:248-263)
-            const uint32_t e = (rec && prev != INT32_MIN)
-                                   ? exp_q16((int)((uint32_t)prev - (uint32_t)sc), lut, coef) : 0u;
-            const uint32_t recs = __ballot_sync(0xffffffffu, rec);
-            const int nvalid = min(32, p - kb + 1);
-            const int8_t *vbase = kv + (size_t)kb * 128 + 64 + 2 * lane;
-            if (recs == 0) {
-                uint32_t ws = w;
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) ws += __shfl_xor_sync(0xffffffffu, ws, o);
-                s += ws;
-                for (int j = 0; j < nvalid; j++) {
-                    uint32_t wj = __shfl_sync(0xffffffffu, w, j);
-                    uint32_t vv = *reinterpret_cast<const uint16_t *>(vbase + (size_t)j * 128);
-                    va0 += wj * (uint32_t)sext8(vv, 0);
-                    va1 += wj * (uint32_t)sext8(vv, 1);
-                }
-            } else {
-                for (int j = 0; j < nvalid; j++) {
-                    uint32_t wj = __shfl_sync(0xffffffffu, w, j);
-                    uint32_t ej = __shfl_sync(0xffffffffu, e, j);
-                    if (((recs >> j) & 1u) && ej != 0u) {
-                        s = (s * ej + 0x8000ull) >> 16;
-                        long long p0 = (long long)(int)va0 * (long long)ej;
-                        long long p1 = (long long)(int)va1 * (long long)ej;
-                        p0 += p0 >= 0 ? (1ll << 15) : -(1ll << 15);
-                        p1 += p1 >= 0 ? (1ll << 15) : -(1ll << 15);
-                        va0 = (uint32_t)(int)(p0 >> 16);
-                        va1 = (uint32_t)(int)(p1 >> 16);
-                    }
-                    s += wj;
-                    uint32_t vv = *reinterpret_cast<const uint16_t *>(vbase + (size_t)j * 128);
-                    va0 += wj * (uint32_t)sext8(vv, 0);
-                    va1 += wj * (uint32_t)sext8(vv, 1);
-                }
-            }
-            m = __shfl_sync(0xffffffffu, incl, 31);
-        }
-        const unsigned long long den = s == 0 ? 1ull : s;
-        int8_t *o = out + (size_t)(r0 + p) * ldo + h * 64 + 2 * lane;
-        uint16_t pk = (uint16_t)(uint8_t)clamp127(div_rne_s32_u64((int)va0, den)) |
-                      ((uint16_t)(uint8_t)clamp127(div_rne_s32_u64((int)va1, den)) << 8);
-        *reinterpret_cast<uint16_t *>(o) = pk;
+        attend_query(qkv + (size_t)(r0 + p) * ldq + h * 64, p, score_mult[h], sink_key, rope_cos, rope_sin,
+                     lut, qbuf[warp], kv, out + (size_t)(r0 + p) * ldo + h * 64);
     }
 }
 
+// Decode step: row r of the batch is a stream at position p; its keys are the
+// rows 0..p of its KV cache (kvc + r * cache_ld).  One warp per (row, head).
+__global__ void __launch_bounds__(256)
+k_attention_decode(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restrict__ kvc,
+                   size_t cache_ld, int M, int p, int n_heads, const int32_t *__restrict__ score_mult,
+                   const int8_t *__restrict__ sink_key, const int16_t *__restrict__ rope_cos,
+                   const int16_t *__restrict__ rope_sin, const uint16_t *__restrict__ lut_g,
+                   int8_t *__restrict__ out, int ldo) {
+    __shared__ uint16_t lut[256];
+    __shared__ __align__(16) int8_t qbuf[8][64];
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) lut[i] = lut_g[i];
+    __syncthreads();
+    const int warp = threadIdx.x >> 5;
+    const int task = blockIdx.x * 8 + warp;
+    if (task >= M * n_heads) return;
+    const int r = task / n_heads, h = task % n_heads;
+    attend_query(qkv + (size_t)r * ldq + h * 64, p, score_mult[h], sink_key, rope_cos, rope_sin, lut,
+                 qbuf[warp], kvc + (size_t)r * cache_ld, out + (size_t)r * ldo + h * 64);
+}
+
 }  // namespace
+
+void launch_attention_decode(const int8_t *qkv, int ldq, const int8_t *kvc, size_t cache_ld, int M, int p,
+                             int n_heads, const int32_t *score_mult, const int8_t *sink_key,
+                             const int16_t *rope_cos, const int16_t *rope_sin, const uint16_t *lut,
+                             int8_t *out, int ldo, cudaStream_t st) {
+    if (M == 0) return;
+    const int tasks = M * n_heads;
+    k_attention_decode<<<(tasks + 7) / 8, 256, 0, st>>>(qkv, ldq, kvc, cache_ld, M, p, n_heads, score_mult,
+                                                        sink_key, rope_cos, rope_sin, lut, out, ldo);
+}
 
 void attention_init() {
     cudaFuncSetAttribute(k_attention<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,

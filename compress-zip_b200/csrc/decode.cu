@@ -1,0 +1,199 @@
+// decode.cu -- batched decompression: many chunks decode in lockstep, one token
+// per chunk per step (the loop of rust/src/main.rs:377-396 for every chunk).
+//
+// Per step the model kernels run on the M active streams (rows), the new K/V
+// row is appended to each stream's int8 cache, and k_cdf_decode turns each
+// stream's logits into its CDF (rust/src/softmax_cdf.rs:85-139) and runs one
+// ArithDecoder::decode_symbol (rust/src/arith_coder.rs:195-264) on it, one warp
+// per stream; the decoded symbol is the next step's input token.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace czg {
+namespace {
+
+// bit `bit` of the chunk, MSB first; reads past the end give 0 (arith_coder.rs:176-190)
+__device__ __forceinline__ uint32_t read_bit(const uint8_t *data, uint64_t len, uint64_t bit) {
+    const uint64_t byte = bit >> 3;
+    if (byte >= len) return 0u;
+    return (uint32_t)(data[byte] >> (7 - (bit & 7))) & 1u;
+}
+
+// ArithDecoder::new: code = the first 32 bits (arith_coder.rs:153-174)
+__global__ void k_dec_init(const uint8_t *__restrict__ data, const uint64_t *__restrict__ data_off,
+                           const uint64_t *__restrict__ data_len, int M, DecState *__restrict__ st,
+                           uint32_t *__restrict__ tok_in) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= M) return;
+    const uint8_t *d = data + data_off[r];
+    const uint64_t len = data_len[r];
+    uint32_t code = 0;
+    for (int i = 0; i < 32; i++) code = (code << 1) | read_bit(d, len, (uint64_t)i);
+    DecState s;
+    s.low = 0;
+    s.high = 0xFFFFFFFFu;
+    s.code = code;
+    s.pad = 0;
+    s.bit = 32;
+    st[r] = s;
+    tok_in[r] = kBos;
+}
+
+// rows of the batch at position pos: K rotated (attention.rs:29-50) and V into the cache
+__global__ void k_kv_append(const int8_t *__restrict__ qkv, int ldq, int d, int pos,
+                            const int16_t *__restrict__ rope_cos, const int16_t *__restrict__ rope_sin,
+                            int M, int8_t *__restrict__ kvc, size_t cache_ld) {
+    const int gid = blockIdx.x * blockDim.x + threadIdx.x;
+    const int r = gid >> 5, i = gid & 31;
+    if (r >= M) return;
+    const int8_t *k = qkv + (size_t)r * ldq + d;
+    const int x = k[i], y = k[i + kHalfDim];
+    const int c = rope_cos[pos * kHalfDim + i], s = rope_sin[pos * kHalfDim + i];
+    int8_t *dst = kvc + (size_t)r * cache_ld + (size_t)pos * 128;
+    dst[i] = (int8_t)clamp127(sra_rne32(x * c - y * s, 15));
+    dst[i + kHalfDim] = (int8_t)clamp127(sra_rne32(x * s + y * c, 15));
+    reinterpret_cast<uint16_t *>(dst + 64)[i] = reinterpret_cast<const uint16_t *>(k + 64)[i];
+}
+
+// One warp per stream: CDF of the logits row, then one decode_symbol.
+// Lane l owns vocabulary entries [l*E, min((l+1)*E, V)), E = ceil(V / 32).
+__global__ void k_cdf_decode(const int32_t *__restrict__ logits, int V, int ld, const uint16_t *__restrict__ lut_g,
+                             uint32_t coef, uint32_t total, unsigned long long inv_total, int M,
+                             DecState *__restrict__ st, const uint8_t *__restrict__ data,
+                             const uint64_t *__restrict__ data_off, const uint64_t *__restrict__ data_len,
+                             const uint64_t *__restrict__ tok_off, int step, uint32_t *__restrict__ out_tok,
+                             uint32_t *__restrict__ tok_in) {
+    __shared__ uint16_t lut[256];
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) lut[i] = lut_g[i];
+    __syncthreads();
+    const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (r >= M) return;
+    const int32_t *lg = logits + (size_t)r * ld;
+    const int E = (V + 31) >> 5;
+    const int i0 = min(V, lane * E), i1 = min(V, i0 + E);
+
+    // max and first argmax (primitives.rs:278-295)
+    int mx = INT32_MIN, am = 0x7fffffff;
+    for (int i = i0; i < i1; i++) {
+        const int v = lg[i];
+        if (v > mx) { mx = v; am = i; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const int om = __shfl_xor_sync(0xffffffffu, mx, o);
+        const int oa = __shfl_xor_sync(0xffffffffu, am, o);
+        if (om > mx || (om == mx && oa < am)) { mx = om; am = oa; }
+    }
+    uint32_t S = 0;
+    for (int i = i0; i < i1; i++) S += exp_q16((int)((uint32_t)lg[i] - (uint32_t)mx), lut, coef);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
+    const unsigned long long R = (unsigned long long)(total - (uint32_t)V);
+    const unsigned long long invS = 0xFFFFFFFFFFFFFFFFull / S;
+    uint32_t F = 0;
+    for (int i = i0; i < i1; i++) {
+        const uint32_t e = exp_q16((int)((uint32_t)lg[i] - (uint32_t)mx), lut, coef);
+        F += 1u + (uint32_t)udiv_by_inv((unsigned long long)e * R, S, invS);
+    }
+    uint32_t all = F;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) all += __shfl_xor_sync(0xffffffffu, all, o);
+    const uint32_t rem = total - all;   // to the argmax (softmax_cdf.rs:125-127)
+    if (am >= i0 && am < i1) F += rem;
+    uint32_t inc = F;   // inclusive scan of lane totals
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t u = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += u;
+    }
+    const uint32_t base = inc - F;
+
+    DecState s = st[r];
+    const unsigned long long range = (unsigned long long)s.high - s.low + 1;
+    // value = ((code - low + 1) * T - 1) / range  (arith_coder.rs:195-200)
+    const unsigned long long value = (((unsigned long long)s.code - s.low + 1) * total - 1) / range;
+    // bisect on the value truncated to 32 bits (arith_coder.rs:203, 225-241): smallest i
+    // with v32 < cum[i], else the last symbol
+    const uint32_t v32 = (uint32_t)value;
+    const bool mine = i0 < i1 && v32 >= base && v32 < base + F;
+    const uint32_t bal = __ballot_sync(0xffffffffu, mine);
+    const bool past_end = bal == 0;
+    const unsigned owner = past_end ? (unsigned)((V - 1) / E) : (unsigned)(__ffs(bal) - 1);
+    uint32_t sym = 0, lo = 0, hi = 0;
+    if (lane == (int)owner) {
+        uint32_t cum = base;
+        for (int i = i0; i < i1; i++) {
+            const uint32_t e = exp_q16((int)((uint32_t)lg[i] - (uint32_t)mx), lut, coef);
+            uint32_t f = 1u + (uint32_t)udiv_by_inv((unsigned long long)e * R, S, invS);
+            if (i == am) f += rem;
+            if ((!past_end && v32 < cum + f) || (past_end && i == V - 1)) {
+                sym = (uint32_t)i;
+                lo = cum;
+                hi = cum + f;
+                break;
+            }
+            cum += f;
+        }
+    }
+    sym = __shfl_sync(0xffffffffu, sym, owner);
+    lo = __shfl_sync(0xffffffffu, lo, owner);
+    hi = __shfl_sync(0xffffffffu, hi, owner);
+    if (lane == 0) {
+        const unsigned long long HALF = 1ull << 31, QUARTER = 1ull << 30, MASK = 0xFFFFFFFFull;
+        unsigned long long low = s.low, high = s.high, code = s.code;
+        uint64_t bit = s.bit;
+        const uint8_t *d = data + data_off[r];
+        const uint64_t len = data_len[r];
+        high = low + udiv_by_inv((unsigned long long)hi * range, total, inv_total) - 1;
+        low = low + udiv_by_inv((unsigned long long)lo * range, total, inv_total);
+        for (;;) {   // arith_coder.rs:244-264
+            if (((low ^ high) & HALF) == 0) {
+                low = (low << 1) & MASK;
+                high = ((high << 1) & MASK) | 1ull;
+                code = ((code << 1) & MASK) | read_bit(d, len, bit++);
+            } else if ((low & ~high & QUARTER) != 0) {
+                low = ((low << 1) ^ HALF) & MASK;
+                high = (((high ^ HALF) << 1) | HALF | 1ull) & MASK;
+                code = (code & HALF) | ((code << 1) & (MASK >> 1)) | read_bit(d, len, bit++);
+            } else {
+                break;
+            }
+        }
+        s.low = (uint32_t)low;
+        s.high = (uint32_t)high;
+        s.code = (uint32_t)code;
+        s.bit = bit;
+        st[r] = s;
+        out_tok[tok_off[r] + step] = sym;
+        tok_in[r] = sym;
+    }
+}
+
+}  // namespace
+
+void launch_dec_init(const uint8_t *data, const uint64_t *data_off, const uint64_t *data_len, int M,
+                     DecState *st, uint32_t *tok_in, cudaStream_t stream) {
+    if (M == 0) return;
+    k_dec_init<<<(M + 127) / 128, 128, 0, stream>>>(data, data_off, data_len, M, st, tok_in);
+}
+
+void launch_kv_append(const int8_t *qkv, int ldq, int d, int pos, const int16_t *rope_cos,
+                      const int16_t *rope_sin, int M, int8_t *kvc, size_t cache_ld, cudaStream_t stream) {
+    if (M == 0) return;
+    const long long threads = (long long)M * 32;
+    k_kv_append<<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(qkv, ldq, d, pos, rope_cos, rope_sin, M,
+                                                                       kvc, cache_ld);
+}
+
+void launch_cdf_decode(const int32_t *logits, int V, int ld, const uint16_t *lut, uint32_t coef, uint32_t total,
+                       int M, DecState *st, const uint8_t *data, const uint64_t *data_off,
+                       const uint64_t *data_len, const uint64_t *tok_off, int step, uint32_t *out_tok,
+                       uint32_t *tok_in, cudaStream_t stream) {
+    if (M == 0) return;
+    const unsigned long long inv = 0xFFFFFFFFFFFFFFFFull / total;
+    k_cdf_decode<<<(M + 7) / 8, 256, 0, stream>>>(logits, V, ld, lut, coef, total, inv, M, st, data, data_off,
+                                                  data_len, tok_off, step, out_tok, tok_in);
+}
+
+}  // namespace czg

@@ -36,11 +36,13 @@ namespace {
 
 enum KernelClass {
     kRows = 0, kEmbedNorm, kGemmQkv, kKvPrep, kAttention, kGemmO, kResidualNorm, kGemmUp,
-    kGemmDown, kGemmHead, kCdf, kEncode, kPack, kNumClasses
+    kGemmDown, kGemmHead, kCdf, kEncode, kPack, kKvAppend, kAttnDecode, kCdfDecode, kNumClasses
 };
+static_assert(kNumClasses <= CZG_MAX_KERNEL_CLASSES, "too many kernel classes");
 const char *kClassNames[kNumClasses] = {
     "rows", "embed_norm", "gemm_qkv", "kv_prep", "attention", "gemm_o", "residual_norm",
-    "gemm_up_reglu", "gemm_down", "gemm_head", "cdf", "encode", "pack"};
+    "gemm_up_reglu", "gemm_down", "gemm_head", "cdf", "encode", "pack", "kv_append",
+    "attention_decode", "cdf_decode"};
 
 thread_local std::string g_create_error;
 
@@ -93,6 +95,14 @@ struct czg_ctx {
     // tcgen05 path: TMA descriptors of the GEMM A operands (wave buffers) and the head
     bool use_tc = false;
     TcMatrix tm_xn, tm_attn, tm_h, tm_head;
+    // decompression buffers (grown on demand)
+    size_t dec_streams = 0, dec_len = 0, dec_bytes = 0, dec_tokens = 0;
+    int8_t *kvc = nullptr;
+    DecState *dstate = nullptr;
+    uint8_t *ddata = nullptr;
+    uint64_t *d_off = nullptr, *d_len = nullptr, *d_tokoff = nullptr;
+    uint32_t *d_outtok = nullptr;
+    std::vector<void *> dec_allocs;
     // pinned host staging
     uint8_t *h_meta = nullptr;
     size_t h_meta_bytes = 0;
@@ -613,6 +623,184 @@ int compress_impl(czg_ctx *c, const uint32_t *tokens, bool device_tokens, const 
     return CZG_OK;
 }
 
+// (Re)allocate the decompression buffers for `streams` streams of up to `len`
+// positions, `bytes` chunk bytes and `tokens` output tokens.
+int dec_reserve(czg_ctx *c, size_t streams, size_t len, size_t bytes, size_t tokens) {
+    const int L = c->info.n_layers;
+    if (streams <= c->dec_streams && len <= c->dec_len && bytes <= c->dec_bytes && tokens <= c->dec_tokens)
+        return CZG_OK;
+    for (void *p : c->dec_allocs) cudaFree(p);
+    c->dec_allocs.clear();
+    streams = std::max(streams, c->dec_streams);
+    len = std::max(len, c->dec_len);
+    bytes = std::max(bytes, c->dec_bytes);
+    tokens = std::max(tokens, c->dec_tokens);
+    auto get = [&](void **p, size_t n) {
+        if (cudaMalloc(p, std::max<size_t>(n, 16)) != cudaSuccess) return false;
+        c->dec_allocs.push_back(*p);
+        return true;
+    };
+    bool ok = get((void **)&c->kvc, (size_t)L * streams * len * 128) &&
+              get((void **)&c->dstate, streams * sizeof(DecState)) && get((void **)&c->ddata, bytes + 16) &&
+              get((void **)&c->d_off, streams * 8) && get((void **)&c->d_len, streams * 8) &&
+              get((void **)&c->d_tokoff, streams * 8) && get((void **)&c->d_outtok, tokens * 4 + 16);
+    if (!ok) {
+        for (void *p : c->dec_allocs) cudaFree(p);
+        c->dec_allocs.clear();
+        c->dec_streams = c->dec_len = c->dec_bytes = c->dec_tokens = 0;
+        cudaGetLastError();
+        return fail(c, CZG_E_DEVICE, "cudaMalloc failed for the decompression buffers");
+    }
+    c->dec_streams = streams;
+    c->dec_len = len;
+    c->dec_bytes = bytes;
+    c->dec_tokens = tokens;
+    return CZG_OK;
+}
+
+// Decompress: all chunks of a wave decode in lockstep, longest first, so the
+// active streams at step i are a prefix of the rows.
+int decompress_impl(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts, const uint32_t *n_tokens,
+                    uint32_t n_chunks, uint32_t *out_tokens) {
+    if (!c) return CZG_E_ARG;
+    if (n_chunks == 0) return CZG_OK;
+    if (!data_starts || !n_tokens || !out_tokens || (!data && data_starts[n_chunks] > data_starts[0]))
+        return fail(c, CZG_E_ARG, "null input pointer");
+    const czg_model_info &m = c->info;
+    const int d = m.d_model, dff = m.d_ff, V = m.vocab_size, H = m.n_heads;
+    const int limit = std::min(m.context_length, m.max_seq_len);
+    uint64_t total_tok = 0;
+    int max_len = 0;
+    for (uint32_t i = 0; i < n_chunks; i++) {
+        if (data_starts[i + 1] < data_starts[i]) return fail(c, CZG_E_ARG, "data_starts must be non-decreasing");
+        if ((int64_t)n_tokens[i] > limit)
+            return fail(c, CZG_E_CHUNK, "chunk " + std::to_string(i) + " is longer than the model's context");
+        total_tok += n_tokens[i];
+        max_len = std::max(max_len, (int)n_tokens[i]);
+    }
+    if (!cuda_ok(c, cudaSetDevice(c->device), "cudaSetDevice")) return CZG_E_DEVICE;
+    stats_begin(c);
+    c->stats.n_tokens = total_tok;
+    c->stats.n_chunks = n_chunks;
+    // stream order: longest first (stable)
+    std::vector<uint32_t> order(n_chunks);
+    for (uint32_t i = 0; i < n_chunks; i++) order[i] = i;
+    std::stable_sort(order.begin(), order.end(), [&](uint32_t a, uint32_t b) { return n_tokens[a] > n_tokens[b]; });
+    std::vector<uint64_t> tok_base(n_chunks + 1, 0);
+    for (uint32_t i = 0; i < n_chunks; i++) tok_base[i + 1] = tok_base[i] + n_tokens[i];
+    // streams per wave: the activation rows and a KV-cache budget
+    const size_t per_stream = (size_t)m.n_layers * std::max(1, max_len) * 128;
+    size_t budget = (size_t)8 << 30;
+    if (const char *ev = getenv("CZG_DECODE_KV_BYTES")) budget = std::max<size_t>(1 << 20, strtoull(ev, nullptr, 10));
+    const size_t wave = std::max<size_t>(1, std::min<size_t>((size_t)c->cap_rows, budget / per_stream));
+    const uint64_t all_bytes = data_starts[n_chunks] - data_starts[0];
+    int st = dec_reserve(c, std::min<size_t>(wave, n_chunks), std::max(1, max_len), all_bytes, total_tok);
+    if (st) return st;
+    cudaStream_t s = c->stream;
+    {
+        EvPair &e = next_ev(c, -1);
+        cudaEventRecord(e.a, s);
+        if (all_bytes) cudaMemcpyAsync(c->ddata, data + data_starts[0], all_bytes, cudaMemcpyHostToDevice, s);
+        cudaEventRecord(e.b, s);
+        c->stats.h2d_bytes += all_bytes;
+    }
+    std::vector<uint64_t> h_off, h_len, h_tok;
+    for (size_t w0 = 0; w0 < n_chunks; w0 += wave) {
+        const size_t w1 = std::min<size_t>(n_chunks, w0 + wave);
+        const int ns = (int)(w1 - w0);
+        h_off.resize(ns);
+        h_len.resize(ns);
+        h_tok.resize(ns);
+        uint64_t wtok = 0;
+        for (int r = 0; r < ns; r++) {
+            const uint32_t ch = order[w0 + r];
+            h_off[r] = data_starts[ch] - data_starts[0];
+            h_len[r] = data_starts[ch + 1] - data_starts[ch];
+            h_tok[r] = wtok;
+            wtok += n_tokens[ch];
+        }
+        cudaMemcpyAsync(c->d_off, h_off.data(), 8 * ns, cudaMemcpyHostToDevice, s);
+        cudaMemcpyAsync(c->d_len, h_len.data(), 8 * ns, cudaMemcpyHostToDevice, s);
+        cudaMemcpyAsync(c->d_tokoff, h_tok.data(), 8 * ns, cudaMemcpyHostToDevice, s);
+        launch_dec_init(c->ddata, c->d_off, c->d_len, ns, c->dstate, c->tok_in, s);
+        const int wmax = (int)n_tokens[order[w0]];
+        const size_t cache_ld = (size_t)c->dec_len * 128;
+        const size_t layer_ld = (size_t)c->dec_streams * cache_ld;
+        int active = ns;
+        for (int step = 0; step < wmax; step++) {
+            while (active > 0 && (int)n_tokens[order[w0 + active - 1]] <= step) active--;
+            const int M = active;
+            timed(c, kEmbedNorm, [&] {
+                launch_embed_norm(c->tok_in, c->embed, c->layers[0].attn_norm, M, d, c->eps, c->x_res, c->xn, s);
+            });
+            for (int l = 0; l < m.n_layers; l++) {
+                const LayerDev &L = c->layers[l];
+                int8_t *kvc = c->kvc + (size_t)l * layer_ld;
+                timed(c, kGemmQkv, [&] {
+                    gemm(c, c->tm_xn, L.tm_qkv, c->xn, L.qkv_w, M, d + 128, d, kEpiRequant, L.qkv_mult, L.qkv_shift,
+                         c->qkv, d + 128);
+                });
+                timed(c, kKvAppend, [&] {
+                    launch_kv_append(c->qkv, d + 128, d, step, c->rope_cos, c->rope_sin, M, kvc, cache_ld, s);
+                });
+                timed(c, kAttnDecode, [&] {
+                    launch_attention_decode(c->qkv, d + 128, kvc, cache_ld, M, step, H, L.score_mult, L.sink_key,
+                                            c->rope_cos, c->rope_sin, c->lut, c->attn, d, s);
+                });
+                timed(c, kGemmO, [&] {
+                    gemm(c, c->tm_attn, L.tm_out, c->attn, L.out_w, M, d, d, kEpiRequant, L.out_mult, L.out_shift,
+                         c->o8, d);
+                });
+                timed(c, kResidualNorm, [&] {
+                    launch_residual_norm(c->o8, L.ffn_norm, L.post_attn_norm, M, d, c->eps, c->x_res, c->xn, s);
+                });
+                timed(c, kGemmUp, [&] {
+                    gemm(c, c->tm_xn, L.tm_up, c->xn, L.up_w, M, 2 * dff, d, kEpiReglu, L.up_mult, L.up_shift,
+                         c->hbuf, dff);
+                });
+                timed(c, kGemmDown, [&] {
+                    gemm(c, c->tm_h, L.tm_down, c->hbuf, L.down_w, M, d, dff, kEpiRequant, L.down_mult,
+                         L.down_shift, c->o8, d);
+                });
+                const int8_t *next = l + 1 < m.n_layers ? c->layers[l + 1].attn_norm : c->final_norm;
+                timed(c, kResidualNorm, [&] {
+                    launch_residual_norm(c->o8, L.post_ffn_norm, next, M, d, c->eps, c->x_res, c->xn, s);
+                });
+            }
+            timed(c, kGemmHead, [&] {
+                gemm(c, c->tm_xn, c->tm_head, c->xn, c->head_w, M, c->vpad, d, kEpiInt32, 1, 0, c->logits, c->vpad);
+            });
+            timed(c, kCdfDecode, [&] {
+                launch_cdf_decode(c->logits, V, c->vpad, c->lut, m.coef_q24, m.target_total, M, c->dstate, c->ddata,
+                                  c->d_off, c->d_len, c->d_tokoff, step, c->d_outtok, c->tok_in, s);
+            });
+            if (c->ev_used > 4096) {   // keep the event pool bounded on long chunks
+                if (!cuda_ok(c, cudaStreamSynchronize(s), "decode step")) return CZG_E_DEVICE;
+                collect_events(c);
+            }
+        }
+        if (!cuda_ok(c, cudaGetLastError(), "kernel launch")) return CZG_E_DEVICE;
+        // tokens of this wave (stream order) -> caller order
+        std::vector<uint32_t> wt(wtok);
+        EvPair &e = next_ev(c, -2);
+        cudaEventRecord(e.a, s);
+        if (wtok) cudaMemcpyAsync(wt.data(), c->d_outtok, wtok * 4, cudaMemcpyDeviceToHost, s);
+        cudaEventRecord(e.b, s);
+        int err = 0;
+        cudaMemcpyAsync(&err, c->err_flag, sizeof(int), cudaMemcpyDeviceToHost, s);
+        if (!cuda_ok(c, cudaStreamSynchronize(s), "decode wave")) return CZG_E_DEVICE;
+        collect_events(c);
+        c->stats.d2h_bytes += wtok * 4;
+        if (err & kErrTimeout) return fail(c, CZG_E_TIMEOUT, "a bounded device wait expired");
+        for (int r = 0; r < ns; r++) {
+            const uint32_t ch = order[w0 + r];
+            memcpy(out_tokens + tok_base[ch], wt.data() + h_tok[r], 4ull * n_tokens[ch]);
+        }
+    }
+    stats_end(c);
+    return CZG_OK;
+}
+
 }  // namespace
 
 // ---- C ABI ------------------------------------------------------------------
@@ -659,6 +847,7 @@ void czg_ctx_destroy(czg_ctx *c) {
     if (c->stream) cudaStreamSynchronize(c->stream);
     if (c->own_stream && c->own_stream != c->stream) cudaStreamSynchronize(c->own_stream);
     for (void *p : c->allocs) cudaFree(p);
+    for (void *p : c->dec_allocs) cudaFree(p);
     if (c->h_meta) cudaFreeHost(c->h_meta);
     for (auto &e : c->evs) { cudaEventDestroy(e.a); cudaEventDestroy(e.b); }
     if (c->ev_begin) cudaEventDestroy(c->ev_begin);
@@ -688,9 +877,9 @@ int czg_compress_chunks_device(czg_ctx *c, const uint32_t *d_tokens, const uint6
     return compress_impl(c, d_tokens, true, starts, n_chunks, out, out_cap, out_lens, out_needed);
 }
 
-int czg_decompress_chunks(czg_ctx *c, const uint8_t *, const uint64_t *, const uint32_t *, uint32_t,
-                          uint32_t *) {
-    return fail(c, CZG_E_UNSUPPORTED, "decompression is not built yet");
+int czg_decompress_chunks(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts, const uint32_t *n_tokens,
+                          uint32_t n_chunks, uint32_t *out_tokens) {
+    return decompress_impl(c, data, data_starts, n_tokens, n_chunks, out_tokens);
 }
 
 int czg_set_stream(czg_ctx *c, void *stream) {

@@ -65,6 +65,24 @@ void launch_attention(const int8_t *qkv, int ldq, const int8_t *kv, const int *c
                       const int16_t *rope_sin, const uint16_t *lut, int8_t *out, int ldo,
                       cudaStream_t st);
 
+// decode.cu: batched decompression
+struct DecState {   // arithmetic decoder state of one stream
+    uint32_t low, high, code, pad;
+    uint64_t bit;   // next bit of the chunk to read
+};
+void launch_dec_init(const uint8_t *data, const uint64_t *data_off, const uint64_t *data_len, int M,
+                     DecState *st, uint32_t *tok_in, cudaStream_t stream);
+void launch_kv_append(const int8_t *qkv, int ldq, int d, int pos, const int16_t *rope_cos,
+                      const int16_t *rope_sin, int M, int8_t *kvc, size_t cache_ld, cudaStream_t stream);
+void launch_cdf_decode(const int32_t *logits, int V, int ld, const uint16_t *lut, uint32_t coef, uint32_t total,
+                       int M, DecState *st, const uint8_t *data, const uint64_t *data_off,
+                       const uint64_t *data_len, const uint64_t *tok_off, int step, uint32_t *out_tok,
+                       uint32_t *tok_in, cudaStream_t stream);
+void launch_attention_decode(const int8_t *qkv, int ldq, const int8_t *kvc, size_t cache_ld, int M, int p,
+                             int n_heads, const int32_t *score_mult, const int8_t *sink_key,
+                             const int16_t *rope_cos, const int16_t *rope_sin, const uint16_t *lut,
+                             int8_t *out, int ldo, cudaStream_t st);
+
 // coder.cu
 void launch_cdf_lohi(const int32_t *logits, int V, int ld, const uint32_t *sym, const uint16_t *lut,
                      uint32_t coef, uint32_t total, int M, uint2 *lohi, cudaStream_t st);

@@ -1,0 +1,98 @@
+"""GPU decompression (czg_decompress_chunks) against the CPU oracle.
+
+Decoding is exact: tokens decoded on the GPU equal the original tokens for
+streams produced by the oracle's encoder, equal the oracle decoder's tokens for
+arbitrary (corrupt) bytes, and round-trip the GPU's own compressed output.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def eng(shipped_path):
+    from compress_zip_b200.engine import Engine
+
+    e = Engine.from_file(shipped_path, 0)
+    yield e
+    e.close()
+
+
+@pytest.fixture(scope="module")
+def doc_tokens(shipped_path):
+    from compress_zip_b200 import czm, synth
+
+    tok = czm.ModelFile.load(shipped_path).tokenizer()
+    return [np.array(tok.encode_with_special_tokens(synth.document(s, n)), np.uint32)
+            for s, n in ((21, 5000), (22, 2200), (23, 300))]
+
+
+def _chunked(docs, C):
+    toks, starts = [], [0]
+    for ids in docs:
+        base = sum(len(t) for t in toks)
+        for s in range(0, len(ids), C):
+            starts.append(base + min(s + C, len(ids)))
+        toks.append(ids)
+    return np.concatenate(toks), np.array(starts, np.uint64)
+
+
+@pytest.mark.parametrize("C", [64, 1024])
+def test_decode_oracle_streams(eng, shipped_oracle, oracle_mod, doc_tokens, C):
+    tokens, starts = _chunked(doc_tokens, C)
+    chunks = oracle_mod.compress_chunks(shipped_oracle, tokens, starts)
+    got = eng.decompress_chunks(chunks, np.diff(starts))
+    assert np.array_equal(got, tokens)
+
+
+def test_gpu_roundtrip_ragged(eng, doc_tokens):
+    tokens, starts = _chunked(doc_tokens, 512)
+    # an empty chunk and one-token chunks in the middle
+    starts = np.concatenate([starts[:2], [starts[1]], [starts[1] + 1], starts[2:]]).astype(np.uint64)
+    starts = np.unique(np.concatenate([starts, [starts[1] + 1]])).astype(np.uint64)
+    starts = np.sort(np.concatenate([starts, [starts[1]]])).astype(np.uint64)   # repeated = empty chunk
+    chunks = eng.compress_chunks(tokens, starts)
+    got = eng.decompress_chunks(chunks, np.diff(starts))
+    assert np.array_equal(got, tokens)
+
+
+def test_decode_corrupt_bytes_match_oracle(eng, shipped_oracle, oracle_mod):
+    rng = np.random.default_rng(9)
+    chunks = [rng.integers(0, 256, int(n), dtype=np.uint8).tobytes() for n in (0, 1, 7, 40, 300)]
+    n_tok = np.array([5, 17, 64, 100, 257], np.uint32)
+    want = oracle_mod.decompress_chunks(shipped_oracle, chunks, n_tok)
+    got = eng.decompress_chunks(chunks, n_tok)
+    assert np.array_equal(got, want)
+
+
+def test_decode_many_streams_small_waves(shipped_path, shipped_oracle, oracle_mod, doc_tokens, monkeypatch):
+    """A KV-cache budget that forces several decode waves."""
+    from compress_zip_b200.engine import Engine
+
+    monkeypatch.setenv("CZG_DECODE_KV_BYTES", str(64 * 64 * 128))
+    e = Engine.from_file(shipped_path, 0)
+    try:
+        tokens, starts = _chunked(doc_tokens, 64)
+        chunks = oracle_mod.compress_chunks(shipped_oracle, tokens, starts)
+        assert np.array_equal(e.decompress_chunks(chunks, np.diff(starts)), tokens)
+    finally:
+        e.close()
+
+
+def test_decode_arch2(tmp_path, shipped_path, oracle_mod, doc_tokens):
+    from compress_zip_b200 import czm, synth
+    from compress_zip_b200.engine import Engine
+
+    data = synth.arch2_model(czm.ModelFile.load(shipped_path), 512)
+    p = tmp_path / "a2.czm"
+    p.write_bytes(data)
+    om = oracle_mod.load_model(str(p))
+    e = Engine(data, 0)
+    try:
+        tokens, starts = _chunked([doc_tokens[1]], 512)
+        chunks = oracle_mod.compress_chunks(om, tokens, starts)
+        assert e.compress_chunks(tokens, starts) == chunks
+        assert np.array_equal(e.decompress_chunks(chunks, np.diff(starts)), tokens)
+    finally:
+        e.close()
