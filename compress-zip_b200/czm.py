@@ -69,7 +69,7 @@ def write_safetensors(tensors: dict, metadata: dict) -> bytes:
     blobs = []
     off = 0
     for name, arr in tensors.items():
-        arr = np.ascontiguousarray(arr)
+        arr = np.asarray(arr)   # keeps 0-d scalars 0-d (ascontiguousarray would not)
         raw = arr.tobytes()
         header[name] = {"dtype": _DT_INV[arr.dtype], "shape": list(arr.shape),
                         "data_offsets": [off, off + len(raw)]}
