@@ -52,7 +52,28 @@ def parse():
     ap.add_argument("--docs", type=int, default=1024)
     ap.add_argument("--ctx", type=int, default=1024)
     ap.add_argument("--cpu-sample-docs", type=int, default=32)
+    ap.add_argument("--decode-docs", type=int, default=4096,
+                    help="config 3: documents of 4,096 B decoded at ctx 512 (0 skips)")
     return ap.parse_args()
+
+
+def shard_seeds(rank: int, per_rank: int, first: int = 1) -> range:
+    """Documents of a rank: ranks take disjoint seed ranges (weak scaling)."""
+    return range(first + rank * per_rank, first + (rank + 1) * per_rank)
+
+
+def reduce_over_ranks(t_max: list, n_sum: list, device) -> tuple[list, list]:
+    """Max of the per-rank times and sum of the per-rank counts over all ranks."""
+    import torch
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return list(t_max), list(n_sum)
+    a = torch.tensor(list(t_max), dtype=torch.float64, device=device)
+    b = torch.tensor(list(n_sum), dtype=torch.float64, device=device)
+    dist.all_reduce(a, op=dist.ReduceOp.MAX)
+    dist.all_reduce(b)
+    return a.tolist(), b.tolist()
 
 
 def workload(mf, seeds, ctx):
@@ -183,7 +204,7 @@ def main():
                                 device_id=torch.device("cuda", local))
     from compress_zip_b200.engine import Engine
 
-    seeds = range(rank * args.docs + 1, rank * args.docs + args.docs + 1)
+    seeds = shard_seeds(rank, args.docs)
     tokens, starts, nbytes = workload(mf, seeds, args.ctx)
     n_tok, n_chunks = int(len(tokens)), int(len(starts) - 1)
 
@@ -261,15 +282,10 @@ def main():
     t_e2e = sum(e2e_times)
     parity = bytes(h_out_np[:nout_h]) == bytes(out[:nout])
 
-    if world > 1:
-        t = torch.tensor([t_rank, t_e2e], dtype=torch.float64, device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        t_max, t_e2e_max = float(t[0]), float(t[1])
-        tot = torch.tensor([n_tok, nbytes], dtype=torch.float64, device=f"cuda:{local}")
-        dist.all_reduce(tot)
-        all_tok, all_bytes = float(tot[0]), float(tot[1])
-    else:
-        t_max, t_e2e_max, all_tok, all_bytes = t_rank, t_e2e, float(n_tok), float(nbytes)
+    dec = decode_bench(eng, mf, rank, args, stream, world) if args.decode_docs > 0 else None
+
+    (t_max, t_e2e_max), (all_tok, all_bytes) = reduce_over_ranks(
+        [t_rank, t_e2e], [float(n_tok), float(nbytes)], f"cuda:{local}")
 
     if rank == 0:
         K = args.steps
@@ -315,12 +331,60 @@ def main():
             "clocks": clk,
             "compressed_bytes_per_gpu": int(nout),
         }
+        if dec is not None:
+            line["decode"] = dec
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
     eng.close()
     if world > 1:
         dist.destroy_process_group()
+
+
+def decode_bench(eng, mf, rank, args, stream, world):
+    """decompression of 4,096 independent streams, each
+    the chunks of a 4 KB document at L4 (ctx 512), seeds 2000.. (rank r: +r*4096).
+    The chunks are produced by the engine itself (untimed); the timed region is
+    czg_decompress_chunks from host bytes to host tokens (H2D/D2H inside), CUDA
+    events on the engine's stream; the tokens must equal the originals."""
+    import torch
+
+    tok = mf.tokenizer()
+    docs = synth.documents(shard_seeds(rank, args.decode_docs, first=2000), 4096)
+    ids = tok.encode_batch(docs, num_threads=min(16, os.cpu_count() or 1))
+    starts, b = [0], 0
+    for t in ids:
+        for s0 in range(0, len(t), 512):
+            starts.append(b + min(s0 + 512, len(t)))
+        b += len(t)
+    tokens = np.concatenate([np.asarray(t, dtype=np.uint32) for t in ids])
+    starts = np.asarray(starts, dtype=np.uint64)
+    counts = np.diff(starts).astype(np.uint32)
+    chunks = eng.compress_chunks(tokens, starts)
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    got = eng.decompress_chunks(chunks, counts)   # warm-up
+    exact = bool(np.array_equal(got, tokens))
+    steps = max(1, min(args.steps, 3))
+    times, launches = [], 0
+    for _ in range(steps):
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        got = eng.decompress_chunks(chunks, counts)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        times.append(ev0.elapsed_time(ev1))
+        launches += sum(v["launches"] for v in eng.last_stats()["kernels"].values())
+        exact = exact and bool(np.array_equal(got, tokens))
+    (t,), (n_tok,) = reduce_over_ranks([sum(times)], [float(len(tokens))],
+                                       f"cuda:{torch.cuda.current_device()}")
+    kern = eng.last_stats()["kernels"]
+    return {"metric": "batched decode tokens/s (config 3: 4096 x 4 KB docs, L4 ctx 512)",
+            "value": round(n_tok * steps / (t / 1e3), 1), "unit": "tokens/s", "steps": steps,
+            "ms_per_step": round(t / steps, 3), "streams_per_gpu": int(len(chunks)),
+            "tokens_per_gpu": int(len(tokens)), "exact_roundtrip": exact,
+            "gpu_launches_per_step": int(launches // steps),
+            "kernels_ms_per_step": {k: round(v["ms"], 3) for k, v in kern.items() if v["launches"]}}
 
 
 def _oracle_sample(mf, ndocs, ctx):
