@@ -404,8 +404,8 @@ int alloc_workspace(czg_ctx *c, int rows, int chunks) {
 // One projection: tcgen05 path when available, else the mma.sync kernel.
 void gemm(czg_ctx *c, const TcMatrix &ta, const TcMatrix &tb, const int8_t *A, const int8_t *B, int M, int N,
           int K, int epi, int mult, int shift, void *out, int ldo) {
-    if (c->use_tc) launch_gemm_tc(ta, tb, M, N, K, epi, mult, shift, out, ldo, c->err_flag, c->stream);
-    else launch_gemm(A, B, M, N, K, epi, mult, shift, out, ldo, c->stream);
+    if (!c->use_tc || !launch_gemm_tc(ta, tb, M, N, K, epi, mult, shift, out, ldo, c->err_flag, c->stream))
+        launch_gemm(A, B, M, N, K, epi, mult, shift, out, ldo, c->stream);
 }
 
 struct Trace {

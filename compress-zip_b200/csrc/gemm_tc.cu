@@ -6,17 +6,23 @@
 // requantisation (rust/src/model.rs:280-300), requantisation + ReGLU on
 // interleaved gate/up columns (rust/src/reglu.rs:20-46), or raw int32.
 //
-// One CTA computes a 128 x BN output tile (BN = 128, 192 or 256):
-//   warp 0 / lane 0  TMA producer: for each 128-byte K block, one box of A
-//                    (128 rows) and one of B (BN rows), 128B-swizzled, into a
-//                    ring of STAGES shared-memory stages (mbarrier full/empty);
-//   warp 1 / lane 0  MMA issuer: 4 x tcgen05.mma (K = 32 each) per stage into
-//                    one TMEM accumulator of BN columns; tcgen05.commit frees the
-//                    stage and finally signals the epilogue;
-//   warps 0..3       epilogue: warp w reads TMEM lanes 32w..32w+31 (its rows)
-//                    with tcgen05.ld 32x32b and stores the converted row slice.
+// Persistent, warp-specialised kernel: one CTA per SM walks the 128 x BN output
+// tiles (BN = 128 or 256) in a strided order.
+//   warp 0 / lane 0  TMA producer: per 128-byte K block one box of A (128 rows)
+//                    and one of B (BN rows), 128B-swizzled, into a ring of
+//                    STAGES shared-memory stages (mbarriers full / empty);
+//   warp 1           allocates TMEM; lane 0 issues 4 x tcgen05.mma (K = 32 each)
+//                    per stage into one of two TMEM accumulators (2 x BN
+//                    columns), tcgen05.commit frees the stage and, after the
+//                    tile's last K block, hands the accumulator to the epilogue;
+//   warps 2..5       epilogue: warp w owns TMEM lanes 32*(w%4).. (its 32 rows),
+//                    converts 128-byte output slices per row, writes them
+//                    128B-swizzled into a per-warp staging buffer and stores
+//                    them with TMA (cp.async.bulk.tensor, global <- shared),
+//                    then releases the accumulator, so the epilogue of tile i
+//                    overlaps the MMAs of tile i+1.
 // Every mbarrier wait is bounded by a clock budget; on expiry the kernel sets
-// kErrTimeout in the error word, skips the remaining work and frees its TMEM.
+// kErrTimeout in the error word, every role stops, and TMEM is freed.
 // No TMA load here uses cluster multicast.
 #include <cuda.h>
 
@@ -28,6 +34,8 @@ namespace {
 
 constexpr int TC_BM = 128;
 constexpr int TC_BK = 128;   // bytes of K per stage = one 128-byte swizzle row
+constexpr int TC_THREADS = 192;
+constexpr int TC_STAGE_OUT = 32 * 128;   // one epilogue warp's staging box: 32 rows x 128 bytes
 constexpr long long kWaitBudget = 4000000000ll;   // clock cycles (about 2 s)
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
@@ -44,8 +52,9 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
                  : "memory");
 }
 
-// Bounded wait for the phase with the given parity; false when the budget ran out.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+// Bounded wait for the phase with the given parity; false when the budget ran
+// out or (abort != nullptr) another role of the CTA has aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, const volatile int *abort) {
     const uint32_t a = smem_addr(bar);
     const long long t0 = clock64();
     for (;;) {
@@ -58,8 +67,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
             : "r"(a), "r"(parity)
             : "memory");
         if (done) return true;
-        if (clock64() - t0 > kWaitBudget) return false;
+        if ((abort != nullptr && *abort) || clock64() - t0 > kWaitBudget) return false;
     }
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y) {
@@ -101,46 +114,96 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar) {
                  : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+                 ::"l"(map), "r"(smem_addr(src)), "r"(x), "r"(y)
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
 
-template <int BN, int STAGES, int EPI>
-__global__ void __launch_bounds__(128, 1)
-k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, int M,
-          int K, int mult, int shift, void *__restrict__ out, int ldo, int *__restrict__ err) {
+// 32 consecutive TMEM columns of this warp's 32 lanes (lane = row).  The load and
+// its wait are one asm statement so that no use of the registers can be
+// scheduled before the data has arrived.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+}
+
+// Requantisation parameters.  When clamp_a > 0 the product of an accumulator
+// clamped to [-clamp_a, clamp_a] with mult fits in int32 and every accumulator
+// beyond the clamp saturates to +-127 either way, so the 64-bit product of
+// model.rs:280-300 reduces to 32-bit arithmetic.
+struct Requant {
+    int mult, shift, clamp_a, bias;   // bias = 2^(shift-1) - 1
+};
+
+template <bool FAST>
+__device__ __forceinline__ int rq(int acc, const Requant &q) {
+    if (FAST) {
+        const int x = min(max(acc, -q.clamp_a), q.clamp_a) * q.mult;
+        return clamp127((x + q.bias + ((x >> q.shift) & 1)) >> q.shift);   // round half to even
+    }
+    return requant(acc, q.mult, q.shift);
+}
+
+__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
+    return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+}
+
+// Output columns (elements) of one 128-byte staging row and accumulator columns it consumes.
+template <int EPI>
+struct EpiShape {
+    static constexpr int kAccCols = EPI == kEpiInt32 ? 32 : (EPI == kEpiReglu ? 256 : 128);
+    static constexpr int kOutCols = EPI == kEpiInt32 ? 32 : 128;
+};
+
+template <int BN, int STAGES, int EPI, bool FAST>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+          const __grid_constant__ CUtensorMap map_o, int M, int N, int K, Requant rqp, int *__restrict__ err) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    // 1024-byte alignment for the swizzle atoms
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     constexpr int A_BYTES = TC_BM * TC_BK;
     constexpr int B_BYTES = BN * TC_BK;
     constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    constexpr int TMEM_COLS = BN <= 128 ? 128 : 256;
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
+    constexpr int TMEM_COLS = 2 * BN;   // two accumulators
+    constexpr int NCH = BN / EpiShape<EPI>::kAccCols;   // staging rows per tile
+    uint8_t *stage_out = smem + STAGES * STAGE_BYTES;   // 4 warps x 2 buffers x 4 KB
+    uint64_t *full = reinterpret_cast<uint64_t *>(stage_out + 8 * TC_STAGE_OUT);
     uint64_t *empty = full + STAGES;
-    uint64_t *done = empty + STAGES;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
-    __shared__ int abort_flag;
+    uint64_t *tfull = empty + STAGES;
+    uint64_t *tempty = tfull + 2;
+    uint64_t *drain = tempty + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    __shared__ volatile int abort_flag;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.y * TC_BM, n0 = blockIdx.x * BN;
     const int KB = K / TC_BK;
+    const int NT = N / BN;
+    const int n_tiles = ((M + TC_BM - 1) / TC_BM) * NT;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(done, 1);
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 4);
+        }
+        mbar_init(drain, 1);
         abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 0) {   // the whole warp allocates the accumulator columns
+    if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
                      "r"(TMEM_COLS));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -150,91 +213,156 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 0 && lane == 0) {
-        // producer
-        for (int kb = 0; kb < KB; kb++) {
-            const int s = kb % STAGES;
-            if (kb >= STAGES && !mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1)) {
-                atomicOr(err, kErrTimeout);
-                abort_flag = 1;
-                break;
+    if (warp == 0) {
+        if (lane == 0) {   // TMA producer
+            int it = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+                const int m0 = (tile / NT) * TC_BM, n0 = (tile % NT) * BN;
+                for (int kb = 0; kb < KB; kb++, it++) {
+                    const int s = it % STAGES;
+                    if (it >= STAGES && !mbar_wait(&empty[s], ((it / STAGES) - 1) & 1, &abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *sa = smem + s * STAGE_BYTES;
+                    mbar_expect_tx(&full[s], STAGE_BYTES);
+                    tma_load_2d(sa, &map_a, &full[s], kb * TC_BK, m0);
+                    tma_load_2d(sa + A_BYTES, &map_b, &full[s], kb * TC_BK, n0);
+                }
             }
-            uint8_t *sa = smem + s * STAGE_BYTES;
-            mbar_expect_tx(&full[s], STAGE_BYTES);
-            tma_load_2d(sa, &map_a, &full[s], kb * TC_BK, m0);
-            tma_load_2d(sa + A_BYTES, &map_b, &full[s], kb * TC_BK, n0);
-        }
-    } else if (warp == 1 && lane == 0) {
-        // MMA issuer
-        const uint32_t idesc = idesc_i8(TC_BM, BN);
-        bool ok = true;
-        for (int kb = 0; kb < KB; kb++) {
-            const int s = kb % STAGES;
-            if (!mbar_wait(&full[s], (kb / STAGES) & 1)) {
+            if (!ok) {
                 atomicOr(err, kErrTimeout);
                 abort_flag = 1;
-                ok = false;
+                // let the loads already issued land before the CTA's shared memory goes away
+                for (int k = max(0, it - STAGES); k < it; k++) mbar_wait(&full[k % STAGES], (k / STAGES) & 1, nullptr);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {   // MMA issuer
+            const uint32_t idesc = idesc_i8(TC_BM, BN);
+            int it = 0, tc = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, tc++) {
+                const int b = tc & 1;
+                if (tc >= 2 && !mbar_wait(&tempty[b], ((tc >> 1) - 1) & 1, &abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t dt = tmem + (uint32_t)(b * BN);
+                for (int kb = 0; kb < KB; kb++, it++) {
+                    const int s = it % STAGES;
+                    if (!mbar_wait(&full[s], (it / STAGES) & 1, &abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const uint32_t sa = smem_addr(smem + s * STAGE_BYTES);
+                    const uint64_t ad = smem_desc_sw128(sa);
+                    const uint64_t bd = smem_desc_sw128(sa + A_BYTES);
+#pragma unroll
+                    for (int k = 0; k < TC_BK / 32; k++)   // advance 32 bytes (2 x 16 B) inside the swizzle row
+                        mma_i8(dt, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+                    mma_commit(&empty[s]);
+                }
+                if (ok) mma_commit(&tfull[b]);
+            }
+            if (!ok) {
+                atomicOr(err, kErrTimeout);
+                abort_flag = 1;
+            }
+            // every MMA issued by this thread has completed once drain fires
+            mma_commit(drain);
+            mbar_wait(drain, 0, nullptr);
+        }
+    } else {   // epilogue warps 2..5
+        const int q = warp & 3;   // TMEM lane quadrant = rows 32q .. 32q+31 of the tile
+        uint8_t *sbuf0 = stage_out + (warp - 2) * 2 * TC_STAGE_OUT;
+        int tc = 0, nb = 0;
+        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, tc++) {
+            const int b = tc & 1;
+            // every lane observes the accumulator's completion itself
+            const bool got = __all_sync(0xffffffffu, mbar_wait(&tfull[b], (tc >> 1) & 1, &abort_flag));
+            if (!got) {
+                if (lane == 0) {
+                    atomicOr(err, kErrTimeout);
+                    abort_flag = 1;
+                }
                 break;
             }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t sa = smem_addr(smem + s * STAGE_BYTES);
-            const uint64_t ad = smem_desc_sw128(sa);
-            const uint64_t bd = smem_desc_sw128(sa + A_BYTES);
-#pragma unroll
-            for (int k = 0; k < TC_BK / 32; k++)   // advance 32 bytes (2 x 16 B) inside the swizzle row
-                mma_i8(tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
-            mma_commit(&empty[s]);
-        }
-        if (ok) mma_commit(done);
-        else asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(done)) : "memory");
-    }
-    __syncwarp();
-
-    // epilogue: all four warps
-    const bool got = mbar_wait(done, 0);
-    if (!got) atomicOr(err, kErrTimeout);
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    const int row = m0 + warp * 32 + lane;
-    const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
-    if (got && !abort_flag) {
+            const int m0 = (tile / NT) * TC_BM, n0 = (tile % NT) * BN;
+            const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * BN);
+            if (m0 + 32 * q >= M) {
+                // no row of this warp exists: nothing to convert or store.  The staging
+                // buffers must stay untouched here, since the stores of the previous
+                // tile may still be reading them (wait_group.read counts only issued stores).
+                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[b]);
+                continue;
+            }
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
-            uint32_t v[16];
-            tmem_ld16(trow + c, v);
-            if (row < M) {
+            for (int ch = 0; ch < NCH; ch++) {
+                uint32_t w[32];   // this row's 128 output bytes
+                const uint32_t tcol = tbase + (uint32_t)(ch * EpiShape<EPI>::kAccCols);
                 if (EPI == kEpiInt32) {
-                    int4 *o = reinterpret_cast<int4 *>(reinterpret_cast<int *>(out) + (size_t)row * ldo + n0 + c);
-#pragma unroll
-                    for (int q = 0; q < 4; q++)
-                        o[q] = make_int4((int)v[4 * q], (int)v[4 * q + 1], (int)v[4 * q + 2], (int)v[4 * q + 3]);
+                    tmem_ld32(tcol, w);
                 } else if (EPI == kEpiRequant) {
-                    uint32_t w[4];
 #pragma unroll
-                    for (int q = 0; q < 4; q++) {
-                        w[q] = 0;
+                    for (int g = 0; g < 4; g++) {
+                        uint32_t v[32];
+                        tmem_ld32(tcol + 32 * g, v);
 #pragma unroll
-                        for (int b = 0; b < 4; b++)
-                            w[q] |= (uint32_t)(uint8_t)requant((int)v[4 * q + b], mult, shift) << (8 * b);
+                        for (int j = 0; j < 8; j++)
+                            w[8 * g + j] = pack4(rq<FAST>((int)v[4 * j], rqp), rq<FAST>((int)v[4 * j + 1], rqp),
+                                                 rq<FAST>((int)v[4 * j + 2], rqp), rq<FAST>((int)v[4 * j + 3], rqp));
                     }
-                    *reinterpret_cast<uint4 *>(reinterpret_cast<int8_t *>(out) + (size_t)row * ldo + n0 + c) =
-                        make_uint4(w[0], w[1], w[2], w[3]);
-                } else {   // ReGLU on (gate_j, up_j) = columns (2j, 2j+1)
-                    uint32_t w[2] = {0, 0};
+                } else {   // ReGLU on (gate_j, up_j) = columns (2j, 2j+1) (reglu.rs:20-46)
 #pragma unroll
-                    for (int j = 0; j < 8; j++) {
-                        int gte = max(requant((int)v[2 * j], mult, shift), 0);
-                        int upv = requant((int)v[2 * j + 1], mult, shift);
-                        w[j >> 2] |= (uint32_t)(uint8_t)clamp127(sra_rne32(gte * upv, 7)) << (8 * (j & 3));
+                    for (int g = 0; g < 8; g++) {
+                        uint32_t v[32];
+                        tmem_ld32(tcol + 32 * g, v);
+                        int y[16];
+#pragma unroll
+                        for (int j = 0; j < 16; j++) {
+                            const int gte = max(rq<FAST>((int)v[2 * j], rqp), 0);
+                            const int x = gte * rq<FAST>((int)v[2 * j + 1], rqp);
+                            y[j] = clamp127((x + 63 + ((x >> 7) & 1)) >> 7);
+                        }
+#pragma unroll
+                        for (int j = 0; j < 4; j++) w[4 * g + j] = pack4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
                     }
-                    *reinterpret_cast<uint2 *>(reinterpret_cast<int8_t *>(out) + (size_t)row * ldo + ((n0 + c) >> 1)) =
-                        make_uint2(w[0], w[1]);
                 }
+                if (ch == NCH - 1) {   // the accumulator is free for the tile after next
+                    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tempty[b]);
+                }
+                // staging buffer nb was handed to a TMA store two slices ago
+                if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+                __syncwarp();
+                uint8_t *sb = sbuf0 + nb * TC_STAGE_OUT + lane * 128;
+#pragma unroll
+                for (int c = 0; c < 8; c++)   // 128B swizzle: 16-byte chunk c lands at c ^ (row & 7)
+                    *reinterpret_cast<uint4 *>(sb + ((c ^ (lane & 7)) << 4)) =
+                        make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) {   // rows at or beyond M are clipped by the map
+                    const int x = (EPI == kEpiReglu ? n0 / 2 : n0) + ch * EpiShape<EPI>::kOutCols;
+                    tma_store_2d(&map_o, sbuf0 + nb * TC_STAGE_OUT, x, m0 + 32 * q);
+                }
+                nb ^= 1;
             }
         }
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+        __syncwarp();
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
-    if (warp == 0)
+    if (warp == 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
 }
 
@@ -254,43 +382,93 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-template <int BN, int STAGES>
-constexpr size_t tc_smem() {
-    return 1024 + (size_t)STAGES * (TC_BM + BN) * TC_BK + (2 * STAGES + 1) * 8 + 16;
+template <int BN>
+struct TcCfg {
+    static constexpr int kStages = BN == 256 ? 3 : 4;
+    static constexpr size_t kSmem = 1024 + (size_t)kStages * (TC_BM + BN) * TC_BK + 8 * TC_STAGE_OUT +
+                                    (2 * kStages + 5) * 8 + 16;
+};
+
+int sm_count() {
+    static int cached[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return 148;
+    if (!cached[dev]) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        cached[dev] = n > 0 ? n : 148;
+    }
+    return cached[dev];
 }
 
-template <int BN, int STAGES, int EPI>
-void launch_tc(const TcMatrix &A, const TcMatrix &B, int M, int N, int K, int mult, int shift, void *out,
+// TMA map of the output: [rows][cols] elements of elem_bytes, row pitch ld_bytes,
+// stored in boxes of 128 bytes x 32 rows with the 128-byte swizzle.
+bool make_out_map(CUtensorMap *map, void *base, uint64_t rows, uint64_t cols, uint64_t ld_bytes, int elem_bytes) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {ld_bytes};
+    cuuint32_t box[2] = {(cuuint32_t)(128 / elem_bytes), 32};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(map, elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_INT32 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, base, dims,
+              strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+Requant make_requant(int mult, int shift) {
+    Requant q{mult, shift, 0, 0};
+    if (shift >= 1 && shift <= 24 && mult != 0) {
+        const long long am = mult < 0 ? -(long long)mult : (long long)mult;
+        const long long a = ((128ll << shift) / am) + 1;   // |a * mult| >= 128 * 2^shift
+        if (a * am + (1ll << (shift - 1)) < (1ll << 31)) {
+            q.clamp_a = (int)a;
+            q.bias = (1 << (shift - 1)) - 1;
+        }
+    }
+    return q;
+}
+
+template <int BN, int EPI>
+bool launch_tc(const TcMatrix &A, const TcMatrix &B, int M, int N, int K, int mult, int shift, void *out,
                int ldo, int *err, cudaStream_t st) {
-    dim3 grid(N / BN, (M + TC_BM - 1) / TC_BM);
-    k_gemm_tc<BN, STAGES, EPI><<<grid, 128, tc_smem<BN, STAGES>(), st>>>(
-        *reinterpret_cast<const CUtensorMap *>(A.map), *reinterpret_cast<const CUtensorMap *>(B.map), M, K,
-        mult, shift, out, ldo, err);
+    alignas(64) CUtensorMap omap;
+    const int eb = EPI == kEpiInt32 ? 4 : 1;
+    const uint64_t cols = EPI == kEpiReglu ? (uint64_t)N / 2 : (uint64_t)N;
+    if (!make_out_map(&omap, out, (uint64_t)M, cols, (uint64_t)ldo * eb, eb)) return false;
+    const int tiles = ((M + TC_BM - 1) / TC_BM) * (N / BN);
+    const int grid = tiles < sm_count() ? tiles : sm_count();
+    const Requant q = make_requant(mult, shift);
+    const CUtensorMap &ma = *reinterpret_cast<const CUtensorMap *>(A.map);
+    const CUtensorMap &mb = *reinterpret_cast<const CUtensorMap *>(B.map);
+    if (q.clamp_a > 0 || EPI == kEpiInt32)
+        k_gemm_tc<BN, TcCfg<BN>::kStages, EPI, true><<<grid, TC_THREADS, TcCfg<BN>::kSmem, st>>>(ma, mb, omap, M, N, K,
+                                                                                                q, err);
+    else
+        k_gemm_tc<BN, TcCfg<BN>::kStages, EPI, false><<<grid, TC_THREADS, TcCfg<BN>::kSmem, st>>>(ma, mb, omap, M, N,
+                                                                                                 K, q, err);
+    return true;
 }
 
-template <int BN, int STAGES>
+template <int BN, int EPI>
+void set_attr_epi() {
+    cudaFuncSetAttribute(k_gemm_tc<BN, TcCfg<BN>::kStages, EPI, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)TcCfg<BN>::kSmem);
+    cudaFuncSetAttribute(k_gemm_tc<BN, TcCfg<BN>::kStages, EPI, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)TcCfg<BN>::kSmem);
+}
+
+template <int BN>
 void set_attr() {
-    cudaFuncSetAttribute(k_gemm_tc<BN, STAGES, kEpiRequant>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)tc_smem<BN, STAGES>());
-    cudaFuncSetAttribute(k_gemm_tc<BN, STAGES, kEpiReglu>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)tc_smem<BN, STAGES>());
-    cudaFuncSetAttribute(k_gemm_tc<BN, STAGES, kEpiInt32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)tc_smem<BN, STAGES>());
-}
-
-template <int BN, int STAGES>
-void dispatch_epi(int epi, const TcMatrix &A, const TcMatrix &B, int M, int N, int K, int mult, int shift,
-                  void *out, int ldo, int *err, cudaStream_t st) {
-    if (epi == kEpiRequant) launch_tc<BN, STAGES, kEpiRequant>(A, B, M, N, K, mult, shift, out, ldo, err, st);
-    else if (epi == kEpiReglu) launch_tc<BN, STAGES, kEpiReglu>(A, B, M, N, K, mult, shift, out, ldo, err, st);
-    else launch_tc<BN, STAGES, kEpiInt32>(A, B, M, N, K, mult, shift, out, ldo, err, st);
+    set_attr_epi<BN, kEpiRequant>();
+    set_attr_epi<BN, kEpiReglu>();
+    set_attr_epi<BN, kEpiInt32>();
 }
 
 }  // namespace
 
 int tc_bn_for(int N) {
     if (N % 256 == 0) return 256;
-    if (N % 192 == 0) return 192;
     if (N % 128 == 0) return 128;
     return 0;
 }
@@ -314,19 +492,22 @@ bool tc_make_matrix(TcMatrix &m, const int8_t *base, uint64_t rows, uint64_t K, 
 }
 
 void gemm_tc_init() {
-    set_attr<128, 3>();
-    set_attr<192, 2>();
-    set_attr<256, 2>();
+    set_attr<128>();
+    set_attr<256>();
 }
 
-void launch_gemm_tc(const TcMatrix &A, const TcMatrix &B, int M, int N, int K, int epi, int mult, int shift,
+bool launch_gemm_tc(const TcMatrix &A, const TcMatrix &B, int M, int N, int K, int epi, int mult, int shift,
                     void *out, int ldo, int *err, cudaStream_t st) {
-    if (M <= 0) return;
-    switch (tc_bn_for(N)) {
-        case 256: dispatch_epi<256, 2>(epi, A, B, M, N, K, mult, shift, out, ldo, err, st); break;
-        case 192: dispatch_epi<192, 2>(epi, A, B, M, N, K, mult, shift, out, ldo, err, st); break;
-        default: dispatch_epi<128, 3>(epi, A, B, M, N, K, mult, shift, out, ldo, err, st); break;
+    if (M <= 0) return true;
+    const int bn = tc_bn_for(N);
+    if (bn == 0 || (epi == kEpiReglu && bn != 256)) return false;
+    if (bn == 256) {
+        if (epi == kEpiRequant) return launch_tc<256, kEpiRequant>(A, B, M, N, K, mult, shift, out, ldo, err, st);
+        if (epi == kEpiReglu) return launch_tc<256, kEpiReglu>(A, B, M, N, K, mult, shift, out, ldo, err, st);
+        return launch_tc<256, kEpiInt32>(A, B, M, N, K, mult, shift, out, ldo, err, st);
     }
+    if (epi == kEpiRequant) return launch_tc<128, kEpiRequant>(A, B, M, N, K, mult, shift, out, ldo, err, st);
+    return launch_tc<128, kEpiInt32>(A, B, M, N, K, mult, shift, out, ldo, err, st);
 }
 
 }  // namespace czg

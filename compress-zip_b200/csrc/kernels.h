@@ -34,9 +34,12 @@ enum GemmEpilogue {
 void launch_gemm(const int8_t *A, const int8_t *B, int M, int N, int K, int epi, int mult,
                  int shift, void *out, int ldo, cudaStream_t st);
 
-// gemm_tc.cu: the same GEMM on tcgen05 (kind::i8) with TMA-staged operands.
-// A TcMatrix is a TMA descriptor of a row-major [rows][K] int8 matrix read in
-// boxes of 128 bytes of K by box_rows rows (128 for A, tc_bn_for(N) for B).
+// gemm_tc.cu: the same GEMM on tcgen05 (kind::i8) with TMA-staged operands and
+// TMA stores of the output.  A TcMatrix is a TMA descriptor of a row-major
+// [rows][K] int8 matrix read in boxes of 128 bytes of K by box_rows rows (128 for
+// A, tc_bn_for(N) for B).  Needs K % 128 == 0, N % 128 == 0 (N % 256 == 0 for
+// ReGLU), a 16-byte aligned output whose row pitch is a multiple of 16 bytes.
+// Returns false (nothing launched) when a shape or the output map is unsupported.
 struct TcMatrix {
     alignas(64) unsigned char map[128];   // CUtensorMap
     uint64_t rows = 0, K = 0;
@@ -45,7 +48,7 @@ struct TcMatrix {
 int tc_bn_for(int N);   // output tile width for N (0: unsupported)
 bool tc_make_matrix(TcMatrix &m, const int8_t *base, uint64_t rows, uint64_t K, int box_rows);
 void gemm_tc_init();
-void launch_gemm_tc(const TcMatrix &A, const TcMatrix &B, int M, int N, int K, int epi, int mult, int shift,
+bool launch_gemm_tc(const TcMatrix &A, const TcMatrix &B, int M, int N, int K, int epi, int mult, int shift,
                     void *out, int ldo, int *err, cudaStream_t st);
 
 void attention_init();

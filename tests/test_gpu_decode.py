@@ -96,3 +96,18 @@ def test_decode_arch2(tmp_path, shipped_path, oracle_mod, doc_tokens):
         assert np.array_equal(e.decompress_chunks(chunks, np.diff(starts)), tokens)
     finally:
         e.close()
+
+
+def test_decode_many_streams_roundtrip(eng, shipped_path):
+    """Thousands of streams of ragged lengths: every GEMM of the lockstep decode
+    runs with a shrinking row count over many output tiles per CTA, including
+    tiles whose last rows lie beyond the active streams."""
+    from compress_zip_b200 import czm, synth
+
+    tok = czm.ModelFile.load(shipped_path).tokenizer()
+    docs = tok.encode_batch(synth.documents(range(3000, 3900), 4096), num_threads=8)
+    tokens, starts = _chunked([np.asarray(d, np.uint32) for d in docs], 128)
+    chunks = eng.compress_chunks(tokens, starts)
+    assert len(chunks) > 6000
+    got = eng.decompress_chunks(chunks, np.diff(starts))
+    assert np.array_equal(got, tokens)
