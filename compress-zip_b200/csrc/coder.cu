@@ -74,6 +74,89 @@ __global__ void k_cdf_lohi(const int32_t *__restrict__ logits, int V, int ld,
     }
 }
 
+// Register-resident version for V <= 128 * G (and so S < 2^30): the row is read
+// once (lane l holds elements 128j + 4l + k), the weights e_i are kept packed,
+// and the division by S uses floor_mul_div.  One warp per row.
+template <int G>
+__global__ void __launch_bounds__(256) k_cdf_lohi_reg(const int32_t *__restrict__ logits, int V, int ld,
+                                                      const uint32_t *__restrict__ sym,
+                                                      const uint16_t *__restrict__ lut_g, uint32_t coef,
+                                                      uint32_t total, int M, uint2 *__restrict__ lohi) {
+    __shared__ uint16_t lut[256];
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) lut[i] = lut_g[i];
+    __syncthreads();
+    const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= M) return;
+    const int4 *src = reinterpret_cast<const int4 *>(logits + (size_t)row * ld);
+    int x[G][4];
+#pragma unroll
+    for (int j = 0; j < G; j++) {
+        int4 v = make_int4(0, 0, 0, 0);
+        if (128 * j + 4 * lane < V) v = __ldcs(src + 32 * j + lane);   // read once: streaming
+        x[j][0] = v.x; x[j][1] = v.y; x[j][2] = v.z; x[j][3] = v.w;
+    }
+    // max and its first index (primitives.rs:278-295); this lane's indices increase with (j, k)
+    int mx = INT32_MIN, am = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < G; j++)
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int i = 128 * j + 4 * lane + k;
+            if (i < V && x[j][k] > mx) { mx = x[j][k]; am = i; }
+        }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const int om = __shfl_xor_sync(0xffffffffu, mx, o);
+        const int oa = __shfl_xor_sync(0xffffffffu, am, o);
+        if (om > mx || (om == mx && oa < am)) { mx = om; am = oa; }
+    }
+    uint32_t ew[G][2];   // packed 16-bit weights
+    uint32_t S = 0;
+#pragma unroll
+    for (int j = 0; j < G; j++) {
+        uint32_t e[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int i = 128 * j + 4 * lane + k;
+            e[k] = i < V ? exp_q16_shift((int)((uint32_t)x[j][k] - (uint32_t)mx), lut, coef) : 0u;
+            S += e[k];
+        }
+        ew[j][0] = e[0] | (e[1] << 16);
+        ew[j][1] = e[2] | (e[3] << 16);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
+    const uint32_t R = total - (uint32_t)V;
+    const uint32_t a = R / S, b = R % S;
+    const float bs = __fdiv_rn((float)b, (float)S);
+    const int sy = (int)sym[row];
+    uint32_t f_all = 0, f_below = 0, f_sym = 0;
+#pragma unroll
+    for (int j = 0; j < G; j++)
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int i = 128 * j + 4 * lane + k;
+            const uint32_t e = (ew[j][k >> 1] >> (16 * (k & 1))) & 0xFFFFu;
+            const uint32_t f = i < V ? 1u + floor_mul_div(e, a, b, S, bs) : 0u;
+            f_all += f;
+            f_below += (i < sy) ? f : 0u;
+            f_sym = (i == sy) ? f : f_sym;
+        }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        f_all += __shfl_xor_sync(0xffffffffu, f_all, o);
+        f_below += __shfl_xor_sync(0xffffffffu, f_below, o);
+        f_sym += __shfl_xor_sync(0xffffffffu, f_sym, o);
+    }
+    if (lane == 0) {
+        const uint32_t rem = total - f_all;   // goes to the argmax (softmax_cdf.rs:125-127)
+        const uint32_t lo = f_below + ((uint32_t)am < (uint32_t)sy ? rem : 0u);
+        const uint32_t hi = lo + f_sym + ((uint32_t)am == (uint32_t)sy ? rem : 0u);
+        lohi[row] = make_uint2(lo, hi);
+    }
+}
+
 struct BitSink {
     uint8_t *out;
     uint32_t cap, len;
@@ -194,7 +277,21 @@ __global__ void k_pack(const uint8_t *__restrict__ slots, const uint64_t *__rest
 void launch_cdf_lohi(const int32_t *logits, int V, int ld, const uint32_t *sym, const uint16_t *lut,
                      uint32_t coef, uint32_t total, int M, uint2 *lohi, cudaStream_t st) {
     if (M == 0) return;
-    k_cdf_lohi<<<(M + 7) / 8, 256, 0, st>>>(logits, V, ld, sym, lut, coef, total, M, lohi);
+    const unsigned grid = (unsigned)((M + 7) / 8);
+    // 16-byte row loads need ld % 4 == 0; the weight bound needs V <= 1024
+    if (ld % 4 == 0 && V <= 1024) {
+        switch ((V + 127) / 128) {
+            case 8: k_cdf_lohi_reg<8><<<grid, 256, 0, st>>>(logits, V, ld, sym, lut, coef, total, M, lohi); return;
+            case 7: k_cdf_lohi_reg<7><<<grid, 256, 0, st>>>(logits, V, ld, sym, lut, coef, total, M, lohi); return;
+            case 6: k_cdf_lohi_reg<6><<<grid, 256, 0, st>>>(logits, V, ld, sym, lut, coef, total, M, lohi); return;
+            case 5: k_cdf_lohi_reg<5><<<grid, 256, 0, st>>>(logits, V, ld, sym, lut, coef, total, M, lohi); return;
+            case 4: k_cdf_lohi_reg<4><<<grid, 256, 0, st>>>(logits, V, ld, sym, lut, coef, total, M, lohi); return;
+            case 3: k_cdf_lohi_reg<3><<<grid, 256, 0, st>>>(logits, V, ld, sym, lut, coef, total, M, lohi); return;
+            case 2: k_cdf_lohi_reg<2><<<grid, 256, 0, st>>>(logits, V, ld, sym, lut, coef, total, M, lohi); return;
+            default: k_cdf_lohi_reg<1><<<grid, 256, 0, st>>>(logits, V, ld, sym, lut, coef, total, M, lohi); return;
+        }
+    }
+    k_cdf_lohi<<<grid, 256, 0, st>>>(logits, V, ld, sym, lut, coef, total, M, lohi);
 }
 
 void launch_encode(const uint2 *lohi, const int *chunk_row0, const int *chunk_len, int n_chunks,

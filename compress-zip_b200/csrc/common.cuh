@@ -62,6 +62,31 @@ __device__ __forceinline__ uint32_t exp_q16(int neg_x, const uint16_t *lut, uint
     return min(65535u, max(1u, out));
 }
 
+// exp_q16 rewritten without the multiply by 65536 >> ip: for ip >= 1,
+// ((2^16 >> ip) * l + 2^15) >> 16 == (l + 2^(ip-1)) >> ip (both are l / 2^ip
+// rounded half up, and 0 for ip > 16).  Same values as exp_q16 for every input.
+__device__ __forceinline__ uint32_t exp_q16_shift(int neg_x, const uint16_t *lut, uint32_t coef) {
+    if (neg_x >= 0) return 65535u;
+    const uint32_t neg = 0u - (uint32_t)neg_x;
+    const uint32_t t256 = (uint32_t)(((unsigned long long)neg * coef + (1ull << 23)) >> 24);
+    const uint32_t ip = t256 >> 8;
+    if (ip >= 31) return 1u;
+    const uint32_t out = ((uint32_t)lut[t256 & 255u] + ((1u << ip) >> 1)) >> ip;
+    return min(65535u, max(1u, out));
+}
+
+// floor(e * R / S) for 0 < e <= S < 2^30 and R < 2^32, with a = R / S and
+// b = R % S precomputed and bs = b / S as a correctly rounded float:
+// e*R/S = e*a + e*b/S; the float estimate of e*b/S (< 2^16) is off by less
+// than 1/64, and one remainder check, exact in wrapping 32-bit arithmetic
+// because the remainder lies in (-S, 2S), fixes it.
+__device__ __forceinline__ uint32_t floor_mul_div(uint32_t e, uint32_t a, uint32_t b, uint32_t S, float bs) {
+    const uint32_t q0 = (uint32_t)__fmul_rn(__uint2float_rn(e), bs);
+    const int r = (int)(e * b - q0 * S);
+    const uint32_t q = q0 - (uint32_t)(r < 0) + (uint32_t)(r >= (int)S);
+    return e * a + q;
+}
+
 // primitives.rs:192-213 -- restoring integer square root
 __device__ __forceinline__ uint32_t isqrt32(uint32_t x) {
     uint32_t op = x, res = 0, one = 1u << 30;

@@ -182,3 +182,33 @@ def test_scalar_attention_kernel(shipped_path, shipped_oracle, oracle_mod, shipp
             oracle_mod.compress_chunks(shipped_oracle, shipped_tokens, starts)
     finally:
         eng.close()
+
+
+@pytest.mark.parametrize("mode", ["ties", "flat", "extreme"])
+def test_cdf_edge_models(shipped_path, tmp_path, oracle_mod, shipped_tokens, mode):
+    """CDF corner cases through real logits: tied maxima (first index wins),
+    a flat row (every weight 65535), and logits far apart (most weights 1)."""
+    from compress_zip_b200 import czm
+    from compress_zip_b200.engine import Engine
+
+    mf = czm.ModelFile.load(shipped_path)
+    t = {k: np.array(v) for k, v in mf.tensors.items()}
+    hw = t["head.weight"].copy()
+    if mode == "ties":
+        hw[1::2] = hw[0::2]                       # logits of tokens 2k and 2k+1 are equal
+    elif mode == "flat":
+        hw[:] = 0                                 # every logit is 0
+    else:
+        hw = np.where(hw >= 0, 127, -127).astype(np.int8)
+    t["head.weight"] = hw
+    p = tmp_path / f"cdf_{mode}.czm"
+    p.write_bytes(czm.write_safetensors(t, mf.metadata))
+    om = oracle_mod.load_model(str(p))
+    eng = Engine.from_file(str(p), 0)
+    try:
+        _trace_equal(eng, om, oracle_mod, shipped_tokens[:400])
+        toks = shipped_tokens[:1500]
+        starts = _starts(len(toks), 512)
+        assert eng.compress_chunks(toks, starts) == oracle_mod.compress_chunks(om, toks, starts)
+    finally:
+        eng.close()
