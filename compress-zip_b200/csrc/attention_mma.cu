@@ -1,40 +1,47 @@
 // attention_mma.cu -- exact causal integer attention on the tensor cores.
 //
 // Same result as rust/src/attention.rs:162-289 run for positions 0..n-1 of a
-// chunk (see attention.cu for the scalar form).  Per warp task: 16 query rows
-// of one head against all their keys, 32 keys per tile.
+// chunk (see attention.cu for the scalar form).  One CTA per chunk stages the
+// chunk's K (RoPE applied) and V in shared memory; its 16 warps take tasks of
+// 8 query rows of one head, longest rows first, and walk their keys in tiles
+// of 32.
 //
-// QK^T: mma.sync m16n8k32 s8*s8 -> s32 gives the exact int32 dot products.  The
-// key order inside a tile is permuted for the QK product so that each thread's
-// accumulator entries are exactly the keys its P fragment needs for P*V
-// (thread t of a quad holds keys 4t..4t+3 and 16+4t..16+4t+3 of rows g, g+8).
+// QK^T: mma.sync m16n8k32 s8*s8 -> s32 gives the exact int32 dot products (the
+// task's 8 rows are A rows 0..7; rows 8..15 are zero).  The key order inside a
+// tile is permuted so that thread t of a quad holds the 8 consecutive keys
+// 8t..8t+7 of its row g, which are also exactly the keys of its P fragment.
 //
 // Online softmax: per row, scores -> prefix max in key order (thread-local run
-// + quad scan) -> records (keys beating everything before them) -> weights
+// + one quad scan) -> records (keys beating everything before them) -> weights
 // w = exp(score - max so far) and rescale factors e = exp(old max - score).
 //
-// P*V: the 16-bit weights are split into a high and a low byte and multiplied
-// with V (s8) as two u8*s8 MMAs into separate accumulators Hi, Lo; each is
-// exactly sum(byte * v) and never overflows (|sum| <= 255*127*4096), so
-// vacc = 256*Hi + Lo (mod 2^32) equals the reference's wrapping i32 sum.
+// P*V is computed transposed, O^T = V^T * P^T (64 dims as the MMA's M, the 8
+// rows as its N): the P^T fragment a thread supplies is its own row's weights.
+// The 16-bit weights are split into a high and a low byte and multiplied with
+// V (s8) as two s8*u8 MMAs into separate accumulators Hi, Lo; each is exactly
+// sum(byte * v) and never overflows (|sum| <= 255*127*4096), so
+// vacc = 256*Hi + Lo (mod 2^32) equals the reference's wrapping i32 sum; an
+// all-ones A operand gives the weight sums.
 // A tile whose rows contain records is replayed in passes: pass q adds the keys
 // of segment q (segment = run of keys between records).  Before pass q every
 // row with a q-th record in the tile folds its state exactly as the reference
 // rescales at that key: state = R(state + 256*Hi + Lo, e),
-// s = ((s + seg_sum) * e + 2^15) >> 16.  The folded state of a warp's 16 rows
-// lives in shared memory as [row][dim] so that all 32 lanes fold one row
-// together (2 dims each).
+// s = ((s + seg_sum) * e + 2^15) >> 16.  The folded state lives in registers in
+// the accumulator layout (row 2t+e of thread (g, t)), each row folded by the 8
+// threads that hold it.  A record whose previous maximum is still INT32_MIN
+// rescales nothing (attention.rs:248-250) and is no segment boundary.
 #include "common.cuh"
 #include "kernels.h"
 
 namespace czg {
 namespace {
 
-constexpr int AM_THREADS = 256;
+constexpr int AM_THREADS = 512;
 constexpr int AM_WARPS = AM_THREADS / 32;
 constexpr int AM_MAX_KEYS = 1024;
-constexpr int AM_ROW = 72;   // words per row of the per-warp state buffers (bank-spread)
-constexpr int AM_WARP_SMEM = 16 * AM_ROW * 4 * 2 + 16 * 32 * 4 + 16 * 4 * 2;   // vst, segbuf, rec_e, nrec, s
+constexpr int AM_ROWS = 8;   // query rows per warp task
+// per warp: record factors [8][32], records per row [8], output staging [8][64]
+constexpr int AM_WARP_SMEM = AM_ROWS * 32 * 4 + AM_ROWS * 4 + AM_ROWS * 64;
 
 __device__ __forceinline__ void mma_s8s8(int (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
     asm volatile(
@@ -44,9 +51,9 @@ __device__ __forceinline__ void mma_s8s8(int (&c)[4], const uint32_t (&a)[4], ui
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ void mma_u8s8(int (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+__device__ __forceinline__ void mma_s8u8(int (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
     asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};\n"
         : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
@@ -83,116 +90,88 @@ __device__ __forceinline__ int score_from_dot(int dot, int mult) {
     return (int)s;
 }
 
-// key (within a 32-key tile) of QK accumulator column / B row n = 8j + r
+// key (within a 32-key tile) of QK accumulator column n = 8j + c: accumulator
+// entry (j, e) of thread t is key 8t + 2j + e, so each thread holds 8
+// consecutive keys and the P*V K index of key 8t + b is 16*(b >> 2) + 4t + (b & 3),
+// which the V^T staging turns into storage position 8t + b = the key itself.
 __device__ __forceinline__ int perm_key(int n) {
-    int j = n >> 3, r = n & 7;
-    return 16 * (j >> 1) + 4 * (r >> 1) + 2 * (j & 1) + (r & 1);
+    const int j = n >> 3, c = n & 7;
+    return 8 * (c >> 1) + 2 * j + (c & 1);
 }
 
 struct Tile {
-    uint32_t w[2][8];     // weights of each row half's 8 entries
-    uint32_t ef[2][8];    // 0, or record flag | rescale factor
-    int lrec[2][2];       // records of this thread per row half and 16-key half
-    int nrec[2];          // records of the row in this tile (quad total)
+    uint32_t w[8];    // weights of the row's 8 entries (keys kb + 8t + i)
+    uint32_t ef[8];   // 0, or (previous max - score) of a record (never 0)
+    int lrec;         // records among this thread's entries
+    int nrec;         // records of the row in this tile (quad total)
 };
 
-// Scores, prefix max, records and weights of one 32-key tile.
-// Entry i of a row half is key kb + 16*(i>>2) + 4t + (i&3).
+// Scores, prefix max, records and weights of row g in one 32-key tile.
 template <bool MASKED, bool WIDE>
-__device__ __forceinline__ void tile_softmax(const int (&sacc)[4][4], int kb, const int (&prow)[2], int n,
-                                             int mult, int t, int lane, int (&m)[2],
-                                             const uint16_t *lut4k, uint32_t c8, Tile &T) {
+__device__ __forceinline__ void tile_softmax(const int (&sacc)[4][4], int kb, int prow, int n, int mult, int t,
+                                             int &m, const uint16_t *lut4k, uint32_t c8, Tile &T) {
+    int sc[8], L[8];
 #pragma unroll
-    for (int hr = 0; hr < 2; hr++) {
-        int sc[8];
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            const int q = i >> 2, b = i & 3;
-            const int j = 2 * q + (b >> 1), e = b & 1;
-            bool valid = true;
-            if (MASKED) valid = kb + 16 * q + 4 * t + b <= prow[hr] && prow[hr] < n;
-            sc[i] = valid ? score_from_dot<WIDE>(sacc[j][2 * hr + e], mult) : INT32_MIN;
-        }
-        int run = m[hr];
-        int total = 0;
-#pragma unroll
-        for (int q = 0; q < 2; q++) {
-            int L[4];
-            L[0] = sc[4 * q];
-#pragma unroll
-            for (int b = 1; b < 4; b++) L[b] = max(L[b - 1], sc[4 * q + b]);
-            int inc = L[3];
-            int u = __shfl_up_sync(0xffffffffu, inc, 1, 4);
-            if (t >= 1) inc = max(inc, u);
-            u = __shfl_up_sync(0xffffffffu, inc, 2, 4);
-            if (t >= 2) inc = max(inc, u);
-            const int excl = __shfl_up_sync(0xffffffffu, inc, 1, 4);
-            const int base = t == 0 ? run : max(run, excl);
-            int prevmax = base;
-            int lrec = 0;
-#pragma unroll
-            for (int b = 0; b < 4; b++) {
-                const int i = 4 * q + b;
-                bool valid = true;
-                if (MASKED) valid = kb + 16 * q + 4 * t + b <= prow[hr] && prow[hr] < n;
-                const int pm = max(base, L[b]);
-                const bool rec = valid && sc[i] > prevmax;
-                T.w[hr][i] = valid ? exp_attn((int)((uint32_t)sc[i] - (uint32_t)pm), lut4k, c8) : 0u;
-                uint32_t f = 0;
-                if (rec) {
-                    // 0x10000 | factor, or 0x20000 while the previous max is still INT32_MIN:
-                    // the reference then keeps its sums unscaled (attention.rs:248-250)
-                    f = prevmax == INT32_MIN
-                            ? 0x20000u
-                            : 0x10000u | exp_attn((int)((uint32_t)prevmax - (uint32_t)sc[i]), lut4k, c8);
-                    lrec++;
-                }
-                T.ef[hr][i] = f;
-                prevmax = pm;
-            }
-            T.lrec[hr][q] = lrec;
-            total += lrec;
-            run = max(run, __shfl_sync(0xffffffffu, inc, (lane & ~3) | 3));
-        }
-        m[hr] = run;
-        total += __shfl_xor_sync(0xffffffffu, total, 1);
-        total += __shfl_xor_sync(0xffffffffu, total, 2);
-        T.nrec[hr] = total;
+    for (int i = 0; i < 8; i++) {
+        bool valid = true;
+        if (MASKED) valid = kb + 8 * t + i <= prow && prow < n;
+        sc[i] = valid ? score_from_dot<WIDE>(sacc[i >> 1][i & 1], mult) : INT32_MIN;
+        L[i] = i ? max(L[i - 1], sc[i]) : sc[i];
     }
+    // exclusive prefix max over the quad: three independent shuffles
+    const int x = L[7];
+    const int y1 = __shfl_up_sync(0xffffffffu, x, 1, 4);
+    const int y2 = __shfl_up_sync(0xffffffffu, x, 2, 4);
+    const int y3 = __shfl_up_sync(0xffffffffu, x, 3, 4);
+    const int z1 = max(x, __shfl_xor_sync(0xffffffffu, x, 1));
+    const int run = m;
+    int base = run;
+    if (t >= 1) base = max(base, y1);
+    if (t >= 2) base = max(base, y2);
+    if (t >= 3) base = max(base, y3);
+    int prevmax = base, lrec = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        bool valid = true;
+        if (MASKED) valid = kb + 8 * t + i <= prow && prow < n;
+        const int pm = max(base, L[i]);
+        T.w[i] = valid ? exp_attn((int)((uint32_t)sc[i] - (uint32_t)pm), lut4k, c8) : 0u;
+        const bool rec = valid && sc[i] > prevmax && prevmax != INT32_MIN;
+        T.ef[i] = rec ? (uint32_t)prevmax - (uint32_t)sc[i] : 0u;
+        lrec += rec;
+        prevmax = pm;
+    }
+    m = max(run, max(z1, __shfl_xor_sync(0xffffffffu, z1, 2)));
+    T.lrec = lrec;
+    const int r1 = lrec + __shfl_xor_sync(0xffffffffu, lrec, 1);
+    T.nrec = r1 + __shfl_xor_sync(0xffffffffu, r1, 2);
 }
 
 // Segment of each entry (records at or before it in key order within the tile),
-// packed one byte per entry in A-fragment word order (word hr + 2q, byte b); the
-// record factors are published to rec_e[row][segment - 1].
-__device__ __forceinline__ void tile_segments(const Tile &T, int t, int g, uint32_t *rec_e, int *nrec_s,
-                                              uint32_t (&segw)[4]) {
+// one byte per entry: word q holds entries 4q..4q+3.  The rescale factors are
+// published to rec_e[row][segment - 1] and the row's record count to rec_n[row].
+__device__ __forceinline__ void tile_segments(const Tile &T, int t, int g, uint32_t *rec_e, int *rec_n,
+                                              uint32_t (&segw)[2], const uint16_t *lut4k, uint32_t c8) {
+    const int c = T.lrec;
+    const int c1 = __shfl_up_sync(0xffffffffu, c, 1, 4);
+    const int c2 = __shfl_up_sync(0xffffffffu, c, 2, 4);
+    const int c3 = __shfl_up_sync(0xffffffffu, c, 3, 4);
+    int sidx = (t >= 1 ? c1 : 0) + (t >= 2 ? c2 : 0) + (t >= 3 ? c3 : 0);
 #pragma unroll
-    for (int hr = 0; hr < 2; hr++) {
-        const int row = g + 8 * hr;
-        int before = 0;
+    for (int q = 0; q < 2; q++) {
+        uint32_t word = 0;
 #pragma unroll
-        for (int q = 0; q < 2; q++) {
-            int cinc = T.lrec[hr][q];
-            int cu = __shfl_up_sync(0xffffffffu, cinc, 1, 4);
-            if (t >= 1) cinc += cu;
-            cu = __shfl_up_sync(0xffffffffu, cinc, 2, 4);
-            if (t >= 2) cinc += cu;
-            int sidx = before + cinc - T.lrec[hr][q];
-            uint32_t word = 0;
-#pragma unroll
-            for (int b = 0; b < 4; b++) {
-                const int i = 4 * q + b;
-                if (T.ef[hr][i]) {
-                    sidx++;
-                    rec_e[row * 32 + sidx - 1] = T.ef[hr][i];
-                }
-                word |= (uint32_t)sidx << (8 * b);
+        for (int b = 0; b < 4; b++) {
+            const int i = 4 * q + b;
+            if (T.ef[i]) {
+                sidx++;
+                rec_e[g * 32 + sidx - 1] = 0x10000u | exp_attn((int)T.ef[i], lut4k, c8);
             }
-            segw[hr + 2 * q] = word;
-            before += __shfl_sync(0xffffffffu, cinc, (threadIdx.x & 31 & ~3) | 3);
+            word |= (uint32_t)sidx << (8 * b);
         }
-        if (t == 0) nrec_s[row] = T.nrec[hr];
+        segw[q] = word;
     }
+    if (t == 0) rec_n[g] = T.nrec;
 }
 
 // 0xFF in each byte of x equal to q, else 0
@@ -216,16 +195,14 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
     const int npad = (n + 31) & ~31;
     const int vt_ld = ((npad + 127) & ~127) + 32;   // 8 dims of a fragment land on distinct banks
     uint8_t *ks = smem;                              // [npad][64], dims permuted per thread quarter
-    uint8_t *vt = ks + npad * 64;                    // [64][vt_ld], keys permuted per 32-key tile
+    uint8_t *vt = ks + npad * 64;                    // [64][vt_ld], keys in order
     uint8_t *wsm = vt + 64 * vt_ld;
     const uint16_t *lut4k = lut4k_g;   // 8 KB, stays in L1
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, t = lane & 3;
-    int *vst = reinterpret_cast<int *>(wsm + warp * AM_WARP_SMEM);   // [16][AM_ROW] folded state
-    int *segbuf = vst + 16 * AM_ROW;                                 // [16][AM_ROW] segment sums
-    uint32_t *rec_e = reinterpret_cast<uint32_t *>(segbuf + 16 * AM_ROW);  // [16][32]
-    int *nrec_s = reinterpret_cast<int *>(rec_e + 16 * 32);          // [16]
-    uint32_t *s_s = reinterpret_cast<uint32_t *>(nrec_s + 16);       // [16] final s (low 32 bits)
+    uint32_t *rec_e = reinterpret_cast<uint32_t *>(wsm + warp * AM_WARP_SMEM);   // [8][32]
+    int *rec_n = reinterpret_cast<int *>(rec_e + AM_ROWS * 32);                  // [8]
+    uint8_t *ostage = reinterpret_cast<uint8_t *>(rec_n + AM_ROWS);              // [8][64]
 
     // K row layout: bytes [16t' + 4k + b] = dim 16k + 4t' + b, so thread t reads its
     // four B words (dims 4t, 16+4t, 32+4t, 48+4t) as one 16-byte load.
@@ -239,17 +216,15 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
         }
         const int kq = wk >> 2, tq = wk & 3;   // dims 16*kq + 4*tq ..
         *reinterpret_cast<uint32_t *>(ks + key * 64 + 16 * tq + 4 * kq) = kw;
-        // V^T: tile position of key: keys 4u..4u+3 -> 8u + 0..3, keys 16+4u.. -> 8u + 4..7
-        const int kt = key & 31;
-        const int pos = (key & ~31) + 8 * ((kt & 15) >> 2) + 4 * (kt >> 4) + (kt & 3);
 #pragma unroll
-        for (int b = 0; b < 4; b++) vt[(4 * wk + b) * vt_ld + pos] = (uint8_t)(v >> (8 * b));
+        for (int b = 0; b < 4; b++) vt[(4 * wk + b) * vt_ld + key] = (uint8_t)(v >> (8 * b));
     }
     if (tid == 0) task_ctr = 0;
     __syncthreads();
 
     const uint32_t c8 = 378194u << 8;   // ATTN_COEF_Q24 (attention.rs:14-19) << 8
-    const int n_rb = (n + 15) >> 4;
+    const uint32_t ones[4] = {0x01010101u, 0x01010101u, 0x01010101u, 0x01010101u};
+    const int n_rb = (n + AM_ROWS - 1) / AM_ROWS;
     const int n_tasks = n_rb * n_heads;
     for (;;) {
         int task = 0;
@@ -258,20 +233,18 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
         if (task >= n_tasks) break;
         const int rb = n_rb - 1 - task / n_heads;   // longest rows first
         const int h = task % n_heads;
-        const int p0 = rb * 16;
-        const int prow[2] = {p0 + g, p0 + g + 8};
-        const int p_last = min(p0 + 15, n - 1);
-        const bool full_rows = p0 + 15 < n;
+        const int p0 = rb * AM_ROWS;
+        const int prow = p0 + g;                     // the QK / softmax row of this thread
+        const int p_last = min(p0 + AM_ROWS - 1, n - 1);
+        const bool full_rows = p0 + AM_ROWS - 1 < n;
         const int mult = score_mult[h];
 
-        // Q fragments with RoPE (attention.rs:53-83); pairs (i, i+32) live in kk = 0 / 1
+        // Q fragment of row g with RoPE (attention.rs:53-83); pairs (i, i+32) live in kk = 0 / 1
         uint32_t qa[2][4];
-#pragma unroll
-        for (int hr = 0; hr < 2; hr++) {
-            const int p = prow[hr];
+        {
             uint32_t raw[4] = {0, 0, 0, 0};   // dims 4t, 16+4t, 32+4t, 48+4t (+0..3)
-            if (p < n) {
-                const int8_t *qr = qkv + (size_t)(r0 + p) * ldq + h * 64;
+            if (prow < n) {
+                const int8_t *qr = qkv + (size_t)(r0 + prow) * ldq + h * 64;
 #pragma unroll
                 for (int k = 0; k < 4; k++) raw[k] = *reinterpret_cast<const uint32_t *>(qr + 16 * k + 4 * t);
             }
@@ -283,22 +256,22 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
                     const int i = 16 * k + 4 * t + b;   // dim in 0..31; partner i + 32
                     int x = sext8(raw[k], b), y = sext8(raw[k + 2], b);
                     int cs = 0, sn = 0;
-                    if (p < n) { cs = rope_cos[p * kHalfDim + i]; sn = rope_sin[p * kHalfDim + i]; }
+                    if (prow < n) { cs = rope_cos[prow * kHalfDim + i]; sn = rope_sin[prow * kHalfDim + i]; }
                     int xr = clamp127(sra_rne32(sra_rne32(x * cs - y * sn, 15), 1));
                     int yr = clamp127(sra_rne32(sra_rne32(x * sn + y * cs, 15), 1));
                     lo[k] |= (uint32_t)(uint8_t)xr << (8 * b);
                     hi[k] |= (uint32_t)(uint8_t)yr << (8 * b);
                 }
-            qa[0][hr] = lo[0];
-            qa[0][hr + 2] = lo[1];
-            qa[1][hr] = hi[0];
-            qa[1][hr + 2] = hi[1];
+            qa[0][0] = lo[0];
+            qa[0][2] = lo[1];
+            qa[1][0] = hi[0];
+            qa[1][2] = hi[1];
+            qa[0][1] = qa[0][3] = qa[1][1] = qa[1][3] = 0u;   // A rows 8..15
         }
 
-        // per-row running max and weight sums, replicated over the quad
-        int m[2] = {INT32_MIN, INT32_MIN};
+        int m = INT32_MIN;   // running max of row g
+        // PV layout: thread (g, t) holds rows 2t + e, dims 16*mi + g + 8*dh at [mi][2*dh + e]
         unsigned long long s_state[2] = {0, 0};
-        int sh[4] = {0, 0, 0, 0}, sl[4] = {0, 0, 0, 0};   // weight sums since the last fold
         if (sink_key != nullptr) {   // attention.rs:211-224
             int accs[4] = {0, 0, 0, 0};
 #pragma unroll
@@ -307,16 +280,15 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
                 uint32_t b1 = *reinterpret_cast<const uint32_t *>(sink_key + 32 * kk + 16 + 4 * t);
                 mma_s8s8(accs, qa[kk], b0, b1);   // every B column is the sink key
             }
-            m[0] = score_from_dot<true>(accs[0], mult);
-            m[1] = score_from_dot<true>(accs[2], mult);
+            m = score_from_dot<true>(accs[0], mult);
             s_state[0] = s_state[1] = 65535ull;
         }
-        for (int i = lane; i < 16 * AM_ROW; i += 32) vst[i] = 0;
-        int hiacc[8][4], loacc[8][4];
+        int hiacc[4][4], loacc[4][4], vst[4][4];
 #pragma unroll
-        for (int jd = 0; jd < 8; jd++)
+        for (int mi = 0; mi < 4; mi++)
 #pragma unroll
-            for (int k = 0; k < 4; k++) { hiacc[jd][k] = 0; loacc[jd][k] = 0; }
+            for (int k = 0; k < 4; k++) { hiacc[mi][k] = 0; loacc[mi][k] = 0; vst[mi][k] = 0; }
+        int shs[4] = {0, 0, 0, 0}, sls[4] = {0, 0, 0, 0};   // weight sums of rows 2t, 2t+1 in [0], [1]
 
         for (int kb = 0; kb <= p_last; kb += 32) {
             // ---- S = Q K^T over 32 keys (permuted columns) ----
@@ -328,137 +300,105 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
                 mma_s8s8(sacc[j], qa[0], kw.x, kw.y);
                 mma_s8s8(sacc[j], qa[1], kw.z, kw.w);
             }
-            uint2 bv[8];
+            // V^T A fragments: dims 16mi+g / +8; K 4t.. (word 0) and 16+4t.. (word 1) = keys 8t..8t+7
+            uint32_t va[4][4];
 #pragma unroll
-            for (int jd = 0; jd < 8; jd++)
-                bv[jd] = *reinterpret_cast<const uint2 *>(vt + (8 * jd + g) * vt_ld + kb + 8 * t);
+            for (int mi = 0; mi < 4; mi++) {
+                const uint2 lo2 = *reinterpret_cast<const uint2 *>(vt + (16 * mi + g) * vt_ld + kb + 8 * t);
+                const uint2 hi2 = *reinterpret_cast<const uint2 *>(vt + (16 * mi + g + 8) * vt_ld + kb + 8 * t);
+                va[mi][0] = lo2.x;
+                va[mi][1] = hi2.x;
+                va[mi][2] = lo2.y;
+                va[mi][3] = hi2.y;
+            }
 
             Tile T;
             if (!full_rows || kb + 31 > p0)
-                tile_softmax<true, WIDE>(sacc, kb, prow, n, mult, t, lane, m, lut4k, c8, T);
+                tile_softmax<true, WIDE>(sacc, kb, prow, n, mult, t, m, lut4k, c8, T);
             else
-                tile_softmax<false, WIDE>(sacc, kb, prow, n, mult, t, lane, m, lut4k, c8, T);
-            // full P fragments (u8 halves of the weights)
-            uint32_t phi[4], plo[4];
+                tile_softmax<false, WIDE>(sacc, kb, prow, n, mult, t, m, lut4k, c8, T);
+            // P^T B fragments (u8 halves of the weights): word q = entries 4q..4q+3
+            uint32_t phi[2], plo[2];
 #pragma unroll
-            for (int hr = 0; hr < 2; hr++)
-#pragma unroll
-                for (int q = 0; q < 2; q++) {
-                    const uint32_t *wq = &T.w[hr][4 * q];
-                    const uint32_t x01 = prmt(wq[0], wq[1], 0x5140u);   // lo0 lo1 hi0 hi1
-                    const uint32_t x23 = prmt(wq[2], wq[3], 0x5140u);
-                    plo[hr + 2 * q] = prmt(x01, x23, 0x5410u);
-                    phi[hr + 2 * q] = prmt(x01, x23, 0x7632u);
-                }
-            const int maxrec = (int)__reduce_max_sync(0xffffffffu, (unsigned)max(T.nrec[0], T.nrec[1]));
-            uint32_t segw[4] = {0, 0, 0, 0};
+            for (int q = 0; q < 2; q++) {
+                const uint32_t x01 = prmt(T.w[4 * q], T.w[4 * q + 1], 0x5140u);   // lo0 lo1 hi0 hi1
+                const uint32_t x23 = prmt(T.w[4 * q + 2], T.w[4 * q + 3], 0x5140u);
+                plo[q] = prmt(x01, x23, 0x5410u);
+                phi[q] = prmt(x01, x23, 0x7632u);
+            }
+            const int maxrec = (int)__reduce_max_sync(0xffffffffu, (unsigned)T.nrec);
+            uint32_t segw[2] = {0, 0};
+            int nr[2] = {0, 0};   // records of the PV rows 2t, 2t+1
             if (maxrec > 0) {
-                tile_segments(T, t, g, rec_e, nrec_s, segw);
+                tile_segments(T, t, g, rec_e, rec_n, segw, lut4k, c8);
                 __syncwarp();
+                nr[0] = rec_n[2 * t];
+                nr[1] = rec_n[2 * t + 1];
             }
             for (int pass = 0; pass <= maxrec; pass++) {
                 if (pass > 0) {
-                    // rows with a pass-th record hand their segment sums to the warp
+                    // rows with a pass-th record fold their state (attention.rs:248-263)
 #pragma unroll
-                    for (int hr = 0; hr < 2; hr++) {
-                        if (T.nrec[hr] >= pass) {
-                            const int row = g + 8 * hr;
-                            const uint32_t f = rec_e[row * 32 + pass - 1];
-                            const unsigned long long stot = s_state[hr] +
-                                256ull * (uint32_t)sh[2 * hr] + (unsigned long long)(uint32_t)sl[2 * hr];
-                            s_state[hr] = (f & 0x20000u) ? stot : (stot * (f & 0xFFFFu) + 0x8000ull) >> 16;
-                            sh[2 * hr] = sh[2 * hr + 1] = sl[2 * hr] = sl[2 * hr + 1] = 0;
+                    for (int e = 0; e < 2; e++) {
+                        if (nr[e] >= pass) {
+                            const uint32_t ef = rec_e[(2 * t + e) * 32 + pass - 1] & 0xFFFFu;
+                            const unsigned long long stot = s_state[e] + 256ull * (uint32_t)shs[e] +
+                                                            (unsigned long long)(uint32_t)sls[e];
+                            s_state[e] = (stot * ef + 0x8000ull) >> 16;
+                            shs[e] = sls[e] = 0;
 #pragma unroll
-                            for (int jd = 0; jd < 8; jd++) {
-                                int2 v2;
-                                v2.x = (int)(((uint32_t)hiacc[jd][2 * hr] << 8) + (uint32_t)loacc[jd][2 * hr]);
-                                v2.y = (int)(((uint32_t)hiacc[jd][2 * hr + 1] << 8) + (uint32_t)loacc[jd][2 * hr + 1]);
-                                *reinterpret_cast<int2 *>(segbuf + row * AM_ROW + 8 * jd + 2 * t) = v2;
-                                hiacc[jd][2 * hr] = hiacc[jd][2 * hr + 1] = 0;
-                                loacc[jd][2 * hr] = loacc[jd][2 * hr + 1] = 0;
-                            }
+                            for (int mi = 0; mi < 4; mi++)
+#pragma unroll
+                                for (int k = e; k < 4; k += 2) {
+                                    const uint32_t x = (uint32_t)vst[mi][k] + ((uint32_t)hiacc[mi][k] << 8) +
+                                                       (uint32_t)loacc[mi][k];
+                                    long long pr = (long long)(int)x * (long long)ef;
+                                    pr += pr >= 0 ? (1ll << 15) : -(1ll << 15);
+                                    vst[mi][k] = (int)(pr >> 16);
+                                    hiacc[mi][k] = 0;
+                                    loacc[mi][k] = 0;
+                                }
                         }
                     }
-                    const uint32_t fold0 = __ballot_sync(0xffffffffu, t == 0 && T.nrec[0] >= pass);
-                    const uint32_t fold1 = __ballot_sync(0xffffffffu, t == 0 && T.nrec[1] >= pass);
-                    __syncwarp();
-                    // the whole warp folds each such row, 2 dims per lane (attention.rs:252-263)
-                    uint32_t rows = 0;
-#pragma unroll
-                    for (int k = 0; k < 8; k++) rows |= (((fold0 >> (4 * k)) & 1u) << k) | (((fold1 >> (4 * k)) & 1u) << (k + 8));
-                    while (rows) {
-                        const int row = __ffs(rows) - 1;
-                        rows &= rows - 1;
-                        const uint32_t f = rec_e[row * 32 + pass - 1];
-                        const long long e = f & 0xFFFFu;
-                        int2 sv = *reinterpret_cast<int2 *>(vst + row * AM_ROW + 2 * lane);
-                        const int2 gv = *reinterpret_cast<const int2 *>(segbuf + row * AM_ROW + 2 * lane);
-                        uint32_t x0 = (uint32_t)sv.x + (uint32_t)gv.x, x1 = (uint32_t)sv.y + (uint32_t)gv.y;
-                        if (!(f & 0x20000u)) {
-                            long long p0_ = (long long)(int)x0 * e, p1_ = (long long)(int)x1 * e;
-                            p0_ += p0_ >= 0 ? (1ll << 15) : -(1ll << 15);
-                            p1_ += p1_ >= 0 ? (1ll << 15) : -(1ll << 15);
-                            x0 = (uint32_t)(int)(p0_ >> 16);
-                            x1 = (uint32_t)(int)(p1_ >> 16);
-                        }
-                        sv.x = (int)x0;
-                        sv.y = (int)x1;
-                        *reinterpret_cast<int2 *>(vst + row * AM_ROW + 2 * lane) = sv;
-                    }
-                    __syncwarp();
                 }
-                // P fragments of this pass: bytes of entries in segment `pass`
-                uint32_t ahi[4], alo[4];
-                if (maxrec == 0) {
-#pragma unroll
-                    for (int a = 0; a < 4; a++) { ahi[a] = phi[a]; alo[a] = plo[a]; }
-                } else {
-#pragma unroll
-                    for (int a = 0; a < 4; a++) {
-                        const uint32_t mk = bytes_equal(segw[a], (uint32_t)pass);
-                        ahi[a] = phi[a] & mk;
-                        alo[a] = plo[a] & mk;
-                    }
+                // P^T of this pass: bytes of entries in segment `pass`
+                uint32_t bh0 = phi[0], bh1 = phi[1], bl0 = plo[0], bl1 = plo[1];
+                if (maxrec > 0) {
+                    const uint32_t m0 = bytes_equal(segw[0], (uint32_t)pass);
+                    const uint32_t m1 = bytes_equal(segw[1], (uint32_t)pass);
+                    bh0 &= m0; bl0 &= m0; bh1 &= m1; bl1 &= m1;
                 }
-                mma_u8s8(sh, ahi, 0x01010101u, 0x01010101u);   // weight sums (all-ones column)
-                mma_u8s8(sl, alo, 0x01010101u, 0x01010101u);
+                mma_s8u8(shs, ones, bh0, bh1);   // weight sums (all-ones rows)
+                mma_s8u8(sls, ones, bl0, bl1);
 #pragma unroll
-                for (int jd = 0; jd < 8; jd++) {
-                    mma_u8s8(hiacc[jd], ahi, bv[jd].x, bv[jd].y);
-                    mma_u8s8(loacc[jd], alo, bv[jd].x, bv[jd].y);
+                for (int mi = 0; mi < 4; mi++) {
+                    mma_s8u8(hiacc[mi], va[mi], bh0, bh1);
+                    mma_s8u8(loacc[mi], va[mi], bl0, bl1);
                 }
             }
         }
 
-        // output: clamp(round_half_even(vacc / s)) (attention.rs:279-284)
+        // output: clamp(round_half_even(vacc / s)) (attention.rs:279-284), staged per warp
 #pragma unroll
-        for (int hr = 0; hr < 2; hr++) {
-            const int row = g + 8 * hr;
+        for (int e = 0; e < 2; e++) {
+            const unsigned long long sv = s_state[e] + 256ull * (uint32_t)shs[e] + (unsigned long long)(uint32_t)sls[e];
+            const unsigned long long den = sv == 0 ? 1ull : sv;
+            uint8_t *orow = ostage + (2 * t + e) * 64;
 #pragma unroll
-            for (int jd = 0; jd < 8; jd++) {
-                int2 v2;
-                v2.x = (int)(((uint32_t)hiacc[jd][2 * hr] << 8) + (uint32_t)loacc[jd][2 * hr]);
-                v2.y = (int)(((uint32_t)hiacc[jd][2 * hr + 1] << 8) + (uint32_t)loacc[jd][2 * hr + 1]);
-                *reinterpret_cast<int2 *>(segbuf + row * AM_ROW + 8 * jd + 2 * t) = v2;
-            }
-            if (t == 0) {
-                const unsigned long long s = s_state[hr] + 256ull * (uint32_t)sh[2 * hr] +
-                                             (unsigned long long)(uint32_t)sl[2 * hr];
-                s_s[row] = s == 0 ? 1u : (uint32_t)min(s, 0xFFFFFFFFull);
-                nrec_s[row] = s > 0xFFFFFFFFull;   // s beyond 32 bits: every quotient is 0
-            }
+            for (int mi = 0; mi < 4; mi++)
+#pragma unroll
+                for (int dh = 0; dh < 2; dh++) {
+                    const int k = 2 * dh + e;
+                    const int x = (int)((uint32_t)vst[mi][k] + ((uint32_t)hiacc[mi][k] << 8) + (uint32_t)loacc[mi][k]);
+                    orow[16 * mi + g + 8 * dh] = (uint8_t)clamp127(div_rne_s32_u64(x, den));
+                }
         }
         __syncwarp();
-        for (int row = 0; row < 16; row++) {
-            const int p = p0 + row;
-            if (p >= n) break;
-            const int2 sv = *reinterpret_cast<const int2 *>(vst + row * AM_ROW + 2 * lane);
-            const int2 gv = *reinterpret_cast<const int2 *>(segbuf + row * AM_ROW + 2 * lane);
-            const unsigned long long den = nrec_s[row] ? 0x100000000ull : s_s[row];
-            const int x0 = (int)((uint32_t)sv.x + (uint32_t)gv.x), x1 = (int)((uint32_t)sv.y + (uint32_t)gv.y);
-            const uint16_t pk = (uint16_t)(uint8_t)clamp127(div_rne_s32_u64(x0, den)) |
-                                ((uint16_t)(uint8_t)clamp127(div_rne_s32_u64(x1, den)) << 8);
-            *reinterpret_cast<uint16_t *>(out + (size_t)(r0 + p) * ldo + h * 64 + 2 * lane) = pk;
+        {   // 8 rows x 4 pieces of 16 bytes: one per lane
+            const int row = lane >> 2, part = lane & 3;
+            if (p0 + row < n)
+                *reinterpret_cast<uint4 *>(out + (size_t)(r0 + p0 + row) * ldo + h * 64 + 16 * part) =
+                    *reinterpret_cast<const uint4 *>(ostage + row * 64 + 16 * part);
         }
         __syncwarp();
     }
