@@ -26,7 +26,8 @@
 // of segment q (segment = run of keys between records).  Before pass q every
 // row with a q-th record in the tile folds its state exactly as the reference
 // rescales at that key: state = R(state + 256*Hi + Lo, e),
-// s = ((s + seg_sum) * e + 2^15) >> 16.  The folded state lives in registers in
+// s = ((s + seg_sum) * e + 2^15) >> 16 (kept as an offset to the running
+// accumulators, which are never reset).  The folded state lives in registers in
 // the accumulator layout (row 2t+e of thread (g, t)), each row folded by the 8
 // threads that hold it.  A record whose previous maximum is still INT32_MIN
 // rescales nothing (attention.rs:248-250) and is no segment boundary.
@@ -65,16 +66,14 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
     return d;
 }
 
-// exp_q16 with the attention coefficient via a 4096-entry table indexed by
-// t256 (entries for t256 >= 4096 are all 1, whatever the exp2 LUT holds).
+// exp_q16 with the attention coefficient via a table indexed by min(t256, 4096)
+// (entry 4096 is 1, the value of every t256 >= 4096, whatever the exp2 LUT holds).
 // t256 = floor((neg * coef + 2^23) / 2^24) = hi + (lo >= 2^31) of neg * (coef << 8).
 __device__ __forceinline__ uint32_t exp_attn(int diff, const uint16_t *lut4k, uint32_t c8) {
-    if (diff >= 0) return 65535u;
-    uint32_t neg = 0u - (uint32_t)diff;
-    uint32_t t = __umulhi(neg, c8) + ((neg * c8) >> 31);
-    uint32_t w = 1u;
-    if (t < 4096u) w = __ldg(lut4k + t);   // only lanes near the running max touch the table
-    return w;
+    const uint32_t neg = 0u - (uint32_t)diff;
+    const uint32_t t = min(__umulhi(neg, c8) + ((neg * c8) >> 31), 4096u);
+    const uint32_t w = __ldg(lut4k + t);
+    return diff >= 0 ? 65535u : w;
 }
 
 // score = round_even(round_even(dot / 4) * mult / 2^15) saturated to int32
@@ -341,22 +340,20 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
 #pragma unroll
                     for (int e = 0; e < 2; e++) {
                         if (nr[e] >= pass) {
+                            // the accumulators keep running: state' = R(state + A) - A, with A the
+                            // accumulator value now, so that state + A stays the reference's value
                             const uint32_t ef = rec_e[(2 * t + e) * 32 + pass - 1] & 0xFFFFu;
-                            const unsigned long long stot = s_state[e] + 256ull * (uint32_t)shs[e] +
-                                                            (unsigned long long)(uint32_t)sls[e];
-                            s_state[e] = (stot * ef + 0x8000ull) >> 16;
-                            shs[e] = sls[e] = 0;
+                            const unsigned long long sa = 256ull * (uint32_t)shs[e] + (unsigned long long)(uint32_t)sls[e];
+                            s_state[e] = (((s_state[e] + sa) * ef + 0x8000ull) >> 16) - sa;
 #pragma unroll
                             for (int mi = 0; mi < 4; mi++)
 #pragma unroll
                                 for (int k = e; k < 4; k += 2) {
-                                    const uint32_t x = (uint32_t)vst[mi][k] + ((uint32_t)hiacc[mi][k] << 8) +
-                                                       (uint32_t)loacc[mi][k];
-                                    long long pr = (long long)(int)x * (long long)ef;
-                                    pr += pr >= 0 ? (1ll << 15) : -(1ll << 15);
-                                    vst[mi][k] = (int)(pr >> 16);
-                                    hiacc[mi][k] = 0;
-                                    loacc[mi][k] = 0;
+                                    const uint32_t a = ((uint32_t)hiacc[mi][k] << 8) + (uint32_t)loacc[mi][k];
+                                    const int x = (int)((uint32_t)vst[mi][k] + a);
+                                    // (x*e +- 2^15) >> 16 with the sign of x (e >= 1)
+                                    const long long pr = (long long)x * (long long)ef + 0x8000ll;
+                                    vst[mi][k] = (int)((uint32_t)(pr >> 16) + (uint32_t)(x >> 31) - a);
                                 }
                         }
                     }

@@ -76,7 +76,7 @@ struct czg_ctx {
     int vpad = 0;           // vocab rounded up to the GEMM tile (extra head rows are zero)
     int8_t *embed = nullptr, *final_norm = nullptr, *head_w = nullptr;
     uint16_t *lut = nullptr;
-    uint16_t *lut4k = nullptr;   // exp_q16 by t256 < 4096 (lut.rs:213-235 unrolled over ip)
+    uint16_t *lut4k = nullptr;   // exp_q16 by t256 <= 4096 (lut.rs:213-235 unrolled over ip)
     int16_t *rope_cos = nullptr, *rope_sin = nullptr;
     std::vector<LayerDev> layers;
     std::vector<void *> allocs;
@@ -281,12 +281,12 @@ int load_model(czg_ctx *c, const uint8_t *bytes, size_t len) {
     {   // t256 -> clamp(((65536 >> (t256 >> 8)) * lut[t256 & 255] + 2^15) >> 16, 1, 65535)
         uint16_t lut8[256];
         memcpy(lut8, t->data, 512);
-        std::vector<uint16_t> l4(4096);
+        std::vector<uint16_t> l4(4104, 1);   // entries 4096.. are 1: every t256 >= 4096 gives 1
         for (uint32_t tt = 0; tt < 4096; tt++) {
             uint32_t o = (((1u << 16) >> (tt >> 8)) * (uint32_t)lut8[tt & 255] + 0x8000u) >> 16;
             l4[tt] = (uint16_t)std::min(65535u, std::max(1u, o));
         }
-        if (!upload(c, &c->lut4k, l4.data(), 8192)) return CZG_E_DEVICE;
+        if (!upload(c, &c->lut4k, l4.data(), l4.size() * 2)) return CZG_E_DEVICE;
     }
     for (int k = 0; k < 2; k++) {
         const char *nm = k ? "lut.rope_sin" : "lut.rope_cos";
