@@ -87,23 +87,18 @@ __device__ __forceinline__ uint32_t floor_mul_div(uint32_t e, uint32_t a, uint32
     return e * a + q;
 }
 
-// primitives.rs:192-213 -- restoring integer square root
+// primitives.rs:192-213 -- floor(sqrt(x)), which the reference computes with the
+// restoring digit-by-digit method.  Here: the correctly rounded float square root
+// of the correctly rounded float of x is within one of floor(sqrt(x)) for every
+// 32-bit x, and one step in each direction makes it exact (checked against the
+// restoring method for all 2^32 inputs).
 __device__ __forceinline__ uint32_t isqrt32(uint32_t x) {
-    uint32_t op = x, res = 0, one = 1u << 30;
-    while (one > op) one >>= 2;
-    while (one != 0) {
-        if (op >= res + one) {
-            op -= res + one;
-            res = (res >> 1) + one;
-        } else {
-            res >>= 1;
-        }
-        one >>= 2;
-    }
-    return res;
+    uint32_t r = (uint32_t)__fsqrt_rn(__uint2float_rn(x));
+    if ((unsigned long long)r * r > x) r--;
+    else if ((unsigned long long)(r + 1) * (r + 1) <= x) r++;
+    return r;
 }
 
-// primitives.rs:80-97 -- ties to even only when 2r == d exactly
 __device__ __forceinline__ uint32_t udiv_rne32(uint32_t n, uint32_t d) {
     if (d == 0) return 0;
     uint32_t q = n / d, r = n - q * d, tr = r << 1;

@@ -85,6 +85,7 @@ struct czg_ctx {
     int cap_rows = 0, cap_chunks = 0;
     uint32_t *tokens = nullptr, *tok_in = nullptr, *tok_out = nullptr;
     int *pos = nullptr, *x_res = nullptr, *err_flag = nullptr;
+    bool res16 = false;   // residual stream stored as int16 (exact for n_layers <= 128)
     int8_t *xn = nullptr, *qkv = nullptr, *kv = nullptr, *attn = nullptr, *o8 = nullptr, *hbuf = nullptr;
     int32_t *logits = nullptr;
     uint2 *lohi = nullptr;
@@ -312,6 +313,7 @@ int load_model(czg_ctx *c, const uint8_t *bytes, size_t len) {
         return fail(c, CZG_E_UNSUPPORTED, "softmax.target_total must lie in (vocab_size, 2^30)");
 
     c->layers.resize(m.n_layers);
+    c->res16 = m.n_layers <= 128 && getenv("CZG_RESIDUAL32") == nullptr;
     for (int i = 0; i < m.n_layers; i++) {
         LayerDev &L = c->layers[i];
         std::string p = "layers." + std::to_string(i) + ".";
@@ -449,7 +451,7 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
                     c->pos, c->err_flag, st);
     });
     timed(c, kEmbedNorm, [&] {
-        launch_embed_norm(c->tok_in, c->embed, c->layers[0].attn_norm, M, d, c->eps, c->x_res, c->xn, st);
+        launch_embed_norm(c->tok_in, c->embed, c->layers[0].attn_norm, M, d, c->eps, c->x_res, c->res16, c->xn, st);
     });
     for (int l = 0; l < m.n_layers; l++) {
         const LayerDev &L = c->layers[l];
@@ -477,7 +479,7 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
                  c->o8, d);
         });
         timed(c, kResidualNorm, [&] {
-            launch_residual_norm(c->o8, L.ffn_norm, L.post_attn_norm, M, d, c->eps, c->x_res, c->xn, st);
+            launch_residual_norm(c->o8, L.ffn_norm, L.post_attn_norm, M, d, c->eps, c->x_res, c->res16, c->xn, st);
         });
         timed(c, kGemmUp, [&] {
             gemm(c, c->tm_xn, L.tm_up, c->xn, L.up_w, M, 2 * dff, d, kEpiReglu, L.up_mult, L.up_shift,
@@ -489,7 +491,7 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
         });
         const int8_t *next = l + 1 < m.n_layers ? c->layers[l + 1].attn_norm : c->final_norm;
         timed(c, kResidualNorm, [&] {
-            launch_residual_norm(c->o8, L.post_ffn_norm, next, M, d, c->eps, c->x_res, c->xn, st);
+            launch_residual_norm(c->o8, L.post_ffn_norm, next, M, d, c->eps, c->x_res, c->res16, c->xn, st);
         });
     }
     if (tr && tr->final_in)
@@ -731,7 +733,7 @@ int decompress_impl(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts
             while (active > 0 && (int)n_tokens[order[w0 + active - 1]] <= step) active--;
             const int M = active;
             timed(c, kEmbedNorm, [&] {
-                launch_embed_norm(c->tok_in, c->embed, c->layers[0].attn_norm, M, d, c->eps, c->x_res, c->xn, s);
+                launch_embed_norm(c->tok_in, c->embed, c->layers[0].attn_norm, M, d, c->eps, c->x_res, c->res16, c->xn, s);
             });
             for (int l = 0; l < m.n_layers; l++) {
                 const LayerDev &L = c->layers[l];
@@ -752,7 +754,7 @@ int decompress_impl(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts
                          c->o8, d);
                 });
                 timed(c, kResidualNorm, [&] {
-                    launch_residual_norm(c->o8, L.ffn_norm, L.post_attn_norm, M, d, c->eps, c->x_res, c->xn, s);
+                    launch_residual_norm(c->o8, L.ffn_norm, L.post_attn_norm, M, d, c->eps, c->x_res, c->res16, c->xn, s);
                 });
                 timed(c, kGemmUp, [&] {
                     gemm(c, c->tm_xn, L.tm_up, c->xn, L.up_w, M, 2 * dff, d, kEpiReglu, L.up_mult, L.up_shift,
@@ -764,7 +766,7 @@ int decompress_impl(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts
                 });
                 const int8_t *next = l + 1 < m.n_layers ? c->layers[l + 1].attn_norm : c->final_norm;
                 timed(c, kResidualNorm, [&] {
-                    launch_residual_norm(c->o8, L.post_ffn_norm, next, M, d, c->eps, c->x_res, c->xn, s);
+                    launch_residual_norm(c->o8, L.post_ffn_norm, next, M, d, c->eps, c->x_res, c->res16, c->xn, s);
                 });
             }
             timed(c, kGemmHead, [&] {

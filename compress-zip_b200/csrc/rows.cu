@@ -1,6 +1,9 @@
 // rows.cu -- per-token row kernels: row set-up, embedding + RMSNorm, and the
 // fused "post-norm, residual add, next pre-norm" step that follows the O and
 // down projections.  One warp per token row; d_model must be a multiple of 128.
+// The residual stream is int32 in the reference; every addend is a norm output
+// (|y| <= 127) and the start an embedding byte, so |x| <= 128 + 254 * n_layers
+// and int16 storage is exact for n_layers <= 128 (RT = int16_t), halving its traffic.
 //
 // Reference: the residual stream and sandwich norms of rust/src/model.rs:362-480,
 // RMSNorm of rust/src/rmsnorm.rs:40-75.
@@ -56,11 +59,24 @@ __device__ __forceinline__ void rmsnorm_words(const uint32_t (&x)[NW], const uin
     }
 }
 
-// x_res[r] = embed[tok_in[r]] (int32 residual), xn[r] = norm(clamp(x_res[r]))
-template <int NW>
+// four consecutive residual elements
+__device__ __forceinline__ int4 load_res4(const int32_t *p) { return *reinterpret_cast<const int4 *>(p); }
+__device__ __forceinline__ int4 load_res4(const int16_t *p) {
+    const uint2 u = *reinterpret_cast<const uint2 *>(p);
+    return make_int4((int)(int16_t)(u.x & 0xFFFFu), (int)(int16_t)(u.x >> 16), (int)(int16_t)(u.y & 0xFFFFu),
+                     (int)(int16_t)(u.y >> 16));
+}
+__device__ __forceinline__ void store_res4(int32_t *p, int4 v) { *reinterpret_cast<int4 *>(p) = v; }
+__device__ __forceinline__ void store_res4(int16_t *p, int4 v) {
+    *reinterpret_cast<uint2 *>(p) = make_uint2(((uint32_t)v.x & 0xFFFFu) | ((uint32_t)v.y << 16),
+                                               ((uint32_t)v.z & 0xFFFFu) | ((uint32_t)v.w << 16));
+}
+
+// x_res[r] = embed[tok_in[r]] (residual), xn[r] = norm(clamp(x_res[r]))
+template <int NW, typename RT>
 __global__ void k_embed_norm(const uint32_t *__restrict__ tok_in, const int8_t *__restrict__ embed,
                              const int8_t *__restrict__ norm_w, int M, int eps,
-                             int *__restrict__ x_res, int8_t *__restrict__ xn) {
+                             RT *__restrict__ x_res, int8_t *__restrict__ xn) {
     constexpr int D = NW * 128;
     int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     int lane = threadIdx.x & 31;
@@ -73,10 +89,10 @@ __global__ void k_embed_norm(const uint32_t *__restrict__ tok_in, const int8_t *
         x[j] = __ldg(e + lane + 32 * j);
         w[j] = __ldg(wv + lane + 32 * j);
     }
-    int4 *xr = reinterpret_cast<int4 *>(x_res + (size_t)warp * D);
+    RT *xr = x_res + (size_t)warp * D;
 #pragma unroll
     for (int j = 0; j < NW; j++)
-        xr[lane + 32 * j] = make_int4(sext8(x[j], 0), sext8(x[j], 1), sext8(x[j], 2), sext8(x[j], 3));
+        store_res4(xr + 4 * (lane + 32 * j), make_int4(sext8(x[j], 0), sext8(x[j], 1), sext8(x[j], 2), sext8(x[j], 3)));
 #pragma unroll
     for (int j = 0; j < NW; j++) {   // clamp_i8 before the norm: -128 becomes -127
         uint32_t c = 0;
@@ -92,10 +108,10 @@ __global__ void k_embed_norm(const uint32_t *__restrict__ tok_in, const int8_t *
 
 // o_n = norm(o, post_w); x_res += o_n (int32, never clamped: model.rs:432-434);
 // xn = norm(clamp(x_res), next_w)
-template <int NW>
+template <int NW, typename RT>
 __global__ void k_residual_norm(const int8_t *__restrict__ o, const int8_t *__restrict__ post_w,
                                 const int8_t *__restrict__ next_w, int M, int eps,
-                                int *__restrict__ x_res, int8_t *__restrict__ xn) {
+                                RT *__restrict__ x_res, int8_t *__restrict__ xn) {
     constexpr int D = NW * 128;
     int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     int lane = threadIdx.x & 31;
@@ -103,27 +119,29 @@ __global__ void k_residual_norm(const int8_t *__restrict__ o, const int8_t *__re
     const uint32_t *ov = reinterpret_cast<const uint32_t *>(o + (size_t)warp * D);
     const uint32_t *pw = reinterpret_cast<const uint32_t *>(post_w);
     const uint32_t *nw = reinterpret_cast<const uint32_t *>(next_w);
-    uint32_t x[NW], w[NW], y[NW];
+    uint32_t x[NW], w[NW], y[NW], w2[NW];
+    RT *xr = x_res + (size_t)warp * D;
+    int4 rv[NW];
 #pragma unroll
-    for (int j = 0; j < NW; j++) {
+    for (int j = 0; j < NW; j++) {   // every load of the row first
         x[j] = ov[lane + 32 * j];
         w[j] = __ldg(pw + lane + 32 * j);
+        w2[j] = __ldg(nw + lane + 32 * j);
+        rv[j] = load_res4(xr + 4 * (lane + 32 * j));
     }
     rmsnorm_words<NW>(x, w, D, eps, y);
-    int4 *xr = reinterpret_cast<int4 *>(x_res + (size_t)warp * D);
 #pragma unroll
     for (int j = 0; j < NW; j++) {
-        int4 r = xr[lane + 32 * j];
+        int4 r = rv[j];
         r.x = (int)((uint32_t)r.x + (uint32_t)sext8(y[j], 0));
         r.y = (int)((uint32_t)r.y + (uint32_t)sext8(y[j], 1));
         r.z = (int)((uint32_t)r.z + (uint32_t)sext8(y[j], 2));
         r.w = (int)((uint32_t)r.w + (uint32_t)sext8(y[j], 3));
-        xr[lane + 32 * j] = r;
+        store_res4(xr + 4 * (lane + 32 * j), r);
         x[j] = (uint32_t)(uint8_t)clamp127(r.x) | ((uint32_t)(uint8_t)clamp127(r.y) << 8) |
                ((uint32_t)(uint8_t)clamp127(r.z) << 16) | ((uint32_t)(uint8_t)clamp127(r.w) << 24);
-        w[j] = __ldg(nw + lane + 32 * j);
     }
-    rmsnorm_words<NW>(x, w, D, eps, y);
+    rmsnorm_words<NW>(x, w2, D, eps, y);
     uint32_t *yo = reinterpret_cast<uint32_t *>(xn + (size_t)warp * D);
 #pragma unroll
     for (int j = 0; j < NW; j++) yo[lane + 32 * j] = y[j];
@@ -158,26 +176,42 @@ void launch_rows(const uint32_t *tokens, const int *chunk_row0, const int *chunk
                                      tok_out, pos, err);
 }
 
-void launch_embed_norm(const uint32_t *tok_in, const int8_t *embed, const int8_t *norm_w, int M,
-                       int d, int eps, int *x_res, int8_t *xn, cudaStream_t st) {
-    int blocks = (M + 7) / 8;
+template <typename RT>
+void embed_norm_t(const uint32_t *tok_in, const int8_t *embed, const int8_t *norm_w, int M, int d, int eps,
+                  RT *x_res, int8_t *xn, cudaStream_t st) {
+    const int blocks = (M + 7) / 8;
     switch (d / 128) {
-        case 2: k_embed_norm<2><<<blocks, 256, 0, st>>>(tok_in, embed, norm_w, M, eps, x_res, xn); break;
-        case 3: k_embed_norm<3><<<blocks, 256, 0, st>>>(tok_in, embed, norm_w, M, eps, x_res, xn); break;
-        case 4: k_embed_norm<4><<<blocks, 256, 0, st>>>(tok_in, embed, norm_w, M, eps, x_res, xn); break;
+        case 2: k_embed_norm<2, RT><<<blocks, 256, 0, st>>>(tok_in, embed, norm_w, M, eps, x_res, xn); break;
+        case 3: k_embed_norm<3, RT><<<blocks, 256, 0, st>>>(tok_in, embed, norm_w, M, eps, x_res, xn); break;
+        case 4: k_embed_norm<4, RT><<<blocks, 256, 0, st>>>(tok_in, embed, norm_w, M, eps, x_res, xn); break;
         default: break;
     }
 }
 
-void launch_residual_norm(const int8_t *o, const int8_t *post_w, const int8_t *next_w, int M, int d,
-                          int eps, int *x_res, int8_t *xn, cudaStream_t st) {
-    int blocks = (M + 7) / 8;
+template <typename RT>
+void residual_norm_t(const int8_t *o, const int8_t *post_w, const int8_t *next_w, int M, int d, int eps,
+                     RT *x_res, int8_t *xn, cudaStream_t st) {
+    const int blocks = (M + 7) / 8;
     switch (d / 128) {
-        case 2: k_residual_norm<2><<<blocks, 256, 0, st>>>(o, post_w, next_w, M, eps, x_res, xn); break;
-        case 3: k_residual_norm<3><<<blocks, 256, 0, st>>>(o, post_w, next_w, M, eps, x_res, xn); break;
-        case 4: k_residual_norm<4><<<blocks, 256, 0, st>>>(o, post_w, next_w, M, eps, x_res, xn); break;
+        case 2: k_residual_norm<2, RT><<<blocks, 256, 0, st>>>(o, post_w, next_w, M, eps, x_res, xn); break;
+        case 3: k_residual_norm<3, RT><<<blocks, 256, 0, st>>>(o, post_w, next_w, M, eps, x_res, xn); break;
+        case 4: k_residual_norm<4, RT><<<blocks, 256, 0, st>>>(o, post_w, next_w, M, eps, x_res, xn); break;
         default: break;
     }
+}
+
+void launch_embed_norm(const uint32_t *tok_in, const int8_t *embed, const int8_t *norm_w, int M,
+                       int d, int eps, void *x_res, bool res16, int8_t *xn, cudaStream_t st) {
+    if (M == 0) return;
+    if (res16) embed_norm_t(tok_in, embed, norm_w, M, d, eps, static_cast<int16_t *>(x_res), xn, st);
+    else embed_norm_t(tok_in, embed, norm_w, M, d, eps, static_cast<int32_t *>(x_res), xn, st);
+}
+
+void launch_residual_norm(const int8_t *o, const int8_t *post_w, const int8_t *next_w, int M, int d,
+                          int eps, void *x_res, bool res16, int8_t *xn, cudaStream_t st) {
+    if (M == 0) return;
+    if (res16) residual_norm_t(o, post_w, next_w, M, d, eps, static_cast<int16_t *>(x_res), xn, st);
+    else residual_norm_t(o, post_w, next_w, M, d, eps, static_cast<int32_t *>(x_res), xn, st);
 }
 
 void launch_kv_prep(const int8_t *qkv, int ldq, int d, const int *pos, const int16_t *rope_cos,

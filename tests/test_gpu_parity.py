@@ -212,3 +212,18 @@ def test_cdf_edge_models(shipped_path, tmp_path, oracle_mod, shipped_tokens, mod
         assert eng.compress_chunks(toks, starts) == oracle_mod.compress_chunks(om, toks, starts)
     finally:
         eng.close()
+
+
+def test_int32_residual_path(shipped_path, shipped_oracle, oracle_mod, shipped_tokens, monkeypatch):
+    """The int32 residual stream (used for models deeper than 128 layers) on the shipped model."""
+    from compress_zip_b200.engine import Engine
+
+    monkeypatch.setenv("CZG_RESIDUAL32", "1")
+    eng = Engine.from_file(shipped_path, 0)
+    try:
+        _trace_equal(eng, shipped_oracle, oracle_mod, shipped_tokens[:300])
+        starts = _starts(len(shipped_tokens), 1024)
+        assert eng.compress_chunks(shipped_tokens, starts) == \
+            oracle_mod.compress_chunks(shipped_oracle, shipped_tokens, starts)
+    finally:
+        eng.close()
