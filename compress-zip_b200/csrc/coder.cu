@@ -76,15 +76,15 @@ __global__ void k_cdf_lohi(const int32_t *__restrict__ logits, int V, int ld,
 
 // Register-resident version for V <= 128 * G (and so S < 2^30): the row is read
 // once (lane l holds elements 128j + 4l + k), the weights e_i are kept packed,
-// and the division by S uses floor_mul_div.  One warp per row.
-template <int G>
+// and the division by S uses floor_mul_div.  The weight is read from lut4k,
+// exp_q16 tabulated by t256 (entries >= 4096 are 1), with
+// t256 = hi + (lo >= 2^31) of neg * (coef << 8), which needs coef < 2^24.
+// FULL: V == 128 * G, so no element is out of range.  One warp per row.
+template <int G, bool FULL>
 __global__ void __launch_bounds__(256) k_cdf_lohi_reg(const int32_t *__restrict__ logits, int V, int ld,
                                                       const uint32_t *__restrict__ sym,
-                                                      const uint16_t *__restrict__ lut_g, uint32_t coef,
+                                                      const uint16_t *__restrict__ lut4k, uint32_t c8,
                                                       uint32_t total, int M, uint2 *__restrict__ lohi) {
-    __shared__ uint16_t lut[256];
-    for (int i = threadIdx.x; i < 256; i += blockDim.x) lut[i] = lut_g[i];
-    __syncthreads();
     const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (row >= M) return;
@@ -93,9 +93,10 @@ __global__ void __launch_bounds__(256) k_cdf_lohi_reg(const int32_t *__restrict_
 #pragma unroll
     for (int j = 0; j < G; j++) {
         int4 v = make_int4(0, 0, 0, 0);
-        if (128 * j + 4 * lane < V) v = __ldcs(src + 32 * j + lane);   // read once: streaming
+        if (FULL || 128 * j + 4 * lane < V) v = __ldcs(src + 32 * j + lane);   // read once: streaming
         x[j][0] = v.x; x[j][1] = v.y; x[j][2] = v.z; x[j][3] = v.w;
     }
+    const int sy = (int)sym[row];
     // max and its first index (primitives.rs:278-295); this lane's indices increase with (j, k)
     int mx = INT32_MIN, am = 0x7fffffff;
 #pragma unroll
@@ -103,7 +104,7 @@ __global__ void __launch_bounds__(256) k_cdf_lohi_reg(const int32_t *__restrict_
 #pragma unroll
         for (int k = 0; k < 4; k++) {
             const int i = 128 * j + 4 * lane + k;
-            if (i < V && x[j][k] > mx) { mx = x[j][k]; am = i; }
+            if ((FULL || i < V) && x[j][k] > mx) { mx = x[j][k]; am = i; }
         }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -119,7 +120,12 @@ __global__ void __launch_bounds__(256) k_cdf_lohi_reg(const int32_t *__restrict_
 #pragma unroll
         for (int k = 0; k < 4; k++) {
             const int i = 128 * j + 4 * lane + k;
-            e[k] = i < V ? exp_q16_shift((int)((uint32_t)x[j][k] - (uint32_t)mx), lut, coef) : 0u;
+            const int dlt = (int)((uint32_t)x[j][k] - (uint32_t)mx);
+            const uint32_t neg = 0u - (uint32_t)dlt;
+            const uint32_t t = min(__umulhi(neg, c8) + ((neg * c8) >> 31), 4096u);
+            uint32_t w = __ldg(lut4k + t);
+            w = dlt >= 0 ? 65535u : w;
+            e[k] = (FULL || i < V) ? w : 0u;
             S += e[k];
         }
         ew[j][0] = e[0] | (e[1] << 16);
@@ -130,7 +136,6 @@ __global__ void __launch_bounds__(256) k_cdf_lohi_reg(const int32_t *__restrict_
     const uint32_t R = total - (uint32_t)V;
     const uint32_t a = R / S, b = R % S;
     const float bs = __fdiv_rn((float)b, (float)S);
-    const int sy = (int)sym[row];
     uint32_t f_all = 0, f_below = 0, f_sym = 0;
 #pragma unroll
     for (int j = 0; j < G; j++)
@@ -138,7 +143,8 @@ __global__ void __launch_bounds__(256) k_cdf_lohi_reg(const int32_t *__restrict_
         for (int k = 0; k < 4; k++) {
             const int i = 128 * j + 4 * lane + k;
             const uint32_t e = (ew[j][k >> 1] >> (16 * (k & 1))) & 0xFFFFu;
-            const uint32_t f = i < V ? 1u + floor_mul_div(e, a, b, S, bs) : 0u;
+            uint32_t f = 1u + floor_mul_div(e, a, b, S, bs);
+            if (!FULL) f = i < V ? f : 0u;
             f_all += f;
             f_below += (i < sy) ? f : 0u;
             f_sym = (i == sy) ? f : f_sym;
@@ -155,6 +161,13 @@ __global__ void __launch_bounds__(256) k_cdf_lohi_reg(const int32_t *__restrict_
         const uint32_t hi = lo + f_sym + ((uint32_t)am == (uint32_t)sy ? rem : 0u);
         lohi[row] = make_uint2(lo, hi);
     }
+}
+
+template <int G>
+void cdf_reg(bool full, const int32_t *logits, int V, int ld, const uint32_t *sym, const uint16_t *lut4k, uint32_t c8,
+             uint32_t total, int M, uint2 *lohi, unsigned grid, cudaStream_t st) {
+    if (full) k_cdf_lohi_reg<G, true><<<grid, 256, 0, st>>>(logits, V, ld, sym, lut4k, c8, total, M, lohi);
+    else k_cdf_lohi_reg<G, false><<<grid, 256, 0, st>>>(logits, V, ld, sym, lut4k, c8, total, M, lohi);
 }
 
 struct BitSink {
@@ -275,20 +288,22 @@ __global__ void k_pack(const uint8_t *__restrict__ slots, const uint64_t *__rest
 }  // namespace
 
 void launch_cdf_lohi(const int32_t *logits, int V, int ld, const uint32_t *sym, const uint16_t *lut,
-                     uint32_t coef, uint32_t total, int M, uint2 *lohi, cudaStream_t st) {
+                     const uint16_t *lut4k, uint32_t coef, uint32_t total, int M, uint2 *lohi, cudaStream_t st) {
     if (M == 0) return;
     const unsigned grid = (unsigned)((M + 7) / 8);
-    // 16-byte row loads need ld % 4 == 0; the weight bound needs V <= 1024
-    if (ld % 4 == 0 && V <= 1024) {
+    // 16-byte row loads need ld % 4 == 0; the weight bound needs V <= 1024; the table index coef < 2^24
+    if (ld % 4 == 0 && V <= 1024 && coef < (1u << 24)) {
+        const bool full = V % 128 == 0;
+        const uint32_t c8 = coef << 8;
         switch ((V + 127) / 128) {
-            case 8: k_cdf_lohi_reg<8><<<grid, 256, 0, st>>>(logits, V, ld, sym, lut, coef, total, M, lohi); return;
-            case 7: k_cdf_lohi_reg<7><<<grid, 256, 0, st>>>(logits, V, ld, sym, lut, coef, total, M, lohi); return;
-            case 6: k_cdf_lohi_reg<6><<<grid, 256, 0, st>>>(logits, V, ld, sym, lut, coef, total, M, lohi); return;
-            case 5: k_cdf_lohi_reg<5><<<grid, 256, 0, st>>>(logits, V, ld, sym, lut, coef, total, M, lohi); return;
-            case 4: k_cdf_lohi_reg<4><<<grid, 256, 0, st>>>(logits, V, ld, sym, lut, coef, total, M, lohi); return;
-            case 3: k_cdf_lohi_reg<3><<<grid, 256, 0, st>>>(logits, V, ld, sym, lut, coef, total, M, lohi); return;
-            case 2: k_cdf_lohi_reg<2><<<grid, 256, 0, st>>>(logits, V, ld, sym, lut, coef, total, M, lohi); return;
-            default: k_cdf_lohi_reg<1><<<grid, 256, 0, st>>>(logits, V, ld, sym, lut, coef, total, M, lohi); return;
+            case 8: cdf_reg<8>(full, logits, V, ld, sym, lut4k, c8, total, M, lohi, grid, st); return;
+            case 7: cdf_reg<7>(full, logits, V, ld, sym, lut4k, c8, total, M, lohi, grid, st); return;
+            case 6: cdf_reg<6>(full, logits, V, ld, sym, lut4k, c8, total, M, lohi, grid, st); return;
+            case 5: cdf_reg<5>(full, logits, V, ld, sym, lut4k, c8, total, M, lohi, grid, st); return;
+            case 4: cdf_reg<4>(full, logits, V, ld, sym, lut4k, c8, total, M, lohi, grid, st); return;
+            case 3: cdf_reg<3>(full, logits, V, ld, sym, lut4k, c8, total, M, lohi, grid, st); return;
+            case 2: cdf_reg<2>(full, logits, V, ld, sym, lut4k, c8, total, M, lohi, grid, st); return;
+            default: cdf_reg<1>(full, logits, V, ld, sym, lut4k, c8, total, M, lohi, grid, st); return;
         }
     }
     k_cdf_lohi<<<grid, 256, 0, st>>>(logits, V, ld, sym, lut, coef, total, M, lohi);

@@ -503,7 +503,7 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
         cudaMemcpy2DAsync(tr->logits, (size_t)V * 4, c->logits, (size_t)c->vpad * 4, (size_t)V * 4, M,
                           cudaMemcpyDeviceToHost, st);
     timed(c, kCdf, [&] {
-        launch_cdf_lohi(c->logits, V, c->vpad, c->tok_out, c->lut, m.coef_q24, m.target_total, M,
+        launch_cdf_lohi(c->logits, V, c->vpad, c->tok_out, c->lut, c->lut4k, m.coef_q24, m.target_total, M,
                         c->lohi, st);
     });
     if (tr && tr->lohi)

@@ -54,7 +54,7 @@ bool launch_gemm_tc(const TcMatrix &A, const TcMatrix &B, int M, int N, int K, i
 
 void attention_init();
 // attention_mma.cu: tensor-core version for chunks of at most 1024 positions;
-// lut4k = exp_q16 for t256 < 4096 (see exp4k_table)
+// lut4k = exp_q16 tabulated by t256 <= 4096 (entries from 4096 on are 1)
 bool attention_mma_fits(int max_len);
 void attention_mma_init();
 void launch_attention_mma(const int8_t *qkv, int ldq, const int8_t *kv, const int *chunk_row0,
@@ -89,7 +89,7 @@ void launch_attention_decode(const int8_t *qkv, int ldq, const int8_t *kvc, size
 
 // coder.cu
 void launch_cdf_lohi(const int32_t *logits, int V, int ld, const uint32_t *sym, const uint16_t *lut,
-                     uint32_t coef, uint32_t total, int M, uint2 *lohi, cudaStream_t st);
+                     const uint16_t *lut4k, uint32_t coef, uint32_t total, int M, uint2 *lohi, cudaStream_t st);
 void launch_encode(const uint2 *lohi, const int *chunk_row0, const int *chunk_len, int n_chunks,
                    uint32_t total, uint8_t *slots, const uint64_t *slot_off, uint32_t *lens,
                    int *err, cudaStream_t st);
