@@ -170,6 +170,139 @@ __global__ void k_cdf_decode(const int32_t *__restrict__ logits, int V, int ld, 
     }
 }
 
+// Register-resident version for V == 32 * E (E in {8, 16, 32}): lane l holds the
+// E consecutive logits [l*E, (l+1)*E) in registers, the weights come from the
+// t256-indexed table lut4k (needs coef < 2^24), the division by S uses
+// floor_mul_div.  The interval search is done by the whole warp: the owner
+// lane's weights go through shared memory, one element per lane, and an
+// inclusive scan gives the cumulative frequencies.
+template <int E>
+__global__ void __launch_bounds__(256) k_cdf_decode_reg(
+    const int32_t *__restrict__ logits, int ld, const uint16_t *__restrict__ lut4k, uint32_t c8, uint32_t total,
+    unsigned long long inv_total, int M, DecState *__restrict__ st, const uint8_t *__restrict__ data,
+    const uint64_t *__restrict__ data_off, const uint64_t *__restrict__ data_len, const uint64_t *__restrict__ tok_off,
+    int step, uint32_t *__restrict__ out_tok, uint32_t *__restrict__ tok_in) {
+    constexpr int V = 32 * E;
+    __shared__ uint32_t ebuf[8][E / 2];
+    const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    if (r >= M) return;
+    const int4 *src = reinterpret_cast<const int4 *>(logits + (size_t)r * ld + lane * E);
+    int x[E];
+#pragma unroll
+    for (int k = 0; k < E / 4; k++) {
+        const int4 v = __ldcs(src + k);
+        x[4 * k] = v.x; x[4 * k + 1] = v.y; x[4 * k + 2] = v.z; x[4 * k + 3] = v.w;
+    }
+    // max and first argmax (primitives.rs:278-295)
+    int mx = INT32_MIN, am = 0x7fffffff;
+#pragma unroll
+    for (int k = 0; k < E; k++)
+        if (x[k] > mx) { mx = x[k]; am = lane * E + k; }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const int om = __shfl_xor_sync(0xffffffffu, mx, o);
+        const int oa = __shfl_xor_sync(0xffffffffu, am, o);
+        if (om > mx || (om == mx && oa < am)) { mx = om; am = oa; }
+    }
+    uint32_t ew[E / 2];
+    uint32_t S = 0;
+#pragma unroll
+    for (int k = 0; k < E; k++) {
+        const int dlt = (int)((uint32_t)x[k] - (uint32_t)mx);
+        const uint32_t neg = 0u - (uint32_t)dlt;
+        const uint32_t t = min(__umulhi(neg, c8) + ((neg * c8) >> 31), 4096u);
+        const uint32_t w = dlt >= 0 ? 65535u : (uint32_t)__ldg(lut4k + t);
+        S += w;
+        if (k & 1) ew[k >> 1] |= w << 16;
+        else ew[k >> 1] = w;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
+    const uint32_t R = total - (uint32_t)V;
+    const uint32_t a = R / S, b = R % S;
+    const float bs = __fdiv_rn((float)b, (float)S);
+    uint32_t F = 0;
+#pragma unroll
+    for (int k = 0; k < E; k++) F += 1u + floor_mul_div((ew[k >> 1] >> (16 * (k & 1))) & 0xFFFFu, a, b, S, bs);
+    uint32_t all = F;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) all += __shfl_xor_sync(0xffffffffu, all, o);
+    const uint32_t rem = total - all;   // to the argmax (softmax_cdf.rs:125-127)
+    if (am / E == lane) F += rem;
+    uint32_t inc = F;   // inclusive scan of lane totals
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t u = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += u;
+    }
+    const uint32_t base = inc - F;
+
+    DecState s = st[r];
+    const unsigned long long range = (unsigned long long)s.high - s.low + 1;
+    // value = ((code - low + 1) * T - 1) / range  (arith_coder.rs:195-200)
+    const unsigned long long value = (((unsigned long long)s.code - s.low + 1) * total - 1) / range;
+    // smallest i with v32 < cum[i], else the last symbol (arith_coder.rs:203, 225-241)
+    const uint32_t v32 = (uint32_t)value;
+    const uint32_t bal = __ballot_sync(0xffffffffu, v32 >= base && v32 < base + F);
+    const bool past_end = bal == 0;
+    const int owner = past_end ? 31 : __ffs(bal) - 1;
+    if (lane == owner) {
+#pragma unroll
+        for (int k = 0; k < E / 2; k++) ebuf[wib][k] = ew[k];
+    }
+    const uint32_t obase = __shfl_sync(0xffffffffu, base, owner);
+    __syncwarp();
+    // lane j < E takes element owner*E + j
+    uint32_t f = 0;
+    const int idx = owner * E + lane;
+    if (lane < E) {
+        const uint32_t e = (ebuf[wib][lane >> 1] >> (16 * (lane & 1))) & 0xFFFFu;
+        f = 1u + floor_mul_div(e, a, b, S, bs) + (idx == am ? rem : 0u);
+    }
+    uint32_t cum = f;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t u = __shfl_up_sync(0xffffffffu, cum, o);
+        if (lane >= o) cum += u;
+    }
+    cum += obase;
+    const uint32_t hit = __ballot_sync(0xffffffffu, lane < E && v32 < cum);
+    const int sl = past_end ? E - 1 : __ffs(hit) - 1;   // hit != 0 unless past the end
+    const uint32_t hi = __shfl_sync(0xffffffffu, cum, sl);
+    const uint32_t lo = hi - __shfl_sync(0xffffffffu, f, sl);
+    if (lane == 0) {
+        const uint32_t sym = (uint32_t)(owner * E + sl);
+        const unsigned long long HALF = 1ull << 31, QUARTER = 1ull << 30, MASK = 0xFFFFFFFFull;
+        unsigned long long low = s.low, high = s.high, code = s.code;
+        uint64_t bit = s.bit;
+        const uint8_t *d = data + data_off[r];
+        const uint64_t len = data_len[r];
+        high = low + udiv_by_inv((unsigned long long)hi * range, total, inv_total) - 1;
+        low = low + udiv_by_inv((unsigned long long)lo * range, total, inv_total);
+        for (;;) {   // arith_coder.rs:244-264
+            if (((low ^ high) & HALF) == 0) {
+                low = (low << 1) & MASK;
+                high = ((high << 1) & MASK) | 1ull;
+                code = ((code << 1) & MASK) | read_bit(d, len, bit++);
+            } else if ((low & ~high & QUARTER) != 0) {
+                low = ((low << 1) ^ HALF) & MASK;
+                high = (((high ^ HALF) << 1) | HALF | 1ull) & MASK;
+                code = (code & HALF) | ((code << 1) & (MASK >> 1)) | read_bit(d, len, bit++);
+            } else {
+                break;
+            }
+        }
+        s.low = (uint32_t)low;
+        s.high = (uint32_t)high;
+        s.code = (uint32_t)code;
+        s.bit = bit;
+        st[r] = s;
+        out_tok[tok_off[r] + step] = sym;
+        tok_in[r] = sym;
+    }
+}
+
 }  // namespace
 
 void launch_dec_init(const uint8_t *data, const uint64_t *data_off, const uint64_t *data_len, int M,
@@ -186,14 +319,28 @@ void launch_kv_append(const int8_t *qkv, int ldq, int d, int pos, const int16_t 
                                                                        kvc, cache_ld);
 }
 
-void launch_cdf_decode(const int32_t *logits, int V, int ld, const uint16_t *lut, uint32_t coef, uint32_t total,
-                       int M, DecState *st, const uint8_t *data, const uint64_t *data_off,
-                       const uint64_t *data_len, const uint64_t *tok_off, int step, uint32_t *out_tok,
-                       uint32_t *tok_in, cudaStream_t stream) {
+void launch_cdf_decode(const int32_t *logits, int V, int ld, const uint16_t *lut, const uint16_t *lut4k,
+                       uint32_t coef, uint32_t total, int M, DecState *st, const uint8_t *data,
+                       const uint64_t *data_off, const uint64_t *data_len, const uint64_t *tok_off, int step,
+                       uint32_t *out_tok, uint32_t *tok_in, cudaStream_t stream) {
     if (M == 0) return;
     const unsigned long long inv = 0xFFFFFFFFFFFFFFFFull / total;
-    k_cdf_decode<<<(M + 7) / 8, 256, 0, stream>>>(logits, V, ld, lut, coef, total, inv, M, st, data, data_off,
-                                                  data_len, tok_off, step, out_tok, tok_in);
+    const unsigned grid = (unsigned)((M + 7) / 8);
+    if (coef < (1u << 24) && ld % 4 == 0 && (V == 1024 || V == 512 || V == 256)) {
+        const uint32_t c8 = coef << 8;
+        if (V == 1024)
+            k_cdf_decode_reg<32><<<grid, 256, 0, stream>>>(logits, ld, lut4k, c8, total, inv, M, st, data, data_off,
+                                                           data_len, tok_off, step, out_tok, tok_in);
+        else if (V == 512)
+            k_cdf_decode_reg<16><<<grid, 256, 0, stream>>>(logits, ld, lut4k, c8, total, inv, M, st, data, data_off,
+                                                           data_len, tok_off, step, out_tok, tok_in);
+        else
+            k_cdf_decode_reg<8><<<grid, 256, 0, stream>>>(logits, ld, lut4k, c8, total, inv, M, st, data, data_off,
+                                                          data_len, tok_off, step, out_tok, tok_in);
+        return;
+    }
+    k_cdf_decode<<<grid, 256, 0, stream>>>(logits, V, ld, lut, coef, total, inv, M, st, data, data_off,
+                                           data_len, tok_off, step, out_tok, tok_in);
 }
 
 }  // namespace czg

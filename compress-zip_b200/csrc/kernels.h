@@ -78,10 +78,10 @@ void launch_dec_init(const uint8_t *data, const uint64_t *data_off, const uint64
                      DecState *st, uint32_t *tok_in, cudaStream_t stream);
 void launch_kv_append(const int8_t *qkv, int ldq, int d, int pos, const int16_t *rope_cos,
                       const int16_t *rope_sin, int M, int8_t *kvc, size_t cache_ld, cudaStream_t stream);
-void launch_cdf_decode(const int32_t *logits, int V, int ld, const uint16_t *lut, uint32_t coef, uint32_t total,
-                       int M, DecState *st, const uint8_t *data, const uint64_t *data_off,
-                       const uint64_t *data_len, const uint64_t *tok_off, int step, uint32_t *out_tok,
-                       uint32_t *tok_in, cudaStream_t stream);
+void launch_cdf_decode(const int32_t *logits, int V, int ld, const uint16_t *lut, const uint16_t *lut4k,
+                       uint32_t coef, uint32_t total, int M, DecState *st, const uint8_t *data,
+                       const uint64_t *data_off, const uint64_t *data_len, const uint64_t *tok_off, int step,
+                       uint32_t *out_tok, uint32_t *tok_in, cudaStream_t stream);
 void launch_attention_decode(const int8_t *qkv, int ldq, const int8_t *kvc, size_t cache_ld, int M, int p,
                              int n_heads, const int32_t *score_mult, const int8_t *sink_key,
                              const int16_t *rope_cos, const int16_t *rope_sin, const uint16_t *lut,
