@@ -401,6 +401,182 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
     }
 }
 
+// Decode: one warp per stream r, the query of every head at position p against
+// the stream's keys 0..p in the split cache layout (K rows of 64 permuted dims,
+// then V^T [64][len]).  The heads are the 8 rows of the attention tile (A rows
+// n_heads..15 are zero); everything else is the chunk kernel's tile step.
+template <bool WIDE>
+__global__ void __launch_bounds__(AM_THREADS, 1)
+k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restrict__ kvc, size_t cache_ld,
+                       int M, int p, int n_heads, const int32_t *__restrict__ score_mult,
+                       const int8_t *__restrict__ sink_key, const int16_t *__restrict__ rope_cos,
+                       const int16_t *__restrict__ rope_sin, const uint16_t *__restrict__ lut4k,
+                       int8_t *__restrict__ out, int ldo) {
+    __shared__ __align__(16) uint8_t wsm[AM_WARPS * AM_WARP_SMEM];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int r = blockIdx.x * AM_WARPS + warp;
+    if (r >= M) return;
+    uint32_t *rec_e = reinterpret_cast<uint32_t *>(wsm + warp * AM_WARP_SMEM);   // [8][32]
+    int *rec_n = reinterpret_cast<int *>(rec_e + AM_ROWS * 32);                  // [8]
+    uint8_t *ostage = reinterpret_cast<uint8_t *>(rec_n + AM_ROWS);              // [8][64]
+    const size_t len = cache_ld / 128;
+    const int8_t *ks = kvc + (size_t)r * cache_ld;    // [len][64], dims permuted
+    const int8_t *vt = ks + len * 64;                 // [64][len]
+    const uint32_t c8 = 378194u << 8;   // ATTN_COEF_Q24 (attention.rs:14-19) << 8
+    const uint32_t ones[4] = {0x01010101u, 0x01010101u, 0x01010101u, 0x01010101u};
+    const bool head = g < n_heads;   // row g of the tile is head g
+    const int mult = head ? score_mult[g] : 0;
+
+    // Q fragment of head g at position p with RoPE (attention.rs:53-83)
+    uint32_t qa[2][4];
+    {
+        uint32_t raw[4] = {0, 0, 0, 0};
+        if (head) {
+            const int8_t *qr = qkv + (size_t)r * ldq + g * 64;
+#pragma unroll
+            for (int k = 0; k < 4; k++) raw[k] = *reinterpret_cast<const uint32_t *>(qr + 16 * k + 4 * t);
+        }
+        uint32_t lo[2] = {0, 0}, hi[2] = {0, 0};
+#pragma unroll
+        for (int k = 0; k < 2; k++)
+#pragma unroll
+            for (int b = 0; b < 4; b++) {
+                const int i = 16 * k + 4 * t + b;
+                int x = sext8(raw[k], b), y = sext8(raw[k + 2], b);
+                const int cs = rope_cos[p * kHalfDim + i], sn = rope_sin[p * kHalfDim + i];
+                int xr = clamp127(sra_rne32(sra_rne32(x * cs - y * sn, 15), 1));
+                int yr = clamp127(sra_rne32(sra_rne32(x * sn + y * cs, 15), 1));
+                lo[k] |= (uint32_t)(uint8_t)xr << (8 * b);
+                hi[k] |= (uint32_t)(uint8_t)yr << (8 * b);
+            }
+        qa[0][0] = lo[0];
+        qa[0][2] = lo[1];
+        qa[1][0] = hi[0];
+        qa[1][2] = hi[1];
+        qa[0][1] = qa[0][3] = qa[1][1] = qa[1][3] = 0u;
+    }
+    int m = INT32_MIN;
+    unsigned long long s_state[2] = {0, 0};
+    if (sink_key != nullptr) {   // attention.rs:211-224
+        int accs[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int kk = 0; kk < 2; kk++) {
+            uint32_t b0 = *reinterpret_cast<const uint32_t *>(sink_key + 32 * kk + 4 * t);
+            uint32_t b1 = *reinterpret_cast<const uint32_t *>(sink_key + 32 * kk + 16 + 4 * t);
+            mma_s8s8(accs, qa[kk], b0, b1);
+        }
+        m = score_from_dot<true>(accs[0], mult);
+        s_state[0] = s_state[1] = 65535ull;
+    }
+    int hiacc[4][4], loacc[4][4], vst[4][4];
+#pragma unroll
+    for (int mi = 0; mi < 4; mi++)
+#pragma unroll
+        for (int k = 0; k < 4; k++) { hiacc[mi][k] = 0; loacc[mi][k] = 0; vst[mi][k] = 0; }
+    int shs[4] = {0, 0, 0, 0}, sls[4] = {0, 0, 0, 0};
+
+    for (int kb = 0; kb <= p; kb += 32) {
+        int sacc[4][4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0;
+            const uint4 kw = *reinterpret_cast<const uint4 *>(ks + (size_t)(kb + perm_key(8 * j + g)) * 64 + 16 * t);
+            mma_s8s8(sacc[j], qa[0], kw.x, kw.y);
+            mma_s8s8(sacc[j], qa[1], kw.z, kw.w);
+        }
+        uint32_t va[4][4];
+#pragma unroll
+        for (int mi = 0; mi < 4; mi++) {
+            const uint2 lo2 = *reinterpret_cast<const uint2 *>(vt + (size_t)(16 * mi + g) * len + kb + 8 * t);
+            const uint2 hi2 = *reinterpret_cast<const uint2 *>(vt + (size_t)(16 * mi + g + 8) * len + kb + 8 * t);
+            va[mi][0] = lo2.x;
+            va[mi][1] = hi2.x;
+            va[mi][2] = lo2.y;
+            va[mi][3] = hi2.y;
+        }
+        Tile T;
+        if (kb + 31 > p)
+            tile_softmax<true, WIDE>(sacc, kb, p, p + 1, mult, t, m, lut4k, c8, T);
+        else
+            tile_softmax<false, WIDE>(sacc, kb, p, p + 1, mult, t, m, lut4k, c8, T);
+        uint32_t phi[2], plo[2];
+#pragma unroll
+        for (int q = 0; q < 2; q++) {
+            const uint32_t x01 = prmt(T.w[4 * q], T.w[4 * q + 1], 0x5140u);
+            const uint32_t x23 = prmt(T.w[4 * q + 2], T.w[4 * q + 3], 0x5140u);
+            plo[q] = prmt(x01, x23, 0x5410u);
+            phi[q] = prmt(x01, x23, 0x7632u);
+        }
+        const int maxrec = (int)__reduce_max_sync(0xffffffffu, (unsigned)T.nrec);
+        uint32_t segw[2] = {0, 0};
+        int nr[2] = {0, 0};
+        if (maxrec > 0) {
+            tile_segments(T, t, g, rec_e, rec_n, segw, lut4k, c8);
+            __syncwarp();
+            nr[0] = rec_n[2 * t];
+            nr[1] = rec_n[2 * t + 1];
+        }
+        for (int pass = 0; pass <= maxrec; pass++) {
+            if (pass > 0) {
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    if (nr[e] >= pass) {
+                        const uint32_t ef = rec_e[(2 * t + e) * 32 + pass - 1] & 0xFFFFu;
+                        const unsigned long long sa = 256ull * (uint32_t)shs[e] + (unsigned long long)(uint32_t)sls[e];
+                        s_state[e] = (((s_state[e] + sa) * ef + 0x8000ull) >> 16) - sa;
+#pragma unroll
+                        for (int mi = 0; mi < 4; mi++)
+#pragma unroll
+                            for (int k = e; k < 4; k += 2) {
+                                const uint32_t a = ((uint32_t)hiacc[mi][k] << 8) + (uint32_t)loacc[mi][k];
+                                const int x = (int)((uint32_t)vst[mi][k] + a);
+                                const long long pr = (long long)x * (long long)ef + 0x8000ll;
+                                vst[mi][k] = (int)((uint32_t)(pr >> 16) + (uint32_t)(x >> 31) - a);
+                            }
+                    }
+                }
+            }
+            uint32_t bh0 = phi[0], bh1 = phi[1], bl0 = plo[0], bl1 = plo[1];
+            if (maxrec > 0) {
+                const uint32_t m0 = bytes_equal(segw[0], (uint32_t)pass);
+                const uint32_t m1 = bytes_equal(segw[1], (uint32_t)pass);
+                bh0 &= m0; bl0 &= m0; bh1 &= m1; bl1 &= m1;
+            }
+            mma_s8u8(shs, ones, bh0, bh1);
+            mma_s8u8(sls, ones, bl0, bl1);
+#pragma unroll
+            for (int mi = 0; mi < 4; mi++) {
+                mma_s8u8(hiacc[mi], va[mi], bh0, bh1);
+                mma_s8u8(loacc[mi], va[mi], bl0, bl1);
+            }
+        }
+    }
+
+    // output of heads 2t, 2t+1 (attention.rs:279-284)
+#pragma unroll
+    for (int e = 0; e < 2; e++) {
+        const unsigned long long sv = s_state[e] + 256ull * (uint32_t)shs[e] + (unsigned long long)(uint32_t)sls[e];
+        const unsigned long long den = sv == 0 ? 1ull : sv;
+        uint8_t *orow = ostage + (2 * t + e) * 64;
+#pragma unroll
+        for (int mi = 0; mi < 4; mi++)
+#pragma unroll
+            for (int dh = 0; dh < 2; dh++) {
+                const int k = 2 * dh + e;
+                const int x = (int)((uint32_t)vst[mi][k] + ((uint32_t)hiacc[mi][k] << 8) + (uint32_t)loacc[mi][k]);
+                orow[16 * mi + g + 8 * dh] = (uint8_t)clamp127(div_rne_s32_u64(x, den));
+            }
+    }
+    __syncwarp();
+    {
+        const int hd = lane >> 2, part = lane & 3;
+        if (hd < n_heads)
+            *reinterpret_cast<uint4 *>(out + (size_t)r * ldo + hd * 64 + 16 * part) =
+                *reinterpret_cast<const uint4 *>(ostage + hd * 64 + 16 * part);
+    }
+}
+
 }  // namespace
 
 size_t attention_mma_smem(int max_len) {
@@ -433,6 +609,22 @@ void launch_attention_mma(const int8_t *qkv, int ldq, const int8_t *kv, const in
         k_attention_mma<false><<<n_chunks, AM_THREADS, smem, st>>>(
             qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
             lut4k, out, ldo);
+}
+
+bool attention_decode_mma_ok(int n_heads) { return n_heads >= 1 && n_heads <= AM_ROWS; }
+
+void launch_attention_decode_mma(const int8_t *qkv, int ldq, const int8_t *kvc, size_t cache_ld, int M, int p,
+                                 int n_heads, const int32_t *score_mult, const int8_t *sink_key,
+                                 const int16_t *rope_cos, const int16_t *rope_sin, const uint16_t *lut4k,
+                                 bool wide_mult, int8_t *out, int ldo, cudaStream_t st) {
+    if (M == 0) return;
+    const unsigned grid = (unsigned)((M + AM_WARPS - 1) / AM_WARPS);
+    if (wide_mult)
+        k_attention_decode_mma<true><<<grid, AM_THREADS, 0, st>>>(qkv, ldq, kvc, cache_ld, M, p, n_heads, score_mult,
+                                                                 sink_key, rope_cos, rope_sin, lut4k, out, ldo);
+    else
+        k_attention_decode_mma<false><<<grid, AM_THREADS, 0, st>>>(qkv, ldq, kvc, cache_ld, M, p, n_heads, score_mult,
+                                                                  sink_key, rope_cos, rope_sin, lut4k, out, ldo);
 }
 
 }  // namespace czg

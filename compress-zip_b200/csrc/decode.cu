@@ -39,20 +39,38 @@ __global__ void k_dec_init(const uint8_t *__restrict__ data, const uint64_t *__r
     tok_in[r] = kBos;
 }
 
-// rows of the batch at position pos: K rotated (attention.rs:29-50) and V into the cache
+// rows of the batch at position pos: K rotated (attention.rs:29-50) and V into the cache.
+// split == false: the row is [k_rot 64 | v 64] at pos * 128.  split == true (the
+// tensor-core decode attention): K at pos * 64 with its dims permuted as
+// bytes [16t' + 4k + b] = dim 16k + 4t' + b, and V transposed, V^T[dim][pos] at
+// len * 64 + dim * len, where len = cache_ld / 128.
 __global__ void k_kv_append(const int8_t *__restrict__ qkv, int ldq, int d, int pos,
                             const int16_t *__restrict__ rope_cos, const int16_t *__restrict__ rope_sin,
-                            int M, int8_t *__restrict__ kvc, size_t cache_ld) {
+                            int M, int8_t *__restrict__ kvc, size_t cache_ld, bool split) {
     const int gid = blockIdx.x * blockDim.x + threadIdx.x;
     const int r = gid >> 5, i = gid & 31;
     if (r >= M) return;
     const int8_t *k = qkv + (size_t)r * ldq + d;
     const int x = k[i], y = k[i + kHalfDim];
     const int c = rope_cos[pos * kHalfDim + i], s = rope_sin[pos * kHalfDim + i];
-    int8_t *dst = kvc + (size_t)r * cache_ld + (size_t)pos * 128;
-    dst[i] = (int8_t)clamp127(sra_rne32(x * c - y * s, 15));
-    dst[i + kHalfDim] = (int8_t)clamp127(sra_rne32(x * s + y * c, 15));
-    reinterpret_cast<uint16_t *>(dst + 64)[i] = reinterpret_cast<const uint16_t *>(k + 64)[i];
+    const int8_t kx = (int8_t)clamp127(sra_rne32(x * c - y * s, 15));
+    const int8_t ky = (int8_t)clamp127(sra_rne32(x * s + y * c, 15));
+    int8_t *base = kvc + (size_t)r * cache_ld;
+    if (!split) {
+        int8_t *dst = base + (size_t)pos * 128;
+        dst[i] = kx;
+        dst[i + kHalfDim] = ky;
+        reinterpret_cast<uint16_t *>(dst + 64)[i] = reinterpret_cast<const uint16_t *>(k + 64)[i];
+    } else {
+        const size_t len = cache_ld / 128;
+        int8_t *kr = base + (size_t)pos * 64;
+        const int i2 = i + kHalfDim;
+        kr[16 * ((i >> 2) & 3) + 4 * (i >> 4) + (i & 3)] = kx;
+        kr[16 * ((i2 >> 2) & 3) + 4 * (i2 >> 4) + (i2 & 3)] = ky;
+        int8_t *vt = base + len * 64;
+        vt[(size_t)(2 * i) * len + pos] = k[64 + 2 * i];
+        vt[(size_t)(2 * i + 1) * len + pos] = k[64 + 2 * i + 1];
+    }
 }
 
 // One warp per stream: CDF of the logits row, then one decode_symbol.
@@ -312,11 +330,11 @@ void launch_dec_init(const uint8_t *data, const uint64_t *data_off, const uint64
 }
 
 void launch_kv_append(const int8_t *qkv, int ldq, int d, int pos, const int16_t *rope_cos,
-                      const int16_t *rope_sin, int M, int8_t *kvc, size_t cache_ld, cudaStream_t stream) {
+                      const int16_t *rope_sin, int M, int8_t *kvc, size_t cache_ld, bool split, cudaStream_t stream) {
     if (M == 0) return;
     const long long threads = (long long)M * 32;
     k_kv_append<<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(qkv, ldq, d, pos, rope_cos, rope_sin, M,
-                                                                       kvc, cache_ld);
+                                                                       kvc, cache_ld, split);
 }
 
 void launch_cdf_decode(const int32_t *logits, int V, int ld, const uint16_t *lut, const uint16_t *lut4k,

@@ -634,7 +634,7 @@ int dec_reserve(czg_ctx *c, size_t streams, size_t len, size_t bytes, size_t tok
     for (void *p : c->dec_allocs) cudaFree(p);
     c->dec_allocs.clear();
     streams = std::max(streams, c->dec_streams);
-    len = std::max(len, c->dec_len);
+    len = (std::max(len, c->dec_len) + 31) & ~(size_t)31;   // the split KV layout reads whole 32-key tiles
     bytes = std::max(bytes, c->dec_bytes);
     tokens = std::max(tokens, c->dec_tokens);
     auto get = [&](void **p, size_t n) {
@@ -727,6 +727,8 @@ int decompress_impl(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts
         launch_dec_init(c->ddata, c->d_off, c->d_len, ns, c->dstate, c->tok_in, s);
         const int wmax = (int)n_tokens[order[w0]];
         const size_t cache_ld = (size_t)c->dec_len * 128;
+        // tensor-core decode attention (heads as tile rows) over the split K / V^T cache layout
+        const bool split = attention_decode_mma_ok(H) && getenv("CZG_SCALAR_DECODE") == nullptr;
         const size_t layer_ld = (size_t)c->dec_streams * cache_ld;
         int active = ns;
         for (int step = 0; step < wmax; step++) {
@@ -743,11 +745,16 @@ int decompress_impl(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts
                          c->qkv, d + 128);
                 });
                 timed(c, kKvAppend, [&] {
-                    launch_kv_append(c->qkv, d + 128, d, step, c->rope_cos, c->rope_sin, M, kvc, cache_ld, s);
+                    launch_kv_append(c->qkv, d + 128, d, step, c->rope_cos, c->rope_sin, M, kvc, cache_ld, split, s);
                 });
                 timed(c, kAttnDecode, [&] {
-                    launch_attention_decode(c->qkv, d + 128, kvc, cache_ld, M, step, H, L.score_mult, L.sink_key,
-                                            c->rope_cos, c->rope_sin, c->lut, c->attn, d, s);
+                    if (split)
+                        launch_attention_decode_mma(c->qkv, d + 128, kvc, cache_ld, M, step, H, L.score_mult,
+                                                    L.sink_key, c->rope_cos, c->rope_sin, c->lut4k, L.wide_mult,
+                                                    c->attn, d, s);
+                    else
+                        launch_attention_decode(c->qkv, d + 128, kvc, cache_ld, M, step, H, L.score_mult, L.sink_key,
+                                                c->rope_cos, c->rope_sin, c->lut, c->attn, d, s);
                 });
                 timed(c, kGemmO, [&] {
                     gemm(c, c->tm_attn, L.tm_out, c->attn, L.out_w, M, d, d, kEpiRequant, L.out_mult, L.out_shift,

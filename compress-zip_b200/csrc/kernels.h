@@ -57,6 +57,14 @@ void attention_init();
 // lut4k = exp_q16 tabulated by t256 <= 4096 (entries from 4096 on are 1)
 bool attention_mma_fits(int max_len);
 void attention_mma_init();
+// Tensor-core decode attention over the split KV layout: one warp per stream, the
+// heads as the rows of the attention tile (n_heads <= 8); cache_ld = 128 * len,
+// len % 32 == 0.
+bool attention_decode_mma_ok(int n_heads);
+void launch_attention_decode_mma(const int8_t *qkv, int ldq, const int8_t *kvc, size_t cache_ld, int M, int p,
+                                 int n_heads, const int32_t *score_mult, const int8_t *sink_key,
+                                 const int16_t *rope_cos, const int16_t *rope_sin, const uint16_t *lut4k,
+                                 bool wide_mult, int8_t *out, int ldo, cudaStream_t st);
 void launch_attention_mma(const int8_t *qkv, int ldq, const int8_t *kv, const int *chunk_row0,
                           const int *chunk_len, int n_chunks, int max_len, int n_heads,
                           const int32_t *score_mult, const int8_t *sink_key, const int16_t *rope_cos,
@@ -76,8 +84,9 @@ struct DecState {   // arithmetic decoder state of one stream
 };
 void launch_dec_init(const uint8_t *data, const uint64_t *data_off, const uint64_t *data_len, int M,
                      DecState *st, uint32_t *tok_in, cudaStream_t stream);
+// split: the tensor-core decode layout (K with permuted dims, V transposed), see decode.cu
 void launch_kv_append(const int8_t *qkv, int ldq, int d, int pos, const int16_t *rope_cos,
-                      const int16_t *rope_sin, int M, int8_t *kvc, size_t cache_ld, cudaStream_t stream);
+                      const int16_t *rope_sin, int M, int8_t *kvc, size_t cache_ld, bool split, cudaStream_t stream);
 void launch_cdf_decode(const int32_t *logits, int V, int ld, const uint16_t *lut, const uint16_t *lut4k,
                        uint32_t coef, uint32_t total, int M, DecState *st, const uint8_t *data,
                        const uint64_t *data_off, const uint64_t *data_len, const uint64_t *tok_off, int step,

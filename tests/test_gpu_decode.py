@@ -111,3 +111,44 @@ def test_decode_many_streams_roundtrip(eng, shipped_path):
     assert len(chunks) > 6000
     got = eng.decompress_chunks(chunks, np.diff(starts))
     assert np.array_equal(got, tokens)
+
+
+@pytest.mark.parametrize("sink,score_mult", [
+    (True, None),
+    (False, [1 << 20, 1 << 24, 2147483647, -2147483647, 3, -60000]),   # record-heavy, clamped scores
+])
+def test_decode_attention_edge_models(tmp_path, shipped_path, oracle_mod, doc_tokens, sink, score_mult):
+    """Decode attention with a sink key and with extreme score multipliers (saturated scores)."""
+    from compress_zip_b200 import czm
+    from compress_zip_b200.engine import Engine
+
+    mf = czm.ModelFile.load(shipped_path)
+    t = {k: np.array(v) for k, v in mf.tensors.items()}
+    if sink:
+        t["layers.0.attn.sink_key"] = np.random.default_rng(11).integers(-127, 128, 64).astype(np.int8)
+    if score_mult is not None:
+        t["layers.0.attn.score_mult"] = np.asarray(score_mult, np.int32)
+    p = tmp_path / "edge.czm"
+    p.write_bytes(czm.write_safetensors(t, mf.metadata))
+    om = oracle_mod.load_model(str(p))
+    e = Engine.from_file(str(p), 0)
+    try:
+        tokens, starts = _chunked(doc_tokens, 300)
+        chunks = oracle_mod.compress_chunks(om, tokens, starts)
+        assert np.array_equal(e.decompress_chunks(chunks, np.diff(starts)), tokens)
+    finally:
+        e.close()
+
+
+def test_decode_scalar_attention_path(shipped_path, shipped_oracle, oracle_mod, doc_tokens, monkeypatch):
+    """The CUDA-core decode attention (used for more than 8 heads) on the shipped model."""
+    from compress_zip_b200.engine import Engine
+
+    monkeypatch.setenv("CZG_SCALAR_DECODE", "1")
+    e = Engine.from_file(shipped_path, 0)
+    try:
+        tokens, starts = _chunked(doc_tokens, 256)
+        chunks = oracle_mod.compress_chunks(shipped_oracle, tokens, starts)
+        assert np.array_equal(e.decompress_chunks(chunks, np.diff(starts)), tokens)
+    finally:
+        e.close()
