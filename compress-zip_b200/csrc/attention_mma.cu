@@ -403,7 +403,7 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
 
 // Decode: one warp per stream r, the query of every head at position p against
 // the stream's keys 0..p in the split cache layout (K rows of 64 permuted dims,
-// then V^T [64][len]).  The heads are the 8 rows of the attention tile (A rows
+// then V in 2 KB tiles of 32 keys as [8 key groups][64 dims][4 keys]).  The heads are the 8 rows of the attention tile (A rows
 // n_heads..15 are zero); everything else is the chunk kernel's tile step.
 template <bool WIDE>
 __global__ void __launch_bounds__(AM_THREADS, 1)
@@ -422,7 +422,7 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__
     uint8_t *ostage = reinterpret_cast<uint8_t *>(rec_n + AM_ROWS);              // [8][64]
     const size_t len = cache_ld / 128;
     const int8_t *ks = kvc + (size_t)r * cache_ld;    // [len][64], dims permuted
-    const int8_t *vt = ks + len * 64;                 // [64][len]
+    const int8_t *vt = ks + len * 64;                 // V tiles
     const uint32_t c8 = 378194u << 8;   // ATTN_COEF_Q24 (attention.rs:14-19) << 8
     const uint32_t ones[4] = {0x01010101u, 0x01010101u, 0x01010101u, 0x01010101u};
     const bool head = g < n_heads;   // row g of the tile is head g
@@ -485,15 +485,15 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__
             mma_s8s8(sacc[j], qa[0], kw.x, kw.y);
             mma_s8s8(sacc[j], qa[1], kw.z, kw.w);
         }
+        // V^T A fragments: word (group 2t or 2t+1 = keys 8t..8t+3 / 8t+4..8t+7, dim)
         uint32_t va[4][4];
+        const uint32_t *vtile = reinterpret_cast<const uint32_t *>(vt + (size_t)kb * 64) + 2 * t * 64;
 #pragma unroll
         for (int mi = 0; mi < 4; mi++) {
-            const uint2 lo2 = *reinterpret_cast<const uint2 *>(vt + (size_t)(16 * mi + g) * len + kb + 8 * t);
-            const uint2 hi2 = *reinterpret_cast<const uint2 *>(vt + (size_t)(16 * mi + g + 8) * len + kb + 8 * t);
-            va[mi][0] = lo2.x;
-            va[mi][1] = hi2.x;
-            va[mi][2] = lo2.y;
-            va[mi][3] = hi2.y;
+            va[mi][0] = vtile[16 * mi + g];
+            va[mi][1] = vtile[16 * mi + g + 8];
+            va[mi][2] = vtile[64 + 16 * mi + g];
+            va[mi][3] = vtile[64 + 16 * mi + g + 8];
         }
         Tile T;
         if (kb + 31 > p)

@@ -84,7 +84,7 @@ struct DecState {   // arithmetic decoder state of one stream
 };
 void launch_dec_init(const uint8_t *data, const uint64_t *data_off, const uint64_t *data_len, int M,
                      DecState *st, uint32_t *tok_in, cudaStream_t stream);
-// split: the tensor-core decode layout (K with permuted dims, V transposed), see decode.cu
+// split: the tensor-core decode layout (K with permuted dims, V in 32-key tiles), see decode.cu
 void launch_kv_append(const int8_t *qkv, int ldq, int d, int pos, const int16_t *rope_cos,
                       const int16_t *rope_sin, int M, int8_t *kvc, size_t cache_ld, bool split, cudaStream_t stream);
 void launch_cdf_decode(const int32_t *logits, int V, int ld, const uint16_t *lut, const uint16_t *lut4k,
