@@ -147,10 +147,11 @@ __device__ __forceinline__ void tile_softmax(const int (&sacc)[4][4], int kb, in
 }
 
 // Segment of each entry (records at or before it in key order within the tile),
-// one byte per entry: word q holds entries 4q..4q+3.  The rescale factors are
-// published to rec_e[row][segment - 1] and the row's record count to rec_n[row].
+// one byte per entry: word q holds entries 4q..4q+3.  The records' (previous
+// max - score) are published to rec_e[row][segment - 1] and the row's record
+// count to rec_n[row]; the fold turns them into rescale factors.
 __device__ __forceinline__ void tile_segments(const Tile &T, int t, int g, uint32_t *rec_e, int *rec_n,
-                                              uint32_t (&segw)[2], const uint16_t *lut4k, uint32_t c8) {
+                                              uint32_t (&segw)[2]) {
     const int c = T.lrec;
     const int c1 = __shfl_up_sync(0xffffffffu, c, 1, 4);
     const int c2 = __shfl_up_sync(0xffffffffu, c, 2, 4);
@@ -164,7 +165,7 @@ __device__ __forceinline__ void tile_segments(const Tile &T, int t, int g, uint3
             const int i = 4 * q + b;
             if (T.ef[i]) {
                 sidx++;
-                rec_e[g * 32 + sidx - 1] = 0x10000u | exp_attn((int)T.ef[i], lut4k, c8);
+                rec_e[g * 32 + sidx - 1] = T.ef[i];
             }
             word |= (uint32_t)sidx << (8 * b);
         }
@@ -329,7 +330,7 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
             uint32_t segw[2] = {0, 0};
             int nr[2] = {0, 0};   // records of the PV rows 2t, 2t+1
             if (maxrec > 0) {
-                tile_segments(T, t, g, rec_e, rec_n, segw, lut4k, c8);
+                tile_segments(T, t, g, rec_e, rec_n, segw);
                 __syncwarp();
                 nr[0] = rec_n[2 * t];
                 nr[1] = rec_n[2 * t + 1];
@@ -342,7 +343,7 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
                         if (nr[e] >= pass) {
                             // the accumulators keep running: state' = R(state + A) - A, with A the
                             // accumulator value now, so that state + A stays the reference's value
-                            const uint32_t ef = rec_e[(2 * t + e) * 32 + pass - 1] & 0xFFFFu;
+                            const uint32_t ef = exp_attn((int)rec_e[(2 * t + e) * 32 + pass - 1], lut4k, c8);
                             const unsigned long long sa = 256ull * (uint32_t)shs[e] + (unsigned long long)(uint32_t)sls[e];
                             s_state[e] = (((s_state[e] + sa) * ef + 0x8000ull) >> 16) - sa;
 #pragma unroll
@@ -512,7 +513,7 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__
         uint32_t segw[2] = {0, 0};
         int nr[2] = {0, 0};
         if (maxrec > 0) {
-            tile_segments(T, t, g, rec_e, rec_n, segw, lut4k, c8);
+            tile_segments(T, t, g, rec_e, rec_n, segw);
             __syncwarp();
             nr[0] = rec_n[2 * t];
             nr[1] = rec_n[2 * t + 1];
@@ -522,7 +523,7 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__
 #pragma unroll
                 for (int e = 0; e < 2; e++) {
                     if (nr[e] >= pass) {
-                        const uint32_t ef = rec_e[(2 * t + e) * 32 + pass - 1] & 0xFFFFu;
+                        const uint32_t ef = exp_attn((int)rec_e[(2 * t + e) * 32 + pass - 1], lut4k, c8);
                         const unsigned long long sa = 256ull * (uint32_t)shs[e] + (unsigned long long)(uint32_t)sls[e];
                         s_state[e] = (((s_state[e] + sa) * ef + 0x8000ull) >> 16) - sa;
 #pragma unroll
