@@ -305,49 +305,51 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
             }
 #pragma unroll 1
             for (int ch = 0; ch < NCH; ch++) {
-                uint32_t w[32];   // this row's 128 output bytes
+                // staging buffer nb was handed to a TMA store two slices ago
+                if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+                __syncwarp();
+                uint8_t *sb = sbuf0 + nb * TC_STAGE_OUT + lane * 128;   // this row's 128 output bytes
                 const uint32_t tcol = tbase + (uint32_t)(ch * EpiShape<EPI>::kAccCols);
-                if (EPI == kEpiInt32) {
-                    tmem_ld32(tcol, w);
-                } else if (EPI == kEpiRequant) {
+                // 32 accumulator columns at a time, converted straight into the staging row;
+                // 128B swizzle: 16-byte chunk c of the row lands at c ^ (row & 7)
+                constexpr int NG = EpiShape<EPI>::kAccCols / 32;
+#pragma unroll 1
+                for (int gi = 0; gi < NG; gi++) {
+                    uint32_t v[32];
+                    tmem_ld32(tcol + 32 * gi, v);
+                    if (ch == NCH - 1 && gi == NG - 1) {   // the accumulator is free for the tile after next
+                        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&tempty[b]);
+                    }
+                    if (EPI == kEpiInt32) {
 #pragma unroll
-                    for (int g = 0; g < 4; g++) {
-                        uint32_t v[32];
-                        tmem_ld32(tcol + 32 * g, v);
+                        for (int c = 0; c < 8; c++)
+                            *reinterpret_cast<uint4 *>(sb + ((c ^ (lane & 7)) << 4)) =
+                                make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+                    } else if (EPI == kEpiRequant) {   // 32 bytes: chunks 2gi, 2gi+1
+                        uint32_t w[8];
 #pragma unroll
                         for (int j = 0; j < 8; j++)
-                            w[8 * g + j] = pack4(rq<FAST>((int)v[4 * j], rqp), rq<FAST>((int)v[4 * j + 1], rqp),
-                                                 rq<FAST>((int)v[4 * j + 2], rqp), rq<FAST>((int)v[4 * j + 3], rqp));
-                    }
-                } else {   // ReGLU on (gate_j, up_j) = columns (2j, 2j+1) (reglu.rs:20-46)
+                            w[j] = pack4(rq<FAST>((int)v[4 * j], rqp), rq<FAST>((int)v[4 * j + 1], rqp),
+                                         rq<FAST>((int)v[4 * j + 2], rqp), rq<FAST>((int)v[4 * j + 3], rqp));
 #pragma unroll
-                    for (int g = 0; g < 8; g++) {
-                        uint32_t v[32];
-                        tmem_ld32(tcol + 32 * g, v);
+                        for (int h = 0; h < 2; h++)
+                            *reinterpret_cast<uint4 *>(sb + (((2 * gi + h) ^ (lane & 7)) << 4)) =
+                                make_uint4(w[4 * h], w[4 * h + 1], w[4 * h + 2], w[4 * h + 3]);
+                    } else {   // ReGLU on (gate_j, up_j) = columns (2j, 2j+1) (reglu.rs:20-46): 16 bytes, chunk gi
                         int y[16];
 #pragma unroll
                         for (int j = 0; j < 16; j++) {
                             const int gte = max(rq<FAST>((int)v[2 * j], rqp), 0);
-                            const int x = gte * rq<FAST>((int)v[2 * j + 1], rqp);
-                            y[j] = clamp127((x + 63 + ((x >> 7) & 1)) >> 7);
+                            const int x = gte * rq<FAST>((int)v[2 * j + 1], rqp);   // |x| <= 127 * 127
+                            y[j] = (x + 63 + ((x >> 7) & 1)) >> 7;                  // |y| <= 126: no clamp
                         }
-#pragma unroll
-                        for (int j = 0; j < 4; j++) w[4 * g + j] = pack4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
+                        *reinterpret_cast<uint4 *>(sb + ((gi ^ (lane & 7)) << 4)) =
+                            make_uint4(pack4(y[0], y[1], y[2], y[3]), pack4(y[4], y[5], y[6], y[7]),
+                                       pack4(y[8], y[9], y[10], y[11]), pack4(y[12], y[13], y[14], y[15]));
                     }
                 }
-                if (ch == NCH - 1) {   // the accumulator is free for the tile after next
-                    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&tempty[b]);
-                }
-                // staging buffer nb was handed to a TMA store two slices ago
-                if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-                __syncwarp();
-                uint8_t *sb = sbuf0 + nb * TC_STAGE_OUT + lane * 128;
-#pragma unroll
-                for (int c = 0; c < 8; c++)   // 128B swizzle: 16-byte chunk c lands at c ^ (row & 7)
-                    *reinterpret_cast<uint4 *>(sb + ((c ^ (lane & 7)) << 4)) =
-                        make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
                 if (lane == 0) {   // rows at or beyond M are clipped by the map
