@@ -15,9 +15,10 @@
 //                    per stage into one of two TMEM accumulators (2 x BN
 //                    columns), tcgen05.commit frees the stage and, after the
 //                    tile's last K block, hands the accumulator to the epilogue;
-//   warps 2..5       epilogue: warp w owns TMEM lanes 32*(w%4).. (its 32 rows),
-//                    converts 128-byte output slices per row, writes them
-//                    128B-swizzled into a per-warp staging buffer and stores
+//   warps 2..9       epilogue: warp w reads TMEM lanes 32*(w%4).. (its 32 rows),
+//                    the two warps of a quadrant each half of every 128-byte
+//                    output slice; each converts its 64 bytes per row, writes
+//                    them 64B-swizzled into its own staging buffer and stores
 //                    them with TMA (cp.async.bulk.tensor, global <- shared),
 //                    then releases the accumulator, so the epilogue of tile i
 //                    overlaps the MMAs of tile i+1.
@@ -34,8 +35,9 @@ namespace {
 
 constexpr int TC_BM = 128;
 constexpr int TC_BK = 128;   // bytes of K per stage = one 128-byte swizzle row
-constexpr int TC_THREADS = 192;
-constexpr int TC_STAGE_OUT = 32 * 128;   // one epilogue warp's staging box: 32 rows x 128 bytes
+constexpr int TC_EPI_WARPS = 8;   // two per TMEM lane quadrant, each taking half of a slice's columns
+constexpr int TC_THREADS = 64 + 32 * TC_EPI_WARPS;
+constexpr int TC_STAGE_OUT = 32 * 64;   // one epilogue warp's staging box: 32 rows x 64 bytes
 constexpr long long kWaitBudget = 4000000000ll;   // clock cycles (about 2 s)
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
@@ -137,6 +139,16 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         : "memory");
 }
 
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+}
+
 // Requantisation parameters.  When clamp_a > 0 the product of an accumulator
 // clamped to [-clamp_a, clamp_a] with mult fits in int32 and every accumulator
 // beyond the clamp saturates to +-127 either way, so the 64-bit product of
@@ -158,11 +170,12 @@ __device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
     return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
 }
 
-// Output columns (elements) of one 128-byte staging row and accumulator columns it consumes.
+// A slice: 128 output bytes per row, made from kAccCols accumulator columns; each of the
+// two epilogue warps of a quadrant converts half of it (64 bytes, kOutCols elements).
 template <int EPI>
 struct EpiShape {
     static constexpr int kAccCols = EPI == kEpiInt32 ? 32 : (EPI == kEpiReglu ? 256 : 128);
-    static constexpr int kOutCols = EPI == kEpiInt32 ? 32 : 128;
+    static constexpr int kOutCols = EPI == kEpiInt32 ? 16 : 64;
 };
 
 template <int BN, int STAGES, int EPI, bool FAST>
@@ -176,8 +189,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
     constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     constexpr int TMEM_COLS = 2 * BN;   // two accumulators
     constexpr int NCH = BN / EpiShape<EPI>::kAccCols;   // staging rows per tile
-    uint8_t *stage_out = smem + STAGES * STAGE_BYTES;   // 4 warps x 2 buffers x 4 KB
-    uint64_t *full = reinterpret_cast<uint64_t *>(stage_out + 8 * TC_STAGE_OUT);
+    uint8_t *stage_out = smem + STAGES * STAGE_BYTES;   // TC_EPI_WARPS warps x 2 buffers x 2 KB
+    uint64_t *full = reinterpret_cast<uint64_t *>(stage_out + 2 * TC_EPI_WARPS * TC_STAGE_OUT);
     uint64_t *empty = full + STAGES;
     uint64_t *tfull = empty + STAGES;
     uint64_t *tempty = tfull + 2;
@@ -197,7 +210,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], 4);
+            mbar_init(&tempty[b], TC_EPI_WARPS);
         }
         mbar_init(drain, 1);
         abort_flag = 0;
@@ -276,8 +289,9 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
             mma_commit(drain);
             mbar_wait(drain, 0, nullptr);
         }
-    } else {   // epilogue warps 2..5
-        const int q = warp & 3;   // TMEM lane quadrant = rows 32q .. 32q+31 of the tile
+    } else {   // epilogue warps 2..9
+        const int q = warp & 3;            // TMEM lane quadrant = rows 32q .. 32q+31 of the tile
+        const int hf = (warp - 2) >> 2;    // which half of each slice's columns
         uint8_t *sbuf0 = stage_out + (warp - 2) * 2 * TC_STAGE_OUT;
         int tc = 0, nb = 0;
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, tc++) {
@@ -308,52 +322,63 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                 // staging buffer nb was handed to a TMA store two slices ago
                 if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
                 __syncwarp();
-                uint8_t *sb = sbuf0 + nb * TC_STAGE_OUT + lane * 128;   // this row's 128 output bytes
-                const uint32_t tcol = tbase + (uint32_t)(ch * EpiShape<EPI>::kAccCols);
-                // 32 accumulator columns at a time, converted straight into the staging row;
-                // 128B swizzle: 16-byte chunk c of the row lands at c ^ (row & 7)
-                constexpr int NG = EpiShape<EPI>::kAccCols / 32;
-#pragma unroll 1
-                for (int gi = 0; gi < NG; gi++) {
-                    uint32_t v[32];
-                    tmem_ld32(tcol + 32 * gi, v);
-                    if (ch == NCH - 1 && gi == NG - 1) {   // the accumulator is free for the tile after next
+                uint8_t *sb = sbuf0 + nb * TC_STAGE_OUT + lane * 64;   // this row's 64 output bytes
+                constexpr int HC = EpiShape<EPI>::kAccCols / 2;          // accumulator columns of this warp
+                const uint32_t tcol = tbase + (uint32_t)(ch * EpiShape<EPI>::kAccCols + hf * HC);
+                // 64B swizzle of a 64-byte row: 16-byte chunk c lands at c ^ ((row >> 1) & 3)
+                const int sw = (lane >> 1) & 3;
+                if (EPI == kEpiInt32) {
+                    uint32_t v[16];
+                    tmem_ld16(tcol, v);
+                    if (ch == NCH - 1) {   // the accumulator is free for the tile after next
                         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&tempty[b]);
                     }
-                    if (EPI == kEpiInt32) {
 #pragma unroll
-                        for (int c = 0; c < 8; c++)
-                            *reinterpret_cast<uint4 *>(sb + ((c ^ (lane & 7)) << 4)) =
-                                make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
-                    } else if (EPI == kEpiRequant) {   // 32 bytes: chunks 2gi, 2gi+1
-                        uint32_t w[8];
-#pragma unroll
-                        for (int j = 0; j < 8; j++)
-                            w[j] = pack4(rq<FAST>((int)v[4 * j], rqp), rq<FAST>((int)v[4 * j + 1], rqp),
-                                         rq<FAST>((int)v[4 * j + 2], rqp), rq<FAST>((int)v[4 * j + 3], rqp));
-#pragma unroll
-                        for (int h = 0; h < 2; h++)
-                            *reinterpret_cast<uint4 *>(sb + (((2 * gi + h) ^ (lane & 7)) << 4)) =
-                                make_uint4(w[4 * h], w[4 * h + 1], w[4 * h + 2], w[4 * h + 3]);
-                    } else {   // ReGLU on (gate_j, up_j) = columns (2j, 2j+1) (reglu.rs:20-46): 16 bytes, chunk gi
-                        int y[16];
-#pragma unroll
-                        for (int j = 0; j < 16; j++) {
-                            const int gte = max(rq<FAST>((int)v[2 * j], rqp), 0);
-                            const int x = gte * rq<FAST>((int)v[2 * j + 1], rqp);   // |x| <= 127 * 127
-                            y[j] = (x + 63 + ((x >> 7) & 1)) >> 7;                  // |y| <= 126: no clamp
+                    for (int c = 0; c < 4; c++)
+                        *reinterpret_cast<uint4 *>(sb + ((c ^ sw) << 4)) =
+                            make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+                } else {
+                    // 32 accumulator columns at a time, converted straight into the staging row
+                    constexpr int NG = HC / 32;
+#pragma unroll 1
+                    for (int gi = 0; gi < NG; gi++) {
+                        uint32_t v[32];
+                        tmem_ld32(tcol + 32 * gi, v);
+                        if (ch == NCH - 1 && gi == NG - 1) {   // the accumulator is free for the tile after next
+                            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(&tempty[b]);
                         }
-                        *reinterpret_cast<uint4 *>(sb + ((gi ^ (lane & 7)) << 4)) =
-                            make_uint4(pack4(y[0], y[1], y[2], y[3]), pack4(y[4], y[5], y[6], y[7]),
-                                       pack4(y[8], y[9], y[10], y[11]), pack4(y[12], y[13], y[14], y[15]));
+                        if (EPI == kEpiRequant) {   // 32 bytes: chunks 2gi, 2gi+1
+                            uint32_t w[8];
+#pragma unroll
+                            for (int j = 0; j < 8; j++)
+                                w[j] = pack4(rq<FAST>((int)v[4 * j], rqp), rq<FAST>((int)v[4 * j + 1], rqp),
+                                             rq<FAST>((int)v[4 * j + 2], rqp), rq<FAST>((int)v[4 * j + 3], rqp));
+#pragma unroll
+                            for (int hh = 0; hh < 2; hh++)
+                                *reinterpret_cast<uint4 *>(sb + (((2 * gi + hh) ^ sw) << 4)) =
+                                    make_uint4(w[4 * hh], w[4 * hh + 1], w[4 * hh + 2], w[4 * hh + 3]);
+                        } else {   // ReGLU on (gate_j, up_j) = columns (2j, 2j+1) (reglu.rs:20-46): 16 bytes, chunk gi
+                            int y[16];
+#pragma unroll
+                            for (int j = 0; j < 16; j++) {
+                                const int gte = max(rq<FAST>((int)v[2 * j], rqp), 0);
+                                const int x = gte * rq<FAST>((int)v[2 * j + 1], rqp);   // |x| <= 127 * 127
+                                y[j] = (x + 63 + ((x >> 7) & 1)) >> 7;                  // |y| <= 126: no clamp
+                            }
+                            *reinterpret_cast<uint4 *>(sb + ((gi ^ sw) << 4)) =
+                                make_uint4(pack4(y[0], y[1], y[2], y[3]), pack4(y[4], y[5], y[6], y[7]),
+                                           pack4(y[8], y[9], y[10], y[11]), pack4(y[12], y[13], y[14], y[15]));
+                        }
                     }
                 }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
                 if (lane == 0) {   // rows at or beyond M are clipped by the map
-                    const int x = (EPI == kEpiReglu ? n0 / 2 : n0) + ch * EpiShape<EPI>::kOutCols;
+                    const int x = (EPI == kEpiReglu ? n0 / 2 : n0) + (2 * ch + hf) * EpiShape<EPI>::kOutCols;
                     tma_store_2d(&map_o, sbuf0 + nb * TC_STAGE_OUT, x, m0 + 32 * q);
                 }
                 nb ^= 1;
@@ -387,7 +412,7 @@ EncodeTiledFn encode_fn() {
 template <int BN>
 struct TcCfg {
     static constexpr int kStages = BN == 256 ? 3 : 4;
-    static constexpr size_t kSmem = 1024 + (size_t)kStages * (TC_BM + BN) * TC_BK + 8 * TC_STAGE_OUT +
+    static constexpr size_t kSmem = 1024 + (size_t)kStages * (TC_BM + BN) * TC_BK + 2 * TC_EPI_WARPS * TC_STAGE_OUT +
                                     (2 * kStages + 5) * 8 + 16;
 };
 
@@ -405,16 +430,16 @@ int sm_count() {
 }
 
 // TMA map of the output: [rows][cols] elements of elem_bytes, row pitch ld_bytes,
-// stored in boxes of 128 bytes x 32 rows with the 128-byte swizzle.
+// stored in boxes of 64 bytes x 32 rows with the 64-byte swizzle.
 bool make_out_map(CUtensorMap *map, void *base, uint64_t rows, uint64_t cols, uint64_t ld_bytes, int elem_bytes) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return false;
     cuuint64_t dims[2] = {cols, rows};
     cuuint64_t strides[1] = {ld_bytes};
-    cuuint32_t box[2] = {(cuuint32_t)(128 / elem_bytes), 32};
+    cuuint32_t box[2] = {(cuuint32_t)(64 / elem_bytes), 32};
     cuuint32_t estr[2] = {1, 1};
     return fn(map, elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_INT32 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, base, dims,
-              strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
               CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
