@@ -32,30 +32,28 @@ __global__ void k_rows(const uint32_t *__restrict__ tokens, const int *__restric
 }
 
 // Warp-level RMSNorm of one row held as D/128 words of 4 int8 per lane
-// (lane owns bytes [4*lane + 128*j, +4)).  rmsnorm.rs:40-75.
+// (lane owns bytes [4*lane + 128*j, +4)).  rmsnorm.rs:40-75.  The sum of squares
+// uses dp4a (exact: at most 4 * 127^2 per call); round_even(t / 2^15) is
+// (t + 2^14 - 1 + ((t >> 15) & 1)) >> 15, exact for |t| <= 127 * 127 * 2^15.
 template <int NW>
-__device__ __forceinline__ void rmsnorm_words(const uint32_t (&x)[NW], const uint32_t (&w)[NW],
-                                              int d, int eps, uint32_t (&y)[NW]) {
-    uint32_t ss = 0;
+__device__ __forceinline__ void rmsnorm_words(const uint32_t (&x)[NW], const uint32_t (&w)[NW], int eps,
+                                              uint32_t (&y)[NW]) {
+    constexpr int D = NW * 128;
+    int ss = 0;
 #pragma unroll
-    for (int j = 0; j < NW; j++)
-#pragma unroll
-        for (int b = 0; b < 4; b++) {
-            int v = sext8(x[j], b);
-            ss += (uint32_t)(v * v);
-        }
+    for (int j = 0; j < NW; j++) ss = __dp4a((int)x[j], (int)x[j], ss);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    int inv = inv_rms_q15(ss, d, eps);
+    const int inv = inv_rms_q15((uint32_t)ss, D, eps);
 #pragma unroll
     for (int j = 0; j < NW; j++) {
-        uint32_t out = 0;
+        int o4[4];
 #pragma unroll
         for (int b = 0; b < 4; b++) {
-            int t = (sext8(x[j], b) * sext8(w[j], b)) * inv;
-            out |= ((uint32_t)(uint8_t)(int8_t)clamp127(sra_rne32(t, 15))) << (8 * b);
+            const int t = (sext8(x[j], b) * sext8(w[j], b)) * inv;
+            o4[b] = clamp127((t + 0x3FFF + ((t >> 15) & 1)) >> 15);
         }
-        y[j] = out;
+        y[j] = __byte_perm(__byte_perm(o4[0], o4[1], 0x0040), __byte_perm(o4[2], o4[3], 0x0040), 0x5410);
     }
 }
 
@@ -100,7 +98,7 @@ __global__ void k_embed_norm(const uint32_t *__restrict__ tok_in, const int8_t *
         for (int b = 0; b < 4; b++) c |= (uint32_t)(uint8_t)clamp127(sext8(x[j], b)) << (8 * b);
         x[j] = c;
     }
-    rmsnorm_words<NW>(x, w, D, eps, y);
+    rmsnorm_words<NW>(x, w, eps, y);
     uint32_t *yo = reinterpret_cast<uint32_t *>(xn + (size_t)warp * D);
 #pragma unroll
     for (int j = 0; j < NW; j++) yo[lane + 32 * j] = y[j];
@@ -129,7 +127,7 @@ __global__ void k_residual_norm(const int8_t *__restrict__ o, const int8_t *__re
         w2[j] = __ldg(nw + lane + 32 * j);
         rv[j] = load_res4(xr + 4 * (lane + 32 * j));
     }
-    rmsnorm_words<NW>(x, w, D, eps, y);
+    rmsnorm_words<NW>(x, w, eps, y);
 #pragma unroll
     for (int j = 0; j < NW; j++) {
         int4 r = rv[j];
@@ -141,7 +139,7 @@ __global__ void k_residual_norm(const int8_t *__restrict__ o, const int8_t *__re
         x[j] = (uint32_t)(uint8_t)clamp127(r.x) | ((uint32_t)(uint8_t)clamp127(r.y) << 8) |
                ((uint32_t)(uint8_t)clamp127(r.z) << 16) | ((uint32_t)(uint8_t)clamp127(r.w) << 24);
     }
-    rmsnorm_words<NW>(x, w2, D, eps, y);
+    rmsnorm_words<NW>(x, w2, eps, y);
     uint32_t *yo = reinterpret_cast<uint32_t *>(xn + (size_t)warp * D);
 #pragma unroll
     for (int j = 0; j < NW; j++) yo[lane + 32 * j] = y[j];
