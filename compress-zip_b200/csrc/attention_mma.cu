@@ -402,6 +402,22 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
     }
 }
 
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+                 : "memory");
+}
+
+// The 4 KB of one 32-key tile of a stream (K rows, then the V tile) into a
+// shared-memory stage, 8 x 16 bytes per lane, as one cp.async group.
+__device__ __forceinline__ void decode_tile_async(uint8_t *stage, const int8_t *ks, const int8_t *vt, int kb, int lane) {
+#pragma unroll
+    for (int i = 0; i < 4; i++) cp_async16(stage + 16 * (lane + 32 * i), ks + (size_t)kb * 64 + 16 * (lane + 32 * i));
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+        cp_async16(stage + 2048 + 16 * (lane + 32 * i), vt + (size_t)kb * 64 + 16 * (lane + 32 * i));
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
 // Decode: one warp per stream r, the query of every head at position p against
 // the stream's keys 0..p in the split cache layout (K rows of 64 permuted dims,
 // then V in 2 KB tiles of 32 keys as [8 key groups][64 dims][4 keys]).  The heads are the 8 rows of the attention tile (A rows
@@ -414,10 +430,12 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__
                        const int16_t *__restrict__ rope_sin, const uint16_t *__restrict__ lut4k,
                        int8_t *__restrict__ out, int ldo) {
     __shared__ __align__(16) uint8_t wsm[AM_WARPS * AM_WARP_SMEM];
+    extern __shared__ __align__(16) uint8_t dsm[];   // per warp: two 4 KB tile stages
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, t = lane & 3;
     const int r = blockIdx.x * AM_WARPS + warp;
     if (r >= M) return;
+    uint8_t *stages = dsm + warp * 8192;
     uint32_t *rec_e = reinterpret_cast<uint32_t *>(wsm + warp * AM_WARP_SMEM);   // [8][32]
     int *rec_n = reinterpret_cast<int *>(rec_e + AM_ROWS * 32);                  // [8]
     uint8_t *ostage = reinterpret_cast<uint8_t *>(rec_n + AM_ROWS);              // [8][64]
@@ -477,18 +495,28 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__
         for (int k = 0; k < 4; k++) { hiacc[mi][k] = 0; loacc[mi][k] = 0; vst[mi][k] = 0; }
     int shs[4] = {0, 0, 0, 0}, sls[4] = {0, 0, 0, 0};
 
+    decode_tile_async(stages, ks, vt, 0, lane);   // tile 0 in flight
     for (int kb = 0; kb <= p; kb += 32) {
+        // the next tile's copy overlaps this tile's work; then wait for this one
+        if (kb + 32 <= p) {
+            decode_tile_async(stages + (((kb >> 5) + 1) & 1) * 4096, ks, vt, kb + 32, lane);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncwarp();
+        const uint8_t *kst = stages + ((kb >> 5) & 1) * 4096;   // K rows of the tile, then the V tile
         int sacc[4][4];
 #pragma unroll
         for (int j = 0; j < 4; j++) {
             sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0;
-            const uint4 kw = *reinterpret_cast<const uint4 *>(ks + (size_t)(kb + perm_key(8 * j + g)) * 64 + 16 * t);
+            const uint4 kw = *reinterpret_cast<const uint4 *>(kst + perm_key(8 * j + g) * 64 + 16 * t);
             mma_s8s8(sacc[j], qa[0], kw.x, kw.y);
             mma_s8s8(sacc[j], qa[1], kw.z, kw.w);
         }
         // V^T A fragments: word (group 2t or 2t+1 = keys 8t..8t+3 / 8t+4..8t+7, dim)
         uint32_t va[4][4];
-        const uint32_t *vtile = reinterpret_cast<const uint32_t *>(vt + (size_t)kb * 64) + 2 * t * 64;
+        const uint32_t *vtile = reinterpret_cast<const uint32_t *>(kst + 2048) + 2 * t * 64;
 #pragma unroll
         for (int mi = 0; mi < 4; mi++) {
             va[mi][0] = vtile[16 * mi + g];
@@ -496,6 +524,7 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__
             va[mi][2] = vtile[64 + 16 * mi + g];
             va[mi][3] = vtile[64 + 16 * mi + g + 8];
         }
+        __syncwarp();   // every lane has its fragments: the stage may be refilled next iteration
         Tile T;
         if (kb + 31 > p)
             tile_softmax<true, WIDE>(sacc, kb, p, p + 1, mult, t, m, lut4k, c8, T);
@@ -589,6 +618,8 @@ size_t attention_mma_smem(int max_len) {
 bool attention_mma_fits(int max_len) { return max_len <= AM_MAX_KEYS; }
 
 void attention_mma_init() {
+    cudaFuncSetAttribute(k_attention_decode_mma<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, AM_WARPS * 8192);
+    cudaFuncSetAttribute(k_attention_decode_mma<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, AM_WARPS * 8192);
     cudaFuncSetAttribute(k_attention_mma<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)attention_mma_smem(AM_MAX_KEYS));
     cudaFuncSetAttribute(k_attention_mma<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -621,10 +652,10 @@ void launch_attention_decode_mma(const int8_t *qkv, int ldq, const int8_t *kvc, 
     if (M == 0) return;
     const unsigned grid = (unsigned)((M + AM_WARPS - 1) / AM_WARPS);
     if (wide_mult)
-        k_attention_decode_mma<true><<<grid, AM_THREADS, 0, st>>>(qkv, ldq, kvc, cache_ld, M, p, n_heads, score_mult,
+        k_attention_decode_mma<true><<<grid, AM_THREADS, AM_WARPS * 8192, st>>>(qkv, ldq, kvc, cache_ld, M, p, n_heads, score_mult,
                                                                  sink_key, rope_cos, rope_sin, lut4k, out, ldo);
     else
-        k_attention_decode_mma<false><<<grid, AM_THREADS, 0, st>>>(qkv, ldq, kvc, cache_ld, M, p, n_heads, score_mult,
+        k_attention_decode_mma<false><<<grid, AM_THREADS, AM_WARPS * 8192, st>>>(qkv, ldq, kvc, cache_ld, M, p, n_heads, score_mult,
                                                                   sink_key, rope_cos, rope_sin, lut4k, out, ldo);
 }
 
