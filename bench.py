@@ -54,6 +54,8 @@ def parse():
     ap.add_argument("--cpu-sample-docs", type=int, default=32)
     ap.add_argument("--decode-docs", type=int, default=4096,
                     help="config 3: documents of 4,096 B decoded at ctx 512 (0 skips)")
+    ap.add_argument("--pipeline-docs", type=int, default=64,
+                    help="host pipeline sample (tokenise + GPU coder + CZIPv1 + brotli); 0 skips")
     return ap.parse_args()
 
 
@@ -283,6 +285,7 @@ def main():
     parity = bytes(h_out_np[:nout_h]) == bytes(out[:nout])
 
     dec = decode_bench(eng, mf, rank, args, stream, world) if args.decode_docs > 0 else None
+    pipe = host_pipeline(eng, mf, args) if rank == 0 and args.pipeline_docs > 0 else None
 
     (t_max, t_e2e_max), (all_tok, all_bytes) = reduce_over_ranks(
         [t_rank, t_e2e], [float(n_tok), float(nbytes)], f"cuda:{local}")
@@ -333,6 +336,8 @@ def main():
         }
         if dec is not None:
             line["decode"] = dec
+        if pipe is not None:
+            line["host_pipeline"] = pipe
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
@@ -385,6 +390,63 @@ def decode_bench(eng, mf, rank, args, stream, world):
             "tokens_per_gpu": int(len(tokens)), "exact_roundtrip": exact,
             "gpu_launches_per_step": int(launches // steps),
             "kernels_ms_per_step": {k: round(v["ms"], 3) for k, v in kern.items() if v["launches"]}}
+
+
+def host_pipeline(eng, mf, args):
+    """The whole compress CLI path on a bounded sample, stage by stage, labelled apart
+    from the hot-path figures: UTF-8 text -> tiktoken ids (all host threads) -> the
+    GPU coder through the C ABI (host buffers) -> CZIPv1 container -> outer brotli
+    q11 / lgwin 22 (rust/src/main.rs:186-281).  Wall clock on the host."""
+    from compress_zip_b200 import container, outer_codec
+    from compress_zip_b200.cli import hash_model_path
+
+    docs = synth.documents(range(1, args.pipeline_docs + 1), DOC_BYTES)
+    text_bytes = sum(len(d.encode("utf-8")) for d in docs)
+    tok = mf.tokenizer()
+    t0 = time.perf_counter()
+    ids = tok.encode_batch(docs, num_threads=min(16, os.cpu_count() or 1))
+    t1 = time.perf_counter()
+    streams = []
+    for t in ids:   # one CZIPv1 stream per document, chunks of ctx (rust/src/main.rs:199-205)
+        a = np.asarray(t, dtype=np.uint32)
+        nch = (len(a) + args.ctx - 1) // args.ctx
+        streams.append((a, np.array([min(i * args.ctx, len(a)) for i in range(nch + 1)], np.uint64)))
+    tokens = np.concatenate([a for a, _ in streams])
+    starts, base = [0], 0
+    for a, st in streams:
+        starts.extend(int(base + x) for x in st[1:])
+        base += len(a)
+    chunks = eng.compress_chunks(tokens, np.asarray(starts, np.uint64))
+    t2 = time.perf_counter()
+    mid = hash_model_path(MODEL)
+    jobs, ci = [], 0
+    for (a, st), d in zip(streams, docs):
+        cf = container.CompressedFile.with_context_length(mid, 0, container.BROTLI, len(d.encode("utf-8")),
+                                                          int(np.log2(args.ctx)))
+        nch = len(st) - 1
+        for k in range(nch):
+            n = int(st[k + 1] - st[k])
+            cf.add_chunk(chunks[ci], k == nch - 1, n if k == nch - 1 else args.ctx)
+            ci += 1
+        jobs.append(cf.to_bytes_uncompressed())
+
+    def finish(job):   # the outer codec runs in C (ctypes releases the GIL): one file per thread
+        outer, payload = job
+        return len(outer) + len(outer_codec.compress(payload, container.BROTLI))
+
+    from concurrent.futures import ThreadPoolExecutor
+    nthr = min(16, os.cpu_count() or 1)
+    with ThreadPoolExecutor(nthr) as ex:
+        out_bytes = sum(ex.map(finish, jobs))
+    t3 = time.perf_counter()
+    mbs = lambda dt: round(text_bytes / dt / 1e6, 3)
+    return {"sample": f"{args.pipeline_docs} docs x {DOC_BYTES} B (seeds 1..{args.pipeline_docs}), "
+                      f"{len(tokens)} tokens, one CZIPv1 file per document",
+            "input_bytes": text_bytes, "output_bytes": out_bytes,
+            "tokenize_mb_per_s": mbs(t1 - t0), "gpu_coder_mb_per_s": mbs(t2 - t1),
+            "container_brotli_mb_per_s": mbs(t3 - t2), "container_brotli_threads": nthr,
+            "total_mb_per_s": mbs(t3 - t0),
+            "clock": "host wall clock, one pass after the timed steps"}
 
 
 def _oracle_sample(mf, ndocs, ctx):

@@ -227,3 +227,27 @@ def test_int32_residual_path(shipped_path, shipped_oracle, oracle_mod, shipped_t
             oracle_mod.compress_chunks(shipped_oracle, shipped_tokens, starts)
     finally:
         eng.close()
+
+
+def test_config4_long_chunk(tmp_path, shipped_path, oracle_mod):
+    """Configuration-4 shape: the arch-2 model at context 4096 with a chunk longer
+    than 1024 positions (the CUDA-core attention kernel over global-memory K/V),
+    compressed bytes equal to the oracle's, and decoded back on the GPU."""
+    from compress_zip_b200 import czm, synth
+    from compress_zip_b200.engine import Engine
+
+    mf = czm.ModelFile.load(shipped_path)
+    data = synth.arch2_model(mf, 4096)
+    p = tmp_path / "arch2_4096.czm"
+    p.write_bytes(data)
+    om = oracle_mod.load_model(str(p))
+    toks = np.array(mf.tokenizer().encode_with_special_tokens(synth.document(10000, 2000)), np.uint32)[:1300]
+    starts = np.array([0, len(toks)], np.uint64)
+    eng = Engine(data, 0)
+    try:
+        want = oracle_mod.compress_chunks(om, toks, starts)
+        got = eng.compress_chunks(toks, starts)
+        assert got == want
+        assert np.array_equal(eng.decompress_chunks(got, np.array([len(toks)], np.uint32)), toks)
+    finally:
+        eng.close()
