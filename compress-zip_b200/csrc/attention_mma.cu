@@ -106,7 +106,7 @@ struct Tile {
 };
 
 // Scores, prefix max, records and weights of row g in one 32-key tile.
-template <bool MASKED, bool WIDE>
+template <bool MASKED, bool WIDE, bool EXP0>
 __device__ __forceinline__ void tile_softmax(const int (&sacc)[4][4], int kb, int prow, int n, int mult, int t,
                                              int &m, const uint16_t *lut4k, uint32_t c8, Tile &T) {
     int sc[8], L[8];
@@ -134,7 +134,14 @@ __device__ __forceinline__ void tile_softmax(const int (&sacc)[4][4], int kb, in
         bool valid = true;
         if (MASKED) valid = kb + 8 * t + i <= prow && prow < n;
         const int pm = max(base, L[i]);
-        T.w[i] = valid ? exp_attn((int)((uint32_t)sc[i] - (uint32_t)pm), lut4k, c8) : 0u;
+        uint32_t w;
+        if (EXP0) {   // pm >= sc without wrap-around (non-saturating scores) and lut4k[0] == 65535
+            const uint32_t neg = (uint32_t)pm - (uint32_t)sc[i];
+            w = __ldg(lut4k + min(__umulhi(neg, c8) + ((neg * c8) >> 31), 4096u));
+        } else {
+            w = exp_attn((int)((uint32_t)sc[i] - (uint32_t)pm), lut4k, c8);
+        }
+        T.w[i] = valid ? w : 0u;
         const bool rec = valid && sc[i] > prevmax && prevmax != INT32_MIN;
         T.ef[i] = rec ? (uint32_t)prevmax - (uint32_t)sc[i] : 0u;
         lrec += rec;
@@ -181,7 +188,7 @@ __device__ __forceinline__ uint32_t bytes_equal(uint32_t x, uint32_t q) {
     return prmt(~nz & 0x80808080u, 0u, 0xBA98u);                    // replicate bit 7 over the byte
 }
 
-template <bool WIDE>
+template <bool WIDE, bool EXP0>
 __global__ void __launch_bounds__(AM_THREADS, 1)
 k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restrict__ kv_g,
                 const int *__restrict__ chunk_row0, const int *__restrict__ chunk_len, int n_heads,
@@ -271,7 +278,7 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
 
         int m = INT32_MIN;   // running max of row g
         // PV layout: thread (g, t) holds rows 2t + e, dims 16*mi + g + 8*dh at [mi][2*dh + e]
-        unsigned long long s_state[2] = {0, 0};
+        uint32_t s_state[2] = {0u, 0u};   // s < 65535 * 1025 < 2^27 for chunks of <= 1024 keys
         if (sink_key != nullptr) {   // attention.rs:211-224
             int accs[4] = {0, 0, 0, 0};
 #pragma unroll
@@ -281,7 +288,7 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
                 mma_s8s8(accs, qa[kk], b0, b1);   // every B column is the sink key
             }
             m = score_from_dot<true>(accs[0], mult);
-            s_state[0] = s_state[1] = 65535ull;
+            s_state[0] = s_state[1] = 65535u;
         }
         int hiacc[4][4], loacc[4][4], vst[4][4];
 #pragma unroll
@@ -314,9 +321,9 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
 
             Tile T;
             if (!full_rows || kb + 31 > p0)
-                tile_softmax<true, WIDE>(sacc, kb, prow, n, mult, t, m, lut4k, c8, T);
+                tile_softmax<true, WIDE, EXP0>(sacc, kb, prow, n, mult, t, m, lut4k, c8, T);
             else
-                tile_softmax<false, WIDE>(sacc, kb, prow, n, mult, t, m, lut4k, c8, T);
+                tile_softmax<false, WIDE, EXP0>(sacc, kb, prow, n, mult, t, m, lut4k, c8, T);
             // P^T B fragments (u8 halves of the weights): word q = entries 4q..4q+3
             uint32_t phi[2], plo[2];
 #pragma unroll
@@ -344,8 +351,8 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
                             // the accumulators keep running: state' = R(state + A) - A, with A the
                             // accumulator value now, so that state + A stays the reference's value
                             const uint32_t ef = exp_attn((int)rec_e[(2 * t + e) * 32 + pass - 1], lut4k, c8);
-                            const unsigned long long sa = 256ull * (uint32_t)shs[e] + (unsigned long long)(uint32_t)sls[e];
-                            s_state[e] = (((s_state[e] + sa) * ef + 0x8000ull) >> 16) - sa;
+                            const uint32_t sa = 256u * (uint32_t)shs[e] + (uint32_t)sls[e];
+                            s_state[e] = (uint32_t)(((unsigned long long)(s_state[e] + sa) * ef + 0x8000ull) >> 16) - sa;
 #pragma unroll
                             for (int mi = 0; mi < 4; mi++)
 #pragma unroll
@@ -379,7 +386,7 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
         // output: clamp(round_half_even(vacc / s)) (attention.rs:279-284), staged per warp
 #pragma unroll
         for (int e = 0; e < 2; e++) {
-            const unsigned long long sv = s_state[e] + 256ull * (uint32_t)shs[e] + (unsigned long long)(uint32_t)sls[e];
+            const uint32_t sv = s_state[e] + 256u * (uint32_t)shs[e] + (uint32_t)sls[e];
             const unsigned long long den = sv == 0 ? 1ull : sv;
             uint8_t *orow = ostage + (2 * t + e) * 64;
 #pragma unroll
@@ -422,7 +429,7 @@ __device__ __forceinline__ void decode_tile_async(uint8_t *stage, const int8_t *
 // the stream's keys 0..p in the split cache layout (K rows of 64 permuted dims,
 // then V in 2 KB tiles of 32 keys as [8 key groups][64 dims][4 keys]).  The heads are the 8 rows of the attention tile (A rows
 // n_heads..15 are zero); everything else is the chunk kernel's tile step.
-template <bool WIDE>
+template <bool WIDE, bool EXP0>
 __global__ void __launch_bounds__(AM_THREADS, 1)
 k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restrict__ kvc, size_t cache_ld,
                        int M, int p, int n_heads, const int32_t *__restrict__ score_mult,
@@ -527,9 +534,9 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__
         __syncwarp();   // every lane has its fragments: the stage may be refilled next iteration
         Tile T;
         if (kb + 31 > p)
-            tile_softmax<true, WIDE>(sacc, kb, p, p + 1, mult, t, m, lut4k, c8, T);
+            tile_softmax<true, WIDE, EXP0>(sacc, kb, p, p + 1, mult, t, m, lut4k, c8, T);
         else
-            tile_softmax<false, WIDE>(sacc, kb, p, p + 1, mult, t, m, lut4k, c8, T);
+            tile_softmax<false, WIDE, EXP0>(sacc, kb, p, p + 1, mult, t, m, lut4k, c8, T);
         uint32_t phi[2], plo[2];
 #pragma unroll
         for (int q = 0; q < 2; q++) {
@@ -618,27 +625,32 @@ size_t attention_mma_smem(int max_len) {
 bool attention_mma_fits(int max_len) { return max_len <= AM_MAX_KEYS; }
 
 void attention_mma_init() {
-    cudaFuncSetAttribute(k_attention_decode_mma<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, AM_WARPS * 8192);
-    cudaFuncSetAttribute(k_attention_decode_mma<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, AM_WARPS * 8192);
-    cudaFuncSetAttribute(k_attention_mma<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)attention_mma_smem(AM_MAX_KEYS));
-    cudaFuncSetAttribute(k_attention_mma<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)attention_mma_smem(AM_MAX_KEYS));
+    cudaFuncSetAttribute(k_attention_decode_mma<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, AM_WARPS * 8192);
+    cudaFuncSetAttribute(k_attention_decode_mma<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, AM_WARPS * 8192);
+    cudaFuncSetAttribute(k_attention_decode_mma<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, AM_WARPS * 8192);
+    const int smem = (int)attention_mma_smem(AM_MAX_KEYS);
+    cudaFuncSetAttribute(k_attention_mma<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(k_attention_mma<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(k_attention_mma<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
 }
 
 void launch_attention_mma(const int8_t *qkv, int ldq, const int8_t *kv, const int *chunk_row0,
                           const int *chunk_len, int n_chunks, int max_len, int n_heads,
                           const int32_t *score_mult, const int8_t *sink_key, const int16_t *rope_cos,
-                          const int16_t *rope_sin, const uint16_t *lut4k, bool wide_mult, int8_t *out,
+                          const int16_t *rope_sin, const uint16_t *lut4k, bool wide_mult, bool exp0, int8_t *out,
                           int ldo, cudaStream_t st) {
     if (n_chunks == 0) return;
     const size_t smem = attention_mma_smem(max_len);
     if (wide_mult)
-        k_attention_mma<true><<<n_chunks, AM_THREADS, smem, st>>>(
+        k_attention_mma<true, false><<<n_chunks, AM_THREADS, smem, st>>>(
+            qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
+            lut4k, out, ldo);
+    else if (exp0)
+        k_attention_mma<false, true><<<n_chunks, AM_THREADS, smem, st>>>(
             qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
             lut4k, out, ldo);
     else
-        k_attention_mma<false><<<n_chunks, AM_THREADS, smem, st>>>(
+        k_attention_mma<false, false><<<n_chunks, AM_THREADS, smem, st>>>(
             qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
             lut4k, out, ldo);
 }
@@ -648,15 +660,18 @@ bool attention_decode_mma_ok(int n_heads) { return n_heads >= 1 && n_heads <= AM
 void launch_attention_decode_mma(const int8_t *qkv, int ldq, const int8_t *kvc, size_t cache_ld, int M, int p,
                                  int n_heads, const int32_t *score_mult, const int8_t *sink_key,
                                  const int16_t *rope_cos, const int16_t *rope_sin, const uint16_t *lut4k,
-                                 bool wide_mult, int8_t *out, int ldo, cudaStream_t st) {
+                                 bool wide_mult, bool exp0, int8_t *out, int ldo, cudaStream_t st) {
     if (M == 0) return;
     const unsigned grid = (unsigned)((M + AM_WARPS - 1) / AM_WARPS);
     if (wide_mult)
-        k_attention_decode_mma<true><<<grid, AM_THREADS, AM_WARPS * 8192, st>>>(qkv, ldq, kvc, cache_ld, M, p, n_heads, score_mult,
-                                                                 sink_key, rope_cos, rope_sin, lut4k, out, ldo);
+        k_attention_decode_mma<true, false><<<grid, AM_THREADS, AM_WARPS * 8192, st>>>(
+            qkv, ldq, kvc, cache_ld, M, p, n_heads, score_mult, sink_key, rope_cos, rope_sin, lut4k, out, ldo);
+    else if (exp0)
+        k_attention_decode_mma<false, true><<<grid, AM_THREADS, AM_WARPS * 8192, st>>>(
+            qkv, ldq, kvc, cache_ld, M, p, n_heads, score_mult, sink_key, rope_cos, rope_sin, lut4k, out, ldo);
     else
-        k_attention_decode_mma<false><<<grid, AM_THREADS, AM_WARPS * 8192, st>>>(qkv, ldq, kvc, cache_ld, M, p, n_heads, score_mult,
-                                                                  sink_key, rope_cos, rope_sin, lut4k, out, ldo);
+        k_attention_decode_mma<false, false><<<grid, AM_THREADS, AM_WARPS * 8192, st>>>(
+            qkv, ldq, kvc, cache_ld, M, p, n_heads, score_mult, sink_key, rope_cos, rope_sin, lut4k, out, ldo);
 }
 
 }  // namespace czg

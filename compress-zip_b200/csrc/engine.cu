@@ -77,6 +77,7 @@ struct czg_ctx {
     int8_t *embed = nullptr, *final_norm = nullptr, *head_w = nullptr;
     uint16_t *lut = nullptr;
     uint16_t *lut4k = nullptr;   // exp_q16 by t256 <= 4096 (lut.rs:213-235 unrolled over ip)
+    bool exp0 = false;           // lut4k[0] == 65535: exp of a zero difference needs no special case
     int16_t *rope_cos = nullptr, *rope_sin = nullptr;
     std::vector<LayerDev> layers;
     std::vector<void *> allocs;
@@ -288,6 +289,7 @@ int load_model(czg_ctx *c, const uint8_t *bytes, size_t len) {
             l4[tt] = (uint16_t)std::min(65535u, std::max(1u, o));
         }
         if (!upload(c, &c->lut4k, l4.data(), l4.size() * 2)) return CZG_E_DEVICE;
+        c->exp0 = l4[0] == 65535;
     }
     for (int k = 0; k < 2; k++) {
         const char *nm = k ? "lut.rope_sin" : "lut.rope_cos";
@@ -466,7 +468,7 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
             if (attention_mma_fits(max_len) && !c->scalar_attention)
                 launch_attention_mma(c->qkv, d + 128, c->kv, c->chunk_row0, c->chunk_len, nc, max_len, H,
                                      L.score_mult, L.sink_key, c->rope_cos, c->rope_sin, c->lut4k,
-                                     L.wide_mult, c->attn, d, st);
+                                     L.wide_mult, c->exp0, c->attn, d, st);
             else
                 launch_attention(c->qkv, d + 128, c->kv, c->chunk_row0, c->chunk_len, nc, max_len, H,
                                  L.score_mult, L.sink_key, c->rope_cos, c->rope_sin, c->lut, c->attn, d, st);
@@ -750,7 +752,7 @@ int decompress_impl(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts
                 timed(c, kAttnDecode, [&] {
                     if (split)
                         launch_attention_decode_mma(c->qkv, d + 128, kvc, cache_ld, M, step, H, L.score_mult,
-                                                    L.sink_key, c->rope_cos, c->rope_sin, c->lut4k, L.wide_mult,
+                                                    L.sink_key, c->rope_cos, c->rope_sin, c->lut4k, L.wide_mult, c->exp0,
                                                     c->attn, d, s);
                     else
                         launch_attention_decode(c->qkv, d + 128, kvc, cache_ld, M, step, H, L.score_mult, L.sink_key,
