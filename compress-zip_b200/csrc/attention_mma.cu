@@ -142,7 +142,9 @@ __device__ __forceinline__ void tile_softmax(const int (&sacc)[4][4], int kb, in
             w = exp_attn((int)((uint32_t)sc[i] - (uint32_t)pm), lut4k, c8);
         }
         T.w[i] = valid ? w : 0u;
-        const bool rec = valid && sc[i] > prevmax && prevmax != INT32_MIN;
+        // a record over INT32_MIN rescales nothing; without saturation only the row's
+        // first key can see that (valid keys are a prefix of the row, scores > INT32_MIN)
+        const bool rec = valid && sc[i] > prevmax && (WIDE ? prevmax != INT32_MIN : (i > 0 || base != INT32_MIN));
         T.ef[i] = rec ? (uint32_t)prevmax - (uint32_t)sc[i] : 0u;
         lrec += rec;
         prevmax = pm;
