@@ -41,6 +41,7 @@ constexpr int AM_THREADS = 512;
 constexpr int AM_WARPS = AM_THREADS / 32;
 constexpr int AM_MAX_KEYS = 1024;
 constexpr int AM_ROWS = 8;   // query rows per warp task
+constexpr int AM_LUT = 4104;   // exp table entries (t256 0..4096, padded)
 // per warp: record factors [8][32], records per row [8], output staging [8][64]
 constexpr int AM_WARP_SMEM = AM_ROWS * 32 * 4 + AM_ROWS * 4 + AM_ROWS * 64;
 
@@ -67,12 +68,13 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
 }
 
 // exp_q16 with the attention coefficient via a table indexed by min(t256, 4096)
-// (entry 4096 is 1, the value of every t256 >= 4096, whatever the exp2 LUT holds).
+// (entry 4096 is 1, the value of every t256 >= 4096, whatever the exp2 LUT holds);
+// the kernels keep the table (8 KB) in shared memory.
 // t256 = floor((neg * coef + 2^23) / 2^24) = hi + (lo >= 2^31) of neg * (coef << 8).
 __device__ __forceinline__ uint32_t exp_attn(int diff, const uint16_t *lut4k, uint32_t c8) {
     const uint32_t neg = 0u - (uint32_t)diff;
     const uint32_t t = min(__umulhi(neg, c8) + ((neg * c8) >> 31), 4096u);
-    const uint32_t w = __ldg(lut4k + t);
+    const uint32_t w = lut4k[t];
     return diff >= 0 ? 65535u : w;
 }
 
@@ -137,7 +139,7 @@ __device__ __forceinline__ void tile_softmax(const int (&sacc)[4][4], int kb, in
         uint32_t w;
         if (EXP0) {   // pm >= sc without wrap-around (non-saturating scores) and lut4k[0] == 65535
             const uint32_t neg = (uint32_t)pm - (uint32_t)sc[i];
-            w = __ldg(lut4k + min(__umulhi(neg, c8) + ((neg * c8) >> 31), 4096u));
+            w = lut4k[min(__umulhi(neg, c8) + ((neg * c8) >> 31), 4096u)];
         } else {
             w = exp_attn((int)((uint32_t)sc[i] - (uint32_t)pm), lut4k, c8);
         }
@@ -206,7 +208,9 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
     uint8_t *ks = smem;                              // [npad][64], dims permuted per thread quarter
     uint8_t *vt = ks + npad * 64;                    // [64][vt_ld], keys in order
     uint8_t *wsm = vt + 64 * vt_ld;
-    const uint16_t *lut4k = lut4k_g;   // 8 KB, stays in L1
+    uint16_t *lut_s = reinterpret_cast<uint16_t *>(wsm + AM_WARPS * AM_WARP_SMEM);   // exp table
+    for (int i = threadIdx.x; i < AM_LUT; i += AM_THREADS) lut_s[i] = lut4k_g[i];
+    const uint16_t *lut4k = lut_s;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, t = lane & 3;
     uint32_t *rec_e = reinterpret_cast<uint32_t *>(wsm + warp * AM_WARP_SMEM);   // [8][32]
@@ -436,12 +440,16 @@ __global__ void __launch_bounds__(AM_THREADS, 1)
 k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restrict__ kvc, size_t cache_ld,
                        int M, int p, int n_heads, const int32_t *__restrict__ score_mult,
                        const int8_t *__restrict__ sink_key, const int16_t *__restrict__ rope_cos,
-                       const int16_t *__restrict__ rope_sin, const uint16_t *__restrict__ lut4k,
+                       const int16_t *__restrict__ rope_sin, const uint16_t *__restrict__ lut4k_g,
                        int8_t *__restrict__ out, int ldo) {
     __shared__ __align__(16) uint8_t wsm[AM_WARPS * AM_WARP_SMEM];
-    extern __shared__ __align__(16) uint8_t dsm[];   // per warp: two 4 KB tile stages
+    extern __shared__ __align__(16) uint8_t dsm[];   // per warp: two 4 KB tile stages; then the exp table
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, t = lane & 3;
+    uint16_t *lut_s = reinterpret_cast<uint16_t *>(dsm + AM_WARPS * 8192);
+    for (int i = tid; i < AM_LUT; i += AM_THREADS) lut_s[i] = lut4k_g[i];
+    __syncthreads();
+    const uint16_t *lut4k = lut_s;
     const int r = blockIdx.x * AM_WARPS + warp;
     if (r >= M) return;
     uint8_t *stages = dsm + warp * 8192;
@@ -621,15 +629,15 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__
 size_t attention_mma_smem(int max_len) {
     const int npad = (max_len + 31) & ~31;
     const int vt_ld = ((npad + 127) & ~127) + 32;
-    return (size_t)npad * 64 + (size_t)64 * vt_ld + (size_t)AM_WARPS * AM_WARP_SMEM;
+    return (size_t)npad * 64 + (size_t)64 * vt_ld + (size_t)AM_WARPS * AM_WARP_SMEM + AM_LUT * 2;
 }
 
 bool attention_mma_fits(int max_len) { return max_len <= AM_MAX_KEYS; }
 
 void attention_mma_init() {
-    cudaFuncSetAttribute(k_attention_decode_mma<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, AM_WARPS * 8192);
-    cudaFuncSetAttribute(k_attention_decode_mma<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, AM_WARPS * 8192);
-    cudaFuncSetAttribute(k_attention_decode_mma<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, AM_WARPS * 8192);
+    cudaFuncSetAttribute(k_attention_decode_mma<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, AM_WARPS * 8192 + AM_LUT * 2);
+    cudaFuncSetAttribute(k_attention_decode_mma<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, AM_WARPS * 8192 + AM_LUT * 2);
+    cudaFuncSetAttribute(k_attention_decode_mma<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, AM_WARPS * 8192 + AM_LUT * 2);
     const int smem = (int)attention_mma_smem(AM_MAX_KEYS);
     cudaFuncSetAttribute(k_attention_mma<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     cudaFuncSetAttribute(k_attention_mma<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -666,13 +674,13 @@ void launch_attention_decode_mma(const int8_t *qkv, int ldq, const int8_t *kvc, 
     if (M == 0) return;
     const unsigned grid = (unsigned)((M + AM_WARPS - 1) / AM_WARPS);
     if (wide_mult)
-        k_attention_decode_mma<true, false><<<grid, AM_THREADS, AM_WARPS * 8192, st>>>(
+        k_attention_decode_mma<true, false><<<grid, AM_THREADS, AM_WARPS * 8192 + AM_LUT * 2, st>>>(
             qkv, ldq, kvc, cache_ld, M, p, n_heads, score_mult, sink_key, rope_cos, rope_sin, lut4k, out, ldo);
     else if (exp0)
-        k_attention_decode_mma<false, true><<<grid, AM_THREADS, AM_WARPS * 8192, st>>>(
+        k_attention_decode_mma<false, true><<<grid, AM_THREADS, AM_WARPS * 8192 + AM_LUT * 2, st>>>(
             qkv, ldq, kvc, cache_ld, M, p, n_heads, score_mult, sink_key, rope_cos, rope_sin, lut4k, out, ldo);
     else
-        k_attention_decode_mma<false, false><<<grid, AM_THREADS, AM_WARPS * 8192, st>>>(
+        k_attention_decode_mma<false, false><<<grid, AM_THREADS, AM_WARPS * 8192 + AM_LUT * 2, st>>>(
             qkv, ldq, kvc, cache_ld, M, p, n_heads, score_mult, sink_key, rope_cos, rope_sin, lut4k, out, ldo);
 }
 
