@@ -70,10 +70,10 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
 // exp_q16 with the attention coefficient via a table indexed by min(t256, 4096)
 // (entry 4096 is 1, the value of every t256 >= 4096, whatever the exp2 LUT holds);
 // the kernels keep the table (8 KB) in shared memory.
-// t256 = floor((neg * coef + 2^23) / 2^24) = hi + (lo >= 2^31) of neg * (coef << 8).
+// t256 = floor((neg * coef + 2^23) / 2^24) = the high word of neg * (coef << 8) + 2^31.
 __device__ __forceinline__ uint32_t exp_attn(int diff, const uint16_t *lut4k, uint32_t c8) {
     const uint32_t neg = 0u - (uint32_t)diff;
-    const uint32_t t = min(__umulhi(neg, c8) + ((neg * c8) >> 31), 4096u);
+    const uint32_t t = min((uint32_t)(((unsigned long long)neg * c8 + 0x80000000ull) >> 32), 4096u);
     const uint32_t w = lut4k[t];
     return diff >= 0 ? 65535u : w;
 }
@@ -139,7 +139,7 @@ __device__ __forceinline__ void tile_softmax(const int (&sacc)[4][4], int kb, in
         uint32_t w;
         if (EXP0) {   // pm >= sc without wrap-around (non-saturating scores) and lut4k[0] == 65535
             const uint32_t neg = (uint32_t)pm - (uint32_t)sc[i];
-            w = lut4k[min(__umulhi(neg, c8) + ((neg * c8) >> 31), 4096u)];
+            w = lut4k[min((uint32_t)(((unsigned long long)neg * c8 + 0x80000000ull) >> 32), 4096u)];
         } else {
             w = exp_attn((int)((uint32_t)sc[i] - (uint32_t)pm), lut4k, c8);
         }

@@ -78,7 +78,7 @@ __global__ void k_cdf_lohi(const int32_t *__restrict__ logits, int V, int ld,
 // once (lane l holds elements 128j + 4l + k), the weights e_i are kept packed,
 // and the division by S uses floor_mul_div.  The weight is read from lut4k,
 // exp_q16 tabulated by t256 (entries >= 4096 are 1), with
-// t256 = hi + (lo >= 2^31) of neg * (coef << 8), which needs coef < 2^24.
+// t256 = the high word of neg * (coef << 8) + 2^31, which needs coef < 2^24.
 // FULL: V == 128 * G, so no element is out of range.  One warp per row.
 template <int G, bool FULL>
 __global__ void __launch_bounds__(256) k_cdf_lohi_reg(const int32_t *__restrict__ logits, int V, int ld,
@@ -122,7 +122,7 @@ __global__ void __launch_bounds__(256) k_cdf_lohi_reg(const int32_t *__restrict_
             const int i = 128 * j + 4 * lane + k;
             const int dlt = (int)((uint32_t)x[j][k] - (uint32_t)mx);
             const uint32_t neg = 0u - (uint32_t)dlt;
-            const uint32_t t = min(__umulhi(neg, c8) + ((neg * c8) >> 31), 4096u);
+            const uint32_t t = min((uint32_t)(((unsigned long long)neg * c8 + 0x80000000ull) >> 32), 4096u);
             uint32_t w = __ldg(lut4k + t);
             w = dlt >= 0 ? 65535u : w;
             e[k] = (FULL || i < V) ? w : 0u;

@@ -232,7 +232,7 @@ __global__ void __launch_bounds__(256) k_cdf_decode_reg(
     for (int k = 0; k < E; k++) {
         const int dlt = (int)((uint32_t)x[k] - (uint32_t)mx);
         const uint32_t neg = 0u - (uint32_t)dlt;
-        const uint32_t t = min(__umulhi(neg, c8) + ((neg * c8) >> 31), 4096u);
+        const uint32_t t = min((uint32_t)(((unsigned long long)neg * c8 + 0x80000000ull) >> 32), 4096u);
         const uint32_t w = dlt >= 0 ? 65535u : (uint32_t)__ldg(lut4k + t);
         S += w;
         if (k & 1) ew[k >> 1] |= w << 16;
