@@ -149,19 +149,27 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         : "memory");
 }
 
-// Requantisation parameters.  When clamp_a > 0 the product of an accumulator
-// clamped to [-clamp_a, clamp_a] with mult fits in int32 and every accumulator
-// beyond the clamp saturates to +-127 either way, so the 64-bit product of
-// model.rs:280-300 reduces to 32-bit arithmetic.
+// Requantisation clamp(round_half_even(acc * mult / 2^shift), +-127) of
+// model.rs:280-300 in three forms (mode):
+//  2: |mult| < 2^(shift-1): A = the largest accumulator whose result is <= 127;
+//     clamp(acc, -A, A) * mult fits int32 and lands exactly on +-127 at the clamp
+//     (steps of the result are below 1/2), so no output clamp is needed;
+//  1: clamp(acc, -A, A) with A * |mult| >= 128 * 2^shift (beyond it the result
+//     saturates either way) fits int32; the output is clamped;
+//  0: the 64-bit form.
 struct Requant {
-    int mult, shift, clamp_a, bias;   // bias = 2^(shift-1) - 1
+    int mult, shift, clamp_a, bias, mode;   // bias = 2^(shift-1) - 1
 };
 
-template <bool FAST>
+template <int RQ>
 __device__ __forceinline__ int rq(int acc, const Requant &q) {
-    if (FAST) {
+    if (RQ == 2) {
         const int x = min(max(acc, -q.clamp_a), q.clamp_a) * q.mult;
-        return clamp127((x + q.bias + ((x >> q.shift) & 1)) >> q.shift);   // round half to even
+        return (x + q.bias + ((x >> q.shift) & 1)) >> q.shift;   // round half to even
+    }
+    if (RQ == 1) {
+        const int x = min(max(acc, -q.clamp_a), q.clamp_a) * q.mult;
+        return clamp127((x + q.bias + ((x >> q.shift) & 1)) >> q.shift);
     }
     return requant(acc, q.mult, q.shift);
 }
@@ -178,7 +186,7 @@ struct EpiShape {
     static constexpr int kOutCols = EPI == kEpiInt32 ? 16 : 64;
 };
 
-template <int BN, int STAGES, int EPI, bool FAST>
+template <int BN, int STAGES, int EPI, int RQ>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
           const __grid_constant__ CUtensorMap map_o, int M, int N, int K, Requant rqp, int *__restrict__ err) {
@@ -355,8 +363,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                             uint32_t w[8];
 #pragma unroll
                             for (int j = 0; j < 8; j++)
-                                w[j] = pack4(rq<FAST>((int)v[4 * j], rqp), rq<FAST>((int)v[4 * j + 1], rqp),
-                                             rq<FAST>((int)v[4 * j + 2], rqp), rq<FAST>((int)v[4 * j + 3], rqp));
+                                w[j] = pack4(rq<RQ>((int)v[4 * j], rqp), rq<RQ>((int)v[4 * j + 1], rqp),
+                                             rq<RQ>((int)v[4 * j + 2], rqp), rq<RQ>((int)v[4 * j + 3], rqp));
 #pragma unroll
                             for (int hh = 0; hh < 2; hh++)
                                 *reinterpret_cast<uint4 *>(sb + (((2 * gi + hh) ^ sw) << 4)) =
@@ -365,8 +373,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                             int y[16];
 #pragma unroll
                             for (int j = 0; j < 16; j++) {
-                                const int gte = max(rq<FAST>((int)v[2 * j], rqp), 0);
-                                const int x = gte * rq<FAST>((int)v[2 * j + 1], rqp);   // |x| <= 127 * 127
+                                const int gte = max(rq<RQ>((int)v[2 * j], rqp), 0);
+                                const int x = gte * rq<RQ>((int)v[2 * j + 1], rqp);   // |x| <= 127 * 127
                                 y[j] = (x + 63 + ((x >> 7) & 1)) >> 7;                  // |y| <= 126: no clamp
                             }
                             *reinterpret_cast<uint4 *>(sb + ((gi ^ sw) << 4)) =
@@ -444,13 +452,18 @@ bool make_out_map(CUtensorMap *map, void *base, uint64_t rows, uint64_t cols, ui
 }
 
 Requant make_requant(int mult, int shift) {
-    Requant q{mult, shift, 0, 0};
+    Requant q{mult, shift, 0, 0, 0};
     if (shift >= 1 && shift <= 24 && mult != 0) {
         const long long am = mult < 0 ? -(long long)mult : (long long)mult;
-        const long long a = ((128ll << shift) / am) + 1;   // |a * mult| >= 128 * 2^shift
-        if (a * am + (1ll << (shift - 1)) < (1ll << 31)) {
-            q.clamp_a = (int)a;
-            q.bias = (1 << (shift - 1)) - 1;
+        q.bias = (1 << (shift - 1)) - 1;
+        const long long a2 = ((255ll << (shift - 1)) + am - 1) / am - 1;   // largest a with a*|mult| < 127.5 * 2^shift
+        const long long a1 = ((128ll << shift) / am) + 1;                 // |a * mult| >= 128 * 2^shift
+        if (am < (1ll << (shift - 1)) && a2 * am + (1ll << (shift - 1)) < (1ll << 31)) {
+            q.clamp_a = (int)a2;
+            q.mode = 2;
+        } else if (a1 * am + (1ll << (shift - 1)) < (1ll << 31)) {
+            q.clamp_a = (int)a1;
+            q.mode = 1;
         }
     }
     return q;
@@ -468,20 +481,23 @@ bool launch_tc(const TcMatrix &A, const TcMatrix &B, int M, int N, int K, int mu
     const Requant q = make_requant(mult, shift);
     const CUtensorMap &ma = *reinterpret_cast<const CUtensorMap *>(A.map);
     const CUtensorMap &mb = *reinterpret_cast<const CUtensorMap *>(B.map);
-    if (q.clamp_a > 0 || EPI == kEpiInt32)
-        k_gemm_tc<BN, TcCfg<BN>::kStages, EPI, true><<<grid, TC_THREADS, TcCfg<BN>::kSmem, st>>>(ma, mb, omap, M, N, K,
-                                                                                                q, err);
+    constexpr int S = TcCfg<BN>::kStages;
+    if (EPI == kEpiInt32 || q.mode == 2)
+        k_gemm_tc<BN, S, EPI, 2><<<grid, TC_THREADS, TcCfg<BN>::kSmem, st>>>(ma, mb, omap, M, N, K, q, err);
+    else if (q.mode == 1)
+        k_gemm_tc<BN, S, EPI, 1><<<grid, TC_THREADS, TcCfg<BN>::kSmem, st>>>(ma, mb, omap, M, N, K, q, err);
     else
-        k_gemm_tc<BN, TcCfg<BN>::kStages, EPI, false><<<grid, TC_THREADS, TcCfg<BN>::kSmem, st>>>(ma, mb, omap, M, N,
-                                                                                                 K, q, err);
+        k_gemm_tc<BN, S, EPI, 0><<<grid, TC_THREADS, TcCfg<BN>::kSmem, st>>>(ma, mb, omap, M, N, K, q, err);
     return true;
 }
 
 template <int BN, int EPI>
 void set_attr_epi() {
-    cudaFuncSetAttribute(k_gemm_tc<BN, TcCfg<BN>::kStages, EPI, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(k_gemm_tc<BN, TcCfg<BN>::kStages, EPI, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)TcCfg<BN>::kSmem);
-    cudaFuncSetAttribute(k_gemm_tc<BN, TcCfg<BN>::kStages, EPI, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(k_gemm_tc<BN, TcCfg<BN>::kStages, EPI, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)TcCfg<BN>::kSmem);
+    cudaFuncSetAttribute(k_gemm_tc<BN, TcCfg<BN>::kStages, EPI, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)TcCfg<BN>::kSmem);
 }
 

@@ -251,3 +251,30 @@ def test_config4_long_chunk(tmp_path, shipped_path, oracle_mod):
         assert np.array_equal(eng.decompress_chunks(got, np.array([len(toks)], np.uint32)), toks)
     finally:
         eng.close()
+
+
+@pytest.mark.parametrize("proj,mult,shift", [
+    ("ffn.up", 819, 10),          # |mult| >= 2^(shift-1): clamped 32-bit requantisation
+    ("ffn.down", 1 << 28, 30),    # product beyond 32 bits: 64-bit requantisation
+    ("attn.qkv", -3000, 16),      # negative multiplier
+])
+def test_requant_forms(shipped_path, tmp_path, oracle_mod, shipped_tokens, proj, mult, shift):
+    """Each requantisation form of the GEMM epilogue against the oracle."""
+    from compress_zip_b200 import czm
+    from compress_zip_b200.engine import Engine
+
+    mf = czm.ModelFile.load(shipped_path)
+    t = {k: np.array(v) for k, v in mf.tensors.items()}
+    t[f"layers.0.{proj}.mult"] = np.asarray(mult, np.int32)
+    t[f"layers.0.{proj}.shift"] = np.asarray(shift, np.int8)
+    p = tmp_path / "rq.czm"
+    p.write_bytes(czm.write_safetensors(t, mf.metadata))
+    om = oracle_mod.load_model(str(p))
+    eng = Engine.from_file(str(p), 0)
+    try:
+        _trace_equal(eng, om, oracle_mod, shipped_tokens[:300])
+        toks = shipped_tokens[:1100]
+        starts = _starts(len(toks), 512)
+        assert eng.compress_chunks(toks, starts) == oracle_mod.compress_chunks(om, toks, starts)
+    finally:
+        eng.close()
