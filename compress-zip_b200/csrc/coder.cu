@@ -79,8 +79,10 @@ __global__ void k_cdf_lohi(const int32_t *__restrict__ logits, int V, int ld,
 // and the division by S uses floor_mul_div.  The weight is read from lut4k,
 // exp_q16 tabulated by t256 (entries >= 4096 are 1), with
 // t256 = the high word of neg * (coef << 8) + 2^31, which needs coef < 2^24.
-// FULL: V == 128 * G, so no element is out of range.  One warp per row.
-template <int G, bool FULL>
+// FULL: V == 128 * G, so no element is out of range.  EXP0: lut4k[0] == 65535 and
+// |logit| < 2^30 (no wrap in logit - max), so a zero difference needs no special
+// case.  One warp per row.
+template <int G, bool FULL, bool EXP0>
 __global__ void __launch_bounds__(256) k_cdf_lohi_reg(const int32_t *__restrict__ logits, int V, int ld,
                                                       const uint32_t *__restrict__ sym,
                                                       const uint16_t *__restrict__ lut4k, uint32_t c8,
@@ -124,7 +126,7 @@ __global__ void __launch_bounds__(256) k_cdf_lohi_reg(const int32_t *__restrict_
             const uint32_t neg = 0u - (uint32_t)dlt;
             const uint32_t t = min((uint32_t)(((unsigned long long)neg * c8 + 0x80000000ull) >> 32), 4096u);
             uint32_t w = __ldg(lut4k + t);
-            w = dlt >= 0 ? 65535u : w;
+            if (!EXP0) w = dlt >= 0 ? 65535u : w;
             e[k] = (FULL || i < V) ? w : 0u;
             S += e[k];
         }
@@ -136,7 +138,7 @@ __global__ void __launch_bounds__(256) k_cdf_lohi_reg(const int32_t *__restrict_
     const uint32_t R = total - (uint32_t)V;
     const uint32_t a = R / S, b = R % S;
     const float bs = __fdiv_rn((float)b, (float)S);
-    uint32_t f_all = 0, f_below = 0, f_sym = 0;
+    uint32_t f_all = 0, f_below = 0;
 #pragma unroll
     for (int j = 0; j < G; j++)
 #pragma unroll
@@ -147,13 +149,18 @@ __global__ void __launch_bounds__(256) k_cdf_lohi_reg(const int32_t *__restrict_
             if (!FULL) f = i < V ? f : 0u;
             f_all += f;
             f_below += (i < sy) ? f : 0u;
-            f_sym = (i == sy) ? f : f_sym;
         }
+    // the symbol's own frequency, from the lane that holds it
+    uint32_t esel = 0;
+#pragma unroll
+    for (int j = 0; j < G; j++)
+        if (j == (sy >> 7)) esel = (sy & 2) ? ew[j][1] : ew[j][0];
+    uint32_t f_sym = 1u + floor_mul_div((esel >> (16 * (sy & 1))) & 0xFFFFu, a, b, S, bs);
+    f_sym = __shfl_sync(0xffffffffu, f_sym, (sy >> 2) & 31);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         f_all += __shfl_xor_sync(0xffffffffu, f_all, o);
         f_below += __shfl_xor_sync(0xffffffffu, f_below, o);
-        f_sym += __shfl_xor_sync(0xffffffffu, f_sym, o);
     }
     if (lane == 0) {
         const uint32_t rem = total - f_all;   // goes to the argmax (softmax_cdf.rs:125-127)
@@ -164,10 +171,11 @@ __global__ void __launch_bounds__(256) k_cdf_lohi_reg(const int32_t *__restrict_
 }
 
 template <int G>
-void cdf_reg(bool full, const int32_t *logits, int V, int ld, const uint32_t *sym, const uint16_t *lut4k, uint32_t c8,
-             uint32_t total, int M, uint2 *lohi, unsigned grid, cudaStream_t st) {
-    if (full) k_cdf_lohi_reg<G, true><<<grid, 256, 0, st>>>(logits, V, ld, sym, lut4k, c8, total, M, lohi);
-    else k_cdf_lohi_reg<G, false><<<grid, 256, 0, st>>>(logits, V, ld, sym, lut4k, c8, total, M, lohi);
+void cdf_reg(bool full, bool exp0, const int32_t *logits, int V, int ld, const uint32_t *sym, const uint16_t *lut4k,
+             uint32_t c8, uint32_t total, int M, uint2 *lohi, unsigned grid, cudaStream_t st) {
+    if (full && exp0) k_cdf_lohi_reg<G, true, true><<<grid, 256, 0, st>>>(logits, V, ld, sym, lut4k, c8, total, M, lohi);
+    else if (full) k_cdf_lohi_reg<G, true, false><<<grid, 256, 0, st>>>(logits, V, ld, sym, lut4k, c8, total, M, lohi);
+    else k_cdf_lohi_reg<G, false, false><<<grid, 256, 0, st>>>(logits, V, ld, sym, lut4k, c8, total, M, lohi);
 }
 
 struct BitSink {
@@ -288,7 +296,8 @@ __global__ void k_pack(const uint8_t *__restrict__ slots, const uint64_t *__rest
 }  // namespace
 
 void launch_cdf_lohi(const int32_t *logits, int V, int ld, const uint32_t *sym, const uint16_t *lut,
-                     const uint16_t *lut4k, uint32_t coef, uint32_t total, int M, uint2 *lohi, cudaStream_t st) {
+                     const uint16_t *lut4k, bool exp0, uint32_t coef, uint32_t total, int M, uint2 *lohi,
+                     cudaStream_t st) {
     if (M == 0) return;
     const unsigned grid = (unsigned)((M + 7) / 8);
     // 16-byte row loads need ld % 4 == 0; the weight bound needs V <= 1024; the table index coef < 2^24
@@ -296,14 +305,14 @@ void launch_cdf_lohi(const int32_t *logits, int V, int ld, const uint32_t *sym, 
         const bool full = V % 128 == 0;
         const uint32_t c8 = coef << 8;
         switch ((V + 127) / 128) {
-            case 8: cdf_reg<8>(full, logits, V, ld, sym, lut4k, c8, total, M, lohi, grid, st); return;
-            case 7: cdf_reg<7>(full, logits, V, ld, sym, lut4k, c8, total, M, lohi, grid, st); return;
-            case 6: cdf_reg<6>(full, logits, V, ld, sym, lut4k, c8, total, M, lohi, grid, st); return;
-            case 5: cdf_reg<5>(full, logits, V, ld, sym, lut4k, c8, total, M, lohi, grid, st); return;
-            case 4: cdf_reg<4>(full, logits, V, ld, sym, lut4k, c8, total, M, lohi, grid, st); return;
-            case 3: cdf_reg<3>(full, logits, V, ld, sym, lut4k, c8, total, M, lohi, grid, st); return;
-            case 2: cdf_reg<2>(full, logits, V, ld, sym, lut4k, c8, total, M, lohi, grid, st); return;
-            default: cdf_reg<1>(full, logits, V, ld, sym, lut4k, c8, total, M, lohi, grid, st); return;
+            case 8: cdf_reg<8>(full, exp0, logits, V, ld, sym, lut4k, c8, total, M, lohi, grid, st); return;
+            case 7: cdf_reg<7>(full, exp0, logits, V, ld, sym, lut4k, c8, total, M, lohi, grid, st); return;
+            case 6: cdf_reg<6>(full, exp0, logits, V, ld, sym, lut4k, c8, total, M, lohi, grid, st); return;
+            case 5: cdf_reg<5>(full, exp0, logits, V, ld, sym, lut4k, c8, total, M, lohi, grid, st); return;
+            case 4: cdf_reg<4>(full, exp0, logits, V, ld, sym, lut4k, c8, total, M, lohi, grid, st); return;
+            case 3: cdf_reg<3>(full, exp0, logits, V, ld, sym, lut4k, c8, total, M, lohi, grid, st); return;
+            case 2: cdf_reg<2>(full, exp0, logits, V, ld, sym, lut4k, c8, total, M, lohi, grid, st); return;
+            default: cdf_reg<1>(full, exp0, logits, V, ld, sym, lut4k, c8, total, M, lohi, grid, st); return;
         }
     }
     k_cdf_lohi<<<grid, 256, 0, st>>>(logits, V, ld, sym, lut, coef, total, M, lohi);

@@ -78,6 +78,7 @@ struct czg_ctx {
     uint16_t *lut = nullptr;
     uint16_t *lut4k = nullptr;   // exp_q16 by t256 <= 4096 (lut.rs:213-235 unrolled over ip)
     bool exp0 = false;           // lut4k[0] == 65535: exp of a zero difference needs no special case
+    bool logit_small = false;    // every |logit| < 2^30: no logit difference wraps
     int16_t *rope_cos = nullptr, *rope_sin = nullptr;
     std::vector<LayerDev> layers;
     std::vector<void *> allocs;
@@ -315,6 +316,7 @@ int load_model(czg_ctx *c, const uint8_t *bytes, size_t len) {
         return fail(c, CZG_E_UNSUPPORTED, "softmax.target_total must lie in (vocab_size, 2^30)");
 
     c->layers.resize(m.n_layers);
+    c->logit_small = (long long)d * 127 * 128 < (1ll << 30);   // |logit| <= d * 127 * 128
     c->res16 = m.n_layers <= 128 && getenv("CZG_RESIDUAL32") == nullptr;
     for (int i = 0; i < m.n_layers; i++) {
         LayerDev &L = c->layers[i];
@@ -505,7 +507,7 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
         cudaMemcpy2DAsync(tr->logits, (size_t)V * 4, c->logits, (size_t)c->vpad * 4, (size_t)V * 4, M,
                           cudaMemcpyDeviceToHost, st);
     timed(c, kCdf, [&] {
-        launch_cdf_lohi(c->logits, V, c->vpad, c->tok_out, c->lut, c->lut4k, m.coef_q24, m.target_total, M,
+        launch_cdf_lohi(c->logits, V, c->vpad, c->tok_out, c->lut, c->lut4k, c->exp0 && c->logit_small, m.coef_q24, m.target_total, M,
                         c->lohi, st);
     });
     if (tr && tr->lohi)

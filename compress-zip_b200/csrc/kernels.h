@@ -97,8 +97,10 @@ void launch_attention_decode(const int8_t *qkv, int ldq, const int8_t *kvc, size
                              int8_t *out, int ldo, cudaStream_t st);
 
 // coder.cu
+// exp0: lut4k[0] == 65535 and |logit| < 2^30 (see k_cdf_lohi_reg)
 void launch_cdf_lohi(const int32_t *logits, int V, int ld, const uint32_t *sym, const uint16_t *lut,
-                     const uint16_t *lut4k, uint32_t coef, uint32_t total, int M, uint2 *lohi, cudaStream_t st);
+                     const uint16_t *lut4k, bool exp0, uint32_t coef, uint32_t total, int M, uint2 *lohi,
+                     cudaStream_t st);
 void launch_encode(const uint2 *lohi, const int *chunk_row0, const int *chunk_len, int n_chunks,
                    uint32_t total, uint8_t *slots, const uint64_t *slot_off, uint32_t *lens,
                    int *err, cudaStream_t st);
