@@ -197,7 +197,7 @@ __global__ void k_cdf_decode(const int32_t *__restrict__ logits, int V, int ld, 
 // floor_mul_div.  The interval search is done by the whole warp: the owner
 // lane's weights go through shared memory, one element per lane, and an
 // inclusive scan gives the cumulative frequencies.
-template <int E>
+template <int E, bool EXP0>
 __global__ void __launch_bounds__(256) k_cdf_decode_reg(
     const int32_t *__restrict__ logits, int ld, const uint16_t *__restrict__ lut4k, uint32_t c8, uint32_t total,
     unsigned long long inv_total, int M, DecState *__restrict__ st, const uint8_t *__restrict__ data,
@@ -233,7 +233,7 @@ __global__ void __launch_bounds__(256) k_cdf_decode_reg(
         const int dlt = (int)((uint32_t)x[k] - (uint32_t)mx);
         const uint32_t neg = 0u - (uint32_t)dlt;
         const uint32_t t = min((uint32_t)(((unsigned long long)neg * c8 + 0x80000000ull) >> 32), 4096u);
-        const uint32_t w = dlt >= 0 ? 65535u : (uint32_t)__ldg(lut4k + t);
+        const uint32_t w = (EXP0 || dlt < 0) ? (uint32_t)__ldg(lut4k + t) : 65535u;   // EXP0: lut4k[0] == 65535
         S += w;
         if (k & 1) ew[k >> 1] |= w << 16;
         else ew[k >> 1] = w;
@@ -340,7 +340,7 @@ void launch_kv_append(const int8_t *qkv, int ldq, int d, int pos, const int16_t 
                                                                        kvc, cache_ld, split);
 }
 
-void launch_cdf_decode(const int32_t *logits, int V, int ld, const uint16_t *lut, const uint16_t *lut4k,
+void launch_cdf_decode(const int32_t *logits, int V, int ld, const uint16_t *lut, const uint16_t *lut4k, bool exp0,
                        uint32_t coef, uint32_t total, int M, DecState *st, const uint8_t *data,
                        const uint64_t *data_off, const uint64_t *data_len, const uint64_t *tok_off, int step,
                        uint32_t *out_tok, uint32_t *tok_in, cudaStream_t stream) {
@@ -349,15 +349,21 @@ void launch_cdf_decode(const int32_t *logits, int V, int ld, const uint16_t *lut
     const unsigned grid = (unsigned)((M + 7) / 8);
     if (coef < (1u << 24) && ld % 4 == 0 && (V == 1024 || V == 512 || V == 256)) {
         const uint32_t c8 = coef << 8;
-        if (V == 1024)
-            k_cdf_decode_reg<32><<<grid, 256, 0, stream>>>(logits, ld, lut4k, c8, total, inv, M, st, data, data_off,
-                                                           data_len, tok_off, step, out_tok, tok_in);
-        else if (V == 512)
-            k_cdf_decode_reg<16><<<grid, 256, 0, stream>>>(logits, ld, lut4k, c8, total, inv, M, st, data, data_off,
-                                                           data_len, tok_off, step, out_tok, tok_in);
-        else
-            k_cdf_decode_reg<8><<<grid, 256, 0, stream>>>(logits, ld, lut4k, c8, total, inv, M, st, data, data_off,
-                                                          data_len, tok_off, step, out_tok, tok_in);
+#define CZG_CDF_DEC(EE)                                                                                       \
+    do {                                                                                                       \
+        if (exp0)                                                                                              \
+            k_cdf_decode_reg<EE, true><<<grid, 256, 0, stream>>>(logits, ld, lut4k, c8, total, inv, M, st, data,   \
+                                                                 data_off, data_len, tok_off, step, out_tok,  \
+                                                                 tok_in);                                      \
+        else                                                                                                   \
+            k_cdf_decode_reg<EE, false><<<grid, 256, 0, stream>>>(logits, ld, lut4k, c8, total, inv, M, st, data,  \
+                                                                  data_off, data_len, tok_off, step, out_tok, \
+                                                                  tok_in);                                     \
+    } while (0)
+        if (V == 1024) CZG_CDF_DEC(32);
+        else if (V == 512) CZG_CDF_DEC(16);
+        else CZG_CDF_DEC(8);
+#undef CZG_CDF_DEC
         return;
     }
     k_cdf_decode<<<grid, 256, 0, stream>>>(logits, V, ld, lut, coef, total, inv, M, st, data, data_off,

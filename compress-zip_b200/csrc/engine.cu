@@ -784,7 +784,7 @@ int decompress_impl(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts
                 gemm(c, c->tm_xn, c->tm_head, c->xn, c->head_w, M, c->vpad, d, kEpiInt32, 1, 0, c->logits, c->vpad);
             });
             timed(c, kCdfDecode, [&] {
-                launch_cdf_decode(c->logits, V, c->vpad, c->lut, c->lut4k, m.coef_q24, m.target_total, M, c->dstate, c->ddata,
+                launch_cdf_decode(c->logits, V, c->vpad, c->lut, c->lut4k, c->exp0 && c->logit_small, m.coef_q24, m.target_total, M, c->dstate, c->ddata,
                                   c->d_off, c->d_len, c->d_tokoff, step, c->d_outtok, c->tok_in, s);
             });
             if (c->ev_used > 4096) {   // keep the event pool bounded on long chunks

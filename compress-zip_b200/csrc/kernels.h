@@ -87,7 +87,7 @@ void launch_dec_init(const uint8_t *data, const uint64_t *data_off, const uint64
 // split: the tensor-core decode layout (K with permuted dims, V in 32-key tiles), see decode.cu
 void launch_kv_append(const int8_t *qkv, int ldq, int d, int pos, const int16_t *rope_cos,
                       const int16_t *rope_sin, int M, int8_t *kvc, size_t cache_ld, bool split, cudaStream_t stream);
-void launch_cdf_decode(const int32_t *logits, int V, int ld, const uint16_t *lut, const uint16_t *lut4k,
+void launch_cdf_decode(const int32_t *logits, int V, int ld, const uint16_t *lut, const uint16_t *lut4k, bool exp0,
                        uint32_t coef, uint32_t total, int M, DecState *st, const uint8_t *data,
                        const uint64_t *data_off, const uint64_t *data_len, const uint64_t *tok_off, int step,
                        uint32_t *out_tok, uint32_t *tok_in, cudaStream_t stream);
