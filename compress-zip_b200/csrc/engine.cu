@@ -77,6 +77,7 @@ struct czg_ctx {
     int8_t *embed = nullptr, *final_norm = nullptr, *head_w = nullptr;
     uint16_t *lut = nullptr;
     uint16_t *lut4k = nullptr;   // exp_q16 by t256 <= 4096 (lut.rs:213-235 unrolled over ip)
+    bool kernel_timing = false;   // CUDA events around every kernel (czg_set_kernel_timing, CZG_KERNEL_TIMING=1)
     bool exp0 = false;           // lut4k[0] == 65535: exp of a zero difference needs no special case
     bool logit_small = false;    // every |logit| < 2^30: no logit difference wraps
     int16_t *rope_cos = nullptr, *rope_sin = nullptr;
@@ -164,11 +165,15 @@ EvPair &next_ev(czg_ctx *c, int cls) {
 
 template <class F>
 void timed(czg_ctx *c, int cls, F &&f) {
+    c->stats.launches[cls]++;
+    if (!c->kernel_timing) {
+        f();
+        return;
+    }
     EvPair &e = next_ev(c, cls);
     cudaEventRecord(e.a, c->stream);
     f();
     cudaEventRecord(e.b, c->stream);
-    c->stats.launches[cls]++;
 }
 
 // Accumulate the recorded event pairs (class -1 = H2D copy, -2 = D2H copy).
@@ -836,6 +841,7 @@ int czg_ctx_create(int device, const uint8_t *czm, size_t czm_len, czg_ctx **out
     c->stream = c->own_stream;
     if (!st) st = load_model(c, czm, czm_len);
     c->scalar_attention = getenv("CZG_SCALAR_ATTENTION") && atoi(getenv("CZG_SCALAR_ATTENTION")) != 0;
+    c->kernel_timing = getenv("CZG_KERNEL_TIMING") && atoi(getenv("CZG_KERNEL_TIMING")) != 0;
     int wave = 1 << 20;
     if (const char *e = getenv("CZG_WAVE_TOKENS")) wave = std::max(4096, atoi(e));
     if (!st) st = alloc_workspace(c, wave, std::max(1024, wave / 16));
@@ -900,6 +906,12 @@ int czg_set_stream(czg_ctx *c, void *stream) {
     if (!cuda_ok(c, cudaSetDevice(c->device), "cudaSetDevice")) return CZG_E_DEVICE;
     if (!cuda_ok(c, cudaStreamSynchronize(c->stream), "cudaStreamSynchronize")) return CZG_E_DEVICE;
     c->stream = stream ? static_cast<cudaStream_t>(stream) : c->own_stream;
+    return CZG_OK;
+}
+
+int czg_set_kernel_timing(czg_ctx *c, int on) {
+    if (!c) return CZG_E_ARG;
+    c->kernel_timing = on != 0;
     return CZG_OK;
 }
 

@@ -23,7 +23,7 @@ MAX_KERNEL_CLASSES = 16
 EXPORTS = ["czg_ctx_create", "czg_ctx_destroy", "czg_last_error", "czg_model_info_get",
            "czg_compress_bound", "czg_compress_chunks", "czg_compress_chunks_device",
            "czg_decompress_chunks", "czg_last_stats", "czg_kernel_name", "czg_debug_trace",
-           "czg_set_stream", "czg_encode_intervals_static"]
+           "czg_set_stream", "czg_encode_intervals_static", "czg_set_kernel_timing"]
 
 
 class CzgError(RuntimeError):
@@ -79,6 +79,8 @@ def lib() -> C.CDLL:
         L.czg_debug_trace.restype = C.c_int
         L.czg_set_stream.argtypes = [P, P]
         L.czg_set_stream.restype = C.c_int
+        L.czg_set_kernel_timing.argtypes = [P, C.c_int]
+        L.czg_set_kernel_timing.restype = C.c_int
         L.czg_encode_intervals_static.argtypes = [P, P, C.c_uint32, C.c_uint64, C.c_uint32, P,
                                                    C.c_uint64, P, C.POINTER(C.c_uint64), P]
         L.czg_encode_intervals_static.restype = C.c_int
@@ -179,6 +181,10 @@ class Engine:
     def set_stream(self, stream_handle: int | None) -> None:
         """Run subsequent work on a caller's cudaStream_t (None: the own stream)."""
         self._check(lib().czg_set_stream(self._h, C.c_void_p(stream_handle or 0)))
+
+    def set_kernel_timing(self, on: bool) -> None:
+        """Time every kernel with CUDA events (last_stats()['kernels']); off by default."""
+        self._check(lib().czg_set_kernel_timing(self._h, int(bool(on))))
 
     # ---- diagnostics -----------------------------------------------------------
     def last_stats(self) -> dict:
