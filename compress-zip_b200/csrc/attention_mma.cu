@@ -31,6 +31,9 @@
 // the accumulator layout (row 2t+e of thread (g, t)), each row folded by the 8
 // threads that hold it.  A record whose previous maximum is still INT32_MIN
 // rescales nothing (attention.rs:248-250) and is no segment boundary.
+// Record bookkeeping per tile: each thread's 8-bit record mask, the row's 32-bit
+// mask (one bit per key), the records' (previous max - score) stored by key in
+// shared memory; a folding thread walks its rows' masks lowest bit first.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -42,11 +45,11 @@ constexpr int AM_WARPS = AM_THREADS / 32;
 constexpr int AM_MAX_KEYS = 1024;
 constexpr int AM_ROWS = 8;   // query rows per warp task
 constexpr int AM_LUT = 4104;   // exp table entries (t256 0..4096, padded)
-// per warp: record factors [8][32], records per row [8], output staging [8][64]
-constexpr int AM_WARP_SMEM = AM_ROWS * 32 * 4 + AM_ROWS * 4 + AM_ROWS * 64;
+// per warp: record differences by key [8][32], output staging [8][64]
+constexpr int AM_WARP_SMEM = AM_ROWS * 32 * 4 + AM_ROWS * 64;
 
 __device__ __forceinline__ void mma_s8s8(int (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};\n"
         : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
@@ -54,7 +57,7 @@ __device__ __forceinline__ void mma_s8s8(int (&c)[4], const uint32_t (&a)[4], ui
 }
 
 __device__ __forceinline__ void mma_s8u8(int (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};\n"
         : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
@@ -78,6 +81,12 @@ __device__ __forceinline__ uint32_t exp_attn(int diff, const uint16_t *lut4k, ui
     return diff >= 0 ? 65535u : w;
 }
 
+// exp_attn of a record's (previous max - score) < 0
+__device__ __forceinline__ uint32_t exp_rec(int diff, const uint16_t *lut4k, uint32_t c8) {
+    const uint32_t neg = 0u - (uint32_t)diff;
+    return lut4k[min((uint32_t)(((unsigned long long)neg * c8 + 0x80000000ull) >> 32), 4096u)];
+}
+
 // score = round_even(round_even(dot / 4) * mult / 2^15) saturated to int32
 // (attention.rs:236-245).  round_even(x / 2^s) = (x + 2^(s-1) - 1 + ((x >> s) & 1)) >> s.
 template <bool WIDE>
@@ -89,6 +98,29 @@ __device__ __forceinline__ int score_from_dot(int dot, int mult) {
         s = s < -2147483648ll ? -2147483648ll : (s > 2147483647ll ? 2147483647ll : s);
     }
     return (int)s;
+}
+
+// The same for |mult| < 2^27 with one 64-bit product: X = (du << 13) * (mult << 4) + 2^31
+// = 2^17 * (du * mult + 2^14), so the high word of X is floor((du * mult + 2^14) / 2^15),
+// the round-half-up quotient, and the low word is zero exactly on a tie, where
+// round-half-even takes the even one of the two candidates.  |du| <= 64*127^2/4 < 2^18
+// keeps du << 13 inside int32; the score stays inside +-2^30.
+__device__ __forceinline__ int score_fast(int dot, int mult16) {
+    const int du = (dot + 1 + ((dot >> 2) & 1)) >> 2;
+    const long long X = (long long)(du * 8192) * (long long)mult16 + 0x80000000ll;
+    const int hi = (int)(X >> 32);
+    return (uint32_t)X == 0u ? (hi & ~1) : hi;
+}
+
+// One rescale of a state value by a record's factor e (attention.rs:252-259):
+// R(x) = (x*e + 2^15) >> 16 for x >= 0, (x*e - 2^15) >> 16 for x < 0
+//      = floor((x*e + 2^15) / 2^16) - [x < 0].
+// With e16 = e << 16 and x taken as unsigned (x + 2^32 when negative), the high word
+// of x*e16 + 2^31 is floor((x*e + 2^15) / 2^16) + [x < 0]*e16, so
+// R(x) = hi - [x < 0]*(e16 + 1) (mod 2^32).
+__device__ __forceinline__ uint32_t rescale_rec(uint32_t x, uint32_t e16, uint32_t e16p1) {
+    const uint32_t h = (uint32_t)(((unsigned long long)x * e16 + 0x80000000ull) >> 32);
+    return h + (uint32_t)((int)x >> 31) * e16p1;
 }
 
 // key (within a 32-key tile) of QK accumulator column n = 8j + c: accumulator
@@ -103,86 +135,112 @@ __device__ __forceinline__ int perm_key(int n) {
 struct Tile {
     uint32_t w[8];    // weights of the row's 8 entries (keys kb + 8t + i)
     uint32_t ef[8];   // 0, or (previous max - score) of a record (never 0)
-    int lrec;         // records among this thread's entries
-    int nrec;         // records of the row in this tile (quad total)
+    uint32_t rm;      // records among this thread's entries (bit i = entry i)
+    uint32_t rowmask; // records of the row in this tile (bit k = key kb + k)
 };
 
 // Scores, prefix max, records and weights of row g in one 32-key tile.
 template <bool MASKED, bool WIDE, bool EXP0>
 __device__ __forceinline__ void tile_softmax(const int (&sacc)[4][4], int kb, int prow, int n, int mult, int t,
                                              int &m, const uint16_t *lut4k, uint32_t c8, Tile &T) {
-    int sc[8], L[8];
+    int sc[8];
+    uint32_t rm = 0;
+    if constexpr (!WIDE) {
+        // |scores| < 2^30, so every difference below fits int32.  The running max is
+        // chained from the quad prefix; a record is an entry whose score beats it.
+        const int mult16 = mult * 16;
 #pragma unroll
-    for (int i = 0; i < 8; i++) {
-        bool valid = true;
-        if (MASKED) valid = kb + 8 * t + i <= prow && prow < n;
-        sc[i] = valid ? score_from_dot<WIDE>(sacc[i >> 1][i & 1], mult) : INT32_MIN;
-        L[i] = i ? max(L[i - 1], sc[i]) : sc[i];
-    }
-    // exclusive prefix max over the quad: three independent shuffles
-    const int x = L[7];
-    const int y1 = __shfl_up_sync(0xffffffffu, x, 1, 4);
-    const int y2 = __shfl_up_sync(0xffffffffu, x, 2, 4);
-    const int y3 = __shfl_up_sync(0xffffffffu, x, 3, 4);
-    const int z1 = max(x, __shfl_xor_sync(0xffffffffu, x, 1));
-    const int run = m;
-    int base = run;
-    if (t >= 1) base = max(base, y1);
-    if (t >= 2) base = max(base, y2);
-    if (t >= 3) base = max(base, y3);
-    int prevmax = base, lrec = 0;
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-        bool valid = true;
-        if (MASKED) valid = kb + 8 * t + i <= prow && prow < n;
-        const int pm = max(base, L[i]);
-        uint32_t w;
-        if (EXP0) {   // pm >= sc without wrap-around (non-saturating scores) and lut4k[0] == 65535
-            const uint32_t neg = (uint32_t)pm - (uint32_t)sc[i];
-            w = lut4k[min((uint32_t)(((unsigned long long)neg * c8 + 0x80000000ull) >> 32), 4096u)];
-        } else {
-            w = exp_attn((int)((uint32_t)sc[i] - (uint32_t)pm), lut4k, c8);
+        for (int i = 0; i < 8; i++) {
+            bool valid = true;
+            if (MASKED) valid = kb + 8 * t + i <= prow && prow < n;
+            sc[i] = valid ? score_fast(sacc[i >> 1][i & 1], mult16) : INT32_MIN;
         }
-        T.w[i] = valid ? w : 0u;
-        // a record over INT32_MIN rescales nothing; without saturation only the row's
-        // first key can see that (valid keys are a prefix of the row, scores > INT32_MIN)
-        const bool rec = valid && sc[i] > prevmax && (WIDE ? prevmax != INT32_MIN : (i > 0 || base != INT32_MIN));
-        T.ef[i] = rec ? (uint32_t)prevmax - (uint32_t)sc[i] : 0u;
-        lrec += rec;
-        prevmax = pm;
+        const int x = max(max(max(sc[0], sc[1]), max(sc[2], sc[3])), max(max(sc[4], sc[5]), max(sc[6], sc[7])));
+        const int y1 = __shfl_up_sync(0xffffffffu, x, 1, 4);
+        const int y2 = __shfl_up_sync(0xffffffffu, x, 2, 4);
+        const int y3 = __shfl_up_sync(0xffffffffu, x, 3, 4);
+        const int z1 = max(x, __shfl_xor_sync(0xffffffffu, x, 1));
+        const int run = m;
+        int pm = run;
+        if (t >= 1) pm = max(pm, y1);
+        if (t >= 2) pm = max(pm, y2);
+        if (t >= 3) pm = max(pm, y3);
+        // nothing before it: the row's first key, whose record over INT32_MIN rescales nothing
+        if (pm == INT32_MIN) pm = sc[0];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            bool valid = true;
+            if (MASKED) valid = kb + 8 * t + i <= prow && prow < n;
+            int ef = min(pm - sc[i], 0);
+            if (MASKED) ef = valid ? ef : 0;
+            pm = max(pm, sc[i]);
+            const uint32_t neg = (uint32_t)pm - (uint32_t)sc[i];
+            uint32_t w = lut4k[min((uint32_t)(((unsigned long long)neg * c8 + 0x80000000ull) >> 32), 4096u)];
+            if (!EXP0) w = neg == 0u ? 65535u : w;
+            T.w[i] = valid ? w : 0u;
+            T.ef[i] = (uint32_t)ef;
+            rm |= ((uint32_t)ef >> (31 - i)) & (1u << i);
+        }
+        m = max(run, max(z1, __shfl_xor_sync(0xffffffffu, z1, 2)));
+    } else {
+        int L[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            bool valid = true;
+            if (MASKED) valid = kb + 8 * t + i <= prow && prow < n;
+            sc[i] = valid ? score_from_dot<true>(sacc[i >> 1][i & 1], mult) : INT32_MIN;
+            L[i] = i ? max(L[i - 1], sc[i]) : sc[i];
+        }
+        // exclusive prefix max over the quad: three independent shuffles
+        const int x = L[7];
+        const int y1 = __shfl_up_sync(0xffffffffu, x, 1, 4);
+        const int y2 = __shfl_up_sync(0xffffffffu, x, 2, 4);
+        const int y3 = __shfl_up_sync(0xffffffffu, x, 3, 4);
+        const int z1 = max(x, __shfl_xor_sync(0xffffffffu, x, 1));
+        const int run = m;
+        int base = run;
+        if (t >= 1) base = max(base, y1);
+        if (t >= 2) base = max(base, y2);
+        if (t >= 3) base = max(base, y3);
+        int prevmax = base;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            bool valid = true;
+            if (MASKED) valid = kb + 8 * t + i <= prow && prow < n;
+            const int pm = max(base, L[i]);
+            const uint32_t w = exp_attn((int)((uint32_t)sc[i] - (uint32_t)pm), lut4k, c8);
+            T.w[i] = valid ? w : 0u;
+            // saturated scores may equal INT32_MIN: a record over INT32_MIN rescales nothing
+            const bool rec = valid && sc[i] > prevmax && prevmax != INT32_MIN;
+            T.ef[i] = rec ? (uint32_t)prevmax - (uint32_t)sc[i] : 0u;
+            rm |= rec ? 1u << i : 0u;
+            prevmax = pm;
+        }
+        m = max(run, max(z1, __shfl_xor_sync(0xffffffffu, z1, 2)));
     }
-    m = max(run, max(z1, __shfl_xor_sync(0xffffffffu, z1, 2)));
-    T.lrec = lrec;
-    const int r1 = lrec + __shfl_xor_sync(0xffffffffu, lrec, 1);
-    T.nrec = r1 + __shfl_xor_sync(0xffffffffu, r1, 2);
+    T.rm = rm;
+    uint32_t rowm = rm << (8 * t);
+    rowm |= __shfl_xor_sync(0xffffffffu, rowm, 1);
+    T.rowmask = rowm | __shfl_xor_sync(0xffffffffu, rowm, 2);
 }
 
-// Segment of each entry (records at or before it in key order within the tile),
-// one byte per entry: word q holds entries 4q..4q+3.  The records' (previous
-// max - score) are published to rec_e[row][segment - 1] and the row's record
-// count to rec_n[row]; the fold turns them into rescale factors.
-__device__ __forceinline__ void tile_segments(const Tile &T, int t, int g, uint32_t *rec_e, int *rec_n,
-                                              uint32_t (&segw)[2]) {
-    const int c = T.lrec;
-    const int c1 = __shfl_up_sync(0xffffffffu, c, 1, 4);
-    const int c2 = __shfl_up_sync(0xffffffffu, c, 2, 4);
-    const int c3 = __shfl_up_sync(0xffffffffu, c, 3, 4);
-    int sidx = (t >= 1 ? c1 : 0) + (t >= 2 ? c2 : 0) + (t >= 3 ? c3 : 0);
-#pragma unroll
-    for (int q = 0; q < 2; q++) {
-        uint32_t word = 0;
-#pragma unroll
-        for (int b = 0; b < 4; b++) {
-            const int i = 4 * q + b;
-            if (T.ef[i]) {
-                sidx++;
-                rec_e[g * 32 + sidx - 1] = T.ef[i];
-            }
-            word |= (uint32_t)sidx << (8 * b);
-        }
-        segw[q] = word;
-    }
-    if (t == 0) rec_n[g] = T.nrec;
+// bits 0..3 of x to bit 0 of bytes 0..3
+__device__ __forceinline__ uint32_t spread4(uint32_t x) { return ((x & 0xFu) * 0x00204081u) & 0x01010101u; }
+
+// Record bookkeeping of a tile with records.  Segment of each entry (records of
+// its row at or before it in key order), one byte per entry: word q holds entries
+// 4q..4q+3.  The entries' (previous max - score) go to rec_e[row][key] (0 where no
+// record); rem[e] = the record mask of PV row 2t+e, which the folds walk.
+__device__ __forceinline__ void tile_records(const Tile &T, int t, int g, uint32_t *rec_e, uint32_t (&segw)[2],
+                                             uint32_t (&rem)[2]) {
+    const uint32_t before = (uint32_t)__popc(T.rowmask & ((1u << (8 * t)) - 1u));
+    segw[0] = (spread4(T.rm) + before) * 0x01010101u;
+    segw[1] = (spread4(T.rm >> 4) + (segw[0] >> 24)) * 0x01010101u;
+    uint4 *dst = reinterpret_cast<uint4 *>(rec_e + g * 32 + 8 * t);
+    dst[0] = make_uint4(T.ef[0], T.ef[1], T.ef[2], T.ef[3]);
+    dst[1] = make_uint4(T.ef[4], T.ef[5], T.ef[6], T.ef[7]);
+    rem[0] = __shfl_sync(0xffffffffu, T.rowmask, 8 * t);       // a lane of row 2t's quad
+    rem[1] = __shfl_sync(0xffffffffu, T.rowmask, 8 * t + 4);   // row 2t+1
 }
 
 // 0xFF in each byte of x equal to q, else 0
@@ -214,8 +272,7 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, t = lane & 3;
     uint32_t *rec_e = reinterpret_cast<uint32_t *>(wsm + warp * AM_WARP_SMEM);   // [8][32]
-    int *rec_n = reinterpret_cast<int *>(rec_e + AM_ROWS * 32);                  // [8]
-    uint8_t *ostage = reinterpret_cast<uint8_t *>(rec_n + AM_ROWS);              // [8][64]
+    uint8_t *ostage = reinterpret_cast<uint8_t *>(rec_e + AM_ROWS * 32);         // [8][64]
 
     // K row layout: bytes [16t' + 4k + b] = dim 16k + 4t' + b, so thread t reads its
     // four B words (dims 4t, 16+4t, 32+4t, 48+4t) as one 16-byte load.
@@ -339,47 +396,58 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
                 plo[q] = prmt(x01, x23, 0x5410u);
                 phi[q] = prmt(x01, x23, 0x7632u);
             }
-            const int maxrec = (int)__reduce_max_sync(0xffffffffu, (unsigned)T.nrec);
+            const int maxrec = (int)__reduce_max_sync(0xffffffffu, (unsigned)__popc(T.rowmask));
             uint32_t segw[2] = {0, 0};
-            int nr[2] = {0, 0};   // records of the PV rows 2t, 2t+1
+            uint32_t rem[2] = {0, 0};   // records of the PV rows 2t, 2t+1 not yet folded
             if (maxrec > 0) {
-                tile_segments(T, t, g, rec_e, rec_n, segw);
+                tile_records(T, t, g, rec_e, segw, rem);
                 __syncwarp();
-                nr[0] = rec_n[2 * t];
-                nr[1] = rec_n[2 * t + 1];
             }
-            for (int pass = 0; pass <= maxrec; pass++) {
-                if (pass > 0) {
-                    // rows with a pass-th record fold their state (attention.rs:248-263)
-#pragma unroll
-                    for (int e = 0; e < 2; e++) {
-                        if (nr[e] >= pass) {
-                            // the accumulators keep running: state' = R(state + A) - A, with A the
-                            // accumulator value now, so that state + A stays the reference's value
-                            const uint32_t ef = exp_attn((int)rec_e[(2 * t + e) * 32 + pass - 1], lut4k, c8);
-                            const uint32_t sa = 256u * (uint32_t)shs[e] + (uint32_t)sls[e];
-                            s_state[e] = (uint32_t)(((unsigned long long)(s_state[e] + sa) * ef + 0x8000ull) >> 16) - sa;
-#pragma unroll
-                            for (int mi = 0; mi < 4; mi++)
-#pragma unroll
-                                for (int k = e; k < 4; k += 2) {
-                                    const uint32_t a = ((uint32_t)hiacc[mi][k] << 8) + (uint32_t)loacc[mi][k];
-                                    const int x = (int)((uint32_t)vst[mi][k] + a);
-                                    // (x*e +- 2^15) >> 16 with the sign of x (e >= 1)
-                                    const long long pr = (long long)x * (long long)ef + 0x8000ll;
-                                    vst[mi][k] = (int)((uint32_t)(pr >> 16) + (uint32_t)(x >> 31) - a);
-                                }
-                        }
-                    }
-                }
-                // P^T of this pass: bytes of entries in segment `pass`
+            {   // pass 0: the whole tile, or segment 0 of each row
                 uint32_t bh0 = phi[0], bh1 = phi[1], bl0 = plo[0], bl1 = plo[1];
                 if (maxrec > 0) {
-                    const uint32_t m0 = bytes_equal(segw[0], (uint32_t)pass);
-                    const uint32_t m1 = bytes_equal(segw[1], (uint32_t)pass);
+                    const uint32_t m0 = bytes_equal(segw[0], 0u);
+                    const uint32_t m1 = bytes_equal(segw[1], 0u);
                     bh0 &= m0; bl0 &= m0; bh1 &= m1; bl1 &= m1;
                 }
                 mma_s8u8(shs, ones, bh0, bh1);   // weight sums (all-ones rows)
+                mma_s8u8(sls, ones, bl0, bl1);
+#pragma unroll
+                for (int mi = 0; mi < 4; mi++) {
+                    mma_s8u8(hiacc[mi], va[mi], bh0, bh1);
+                    mma_s8u8(loacc[mi], va[mi], bl0, bl1);
+                }
+            }
+            for (int pass = 1; pass <= maxrec; pass++) {
+                // rows with a pass-th record fold their state (attention.rs:248-263)
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    if (rem[e] != 0u) {
+                        const int key = __ffs(rem[e]) - 1;
+                        rem[e] &= rem[e] - 1u;
+                        // the accumulators keep running: state' = R(state + A) - A, with A the
+                        // accumulator value now, so that state + A stays the reference's value
+                        // saturated (WIDE) scores can wrap the difference to >= 0, where exp gives 65535
+                        const int rd = (int)rec_e[(2 * t + e) * 32 + key];
+                        const uint32_t ef = WIDE ? exp_attn(rd, lut4k, c8) : exp_rec(rd, lut4k, c8);
+                        const uint32_t e16 = ef << 16, e16p1 = e16 + 1u;
+                        const uint32_t sa = 256u * (uint32_t)shs[e] + (uint32_t)sls[e];
+                        // s + sa >= 0: R(s + sa) is the high word alone
+                        s_state[e] = (uint32_t)(((unsigned long long)(s_state[e] + sa) * e16 + 0x80000000ull) >> 32) - sa;
+#pragma unroll
+                        for (int mi = 0; mi < 4; mi++)
+#pragma unroll
+                            for (int k = e; k < 4; k += 2) {
+                                const uint32_t a = ((uint32_t)hiacc[mi][k] << 8) + (uint32_t)loacc[mi][k];
+                                vst[mi][k] = (int)(rescale_rec((uint32_t)vst[mi][k] + a, e16, e16p1) - a);
+                            }
+                    }
+                }
+                // P^T of this pass: bytes of entries in segment `pass`
+                const uint32_t m0 = bytes_equal(segw[0], (uint32_t)pass);
+                const uint32_t m1 = bytes_equal(segw[1], (uint32_t)pass);
+                const uint32_t bh0 = phi[0] & m0, bl0 = plo[0] & m0, bh1 = phi[1] & m1, bl1 = plo[1] & m1;
+                mma_s8u8(shs, ones, bh0, bh1);
                 mma_s8u8(sls, ones, bl0, bl1);
 #pragma unroll
                 for (int mi = 0; mi < 4; mi++) {
@@ -454,8 +522,7 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__
     if (r >= M) return;
     uint8_t *stages = dsm + warp * 8192;
     uint32_t *rec_e = reinterpret_cast<uint32_t *>(wsm + warp * AM_WARP_SMEM);   // [8][32]
-    int *rec_n = reinterpret_cast<int *>(rec_e + AM_ROWS * 32);                  // [8]
-    uint8_t *ostage = reinterpret_cast<uint8_t *>(rec_n + AM_ROWS);              // [8][64]
+    uint8_t *ostage = reinterpret_cast<uint8_t *>(rec_e + AM_ROWS * 32);         // [8][64]
     const size_t len = cache_ld / 128;
     const int8_t *ks = kvc + (size_t)r * cache_ld;    // [len][64], dims permuted
     const int8_t *vt = ks + len * 64;                 // V tiles
@@ -555,21 +622,24 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__
             plo[q] = prmt(x01, x23, 0x5410u);
             phi[q] = prmt(x01, x23, 0x7632u);
         }
-        const int maxrec = (int)__reduce_max_sync(0xffffffffu, (unsigned)T.nrec);
+        const int maxrec = (int)__reduce_max_sync(0xffffffffu, (unsigned)__popc(T.rowmask));
         uint32_t segw[2] = {0, 0};
-        int nr[2] = {0, 0};
+        uint32_t rem[2] = {0, 0};
         if (maxrec > 0) {
-            tile_segments(T, t, g, rec_e, rec_n, segw);
+            tile_records(T, t, g, rec_e, segw, rem);
             __syncwarp();
-            nr[0] = rec_n[2 * t];
-            nr[1] = rec_n[2 * t + 1];
         }
         for (int pass = 0; pass <= maxrec; pass++) {
             if (pass > 0) {
 #pragma unroll
                 for (int e = 0; e < 2; e++) {
-                    if (nr[e] >= pass) {
-                        const uint32_t ef = exp_attn((int)rec_e[(2 * t + e) * 32 + pass - 1], lut4k, c8);
+                    if (rem[e] != 0u) {
+                        const int key = __ffs(rem[e]) - 1;
+                        rem[e] &= rem[e] - 1u;
+                        // saturated (WIDE) scores can wrap the difference to >= 0, where exp gives 65535
+                        const int rd = (int)rec_e[(2 * t + e) * 32 + key];
+                        const uint32_t ef = WIDE ? exp_attn(rd, lut4k, c8) : exp_rec(rd, lut4k, c8);
+                        const uint32_t e16 = ef << 16, e16p1 = e16 + 1u;
                         const unsigned long long sa = 256ull * (uint32_t)shs[e] + (unsigned long long)(uint32_t)sls[e];
                         s_state[e] = (((s_state[e] + sa) * ef + 0x8000ull) >> 16) - sa;
 #pragma unroll
@@ -577,9 +647,7 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__
 #pragma unroll
                             for (int k = e; k < 4; k += 2) {
                                 const uint32_t a = ((uint32_t)hiacc[mi][k] << 8) + (uint32_t)loacc[mi][k];
-                                const int x = (int)((uint32_t)vst[mi][k] + a);
-                                const long long pr = (long long)x * (long long)ef + 0x8000ll;
-                                vst[mi][k] = (int)((uint32_t)(pr >> 16) + (uint32_t)(x >> 31) - a);
+                                vst[mi][k] = (int)(rescale_rec((uint32_t)vst[mi][k] + a, e16, e16p1) - a);
                             }
                     }
                 }

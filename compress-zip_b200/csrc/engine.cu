@@ -52,7 +52,7 @@ struct LayerDev {
     int8_t *qkv_w = nullptr, *out_w = nullptr, *up_w = nullptr, *down_w = nullptr;
     int32_t *score_mult = nullptr;
     int8_t *sink_key = nullptr;
-    bool wide_mult = false;   // some |score_mult| >= 2^28: scores may saturate int32
+    bool wide_mult = false;   // some |score_mult| >= 2^27: the attention kernels take the general score path
     int qkv_mult = 1, out_mult = 1, up_mult = 1, down_mult = 1;
     int qkv_shift = 0, out_shift = 0, up_shift = 0, down_shift = 0;
     TcMatrix tm_qkv, tm_out, tm_up, tm_down;   // TMA descriptors of the weights
@@ -354,7 +354,7 @@ int load_model(czg_ctx *c, const uint8_t *bytes, size_t len) {
         for (int hh = 0; hh < H; hh++) {
             int32_t sm;
             memcpy(&sm, t->data + 4 * hh, 4);
-            if (sm >= (1 << 28) || sm <= -(1 << 28)) L.wide_mult = true;
+            if (sm >= (1 << 27) || sm <= -(1 << 27)) L.wide_mult = true;
         }
         if (const TensorRef *sk = find(f, p + "attn.sink_key")) {
             if (sk->dtype != "I8" || sk->numel() < 64 || sk->nbytes < 64)
