@@ -25,9 +25,10 @@
 // A tile whose rows contain records is replayed in passes: pass q adds the keys
 // of segment q (segment = run of keys between records).  Before pass q every
 // row with a q-th record in the tile folds its state exactly as the reference
-// rescales at that key: state = R(state + 256*Hi + Lo, e),
-// s = ((s + seg_sum) * e + 2^15) >> 16 (kept as an offset to the running
-// accumulators, which are never reset).  The folded state lives in registers in
+// rescales at that key: Lo = R(256*Hi + Lo, e), Hi = 0, so the folded value
+// lives on in the Lo accumulator (the MMA's s32 accumulation wraps modulo 2^32
+// like the reference's i32 sum), and s = ((s + seg_sum) * e + 2^15) >> 16 (kept
+// as an offset to the running weight sums).  The state stays in registers in
 // the accumulator layout (row 2t+e of thread (g, t)), each row folded by the 8
 // threads that hold it.  A record whose previous maximum is still INT32_MIN
 // rescales nothing (attention.rs:248-250) and is no segment boundary.
@@ -353,11 +354,11 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
             m = score_from_dot<true>(accs[0], mult);
             s_state[0] = s_state[1] = 65535u;
         }
-        int hiacc[4][4], loacc[4][4], vst[4][4];
+        int hiacc[4][4], loacc[4][4];
 #pragma unroll
         for (int mi = 0; mi < 4; mi++)
 #pragma unroll
-            for (int k = 0; k < 4; k++) { hiacc[mi][k] = 0; loacc[mi][k] = 0; vst[mi][k] = 0; }
+            for (int k = 0; k < 4; k++) { hiacc[mi][k] = 0; loacc[mi][k] = 0; }
         int shs[4] = {0, 0, 0, 0}, sls[4] = {0, 0, 0, 0};   // weight sums of rows 2t, 2t+1 in [0], [1]
 
         for (int kb = 0; kb <= p_last; kb += 32) {
@@ -425,8 +426,6 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
                     if (rem[e] != 0u) {
                         const int key = __ffs(rem[e]) - 1;
                         rem[e] &= rem[e] - 1u;
-                        // the accumulators keep running: state' = R(state + A) - A, with A the
-                        // accumulator value now, so that state + A stays the reference's value
                         // saturated (WIDE) scores can wrap the difference to >= 0, where exp gives 65535
                         const int rd = (int)rec_e[(2 * t + e) * 32 + key];
                         const uint32_t ef = WIDE ? exp_attn(rd, lut4k, c8) : exp_rec(rd, lut4k, c8);
@@ -438,8 +437,9 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
                         for (int mi = 0; mi < 4; mi++)
 #pragma unroll
                             for (int k = e; k < 4; k += 2) {
-                                const uint32_t a = ((uint32_t)hiacc[mi][k] << 8) + (uint32_t)loacc[mi][k];
-                                vst[mi][k] = (int)(rescale_rec((uint32_t)vst[mi][k] + a, e16, e16p1) - a);
+                                const uint32_t x = ((uint32_t)hiacc[mi][k] << 8) + (uint32_t)loacc[mi][k];
+                                loacc[mi][k] = (int)rescale_rec(x, e16, e16p1);
+                                hiacc[mi][k] = 0;
                             }
                     }
                 }
@@ -468,7 +468,7 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
 #pragma unroll
                 for (int dh = 0; dh < 2; dh++) {
                     const int k = 2 * dh + e;
-                    const int x = (int)((uint32_t)vst[mi][k] + ((uint32_t)hiacc[mi][k] << 8) + (uint32_t)loacc[mi][k]);
+                    const int x = (int)(((uint32_t)hiacc[mi][k] << 8) + (uint32_t)loacc[mi][k]);
                     orow[16 * mi + g + 8 * dh] = (uint8_t)clamp127(div_rne_s32_u64(x, den));
                 }
         }
@@ -572,11 +572,11 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__
         m = score_from_dot<true>(accs[0], mult);
         s_state[0] = s_state[1] = 65535ull;
     }
-    int hiacc[4][4], loacc[4][4], vst[4][4];
+    int hiacc[4][4], loacc[4][4];
 #pragma unroll
     for (int mi = 0; mi < 4; mi++)
 #pragma unroll
-        for (int k = 0; k < 4; k++) { hiacc[mi][k] = 0; loacc[mi][k] = 0; vst[mi][k] = 0; }
+        for (int k = 0; k < 4; k++) { hiacc[mi][k] = 0; loacc[mi][k] = 0; }
     int shs[4] = {0, 0, 0, 0}, sls[4] = {0, 0, 0, 0};
 
     decode_tile_async(stages, ks, vt, 0, lane);   // tile 0 in flight
@@ -646,8 +646,9 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__
                         for (int mi = 0; mi < 4; mi++)
 #pragma unroll
                             for (int k = e; k < 4; k += 2) {
-                                const uint32_t a = ((uint32_t)hiacc[mi][k] << 8) + (uint32_t)loacc[mi][k];
-                                vst[mi][k] = (int)(rescale_rec((uint32_t)vst[mi][k] + a, e16, e16p1) - a);
+                                const uint32_t x = ((uint32_t)hiacc[mi][k] << 8) + (uint32_t)loacc[mi][k];
+                                loacc[mi][k] = (int)rescale_rec(x, e16, e16p1);
+                                hiacc[mi][k] = 0;
                             }
                     }
                 }
@@ -679,7 +680,7 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__
 #pragma unroll
             for (int dh = 0; dh < 2; dh++) {
                 const int k = 2 * dh + e;
-                const int x = (int)((uint32_t)vst[mi][k] + ((uint32_t)hiacc[mi][k] << 8) + (uint32_t)loacc[mi][k]);
+                const int x = (int)(((uint32_t)hiacc[mi][k] << 8) + (uint32_t)loacc[mi][k]);
                 orow[16 * mi + g + 8 * dh] = (uint8_t)clamp127(div_rne_s32_u64(x, den));
             }
     }
