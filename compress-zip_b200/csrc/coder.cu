@@ -74,16 +74,21 @@ __global__ void k_cdf_lohi(const int32_t *__restrict__ logits, int V, int ld,
     }
 }
 
-// Register-resident version for V <= 128 * G (and so S < 2^30): the row is read
+// Register-resident version for V <= 128 * G (and so S < 2^26): the row is read
 // once (lane l holds elements 128j + 4l + k), the weights e_i are kept packed,
-// and the division by S uses floor_mul_div.  The weight is read from lut4k,
+// and the division by S uses freq_of.  The weight is read from lut4k,
 // exp_q16 tabulated by t256 (entries >= 4096 are 1), with
 // t256 = the high word of neg * (coef << 8) + 2^31, which needs coef < 2^24.
+// Everything below the symbol is summed per block of 4 entries: the blocks
+// 128j + 4l.. wholly below it add their block sums, and the one block that holds
+// it (j = sym >> 7) is taken apart.  The first argmax lies below the symbol iff
+// the maximum of the entries below it equals the row's maximum, and is the symbol
+// iff it does not and the symbol's logit is the maximum.
 // FULL: V == 128 * G, so no element is out of range.  EXP0: lut4k[0] == 65535 and
 // |logit| < 2^30 (no wrap in logit - max), so a zero difference needs no special
 // case.  One warp per row.
 template <int G, bool FULL, bool EXP0>
-__global__ void __launch_bounds__(256) k_cdf_lohi_reg(const int32_t *__restrict__ logits, int V, int ld,
+__global__ void __launch_bounds__(256, 4) k_cdf_lohi_reg(const int32_t *__restrict__ logits, int V, int ld,
                                                       const uint32_t *__restrict__ sym,
                                                       const uint16_t *__restrict__ lut4k, uint32_t c8,
                                                       uint32_t total, int M, uint2 *__restrict__ lohi) {
@@ -94,25 +99,35 @@ __global__ void __launch_bounds__(256) k_cdf_lohi_reg(const int32_t *__restrict_
     int x[G][4];
 #pragma unroll
     for (int j = 0; j < G; j++) {
-        int4 v = make_int4(0, 0, 0, 0);
+        int4 v = make_int4(INT32_MIN, INT32_MIN, INT32_MIN, INT32_MIN);
         if (FULL || 128 * j + 4 * lane < V) v = __ldcs(src + 32 * j + lane);   // read once: streaming
         x[j][0] = v.x; x[j][1] = v.y; x[j][2] = v.z; x[j][3] = v.w;
+        if (!FULL) {   // a partly valid block
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+                if (128 * j + 4 * lane + k >= V) x[j][k] = INT32_MIN;
+        }
     }
     const int sy = (int)sym[row];
-    // max and its first index (primitives.rs:278-295); this lane's indices increase with (j, k)
-    int mx = INT32_MIN, am = 0x7fffffff;
+    const int J = sy >> 7;                  // block index of the symbol
+    const int kk = (sy & 127) - 4 * lane;   // entries k < kk of this lane's block J lie below it
+    // this lane's block J, the row max, and the max below the symbol
+    int xJ[4] = {INT32_MIN, INT32_MIN, INT32_MIN, INT32_MIN};
+    int mx = INT32_MIN, mb = INT32_MIN;
 #pragma unroll
-    for (int j = 0; j < G; j++)
+    for (int j = 0; j < G; j++) {
+        const int bm = max(max(x[j][0], x[j][1]), max(x[j][2], x[j][3]));
+        mx = max(mx, bm);
+        if (j < J) mb = max(mb, bm);
+        if (j == J) { xJ[0] = x[j][0]; xJ[1] = x[j][1]; xJ[2] = x[j][2]; xJ[3] = x[j][3]; }
+    }
 #pragma unroll
-        for (int k = 0; k < 4; k++) {
-            const int i = 128 * j + 4 * lane + k;
-            if ((FULL || i < V) && x[j][k] > mx) { mx = x[j][k]; am = i; }
-        }
+    for (int k = 0; k < 4; k++)
+        if (k < kk) mb = max(mb, xJ[k]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
-        const int om = __shfl_xor_sync(0xffffffffu, mx, o);
-        const int oa = __shfl_xor_sync(0xffffffffu, am, o);
-        if (om > mx || (om == mx && oa < am)) { mx = om; am = oa; }
+        mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, o));
     }
     uint32_t ew[G][2];   // packed 16-bit weights
     uint32_t S = 0;
@@ -122,11 +137,10 @@ __global__ void __launch_bounds__(256) k_cdf_lohi_reg(const int32_t *__restrict_
 #pragma unroll
         for (int k = 0; k < 4; k++) {
             const int i = 128 * j + 4 * lane + k;
-            const int dlt = (int)((uint32_t)x[j][k] - (uint32_t)mx);
-            const uint32_t neg = 0u - (uint32_t)dlt;
+            const uint32_t neg = (uint32_t)mx - (uint32_t)x[j][k];
             const uint32_t t = min((uint32_t)(((unsigned long long)neg * c8 + 0x80000000ull) >> 32), 4096u);
             uint32_t w = __ldg(lut4k + t);
-            if (!EXP0) w = dlt >= 0 ? 65535u : w;
+            if (!EXP0) w = neg == 0u ? 65535u : w;
             e[k] = (FULL || i < V) ? w : 0u;
             S += e[k];
         }
@@ -135,37 +149,45 @@ __global__ void __launch_bounds__(256) k_cdf_lohi_reg(const int32_t *__restrict_
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
-    const uint32_t R = total - (uint32_t)V;
-    const uint32_t a = R / S, b = R % S;
-    const float bs = __fdiv_rn((float)b, (float)S);
-    uint32_t f_all = 0, f_below = 0;
+    const FreqDiv fd = make_freq_div(total - (uint32_t)V, S);
+    uint32_t f_all = 0, f_below = 0, eJ[2] = {0u, 0u};
 #pragma unroll
-    for (int j = 0; j < G; j++)
+    for (int j = 0; j < G; j++) {
+        uint32_t fs = 0;
 #pragma unroll
         for (int k = 0; k < 4; k++) {
-            const int i = 128 * j + 4 * lane + k;
             const uint32_t e = (ew[j][k >> 1] >> (16 * (k & 1))) & 0xFFFFu;
-            uint32_t f = 1u + floor_mul_div(e, a, b, S, bs);
-            if (!FULL) f = i < V ? f : 0u;
-            f_all += f;
-            f_below += (i < sy) ? f : 0u;
+            uint32_t f = freq_of(e, fd);
+            if (!FULL) f = 128 * j + 4 * lane + k < V ? f : 0u;
+            fs += f;
         }
-    // the symbol's own frequency, from the lane that holds it
-    uint32_t esel = 0;
+        f_all += fs;
+        if (j < J) f_below += fs;
+        if (j == J) { eJ[0] = ew[j][0]; eJ[1] = ew[j][1]; }
+    }
+    // block J entry by entry: those below the symbol, and the symbol itself
+    uint32_t f_sym = 0;
 #pragma unroll
-    for (int j = 0; j < G; j++)
-        if (j == (sy >> 7)) esel = (sy & 2) ? ew[j][1] : ew[j][0];
-    uint32_t f_sym = 1u + floor_mul_div((esel >> (16 * (sy & 1))) & 0xFFFFu, a, b, S, bs);
-    f_sym = __shfl_sync(0xffffffffu, f_sym, (sy >> 2) & 31);
+    for (int k = 0; k < 4; k++) {
+        const uint32_t f = freq_of((eJ[k >> 1] >> (16 * (k & 1))) & 0xFFFFu, fd);
+        if (k < kk) f_below += f;
+        if (k == kk) f_sym = f;
+    }
+    const int owner = (sy & 127) >> 2;
+    f_sym = __shfl_sync(0xffffffffu, f_sym, owner);
+    const int sk = sy & 3;
+    const int xs = sk == 0 ? xJ[0] : sk == 1 ? xJ[1] : sk == 2 ? xJ[2] : xJ[3];
+    const int x_sym = __shfl_sync(0xffffffffu, xs, owner);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         f_all += __shfl_xor_sync(0xffffffffu, f_all, o);
         f_below += __shfl_xor_sync(0xffffffffu, f_below, o);
     }
     if (lane == 0) {
-        const uint32_t rem = total - f_all;   // goes to the argmax (softmax_cdf.rs:125-127)
-        const uint32_t lo = f_below + ((uint32_t)am < (uint32_t)sy ? rem : 0u);
-        const uint32_t hi = lo + f_sym + ((uint32_t)am == (uint32_t)sy ? rem : 0u);
+        const uint32_t rem = total - f_all;   // goes to the first argmax (softmax_cdf.rs:125-127)
+        const bool am_below = mb == mx, am_sym = !am_below && x_sym == mx;
+        const uint32_t lo = f_below + (am_below ? rem : 0u);
+        const uint32_t hi = lo + f_sym + (am_sym ? rem : 0u);
         lohi[row] = make_uint2(lo, hi);
     }
 }

@@ -75,16 +75,31 @@ __device__ __forceinline__ uint32_t exp_q16_shift(int neg_x, const uint16_t *lut
     return min(65535u, max(1u, out));
 }
 
-// floor(e * R / S) for 0 < e <= S < 2^30 and R < 2^32, with a = R / S and
-// b = R % S precomputed and bs = b / S as a correctly rounded float:
-// e*R/S = e*a + e*b/S; the float estimate of e*b/S (< 2^16) is off by less
-// than 1/64, and one remainder check, exact in wrapping 32-bit arithmetic
-// because the remainder lies in (-S, 2S), fixes it.
-__device__ __forceinline__ uint32_t floor_mul_div(uint32_t e, uint32_t a, uint32_t b, uint32_t S, float bs) {
-    const uint32_t q0 = (uint32_t)__fmul_rn(__uint2float_rn(e), bs);
-    const int r = (int)(e * b - q0 * S);
-    const uint32_t q = q0 - (uint32_t)(r < 0) + (uint32_t)(r >= (int)S);
-    return e * a + q;
+// 1 + floor(e * R / S) (softmax_cdf.rs:113-121) for e < 2^16 and S < 2^26, with
+// a = R / S and F a 32-bit fixed-point fraction of b / S (b = R % S) from below:
+// F <= b * 2^32 / S < F + 2818.  Then q0 = hi(e * F) is floor(e * b / S) or one
+// less, and the remainder e*R - (e*a + q0)*S, which lies in [0, 2S) and so is
+// exact in wrapping 32-bit arithmetic, decides.  F comes from the correctly
+// rounded float b / S: b, S and the quotient each round with relative error
+// <= 2^-24, so bs * 2^32 is within 770 of b * 2^32 / S, and 2048 less is below it.
+struct FreqDiv {
+    uint32_t R, S, a, F;
+};
+__device__ __forceinline__ FreqDiv make_freq_div(uint32_t R, uint32_t S) {
+    FreqDiv d;
+    d.R = R;
+    d.S = S;
+    d.a = R / S;
+    const float bs = __fdiv_rn(__uint2float_rn(R - d.a * S), __uint2float_rn(S));
+    const float p = __fmul_rn(bs, 4294967296.0f);
+    const uint32_t fe = p >= 4294967296.0f ? 0xFFFFFFFFu : __float2uint_rz(p);
+    d.F = fe > 2048u ? fe - 2048u : 0u;
+    return d;
+}
+__device__ __forceinline__ uint32_t freq_of(uint32_t e, const FreqDiv &d) {
+    const uint32_t q = e * d.a + __umulhi(e, d.F);
+    const uint32_t r = e * d.R - q * d.S;
+    return q + (r >= d.S ? 2u : 1u);
 }
 
 // primitives.rs:192-213 -- floor(sqrt(x)), which the reference computes with the

@@ -194,7 +194,7 @@ __global__ void k_cdf_decode(const int32_t *__restrict__ logits, int V, int ld, 
 // Register-resident version for V == 32 * E (E in {8, 16, 32}): lane l holds the
 // E consecutive logits [l*E, (l+1)*E) in registers, the weights come from the
 // t256-indexed table lut4k (needs coef < 2^24), the division by S uses
-// floor_mul_div.  The interval search is done by the whole warp: the owner
+// freq_of.  The interval search is done by the whole warp: the owner
 // lane's weights go through shared memory, one element per lane, and an
 // inclusive scan gives the cumulative frequencies.
 template <int E, bool EXP0>
@@ -240,12 +240,10 @@ __global__ void __launch_bounds__(256) k_cdf_decode_reg(
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
-    const uint32_t R = total - (uint32_t)V;
-    const uint32_t a = R / S, b = R % S;
-    const float bs = __fdiv_rn((float)b, (float)S);
+    const FreqDiv fd = make_freq_div(total - (uint32_t)V, S);
     uint32_t F = 0;
 #pragma unroll
-    for (int k = 0; k < E; k++) F += 1u + floor_mul_div((ew[k >> 1] >> (16 * (k & 1))) & 0xFFFFu, a, b, S, bs);
+    for (int k = 0; k < E; k++) F += freq_of((ew[k >> 1] >> (16 * (k & 1))) & 0xFFFFu, fd);
     uint32_t all = F;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) all += __shfl_xor_sync(0xffffffffu, all, o);
@@ -279,7 +277,7 @@ __global__ void __launch_bounds__(256) k_cdf_decode_reg(
     const int idx = owner * E + lane;
     if (lane < E) {
         const uint32_t e = (ebuf[wib][lane >> 1] >> (16 * (lane & 1))) & 0xFFFFu;
-        f = 1u + floor_mul_div(e, a, b, S, bs) + (idx == am ? rem : 0u);
+        f = freq_of(e, fd) + (idx == am ? rem : 0u);
     }
     uint32_t cum = f;
 #pragma unroll

@@ -77,6 +77,7 @@ struct czg_ctx {
     int8_t *embed = nullptr, *final_norm = nullptr, *head_w = nullptr;
     uint16_t *lut = nullptr;
     uint16_t *lut4k = nullptr;   // exp_q16 by t256 <= 4096 (lut.rs:213-235 unrolled over ip)
+    uint16_t *inv_tab = nullptr;   // inv_rms_q15 by floor(sum_sq / d), eps folded in
     bool kernel_timing = false;   // CUDA events around every kernel (czg_set_kernel_timing, CZG_KERNEL_TIMING=1)
     bool exp0 = false;           // lut4k[0] == 65535: exp of a zero difference needs no special case
     bool logit_small = false;    // every |logit| < 2^30: no logit difference wraps
@@ -297,6 +298,8 @@ int load_model(czg_ctx *c, const uint8_t *bytes, size_t len) {
         if (!upload(c, &c->lut4k, l4.data(), l4.size() * 2)) return CZG_E_DEVICE;
         c->exp0 = l4[0] == 65535;
     }
+    if (!dalloc(c, &c->inv_tab, (size_t)kInvTabEntries)) return CZG_E_DEVICE;
+    launch_inv_table(c->eps, c->inv_tab, c->stream);
     for (int k = 0; k < 2; k++) {
         const char *nm = k ? "lut.rope_sin" : "lut.rope_cos";
         if ((st = need(c, f, nm, "I16", (int64_t)ctx * 32, &t))) return st;
@@ -460,7 +463,7 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
                     c->pos, c->err_flag, st);
     });
     timed(c, kEmbedNorm, [&] {
-        launch_embed_norm(c->tok_in, c->embed, c->layers[0].attn_norm, M, d, c->eps, c->x_res, c->res16, c->xn, st);
+        launch_embed_norm(c->tok_in, c->embed, c->layers[0].attn_norm, M, d, c->inv_tab, c->x_res, c->res16, c->xn, st);
     });
     for (int l = 0; l < m.n_layers; l++) {
         const LayerDev &L = c->layers[l];
@@ -488,7 +491,7 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
                  c->o8, d);
         });
         timed(c, kResidualNorm, [&] {
-            launch_residual_norm(c->o8, L.ffn_norm, L.post_attn_norm, M, d, c->eps, c->x_res, c->res16, c->xn, st);
+            launch_residual_norm(c->o8, L.ffn_norm, L.post_attn_norm, M, d, c->inv_tab, c->x_res, c->res16, c->xn, st);
         });
         timed(c, kGemmUp, [&] {
             gemm(c, c->tm_xn, L.tm_up, c->xn, L.up_w, M, 2 * dff, d, kEpiReglu, L.up_mult, L.up_shift,
@@ -500,7 +503,7 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
         });
         const int8_t *next = l + 1 < m.n_layers ? c->layers[l + 1].attn_norm : c->final_norm;
         timed(c, kResidualNorm, [&] {
-            launch_residual_norm(c->o8, L.post_ffn_norm, next, M, d, c->eps, c->x_res, c->res16, c->xn, st);
+            launch_residual_norm(c->o8, L.post_ffn_norm, next, M, d, c->inv_tab, c->x_res, c->res16, c->xn, st);
         });
     }
     if (tr && tr->final_in)
@@ -744,7 +747,7 @@ int decompress_impl(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts
             while (active > 0 && (int)n_tokens[order[w0 + active - 1]] <= step) active--;
             const int M = active;
             timed(c, kEmbedNorm, [&] {
-                launch_embed_norm(c->tok_in, c->embed, c->layers[0].attn_norm, M, d, c->eps, c->x_res, c->res16, c->xn, s);
+                launch_embed_norm(c->tok_in, c->embed, c->layers[0].attn_norm, M, d, c->inv_tab, c->x_res, c->res16, c->xn, s);
             });
             for (int l = 0; l < m.n_layers; l++) {
                 const LayerDev &L = c->layers[l];
@@ -770,7 +773,7 @@ int decompress_impl(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts
                          c->o8, d);
                 });
                 timed(c, kResidualNorm, [&] {
-                    launch_residual_norm(c->o8, L.ffn_norm, L.post_attn_norm, M, d, c->eps, c->x_res, c->res16, c->xn, s);
+                    launch_residual_norm(c->o8, L.ffn_norm, L.post_attn_norm, M, d, c->inv_tab, c->x_res, c->res16, c->xn, s);
                 });
                 timed(c, kGemmUp, [&] {
                     gemm(c, c->tm_xn, L.tm_up, c->xn, L.up_w, M, 2 * dff, d, kEpiReglu, L.up_mult, L.up_shift,
@@ -782,7 +785,7 @@ int decompress_impl(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts
                 });
                 const int8_t *next = l + 1 < m.n_layers ? c->layers[l + 1].attn_norm : c->final_norm;
                 timed(c, kResidualNorm, [&] {
-                    launch_residual_norm(c->o8, L.post_ffn_norm, next, M, d, c->eps, c->x_res, c->res16, c->xn, s);
+                    launch_residual_norm(c->o8, L.post_ffn_norm, next, M, d, c->inv_tab, c->x_res, c->res16, c->xn, s);
                 });
             }
             timed(c, kGemmHead, [&] {

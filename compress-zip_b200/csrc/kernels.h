@@ -17,11 +17,14 @@ void kernels_init();
 void launch_rows(const uint32_t *tokens, const int *chunk_row0, const int *chunk_len,
                  const uint64_t *chunk_tok0, int n_chunks, int vocab, uint32_t *tok_in,
                  uint32_t *tok_out, int *pos, int *err, cudaStream_t st);
+// inv_tab: inv_rms_q15 by floor(sum_sq / d), kInvTabEntries entries, from launch_inv_table.
 // x_res: the residual stream, int16 when res16 (exact for n_layers <= 128), else int32
+constexpr int kInvTabEntries = 16384;
+void launch_inv_table(int eps, uint16_t *tab, cudaStream_t st);
 void launch_embed_norm(const uint32_t *tok_in, const int8_t *embed, const int8_t *norm_w, int M,
-                       int d, int eps, void *x_res, bool res16, int8_t *xn, cudaStream_t st);
+                       int d, const uint16_t *inv_tab, void *x_res, bool res16, int8_t *xn, cudaStream_t st);
 void launch_residual_norm(const int8_t *o, const int8_t *post_w, const int8_t *next_w, int M, int d,
-                          int eps, void *x_res, bool res16, int8_t *xn, cudaStream_t st);
+                          const uint16_t *inv_tab, void *x_res, bool res16, int8_t *xn, cudaStream_t st);
 void launch_kv_prep(const int8_t *qkv, int ldq, int d, const int *pos, const int16_t *rope_cos,
                     const int16_t *rope_sin, int M, int8_t *kv, cudaStream_t st);
 

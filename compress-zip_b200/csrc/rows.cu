@@ -31,20 +31,28 @@ __global__ void k_rows(const uint32_t *__restrict__ tokens, const int *__restric
     }
 }
 
+// inv_rms_q15 by floor(sum_sq / d): every norm input is clamped to +-127, so the
+// mean square is at most 127^2 (rmsnorm.rs:14-30 with the model's eps folded in).
+constexpr int kInvTab = kInvTabEntries;
+__global__ void k_inv_table(int eps, uint16_t *__restrict__ tab) {
+    const int m = blockIdx.x * blockDim.x + threadIdx.x;
+    if (m < kInvTab) tab[m] = (uint16_t)inv_rms_q15((uint32_t)m, 1, eps);   // floor(m / 1) + eps
+}
+
 // Warp-level RMSNorm of one row held as D/128 words of 4 int8 per lane
 // (lane owns bytes [4*lane + 128*j, +4)).  rmsnorm.rs:40-75.  The sum of squares
 // uses dp4a (exact: at most 4 * 127^2 per call); round_even(t / 2^15) is
 // (t + 2^14 - 1 + ((t >> 15) & 1)) >> 15, exact for |t| <= 127 * 127 * 2^15.
 template <int NW>
-__device__ __forceinline__ void rmsnorm_words(const uint32_t (&x)[NW], const uint32_t (&w)[NW], int eps,
-                                              uint32_t (&y)[NW]) {
+__device__ __forceinline__ void rmsnorm_words(const uint32_t (&x)[NW], const uint32_t (&w)[NW],
+                                              const uint16_t *__restrict__ inv_tab, uint32_t (&y)[NW]) {
     constexpr int D = NW * 128;
     int ss = 0;
 #pragma unroll
     for (int j = 0; j < NW; j++) ss = __dp4a((int)x[j], (int)x[j], ss);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const int inv = inv_rms_q15((uint32_t)ss, D, eps);
+    const int inv = __ldg(inv_tab + min((uint32_t)ss / (uint32_t)D, (uint32_t)kInvTab - 1u));
 #pragma unroll
     for (int j = 0; j < NW; j++) {
         int o4[4];
@@ -73,7 +81,7 @@ __device__ __forceinline__ void store_res4(int16_t *p, int4 v) {
 // x_res[r] = embed[tok_in[r]] (residual), xn[r] = norm(clamp(x_res[r]))
 template <int NW, typename RT>
 __global__ void k_embed_norm(const uint32_t *__restrict__ tok_in, const int8_t *__restrict__ embed,
-                             const int8_t *__restrict__ norm_w, int M, int eps,
+                             const int8_t *__restrict__ norm_w, int M, const uint16_t *__restrict__ inv_tab,
                              RT *__restrict__ x_res, int8_t *__restrict__ xn) {
     constexpr int D = NW * 128;
     int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -98,7 +106,7 @@ __global__ void k_embed_norm(const uint32_t *__restrict__ tok_in, const int8_t *
         for (int b = 0; b < 4; b++) c |= (uint32_t)(uint8_t)clamp127(sext8(x[j], b)) << (8 * b);
         x[j] = c;
     }
-    rmsnorm_words<NW>(x, w, eps, y);
+    rmsnorm_words<NW>(x, w, inv_tab, y);
     uint32_t *yo = reinterpret_cast<uint32_t *>(xn + (size_t)warp * D);
 #pragma unroll
     for (int j = 0; j < NW; j++) yo[lane + 32 * j] = y[j];
@@ -108,7 +116,7 @@ __global__ void k_embed_norm(const uint32_t *__restrict__ tok_in, const int8_t *
 // xn = norm(clamp(x_res), next_w)
 template <int NW, typename RT>
 __global__ void k_residual_norm(const int8_t *__restrict__ o, const int8_t *__restrict__ post_w,
-                                const int8_t *__restrict__ next_w, int M, int eps,
+                                const int8_t *__restrict__ next_w, int M, const uint16_t *__restrict__ inv_tab,
                                 RT *__restrict__ x_res, int8_t *__restrict__ xn) {
     constexpr int D = NW * 128;
     int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -127,7 +135,7 @@ __global__ void k_residual_norm(const int8_t *__restrict__ o, const int8_t *__re
         w2[j] = __ldg(nw + lane + 32 * j);
         rv[j] = load_res4(xr + 4 * (lane + 32 * j));
     }
-    rmsnorm_words<NW>(x, w, eps, y);
+    rmsnorm_words<NW>(x, w, inv_tab, y);
 #pragma unroll
     for (int j = 0; j < NW; j++) {
         int4 r = rv[j];
@@ -139,7 +147,7 @@ __global__ void k_residual_norm(const int8_t *__restrict__ o, const int8_t *__re
         x[j] = (uint32_t)(uint8_t)clamp127(r.x) | ((uint32_t)(uint8_t)clamp127(r.y) << 8) |
                ((uint32_t)(uint8_t)clamp127(r.z) << 16) | ((uint32_t)(uint8_t)clamp127(r.w) << 24);
     }
-    rmsnorm_words<NW>(x, w2, eps, y);
+    rmsnorm_words<NW>(x, w2, inv_tab, y);
     uint32_t *yo = reinterpret_cast<uint32_t *>(xn + (size_t)warp * D);
 #pragma unroll
     for (int j = 0; j < NW; j++) yo[lane + 32 * j] = y[j];
@@ -175,41 +183,45 @@ void launch_rows(const uint32_t *tokens, const int *chunk_row0, const int *chunk
 }
 
 template <typename RT>
-void embed_norm_t(const uint32_t *tok_in, const int8_t *embed, const int8_t *norm_w, int M, int d, int eps,
+void embed_norm_t(const uint32_t *tok_in, const int8_t *embed, const int8_t *norm_w, int M, int d, const uint16_t *inv_tab,
                   RT *x_res, int8_t *xn, cudaStream_t st) {
     const int blocks = (M + 7) / 8;
     switch (d / 128) {
-        case 2: k_embed_norm<2, RT><<<blocks, 256, 0, st>>>(tok_in, embed, norm_w, M, eps, x_res, xn); break;
-        case 3: k_embed_norm<3, RT><<<blocks, 256, 0, st>>>(tok_in, embed, norm_w, M, eps, x_res, xn); break;
-        case 4: k_embed_norm<4, RT><<<blocks, 256, 0, st>>>(tok_in, embed, norm_w, M, eps, x_res, xn); break;
+        case 2: k_embed_norm<2, RT><<<blocks, 256, 0, st>>>(tok_in, embed, norm_w, M, inv_tab, x_res, xn); break;
+        case 3: k_embed_norm<3, RT><<<blocks, 256, 0, st>>>(tok_in, embed, norm_w, M, inv_tab, x_res, xn); break;
+        case 4: k_embed_norm<4, RT><<<blocks, 256, 0, st>>>(tok_in, embed, norm_w, M, inv_tab, x_res, xn); break;
         default: break;
     }
 }
 
 template <typename RT>
-void residual_norm_t(const int8_t *o, const int8_t *post_w, const int8_t *next_w, int M, int d, int eps,
+void residual_norm_t(const int8_t *o, const int8_t *post_w, const int8_t *next_w, int M, int d, const uint16_t *inv_tab,
                      RT *x_res, int8_t *xn, cudaStream_t st) {
     const int blocks = (M + 7) / 8;
     switch (d / 128) {
-        case 2: k_residual_norm<2, RT><<<blocks, 256, 0, st>>>(o, post_w, next_w, M, eps, x_res, xn); break;
-        case 3: k_residual_norm<3, RT><<<blocks, 256, 0, st>>>(o, post_w, next_w, M, eps, x_res, xn); break;
-        case 4: k_residual_norm<4, RT><<<blocks, 256, 0, st>>>(o, post_w, next_w, M, eps, x_res, xn); break;
+        case 2: k_residual_norm<2, RT><<<blocks, 256, 0, st>>>(o, post_w, next_w, M, inv_tab, x_res, xn); break;
+        case 3: k_residual_norm<3, RT><<<blocks, 256, 0, st>>>(o, post_w, next_w, M, inv_tab, x_res, xn); break;
+        case 4: k_residual_norm<4, RT><<<blocks, 256, 0, st>>>(o, post_w, next_w, M, inv_tab, x_res, xn); break;
         default: break;
     }
 }
 
+void launch_inv_table(int eps, uint16_t *tab, cudaStream_t st) {
+    k_inv_table<<<kInvTab / 256, 256, 0, st>>>(eps, tab);
+}
+
 void launch_embed_norm(const uint32_t *tok_in, const int8_t *embed, const int8_t *norm_w, int M,
-                       int d, int eps, void *x_res, bool res16, int8_t *xn, cudaStream_t st) {
+                       int d, const uint16_t *inv_tab, void *x_res, bool res16, int8_t *xn, cudaStream_t st) {
     if (M == 0) return;
-    if (res16) embed_norm_t(tok_in, embed, norm_w, M, d, eps, static_cast<int16_t *>(x_res), xn, st);
-    else embed_norm_t(tok_in, embed, norm_w, M, d, eps, static_cast<int32_t *>(x_res), xn, st);
+    if (res16) embed_norm_t(tok_in, embed, norm_w, M, d, inv_tab, static_cast<int16_t *>(x_res), xn, st);
+    else embed_norm_t(tok_in, embed, norm_w, M, d, inv_tab, static_cast<int32_t *>(x_res), xn, st);
 }
 
 void launch_residual_norm(const int8_t *o, const int8_t *post_w, const int8_t *next_w, int M, int d,
-                          int eps, void *x_res, bool res16, int8_t *xn, cudaStream_t st) {
+                          const uint16_t *inv_tab, void *x_res, bool res16, int8_t *xn, cudaStream_t st) {
     if (M == 0) return;
-    if (res16) residual_norm_t(o, post_w, next_w, M, d, eps, static_cast<int16_t *>(x_res), xn, st);
-    else residual_norm_t(o, post_w, next_w, M, d, eps, static_cast<int32_t *>(x_res), xn, st);
+    if (res16) residual_norm_t(o, post_w, next_w, M, d, inv_tab, static_cast<int16_t *>(x_res), xn, st);
+    else residual_norm_t(o, post_w, next_w, M, d, inv_tab, static_cast<int32_t *>(x_res), xn, st);
 }
 
 void launch_kv_prep(const int8_t *qkv, int ldq, int d, const int *pos, const int16_t *rope_cos,
