@@ -160,14 +160,19 @@ def peaks():
         return 6650.0, 1590.0, 1400.0, "of fallback"
 
 
-def traffic_per_token():
-    """dram bytes per token of each kernel class from the committed ncu summary."""
-    p = os.path.join(ROOT, "profiles", "dram_bytes_per_token.json")
+def per_token(name: str) -> dict:
+    """A per-token figure of each kernel class from a committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", name)
     try:
         with open(p) as f:
             return json.load(f)
     except (OSError, ValueError):
         return {}
+
+
+def traffic_per_token():
+    """dram bytes per token of each kernel class (read + write, one launch)."""
+    return per_token("dram_bytes_per_token.json")
 
 
 def algorithmic(kernel: str, info: dict, tokens_per_launch: float):
@@ -312,6 +317,19 @@ def main():
                     "traffic": None if tpt is None else round(tpt * tok_per_launch),
                     "peak_basis": (f"hbm_gbs {basis}" if bound == "hbm" else
                                    f"2 x bf16_tflops_sustained {basis} (dense int8 = 2 x bf16)")}
+        ipt = per_token("inst_per_token.json").get(dom)
+        if ipt is not None:
+            # the issue limit: 4 warp instructions per cycle per SM at the clock seen under load
+            sms = torch.cuda.get_device_properties(local).multi_processor_count
+            mhz = (clk or {}).get("sm_mhz") or 1965.0
+            issued = ipt * tok_per_launch / (per_launch_ms / 1e3) / 1e9
+            peak_i = sms * 4 * mhz / 1e3
+            roofline["issue"] = {"achieved": round(issued, 1), "peak": round(peak_i, 1),
+                                 "unit": "G warp instructions/s", "frac": round(issued / peak_i, 4),
+                                 "inst_per_token": ipt,
+                                 "basis": "ncu smsp__inst_executed per token (profiles/inst_per_token.json) "
+                                          "x tokens per launch / CUDA-event duration; peak = SMs x 4 "
+                                          "schedulers x median SM clock under load"}
         cpu = cpu_baseline(mf, args) if world == 1 else None
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
