@@ -85,8 +85,9 @@ struct czg_ctx {
     std::vector<LayerDev> layers;
     std::vector<void *> allocs;
 
-    // wave workspace
-    int cap_rows = 0, cap_chunks = 0;
+    // wave workspace (grown on demand up to wave_cap rows)
+    int cap_rows = 0, cap_chunks = 0, wave_cap = 0;
+    std::vector<void *> ws_allocs;
     uint32_t *tokens = nullptr, *tok_in = nullptr, *tok_out = nullptr;
     int *pos = nullptr, *x_res = nullptr, *err_flag = nullptr;
     bool res16 = false;   // residual stream stored as int16 (exact for n_layers <= 128)
@@ -143,6 +144,14 @@ bool dalloc(czg_ctx *c, T **p, size_t n) {
     }
     c->allocs.push_back(q);
     *p = static_cast<T *>(q);
+    return true;
+}
+
+template <class T>
+bool dalloc_ws(czg_ctx *c, T **p, size_t n) {
+    if (!dalloc(c, p, n)) return false;
+    c->ws_allocs.push_back(c->allocs.back());   // freed with the workspace
+    c->allocs.pop_back();
     return true;
 }
 
@@ -376,24 +385,40 @@ int load_model(czg_ctx *c, const uint8_t *bytes, size_t len) {
     return CZG_OK;
 }
 
+// device bytes of the wave workspace per row (the per-chunk arrays are small)
+size_t workspace_row_bytes(const czg_ctx *c) {
+    const czg_model_info &m = c->info;
+    const size_t d = (size_t)m.d_model;
+    return 16 + 4 * d + d + (d + 128) + 128 + d + d + (size_t)m.d_ff + 4 * (size_t)c->vpad + 8 + 4 + 4;
+}
+
+// (Re)allocate the wave workspace for `rows` tokens and `chunks` chunks per wave;
+// the previous workspace, if any, is released after the stream drains.
 int alloc_workspace(czg_ctx *c, int rows, int chunks) {
     const czg_model_info &m = c->info;
     const int d = m.d_model;
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    for (void *p : c->ws_allocs) cudaFree(p);
+    c->ws_allocs.clear();
+    if (c->h_meta) cudaFreeHost(c->h_meta);
+    c->h_meta = nullptr;
+    c->cap_rows = c->cap_chunks = 0;
     size_t R = (size_t)(rows + 127) / 128 * 128 + 128;
+    bool ok = dalloc_ws(c, &c->tokens, R) && dalloc_ws(c, &c->tok_in, R) && dalloc_ws(c, &c->tok_out, R) &&
+              dalloc_ws(c, &c->pos, R) && dalloc_ws(c, &c->x_res, R * d) && dalloc_ws(c, &c->xn, R * d) &&
+              dalloc_ws(c, &c->qkv, R * (d + 128)) && dalloc_ws(c, &c->kv, R * 128) &&
+              dalloc_ws(c, &c->attn, R * d) && dalloc_ws(c, &c->o8, R * d) &&
+              dalloc_ws(c, &c->hbuf, R * m.d_ff) && dalloc_ws(c, &c->logits, R * c->vpad) &&
+              dalloc_ws(c, &c->lohi, R) && dalloc_ws(c, &c->slots, 4 * R + 8 * (size_t)chunks + 64) &&
+              dalloc_ws(c, &c->packed, 4 * R + 8 * (size_t)chunks + 64) &&
+              dalloc_ws(c, &c->lens, (size_t)chunks) && dalloc_ws(c, &c->slot_off, (size_t)chunks + 1) &&
+              dalloc_ws(c, &c->pack_off, (size_t)chunks + 1) && dalloc_ws(c, &c->chunk_tok0, (size_t)chunks) &&
+              dalloc_ws(c, &c->chunk_row0, (size_t)chunks) && dalloc_ws(c, &c->chunk_len, (size_t)chunks) &&
+              dalloc_ws(c, &c->err_flag, 1);
+    if (!ok) return CZG_E_DEVICE;
+    cudaMemsetAsync(c->err_flag, 0, sizeof(int), c->stream);
     c->cap_rows = rows;
     c->cap_chunks = chunks;
-    bool ok = dalloc(c, &c->tokens, R) && dalloc(c, &c->tok_in, R) && dalloc(c, &c->tok_out, R) &&
-              dalloc(c, &c->pos, R) && dalloc(c, &c->x_res, R * d) && dalloc(c, &c->xn, R * d) &&
-              dalloc(c, &c->qkv, R * (d + 128)) && dalloc(c, &c->kv, R * 128) &&
-              dalloc(c, &c->attn, R * d) && dalloc(c, &c->o8, R * d) &&
-              dalloc(c, &c->hbuf, R * m.d_ff) && dalloc(c, &c->logits, R * c->vpad) &&
-              dalloc(c, &c->lohi, R) && dalloc(c, &c->slots, 4 * R + 8 * (size_t)chunks + 64) &&
-              dalloc(c, &c->packed, 4 * R + 8 * (size_t)chunks + 64) &&
-              dalloc(c, &c->lens, (size_t)chunks) && dalloc(c, &c->slot_off, (size_t)chunks + 1) &&
-              dalloc(c, &c->pack_off, (size_t)chunks + 1) && dalloc(c, &c->chunk_tok0, (size_t)chunks) &&
-              dalloc(c, &c->chunk_row0, (size_t)chunks) && dalloc(c, &c->chunk_len, (size_t)chunks) &&
-              dalloc(c, &c->err_flag, 1);
-    if (!ok) return CZG_E_DEVICE;
     // tcgen05 GEMMs need K % 128 == 0 and N % 128 == 0 for every projection
     const char *ge = getenv("CZG_GEMM");
     c->use_tc = !(ge && std::string(ge) == "mma") && d % 128 == 0 && m.d_ff % 128 == 0 &&
@@ -413,6 +438,24 @@ int alloc_workspace(czg_ctx *c, int rows, int chunks) {
     c->h_meta_bytes = (size_t)chunks * 32 + 64;
     if (!cuda_ok(c, cudaMallocHost(&c->h_meta, c->h_meta_bytes), "cudaMallocHost")) return CZG_E_DEVICE;
     return CZG_OK;
+}
+
+// Grow the workspace to hold `rows` tokens per wave (at most wave_cap, and at most
+// ~40% of the free device memory); small calls keep a small workspace.
+int ensure_workspace(czg_ctx *c, size_t rows) {
+    rows = std::min<size_t>(rows, (size_t)c->wave_cap);
+    if (rows <= (size_t)c->cap_rows) return CZG_OK;
+    size_t want = std::min<size_t>((size_t)c->wave_cap, std::max<size_t>(rows, 2 * (size_t)c->cap_rows));
+    size_t free_b = 0, total_b = 0;
+    if (cudaMemGetInfo(&free_b, &total_b) == cudaSuccess) {
+        // the current workspace is released first, so it counts as free
+        const size_t have = (size_t)c->cap_rows * workspace_row_bytes(c);
+        const size_t fit = (size_t)((free_b + have) * 0.4) / workspace_row_bytes(c);
+        want = std::max<size_t>((size_t)c->cap_rows, std::min(want, fit));
+    }
+    if (want <= (size_t)c->cap_rows) return CZG_OK;
+    const int rows_i = (int)want;
+    return alloc_workspace(c, rows_i, std::max(1024, rows_i / 16));
 }
 
 // One projection: tcgen05 path when available, else the mma.sync kernel.
@@ -585,6 +628,7 @@ int compress_impl(czg_ctx *c, const uint32_t *tokens, bool device_tokens, const 
     c->stats.n_chunks = n_chunks;
     uint64_t total = 0;
     int status = CZG_OK;
+    if (int st = ensure_workspace(c, ntok)) return st;
     for (const WavePlan &w : plan_waves(c, starts, n_chunks)) {
         const uint64_t t0 = starts[w.c0], nt = starts[w.c1] - t0;
         const uint32_t *d_tok;
@@ -706,6 +750,7 @@ int decompress_impl(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts
     const size_t per_stream = (size_t)m.n_layers * std::max(1, max_len) * 128;
     size_t budget = (size_t)8 << 30;
     if (const char *ev = getenv("CZG_DECODE_KV_BYTES")) budget = std::max<size_t>(1 << 20, strtoull(ev, nullptr, 10));
+    if (int st = ensure_workspace(c, std::min<size_t>(n_chunks, budget / per_stream))) return st;
     const size_t wave = std::max<size_t>(1, std::min<size_t>((size_t)c->cap_rows, budget / per_stream));
     const uint64_t all_bytes = data_starts[n_chunks] - data_starts[0];
     int st = dec_reserve(c, std::min<size_t>(wave, n_chunks), std::max(1, max_len), all_bytes, total_tok);
@@ -845,9 +890,12 @@ int czg_ctx_create(int device, const uint8_t *czm, size_t czm_len, czg_ctx **out
     if (!st) st = load_model(c, czm, czm_len);
     c->scalar_attention = getenv("CZG_SCALAR_ATTENTION") && atoi(getenv("CZG_SCALAR_ATTENTION")) != 0;
     c->kernel_timing = getenv("CZG_KERNEL_TIMING") && atoi(getenv("CZG_KERNEL_TIMING")) != 0;
-    int wave = 1 << 20;
-    if (const char *e = getenv("CZG_WAVE_TOKENS")) wave = std::max(4096, atoi(e));
-    if (!st) st = alloc_workspace(c, wave, std::max(1024, wave / 16));
+    // tokens per wave: large waves keep every SM busy through the per-chunk serial
+    // encoder and the attention's last CTAs; the workspace grows to it on demand
+    int wave = 1 << 22;
+    if (const char *e = getenv("CZG_WAVE_TOKENS")) wave = std::max(16384, atoi(e));
+    c->wave_cap = wave;
+    if (!st) st = alloc_workspace(c, std::min(wave, 1 << 16), std::max(1024, std::min(wave, 1 << 16) / 16));
     if (!st) {
         cudaEventCreate(&c->ev_begin);
         cudaEventCreate(&c->ev_end);
@@ -869,6 +917,7 @@ void czg_ctx_destroy(czg_ctx *c) {
     if (c->stream) cudaStreamSynchronize(c->stream);
     if (c->own_stream && c->own_stream != c->stream) cudaStreamSynchronize(c->own_stream);
     for (void *p : c->allocs) cudaFree(p);
+    for (void *p : c->ws_allocs) cudaFree(p);
     for (void *p : c->dec_allocs) cudaFree(p);
     if (c->h_meta) cudaFreeHost(c->h_meta);
     for (auto &e : c->evs) { cudaEventDestroy(e.a); cudaEventDestroy(e.b); }

@@ -85,6 +85,41 @@ def test_compress_many_docs(shipped_engine, shipped_oracle, oracle_mod, shipped_
     assert got == want
 
 
+def test_compress_waves_and_workspace_growth(shipped_path, shipped_oracle, oracle_mod, monkeypatch):
+    """A call spanning several waves (small wave cap), and a workspace that grows
+    from a small call to a larger one on the same context (default cap, which starts
+    at 65,536 rows); bytes equal the oracle's."""
+    from compress_zip_b200 import czm, synth
+    from compress_zip_b200.engine import Engine
+
+    tok = czm.ModelFile.load(shipped_path).tokenizer()
+    ids = [tok.encode_with_special_tokens(synth.document(seed, 15000)) for seed in range(21, 28)]
+
+    def packed(docs):
+        starts, base = [0], 0
+        for d in docs:
+            for s in range(0, len(d), 1024):
+                starts.append(base + min(s + 1024, len(d)))
+            base += len(d)
+        return np.concatenate([np.array(d, np.uint32) for d in docs]), np.array(starts, np.uint64)
+
+    small, large = packed(ids[:1]), packed(ids)   # ~11 K and ~80 K tokens
+    assert len(large[0]) > 65536
+    want_small = oracle_mod.compress_chunks(shipped_oracle, *small)
+    want_large = oracle_mod.compress_chunks(shipped_oracle, *large)
+    for cap in ("16384", None):
+        if cap:
+            monkeypatch.setenv("CZG_WAVE_TOKENS", cap)
+        else:
+            monkeypatch.delenv("CZG_WAVE_TOKENS", raising=False)
+        e = Engine.from_file(shipped_path, 0)
+        try:
+            assert e.compress_chunks(*small) == want_small
+            assert e.compress_chunks(*large) == want_large
+        finally:
+            e.close()
+
+
 def test_edge_cases(shipped_engine, shipped_oracle, oracle_mod):
     from compress_zip_b200.engine import CzgError
 
