@@ -81,7 +81,7 @@ def reduce_over_ranks(t_max: list, n_sum: list, device) -> tuple[list, list]:
 def workload(mf, seeds, ctx):
     tok = mf.tokenizer()
     docs = synth.documents(seeds, DOC_BYTES)
-    ids = tok.encode_batch(docs, num_threads=min(16, os.cpu_count() or 1))
+    ids = tok.encode_batch_arrays(docs, num_threads=min(16, os.cpu_count() or 1))
     starts = [0]
     base = 0
     for t in ids:
@@ -377,7 +377,7 @@ def decode_bench(eng, mf, rank, args, stream, world):
 
     tok = mf.tokenizer()
     docs = synth.documents(shard_seeds(rank, args.decode_docs, first=2000), 4096)
-    ids = tok.encode_batch(docs, num_threads=min(16, os.cpu_count() or 1))
+    ids = tok.encode_batch_arrays(docs, num_threads=min(16, os.cpu_count() or 1))
     starts, b = [0], 0
     for t in ids:
         for s0 in range(0, len(t), 512):
@@ -422,7 +422,8 @@ def decode_bench(eng, mf, rank, args, stream, world):
 
 def host_pipeline(eng, mf, args):
     """The whole compress CLI path on a bounded sample, stage by stage, labelled apart
-    from the hot-path figures: UTF-8 text -> tiktoken ids (all host threads) -> the
+    from the hot-path figures: UTF-8 text -> token ids (the native BPE tokenizer,
+    csrc/bpe_tokenizer.cpp, on up to 16 host threads) -> the
     GPU coder through the C ABI (host buffers) -> CZIPv1 container -> outer brotli
     q11 / lgwin 22 (rust/src/main.rs:186-281).  Wall clock on the host."""
     from compress_zip_b200 import container, outer_codec
@@ -432,7 +433,7 @@ def host_pipeline(eng, mf, args):
     text_bytes = sum(len(d.encode("utf-8")) for d in docs)
     tok = mf.tokenizer()
     t0 = time.perf_counter()
-    ids = tok.encode_batch(docs, num_threads=min(16, os.cpu_count() or 1))
+    ids = tok.encode_batch_arrays(docs, num_threads=min(16, os.cpu_count() or 1))
     t1 = time.perf_counter()
     streams = []
     for t in ids:   # one CZIPv1 stream per document, chunks of ctx (rust/src/main.rs:199-205)
@@ -471,7 +472,9 @@ def host_pipeline(eng, mf, args):
     return {"sample": f"{args.pipeline_docs} docs x {DOC_BYTES} B (seeds 1..{args.pipeline_docs}), "
                       f"{len(tokens)} tokens, one CZIPv1 file per document",
             "input_bytes": text_bytes, "output_bytes": out_bytes,
-            "tokenize_mb_per_s": mbs(t1 - t0), "gpu_coder_mb_per_s": mbs(t2 - t1),
+            "tokenize_mb_per_s": mbs(t1 - t0),
+            "tokenizer": "native" if tok.native is not None else "tiktoken",
+            "gpu_coder_mb_per_s": mbs(t2 - t1),
             "container_brotli_mb_per_s": mbs(t3 - t2), "container_brotli_threads": nthr,
             "total_mb_per_s": mbs(t3 - t0),
             "clock": "host wall clock, one pass after the timed steps"}

@@ -1,9 +1,11 @@
-"""Build libczg.so (CUDA kernels for sm_100a + the C-ABI host engine) in-tree.
+"""Build libczg.so (CUDA kernels for sm_100a + the C-ABI host engine) and
+libczg_tok.so (the host BPE tokenizer, plain C++) in-tree.
 
     python compress-zip_b200/build.py
 
-Objects go to compress-zip_b200/_build/ (git-ignored); the shared library is
-compress-zip_b200/libczg.so, which the Python binding (engine.py) loads.
+Objects go to compress-zip_b200/_build/ (git-ignored); the shared libraries are
+compress-zip_b200/libczg.so, which the Python binding (engine.py) loads, and
+compress-zip_b200/libczg_tok.so (tokenizer.py).
 """
 from __future__ import annotations
 
@@ -17,6 +19,9 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 OUT_DIR = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libczg.so")
+TOK_LIB = os.path.join(HERE, "libczg_tok.so")
+TOK_SRC = os.path.join(CSRC, "bpe_tokenizer.cpp")
+CXX = os.environ.get("CXX", "g++")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-I" + os.path.join(ROOT, "include"),
@@ -24,7 +29,21 @@ FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-I" + os.path
 
 
 def _sources():
-    return sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cu", ".cpp")))
+    return sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC)
+                  if f.endswith((".cu", ".cpp")) and os.path.join(CSRC, f) != TOK_SRC)
+
+
+def build_tokenizer() -> str:
+    """libczg_tok.so: host C++ only (no CUDA), so it also builds and runs without a GPU."""
+    deps = [TOK_SRC, os.path.join(CSRC, "unicode_classes.inc"), os.path.join(ROOT, "include", "czg_tok.h")]
+    if os.path.exists(TOK_LIB) and os.path.getmtime(TOK_LIB) >= max(os.path.getmtime(d) for d in deps):
+        return TOK_LIB
+    cmd = [CXX, "-O3", "-std=c++17", "-fPIC", "-shared", "-pthread", "-I" + os.path.join(ROOT, "include"),
+           "-I" + CSRC, TOK_SRC, "-o", TOK_LIB]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"{CXX} failed on {TOK_SRC}:\n{r.stdout}\n{r.stderr}")
+    return TOK_LIB
 
 
 def _headers_mtime():
@@ -55,8 +74,10 @@ def build(verbose: bool = False) -> str:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    build_tokenizer()
     if verbose:
         print(LIB)
+        print(TOK_LIB)
     return LIB
 
 
