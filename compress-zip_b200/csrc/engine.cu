@@ -30,19 +30,20 @@ void czg::kernels_init() {
     attention_init();
     attention_mma_init();
     gemm_tc_init();
+    head_cdf_init();
 }
 
 namespace {
 
 enum KernelClass {
     kRows = 0, kEmbedNorm, kGemmQkv, kKvPrep, kAttention, kGemmO, kResidualNorm, kGemmUp,
-    kGemmDown, kGemmHead, kCdf, kEncode, kPack, kKvAppend, kAttnDecode, kCdfDecode, kNumClasses
+    kGemmDown, kGemmHead, kCdf, kEncode, kPack, kKvAppend, kAttnDecode, kCdfDecode, kHeadCdf, kNumClasses
 };
 static_assert(kNumClasses <= CZG_MAX_KERNEL_CLASSES, "too many kernel classes");
 const char *kClassNames[kNumClasses] = {
     "rows", "embed_norm", "gemm_qkv", "kv_prep", "attention", "gemm_o", "residual_norm",
     "gemm_up_reglu", "gemm_down", "gemm_head", "cdf", "encode", "pack", "kv_append",
-    "attention_decode", "cdf_decode"};
+    "attention_decode", "cdf_decode", "head_cdf"};
 
 thread_local std::string g_create_error;
 
@@ -81,6 +82,7 @@ struct czg_ctx {
     bool kernel_timing = false;   // CUDA events around every kernel (czg_set_kernel_timing, CZG_KERNEL_TIMING=1)
     bool exp0 = false;           // lut4k[0] == 65535: exp of a zero difference needs no special case
     bool logit_small = false;    // every |logit| < 2^30: no logit difference wraps
+    bool head_cdf = false;       // the fused head GEMM + coder interval kernel applies
     int16_t *rope_cos = nullptr, *rope_sin = nullptr;
     std::vector<LayerDev> layers;
     std::vector<void *> allocs;
@@ -435,6 +437,10 @@ int alloc_workspace(czg_ctx *c, int rows, int chunks) {
         }
         if (!ok) c->use_tc = false;
     }
+    // fused head + coder interval: the shipped exp table, |logit| < 2^30, V a multiple of 256
+    const char *hc = getenv("CZG_HEAD_CDF");
+    c->head_cdf = c->use_tc && !(hc && std::string(hc) == "0") && c->exp0 && c->logit_small &&
+                  m.vocab_size == c->vpad && c->vpad % 256 == 0 && m.coef_q24 < (1u << 24) && d % 128 == 0;
     c->h_meta_bytes = (size_t)chunks * 32 + 64;
     if (!cuda_ok(c, cudaMallocHost(&c->h_meta, c->h_meta_bytes), "cudaMallocHost")) return CZG_E_DEVICE;
     return CZG_OK;
@@ -551,16 +557,25 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
     }
     if (tr && tr->final_in)
         cudaMemcpyAsync(tr->final_in, c->xn, (size_t)M * d, cudaMemcpyDeviceToHost, st);
-    timed(c, kGemmHead, [&] {
-        gemm(c, c->tm_xn, c->tm_head, c->xn, c->head_w, M, c->vpad, d, kEpiInt32, 1, 0, c->logits, c->vpad);
-    });
-    if (tr && tr->logits)
-        cudaMemcpy2DAsync(tr->logits, (size_t)V * 4, c->logits, (size_t)c->vpad * 4, (size_t)V * 4, M,
-                          cudaMemcpyDeviceToHost, st);
-    timed(c, kCdf, [&] {
-        launch_cdf_lohi(c->logits, V, c->vpad, c->tok_out, c->lut, c->lut4k, c->exp0 && c->logit_small, m.coef_q24, m.target_total, M,
-                        c->lohi, st);
-    });
+    bool fused = false;
+    if (c->head_cdf && !tr) {   // a trace wants the logits themselves
+        timed(c, kHeadCdf, [&] {
+            fused = launch_head_cdf(c->tm_xn, c->tm_head, M, V, d, c->tok_out, c->lut4k, m.coef_q24 << 8,
+                                    m.target_total, c->lohi, c->err_flag, st);
+        });
+    }
+    if (!fused) {
+        timed(c, kGemmHead, [&] {
+            gemm(c, c->tm_xn, c->tm_head, c->xn, c->head_w, M, c->vpad, d, kEpiInt32, 1, 0, c->logits, c->vpad);
+        });
+        if (tr && tr->logits)
+            cudaMemcpy2DAsync(tr->logits, (size_t)V * 4, c->logits, (size_t)c->vpad * 4, (size_t)V * 4, M,
+                              cudaMemcpyDeviceToHost, st);
+        timed(c, kCdf, [&] {
+            launch_cdf_lohi(c->logits, V, c->vpad, c->tok_out, c->lut, c->lut4k, c->exp0 && c->logit_small, m.coef_q24,
+                            m.target_total, M, c->lohi, st);
+        });
+    }
     if (tr && tr->lohi)
         cudaMemcpyAsync(tr->lohi, c->lohi, (size_t)M * 8, cudaMemcpyDeviceToHost, st);
     timed(c, kEncode, [&] {

@@ -52,6 +52,12 @@ struct TcMatrix {
 int tc_bn_for(int N);   // output tile width for N (0: unsupported)
 bool tc_make_matrix(TcMatrix &m, const int8_t *base, uint64_t rows, uint64_t K, int box_rows);
 void gemm_tc_init();
+// head_cdf.cu: the head GEMM and the coder interval in one kernel (A = final-norm
+// output, B = head weight as TcMatrix; V % 256 == 0, lut4k[0] == 65535, |logit| < 2^30).
+// false: unsupported shape, nothing launched.
+void head_cdf_init();
+bool launch_head_cdf(const TcMatrix &A, const TcMatrix &B, int M, int V, int K, const uint32_t *sym,
+                     const uint16_t *lut4k, uint32_t c8, uint32_t total, uint2 *lohi, int *err, cudaStream_t st);
 bool launch_gemm_tc(const TcMatrix &A, const TcMatrix &B, int M, int N, int K, int epi, int mult, int shift,
                     void *out, int ldo, int *err, cudaStream_t st);
 

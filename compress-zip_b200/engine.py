@@ -17,7 +17,7 @@ CZG_OK = 0
 STATUS_NAMES = {1: "CZG_E_ARG", 2: "CZG_E_MODEL", 3: "CZG_E_UNSUPPORTED", 4: "CZG_E_CAPACITY",
                 5: "CZG_E_DEVICE", 6: "CZG_E_TIMEOUT", 7: "CZG_E_TOKEN", 8: "CZG_E_CHUNK",
                 9: "CZG_E_LIMIT"}
-MAX_KERNEL_CLASSES = 16
+MAX_KERNEL_CLASSES = 24
 
 # The exported symbols of include/czg.h, checked by the CPU test suite.
 EXPORTS = ["czg_ctx_create", "czg_ctx_destroy", "czg_last_error", "czg_model_info_get",

@@ -52,7 +52,7 @@ typedef struct {
 /* Device-side timing of the last compress/decompress call, from CUDA events on
  * the context's stream.  kernel_ms[i] is the summed duration of kernel class i
  * (names from czg_kernel_name), launches[i] its launch count. */
-#define CZG_MAX_KERNEL_CLASSES 16
+#define CZG_MAX_KERNEL_CLASSES 24
 typedef struct {
     double total_ms;                 /* first launch to last completion, device clock */
     double h2d_ms, d2h_ms;           /* copies inside the call                        */
