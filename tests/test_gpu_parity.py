@@ -56,6 +56,31 @@ def test_trace_random_tokens(shipped_engine, shipped_oracle, oracle_mod):
     _trace_equal(shipped_engine, shipped_oracle, oracle_mod, toks)
 
 
+def test_head_cdf_fused_matches_unfused(shipped_path, monkeypatch):
+    """The fused head + coder-interval kernel against the head GEMM + CDF pair on the
+    same engine build: random token ids (unusual logit rows), ragged chunks and more
+    128-row blocks than SMs (several blocks per CTA, the per-quadrant mbarriers
+    cycling through their phases)."""
+    from compress_zip_b200.engine import Engine
+
+    rng = np.random.default_rng(17)
+    lens = rng.integers(1, 1025, 80)   # ~41 K rows: ~320 blocks of 128 over 148 SMs
+    starts = np.concatenate([[0], np.cumsum(lens)]).astype(np.uint64)
+    toks = rng.integers(0, 1024, int(starts[-1])).astype(np.uint32)
+    out = {}
+    for mode in ("0", "1"):
+        monkeypatch.setenv("CZG_HEAD_CDF", mode)
+        e = Engine.from_file(shipped_path, 0)
+        try:
+            e.set_kernel_timing(True)
+            out[mode] = e.compress_chunks(toks, starts)
+            stats = e.last_stats()["kernels"]
+            assert (stats["head_cdf"]["launches"] > 0) == (mode == "1")
+        finally:
+            e.close()
+    assert out["0"] == out["1"]
+
+
 @pytest.mark.parametrize("C", [64, 1024])
 def test_compress_bytes_match_oracle(shipped_engine, shipped_oracle, oracle_mod, shipped_tokens, C):
     starts = _starts(len(shipped_tokens), C)
