@@ -440,7 +440,7 @@ int alloc_workspace(czg_ctx *c, int rows, int chunks) {
     // fused head + coder interval: the shipped exp table, |logit| < 2^30, V a multiple of 256
     const char *hc = getenv("CZG_HEAD_CDF");
     c->head_cdf = c->use_tc && !(hc && std::string(hc) == "0") && c->exp0 && c->logit_small &&
-                  m.vocab_size == c->vpad && c->vpad % 256 == 0 && m.coef_q24 < (1u << 24) && d % 128 == 0;
+                  m.vocab_size == c->vpad && c->vpad % 256 == 0 && m.coef_q24 < (1u << 23) && d % 128 == 0;
     c->h_meta_bytes = (size_t)chunks * 32 + 64;
     if (!cuda_ok(c, cudaMallocHost(&c->h_meta, c->h_meta_bytes), "cudaMallocHost")) return CZG_E_DEVICE;
     return CZG_OK;

@@ -21,7 +21,7 @@
 // through a per-quadrant mbarrier.  Every wait is bounded (kErrTimeout, as
 // gemm_tc.cu).  The epilogue (about 34 instructions per logit over the three
 // passes) is the limit, not the tensor pipe (26% busy) or L2 (25%).
-// Needs V % 256 == 0, K % 128 == 0, lut4k[0] == 65535 and |logit| < 2^30.
+// Needs V % 256 == 0, K % 128 == 0, lut4k[0] == 65535, |logit| < 2^30, coef < 2^23.
 // No TMA load here uses cluster multicast.
 #include "kernels.h"
 #include "tc_common.cuh"
@@ -44,9 +44,11 @@ constexpr int HC_BARS = 2 * HC_STAGES + 5 + 12;
 constexpr size_t HC_SMEM = 1024 + (size_t)HC_STAGES * HC_STAGE + HC_LUT * 2 + (size_t)HC_XCHG_WORDS * 4 +
                            (size_t)HC_BARS * 8 + 16;
 
-__device__ __forceinline__ uint32_t weight_of(int mx, int x, const uint16_t *lut, uint32_t c8) {
-    const uint32_t neg = (uint32_t)mx - (uint32_t)x;   // >= 0: mx is the row maximum
-    return lut[min((uint32_t)(((unsigned long long)neg * c8 + 0x80000000ull) >> 32), 4096u)];
+// exp_q16 of (x - row max) by table: t256 = floor(((max - x) * coef + 2^23) / 2^24) is the
+// high word of krow - x * (coef << 8), krow = max * (coef << 8) + 2^31 (one 64-bit product;
+// coef < 2^23 and |x| < 2^30 keep it inside int64 and the word non-negative).
+__device__ __forceinline__ uint32_t weight_of(long long krow, int x, const uint16_t *lut, int nc8) {
+    return lut[min((uint32_t)(((long long)x * nc8 + krow) >> 32), 4096u)];
 }
 
 __global__ void __launch_bounds__(HC_THREADS, 1)
@@ -163,6 +165,8 @@ k_head_cdf(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CU
     } else {   // epilogue: one row per lane
         const int q = warp & 3, h = (warp - 2) >> 2;
         const uint32_t R = total - (uint32_t)V;
+        const int nc8 = -(int)c8;
+        long long krow = 0;
         int mx = INT32_MIN, mb = INT32_MIN, xs = INT32_MIN;
         uint32_t S = 0, f_all = 0, f_below = 0, f_sym = 0, sy = 0;
         FreqDiv fd{};
@@ -207,17 +211,17 @@ k_head_cdf(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CU
                     }
                 } else if (pass == 1) {
 #pragma unroll
-                    for (int k = 0; k < 32; k++) S += weight_of(mx, (int)x[k], lut, c8);
+                    for (int k = 0; k < 32; k++) S += weight_of(krow, (int)x[k], lut, nc8);
                 } else if (!holds_sym) {
                     uint32_t fs = 0;
 #pragma unroll
-                    for (int k = 0; k < 32; k++) fs += freq_of(weight_of(mx, (int)x[k], lut, c8), fd);
+                    for (int k = 0; k < 32; k++) fs += freq_of(weight_of(krow, (int)x[k], lut, nc8), fd);
                     f_all += fs;
                     if (whole_below) f_below += fs;
                 } else {
 #pragma unroll
                     for (int k = 0; k < 32; k++) {
-                        const uint32_t f = freq_of(weight_of(mx, (int)x[k], lut, c8), fd);
+                        const uint32_t f = freq_of(weight_of(krow, (int)x[k], lut, nc8), fd);
                         f_all += f;
                         if (c0 + k < sy) f_below += f;
                         if (c0 + k == sy) f_sym = f;
@@ -253,6 +257,7 @@ k_head_cdf(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CU
             }
             if (pass == 0) {
                 mx = m0v; mb = m1v; xs = m2v;   // a real logit is never INT32_MIN (|logit| < 2^30)
+                krow = (long long)mx * (long long)c8 + 0x80000000ll;
             } else if (pass == 1) {
                 S = a0;
                 fd = make_freq_div(R, S);
