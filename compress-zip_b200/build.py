@@ -21,6 +21,8 @@ OUT_DIR = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libczg.so")
 TOK_LIB = os.path.join(HERE, "libczg_tok.so")
 TOK_SRC = os.path.join(CSRC, "bpe_tokenizer.cpp")
+CLI_SRC = os.path.join(CSRC, "czg_cli.cpp")
+CLI = os.path.join(HERE, "czg-cli")
 CXX = os.environ.get("CXX", "g++")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -30,7 +32,7 @@ FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-I" + os.path
 
 def _sources():
     return sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC)
-                  if f.endswith((".cu", ".cpp")) and os.path.join(CSRC, f) != TOK_SRC)
+                  if f.endswith((".cu", ".cpp")) and os.path.join(CSRC, f) not in (TOK_SRC, CLI_SRC))
 
 
 def build_tokenizer() -> str:
@@ -63,6 +65,21 @@ def _compile(src, hdr_mtime):
     return obj
 
 
+def build_cli() -> str:
+    """czg-cli: the native compress / decompress command line over both libraries."""
+    deps = [CLI_SRC, os.path.join(CSRC, "czm_parse.cpp"), LIB, TOK_LIB,
+            os.path.join(ROOT, "include", "czg.h"), os.path.join(ROOT, "include", "czg_tok.h")]
+    if os.path.exists(CLI) and os.path.getmtime(CLI) >= max(os.path.getmtime(d) for d in deps):
+        return CLI
+    cmd = [CXX, "-O2", "-std=c++17", "-I" + os.path.join(ROOT, "include"), "-I" + CSRC, CLI_SRC,
+           os.path.join(CSRC, "czm_parse.cpp"), "-L" + HERE, "-l:libczg.so", "-l:libczg_tok.so", "-ldl",
+           "-Wl,-rpath,$ORIGIN", "-o", CLI]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"{CXX} failed on {CLI_SRC}:\n{r.stdout}\n{r.stderr}")
+    return CLI
+
+
 def build(verbose: bool = False) -> str:
     os.makedirs(OUT_DIR, exist_ok=True)
     hm = _headers_mtime()
@@ -75,6 +92,7 @@ def build(verbose: bool = False) -> str:
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
     build_tokenizer()
+    build_cli()
     if verbose:
         print(LIB)
         print(TOK_LIB)

@@ -51,3 +51,57 @@ def test_cli_errors(tmp_path, shipped_path):
     assert cli.main(["compress", "-m", shipped_path, "-i", str(empty), "-o", str(out), "-L", "3"]) == 0
     assert cli.main(["decompress", "-m", shipped_path, "-i", str(out), "-o", str(tmp_path / "e.txt")]) == 0
     assert (tmp_path / "e.txt").read_bytes() == b""
+
+
+@pytest.mark.parametrize("codec,level", [("brotli", None), ("zstd", 1), ("brotli", 4)])
+def test_native_cli_matches_python_cli(tmp_path, shipped_path, root, codec, level):
+    """czg-cli writes the same .czip bytes as the Python host layer, and each
+    decompresses the other's file back to the input text."""
+    import os
+    import subprocess
+
+    from compress_zip_b200 import cli, synth
+
+    exe = os.path.join(root, "compress-zip_b200", "czg-cli")
+    text = synth.document(11, 20000) + "\n<|eos|>tail é中\U0001F600\n"
+    src = tmp_path / "in.txt"
+    src.write_bytes(text.encode())
+    py_out, nat_out = tmp_path / "py.czip", tmp_path / "nat.czip"
+    cli.compress(shipped_path, None, str(src), str(py_out), codec, level)
+    args = [exe, "compress", "-m", shipped_path, "-i", str(src), "-o", str(nat_out), "-c", codec]
+    if level:
+        args += ["-L", str(level)]
+    r = subprocess.run(args, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr
+    assert nat_out.read_bytes() == py_out.read_bytes()
+    for f in (py_out, nat_out):
+        back = tmp_path / (f.name + ".txt")
+        r = subprocess.run([exe, "decompress", "-m", shipped_path, "-i", str(f), "-o", str(back)],
+                           capture_output=True, text=True, timeout=600)
+        assert r.returncode == 0, r.stderr
+        assert back.read_bytes() == text.encode()
+
+
+def test_native_cli_errors(tmp_path, shipped_path, root):
+    import os
+    import subprocess
+
+    exe = os.path.join(root, "compress-zip_b200", "czg-cli")
+    bad_text = tmp_path / "bad.txt"
+    bad_text.write_bytes(b"ok \xff\xfe not utf-8")
+    r = subprocess.run([exe, "compress", "-m", shipped_path, "-i", str(bad_text), "-o", str(tmp_path / "o")],
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 1 and "UTF-8" in r.stderr   # main.rs:170 reads with read_to_string
+    bad = tmp_path / "bad.czip"
+    bad.write_bytes(b"NOTCZIP" + bytes(20))
+    r = subprocess.run([exe, "decompress", "-m", shipped_path, "-i", str(bad), "-o", str(tmp_path / "x")],
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 1
+    empty = tmp_path / "empty.txt"
+    empty.write_bytes(b"")
+    out = tmp_path / "e.czip"
+    assert subprocess.run([exe, "compress", "-m", shipped_path, "-i", str(empty), "-o", str(out), "-L", "3"],
+                          capture_output=True, timeout=600).returncode == 0
+    assert subprocess.run([exe, "decompress", "-m", shipped_path, "-i", str(out), "-o", str(tmp_path / "e.txt")],
+                          capture_output=True, timeout=600).returncode == 0
+    assert (tmp_path / "e.txt").read_bytes() == b""
