@@ -461,7 +461,7 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
 #pragma unroll
         for (int e = 0; e < 2; e++) {
             const uint32_t sv = s_state[e] + 256u * (uint32_t)shs[e] + (uint32_t)sls[e];
-            const unsigned long long den = sv == 0 ? 1ull : sv;
+            const RneDiv dv = make_rne_div(sv == 0 ? 1ull : sv);
             uint8_t *orow = ostage + (2 * t + e) * 64;
 #pragma unroll
             for (int mi = 0; mi < 4; mi++)
@@ -469,7 +469,7 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
                 for (int dh = 0; dh < 2; dh++) {
                     const int k = 2 * dh + e;
                     const int x = (int)(((uint32_t)hiacc[mi][k] << 8) + (uint32_t)loacc[mi][k]);
-                    orow[16 * mi + g + 8 * dh] = (uint8_t)clamp127(div_rne_s32_u64(x, den));
+                    orow[16 * mi + g + 8 * dh] = (uint8_t)clamp127(div_rne_s32_by(x, dv));
                 }
         }
         __syncwarp();
@@ -503,6 +503,13 @@ __device__ __forceinline__ void decode_tile_async(uint8_t *stage, const int8_t *
 // the stream's keys 0..p in the split cache layout (K rows of 64 permuted dims,
 // then V in 2 KB tiles of 32 keys as [8 key groups][64 dims][4 keys]).  The heads are the 8 rows of the attention tile (A rows
 // n_heads..15 are zero); everything else is the chunk kernel's tile step.
+// Persistent: one CTA per SM, warp w takes streams w, w + W, w + 2W, ... (W the
+// warps of the grid).  A warp's tiles, stream after stream, flow through a ring of
+// DEC_STAGES 4 KB shared-memory stages with DEC_STAGES - 1 tile copies in flight,
+// so the first tiles of the next stream load while the current one finishes.
+constexpr int DEC_STAGES = 2;
+constexpr int DEC_SMEM = AM_WARPS * DEC_STAGES * 4096 + AM_LUT * 2;
+
 template <bool WIDE, bool EXP0>
 __global__ void __launch_bounds__(AM_THREADS, 1)
 k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restrict__ kvc, size_t cache_ld,
@@ -511,25 +518,43 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__
                        const int16_t *__restrict__ rope_sin, const uint16_t *__restrict__ lut4k_g,
                        int8_t *__restrict__ out, int ldo) {
     __shared__ __align__(16) uint8_t wsm[AM_WARPS * AM_WARP_SMEM];
-    extern __shared__ __align__(16) uint8_t dsm[];   // per warp: two 4 KB tile stages; then the exp table
+    extern __shared__ __align__(16) uint8_t dsm[];   // per warp: DEC_STAGES 4 KB tile stages; then the exp table
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, t = lane & 3;
-    uint16_t *lut_s = reinterpret_cast<uint16_t *>(dsm + AM_WARPS * 8192);
+    uint16_t *lut_s = reinterpret_cast<uint16_t *>(dsm + AM_WARPS * DEC_STAGES * 4096);
     for (int i = tid; i < AM_LUT; i += AM_THREADS) lut_s[i] = lut4k_g[i];
     __syncthreads();
     const uint16_t *lut4k = lut_s;
-    const int r = blockIdx.x * AM_WARPS + warp;
+    const int stride = gridDim.x * AM_WARPS;
+    int r = blockIdx.x * AM_WARPS + warp;
     if (r >= M) return;
-    uint8_t *stages = dsm + warp * 8192;
+    uint8_t *stages = dsm + warp * (DEC_STAGES * 4096);
     uint32_t *rec_e = reinterpret_cast<uint32_t *>(wsm + warp * AM_WARP_SMEM);   // [8][32]
     uint8_t *ostage = reinterpret_cast<uint8_t *>(rec_e + AM_ROWS * 32);         // [8][64]
     const size_t len = cache_ld / 128;
-    const int8_t *ks = kvc + (size_t)r * cache_ld;    // [len][64], dims permuted
-    const int8_t *vt = ks + len * 64;                 // V tiles
     const uint32_t c8 = 378194u << 8;   // ATTN_COEF_Q24 (attention.rs:14-19) << 8
     const uint32_t ones[4] = {0x01010101u, 0x01010101u, 0x01010101u, 0x01010101u};
     const bool head = g < n_heads;   // row g of the tile is head g
     const int mult = head ? score_mult[g] : 0;
+    const int ntiles = (p >> 5) + 1;
+
+    // the tile sequence (stream fr, tile fk), its next copy going to stage fslot;
+    // past the warp's last tile an empty group keeps the group count in step
+    int fr = r, fk = 0, fslot = 0, cslot = 0;
+    auto fetch = [&]() {
+        if (fr < M) {
+            const int8_t *k0 = kvc + (size_t)fr * cache_ld;   // [len][64] K rows, then the V tiles
+            decode_tile_async(stages + fslot * 4096, k0, k0 + len * 64, 32 * fk, lane);
+            if (++fk == ntiles) { fk = 0; fr += stride; }
+        } else {
+            asm volatile("cp.async.commit_group;" ::: "memory");
+        }
+        fslot = fslot + 1 == DEC_STAGES ? 0 : fslot + 1;
+    };
+#pragma unroll
+    for (int i = 0; i < DEC_STAGES - 1; i++) fetch();
+
+    for (; r < M; r += stride) {
 
     // Q fragment of head g at position p with RoPE (attention.rs:53-83)
     uint32_t qa[2][4];
@@ -579,17 +604,13 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__
         for (int k = 0; k < 4; k++) { hiacc[mi][k] = 0; loacc[mi][k] = 0; }
     int shs[4] = {0, 0, 0, 0}, sls[4] = {0, 0, 0, 0};
 
-    decode_tile_async(stages, ks, vt, 0, lane);   // tile 0 in flight
     for (int kb = 0; kb <= p; kb += 32) {
-        // the next tile's copy overlaps this tile's work; then wait for this one
-        if (kb + 32 <= p) {
-            decode_tile_async(stages + (((kb >> 5) + 1) & 1) * 4096, ks, vt, kb + 32, lane);
-            asm volatile("cp.async.wait_group 1;" ::: "memory");
-        } else {
-            asm volatile("cp.async.wait_group 0;" ::: "memory");
-        }
+        // keep DEC_STAGES - 1 copies in flight ahead of this tile, then wait for it
+        fetch();
+        asm volatile("cp.async.wait_group %0;" ::"n"(DEC_STAGES - 1) : "memory");
         __syncwarp();
-        const uint8_t *kst = stages + ((kb >> 5) & 1) * 4096;   // K rows of the tile, then the V tile
+        const uint8_t *kst = stages + cslot * 4096;   // K rows of the tile, then the V tile
+        cslot = cslot + 1 == DEC_STAGES ? 0 : cslot + 1;
         int sacc[4][4];
 #pragma unroll
         for (int j = 0; j < 4; j++) {
@@ -673,7 +694,7 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__
 #pragma unroll
     for (int e = 0; e < 2; e++) {
         const unsigned long long sv = s_state[e] + 256ull * (uint32_t)shs[e] + (unsigned long long)(uint32_t)sls[e];
-        const unsigned long long den = sv == 0 ? 1ull : sv;
+        const RneDiv dv = make_rne_div(sv == 0 ? 1ull : sv);
         uint8_t *orow = ostage + (2 * t + e) * 64;
 #pragma unroll
         for (int mi = 0; mi < 4; mi++)
@@ -681,7 +702,7 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__
             for (int dh = 0; dh < 2; dh++) {
                 const int k = 2 * dh + e;
                 const int x = (int)(((uint32_t)hiacc[mi][k] << 8) + (uint32_t)loacc[mi][k]);
-                orow[16 * mi + g + 8 * dh] = (uint8_t)clamp127(div_rne_s32_u64(x, den));
+                orow[16 * mi + g + 8 * dh] = (uint8_t)clamp127(div_rne_s32_by(x, dv));
             }
     }
     __syncwarp();
@@ -691,6 +712,9 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__
             *reinterpret_cast<uint4 *>(out + (size_t)r * ldo + hd * 64 + 16 * part) =
                 *reinterpret_cast<const uint4 *>(ostage + hd * 64 + 16 * part);
     }
+    __syncwarp();   // ostage and rec_e are reused by the next stream
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
 }  // namespace
@@ -704,9 +728,9 @@ size_t attention_mma_smem(int max_len) {
 bool attention_mma_fits(int max_len) { return max_len <= AM_MAX_KEYS; }
 
 void attention_mma_init() {
-    cudaFuncSetAttribute(k_attention_decode_mma<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, AM_WARPS * 8192 + AM_LUT * 2);
-    cudaFuncSetAttribute(k_attention_decode_mma<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, AM_WARPS * 8192 + AM_LUT * 2);
-    cudaFuncSetAttribute(k_attention_decode_mma<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, AM_WARPS * 8192 + AM_LUT * 2);
+    cudaFuncSetAttribute(k_attention_decode_mma<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM);
+    cudaFuncSetAttribute(k_attention_decode_mma<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM);
+    cudaFuncSetAttribute(k_attention_decode_mma<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM);
     const int smem = (int)attention_mma_smem(AM_MAX_KEYS);
     cudaFuncSetAttribute(k_attention_mma<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     cudaFuncSetAttribute(k_attention_mma<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -741,15 +765,15 @@ void launch_attention_decode_mma(const int8_t *qkv, int ldq, const int8_t *kvc, 
                                  const int16_t *rope_cos, const int16_t *rope_sin, const uint16_t *lut4k,
                                  bool wide_mult, bool exp0, int8_t *out, int ldo, cudaStream_t st) {
     if (M == 0) return;
-    const unsigned grid = (unsigned)((M + AM_WARPS - 1) / AM_WARPS);
+    const unsigned grid = (unsigned)std::min<long>((M + AM_WARPS - 1) / AM_WARPS, (long)sm_count());
     if (wide_mult)
-        k_attention_decode_mma<true, false><<<grid, AM_THREADS, AM_WARPS * 8192 + AM_LUT * 2, st>>>(
+        k_attention_decode_mma<true, false><<<grid, AM_THREADS, DEC_SMEM, st>>>(
             qkv, ldq, kvc, cache_ld, M, p, n_heads, score_mult, sink_key, rope_cos, rope_sin, lut4k, out, ldo);
     else if (exp0)
-        k_attention_decode_mma<false, true><<<grid, AM_THREADS, AM_WARPS * 8192 + AM_LUT * 2, st>>>(
+        k_attention_decode_mma<false, true><<<grid, AM_THREADS, DEC_SMEM, st>>>(
             qkv, ldq, kvc, cache_ld, M, p, n_heads, score_mult, sink_key, rope_cos, rope_sin, lut4k, out, ldo);
     else
-        k_attention_decode_mma<false, false><<<grid, AM_THREADS, AM_WARPS * 8192 + AM_LUT * 2, st>>>(
+        k_attention_decode_mma<false, false><<<grid, AM_THREADS, DEC_SMEM, st>>>(
             qkv, ldq, kvc, cache_ld, M, p, n_heads, score_mult, sink_key, rope_cos, rope_sin, lut4k, out, ldo);
 }
 

@@ -13,6 +13,20 @@ constexpr int kHeadDim = 64;
 constexpr int kHalfDim = 32;
 constexpr uint32_t kBos = 1022u;   // rust/src/main.rs:214
 
+// SMs of the current device (cached per device): persistent grids are sized by it
+inline int sm_count() {
+    static int cached[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return 148;
+    if (!cached[dev]) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        cached[dev] = n > 0 ? n : 148;
+    }
+    return cached[dev];
+}
+
 // primitives.rs:9-11
 __device__ __forceinline__ int clamp127(int x) { return min(127, max(-127, x)); }
 
@@ -150,6 +164,35 @@ __device__ __forceinline__ int div_rne_s32_u64(int num, unsigned long long den) 
     else if (tr == den) q += (q & 1ull);
     uint32_t q32 = (uint32_t)q;
     return (int)(neg ? 0u - q32 : q32);
+}
+
+// div_rne_s32_u64 for many numerators over one denominator.  A denominator of
+// 2^32 or more gives 0 for every |num| <= 2^31 (the doubled remainder never
+// exceeds it, and a tie rounds to the even 0).  Below that, inv = floor((2^32-1)/d)
+// makes umulhi(|num|, inv) at most one below floor(|num| / d) for |num| <= 2^31,
+// so one correction step gives the exact quotient and remainder.
+struct RneDiv {
+    uint32_t d, inv;
+};
+
+__device__ __forceinline__ RneDiv make_rne_div(unsigned long long den) {
+    RneDiv v;
+    v.d = den > 0xFFFFFFFFull ? 0u : (uint32_t)den;   // 0: every quotient is 0
+    v.inv = v.d ? 0xFFFFFFFFu / v.d : 0u;
+    return v;
+}
+
+__device__ __forceinline__ int div_rne_s32_by(int num, RneDiv v) {
+    if (v.d == 0u) return 0;
+    const bool neg = num < 0;
+    const uint32_t an = neg ? 0u - (uint32_t)num : (uint32_t)num;
+    uint32_t q = __umulhi(an, v.inv);
+    uint32_t r = an - q * v.d;
+    if (r >= v.d) { q += 1u; r -= v.d; }
+    const uint32_t half = v.d - r;   // 2r > d  <=>  r > d - r
+    if (r > half) q += 1u;
+    else if (r == half) q += q & 1u;
+    return (int)(neg ? 0u - q : q);
 }
 
 // floor(a / d) for a < 2^62 and d > 0 given inv = floor((2^64 - 1) / d):

@@ -138,18 +138,5 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-int sm_count() {
-    static int cached[64] = {0};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64) return 148;
-    if (!cached[dev]) {
-        int n = 0;
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        cached[dev] = n > 0 ? n : 148;
-    }
-    return cached[dev];
-}
-
 }  // namespace
 }  // namespace czg
