@@ -56,6 +56,8 @@ def parse():
                     help="config 3: documents of 4,096 B decoded at ctx 512 (0 skips)")
     ap.add_argument("--pipeline-docs", type=int, default=64,
                     help="host pipeline sample (tokenise + GPU coder + CZIPv1 + brotli); 0 skips")
+    ap.add_argument("--config2-docs", type=int, default=256,
+                    help="config 2: documents of 64 KiB compressed with the arch-2 model at ctx 512 (0 skips)")
     return ap.parse_args()
 
 
@@ -293,6 +295,7 @@ def main():
     parity = bytes(h_out_np[:nout_h]) == bytes(out[:nout])
 
     dec = decode_bench(eng, mf, rank, args, stream, world) if args.decode_docs > 0 else None
+    cfg2 = config2_bench(mf, rank, args, stream, local) if args.config2_docs > 0 else None
     pipe = host_pipeline(eng, mf, args) if rank == 0 and args.pipeline_docs > 0 else None
 
     (t_max, t_e2e_max), (all_tok, all_bytes) = reduce_over_ranks(
@@ -357,6 +360,8 @@ def main():
         }
         if dec is not None:
             line["decode"] = dec
+        if cfg2 is not None:
+            line["config2"] = cfg2
         if pipe is not None:
             line["host_pipeline"] = pipe
         if cpu is not None:
@@ -365,6 +370,76 @@ def main():
     eng.close()
     if world > 1:
         dist.destroy_process_group()
+
+
+def config2_bench(mf, rank, args, stream, local):
+    """documents of 64 KiB (seeds 3000.., rank r: +r*N)
+    compressed at ctx 512 with the arch-2 model (d 512, 8 layers, 8 heads, 2 KV
+    heads, d_ff 2048; synthetic int8 weights from seed 7, compress_zip_b200/synth.py).
+    Tokens resident in HBM, L2 flushed before each timed step, CUDA events on the
+    engine's stream; the per-kernel split gives the GEMMs' int8 tensor throughput.
+    Each rank reports its own figure (no collective here)."""
+    import torch
+    from compress_zip_b200.engine import Engine
+
+    model = synth.arch2_model(mf, 512)
+    a = synth.ARCH2
+    tok = mf.tokenizer()
+    docs = synth.documents(shard_seeds(rank, args.config2_docs, first=3000), 65536)
+    ids = tok.encode_batch_arrays(docs, num_threads=min(16, os.cpu_count() or 1))
+    starts, b = [0], 0
+    for t in ids:
+        for s0 in range(0, len(t), 512):
+            starts.append(b + min(s0 + 512, len(t)))
+        b += len(t)
+    tokens = np.concatenate([np.asarray(t, dtype=np.uint32) for t in ids])
+    starts = np.asarray(starts, dtype=np.uint64)
+    n_tok, n_chunks = int(len(tokens)), int(len(starts) - 1)
+    eng = Engine(model, local)
+    try:
+        eng.set_stream(stream.cuda_stream)
+        d_tokens = torch.from_numpy(tokens.view(np.int32)).to(f"cuda:{local}")
+        out = np.empty(4 * n_tok + 8 * n_chunks, dtype=np.uint8)
+        lens = np.empty(n_chunks, dtype=np.uint32)
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=f"cuda:{local}")
+        eng.set_kernel_timing(True)
+        eng.compress_device(d_tokens.data_ptr(), starts, out, lens)   # warm-up
+        torch.cuda.synchronize()
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        steps = max(1, min(args.steps, 2))
+        times, kern = [], {}
+        for _ in range(steps):
+            flush.zero_()
+            ev0.record(stream)
+            eng.compress_device(d_tokens.data_ptr(), starts, out, lens)
+            ev1.record(stream)
+            torch.cuda.synchronize()
+            times.append(ev0.elapsed_time(ev1))
+            for k, v in eng.last_stats()["kernels"].items():
+                kern[k] = kern.get(k, 0.0) + v["ms"]
+    finally:
+        eng.close()
+    t = sum(times)
+    d, dff, kvd, L, V = a["d_model"], a["d_ff"], a["n_kv_heads"] * 64, a["n_layers"], a["vocab_size"]
+    macs = {"gemm_qkv": (d + 2 * kvd) * d * L, "gemm_o": d * d * L, "gemm_up_reglu": 2 * dff * d * L,
+            "gemm_down": d * dff * L, "head_cdf": V * d, "gemm_head": V * d}
+    gemm_ms = sum(kern.get(k, 0.0) for k in macs)
+    gemm_ops = sum(2.0 * m * n_tok * steps for k, m in macs.items() if kern.get(k, 0.0) > 0)
+    _, _, bf16_sus, basis = peaks()
+    tops = gemm_ops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else 0.0
+    return {"metric": "compress tokens/s (config 2: arch-2 model, ctx 512, 64 KiB docs)",
+            "value": round(n_tok * steps / (t / 1e3), 1), "unit": "tokens/s", "steps": steps,
+            "ms_per_step": round(t / steps, 3), "docs_per_gpu": args.config2_docs, "tokens_per_gpu": n_tok,
+            "chunks_per_gpu": n_chunks,
+            "mb_per_s": round(sum(len(x.encode()) for x in docs) * steps / (t / 1e3) / 1e6, 3),
+            "kernels_ms_per_step": {k: round(v / steps, 3) for k, v in kern.items() if v > 0},
+            "gemm_tensor": {"achieved": round(tops, 1), "unit": "TOP/s (int8, 2 x MACs)",
+                            "peak": round(2.0 * bf16_sus, 1), "frac": round(tops / (2.0 * bf16_sus), 4),
+                            "peak_basis": f"2 x bf16_tflops_sustained {basis} (dense int8 = 2 x bf16)",
+                            "kernels": "QKV, O, up+ReGLU, down GEMMs and the head GEMM of head_cdf, "
+                                       "CUDA-event time per class"},
+            "model": "arch-2 synthetic (d 512, 8 layers, 8 heads, 2 KV heads, d_ff 2048, V 1024)"}
 
 
 def decode_bench(eng, mf, rank, args, stream, world):

@@ -512,7 +512,8 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
                     c->pos, c->err_flag, st);
     });
     timed(c, kEmbedNorm, [&] {
-        launch_embed_norm(c->tok_in, c->embed, c->layers[0].attn_norm, M, d, c->inv_tab, c->x_res, c->res16, c->xn, st);
+        launch_embed_norm(c->tok_in, c->embed, c->layers[0].attn_norm, M, d, c->inv_tab, c->x_res, c->res16, false,
+                          c->xn, st);
     });
     for (int l = 0; l < m.n_layers; l++) {
         const LayerDev &L = c->layers[l];
@@ -540,7 +541,8 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
                  c->o8, d);
         });
         timed(c, kResidualNorm, [&] {
-            launch_residual_norm(c->o8, L.ffn_norm, L.post_attn_norm, M, d, c->inv_tab, c->x_res, c->res16, c->xn, st);
+            launch_residual_norm(c->o8, L.ffn_norm, L.post_attn_norm, M, d, c->inv_tab, c->tok_in,
+                                 l == 0 ? c->embed : nullptr, true, c->x_res, c->res16, c->xn, st);
         });
         timed(c, kGemmUp, [&] {
             gemm(c, c->tm_xn, L.tm_up, c->xn, L.up_w, M, 2 * dff, d, kEpiReglu, L.up_mult, L.up_shift,
@@ -552,7 +554,8 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
         });
         const int8_t *next = l + 1 < m.n_layers ? c->layers[l + 1].attn_norm : c->final_norm;
         timed(c, kResidualNorm, [&] {
-            launch_residual_norm(c->o8, L.post_ffn_norm, next, M, d, c->inv_tab, c->x_res, c->res16, c->xn, st);
+            launch_residual_norm(c->o8, L.post_ffn_norm, next, M, d, c->inv_tab, c->tok_in, nullptr,
+                                 l + 1 < m.n_layers, c->x_res, c->res16, c->xn, st);
         });
     }
     if (tr && tr->final_in)
@@ -807,7 +810,8 @@ int decompress_impl(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts
             while (active > 0 && (int)n_tokens[order[w0 + active - 1]] <= step) active--;
             const int M = active;
             timed(c, kEmbedNorm, [&] {
-                launch_embed_norm(c->tok_in, c->embed, c->layers[0].attn_norm, M, d, c->inv_tab, c->x_res, c->res16, c->xn, s);
+                launch_embed_norm(c->tok_in, c->embed, c->layers[0].attn_norm, M, d, c->inv_tab, c->x_res, c->res16,
+                                  false, c->xn, s);
             });
             for (int l = 0; l < m.n_layers; l++) {
                 const LayerDev &L = c->layers[l];
@@ -833,7 +837,8 @@ int decompress_impl(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts
                          c->o8, d);
                 });
                 timed(c, kResidualNorm, [&] {
-                    launch_residual_norm(c->o8, L.ffn_norm, L.post_attn_norm, M, d, c->inv_tab, c->x_res, c->res16, c->xn, s);
+                    launch_residual_norm(c->o8, L.ffn_norm, L.post_attn_norm, M, d, c->inv_tab, c->tok_in,
+                                         l == 0 ? c->embed : nullptr, true, c->x_res, c->res16, c->xn, s);
                 });
                 timed(c, kGemmUp, [&] {
                     gemm(c, c->tm_xn, L.tm_up, c->xn, L.up_w, M, 2 * dff, d, kEpiReglu, L.up_mult, L.up_shift,
@@ -845,7 +850,8 @@ int decompress_impl(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts
                 });
                 const int8_t *next = l + 1 < m.n_layers ? c->layers[l + 1].attn_norm : c->final_norm;
                 timed(c, kResidualNorm, [&] {
-                    launch_residual_norm(c->o8, L.post_ffn_norm, next, M, d, c->inv_tab, c->x_res, c->res16, c->xn, s);
+                    launch_residual_norm(c->o8, L.post_ffn_norm, next, M, d, c->inv_tab, c->tok_in, nullptr,
+                                         l + 1 < m.n_layers, c->x_res, c->res16, c->xn, s);
                 });
             }
             timed(c, kGemmHead, [&] {

@@ -21,10 +21,16 @@ void launch_rows(const uint32_t *tokens, const int *chunk_row0, const int *chunk
 // x_res: the residual stream, int16 when res16 (exact for n_layers <= 128), else int32
 constexpr int kInvTabEntries = 16384;
 void launch_inv_table(int eps, uint16_t *tab, cudaStream_t st);
+// store_res false: x_res is not written (the residual of layer 0 is then re-read from
+// the embedding by the first residual norm, whose embed / tok_in are given)
 void launch_embed_norm(const uint32_t *tok_in, const int8_t *embed, const int8_t *norm_w, int M,
-                       int d, const uint16_t *inv_tab, void *x_res, bool res16, int8_t *xn, cudaStream_t st);
+                       int d, const uint16_t *inv_tab, void *x_res, bool res16, bool store_res, int8_t *xn,
+                       cudaStream_t st);
+// embed != nullptr: the residual input is embed[tok_in[r]] instead of x_res;
+// store_res false: the updated residual is not written back (the model's last norm)
 void launch_residual_norm(const int8_t *o, const int8_t *post_w, const int8_t *next_w, int M, int d,
-                          const uint16_t *inv_tab, void *x_res, bool res16, int8_t *xn, cudaStream_t st);
+                          const uint16_t *inv_tab, const uint32_t *tok_in, const int8_t *embed, bool store_res,
+                          void *x_res, bool res16, int8_t *xn, cudaStream_t st);
 void launch_kv_prep(const int8_t *qkv, int ldq, int d, const int *pos, const int16_t *rope_cos,
                     const int16_t *rope_sin, int M, int8_t *kv, cudaStream_t st);
 

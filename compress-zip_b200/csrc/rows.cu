@@ -78,8 +78,10 @@ __device__ __forceinline__ void store_res4(int16_t *p, int4 v) {
                                                ((uint32_t)v.z & 0xFFFFu) | ((uint32_t)v.w << 16));
 }
 
-// x_res[r] = embed[tok_in[r]] (residual), xn[r] = norm(clamp(x_res[r]))
-template <int NW, typename RT>
+// x_res[r] = embed[tok_in[r]] (residual), xn[r] = norm(clamp(x_res[r])).  STORE
+// false: the residual is not written (the first residual norm then reads the
+// embedding row again, which stays in L2, instead of x_res from HBM).
+template <int NW, typename RT, bool STORE>
 __global__ void k_embed_norm(const uint32_t *__restrict__ tok_in, const int8_t *__restrict__ embed,
                              const int8_t *__restrict__ norm_w, int M, const uint16_t *__restrict__ inv_tab,
                              RT *__restrict__ x_res, int8_t *__restrict__ xn) {
@@ -95,10 +97,13 @@ __global__ void k_embed_norm(const uint32_t *__restrict__ tok_in, const int8_t *
         x[j] = __ldg(e + lane + 32 * j);
         w[j] = __ldg(wv + lane + 32 * j);
     }
-    RT *xr = x_res + (size_t)warp * D;
+    if (STORE) {
+        RT *xr = x_res + (size_t)warp * D;
 #pragma unroll
-    for (int j = 0; j < NW; j++)
-        store_res4(xr + 4 * (lane + 32 * j), make_int4(sext8(x[j], 0), sext8(x[j], 1), sext8(x[j], 2), sext8(x[j], 3)));
+        for (int j = 0; j < NW; j++)
+            store_res4(xr + 4 * (lane + 32 * j),
+                       make_int4(sext8(x[j], 0), sext8(x[j], 1), sext8(x[j], 2), sext8(x[j], 3)));
+    }
 #pragma unroll
     for (int j = 0; j < NW; j++) {   // clamp_i8 before the norm: -128 becomes -127
         uint32_t c = 0;
@@ -113,10 +118,17 @@ __global__ void k_embed_norm(const uint32_t *__restrict__ tok_in, const int8_t *
 }
 
 // o_n = norm(o, post_w); x_res += o_n (int32, never clamped: model.rs:432-434);
-// xn = norm(clamp(x_res), next_w)
-template <int NW, typename RT>
+// xn = norm(clamp(x_res), next_w).  Where the residual comes from and goes (MODE):
+// kResFromRes: read x_res, write it back; kResFromEmbed: the residual is still the
+// embedding row of tok_in (the first norm of layer 0), written to x_res;
+// kResNoStore: read x_res, write nothing back (the last norm of the model: nothing
+// reads the residual afterwards).
+enum { kResFromRes = 0, kResFromEmbed = 1, kResNoStore = 2 };
+
+template <int NW, typename RT, int MODE>
 __global__ void k_residual_norm(const int8_t *__restrict__ o, const int8_t *__restrict__ post_w,
                                 const int8_t *__restrict__ next_w, int M, const uint16_t *__restrict__ inv_tab,
+                                const uint32_t *__restrict__ tok_in, const int8_t *__restrict__ embed,
                                 RT *__restrict__ x_res, int8_t *__restrict__ xn) {
     constexpr int D = NW * 128;
     int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -127,13 +139,20 @@ __global__ void k_residual_norm(const int8_t *__restrict__ o, const int8_t *__re
     const uint32_t *nw = reinterpret_cast<const uint32_t *>(next_w);
     uint32_t x[NW], w[NW], y[NW], w2[NW];
     RT *xr = x_res + (size_t)warp * D;
+    const uint32_t *er = MODE == kResFromEmbed ? reinterpret_cast<const uint32_t *>(embed + (size_t)tok_in[warp] * D)
+                                               : nullptr;
     int4 rv[NW];
 #pragma unroll
     for (int j = 0; j < NW; j++) {   // every load of the row first
         x[j] = ov[lane + 32 * j];
         w[j] = __ldg(pw + lane + 32 * j);
         w2[j] = __ldg(nw + lane + 32 * j);
-        rv[j] = load_res4(xr + 4 * (lane + 32 * j));
+        if (MODE == kResFromEmbed) {
+            const uint32_t ev = __ldg(er + lane + 32 * j);
+            rv[j] = make_int4(sext8(ev, 0), sext8(ev, 1), sext8(ev, 2), sext8(ev, 3));
+        } else {
+            rv[j] = load_res4(xr + 4 * (lane + 32 * j));
+        }
     }
     rmsnorm_words<NW>(x, w, inv_tab, y);
 #pragma unroll
@@ -143,7 +162,7 @@ __global__ void k_residual_norm(const int8_t *__restrict__ o, const int8_t *__re
         r.y = (int)((uint32_t)r.y + (uint32_t)sext8(y[j], 1));
         r.z = (int)((uint32_t)r.z + (uint32_t)sext8(y[j], 2));
         r.w = (int)((uint32_t)r.w + (uint32_t)sext8(y[j], 3));
-        store_res4(xr + 4 * (lane + 32 * j), r);
+        if (MODE != kResNoStore) store_res4(xr + 4 * (lane + 32 * j), r);
         x[j] = (uint32_t)(uint8_t)clamp127(r.x) | ((uint32_t)(uint8_t)clamp127(r.y) << 8) |
                ((uint32_t)(uint8_t)clamp127(r.z) << 16) | ((uint32_t)(uint8_t)clamp127(r.w) << 24);
     }
@@ -182,28 +201,40 @@ void launch_rows(const uint32_t *tokens, const int *chunk_row0, const int *chunk
                                      tok_out, pos, err);
 }
 
-template <typename RT>
+template <typename RT, bool STORE>
 void embed_norm_t(const uint32_t *tok_in, const int8_t *embed, const int8_t *norm_w, int M, int d, const uint16_t *inv_tab,
                   RT *x_res, int8_t *xn, cudaStream_t st) {
     const int blocks = (M + 7) / 8;
     switch (d / 128) {
-        case 2: k_embed_norm<2, RT><<<blocks, 256, 0, st>>>(tok_in, embed, norm_w, M, inv_tab, x_res, xn); break;
-        case 3: k_embed_norm<3, RT><<<blocks, 256, 0, st>>>(tok_in, embed, norm_w, M, inv_tab, x_res, xn); break;
-        case 4: k_embed_norm<4, RT><<<blocks, 256, 0, st>>>(tok_in, embed, norm_w, M, inv_tab, x_res, xn); break;
+        case 2: k_embed_norm<2, RT, STORE><<<blocks, 256, 0, st>>>(tok_in, embed, norm_w, M, inv_tab, x_res, xn); break;
+        case 3: k_embed_norm<3, RT, STORE><<<blocks, 256, 0, st>>>(tok_in, embed, norm_w, M, inv_tab, x_res, xn); break;
+        case 4: k_embed_norm<4, RT, STORE><<<blocks, 256, 0, st>>>(tok_in, embed, norm_w, M, inv_tab, x_res, xn); break;
+        default: break;
+    }
+}
+
+template <typename RT, int MODE>
+void residual_norm_t(const int8_t *o, const int8_t *post_w, const int8_t *next_w, int M, int d, const uint16_t *inv_tab,
+                     const uint32_t *tok_in, const int8_t *embed, RT *x_res, int8_t *xn, cudaStream_t st) {
+    const int blocks = (M + 7) / 8;
+    switch (d / 128) {
+        case 2: k_residual_norm<2, RT, MODE><<<blocks, 256, 0, st>>>(o, post_w, next_w, M, inv_tab, tok_in, embed, x_res, xn); break;
+        case 3: k_residual_norm<3, RT, MODE><<<blocks, 256, 0, st>>>(o, post_w, next_w, M, inv_tab, tok_in, embed, x_res, xn); break;
+        case 4: k_residual_norm<4, RT, MODE><<<blocks, 256, 0, st>>>(o, post_w, next_w, M, inv_tab, tok_in, embed, x_res, xn); break;
         default: break;
     }
 }
 
 template <typename RT>
-void residual_norm_t(const int8_t *o, const int8_t *post_w, const int8_t *next_w, int M, int d, const uint16_t *inv_tab,
-                     RT *x_res, int8_t *xn, cudaStream_t st) {
-    const int blocks = (M + 7) / 8;
-    switch (d / 128) {
-        case 2: k_residual_norm<2, RT><<<blocks, 256, 0, st>>>(o, post_w, next_w, M, inv_tab, x_res, xn); break;
-        case 3: k_residual_norm<3, RT><<<blocks, 256, 0, st>>>(o, post_w, next_w, M, inv_tab, x_res, xn); break;
-        case 4: k_residual_norm<4, RT><<<blocks, 256, 0, st>>>(o, post_w, next_w, M, inv_tab, x_res, xn); break;
-        default: break;
-    }
+void residual_norm_mode(const int8_t *o, const int8_t *post_w, const int8_t *next_w, int M, int d,
+                        const uint16_t *inv_tab, const uint32_t *tok_in, const int8_t *embed, bool store_res,
+                        RT *x_res, int8_t *xn, cudaStream_t st) {
+    if (embed != nullptr)
+        residual_norm_t<RT, kResFromEmbed>(o, post_w, next_w, M, d, inv_tab, tok_in, embed, x_res, xn, st);
+    else if (store_res)
+        residual_norm_t<RT, kResFromRes>(o, post_w, next_w, M, d, inv_tab, tok_in, embed, x_res, xn, st);
+    else
+        residual_norm_t<RT, kResNoStore>(o, post_w, next_w, M, d, inv_tab, tok_in, embed, x_res, xn, st);
 }
 
 void launch_inv_table(int eps, uint16_t *tab, cudaStream_t st) {
@@ -211,17 +242,26 @@ void launch_inv_table(int eps, uint16_t *tab, cudaStream_t st) {
 }
 
 void launch_embed_norm(const uint32_t *tok_in, const int8_t *embed, const int8_t *norm_w, int M,
-                       int d, const uint16_t *inv_tab, void *x_res, bool res16, int8_t *xn, cudaStream_t st) {
+                       int d, const uint16_t *inv_tab, void *x_res, bool res16, bool store_res, int8_t *xn,
+                       cudaStream_t st) {
     if (M == 0) return;
-    if (res16) embed_norm_t(tok_in, embed, norm_w, M, d, inv_tab, static_cast<int16_t *>(x_res), xn, st);
-    else embed_norm_t(tok_in, embed, norm_w, M, d, inv_tab, static_cast<int32_t *>(x_res), xn, st);
+    if (res16) {
+        if (store_res) embed_norm_t<int16_t, true>(tok_in, embed, norm_w, M, d, inv_tab, static_cast<int16_t *>(x_res), xn, st);
+        else embed_norm_t<int16_t, false>(tok_in, embed, norm_w, M, d, inv_tab, static_cast<int16_t *>(x_res), xn, st);
+    } else {
+        if (store_res) embed_norm_t<int32_t, true>(tok_in, embed, norm_w, M, d, inv_tab, static_cast<int32_t *>(x_res), xn, st);
+        else embed_norm_t<int32_t, false>(tok_in, embed, norm_w, M, d, inv_tab, static_cast<int32_t *>(x_res), xn, st);
+    }
 }
 
 void launch_residual_norm(const int8_t *o, const int8_t *post_w, const int8_t *next_w, int M, int d,
-                          const uint16_t *inv_tab, void *x_res, bool res16, int8_t *xn, cudaStream_t st) {
+                          const uint16_t *inv_tab, const uint32_t *tok_in, const int8_t *embed, bool store_res,
+                          void *x_res, bool res16, int8_t *xn, cudaStream_t st) {
     if (M == 0) return;
-    if (res16) residual_norm_t(o, post_w, next_w, M, d, inv_tab, static_cast<int16_t *>(x_res), xn, st);
-    else residual_norm_t(o, post_w, next_w, M, d, inv_tab, static_cast<int32_t *>(x_res), xn, st);
+    if (res16)
+        residual_norm_mode(o, post_w, next_w, M, d, inv_tab, tok_in, embed, store_res, static_cast<int16_t *>(x_res), xn, st);
+    else
+        residual_norm_mode(o, post_w, next_w, M, d, inv_tab, tok_in, embed, store_res, static_cast<int32_t *>(x_res), xn, st);
 }
 
 void launch_kv_prep(const int8_t *qkv, int ldq, int d, const int *pos, const int16_t *rope_cos,
