@@ -522,7 +522,9 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, t = lane & 3;
     uint16_t *lut_s = reinterpret_cast<uint16_t *>(dsm + AM_WARPS * DEC_STAGES * 4096);
-    for (int i = tid; i < AM_LUT; i += AM_THREADS) lut_s[i] = lut4k_g[i];
+    for (int i = tid; i < AM_LUT; i += AM_THREADS) lut_s[i] = lut4k_g[i];   // model constant
+    pdl_wait();
+    pdl_trigger();
     __syncthreads();
     const uint16_t *lut4k = lut_s;
     const int stride = gridDim.x * AM_WARPS;
@@ -767,14 +769,14 @@ void launch_attention_decode_mma(const int8_t *qkv, int ldq, const int8_t *kvc, 
     if (M == 0) return;
     const unsigned grid = (unsigned)std::min<long>((M + AM_WARPS - 1) / AM_WARPS, (long)sm_count());
     if (wide_mult)
-        k_attention_decode_mma<true, false><<<grid, AM_THREADS, DEC_SMEM, st>>>(
-            qkv, ldq, kvc, cache_ld, M, p, n_heads, score_mult, sink_key, rope_cos, rope_sin, lut4k, out, ldo);
+        launch_k(k_attention_decode_mma<true, false>, grid, AM_THREADS, DEC_SMEM, st, qkv, ldq, kvc, cache_ld, M, p,
+                 n_heads, score_mult, sink_key, rope_cos, rope_sin, lut4k, out, ldo);
     else if (exp0)
-        k_attention_decode_mma<false, true><<<grid, AM_THREADS, DEC_SMEM, st>>>(
-            qkv, ldq, kvc, cache_ld, M, p, n_heads, score_mult, sink_key, rope_cos, rope_sin, lut4k, out, ldo);
+        launch_k(k_attention_decode_mma<false, true>, grid, AM_THREADS, DEC_SMEM, st, qkv, ldq, kvc, cache_ld, M, p,
+                 n_heads, score_mult, sink_key, rope_cos, rope_sin, lut4k, out, ldo);
     else
-        k_attention_decode_mma<false, false><<<grid, AM_THREADS, DEC_SMEM, st>>>(
-            qkv, ldq, kvc, cache_ld, M, p, n_heads, score_mult, sink_key, rope_cos, rope_sin, lut4k, out, ldo);
+        launch_k(k_attention_decode_mma<false, false>, grid, AM_THREADS, DEC_SMEM, st, qkv, ldq, kvc, cache_ld, M, p,
+                 n_heads, score_mult, sink_key, rope_cos, rope_sin, lut4k, out, ldo);
 }
 
 }  // namespace czg

@@ -7,6 +7,10 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#include <utility>
+
+#include "kernels.h"
+
 namespace czg {
 
 constexpr int kHeadDim = 64;
@@ -25,6 +29,34 @@ inline int sm_count() {
         cached[dev] = n > 0 ? n : 148;
     }
     return cached[dev];
+}
+
+// Programmatic dependent launch.  A kernel launched with the PDL attribute may be
+// scheduled while the previous kernel of its stream is still running: pdl_wait()
+// blocks until that kernel has completed and its memory writes are visible (for a
+// normal launch it returns at once), so every kernel that launch_k may launch with
+// the attribute calls it before its first access to memory that another kernel
+// writes.  pdl_trigger() lets the next kernel of the stream begin to launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// launch_k: a kernel launch that carries the PDL attribute while g_pdl_launch is set
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                            Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    if (g_pdl_launch) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // primitives.rs:9-11

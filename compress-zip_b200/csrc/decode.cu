@@ -48,6 +48,8 @@ __global__ void k_dec_init(const uint8_t *__restrict__ data, const uint64_t *__r
 __global__ void k_kv_append(const int8_t *__restrict__ qkv, int ldq, int d, int pos,
                             const int16_t *__restrict__ rope_cos, const int16_t *__restrict__ rope_sin,
                             int M, int8_t *__restrict__ kvc, size_t cache_ld, bool split) {
+    pdl_wait();
+    pdl_trigger();
     const int gid = blockIdx.x * blockDim.x + threadIdx.x;
     const int r = gid >> 5, i = gid & 31;
     if (r >= M) return;
@@ -85,7 +87,9 @@ __global__ void k_cdf_decode(const int32_t *__restrict__ logits, int V, int ld, 
                              const uint64_t *__restrict__ tok_off, int step, uint32_t *__restrict__ out_tok,
                              uint32_t *__restrict__ tok_in) {
     __shared__ uint16_t lut[256];
-    for (int i = threadIdx.x; i < 256; i += blockDim.x) lut[i] = lut_g[i];
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) lut[i] = lut_g[i];   // model constant
+    pdl_wait();
+    pdl_trigger();
     __syncthreads();
     const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
@@ -205,6 +209,8 @@ __global__ void __launch_bounds__(256) k_cdf_decode_reg(
     int step, uint32_t *__restrict__ out_tok, uint32_t *__restrict__ tok_in) {
     constexpr int V = 32 * E;
     __shared__ uint32_t ebuf[8][E / 2];
+    pdl_wait();
+    pdl_trigger();
     const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     if (r >= M) return;
@@ -334,8 +340,8 @@ void launch_kv_append(const int8_t *qkv, int ldq, int d, int pos, const int16_t 
                       const int16_t *rope_sin, int M, int8_t *kvc, size_t cache_ld, bool split, cudaStream_t stream) {
     if (M == 0) return;
     const long long threads = (long long)M * 32;
-    k_kv_append<<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(qkv, ldq, d, pos, rope_cos, rope_sin, M,
-                                                                       kvc, cache_ld, split);
+    launch_k(k_kv_append, (unsigned)((threads + 255) / 256), 256, 0, stream, qkv, ldq, d, pos, rope_cos, rope_sin, M,
+             kvc, cache_ld, split);
 }
 
 void launch_cdf_decode(const int32_t *logits, int V, int ld, const uint16_t *lut, const uint16_t *lut4k, bool exp0,
@@ -350,13 +356,11 @@ void launch_cdf_decode(const int32_t *logits, int V, int ld, const uint16_t *lut
 #define CZG_CDF_DEC(EE)                                                                                       \
     do {                                                                                                       \
         if (exp0)                                                                                              \
-            k_cdf_decode_reg<EE, true><<<grid, 256, 0, stream>>>(logits, ld, lut4k, c8, total, inv, M, st, data,   \
-                                                                 data_off, data_len, tok_off, step, out_tok,  \
-                                                                 tok_in);                                      \
+            launch_k(k_cdf_decode_reg<EE, true>, grid, 256, 0, stream, logits, ld, lut4k, c8, total, inv, M, st,  \
+                     data, data_off, data_len, tok_off, step, out_tok, tok_in);                                \
         else                                                                                                   \
-            k_cdf_decode_reg<EE, false><<<grid, 256, 0, stream>>>(logits, ld, lut4k, c8, total, inv, M, st, data,  \
-                                                                  data_off, data_len, tok_off, step, out_tok, \
-                                                                  tok_in);                                     \
+            launch_k(k_cdf_decode_reg<EE, false>, grid, 256, 0, stream, logits, ld, lut4k, c8, total, inv, M, st, \
+                     data, data_off, data_len, tok_off, step, out_tok, tok_in);                                \
     } while (0)
         if (V == 1024) CZG_CDF_DEC(32);
         else if (V == 512) CZG_CDF_DEC(16);
@@ -364,8 +368,8 @@ void launch_cdf_decode(const int32_t *logits, int V, int ld, const uint16_t *lut
 #undef CZG_CDF_DEC
         return;
     }
-    k_cdf_decode<<<grid, 256, 0, stream>>>(logits, V, ld, lut, coef, total, inv, M, st, data, data_off,
-                                           data_len, tok_off, step, out_tok, tok_in);
+    launch_k(k_cdf_decode, grid, 256, 0, stream, logits, V, ld, lut, coef, total, inv, M, st, data, data_off, data_len,
+             tok_off, step, out_tok, tok_in);
 }
 
 }  // namespace czg

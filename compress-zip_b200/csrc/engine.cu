@@ -175,6 +175,13 @@ EvPair &next_ev(czg_ctx *c, int cls) {
     return e;
 }
 
+struct PdlScope {   // g_pdl_launch on for the scope's lifetime
+    explicit PdlScope(bool on) { g_pdl_launch = on; }
+    ~PdlScope() { g_pdl_launch = false; }
+    PdlScope(const PdlScope &) = delete;
+    PdlScope &operator=(const PdlScope &) = delete;
+};
+
 template <class F>
 void timed(czg_ctx *c, int cls, F &&f) {
     c->stats.launches[cls]++;
@@ -806,6 +813,11 @@ int decompress_impl(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts
         const bool split = attention_decode_mma_ok(H) && getenv("CZG_SCALAR_DECODE") == nullptr;
         const size_t layer_ld = (size_t)c->dec_streams * cache_ld;
         int active = ns;
+        // programmatic dependent launches for the step kernels: each may be scheduled
+        // while its predecessor finishes and waits on the device for its results
+        // (off with per-kernel events, or CZG_PDL=0)
+        const char *pdl_env = getenv("CZG_PDL");
+        const PdlScope pdl_scope(!c->kernel_timing && !(pdl_env && atoi(pdl_env) == 0));
         for (int step = 0; step < wmax; step++) {
             while (active > 0 && (int)n_tokens[order[w0 + active - 1]] <= step) active--;
             const int M = active;

@@ -119,6 +119,10 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
+    // the setup above overlaps the previous kernel under a PDL launch; the operands
+    // and the output buffer are touched only from here on
+    pdl_wait();
+    pdl_trigger();
 
     if (warp == 0) {
         if (lane == 0) {   // TMA producer
@@ -340,11 +344,11 @@ bool launch_tc(const TcMatrix &A, const TcMatrix &B, int M, int N, int K, int mu
     const CUtensorMap &mb = *reinterpret_cast<const CUtensorMap *>(B.map);
     constexpr int S = TcCfg<BN>::kStages;
     if (EPI == kEpiInt32 || q.mode == 2)
-        k_gemm_tc<BN, S, EPI, 2><<<grid, TC_THREADS, TcCfg<BN>::kSmem, st>>>(ma, mb, omap, M, N, K, q, err);
+        launch_k(k_gemm_tc<BN, S, EPI, 2>, grid, TC_THREADS, TcCfg<BN>::kSmem, st, ma, mb, omap, M, N, K, q, err);
     else if (q.mode == 1)
-        k_gemm_tc<BN, S, EPI, 1><<<grid, TC_THREADS, TcCfg<BN>::kSmem, st>>>(ma, mb, omap, M, N, K, q, err);
+        launch_k(k_gemm_tc<BN, S, EPI, 1>, grid, TC_THREADS, TcCfg<BN>::kSmem, st, ma, mb, omap, M, N, K, q, err);
     else
-        k_gemm_tc<BN, S, EPI, 0><<<grid, TC_THREADS, TcCfg<BN>::kSmem, st>>>(ma, mb, omap, M, N, K, q, err);
+        launch_k(k_gemm_tc<BN, S, EPI, 0>, grid, TC_THREADS, TcCfg<BN>::kSmem, st, ma, mb, omap, M, N, K, q, err);
     return true;
 }
 

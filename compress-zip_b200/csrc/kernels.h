@@ -5,6 +5,10 @@
 
 namespace czg {
 
+// Kernels of the lockstep decode step launch with the programmatic-dependent-launch
+// attribute while this is set on the calling thread (common.cuh: launch_k).
+inline thread_local bool g_pdl_launch = false;
+
 // bits of the device error word
 constexpr int kErrToken = 1;     // token id >= vocab
 constexpr int kErrOverflow = 2;  // an encoded chunk outgrew its slot

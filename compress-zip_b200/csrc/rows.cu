@@ -85,6 +85,8 @@ template <int NW, typename RT, bool STORE>
 __global__ void k_embed_norm(const uint32_t *__restrict__ tok_in, const int8_t *__restrict__ embed,
                              const int8_t *__restrict__ norm_w, int M, const uint16_t *__restrict__ inv_tab,
                              RT *__restrict__ x_res, int8_t *__restrict__ xn) {
+    pdl_wait();
+    pdl_trigger();
     constexpr int D = NW * 128;
     int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     int lane = threadIdx.x & 31;
@@ -130,6 +132,8 @@ __global__ void k_residual_norm(const int8_t *__restrict__ o, const int8_t *__re
                                 const int8_t *__restrict__ next_w, int M, const uint16_t *__restrict__ inv_tab,
                                 const uint32_t *__restrict__ tok_in, const int8_t *__restrict__ embed,
                                 RT *__restrict__ x_res, int8_t *__restrict__ xn) {
+    pdl_wait();
+    pdl_trigger();
     constexpr int D = NW * 128;
     int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     int lane = threadIdx.x & 31;
@@ -206,9 +210,9 @@ void embed_norm_t(const uint32_t *tok_in, const int8_t *embed, const int8_t *nor
                   RT *x_res, int8_t *xn, cudaStream_t st) {
     const int blocks = (M + 7) / 8;
     switch (d / 128) {
-        case 2: k_embed_norm<2, RT, STORE><<<blocks, 256, 0, st>>>(tok_in, embed, norm_w, M, inv_tab, x_res, xn); break;
-        case 3: k_embed_norm<3, RT, STORE><<<blocks, 256, 0, st>>>(tok_in, embed, norm_w, M, inv_tab, x_res, xn); break;
-        case 4: k_embed_norm<4, RT, STORE><<<blocks, 256, 0, st>>>(tok_in, embed, norm_w, M, inv_tab, x_res, xn); break;
+        case 2: launch_k(k_embed_norm<2, RT, STORE>, blocks, 256, 0, st, tok_in, embed, norm_w, M, inv_tab, x_res, xn); break;
+        case 3: launch_k(k_embed_norm<3, RT, STORE>, blocks, 256, 0, st, tok_in, embed, norm_w, M, inv_tab, x_res, xn); break;
+        case 4: launch_k(k_embed_norm<4, RT, STORE>, blocks, 256, 0, st, tok_in, embed, norm_w, M, inv_tab, x_res, xn); break;
         default: break;
     }
 }
@@ -218,9 +222,9 @@ void residual_norm_t(const int8_t *o, const int8_t *post_w, const int8_t *next_w
                      const uint32_t *tok_in, const int8_t *embed, RT *x_res, int8_t *xn, cudaStream_t st) {
     const int blocks = (M + 7) / 8;
     switch (d / 128) {
-        case 2: k_residual_norm<2, RT, MODE><<<blocks, 256, 0, st>>>(o, post_w, next_w, M, inv_tab, tok_in, embed, x_res, xn); break;
-        case 3: k_residual_norm<3, RT, MODE><<<blocks, 256, 0, st>>>(o, post_w, next_w, M, inv_tab, tok_in, embed, x_res, xn); break;
-        case 4: k_residual_norm<4, RT, MODE><<<blocks, 256, 0, st>>>(o, post_w, next_w, M, inv_tab, tok_in, embed, x_res, xn); break;
+        case 2: launch_k(k_residual_norm<2, RT, MODE>, blocks, 256, 0, st, o, post_w, next_w, M, inv_tab, tok_in, embed, x_res, xn); break;
+        case 3: launch_k(k_residual_norm<3, RT, MODE>, blocks, 256, 0, st, o, post_w, next_w, M, inv_tab, tok_in, embed, x_res, xn); break;
+        case 4: launch_k(k_residual_norm<4, RT, MODE>, blocks, 256, 0, st, o, post_w, next_w, M, inv_tab, tok_in, embed, x_res, xn); break;
         default: break;
     }
 }
