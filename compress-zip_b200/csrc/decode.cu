@@ -200,20 +200,30 @@ __global__ void k_cdf_decode(const int32_t *__restrict__ logits, int V, int ld, 
 // t256-indexed table lut4k (needs coef < 2^24), the division by S uses
 // freq_of.  The interval search is done by the whole warp: the owner
 // lane's weights go through shared memory, one element per lane, and an
-// inclusive scan gives the cumulative frequencies.
+// inclusive scan gives the cumulative frequencies.  Persistent (CDF_BLOCKS_PER_SM
+// blocks per SM, warp w takes streams w, w + W, ...), with the table in shared
+// memory: its 32 x E random lookups per stream are gathers that the L1 path
+// serves one cache line at a time, shared memory one bank conflict at a time.
+constexpr int CDF_LUT_WORDS = 4104 / 2;   // lut4k: t256 0..4096, padded
+constexpr int CDF_BLOCKS_PER_SM = 4;
+
 template <int E, bool EXP0>
-__global__ void __launch_bounds__(256) k_cdf_decode_reg(
-    const int32_t *__restrict__ logits, int ld, const uint16_t *__restrict__ lut4k, uint32_t c8, uint32_t total,
+__global__ void __launch_bounds__(256, CDF_BLOCKS_PER_SM) k_cdf_decode_reg(
+    const int32_t *__restrict__ logits, int ld, const uint16_t *__restrict__ lut4k_g, uint32_t c8, uint32_t total,
     unsigned long long inv_total, int M, DecState *__restrict__ st, const uint8_t *__restrict__ data,
     const uint64_t *__restrict__ data_off, const uint64_t *__restrict__ data_len, const uint64_t *__restrict__ tok_off,
     int step, uint32_t *__restrict__ out_tok, uint32_t *__restrict__ tok_in) {
     constexpr int V = 32 * E;
     __shared__ uint32_t ebuf[8][E / 2];
+    __shared__ uint32_t lut_w[CDF_LUT_WORDS];
+    for (int i = threadIdx.x; i < CDF_LUT_WORDS; i += blockDim.x)   // model constant: before the wait
+        lut_w[i] = __ldg(reinterpret_cast<const uint32_t *>(lut4k_g) + i);
     pdl_wait();
     pdl_trigger();
-    const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    __syncthreads();
+    const uint16_t *lut4k = reinterpret_cast<const uint16_t *>(lut_w);
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-    if (r >= M) return;
+    for (int r = blockIdx.x * 8 + wib; r < M; r += gridDim.x * 8) {
     const int4 *src = reinterpret_cast<const int4 *>(logits + (size_t)r * ld + lane * E);
     int x[E];
 #pragma unroll
@@ -239,7 +249,7 @@ __global__ void __launch_bounds__(256) k_cdf_decode_reg(
         const int dlt = (int)((uint32_t)x[k] - (uint32_t)mx);
         const uint32_t neg = 0u - (uint32_t)dlt;
         const uint32_t t = min((uint32_t)(((unsigned long long)neg * c8 + 0x80000000ull) >> 32), 4096u);
-        const uint32_t w = (EXP0 || dlt < 0) ? (uint32_t)__ldg(lut4k + t) : 65535u;   // EXP0: lut4k[0] == 65535
+        const uint32_t w = (EXP0 || dlt < 0) ? (uint32_t)lut4k[t] : 65535u;   // EXP0: lut4k[0] == 65535
         S += w;
         if (k & 1) ew[k >> 1] |= w << 16;
         else ew[k >> 1] = w;
@@ -326,6 +336,8 @@ __global__ void __launch_bounds__(256) k_cdf_decode_reg(
         out_tok[tok_off[r] + step] = sym;
         tok_in[r] = sym;
     }
+    __syncwarp();   // ebuf is rewritten for the warp's next stream
+    }
 }
 
 }  // namespace
@@ -352,14 +364,15 @@ void launch_cdf_decode(const int32_t *logits, int V, int ld, const uint16_t *lut
     const unsigned long long inv = 0xFFFFFFFFFFFFFFFFull / total;
     const unsigned grid = (unsigned)((M + 7) / 8);
     if (coef < (1u << 24) && ld % 4 == 0 && (V == 1024 || V == 512 || V == 256)) {
+        const unsigned pgrid = std::min<unsigned>(grid, (unsigned)(CDF_BLOCKS_PER_SM * sm_count()));
         const uint32_t c8 = coef << 8;
 #define CZG_CDF_DEC(EE)                                                                                       \
     do {                                                                                                       \
         if (exp0)                                                                                              \
-            launch_k(k_cdf_decode_reg<EE, true>, grid, 256, 0, stream, logits, ld, lut4k, c8, total, inv, M, st,  \
+            launch_k(k_cdf_decode_reg<EE, true>, pgrid, 256, 0, stream, logits, ld, lut4k, c8, total, inv, M, st,  \
                      data, data_off, data_len, tok_off, step, out_tok, tok_in);                                \
         else                                                                                                   \
-            launch_k(k_cdf_decode_reg<EE, false>, grid, 256, 0, stream, logits, ld, lut4k, c8, total, inv, M, st, \
+            launch_k(k_cdf_decode_reg<EE, false>, pgrid, 256, 0, stream, logits, ld, lut4k, c8, total, inv, M, st, \
                      data, data_off, data_len, tok_off, step, out_tok, tok_in);                                \
     } while (0)
         if (V == 1024) CZG_CDF_DEC(32);
