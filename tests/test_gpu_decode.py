@@ -152,3 +152,22 @@ def test_decode_scalar_attention_path(shipped_path, shipped_oracle, oracle_mod, 
         assert np.array_equal(e.decompress_chunks(chunks, np.diff(starts)), tokens)
     finally:
         e.close()
+
+
+def test_decode_launch_modes_agree(eng, shipped_oracle, oracle_mod, doc_tokens, monkeypatch):
+    """The step kernels under programmatic dependent launch (the default), plain
+    launches (CZG_PDL=0) and plain launches with per-kernel events decode the same
+    oracle-encoded streams to the original tokens."""
+    tokens, starts = _chunked(doc_tokens, 256)
+    chunks = oracle_mod.compress_chunks(shipped_oracle, tokens, starts)
+    n_tok = np.diff(starts)
+    assert np.array_equal(eng.decompress_chunks(chunks, n_tok), tokens)
+    monkeypatch.setenv("CZG_PDL", "0")
+    assert np.array_equal(eng.decompress_chunks(chunks, n_tok), tokens)
+    monkeypatch.delenv("CZG_PDL")
+    eng.set_kernel_timing(True)
+    try:
+        assert np.array_equal(eng.decompress_chunks(chunks, n_tok), tokens)
+        assert eng.last_stats()["kernels"]["cdf_decode"]["launches"] > 0
+    finally:
+        eng.set_kernel_timing(False)
