@@ -100,6 +100,7 @@ struct czg_ctx {
     uint32_t *lens = nullptr;
     uint64_t *slot_off = nullptr, *pack_off = nullptr, *chunk_tok0 = nullptr;
     int *chunk_row0 = nullptr, *chunk_len = nullptr;
+    int *att_row0 = nullptr, *att_len = nullptr;   // the chunks in attention launch order
     // tcgen05 path: TMA descriptors of the GEMM A operands (wave buffers) and the head
     bool use_tc = false;
     TcMatrix tm_xn, tm_attn, tm_h, tm_head;
@@ -113,6 +114,7 @@ struct czg_ctx {
     std::vector<void *> dec_allocs;
     // pinned host staging
     uint8_t *h_meta = nullptr;
+    std::vector<int> att_order;
     size_t h_meta_bytes = 0;
 
     // statistics
@@ -423,6 +425,7 @@ int alloc_workspace(czg_ctx *c, int rows, int chunks) {
               dalloc_ws(c, &c->lens, (size_t)chunks) && dalloc_ws(c, &c->slot_off, (size_t)chunks + 1) &&
               dalloc_ws(c, &c->pack_off, (size_t)chunks + 1) && dalloc_ws(c, &c->chunk_tok0, (size_t)chunks) &&
               dalloc_ws(c, &c->chunk_row0, (size_t)chunks) && dalloc_ws(c, &c->chunk_len, (size_t)chunks) &&
+              dalloc_ws(c, &c->att_row0, (size_t)chunks) && dalloc_ws(c, &c->att_len, (size_t)chunks) &&
               dalloc_ws(c, &c->err_flag, 1);
     if (!ok) return CZG_E_DEVICE;
     cudaMemsetAsync(c->err_flag, 0, sizeof(int), c->stream);
@@ -448,7 +451,7 @@ int alloc_workspace(czg_ctx *c, int rows, int chunks) {
     const char *hc = getenv("CZG_HEAD_CDF");
     c->head_cdf = c->use_tc && !(hc && std::string(hc) == "0") && c->exp0 && c->logit_small &&
                   m.vocab_size == c->vpad && c->vpad % 256 == 0 && m.coef_q24 < (1u << 23) && d % 128 == 0;
-    c->h_meta_bytes = (size_t)chunks * 32 + 64;
+    c->h_meta_bytes = (size_t)chunks * 40 + 64;
     if (!cuda_ok(c, cudaMallocHost(&c->h_meta, c->h_meta_bytes), "cudaMallocHost")) return CZG_E_DEVICE;
     return CZG_OK;
 }
@@ -508,8 +511,21 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
         h_slot[i + 1] = h_slot[i] + 4ull * (uint64_t)h_len[i] + 8ull;
         max_len = std::max(max_len, h_len[i]);
     }
+    // attention CTAs (one per chunk) longest chunk first: the short chunks (document
+    // tails) then fill the last round of CTAs instead of leaving SMs idle
+    int *h_arow0 = reinterpret_cast<int *>(h_slot + nc + 1);
+    int *h_alen = h_arow0 + nc;
+    c->att_order.resize(nc);
+    for (int i = 0; i < nc; i++) c->att_order[i] = i;
+    std::stable_sort(c->att_order.begin(), c->att_order.end(), [&](int a, int b) { return h_len[a] > h_len[b]; });
+    for (int i = 0; i < nc; i++) {
+        h_arow0[i] = h_row0[c->att_order[i]];
+        h_alen[i] = h_len[c->att_order[i]];
+    }
     cudaMemcpyAsync(c->chunk_row0, h_row0, sizeof(int) * nc, cudaMemcpyHostToDevice, st);
     cudaMemcpyAsync(c->chunk_len, h_len, sizeof(int) * nc, cudaMemcpyHostToDevice, st);
+    cudaMemcpyAsync(c->att_row0, h_arow0, sizeof(int) * nc, cudaMemcpyHostToDevice, st);
+    cudaMemcpyAsync(c->att_len, h_alen, sizeof(int) * nc, cudaMemcpyHostToDevice, st);
     cudaMemcpyAsync(c->chunk_tok0, h_tok0, sizeof(uint64_t) * nc, cudaMemcpyHostToDevice, st);
     cudaMemcpyAsync(c->slot_off, h_slot, sizeof(uint64_t) * (nc + 1), cudaMemcpyHostToDevice, st);
     cudaMemsetAsync(c->err_flag, 0, sizeof(int), st);
@@ -533,11 +549,11 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
         });
         timed(c, kAttention, [&] {
             if (attention_mma_fits(max_len) && !c->scalar_attention)
-                launch_attention_mma(c->qkv, d + 128, c->kv, c->chunk_row0, c->chunk_len, nc, max_len, H,
+                launch_attention_mma(c->qkv, d + 128, c->kv, c->att_row0, c->att_len, nc, max_len, H,
                                      L.score_mult, L.sink_key, c->rope_cos, c->rope_sin, c->lut4k,
                                      L.wide_mult, c->exp0, c->attn, d, st);
             else
-                launch_attention(c->qkv, d + 128, c->kv, c->chunk_row0, c->chunk_len, nc, max_len, H,
+                launch_attention(c->qkv, d + 128, c->kv, c->att_row0, c->att_len, nc, max_len, H,
                                  L.score_mult, L.sink_key, c->rope_cos, c->rope_sin, c->lut, c->attn, d, st);
         });
         if (tr && tr->attn)
