@@ -230,26 +230,28 @@ struct BitSink {
     }
 };
 
-// One warp per chunk.  The warp stages the chunk's (sym_low, sym_high) pairs
-// through shared memory 32 at a time (the next block is loaded while lane 0
-// encodes the current one); lane 0 runs the coder.  Renormalisation takes the
-// reference's loop (arith_coder.rs:101-119) in bulk steps:
+// One lane per chunk: the 32 chunks of a warp are encoded side by side, each lane
+// walking its own chunk's (sym_low, sym_high) pairs with the next pair loaded a
+// step ahead (loading 4 or 8 ahead measured the same: the coder's own dependent
+// steps and the lanes' diverging renormalisations set the pace).
+// Renormalisation takes the reference's loop (arith_coder.rs:101-119) in bulk
+// steps:
 //  * E1/E2: the k = clz(low ^ high) leading bits that agree are emitted at once
 //    (the first followed by the pending bits), then low/high shift by k;
 //  * E3: while bit 30 of low is 1 and bit 30 of high is 0 the reference repeats
 //    the E3 step; j such steps keep bit 31, drop the j bits below it and add j
 //    pending bits.
-constexpr int ENC_WARPS = 4;
+// A lane-per-chunk warp issues one instruction stream for 32 coders, where a
+// warp per chunk spent a whole warp's issue slot on each coder step.
+constexpr int ENC_THREADS = 128;
 
-__global__ void __launch_bounds__(ENC_WARPS * 32)
+__global__ void __launch_bounds__(ENC_THREADS)
 k_encode(const uint2 *__restrict__ lohi, const int *__restrict__ chunk_row0,
          const int *__restrict__ chunk_len, int n_chunks, uint32_t total,
          unsigned long long inv_total, uint8_t *__restrict__ slots,
          const uint64_t *__restrict__ slot_off, uint32_t *__restrict__ lens,
          int *__restrict__ err) {
-    __shared__ uint2 stage[ENC_WARPS][2][32];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int c = blockIdx.x * ENC_WARPS + warp;
+    const int c = blockIdx.x * ENC_THREADS + threadIdx.x;
     if (c >= n_chunks) return;
     const unsigned long long HALF = 1ull << 31, QUARTER = 1ull << 30, MASK = 0xFFFFFFFFull;
     const int r0 = chunk_row0[c], n = chunk_len[c];
@@ -259,49 +261,37 @@ k_encode(const uint2 *__restrict__ lohi, const int *__restrict__ chunk_row0,
     bs.len = 0; bs.acc = 0; bs.n = 0; bs.overflow = false;
     unsigned long long low = 0, high = MASK;
     uint32_t pending = 0;
-    if (lane < n) stage[warp][0][lane] = lohi[r0 + lane];
-    __syncwarp();
-    for (int b0 = 0; b0 < n; b0 += 32) {
-        const int cur = (b0 >> 5) & 1;
-        uint2 nxt = make_uint2(0, 0);
-        if (b0 + 32 + lane < n) nxt = lohi[r0 + b0 + 32 + lane];   // prefetch the next block
-        if (lane == 0) {
-            const int cnt = min(32, n - b0);
-            for (int i = 0; i < cnt; i++) {
-                const uint2 lh = stage[warp][cur][i];
-                const unsigned long long range = high - low + 1;
-                high = low + udiv_by_inv((unsigned long long)lh.y * range, total, inv_total) - 1;
-                low = low + udiv_by_inv((unsigned long long)lh.x * range, total, inv_total);
-                for (;;) {
-                    const uint32_t x = (uint32_t)(low ^ high);
-                    if ((x & 0x80000000u) == 0) {   // E1/E2, k >= 1 agreeing leading bits
-                        const int k = x == 0 ? 32 : __clz(x);
-                        bs.bit_plus_pending((uint32_t)(low >> 31) & 1u, pending);
-                        pending = 0;
-                        if (k > 1) bs.push((uint32_t)(low >> (32 - k)) & ((1u << (k - 1)) - 1u), k - 1);
-                        low = (low << k) & MASK;
-                        high = ((high << k) & MASK) | ((1ull << k) - 1ull);
-                    } else if ((low & ~high & QUARTER) != 0) {   // E3, j steps
-                        const int j = min(31, min(__clz(~(uint32_t)low << 1), __clz((uint32_t)high << 1)));
-                        pending += (uint32_t)j;
-                        low = (low << j) & 0x7FFFFFFFull;
-                        high = ((high << j) & MASK) | HALF | ((1ull << j) - 1ull);
-                    } else {
-                        break;
-                    }
-                }
+    const uint2 *src = lohi + r0;
+    uint2 nxt = n > 0 ? src[0] : make_uint2(0, 0);
+    for (int i = 0; i < n; i++) {
+        const uint2 lh = nxt;
+        if (i + 1 < n) nxt = src[i + 1];   // in flight during this step
+        const unsigned long long range = high - low + 1;
+        high = low + udiv_by_inv((unsigned long long)lh.y * range, total, inv_total) - 1;
+        low = low + udiv_by_inv((unsigned long long)lh.x * range, total, inv_total);
+        for (;;) {
+            const uint32_t x = (uint32_t)(low ^ high);
+            if ((x & 0x80000000u) == 0) {   // E1/E2, k >= 1 agreeing leading bits
+                const int k = x == 0 ? 32 : __clz(x);
+                bs.bit_plus_pending((uint32_t)(low >> 31) & 1u, pending);
+                pending = 0;
+                if (k > 1) bs.push((uint32_t)(low >> (32 - k)) & ((1u << (k - 1)) - 1u), k - 1);
+                low = (low << k) & MASK;
+                high = ((high << k) & MASK) | ((1ull << k) - 1ull);
+            } else if ((low & ~high & QUARTER) != 0) {   // E3, j steps
+                const int j = min(31, min(__clz(~(uint32_t)low << 1), __clz((uint32_t)high << 1)));
+                pending += (uint32_t)j;
+                low = (low << j) & 0x7FFFFFFFull;
+                high = ((high << j) & MASK) | HALF | ((1ull << j) - 1ull);
+            } else {
+                break;
             }
         }
-        __syncwarp();
-        stage[warp][cur ^ 1][lane] = nxt;
-        __syncwarp();
     }
-    if (lane == 0) {
-        bs.push(1u, 1);   // finish: terminating '1', then pad the partial byte
-        if (bs.n > 0) bs.push(0u, 8 - bs.n);
-        lens[c] = bs.len;
-        if (bs.overflow) atomicOr(err, kErrOverflow);
-    }
+    bs.push(1u, 1);   // finish: terminating '1', then pad the partial byte
+    if (bs.n > 0) bs.push(0u, 8 - bs.n);
+    lens[c] = bs.len;
+    if (bs.overflow) atomicOr(err, kErrOverflow);
 }
 
 // one CTA per chunk: slot bytes -> packed position
@@ -345,7 +335,7 @@ void launch_encode(const uint2 *lohi, const int *chunk_row0, const int *chunk_le
                    int *err, cudaStream_t st) {
     if (n_chunks == 0) return;
     unsigned long long inv = 0xFFFFFFFFFFFFFFFFull / total;
-    k_encode<<<(n_chunks + ENC_WARPS - 1) / ENC_WARPS, ENC_WARPS * 32, 0, st>>>(
+    k_encode<<<(n_chunks + ENC_THREADS - 1) / ENC_THREADS, ENC_THREADS, 0, st>>>(
         lohi, chunk_row0, chunk_len, n_chunks, total, inv, slots, slot_off, lens, err);
 }
 
