@@ -251,13 +251,35 @@ __device__ __forceinline__ uint32_t bytes_equal(uint32_t x, uint32_t q) {
     return prmt(~nz & 0x80808080u, 0u, 0xBA98u);                    // replicate bit 7 over the byte
 }
 
-template <bool WIDE, bool EXP0>
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+                 : "memory");
+}
+
+// The 4 KB of one 32-key tile of a stream (K rows, then the V tile) into a
+// shared-memory stage, 8 x 16 bytes per lane, as one cp.async group.
+__device__ __forceinline__ void decode_tile_async(uint8_t *stage, const int8_t *ks, const int8_t *vt, int kb, int lane) {
+#pragma unroll
+    for (int i = 0; i < 4; i++) cp_async16(stage + 16 * (lane + 32 * i), ks + (size_t)kb * 64 + 16 * (lane + 32 * i));
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+        cp_async16(stage + 2048 + 16 * (lane + 32 * i), vt + (size_t)kb * 64 + 16 * (lane + 32 * i));
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+// STREAM: chunks longer than shared memory holds.  K and V stay in the per-chunk
+// streaming layout of k_kv_prep_split (chunk_kvoff[c] * 128 bytes into kv_g) and
+// each warp copies its task's 32-key tiles (K rows, then the V tile: 4 KB) into a
+// two-stage shared-memory ring with cp.async, the next tile's copy overlapping the
+// current tile's work; the fragments then come from the tile as in the decode kernel.
+template <bool WIDE, bool EXP0, bool STREAM>
 __global__ void __launch_bounds__(AM_THREADS, 1)
 k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restrict__ kv_g,
                 const int *__restrict__ chunk_row0, const int *__restrict__ chunk_len, int n_heads,
                 const int32_t *__restrict__ score_mult, const int8_t *__restrict__ sink_key,
                 const int16_t *__restrict__ rope_cos, const int16_t *__restrict__ rope_sin,
-                const uint16_t *__restrict__ lut4k_g, int8_t *__restrict__ out, int ldo) {
+                const uint16_t *__restrict__ lut4k_g, int8_t *__restrict__ out, int ldo,
+                const int *__restrict__ chunk_kvoff) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ int task_ctr;
     const int c = blockIdx.x;
@@ -266,7 +288,7 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
     const int vt_ld = ((npad + 127) & ~127) + 32;   // 8 dims of a fragment land on distinct banks
     uint8_t *ks = smem;                              // [npad][64], dims permuted per thread quarter
     uint8_t *vt = ks + npad * 64;                    // [64][vt_ld], keys in order
-    uint8_t *wsm = vt + 64 * vt_ld;
+    uint8_t *wsm = STREAM ? smem : vt + 64 * vt_ld;
     uint16_t *lut_s = reinterpret_cast<uint16_t *>(wsm + AM_WARPS * AM_WARP_SMEM);   // exp table
     for (int i = threadIdx.x; i < AM_LUT; i += AM_THREADS) lut_s[i] = lut4k_g[i];
     const uint16_t *lut4k = lut_s;
@@ -274,10 +296,14 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
     const int g = lane >> 2, t = lane & 3;
     uint32_t *rec_e = reinterpret_cast<uint32_t *>(wsm + warp * AM_WARP_SMEM);   // [8][32]
     uint8_t *ostage = reinterpret_cast<uint8_t *>(rec_e + AM_ROWS * 32);         // [8][64]
+    // STREAM: this warp's two 4 KB tile stages, and the chunk's K rows / V tiles in global memory
+    uint8_t *ring = reinterpret_cast<uint8_t *>(lut_s + AM_LUT) + warp * 8192;
+    const int8_t *kg = STREAM ? kv_g + (size_t)chunk_kvoff[c] * 128 : nullptr;
+    const int8_t *vg = STREAM ? kg + (size_t)npad * 64 : nullptr;
 
     // K row layout: bytes [16t' + 4k + b] = dim 16k + 4t' + b, so thread t reads its
     // four B words (dims 4t, 16+4t, 32+4t, 48+4t) as one 16-byte load.
-    for (int i = tid; i < npad * 16; i += AM_THREADS) {
+    for (int i = tid; i < (STREAM ? 0 : npad * 16); i += AM_THREADS) {
         const int key = i >> 4, wk = i & 15;   // source word: dims 4*wk .. 4*wk+3
         uint32_t v = 0, kw = 0;
         if (key < n) {
@@ -361,26 +387,50 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
             for (int k = 0; k < 4; k++) { hiacc[mi][k] = 0; loacc[mi][k] = 0; }
         int shs[4] = {0, 0, 0, 0}, sls[4] = {0, 0, 0, 0};   // weight sums of rows 2t, 2t+1 in [0], [1]
 
+        if (STREAM) decode_tile_async(ring, kg, vg, 0, lane);   // the task's tile 0 in flight
         for (int kb = 0; kb <= p_last; kb += 32) {
+            const uint8_t *kst = ks + kb * 64;   // K rows of the tile
+            if (STREAM) {   // the next tile's copy overlaps this tile's work; then wait for this one
+                if (kb + 32 <= p_last) {
+                    decode_tile_async(ring + (((kb >> 5) + 1) & 1) * 4096, kg, vg, kb + 32, lane);
+                    asm volatile("cp.async.wait_group 1;" ::: "memory");
+                } else {
+                    asm volatile("cp.async.wait_group 0;" ::: "memory");
+                }
+                __syncwarp();
+                kst = ring + ((kb >> 5) & 1) * 4096;
+            }
             // ---- S = Q K^T over 32 keys (permuted columns) ----
             int sacc[4][4];
 #pragma unroll
             for (int j = 0; j < 4; j++) {
                 sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0;
-                const uint4 kw = *reinterpret_cast<const uint4 *>(ks + (kb + perm_key(8 * j + g)) * 64 + 16 * t);
+                const uint4 kw = *reinterpret_cast<const uint4 *>(kst + perm_key(8 * j + g) * 64 + 16 * t);
                 mma_s8s8(sacc[j], qa[0], kw.x, kw.y);
                 mma_s8s8(sacc[j], qa[1], kw.z, kw.w);
             }
             // V^T A fragments: dims 16mi+g / +8; K 4t.. (word 0) and 16+4t.. (word 1) = keys 8t..8t+7
             uint32_t va[4][4];
+            if (STREAM) {   // V tile [8 key groups][64 dims][4 keys]: words of groups 2t, 2t+1
+                const uint32_t *vtile = reinterpret_cast<const uint32_t *>(kst + 2048) + 2 * t * 64;
 #pragma unroll
-            for (int mi = 0; mi < 4; mi++) {
-                const uint2 lo2 = *reinterpret_cast<const uint2 *>(vt + (16 * mi + g) * vt_ld + kb + 8 * t);
-                const uint2 hi2 = *reinterpret_cast<const uint2 *>(vt + (16 * mi + g + 8) * vt_ld + kb + 8 * t);
-                va[mi][0] = lo2.x;
-                va[mi][1] = hi2.x;
-                va[mi][2] = lo2.y;
-                va[mi][3] = hi2.y;
+                for (int mi = 0; mi < 4; mi++) {
+                    va[mi][0] = vtile[16 * mi + g];
+                    va[mi][1] = vtile[16 * mi + g + 8];
+                    va[mi][2] = vtile[64 + 16 * mi + g];
+                    va[mi][3] = vtile[64 + 16 * mi + g + 8];
+                }
+                __syncwarp();   // every lane has its fragments: the stage may be refilled next tile
+            } else {
+#pragma unroll
+                for (int mi = 0; mi < 4; mi++) {
+                    const uint2 lo2 = *reinterpret_cast<const uint2 *>(vt + (16 * mi + g) * vt_ld + kb + 8 * t);
+                    const uint2 hi2 = *reinterpret_cast<const uint2 *>(vt + (16 * mi + g + 8) * vt_ld + kb + 8 * t);
+                    va[mi][0] = lo2.x;
+                    va[mi][1] = hi2.x;
+                    va[mi][2] = lo2.y;
+                    va[mi][3] = hi2.y;
+                }
             }
 
             Tile T;
@@ -481,22 +531,6 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
         }
         __syncwarp();
     }
-}
-
-__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
-                 : "memory");
-}
-
-// The 4 KB of one 32-key tile of a stream (K rows, then the V tile) into a
-// shared-memory stage, 8 x 16 bytes per lane, as one cp.async group.
-__device__ __forceinline__ void decode_tile_async(uint8_t *stage, const int8_t *ks, const int8_t *vt, int kb, int lane) {
-#pragma unroll
-    for (int i = 0; i < 4; i++) cp_async16(stage + 16 * (lane + 32 * i), ks + (size_t)kb * 64 + 16 * (lane + 32 * i));
-#pragma unroll
-    for (int i = 0; i < 4; i++)
-        cp_async16(stage + 2048 + 16 * (lane + 32 * i), vt + (size_t)kb * 64 + 16 * (lane + 32 * i));
-    asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
 // Decode: one warp per stream r, the query of every head at position p against
@@ -729,14 +763,22 @@ size_t attention_mma_smem(int max_len) {
 
 bool attention_mma_fits(int max_len) { return max_len <= AM_MAX_KEYS; }
 
+constexpr int AM_STREAM_SMEM = AM_WARPS * AM_WARP_SMEM + AM_LUT * 2 + AM_WARPS * 8192;
+
 void attention_mma_init() {
     cudaFuncSetAttribute(k_attention_decode_mma<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM);
     cudaFuncSetAttribute(k_attention_decode_mma<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM);
     cudaFuncSetAttribute(k_attention_decode_mma<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM);
     const int smem = (int)attention_mma_smem(AM_MAX_KEYS);
-    cudaFuncSetAttribute(k_attention_mma<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    cudaFuncSetAttribute(k_attention_mma<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    cudaFuncSetAttribute(k_attention_mma<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(k_attention_mma<false, false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(k_attention_mma<false, true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(k_attention_mma<true, false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(k_attention_mma<false, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         AM_STREAM_SMEM);
+    cudaFuncSetAttribute(k_attention_mma<false, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         AM_STREAM_SMEM);
+    cudaFuncSetAttribute(k_attention_mma<true, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         AM_STREAM_SMEM);
 }
 
 void launch_attention_mma(const int8_t *qkv, int ldq, const int8_t *kv, const int *chunk_row0,
@@ -747,17 +789,37 @@ void launch_attention_mma(const int8_t *qkv, int ldq, const int8_t *kv, const in
     if (n_chunks == 0) return;
     const size_t smem = attention_mma_smem(max_len);
     if (wide_mult)
-        k_attention_mma<true, false><<<n_chunks, AM_THREADS, smem, st>>>(
+        k_attention_mma<true, false, false><<<n_chunks, AM_THREADS, smem, st>>>(
             qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
-            lut4k, out, ldo);
+            lut4k, out, ldo, nullptr);
     else if (exp0)
-        k_attention_mma<false, true><<<n_chunks, AM_THREADS, smem, st>>>(
+        k_attention_mma<false, true, false><<<n_chunks, AM_THREADS, smem, st>>>(
             qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
-            lut4k, out, ldo);
+            lut4k, out, ldo, nullptr);
     else
-        k_attention_mma<false, false><<<n_chunks, AM_THREADS, smem, st>>>(
+        k_attention_mma<false, false, false><<<n_chunks, AM_THREADS, smem, st>>>(
             qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
-            lut4k, out, ldo);
+            lut4k, out, ldo, nullptr);
+}
+
+void launch_attention_mma_stream(const int8_t *qkv, int ldq, const int8_t *kv, const int *chunk_row0,
+                                 const int *chunk_len, const int *chunk_kvoff, int n_chunks, int n_heads,
+                                 const int32_t *score_mult, const int8_t *sink_key, const int16_t *rope_cos,
+                                 const int16_t *rope_sin, const uint16_t *lut4k, bool wide_mult, bool exp0,
+                                 int8_t *out, int ldo, cudaStream_t st) {
+    if (n_chunks == 0) return;
+    if (wide_mult)
+        k_attention_mma<true, false, true><<<n_chunks, AM_THREADS, AM_STREAM_SMEM, st>>>(
+            qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
+            lut4k, out, ldo, chunk_kvoff);
+    else if (exp0)
+        k_attention_mma<false, true, true><<<n_chunks, AM_THREADS, AM_STREAM_SMEM, st>>>(
+            qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
+            lut4k, out, ldo, chunk_kvoff);
+    else
+        k_attention_mma<false, false, true><<<n_chunks, AM_THREADS, AM_STREAM_SMEM, st>>>(
+            qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
+            lut4k, out, ldo, chunk_kvoff);
 }
 
 bool attention_decode_mma_ok(int n_heads) { return n_heads >= 1 && n_heads <= AM_ROWS; }

@@ -101,6 +101,8 @@ struct czg_ctx {
     uint64_t *slot_off = nullptr, *pack_off = nullptr, *chunk_tok0 = nullptr;
     int *chunk_row0 = nullptr, *chunk_len = nullptr;
     int *att_row0 = nullptr, *att_len = nullptr;   // the chunks in attention launch order
+    int *att_kvoff = nullptr;                        // and their streaming K/V offsets (128-byte units)
+    int *rowchunk = nullptr;                         // chunk of each row of a wave
     // tcgen05 path: TMA descriptors of the GEMM A operands (wave buffers) and the head
     bool use_tc = false;
     TcMatrix tm_xn, tm_attn, tm_h, tm_head;
@@ -417,7 +419,8 @@ int alloc_workspace(czg_ctx *c, int rows, int chunks) {
     size_t R = (size_t)(rows + 127) / 128 * 128 + 128;
     bool ok = dalloc_ws(c, &c->tokens, R) && dalloc_ws(c, &c->tok_in, R) && dalloc_ws(c, &c->tok_out, R) &&
               dalloc_ws(c, &c->pos, R) && dalloc_ws(c, &c->x_res, R * d) && dalloc_ws(c, &c->xn, R * d) &&
-              dalloc_ws(c, &c->qkv, R * (d + 128)) && dalloc_ws(c, &c->kv, R * 128) &&
+              dalloc_ws(c, &c->qkv, R * (d + 128)) && dalloc_ws(c, &c->kv, R * 128 + (size_t)chunks * 4096) &&
+              dalloc_ws(c, &c->rowchunk, R) &&
               dalloc_ws(c, &c->attn, R * d) && dalloc_ws(c, &c->o8, R * d) &&
               dalloc_ws(c, &c->hbuf, R * m.d_ff) && dalloc_ws(c, &c->logits, R * c->vpad) &&
               dalloc_ws(c, &c->lohi, R) && dalloc_ws(c, &c->slots, 4 * R + 8 * (size_t)chunks + 64) &&
@@ -426,6 +429,7 @@ int alloc_workspace(czg_ctx *c, int rows, int chunks) {
               dalloc_ws(c, &c->pack_off, (size_t)chunks + 1) && dalloc_ws(c, &c->chunk_tok0, (size_t)chunks) &&
               dalloc_ws(c, &c->chunk_row0, (size_t)chunks) && dalloc_ws(c, &c->chunk_len, (size_t)chunks) &&
               dalloc_ws(c, &c->att_row0, (size_t)chunks) && dalloc_ws(c, &c->att_len, (size_t)chunks) &&
+              dalloc_ws(c, &c->att_kvoff, (size_t)chunks) &&
               dalloc_ws(c, &c->err_flag, 1);
     if (!ok) return CZG_E_DEVICE;
     cudaMemsetAsync(c->err_flag, 0, sizeof(int), c->stream);
@@ -451,7 +455,7 @@ int alloc_workspace(czg_ctx *c, int rows, int chunks) {
     const char *hc = getenv("CZG_HEAD_CDF");
     c->head_cdf = c->use_tc && !(hc && std::string(hc) == "0") && c->exp0 && c->logit_small &&
                   m.vocab_size == c->vpad && c->vpad % 256 == 0 && m.coef_q24 < (1u << 23) && d % 128 == 0;
-    c->h_meta_bytes = (size_t)chunks * 40 + 64;
+    c->h_meta_bytes = (size_t)chunks * 48 + 64;
     if (!cuda_ok(c, cudaMallocHost(&c->h_meta, c->h_meta_bytes), "cudaMallocHost")) return CZG_E_DEVICE;
     return CZG_OK;
 }
@@ -515,24 +519,27 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
     // tails) then fill the last round of CTAs instead of leaving SMs idle
     int *h_arow0 = reinterpret_cast<int *>(h_slot + nc + 1);
     int *h_alen = h_arow0 + nc;
+    int *h_akv = h_alen + nc;
     c->att_order.resize(nc);
     for (int i = 0; i < nc; i++) c->att_order[i] = i;
     std::stable_sort(c->att_order.begin(), c->att_order.end(), [&](int a, int b) { return h_len[a] > h_len[b]; });
     for (int i = 0; i < nc; i++) {
         h_arow0[i] = h_row0[c->att_order[i]];
         h_alen[i] = h_len[c->att_order[i]];
+        h_akv[i] = h_row0[c->att_order[i]] + 32 * c->att_order[i];   // k_kv_prep_split's chunk offsets
     }
     cudaMemcpyAsync(c->chunk_row0, h_row0, sizeof(int) * nc, cudaMemcpyHostToDevice, st);
     cudaMemcpyAsync(c->chunk_len, h_len, sizeof(int) * nc, cudaMemcpyHostToDevice, st);
     cudaMemcpyAsync(c->att_row0, h_arow0, sizeof(int) * nc, cudaMemcpyHostToDevice, st);
     cudaMemcpyAsync(c->att_len, h_alen, sizeof(int) * nc, cudaMemcpyHostToDevice, st);
+    cudaMemcpyAsync(c->att_kvoff, h_akv, sizeof(int) * nc, cudaMemcpyHostToDevice, st);
     cudaMemcpyAsync(c->chunk_tok0, h_tok0, sizeof(uint64_t) * nc, cudaMemcpyHostToDevice, st);
     cudaMemcpyAsync(c->slot_off, h_slot, sizeof(uint64_t) * (nc + 1), cudaMemcpyHostToDevice, st);
     cudaMemsetAsync(c->err_flag, 0, sizeof(int), st);
 
     timed(c, kRows, [&] {
         launch_rows(d_tok, c->chunk_row0, c->chunk_len, c->chunk_tok0, nc, V, c->tok_in, c->tok_out,
-                    c->pos, c->err_flag, st);
+                    c->pos, c->rowchunk, c->err_flag, st);
     });
     timed(c, kEmbedNorm, [&] {
         launch_embed_norm(c->tok_in, c->embed, c->layers[0].attn_norm, M, d, c->inv_tab, c->x_res, c->res16, false,
@@ -544,14 +551,25 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
             gemm(c, c->tm_xn, L.tm_qkv, c->xn, L.qkv_w, M, d + 128, d, kEpiRequant, L.qkv_mult, L.qkv_shift,
                  c->qkv, d + 128);
         });
+        // tensor-core attention: K / V^T of a chunk staged in shared memory up to 1024
+        // keys, streamed from a per-chunk tile layout beyond
+        const bool stream = !attention_mma_fits(max_len) && !c->scalar_attention;
         timed(c, kKvPrep, [&] {
-            launch_kv_prep(c->qkv, d + 128, d, c->pos, c->rope_cos, c->rope_sin, M, c->kv, st);
+            if (stream)
+                launch_kv_prep_split(c->qkv, d + 128, d, c->pos, c->rowchunk, c->chunk_row0, c->chunk_len,
+                                     c->rope_cos, c->rope_sin, M, c->kv, st);
+            else
+                launch_kv_prep(c->qkv, d + 128, d, c->pos, c->rope_cos, c->rope_sin, M, c->kv, st);
         });
         timed(c, kAttention, [&] {
             if (attention_mma_fits(max_len) && !c->scalar_attention)
                 launch_attention_mma(c->qkv, d + 128, c->kv, c->att_row0, c->att_len, nc, max_len, H,
                                      L.score_mult, L.sink_key, c->rope_cos, c->rope_sin, c->lut4k,
                                      L.wide_mult, c->exp0, c->attn, d, st);
+            else if (stream)
+                launch_attention_mma_stream(c->qkv, d + 128, c->kv, c->att_row0, c->att_len, c->att_kvoff, nc, H,
+                                            L.score_mult, L.sink_key, c->rope_cos, c->rope_sin, c->lut4k,
+                                            L.wide_mult, c->exp0, c->attn, d, st);
             else
                 launch_attention(c->qkv, d + 128, c->kv, c->att_row0, c->att_len, nc, max_len, H,
                                  L.score_mult, L.sink_key, c->rope_cos, c->rope_sin, c->lut, c->attn, d, st);

@@ -20,7 +20,7 @@ void kernels_init();
 // rows.cu
 void launch_rows(const uint32_t *tokens, const int *chunk_row0, const int *chunk_len,
                  const uint64_t *chunk_tok0, int n_chunks, int vocab, uint32_t *tok_in,
-                 uint32_t *tok_out, int *pos, int *err, cudaStream_t st);
+                 uint32_t *tok_out, int *pos, int *rowchunk, int *err, cudaStream_t st);
 // inv_tab: inv_rms_q15 by floor(sum_sq / d), kInvTabEntries entries, from launch_inv_table.
 // x_res: the residual stream, int16 when res16 (exact for n_layers <= 128), else int32
 constexpr int kInvTabEntries = 16384;
@@ -37,6 +37,11 @@ void launch_residual_norm(const int8_t *o, const int8_t *post_w, const int8_t *n
                           void *x_res, bool res16, int8_t *xn, cudaStream_t st);
 void launch_kv_prep(const int8_t *qkv, int ldq, int d, const int *pos, const int16_t *rope_cos,
                     const int16_t *rope_sin, int M, int8_t *kv, cudaStream_t st);
+// the per-chunk streaming layout (see rows.cu): chunk c from (chunk_row0[c] + 32 c) * 128
+// bytes of kv, which holds (rows + 32 * chunks) * 128 bytes
+void launch_kv_prep_split(const int8_t *qkv, int ldq, int d, const int *pos, const int *rowchunk,
+                          const int *chunk_row0, const int *chunk_len, const int16_t *rope_cos,
+                          const int16_t *rope_sin, int M, int8_t *kv, cudaStream_t st);
 
 // gemm_mma.cu: C[M,N] = A[M,K] . B[N,K]^T in int8 -> int32 with an epilogue.
 // A must hold ceil(M/128)*128 readable rows; N % 128 == 0; K % 64 == 0.
@@ -72,7 +77,8 @@ bool launch_gemm_tc(const TcMatrix &A, const TcMatrix &B, int M, int N, int K, i
                     void *out, int ldo, int *err, cudaStream_t st);
 
 void attention_init();
-// attention_mma.cu: tensor-core version for chunks of at most 1024 positions;
+// attention_mma.cu: tensor-core version, K/V of a chunk staged in shared memory for
+// chunks of at most 1024 positions (launch_attention_mma_stream for longer ones);
 // lut4k = exp_q16 tabulated by t256 <= 4096 (entries from 4096 on are 1); exp0: lut4k[0] == 65535
 bool attention_mma_fits(int max_len);
 void attention_mma_init();
@@ -89,6 +95,13 @@ void launch_attention_mma(const int8_t *qkv, int ldq, const int8_t *kv, const in
                           const int32_t *score_mult, const int8_t *sink_key, const int16_t *rope_cos,
                           const int16_t *rope_sin, const uint16_t *lut4k, bool wide_mult, bool exp0,
                           int8_t *out, int ldo, cudaStream_t st);
+// Chunks of any length: K and V in the streaming layout of launch_kv_prep_split,
+// chunk i of the launch at chunk_kvoff[i] * 128 bytes of kv
+void launch_attention_mma_stream(const int8_t *qkv, int ldq, const int8_t *kv, const int *chunk_row0,
+                                 const int *chunk_len, const int *chunk_kvoff, int n_chunks, int n_heads,
+                                 const int32_t *score_mult, const int8_t *sink_key, const int16_t *rope_cos,
+                                 const int16_t *rope_sin, const uint16_t *lut4k, bool wide_mult, bool exp0,
+                                 int8_t *out, int ldo, cudaStream_t st);
 // attention.cu: one CTA per chunk; rows of chunk c are chunk_row0[c] ..+chunk_len[c]
 void launch_attention(const int8_t *qkv, int ldq, const int8_t *kv, const int *chunk_row0,
                       const int *chunk_len, int n_chunks, int max_len, int n_heads,

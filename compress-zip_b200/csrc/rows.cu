@@ -13,11 +13,12 @@
 namespace czg {
 
 // One CTA per chunk: token ids into the forward (BOS at position 0, else the
-// previous token, rust/src/main.rs:212-214), the symbol to encode, the position.
+// previous token, rust/src/main.rs:212-214), the symbol to encode, the position,
+// and the row's chunk.
 __global__ void k_rows(const uint32_t *__restrict__ tokens, const int *__restrict__ chunk_row0,
                        const int *__restrict__ chunk_len, const uint64_t *__restrict__ chunk_tok0,
                        int vocab, uint32_t *__restrict__ tok_in, uint32_t *__restrict__ tok_out,
-                       int *__restrict__ pos, int *__restrict__ err) {
+                       int *__restrict__ pos, int *__restrict__ rowchunk, int *__restrict__ err) {
     int c = blockIdx.x;
     int r0 = chunk_row0[c], n = chunk_len[c];
     const uint32_t *src = tokens + chunk_tok0[c];
@@ -28,6 +29,7 @@ __global__ void k_rows(const uint32_t *__restrict__ tokens, const int *__restric
         tok_in[r0 + i] = min(prev, (uint32_t)(vocab - 1));   // kept in bounds; the error flag reports it
         tok_out[r0 + i] = min(t, (uint32_t)(vocab - 1));
         pos[r0 + i] = i;
+        rowchunk[r0 + i] = c;
     }
 }
 
@@ -195,14 +197,43 @@ __global__ void k_kv_prep(const int8_t *__restrict__ qkv, int ldq, int d, const 
     reinterpret_cast<uint16_t *>(dst + 64)[i] = reinterpret_cast<const uint16_t *>(k + 64)[i];
 }
 
+// K rotated (attention.rs:29-50) and V of every row into its chunk's streaming
+// layout (the tensor-core attention for chunks longer than its shared memory
+// holds): chunk c at kv + (chunk_row0[c] + 32 c) * 128 bytes, its keys' K rows of
+// 64 permuted dims (bytes [16t' + 4k + b] = dim 16k + 4t' + b) first, then V in
+// 32-key tiles of 2 KB from npad * 64 on (npad = len rounded up to 32), byte
+// (key, dim) at tile * 2048 + (key % 32 / 4) * 256 + dim * 4 + key % 4 -- the
+// decode cache layout of k_kv_append, per chunk.  One warp per row.
+__global__ void k_kv_prep_split(const int8_t *__restrict__ qkv, int ldq, int d, const int *__restrict__ pos,
+                                const int *__restrict__ rowchunk, const int *__restrict__ chunk_row0,
+                                const int *__restrict__ chunk_len, const int16_t *__restrict__ rope_cos,
+                                const int16_t *__restrict__ rope_sin, int M, int8_t *__restrict__ kv) {
+    const int gid = blockIdx.x * blockDim.x + threadIdx.x;
+    const int row = gid >> 5, i = gid & 31;
+    if (row >= M) return;
+    const int8_t *k = qkv + (size_t)row * ldq + d;
+    const int p = pos[row], c = rowchunk[row];
+    const int npad = (chunk_len[c] + 31) & ~31;
+    int8_t *base = kv + ((size_t)chunk_row0[c] + 32 * (size_t)c) * 128;
+    const int x = k[i], y = k[i + kHalfDim];
+    const int cs = rope_cos[p * kHalfDim + i], sn = rope_sin[p * kHalfDim + i];
+    int8_t *kr = base + (size_t)p * 64;
+    const int i2 = i + kHalfDim;
+    kr[16 * ((i >> 2) & 3) + 4 * (i >> 4) + (i & 3)] = (int8_t)clamp127(sra_rne32(x * cs - y * sn, 15));
+    kr[16 * ((i2 >> 2) & 3) + 4 * (i2 >> 4) + (i2 & 3)] = (int8_t)clamp127(sra_rne32(x * sn + y * cs, 15));
+    int8_t *vt = base + (size_t)npad * 64 + (size_t)(p >> 5) * 2048 + ((p & 31) >> 2) * 256 + (p & 3);
+    vt[(2 * i) * 4] = k[64 + 2 * i];
+    vt[(2 * i + 1) * 4] = k[64 + 2 * i + 1];
+}
+
 // ---- host launchers -------------------------------------------------------
 
 void launch_rows(const uint32_t *tokens, const int *chunk_row0, const int *chunk_len,
                  const uint64_t *chunk_tok0, int n_chunks, int vocab, uint32_t *tok_in,
-                 uint32_t *tok_out, int *pos, int *err, cudaStream_t st) {
+                 uint32_t *tok_out, int *pos, int *rowchunk, int *err, cudaStream_t st) {
     if (n_chunks == 0) return;
     k_rows<<<n_chunks, 256, 0, st>>>(tokens, chunk_row0, chunk_len, chunk_tok0, vocab, tok_in,
-                                     tok_out, pos, err);
+                                     tok_out, pos, rowchunk, err);
 }
 
 template <typename RT, bool STORE>
@@ -266,6 +297,15 @@ void launch_residual_norm(const int8_t *o, const int8_t *post_w, const int8_t *n
         residual_norm_mode(o, post_w, next_w, M, d, inv_tab, tok_in, embed, store_res, static_cast<int16_t *>(x_res), xn, st);
     else
         residual_norm_mode(o, post_w, next_w, M, d, inv_tab, tok_in, embed, store_res, static_cast<int32_t *>(x_res), xn, st);
+}
+
+void launch_kv_prep_split(const int8_t *qkv, int ldq, int d, const int *pos, const int *rowchunk,
+                          const int *chunk_row0, const int *chunk_len, const int16_t *rope_cos,
+                          const int16_t *rope_sin, int M, int8_t *kv, cudaStream_t st) {
+    if (M == 0) return;
+    const long long threads = (long long)M * 32;
+    k_kv_prep_split<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(qkv, ldq, d, pos, rowchunk, chunk_row0,
+                                                                       chunk_len, rope_cos, rope_sin, M, kv);
 }
 
 void launch_kv_prep(const int8_t *qkv, int ldq, int d, const int *pos, const int16_t *rope_cos,

@@ -289,10 +289,11 @@ def test_int32_residual_path(shipped_path, shipped_oracle, oracle_mod, shipped_t
         eng.close()
 
 
-def test_config4_long_chunk(tmp_path, shipped_path, oracle_mod):
-    """Configuration-4 shape: the arch-2 model at context 4096 with a chunk longer
-    than 1024 positions (the CUDA-core attention kernel over global-memory K/V),
-    compressed bytes equal to the oracle's, and decoded back on the GPU."""
+def test_config4_long_chunks(tmp_path, shipped_path, oracle_mod, monkeypatch):
+    """Configuration-4 shape: the arch-2 model at context 4096 with chunks longer
+    than 1024 positions next to short ones (the tensor-core attention streaming
+    K/V tiles from the per-chunk layout), compressed bytes equal to the oracle's
+    and to the CUDA-core attention's, and decoded back on the GPU."""
     from compress_zip_b200 import czm, synth
     from compress_zip_b200.engine import Engine
 
@@ -301,14 +302,20 @@ def test_config4_long_chunk(tmp_path, shipped_path, oracle_mod):
     p = tmp_path / "arch2_4096.czm"
     p.write_bytes(data)
     om = oracle_mod.load_model(str(p))
-    toks = np.array(mf.tokenizer().encode_with_special_tokens(synth.document(10000, 2000)), np.uint32)[:1300]
-    starts = np.array([0, len(toks)], np.uint64)
+    toks = np.array(mf.tokenizer().encode_with_special_tokens(synth.document(10000, 4000)), np.uint32)[:2500]
+    starts = np.array([0, 1300, 1337, 2500], np.uint64)
     eng = Engine(data, 0)
     try:
         want = oracle_mod.compress_chunks(om, toks, starts)
         got = eng.compress_chunks(toks, starts)
         assert got == want
-        assert np.array_equal(eng.decompress_chunks(got, np.array([len(toks)], np.uint32)), toks)
+        assert np.array_equal(eng.decompress_chunks(got, np.diff(starts).astype(np.uint32)), toks)
+    finally:
+        eng.close()
+    monkeypatch.setenv("CZG_SCALAR_ATTENTION", "1")
+    eng = Engine(data, 0)
+    try:
+        assert eng.compress_chunks(toks, starts) == want
     finally:
         eng.close()
 
