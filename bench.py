@@ -58,6 +58,8 @@ def parse():
                     help="host pipeline sample (tokenise + GPU coder + CZIPv1 + brotli); 0 skips")
     ap.add_argument("--config2-docs", type=int, default=256,
                     help="config 2: documents of 64 KiB compressed with the arch-2 model at ctx 512 (0 skips)")
+    ap.add_argument("--config4-docs", type=int, default=64,
+                    help="config 4 sample: documents of 64 KiB with the arch-2 model at ctx 4096 (0 skips)")
     return ap.parse_args()
 
 
@@ -295,7 +297,8 @@ def main():
     parity = bytes(h_out_np[:nout_h]) == bytes(out[:nout])
 
     dec = decode_bench(eng, mf, rank, args, stream, world) if args.decode_docs > 0 else None
-    cfg2 = config2_bench(mf, rank, args, stream, local) if args.config2_docs > 0 else None
+    cfg2 = arch2_bench(mf, rank, args, stream, local, 2) if args.config2_docs > 0 else None
+    cfg4 = arch2_bench(mf, rank, args, stream, local, 4) if args.config4_docs > 0 else None
     pipe = host_pipeline(eng, mf, args) if rank == 0 and args.pipeline_docs > 0 else None
 
     (t_max, t_e2e_max), (all_tok, all_bytes) = reduce_over_ranks(
@@ -362,6 +365,8 @@ def main():
             line["decode"] = dec
         if cfg2 is not None:
             line["config2"] = cfg2
+        if cfg4 is not None:
+            line["config4"] = cfg4
         if pipe is not None:
             line["host_pipeline"] = pipe
         if cpu is not None:
@@ -372,25 +377,28 @@ def main():
         dist.destroy_process_group()
 
 
-def config2_bench(mf, rank, args, stream, local):
-    """documents of 64 KiB (seeds 3000.., rank r: +r*N)
-    compressed at ctx 512 with the arch-2 model (d 512, 8 layers, 8 heads, 2 KV
-    heads, d_ff 2048; synthetic int8 weights from seed 7, compress_zip_b200/synth.py).
-    Tokens resident in HBM, L2 flushed before each timed step, CUDA events on the
-    engine's stream; the per-kernel split gives the GEMMs' int8 tensor throughput.
-    Each rank reports its own figure (no collective here)."""
+def arch2_bench(mf, rank, args, stream, local, cfg):
+    """BASELINE configuration 2 (cfg 2: documents of 64 KiB, seeds 3000.., at ctx 512)
+    or a bounded sample of configuration 4 (cfg 4: documents of 64 KiB, seeds
+    10000.., at ctx 4096; the configuration itself is a 1 GB corpus) compressed with
+    the arch-2 model (d 512, 8 layers, 8 heads, 2 KV heads, d_ff 2048; synthetic
+    int8 weights from seed 7, compress_zip_b200/synth.py) at that context.  Rank r
+    takes seeds +r*N.  Tokens resident in HBM, L2 flushed before each timed step,
+    CUDA events on the engine's stream; the per-kernel split gives the GEMMs' int8
+    tensor throughput.  Each rank reports its own figure (no collective here)."""
     import torch
     from compress_zip_b200.engine import Engine
 
-    model = synth.arch2_model(mf, 512)
+    ctx, n_docs, first = (512, args.config2_docs, 3000) if cfg == 2 else (4096, args.config4_docs, 10000)
+    model = synth.arch2_model(mf, ctx)
     a = synth.ARCH2
     tok = mf.tokenizer()
-    docs = synth.documents(shard_seeds(rank, args.config2_docs, first=3000), 65536)
+    docs = synth.documents(shard_seeds(rank, n_docs, first=first), 65536)
     ids = tok.encode_batch_arrays(docs, num_threads=min(16, os.cpu_count() or 1))
     starts, b = [0], 0
     for t in ids:
-        for s0 in range(0, len(t), 512):
-            starts.append(b + min(s0 + 512, len(t)))
+        for s0 in range(0, len(t), ctx):
+            starts.append(b + min(s0 + ctx, len(t)))
         b += len(t)
     tokens = np.concatenate([np.asarray(t, dtype=np.uint32) for t in ids])
     starts = np.asarray(starts, dtype=np.uint64)
@@ -428,9 +436,10 @@ def config2_bench(mf, rank, args, stream, local):
     gemm_ops = sum(2.0 * m * n_tok * steps for k, m in macs.items() if kern.get(k, 0.0) > 0)
     _, _, bf16_sus, basis = peaks()
     tops = gemm_ops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else 0.0
-    return {"metric": "compress tokens/s (config 2: arch-2 model, ctx 512, 64 KiB docs)",
+    return {"metric": f"compress tokens/s (config {cfg}{'' if cfg == 2 else ' sample'}: arch-2 model, "
+                      f"ctx {ctx}, 64 KiB docs)",
             "value": round(n_tok * steps / (t / 1e3), 1), "unit": "tokens/s", "steps": steps,
-            "ms_per_step": round(t / steps, 3), "docs_per_gpu": args.config2_docs, "tokens_per_gpu": n_tok,
+            "ms_per_step": round(t / steps, 3), "docs_per_gpu": n_docs, "tokens_per_gpu": n_tok,
             "chunks_per_gpu": n_chunks,
             "mb_per_s": round(sum(len(x.encode()) for x in docs) * steps / (t / 1e3) / 1e6, 3),
             "kernels_ms_per_step": {k: round(v / steps, 3) for k, v in kern.items() if v > 0},
