@@ -74,6 +74,7 @@ struct czg_ctx {
     czg_model_info info{};
     int eps = 1;
     bool scalar_attention = false;   // CZG_SCALAR_ATTENTION=1 selects the CUDA-core kernel
+    bool staged_attention = false;   // CZG_ATTN_STAGED=1: chunks <= 1024 keys with K/V^T staged in shared memory
     int vpad = 0;           // vocab rounded up to the GEMM tile (extra head rows are zero)
     int8_t *embed = nullptr, *final_norm = nullptr, *head_w = nullptr;
     uint16_t *lut = nullptr;
@@ -551,9 +552,11 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
             gemm(c, c->tm_xn, L.tm_qkv, c->xn, L.qkv_w, M, d + 128, d, kEpiRequant, L.qkv_mult, L.qkv_shift,
                  c->qkv, d + 128);
         });
-        // tensor-core attention: K / V^T of a chunk staged in shared memory up to 1024
-        // keys, streamed from a per-chunk tile layout beyond
-        const bool stream = !attention_mma_fits(max_len) && !c->scalar_attention;
+        // tensor-core attention, K/V tiles streamed per warp from a per-chunk layout (at
+        // 1024 keys 129.6 ms per configuration-1 step against 136.0 with the chunk's
+        // K/V^T staged in shared memory, which CZG_ATTN_STAGED=1 selects up to 1024 keys)
+        const bool staged = c->staged_attention && attention_mma_fits(max_len) && !c->scalar_attention;
+        const bool stream = !staged && !c->scalar_attention;
         timed(c, kKvPrep, [&] {
             if (stream)
                 launch_kv_prep_split(c->qkv, d + 128, d, c->pos, c->rowchunk, c->chunk_row0, c->chunk_len,
@@ -562,7 +565,7 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
                 launch_kv_prep(c->qkv, d + 128, d, c->pos, c->rope_cos, c->rope_sin, M, c->kv, st);
         });
         timed(c, kAttention, [&] {
-            if (attention_mma_fits(max_len) && !c->scalar_attention)
+            if (staged)
                 launch_attention_mma(c->qkv, d + 128, c->kv, c->att_row0, c->att_len, nc, max_len, H,
                                      L.score_mult, L.sink_key, c->rope_cos, c->rope_sin, c->lut4k,
                                      L.wide_mult, c->exp0, c->attn, d, st);
@@ -956,6 +959,7 @@ int czg_ctx_create(int device, const uint8_t *czm, size_t czm_len, czg_ctx **out
     c->stream = c->own_stream;
     if (!st) st = load_model(c, czm, czm_len);
     c->scalar_attention = getenv("CZG_SCALAR_ATTENTION") && atoi(getenv("CZG_SCALAR_ATTENTION")) != 0;
+    c->staged_attention = getenv("CZG_ATTN_STAGED") && atoi(getenv("CZG_ATTN_STAGED")) != 0;
     c->kernel_timing = getenv("CZG_KERNEL_TIMING") && atoi(getenv("CZG_KERNEL_TIMING")) != 0;
     // tokens per wave: large waves keep every SM busy through the per-chunk serial
     // encoder and the attention's last CTAs; the workspace grows to it on demand

@@ -209,14 +209,20 @@ def _variant_model(shipped_path, tmp_path, sink=False, score_mult=None):
     return data, str(p)
 
 
+@pytest.mark.parametrize("staged", [False, True])
 @pytest.mark.parametrize("sink,score_mult", [
     (True, None),
     (False, [1 << 20, 1 << 24, 2147483647, -2147483647, 3, -60000]),   # record-heavy, clamped scores
     (True, [400000, 1, 70000, 58218, -58218, 900000]),
 ])
-def test_attention_edge_models(shipped_path, tmp_path, oracle_mod, shipped_tokens, sink, score_mult):
+def test_attention_edge_models(shipped_path, tmp_path, oracle_mod, shipped_tokens, sink, score_mult, staged,
+                               monkeypatch):
+    """Both tensor-core chunk attention forms: K/V tiles streamed per warp (the
+    default) and the chunk's K/V^T staged in shared memory (CZG_ATTN_STAGED=1)."""
     from compress_zip_b200.engine import Engine
 
+    if staged:
+        monkeypatch.setenv("CZG_ATTN_STAGED", "1")
     data, path = _variant_model(shipped_path, tmp_path, sink, score_mult)
     om = oracle_mod.load_model(path)
     eng = Engine(data, 0)
@@ -229,11 +235,13 @@ def test_attention_edge_models(shipped_path, tmp_path, oracle_mod, shipped_token
         eng.close()
 
 
-def test_scalar_attention_kernel(shipped_path, shipped_oracle, oracle_mod, shipped_tokens, monkeypatch):
-    """The CUDA-core attention kernel (used beyond 1024 positions) on short chunks too."""
+@pytest.mark.parametrize("env", ["CZG_SCALAR_ATTENTION", "CZG_ATTN_STAGED"])
+def test_other_attention_kernels(shipped_path, shipped_oracle, oracle_mod, shipped_tokens, monkeypatch, env):
+    """The CUDA-core attention kernel and the shared-memory-staged tensor-core kernel,
+    each selected by its switch, against the oracle."""
     from compress_zip_b200.engine import Engine
 
-    monkeypatch.setenv("CZG_SCALAR_ATTENTION", "1")
+    monkeypatch.setenv(env, "1")
     eng = Engine.from_file(shipped_path, 0)
     try:
         _trace_equal(eng, shipped_oracle, oracle_mod, shipped_tokens[:300])
