@@ -200,49 +200,65 @@ void cdf_reg(bool full, bool exp0, const int32_t *logits, int V, int ld, const u
     else k_cdf_lohi_reg<G, false, false><<<grid, 256, 0, st>>>(logits, V, ld, sym, lut4k, c8, total, M, lohi);
 }
 
-struct BitSink {
+// MSB-first bit output of one coder (arith_coder.rs:66-73, 122-131): bits gather in
+// a 64-bit accumulator and leave as 4 bytes once 32 are there; bytes past the
+// slot's capacity are counted but not written (the caller reports the overflow).
+struct WordSink {
     uint8_t *out;
     uint32_t cap, len;
     unsigned long long acc;   // pending bits, right-aligned
-    int n;                    // number of pending bits (< 8 between calls)
+    int n;                    // number of pending bits (< 32 between calls)
     bool overflow;
 
-    __device__ __forceinline__ void push(uint32_t bits, int count) {   // count <= 32
-        acc = (acc << count) | bits;
-        n += count;
-        while (n >= 8) {
-            n -= 8;
-            uint8_t b = (uint8_t)(acc >> n);
-            if (len < cap) out[len] = b; else overflow = true;
-            len++;
+    __device__ __forceinline__ void put_byte(uint32_t v) {
+        if (len < cap) out[len] = (uint8_t)v;
+        else overflow = true;
+        len++;
+    }
+    __device__ __forceinline__ void put_word() {   // the top 32 of n >= 32 pending bits
+        n -= 32;
+        const uint32_t w = (uint32_t)(acc >> n);
+        if (len + 4 <= cap && (len & 3u) == 0u) {   // slots start 4-byte aligned
+            *reinterpret_cast<uint32_t *>(out + len) = __byte_perm(w, 0u, 0x0123u);
+            len += 4;
+        } else {
+#pragma unroll
+            for (int q = 0; q < 4; q++) put_byte(w >> (24 - 8 * q));
         }
         acc &= (1ull << n) - 1ull;
     }
-    // one bit followed by `run` copies of its complement (arith_coder.rs:66-73)
-    __device__ __forceinline__ void bit_plus_pending(uint32_t bit, uint32_t run) {
-        push(bit, 1);
-        uint32_t fill = bit ? 0u : 0xFFFFFFFFu;
-        while (run > 0) {
-            int c = run > 32 ? 32 : (int)run;
-            push(c == 32 ? fill : (fill & ((1u << c) - 1u)), c);
-            run -= c;
+    __device__ __forceinline__ void push(uint32_t bits, int count) {   // count <= 32
+        acc = (acc << count) | bits;
+        n += count;
+        if (n >= 32) put_word();
+    }
+    // finish (arith_coder.rs:122-131): a terminating '1', the partial byte padded with zeros
+    __device__ __forceinline__ void finish() {
+        push(1u, 1);
+        const int pad = (8 - (n & 7)) & 7;
+        acc <<= pad;
+        n += pad;
+        while (n >= 8) {
+            n -= 8;
+            put_byte((uint32_t)(acc >> n) & 0xFFu);
         }
     }
 };
 
 // One lane per chunk: the 32 chunks of a warp are encoded side by side, each lane
 // walking its own chunk's (sym_low, sym_high) pairs with the next pair loaded a
-// step ahead (loading 4 or 8 ahead measured the same: the coder's own dependent
-// steps and the lanes' diverging renormalisations set the pace).
-// Renormalisation takes the reference's loop (arith_coder.rs:101-119) in bulk
-// steps:
-//  * E1/E2: the k = clz(low ^ high) leading bits that agree are emitted at once
-//    (the first followed by the pending bits), then low/high shift by k;
+// step ahead.  The reference's renormalisation loop (arith_coder.rs:101-119) in
+// closed form, one pass per symbol:
+//  * E1/E2: the k = clz(low ^ high) leading bits that agree leave at once -- the
+//    first, then the pending bits (its complement), then the other k - 1 -- and
+//    low/high shift by k (low taking 0s, high 1s);
 //  * E3: while bit 30 of low is 1 and bit 30 of high is 0 the reference repeats
 //    the E3 step; j such steps keep bit 31, drop the j bits below it and add j
-//    pending bits.
-// A lane-per-chunk warp issues one instruction stream for 32 coders, where a
-// warp per chunk spent a whole warp's issue slot on each coder step.
+//    pending bits.  After an E3 step the top bits of low and high differ, so no
+//    E1/E2 step follows within the symbol, and after the bulk E1/E2 step the E3
+//    test is the only one left.
+// Output leaves in 32-bit words; a pending run that does not fit one push (over
+// 32 bits together with the symbol's agreeing bits) goes out in pieces.
 constexpr int ENC_THREADS = 128;
 
 __global__ void __launch_bounds__(ENC_THREADS)
@@ -253,43 +269,54 @@ k_encode(const uint2 *__restrict__ lohi, const int *__restrict__ chunk_row0,
          int *__restrict__ err) {
     const int c = blockIdx.x * ENC_THREADS + threadIdx.x;
     if (c >= n_chunks) return;
-    const unsigned long long HALF = 1ull << 31, QUARTER = 1ull << 30, MASK = 0xFFFFFFFFull;
     const int r0 = chunk_row0[c], n = chunk_len[c];
-    BitSink bs;
+    WordSink bs;
     bs.out = slots + slot_off[c];
     bs.cap = (uint32_t)(slot_off[c + 1] - slot_off[c]);
     bs.len = 0; bs.acc = 0; bs.n = 0; bs.overflow = false;
-    unsigned long long low = 0, high = MASK;
-    uint32_t pending = 0;
+    uint32_t low = 0, high = 0xFFFFFFFFu, pending = 0;
     const uint2 *src = lohi + r0;
     uint2 nxt = n > 0 ? src[0] : make_uint2(0, 0);
     for (int i = 0; i < n; i++) {
         const uint2 lh = nxt;
         if (i + 1 < n) nxt = src[i + 1];   // in flight during this step
-        const unsigned long long range = high - low + 1;
-        high = low + udiv_by_inv((unsigned long long)lh.y * range, total, inv_total) - 1;
-        low = low + udiv_by_inv((unsigned long long)lh.x * range, total, inv_total);
-        for (;;) {
-            const uint32_t x = (uint32_t)(low ^ high);
-            if ((x & 0x80000000u) == 0) {   // E1/E2, k >= 1 agreeing leading bits
-                const int k = x == 0 ? 32 : __clz(x);
-                bs.bit_plus_pending((uint32_t)(low >> 31) & 1u, pending);
-                pending = 0;
-                if (k > 1) bs.push((uint32_t)(low >> (32 - k)) & ((1u << (k - 1)) - 1u), k - 1);
-                low = (low << k) & MASK;
-                high = ((high << k) & MASK) | ((1ull << k) - 1ull);
-            } else if ((low & ~high & QUARTER) != 0) {   // E3, j steps
-                const int j = min(31, min(__clz(~(uint32_t)low << 1), __clz((uint32_t)high << 1)));
-                pending += (uint32_t)j;
-                low = (low << j) & 0x7FFFFFFFull;
-                high = ((high << j) & MASK) | HALF | ((1ull << j) - 1ull);
-            } else {
-                break;
+        // interval update (arith_coder.rs:86-97); both ends stay inside [low, high]
+        const unsigned long long range = (unsigned long long)high - low + 1ull;
+        const uint32_t nh = low + (uint32_t)udiv_by_inv((unsigned long long)lh.y * range, total, inv_total) - 1u;
+        low = low + (uint32_t)udiv_by_inv((unsigned long long)lh.x * range, total, inv_total);
+        high = nh;
+        const uint32_t x = low ^ high;
+        const int k1 = (x & 0x80000000u) ? 0 : (x == 0u ? 32 : __clz(x));
+        if (k1 > 0) {   // E1/E2 in bulk
+            const uint32_t b = low >> 31;
+            const uint32_t rest = k1 > 1 ? (uint32_t)(((unsigned long long)low << 1) >> (33 - k1)) & ((1u << (k1 - 1)) - 1u)
+                                         : 0u;
+            const uint32_t tot = pending + (uint32_t)k1;
+            if (tot <= 32u) {
+                const unsigned long long fill = b ? 0ull : ((1ull << pending) - 1ull);
+                bs.push((uint32_t)(((unsigned long long)b << (tot - 1)) | (fill << (k1 - 1)) | rest), (int)tot);
+            } else {   // a long pending run
+                bs.push(b, 1);
+                const uint32_t f = b ? 0u : 0xFFFFFFFFu;
+                for (uint32_t run = pending; run > 0;) {
+                    const int cnt = run > 31u ? 31 : (int)run;
+                    bs.push(f & ((1u << cnt) - 1u), cnt);
+                    run -= (uint32_t)cnt;
+                }
+                if (k1 > 1) bs.push(rest, k1 - 1);
             }
+            pending = 0;
+            low = (uint32_t)((unsigned long long)low << k1);
+            high = (uint32_t)(((unsigned long long)high << k1) | ((1ull << k1) - 1ull));
+        }
+        if ((low & ~high & 0x40000000u) != 0u) {   // E3 in bulk
+            const int j = min(__clz(~(low << 1)), __clz(high << 1));   // <= 31: bit 0 of ~(low << 1) is 1
+            pending += (uint32_t)j;
+            low = (low << j) & 0x7FFFFFFFu;
+            high = (high << j) | 0x80000000u | ((1u << j) - 1u);
         }
     }
-    bs.push(1u, 1);   // finish: terminating '1', then pad the partial byte
-    if (bs.n > 0) bs.push(0u, 8 - bs.n);
+    bs.finish();
     lens[c] = bs.len;
     if (bs.overflow) atomicOr(err, kErrOverflow);
 }
