@@ -60,6 +60,14 @@ def parse():
                     help="config 2: documents of 64 KiB compressed with the arch-2 model at ctx 512 (0 skips)")
     ap.add_argument("--config4-docs", type=int, default=64,
                     help="config 4 sample: documents of 64 KiB with the arch-2 model at ctx 4096 (0 skips)")
+    ap.add_argument("--parity", type=int, default=1,
+                    help="1: compare GPU bytes with the CPU oracle on samples of every configuration "
+                         "(outside the timed regions); a mismatch exits non-zero.  0 skips")
+    ap.add_argument("--corpus-mb", type=int, default=0,
+                    help="configuration 4 proper (strong scaling): this many MB of 64 KiB documents "
+                         "(seeds 10000..; 1024 = the 1 GB corpus) split by document over the ranks, "
+                         "compressed once per step with the arch-2 model at ctx 4096; replaces the "
+                         "configuration-1 headline.  0 (default) keeps configuration 1")
     return ap.parse_args()
 
 
@@ -82,18 +90,54 @@ def reduce_over_ranks(t_max: list, n_sum: list, device) -> tuple[list, list]:
     return a.tolist(), b.tolist()
 
 
-def workload(mf, seeds, ctx):
-    tok = mf.tokenizer()
-    docs = synth.documents(seeds, DOC_BYTES)
-    ids = tok.encode_batch_arrays(docs, num_threads=min(16, os.cpu_count() or 1))
-    starts = [0]
-    base = 0
+def chunked(ids, ctx):
+    """Token arrays of documents -> (tokens, chunk starts, first chunk of each document):
+    each document is cut into chunks of ctx tokens, the last one shorter
+    (rust/src/main.rs:199-205)."""
+    starts, doc_chunk0, base = [0], [0], 0
     for t in ids:
         for s in range(0, len(t), ctx):
             starts.append(base + min(s + ctx, len(t)))
         base += len(t)
+        doc_chunk0.append(len(starts) - 1)
     tokens = np.concatenate([np.asarray(t, dtype=np.uint32) for t in ids])
-    return tokens, np.asarray(starts, dtype=np.uint64), sum(len(d.encode()) for d in docs)
+    return tokens, np.asarray(starts, dtype=np.uint64), doc_chunk0
+
+
+def workload(mf, seeds, ctx, doc_bytes=DOC_BYTES):
+    tok = mf.tokenizer()
+    docs = synth.documents(seeds, doc_bytes)
+    ids = tok.encode_batch_arrays(docs, num_threads=min(16, os.cpu_count() or 1))
+    tokens, starts, doc_chunk0 = chunked(ids, ctx)
+    return tokens, starts, sum(len(d.encode()) for d in docs), doc_chunk0
+
+
+def doc_slice(tokens, starts, doc_chunk0, docs):
+    """Tokens and chunk starts (rebased to 0) of a run of consecutive documents."""
+    c0, c1 = doc_chunk0[docs[0]], doc_chunk0[docs[-1] + 1]
+    st = starts[c0:c1 + 1]
+    return tokens[int(st[0]):int(st[-1])], st - st[0], (c0, c1)
+
+
+def gpu_chunks(out, lens, c0, c1):
+    """Chunks c0..c1-1 of a packed output (chunk bytes back to back in chunk order)."""
+    offs = np.concatenate([[0], np.cumsum(lens, dtype=np.uint64)]).astype(np.int64)
+    raw = out[offs[c0]:offs[c1]].tobytes()
+    return [raw[offs[i] - offs[c0]:offs[i + 1] - offs[c0]] for i in range(c0, c1)]
+
+
+def oracle_parity(om, tokens, starts, doc_chunk0, docs, out, lens):
+    """The CPU oracle's bytes for the given documents against the GPU's bytes for them."""
+    from oracle import oracle as O
+
+    toks, st, (c0, c1) = doc_slice(tokens, starts, doc_chunk0, docs)
+    want = O.compress_chunks(om, toks, st, nthreads=os.cpu_count() or 1, variant="avx2")
+    got = gpu_chunks(out, lens, c0, c1)
+    bad = [i for i, (a, b) in enumerate(zip(got, want)) if a != b]
+    return {"docs": [int(docs[0]), int(docs[-1])] if len(docs) > 1 else [int(docs[0])],
+            "chunks": int(c1 - c0), "tokens": int(len(toks)),
+            "identical": len(got) == len(want) and not bad,
+            **({"first_bad_chunk": int(bad[0] + c0)} if bad else {})}
 
 
 # ---------------------------------------------------------------------------
@@ -179,21 +223,93 @@ def traffic_per_token():
     return per_token("dram_bytes_per_token.json")
 
 
-def algorithmic(kernel: str, info: dict, tokens_per_launch: float):
-    """(bound, algorithmic amount per launch, unit) of a kernel class."""
+def gemm_macs(info: dict) -> dict:
+    """int8 MACs per token of each GEMM class as the engine computes them (the QKV
+    GEMM computes the d + 128 rows the reference reads, rust/src/attention.rs:174-194)."""
     d, dff, V, L = info["d_model"], info["d_ff"], info["vocab_size"], info["n_layers"]
-    if kernel == "attention":
-        # per token and layer: K/V row (128 B) + Q row (d) read once, output (d) written once
-        return "hbm", (128 + 2 * d) * tokens_per_launch, "GB/s"
-    if kernel == "cdf":
-        return "hbm", (4 * V + 4 + 8) * tokens_per_launch, "GB/s"
-    if kernel == "encode":
-        return "hbm", 8.0 * tokens_per_launch + 1.2 * tokens_per_launch, "GB/s"
-    macs = {"gemm_qkv": (d + 128) * d, "gemm_o": d * d, "gemm_up_reglu": 2 * dff * d,
-            "gemm_down": d * dff, "gemm_head": V * d}.get(kernel)
-    if macs is not None:
-        return "tensor", 2.0 * macs * tokens_per_launch, "TFLOP/s"
-    return "hbm", 0.0, "GB/s"
+    return {"gemm_qkv": (d + 128) * d * L, "gemm_o": d * d * L, "gemm_up_reglu": 2 * dff * d * L,
+            "gemm_down": d * dff * L, "gemm_head": V * d, "head_cdf": V * d}
+
+
+def attention_pairs_per_token(starts) -> float:
+    """Mean (query, key) pairs per position and head: a chunk of n positions has
+    n (n + 1) / 2 (position p attends to keys 0..p)."""
+    n = np.diff(np.asarray(starts, dtype=np.int64)).astype(np.float64)
+    return float((n * (n + 1) / 2).sum() / max(1.0, n.sum()))
+
+
+# Algorithmic integer ALU work per token beyond the GEMMs (bench and DESIGN figures):
+# ~20 integer operations per (query, key, head) pair of the exact softmax (score
+# rounding, running max, exp lookup, weight) and ~20 per logit of the CDF
+# (exp lookup, frequency division, prefix sums).
+ALU_OPS_PER_PAIR = 20
+ALU_OPS_PER_LOGIT = 20
+
+
+def roofline_object(dom, info, pairs_per_tok, tok_per_launch, per_launch_ms, hbm, bf16, basis, sms, mhz) -> dict:
+    """The dominant kernel against its rooflines.  For the attention the contract's
+    primary ``bound`` is the int8 tensor pipe (QK^T and P.V: 2 x 64 MACs per (query,
+    key, head) pair); ``hbm`` (its algorithmic bytes) and ``issue`` (warp instructions
+    against 4 per cycle per SM) are given beside it."""
+    d, H, L = info["d_model"], info["n_heads"], info["n_layers"]
+    secs = per_launch_ms / 1e3
+    tpt = traffic_per_token().get(dom)
+    if dom == "attention":
+        ops = 2.0 * 128 * pairs_per_tok * H * tok_per_launch   # one launch per layer and wave
+        achieved = ops / secs / 1e12
+        out = {"kernel": dom, "bound": "tensor", "achieved": round(achieved, 3), "peak": round(2 * bf16, 1),
+               "unit": "TOP/s", "frac": round(achieved / (2 * bf16), 5),
+               "peak_basis": f"2 x bf16_tflops {basis} (dense int8 = 2 x bf16; the kernel runs at the max clock)",
+               "algorithmic": "2 x 128 MACs (QK^T 64 + P.V 64) per (query, key, head) pair; "
+                              f"{pairs_per_tok:.1f} pairs per position and head in this workload"}
+        hb = (128 + 2 * d) * tok_per_launch
+        out["hbm"] = {"achieved": round(hb / secs / 1e9, 1), "peak": hbm, "unit": "GB/s",
+                      "frac": round(hb / secs / 1e9 / hbm, 5),
+                      "algorithmic": "K/V row 128 B + Q row d B read, output d B written, per position"}
+    else:
+        macs = gemm_macs(info).get(dom)
+        if macs is not None:
+            ops = 2.0 * macs * tok_per_launch / (L if dom not in ("gemm_head", "head_cdf") else 1)
+            achieved = ops / secs / 1e12
+            out = {"kernel": dom, "bound": "tensor", "achieved": round(achieved, 3), "peak": round(2 * bf16, 1),
+                   "unit": "TOP/s", "frac": round(achieved / (2 * bf16), 5),
+                   "peak_basis": f"2 x bf16_tflops {basis} (dense int8 = 2 x bf16)"}
+        else:
+            V = info["vocab_size"]
+            by = {"cdf": 4 * V + 12, "encode": 9.2}.get(dom, 0.0) * tok_per_launch
+            out = {"kernel": dom, "bound": "hbm", "achieved": round(by / secs / 1e9, 1), "peak": hbm,
+                   "unit": "GB/s", "frac": round(by / secs / 1e9 / hbm, 5), "peak_basis": f"hbm_gbs {basis}"}
+    out["traffic"] = None if tpt is None else round(tpt * tok_per_launch)
+    out["traffic_basis"] = ("ncu dram__bytes_read.sum + dram__bytes_write.sum per token of a 24-document "
+                            "capture (profiles/dram_bytes_per_token.json) x tokens per launch")
+    ipt = per_token("inst_per_token.json").get(dom)
+    if ipt is not None:
+        issued = ipt * tok_per_launch / secs / 1e9
+        peak_i = sms * 4 * mhz / 1e3
+        out["issue"] = {"achieved": round(issued, 1), "peak": round(peak_i, 1),
+                        "unit": "G warp instructions/s", "frac": round(issued / peak_i, 4),
+                        "inst_per_token": ipt,
+                        "basis": "ncu smsp__inst_executed per token (profiles/inst_per_token.json) x tokens "
+                                 "per launch / CUDA-event duration; peak = SMs x 4 schedulers x median SM "
+                                 "clock under load"}
+    return out
+
+
+def pipeline_bound(info, pairs_per_tok, value, bf16, sms, mhz, basis) -> dict:
+    """Whole-pipeline bound: tokens/s against min(GEMM-bound, ALU-bound tokens/s).
+    GEMM bound: int8 GEMM ops per token at 2 x the measured bf16 peak.  ALU bound:
+    the algorithmic integer work of the softmax and the CDF per token at one
+    operation per lane per cycle (SMs x 128 lanes x clock)."""
+    gemm_ops = 2.0 * sum(v for k, v in gemm_macs(info).items() if k != "head_cdf")
+    gemm_tps = 2 * bf16 * 1e12 / gemm_ops
+    alu_ops = (ALU_OPS_PER_PAIR * pairs_per_tok * info["n_heads"] * info["n_layers"]
+               + ALU_OPS_PER_LOGIT * info["vocab_size"])
+    alu_tps = sms * 128 * mhz * 1e6 / alu_ops
+    bound = min(gemm_tps, alu_tps)
+    return {"gemm_bound_tokens_per_s": round(gemm_tps, 1), "alu_bound_tokens_per_s": round(alu_tps, 1),
+            "frac": round(value / bound, 4), "gemm_ops_per_token": gemm_ops, "alu_ops_per_token": alu_ops,
+            "basis": f"GEMM: 2 x bf16_tflops {basis}; ALU: {ALU_OPS_PER_PAIR} ops per (query, key, head) pair "
+                     f"+ {ALU_OPS_PER_LOGIT} per logit at SMs x 128 lanes x median SM clock"}
 
 
 def main():
@@ -215,8 +331,10 @@ def main():
                                 device_id=torch.device("cuda", local))
     from compress_zip_b200.engine import Engine
 
+    if args.corpus_mb > 0:
+        return corpus_bench(args, mf, rank, world, local)
     seeds = shard_seeds(rank, args.docs)
-    tokens, starts, nbytes = workload(mf, seeds, args.ctx)
+    tokens, starts, nbytes, doc_chunk0 = workload(mf, seeds, args.ctx)
     n_tok, n_chunks = int(len(tokens)), int(len(starts) - 1)
 
     eng = Engine(mf.raw, local)
@@ -294,11 +412,23 @@ def main():
         e2e_times.append(ev0.elapsed_time(ev1))
     barrier()
     t_e2e = sum(e2e_times)
-    parity = bytes(h_out_np[:nout_h]) == bytes(out[:nout])
+    e2e_same = bytes(h_out_np[:nout_h]) == bytes(out[:nout])
 
-    dec = decode_bench(eng, mf, rank, args, stream, world) if args.decode_docs > 0 else None
-    cfg2 = arch2_bench(mf, rank, args, stream, local, 2) if args.config2_docs > 0 else None
-    cfg4 = arch2_bench(mf, rank, args, stream, local, 4) if args.config4_docs > 0 else None
+    # parity at benchmark scale (rank 0, untimed): the oracle's bytes for the first
+    # documents and for the documents of the last wave against the timed run's bytes
+    parity = {}
+    if args.parity and rank == 0:
+        from oracle import oracle as O
+
+        om1 = O.load_model(MODEL)
+        first = list(range(min(args.cpu_sample_docs, args.docs)))
+        last = list(range(max(0, args.docs - 8), args.docs))
+        parity["config1_first_docs"] = oracle_parity(om1, tokens, starts, doc_chunk0, first, out, lens)
+        parity["config1_last_wave"] = oracle_parity(om1, tokens, starts, doc_chunk0, last, out, lens)
+
+    dec = decode_bench(eng, mf, rank, args, stream, world, parity) if args.decode_docs > 0 else None
+    cfg2 = arch2_bench(mf, rank, args, stream, local, 2, parity) if args.config2_docs > 0 else None
+    cfg4 = arch2_bench(mf, rank, args, stream, local, 4, parity) if args.config4_docs > 0 else None
     pipe = host_pipeline(eng, mf, args) if rank == 0 and args.pipeline_docs > 0 else None
 
     (t_max, t_e2e_max), (all_tok, all_bytes) = reduce_over_ranks(
@@ -312,30 +442,11 @@ def main():
         dom = max(kern_ms, key=kern_ms.get)
         per_launch_ms = kern_ms[dom] / max(1, kern_n[dom])
         tok_per_launch = n_tok * K / max(1, kern_n[dom])
-        if dom.startswith("gemm") or dom == "attention":
-            tok_per_launch *= 1  # one launch per layer per wave
-        bound, amount, unit = algorithmic(dom, eng.info, tok_per_launch)
-        achieved = amount / (per_launch_ms / 1e3) / (1e9 if unit == "GB/s" else 1e12)
-        peak = hbm if bound == "hbm" else 2.0 * bf16_sus
-        tpt = traffic_per_token().get(dom)
-        roofline = {"kernel": dom, "bound": bound, "achieved": round(achieved, 3), "peak": peak,
-                    "unit": unit, "frac": round(achieved / peak, 5),
-                    "traffic": None if tpt is None else round(tpt * tok_per_launch),
-                    "peak_basis": (f"hbm_gbs {basis}" if bound == "hbm" else
-                                   f"2 x bf16_tflops_sustained {basis} (dense int8 = 2 x bf16)")}
-        ipt = per_token("inst_per_token.json").get(dom)
-        if ipt is not None:
-            # the issue limit: 4 warp instructions per cycle per SM at the clock seen under load
-            sms = torch.cuda.get_device_properties(local).multi_processor_count
-            mhz = (clk or {}).get("sm_mhz") or 1965.0
-            issued = ipt * tok_per_launch / (per_launch_ms / 1e3) / 1e9
-            peak_i = sms * 4 * mhz / 1e3
-            roofline["issue"] = {"achieved": round(issued, 1), "peak": round(peak_i, 1),
-                                 "unit": "G warp instructions/s", "frac": round(issued / peak_i, 4),
-                                 "inst_per_token": ipt,
-                                 "basis": "ncu smsp__inst_executed per token (profiles/inst_per_token.json) "
-                                          "x tokens per launch / CUDA-event duration; peak = SMs x 4 "
-                                          "schedulers x median SM clock under load"}
+        mhz = (clk or {}).get("sm_mhz") or 1965.0
+        sms = torch.cuda.get_device_properties(local).multi_processor_count
+        ppt = attention_pairs_per_token(starts)
+        roofline = roofline_object(dom, eng.info, ppt, tok_per_launch, per_launch_ms, hbm, bf16, basis, sms, mhz)
+        roofline["pipeline"] = pipeline_bound(eng.info, ppt, value, bf16, sms, mhz, basis)
         cpu = cpu_baseline(mf, args) if world == 1 else None
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
@@ -354,8 +465,9 @@ def main():
                     "h2d_bytes_per_step": 4 * n_tok,
                     "d2h_bytes_per_step": int(nout_h + 4 * n_chunks),
                     "mb_per_s": round(all_bytes * K / (t_e2e_max / 1e3) / 1e6, 3),
-                    "bytes_identical_to_device_path": parity},
+                    "bytes_identical_to_device_path": e2e_same},
             "roofline": roofline,
+            "parity": parity if parity else None,
             "kernels_ms_per_step": {k: round(v / K, 3) for k, v in kern_ms.items()},
             "gpu_launches": int(launches),
             "clocks": clk,
@@ -375,17 +487,27 @@ def main():
     eng.close()
     if world > 1:
         dist.destroy_process_group()
+    if rank == 0 and not parity_ok(parity):
+        print("parity FAILED: GPU bytes differ from the CPU oracle (see the parity object)", file=sys.stderr)
+        return 1
+    return 0
 
 
-def arch2_bench(mf, rank, args, stream, local, cfg):
+def parity_ok(parity) -> bool:
+    return all(v.get("identical", False) for v in (parity or {}).values())
+
+
+def arch2_bench(mf, rank, args, stream, local, cfg, parity):
     """BASELINE configuration 2 (cfg 2: documents of 64 KiB, seeds 3000.., at ctx 512)
     or a bounded sample of configuration 4 (cfg 4: documents of 64 KiB, seeds
-    10000.., at ctx 4096; the configuration itself is a 1 GB corpus) compressed with
-    the arch-2 model (d 512, 8 layers, 8 heads, 2 KV heads, d_ff 2048; synthetic
-    int8 weights from seed 7, compress_zip_b200/synth.py) at that context.  Rank r
-    takes seeds +r*N.  Tokens resident in HBM, L2 flushed before each timed step,
-    CUDA events on the engine's stream; the per-kernel split gives the GEMMs' int8
-    tensor throughput.  Each rank reports its own figure (no collective here)."""
+    10000.., at ctx 4096; the configuration itself is a 1 GB corpus, --corpus-mb)
+    compressed with the arch-2 model (d 512, 8 layers, 8 heads, 2 KV heads, d_ff
+    2048; synthetic int8 weights from seed 7, compress_zip_b200/synth.py) at that
+    context.  Rank r takes seeds +r*N.  Tokens resident in HBM, L2 flushed before
+    each timed step, CUDA events on the engine's stream; the per-kernel split gives
+    the GEMMs' int8 tensor throughput.  Each rank reports its own figure (no
+    collective here).  Rank 0 then compares the first document's chunks with the
+    CPU oracle's (parity[f"config{cfg}"])."""
     import torch
     from compress_zip_b200.engine import Engine
 
@@ -395,13 +517,7 @@ def arch2_bench(mf, rank, args, stream, local, cfg):
     tok = mf.tokenizer()
     docs = synth.documents(shard_seeds(rank, n_docs, first=first), 65536)
     ids = tok.encode_batch_arrays(docs, num_threads=min(16, os.cpu_count() or 1))
-    starts, b = [0], 0
-    for t in ids:
-        for s0 in range(0, len(t), ctx):
-            starts.append(b + min(s0 + ctx, len(t)))
-        b += len(t)
-    tokens = np.concatenate([np.asarray(t, dtype=np.uint32) for t in ids])
-    starts = np.asarray(starts, dtype=np.uint64)
+    tokens, starts, doc_chunk0 = chunked(ids, ctx)
     n_tok, n_chunks = int(len(tokens)), int(len(starts) - 1)
     eng = Engine(model, local)
     try:
@@ -428,13 +544,21 @@ def arch2_bench(mf, rank, args, stream, local, cfg):
                 kern[k] = kern.get(k, 0.0) + v["ms"]
     finally:
         eng.close()
+    if args.parity and rank == 0:
+        import tempfile
+
+        from oracle import oracle as O
+
+        with tempfile.NamedTemporaryFile(suffix=".czm") as f:
+            f.write(model)
+            f.flush()
+            om = O.load_model(f.name)
+        parity[f"config{cfg}"] = oracle_parity(om, tokens, starts, doc_chunk0, [0], out, lens)
     t = sum(times)
-    d, dff, kvd, L, V = a["d_model"], a["d_ff"], a["n_kv_heads"] * 64, a["n_layers"], a["vocab_size"]
-    macs = {"gemm_qkv": (d + 2 * kvd) * d * L, "gemm_o": d * d * L, "gemm_up_reglu": 2 * dff * d * L,
-            "gemm_down": d * dff * L, "head_cdf": V * d, "gemm_head": V * d}
+    macs = gemm_macs(a)
     gemm_ms = sum(kern.get(k, 0.0) for k in macs)
     gemm_ops = sum(2.0 * m * n_tok * steps for k, m in macs.items() if kern.get(k, 0.0) > 0)
-    _, _, bf16_sus, basis = peaks()
+    _, bf16, bf16_sus, basis = peaks()
     tops = gemm_ops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else 0.0
     return {"metric": f"compress tokens/s (config {cfg}{'' if cfg == 2 else ' sample'}: arch-2 model, "
                       f"ctx {ctx}, 64 KiB docs)",
@@ -444,31 +568,31 @@ def arch2_bench(mf, rank, args, stream, local, cfg):
             "mb_per_s": round(sum(len(x.encode()) for x in docs) * steps / (t / 1e3) / 1e6, 3),
             "kernels_ms_per_step": {k: round(v / steps, 3) for k, v in kern.items() if v > 0},
             "gemm_tensor": {"achieved": round(tops, 1), "unit": "TOP/s (int8, 2 x MACs)",
-                            "peak": round(2.0 * bf16_sus, 1), "frac": round(tops / (2.0 * bf16_sus), 4),
-                            "peak_basis": f"2 x bf16_tflops_sustained {basis} (dense int8 = 2 x bf16)",
-                            "kernels": "QKV, O, up+ReGLU, down GEMMs and the head GEMM of head_cdf, "
-                                       "CUDA-event time per class"},
+                            "peak": round(2.0 * bf16, 1), "frac": round(tops / (2.0 * bf16), 4),
+                            "peak_sustained": round(2.0 * bf16_sus, 1),
+                            "frac_sustained": round(tops / (2.0 * bf16_sus), 4),
+                            "peak_basis": f"2 x bf16_tflops {basis} (burst; dense int8 = 2 x bf16); "
+                                          "frac_sustained against 2 x bf16_tflops_sustained",
+                            "kernels": "QKV (d + 128 rows computed), O, up+ReGLU, down GEMMs and the head "
+                                       "GEMM of head_cdf, CUDA-event time per class"},
             "model": "arch-2 synthetic (d 512, 8 layers, 8 heads, 2 KV heads, d_ff 2048, V 1024)"}
 
 
-def decode_bench(eng, mf, rank, args, stream, world):
+def decode_bench(eng, mf, rank, args, stream, world, parity):
     """decompression of 4,096 independent streams, each
     the chunks of a 4 KB document at L4 (ctx 512), seeds 2000.. (rank r: +r*4096).
     The chunks are produced by the engine itself (untimed); the timed region is
     czg_decompress_chunks from host bytes to host tokens (H2D/D2H inside), CUDA
-    events on the engine's stream; the tokens must equal the originals."""
+    events on the engine's stream; the tokens must equal the originals.  Rank 0
+    then encodes the first and last 32 documents with the CPU oracle: its bytes
+    must equal the GPU's, and the GPU must decode the oracle's streams back to the
+    tokens (parity["config3"])."""
     import torch
 
     tok = mf.tokenizer()
     docs = synth.documents(shard_seeds(rank, args.decode_docs, first=2000), 4096)
     ids = tok.encode_batch_arrays(docs, num_threads=min(16, os.cpu_count() or 1))
-    starts, b = [0], 0
-    for t in ids:
-        for s0 in range(0, len(t), 512):
-            starts.append(b + min(s0 + 512, len(t)))
-        b += len(t)
-    tokens = np.concatenate([np.asarray(t, dtype=np.uint32) for t in ids])
-    starts = np.asarray(starts, dtype=np.uint64)
+    tokens, starts, doc_chunk0 = chunked(ids, 512)
     counts = np.diff(starts).astype(np.uint32)
     chunks = eng.compress_chunks(tokens, starts)
     ev0 = torch.cuda.Event(enable_timing=True)
@@ -495,6 +619,24 @@ def decode_bench(eng, mf, rank, args, stream, world):
     exact = exact and bool(np.array_equal(eng.decompress_chunks(chunks, counts), tokens))
     kern = eng.last_stats()["kernels"]
     eng.set_kernel_timing(False)
+    if args.parity and rank == 0:
+        from oracle import oracle as O
+
+        om = O.load_model(MODEL)
+        nd = len(ids)
+        sample = sorted(set(range(min(32, nd))) | set(range(max(0, nd - 32), nd)))
+        ok_bytes, ok_tokens, n_ch, n_tk = True, True, 0, 0
+        for run in (sample[: len(sample) // 2], sample[len(sample) // 2:]):
+            toks, st, (c0, c1) = doc_slice(tokens, starts, doc_chunk0, run)
+            want = O.compress_chunks(om, toks, st, nthreads=os.cpu_count() or 1, variant="avx2")
+            ok_bytes = ok_bytes and want == chunks[c0:c1]
+            back = eng.decompress_chunks(want, np.diff(st).astype(np.uint32))
+            ok_tokens = ok_tokens and bool(np.array_equal(back, toks))
+            n_ch += c1 - c0
+            n_tk += len(toks)
+        parity["config3"] = {"docs": [sample[0], sample[-1]], "chunks": int(n_ch), "tokens": int(n_tk),
+                             "identical": ok_bytes and ok_tokens, "gpu_bytes_equal_oracle": ok_bytes,
+                             "gpu_decodes_oracle_streams": ok_tokens}
     return {"metric": "batched decode tokens/s (config 3: 4096 x 4 KB docs, L4 ctx 512)",
             "value": round(n_tok * steps / (t / 1e3), 1), "unit": "tokens/s", "steps": steps,
             "ms_per_step": round(t / steps, 3), "streams_per_gpu": int(len(chunks)),
@@ -502,6 +644,92 @@ def decode_bench(eng, mf, rank, args, stream, world):
             "gpu_launches_per_step": int(launches // steps),
             "kernels_ms_per_step": {k: round(v["ms"], 3) for k, v in kern.items() if v["launches"]},
             "kernel_split": "from one more, untimed run with per-kernel CUDA events"}
+
+
+def corpus_bench(args, mf, rank, world, local):
+    """Configuration 4 proper: a corpus of args.corpus_mb MB of 64 KiB documents
+    (seeds 10000..) split by document over the ranks (strong scaling: the corpus is
+    fixed, each rank compresses its contiguous share), the arch-2 model at ctx 4096.
+    A step compresses the rank's whole share once (tokens resident in HBM); warm-up
+    runs the first 16 documents of the share.  value = corpus tokens / max over ranks
+    of the device time per step.  No collective on the data path: only the timing
+    reduction."""
+    import torch
+    import torch.distributed as dist
+    from compress_zip_b200.engine import Engine
+
+    n_docs = args.corpus_mb * (1 << 20) // 65536
+    lo, hi = rank * n_docs // world, (rank + 1) * n_docs // world
+    model = synth.arch2_model(mf, 4096)
+    tok = mf.tokenizer()
+    docs = synth.documents(range(10000 + lo, 10000 + hi), 65536)
+    ids = tok.encode_batch_arrays(docs, num_threads=min(16, os.cpu_count() or 1))
+    tokens, starts, doc_chunk0 = chunked(ids, 4096)
+    n_tok, n_chunks, nbytes = int(len(tokens)), int(len(starts) - 1), sum(len(d.encode()) for d in docs)
+    del docs
+    stream = torch.cuda.current_stream()
+    eng = Engine(model, local)
+    eng.set_stream(stream.cuda_stream)
+    d_tokens = torch.from_numpy(tokens.view(np.int32)).to(f"cuda:{local}")
+    out = np.empty(4 * n_tok + 8 * n_chunks, dtype=np.uint8)
+    lens = np.empty(n_chunks, dtype=np.uint32)
+    w_end = doc_chunk0[min(16, len(ids))]
+    for _ in range(max(args.warmup, 1)):
+        eng.compress_device(d_tokens.data_ptr(), starts[: w_end + 1], out, lens)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    times = []
+    for _ in range(args.steps):
+        ev0.record(stream)
+        nout = eng.compress_device(d_tokens.data_ptr(), starts, out, lens)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        times.append(ev0.elapsed_time(ev1))
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    (t_max,), (all_tok, all_bytes, all_out) = reduce_over_ranks(
+        [sum(times)], [float(n_tok), float(nbytes), float(nout)], f"cuda:{local}")
+    parity = {}
+    if args.parity and rank == 0:
+        import tempfile
+
+        from oracle import oracle as O
+
+        with tempfile.NamedTemporaryFile(suffix=".czm") as f:
+            f.write(model)
+            f.flush()
+            om = O.load_model(f.name)
+        parity["config4"] = oracle_parity(om, tokens, starts, doc_chunk0, [0], out, lens)
+    eng.close()
+    if rank == 0:
+        K = args.steps
+        line = {"metric": "compress tokens/s & MB/s, config 4: 1 GB-class corpus, arch-2 model at ctx 4096",
+                "value": round(all_tok * K / (t_max / 1e3), 1), "unit": "tokens/s", "n_gpus": world,
+                "steps": K, "warmup": args.warmup, "ms_per_step": round(t_max / K, 3), "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+                "data": "synthetic (seeded Zipf lexicon text, BASELINE config 4 shapes)",
+                "mb_per_s": round(all_bytes * K / (t_max / 1e3) / 1e6, 3),
+                "config": {"workload": f"config4: {args.corpus_mb} MB = {n_docs} docs x 64 KiB (seeds "
+                                       f"10000..{10000 + n_docs - 1}) split by document over {world} GPUs",
+                           "model": "arch-2 synthetic (d 512, 8 layers, 8 heads, 2 KV heads, d_ff 2048)",
+                           "ctx_len": 4096, "corpus_tokens": int(all_tok), "compressed_bytes": int(all_out),
+                           "parallelism": f"dp{world} (documents)",
+                           "l2": "inputs (GBs of tokens per rank) far larger than L2"},
+                "clocks": clk, "parity": parity or None}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    if rank == 0 and not parity_ok(parity):
+        print("parity FAILED: GPU bytes differ from the CPU oracle", file=sys.stderr)
+        return 1
+    return 0
 
 
 def host_pipeline(eng, mf, args):
@@ -565,7 +793,7 @@ def host_pipeline(eng, mf, args):
 
 
 def _oracle_sample(mf, ndocs, ctx):
-    tokens, starts, nbytes = workload(mf, range(1, ndocs + 1), ctx)
+    tokens, starts, nbytes, _ = workload(mf, range(1, ndocs + 1), ctx)
     return tokens, starts, nbytes
 
 
@@ -626,7 +854,9 @@ def run_reference(args, mf, rank, world):
                    "model": "v001_eng.czm", "ctx_len": args.ctx, "tokens_per_step": int(len(tokens))},
         "cpu_baseline": {"value": round(value, 1), "unit": "tokens/s", "cores": cores,
                          "kind": "port",
-                         "sample": f"{ndocs} docs (seeds 1..{ndocs}), {len(tokens)} tokens per step; "
+                         "sample": f"{ndocs} docs (seeds 1..{ndocs}), {len(tokens)} tokens in {len(starts) - 1} "
+                                   f"chunks per step (one chunk per thread at a time: {cores} threads, "
+                                   f"{(len(starts) - 1) / cores:.1f} chunks each); "
                                    "C restatement of the reference Rust path built for x86-64-v3 "
                                    "(cargo is absent, the Rust crate cannot be built)"},
         "e2e": {"value": round(value, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0,

@@ -13,8 +13,10 @@
 // In host code g_encode_scratch is only a host-side stand-in for the device
 // array, so it is never passed to a kernel.  The first call on a device (with
 // that device current) looks up the array's device address with
-// cudaGetSymbolAddress and keeps it for later calls on that device; make that
-// first call before any stream capture.  All calls share the one array, which
+// cudaGetSymbolAddress and keeps it, together with the CUDA context it belongs
+// to, for later calls on that device; a call in a newer context (after a
+// cudaDeviceReset) looks it up again.  Make the first call on each device, and
+// the first after a reset, before any stream capture.  All calls share the one array, which
 // keeps the previous call's contents: each call clears what must start at zero.
 // Calls whose work overlaps on the GPU (other streams, other host threads) race
 // on the array and must be serialised by the caller.
@@ -45,7 +47,7 @@ static_assert(kOffBytes + 4 * kMaxTokens + 8ull * kMaxChunks <= kStaticScratchBy
 
 __device__ __align__(256) uint8_t g_encode_scratch[kStaticScratchBytes];
 
-constexpr int kErrCap = 1, kErrSlot = 2;
+constexpr int kErrCap = 1, kErrSlot = 2, kErrSum = 4;
 
 struct Scratch {
     uint32_t *err;
@@ -70,7 +72,10 @@ __host__ __device__ inline Scratch scratch_at(uint8_t *base) {
 }
 
 // Exclusive scans of the chunk lengths: rows and slot bytes (4*len + 8); one CTA.
-__global__ void k_static_layout(const uint32_t *__restrict__ chunk_len, uint32_t n, uint8_t *base) {
+// Lengths that do not add up to n_tokens (the caller's interval count) set kErrSum,
+// and the kernels after this one then read no interval and write no output.
+__global__ void k_static_layout(const uint32_t *__restrict__ chunk_len, uint32_t n, uint64_t n_tokens,
+                                uint8_t *base) {
     Scratch s = scratch_at(base);
     __shared__ uint64_t carry_rows, carry_slot;
     if (threadIdx.x == 0) {
@@ -111,6 +116,7 @@ __global__ void k_static_layout(const uint32_t *__restrict__ chunk_len, uint32_t
     if (threadIdx.x == 0) {
         s.row_off[n] = carry_rows;
         s.slot_off[n] = carry_slot;
+        if (carry_rows != n_tokens) *s.err = kErrSum;
     }
 }
 
@@ -148,6 +154,7 @@ __global__ void k_static_encode(const uint2 *__restrict__ lohi, uint32_t n, uint
     const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= n) return;
     Scratch s = scratch_at(base);
+    if (*s.err & kErrSum) return;   // the row offsets would leave the caller's intervals
     const unsigned long long HALF = 1ull << 31, QUARTER = 1ull << 30, MASK = 0xFFFFFFFFull;
     const uint64_t r0 = s.row_off[c], cnt = s.row_off[c + 1] - r0;
     if (s.slot_off[c + 1] > slot_limit) {
@@ -223,6 +230,7 @@ __global__ void k_static_pack(uint32_t n, uint64_t out_cap, uint8_t *__restrict_
                               uint32_t *__restrict__ out_lens, uint8_t *base) {
     Scratch s = scratch_at(base);
     const uint32_t c = blockIdx.x;
+    if (*s.err & kErrSum) return;
     if (*s.total > out_cap) {
         if (c == 0 && threadIdx.x == 0) atomicOr(s.err, (uint32_t)kErrCap);
         return;
@@ -234,17 +242,43 @@ __global__ void k_static_pack(uint32_t n, uint64_t out_cap, uint8_t *__restrict_
     if (threadIdx.x == 0) out_lens[c] = len;
 }
 
-// device address of g_encode_scratch, looked up once per device
+// device address of g_encode_scratch, looked up once per device and context
+// (cuCtxGetCurrent through the runtime's driver entry point: a cudaDeviceReset
+// makes a new primary context, in which the array may sit elsewhere)
+using CtxGetCurrentFn = int (*)(void **);
+
+CtxGetCurrentFn ctx_get_current() {
+    static CtxGetCurrentFn fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<CtxGetCurrentFn>(p);
+    }
+    return fn;
+}
+
 std::mutex g_addr_mu;
 uint8_t *g_addr[256] = {nullptr};
+void *g_addr_ctx[256] = {nullptr};
 
 int scratch_address(int dev, uint8_t **out) {
     if (dev < 0 || dev >= 256) return CZG_E_DEVICE;
+    CtxGetCurrentFn get_ctx = ctx_get_current();
+    if (!get_ctx) return CZG_E_DEVICE;
     std::lock_guard<std::mutex> lk(g_addr_mu);
-    if (!g_addr[dev]) {
+    void *ctx = nullptr;
+    if (get_ctx(&ctx) != 0) return CZG_E_DEVICE;
+    if (!ctx) {   // no context current yet: cudaSetDevice makes the device's primary context current
+        if (cudaSetDevice(dev) != cudaSuccess || get_ctx(&ctx) != 0 || !ctx) return CZG_E_DEVICE;
+    }
+    if (!g_addr[dev] || g_addr_ctx[dev] != ctx) {
+        g_addr[dev] = nullptr;
         void *p = nullptr;
         if (cudaGetSymbolAddress(&p, g_encode_scratch) != cudaSuccess || !p) return CZG_E_DEVICE;
         g_addr[dev] = static_cast<uint8_t *>(p);
+        g_addr_ctx[dev] = ctx;
     }
     *out = g_addr[dev];
     return CZG_OK;
@@ -270,7 +304,7 @@ extern "C" int czg_encode_intervals_static(const uint32_t *d_lohi, const uint32_
     if (st != CZG_OK) return st;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const uint64_t slot_limit = kStaticScratchBytes - kOffBytes;
-    k_static_layout<<<1, 1024, 0, s>>>(d_chunk_len, n_chunks, base);
+    k_static_layout<<<1, 1024, 0, s>>>(d_chunk_len, n_chunks, n_tokens, base);
     k_static_encode<<<(n_chunks + 127) / 128, 128, 0, s>>>(reinterpret_cast<const uint2 *>(d_lohi), n_chunks,
                                                            target_total, 0xFFFFFFFFFFFFFFFFull / target_total,
                                                            slot_limit, base);
@@ -283,6 +317,10 @@ extern "C" int czg_encode_intervals_static(const uint32_t *d_lohi, const uint32_
         return CZG_E_DEVICE;
     const uint32_t err = (uint32_t)head[0];
     *out_bytes = head[1];
+    if (err & kErrSum) {   // nothing was encoded or written
+        *out_bytes = 0;
+        return CZG_E_ARG;
+    }
     if (err & kErrSlot) return CZG_E_LIMIT;   // chunk lengths summing past the stated limit
     if (err & kErrCap) return CZG_E_CAPACITY;
     return CZG_OK;

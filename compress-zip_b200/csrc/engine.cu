@@ -76,6 +76,7 @@ struct czg_ctx {
     bool scalar_attention = false;   // CZG_SCALAR_ATTENTION=1 selects the CUDA-core kernel
     bool staged_attention = false;   // CZG_ATTN_STAGED=1: chunks <= 1024 keys with K/V^T staged in shared memory
     int vpad = 0;           // vocab rounded up to the GEMM tile (extra head rows are zero)
+    int dff_pad = 0;        // d_ff rounded up to the GEMM tile (extra hidden units are zero)
     int8_t *embed = nullptr, *final_norm = nullptr, *head_w = nullptr;
     uint16_t *lut = nullptr;
     uint16_t *lut4k = nullptr;   // exp_q16 by t256 <= 4096 (lut.rs:213-235 unrolled over ip)
@@ -84,6 +85,7 @@ struct czg_ctx {
     bool exp0 = false;           // lut4k[0] == 65535: exp of a zero difference needs no special case
     bool logit_small = false;    // every |logit| < 2^30: no logit difference wraps
     bool head_cdf = false;       // the fused head GEMM + coder interval kernel applies
+    bool gemm_failed = false;    // a GEMM launch was refused (shape or output map); the call fails
     int16_t *rope_cos = nullptr, *rope_sin = nullptr;
     std::vector<LayerDev> layers;
     std::vector<void *> allocs;
@@ -104,8 +106,7 @@ struct czg_ctx {
     int *att_row0 = nullptr, *att_len = nullptr;   // the chunks in attention launch order
     int *att_kvoff = nullptr;                        // and their streaming K/V offsets (128-byte units)
     int *rowchunk = nullptr;                         // chunk of each row of a wave
-    // tcgen05 path: TMA descriptors of the GEMM A operands (wave buffers) and the head
-    bool use_tc = false;
+    // TMA descriptors of the GEMM A operands (wave buffers) and the head
     TcMatrix tm_xn, tm_attn, tm_h, tm_head;
     // decompression buffers (grown on demand)
     size_t dec_streams = 0, dec_len = 0, dec_bytes = 0, dec_tokens = 0;
@@ -346,6 +347,12 @@ int load_model(czg_ctx *c, const uint8_t *bytes, size_t len) {
     if (m.target_total <= (uint32_t)V || m.target_total >= (1u << 30))
         return fail(c, CZG_E_UNSUPPORTED, "softmax.target_total must lie in (vocab_size, 2^30)");
 
+    // The tcgen05 GEMMs take K and N in multiples of 128.  d = 64 * n_heads is one
+    // (n_heads 4, 6, 8 give 256, 384, 512); d_ff (a multiple of 64) is padded to dffp
+    // with zero gate/up rows and zero down columns: requant(0) = 0 and ReGLU(0, 0) = 0,
+    // so the padded hidden units are 0 and add nothing to the down projection.
+    const int dffp = (dff + 127) / 128 * 128;
+    c->dff_pad = dffp;
     c->layers.resize(m.n_layers);
     c->logit_small = (long long)d * 127 * 128 < (1ll << 30);   // |logit| <= d * 127 * 128
     c->res16 = m.n_layers <= 128 && getenv("CZG_RESIDUAL32") == nullptr;
@@ -365,8 +372,9 @@ int load_model(czg_ctx *c, const uint8_t *bytes, size_t len) {
         if ((st = need(c, f, p + "attn.out.weight", "I8", (int64_t)d * d, &t))) return st;
         if (!upload(c, &L.out_w, t->data, (size_t)d * d)) return CZG_E_DEVICE;
         if ((st = need(c, f, p + "ffn.up.weight", "I8", (int64_t)2 * dff * d, &t))) return st;
-        {   // interleave gate row j and up row j so the GEMM epilogue sees both
-            std::vector<int8_t> il((size_t)2 * dff * d);
+        {   // interleave gate row j and up row j so the GEMM epilogue sees both; rows
+            // j >= d_ff (padding to dffp) stay zero
+            std::vector<int8_t> il((size_t)2 * dffp * d, 0);
             for (int j = 0; j < dff; j++) {
                 memcpy(&il[(size_t)(2 * j) * d], t->data + (size_t)j * d, d);
                 memcpy(&il[(size_t)(2 * j + 1) * d], t->data + (size_t)(dff + j) * d, d);
@@ -374,7 +382,11 @@ int load_model(czg_ctx *c, const uint8_t *bytes, size_t len) {
             if (!upload(c, &L.up_w, il.data(), il.size())) return CZG_E_DEVICE;
         }
         if ((st = need(c, f, p + "ffn.down.weight", "I8", (int64_t)d * dff, &t))) return st;
-        if (!upload(c, &L.down_w, t->data, (size_t)d * dff)) return CZG_E_DEVICE;
+        {   // [d][dffp]: columns j >= d_ff are zero
+            std::vector<int8_t> dw((size_t)d * dffp, 0);
+            for (int i = 0; i < d; i++) memcpy(&dw[(size_t)i * dffp], t->data + (size_t)i * dff, dff);
+            if (!upload(c, &L.down_w, dw.data(), dw.size())) return CZG_E_DEVICE;
+        }
         if ((st = need(c, f, p + "attn.score_mult", "I32", H, &t))) return st;
         if (!upload(c, &L.score_mult, t->data, (size_t)H * 4)) return CZG_E_DEVICE;
         for (int hh = 0; hh < H; hh++) {
@@ -403,7 +415,7 @@ int load_model(czg_ctx *c, const uint8_t *bytes, size_t len) {
 size_t workspace_row_bytes(const czg_ctx *c) {
     const czg_model_info &m = c->info;
     const size_t d = (size_t)m.d_model;
-    return 16 + 4 * d + d + (d + 128) + 128 + d + d + (size_t)m.d_ff + 4 * (size_t)c->vpad + 8 + 4 + 4;
+    return 16 + 4 * d + d + (d + 128) + 128 + d + d + (size_t)c->dff_pad + 4 * (size_t)c->vpad + 8 + 4 + 4;
 }
 
 // (Re)allocate the wave workspace for `rows` tokens and `chunks` chunks per wave;
@@ -423,7 +435,7 @@ int alloc_workspace(czg_ctx *c, int rows, int chunks) {
               dalloc_ws(c, &c->qkv, R * (d + 128)) && dalloc_ws(c, &c->kv, R * 128 + (size_t)chunks * 4096) &&
               dalloc_ws(c, &c->rowchunk, R) &&
               dalloc_ws(c, &c->attn, R * d) && dalloc_ws(c, &c->o8, R * d) &&
-              dalloc_ws(c, &c->hbuf, R * m.d_ff) && dalloc_ws(c, &c->logits, R * c->vpad) &&
+              dalloc_ws(c, &c->hbuf, R * c->dff_pad) && dalloc_ws(c, &c->logits, R * c->vpad) &&
               dalloc_ws(c, &c->lohi, R) && dalloc_ws(c, &c->slots, 4 * R + 8 * (size_t)chunks + 64) &&
               dalloc_ws(c, &c->packed, 4 * R + 8 * (size_t)chunks + 64) &&
               dalloc_ws(c, &c->lens, (size_t)chunks) && dalloc_ws(c, &c->slot_off, (size_t)chunks + 1) &&
@@ -436,25 +448,22 @@ int alloc_workspace(czg_ctx *c, int rows, int chunks) {
     cudaMemsetAsync(c->err_flag, 0, sizeof(int), c->stream);
     c->cap_rows = rows;
     c->cap_chunks = chunks;
-    // tcgen05 GEMMs need K % 128 == 0 and N % 128 == 0 for every projection
-    const char *ge = getenv("CZG_GEMM");
-    c->use_tc = !(ge && std::string(ge) == "mma") && d % 128 == 0 && m.d_ff % 128 == 0 &&
-                tc_bn_for(d + 128) && tc_bn_for(d) && tc_bn_for(2 * m.d_ff) && tc_bn_for(c->vpad);
-    if (c->use_tc) {
-        bool ok = tc_make_matrix(c->tm_xn, c->xn, R, d, 128) && tc_make_matrix(c->tm_attn, c->attn, R, d, 128) &&
-                  tc_make_matrix(c->tm_h, c->hbuf, R, m.d_ff, 128) &&
-                  tc_make_matrix(c->tm_head, c->head_w, c->vpad, d, tc_bn_for(c->vpad));
-        for (auto &L : c->layers) {
-            ok = ok && tc_make_matrix(L.tm_qkv, L.qkv_w, d + 128, d, tc_bn_for(d + 128)) &&
-                 tc_make_matrix(L.tm_out, L.out_w, d, d, tc_bn_for(d)) &&
-                 tc_make_matrix(L.tm_up, L.up_w, 2 * m.d_ff, d, tc_bn_for(2 * m.d_ff)) &&
-                 tc_make_matrix(L.tm_down, L.down_w, d, m.d_ff, tc_bn_for(d));
-        }
-        if (!ok) c->use_tc = false;
+    // TMA descriptors of every GEMM operand (d, d + 128, 2 * dff_pad and vpad are
+    // multiples of 128 by construction)
+    const int dffp = c->dff_pad;
+    bool maps = tc_make_matrix(c->tm_xn, c->xn, R, d, 128) && tc_make_matrix(c->tm_attn, c->attn, R, d, 128) &&
+                tc_make_matrix(c->tm_h, c->hbuf, R, dffp, 128) &&
+                tc_make_matrix(c->tm_head, c->head_w, c->vpad, d, tc_bn_for(c->vpad));
+    for (auto &L : c->layers) {
+        maps = maps && tc_make_matrix(L.tm_qkv, L.qkv_w, d + 128, d, tc_bn_for(d + 128)) &&
+               tc_make_matrix(L.tm_out, L.out_w, d, d, tc_bn_for(d)) &&
+               tc_make_matrix(L.tm_up, L.up_w, 2 * dffp, d, tc_bn_for(2 * dffp)) &&
+               tc_make_matrix(L.tm_down, L.down_w, d, dffp, tc_bn_for(d));
     }
+    if (!maps) return fail(c, CZG_E_DEVICE, "cuTensorMapEncodeTiled failed for a GEMM operand");
     // fused head + coder interval: the shipped exp table, |logit| < 2^30, V a multiple of 256
     const char *hc = getenv("CZG_HEAD_CDF");
-    c->head_cdf = c->use_tc && !(hc && std::string(hc) == "0") && c->exp0 && c->logit_small &&
+    c->head_cdf = !(hc && std::string(hc) == "0") && c->exp0 && c->logit_small &&
                   m.vocab_size == c->vpad && c->vpad % 256 == 0 && m.coef_q24 < (1u << 23) && d % 128 == 0;
     c->h_meta_bytes = (size_t)chunks * 48 + 64;
     if (!cuda_ok(c, cudaMallocHost(&c->h_meta, c->h_meta_bytes), "cudaMallocHost")) return CZG_E_DEVICE;
@@ -479,11 +488,13 @@ int ensure_workspace(czg_ctx *c, size_t rows) {
     return alloc_workspace(c, rows_i, std::max(1024, rows_i / 16));
 }
 
-// One projection: tcgen05 path when available, else the mma.sync kernel.
-void gemm(czg_ctx *c, const TcMatrix &ta, const TcMatrix &tb, const int8_t *A, const int8_t *B, int M, int N,
-          int K, int epi, int mult, int shift, void *out, int ldo) {
-    if (!c->use_tc || !launch_gemm_tc(ta, tb, M, N, K, epi, mult, shift, out, ldo, c->err_flag, c->stream))
-        launch_gemm(A, B, M, N, K, epi, mult, shift, out, ldo, c->stream);
+// One projection on the tcgen05 GEMM.  A shape it cannot take or an output map
+// that cannot be encoded is an error of the call (there is no other GEMM).
+bool gemm(czg_ctx *c, const TcMatrix &ta, const TcMatrix &tb, int M, int N, int K, int epi, int mult, int shift,
+          void *out, int ldo) {
+    if (launch_gemm_tc(ta, tb, M, N, K, epi, mult, shift, out, ldo, c->err_flag, c->stream)) return true;
+    c->gemm_failed = true;
+    return false;
 }
 
 struct Trace {
@@ -493,16 +504,12 @@ struct Trace {
     int8_t *final_in = nullptr;
 };
 
-// Run the model + CDF + encoder for chunks [c0, c1); rows are the wave's tokens.
-// d_tok: device pointer to the wave's first token.  Results stay on device.
-int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t c0, uint32_t c1,
-             const Trace *tr) {
-    const czg_model_info &m = c->info;
-    const int d = m.d_model, dff = m.d_ff, V = m.vocab_size, H = m.n_heads;
+// Chunk tables of the wave [c0, c1) to the device: row offset, length, token
+// offset, slot offsets, and the chunks in attention launch order.  Returns the
+// longest chunk.
+int wave_meta(czg_ctx *c, const uint64_t *starts, uint32_t c0, uint32_t c1) {
     const int nc = (int)(c1 - c0);
-    const int M = (int)(starts[c1] - starts[c0]);
     cudaStream_t st = c->stream;
-    // chunk metadata: row0 / len / token offset / slot offsets
     int *h_row0 = reinterpret_cast<int *>(c->h_meta);
     int *h_len = h_row0 + nc;
     uint64_t *h_tok0 = reinterpret_cast<uint64_t *>(h_len + nc + (nc & 1));
@@ -537,6 +544,19 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
     cudaMemcpyAsync(c->chunk_tok0, h_tok0, sizeof(uint64_t) * nc, cudaMemcpyHostToDevice, st);
     cudaMemcpyAsync(c->slot_off, h_slot, sizeof(uint64_t) * (nc + 1), cudaMemcpyHostToDevice, st);
     cudaMemsetAsync(c->err_flag, 0, sizeof(int), st);
+    return max_len;
+}
+
+// Run the model + CDF + encoder for chunks [c0, c1); rows are the wave's tokens.
+// d_tok: device pointer to the wave's first token.  Results stay on device.
+int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t c0, uint32_t c1,
+             const Trace *tr) {
+    const czg_model_info &m = c->info;
+    const int d = m.d_model, dff = c->dff_pad, V = m.vocab_size, H = m.n_heads;
+    const int nc = (int)(c1 - c0);
+    const int M = (int)(starts[c1] - starts[c0]);
+    cudaStream_t st = c->stream;
+    const int max_len = wave_meta(c, starts, c0, c1);
 
     timed(c, kRows, [&] {
         launch_rows(d_tok, c->chunk_row0, c->chunk_len, c->chunk_tok0, nc, V, c->tok_in, c->tok_out,
@@ -549,7 +569,7 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
     for (int l = 0; l < m.n_layers; l++) {
         const LayerDev &L = c->layers[l];
         timed(c, kGemmQkv, [&] {
-            gemm(c, c->tm_xn, L.tm_qkv, c->xn, L.qkv_w, M, d + 128, d, kEpiRequant, L.qkv_mult, L.qkv_shift,
+            gemm(c, c->tm_xn, L.tm_qkv, M, d + 128, d, kEpiRequant, L.qkv_mult, L.qkv_shift,
                  c->qkv, d + 128);
         });
         // tensor-core attention, K/V tiles streamed per warp from a per-chunk layout (at
@@ -581,7 +601,7 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
             cudaMemcpy2DAsync(tr->attn + (size_t)l * d, (size_t)m.n_layers * d, c->attn, d, d, M,
                               cudaMemcpyDeviceToHost, st);
         timed(c, kGemmO, [&] {
-            gemm(c, c->tm_attn, L.tm_out, c->attn, L.out_w, M, d, d, kEpiRequant, L.out_mult, L.out_shift,
+            gemm(c, c->tm_attn, L.tm_out, M, d, d, kEpiRequant, L.out_mult, L.out_shift,
                  c->o8, d);
         });
         timed(c, kResidualNorm, [&] {
@@ -589,11 +609,11 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
                                  l == 0 ? c->embed : nullptr, true, c->x_res, c->res16, c->xn, st);
         });
         timed(c, kGemmUp, [&] {
-            gemm(c, c->tm_xn, L.tm_up, c->xn, L.up_w, M, 2 * dff, d, kEpiReglu, L.up_mult, L.up_shift,
+            gemm(c, c->tm_xn, L.tm_up, M, 2 * dff, d, kEpiReglu, L.up_mult, L.up_shift,
                  c->hbuf, dff);
         });
         timed(c, kGemmDown, [&] {
-            gemm(c, c->tm_h, L.tm_down, c->hbuf, L.down_w, M, d, dff, kEpiRequant, L.down_mult,
+            gemm(c, c->tm_h, L.tm_down, M, d, dff, kEpiRequant, L.down_mult,
                  L.down_shift, c->o8, d);
         });
         const int8_t *next = l + 1 < m.n_layers ? c->layers[l + 1].attn_norm : c->final_norm;
@@ -613,7 +633,7 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
     }
     if (!fused) {
         timed(c, kGemmHead, [&] {
-            gemm(c, c->tm_xn, c->tm_head, c->xn, c->head_w, M, c->vpad, d, kEpiInt32, 1, 0, c->logits, c->vpad);
+            gemm(c, c->tm_xn, c->tm_head, M, c->vpad, d, kEpiInt32, 1, 0, c->logits, c->vpad);
         });
         if (tr && tr->logits)
             cudaMemcpy2DAsync(tr->logits, (size_t)V * 4, c->logits, (size_t)c->vpad * 4, (size_t)V * 4, M,
@@ -629,6 +649,10 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
         launch_encode(c->lohi, c->chunk_row0, c->chunk_len, nc, m.target_total, c->slots, c->slot_off,
                       c->lens, c->err_flag, st);
     });
+    if (c->gemm_failed) {
+        c->gemm_failed = false;
+        return fail(c, CZG_E_DEVICE, "a GEMM launch was refused (output tensor map)");
+    }
     if (!cuda_ok(c, cudaGetLastError(), "kernel launch")) return CZG_E_DEVICE;
     return CZG_OK;
 }
@@ -664,6 +688,39 @@ void stats_end(czg_ctx *c) {
     float ms = 0;
     cudaEventElapsedTime(&ms, c->ev_begin, c->ev_end);
     c->stats.total_ms = ms;
+}
+
+// After a wave's encoder: the chunk lengths and the error word to the host, packed
+// offsets, then pack the chunks and copy them to out + total (when they fit).
+int wave_copy_out(czg_ctx *c, uint32_t c0, int nc, uint8_t *out, uint64_t out_cap, uint32_t *out_lens,
+                  uint64_t &total, int &status) {
+    int err = 0;
+    cudaMemcpyAsync(out_lens + c0, c->lens, sizeof(uint32_t) * nc, cudaMemcpyDeviceToHost, c->stream);
+    cudaMemcpyAsync(&err, c->err_flag, sizeof(int), cudaMemcpyDeviceToHost, c->stream);
+    if (!cuda_ok(c, cudaStreamSynchronize(c->stream), "wave")) return CZG_E_DEVICE;
+    c->stats.d2h_bytes += sizeof(uint32_t) * nc;
+    if (err & kErrToken) return fail(c, CZG_E_TOKEN, "token id >= vocab_size");
+    if (err & kErrOverflow) return fail(c, CZG_E_DEVICE, "encoder slot overflow");
+    if (err & kErrTimeout) return fail(c, CZG_E_TIMEOUT, "a bounded device wait expired");
+    uint64_t *h_pack = reinterpret_cast<uint64_t *>(c->h_meta);
+    h_pack[0] = 0;
+    for (int i = 0; i < nc; i++) h_pack[i + 1] = h_pack[i] + out_lens[c0 + i];
+    const uint64_t wave_bytes = h_pack[nc];
+    if (total + wave_bytes <= out_cap) {
+        cudaMemcpyAsync(c->pack_off, h_pack, sizeof(uint64_t) * (nc + 1), cudaMemcpyHostToDevice, c->stream);
+        timed(c, kPack, [&] { launch_pack(c->slots, c->slot_off, c->lens, c->pack_off, nc, c->packed, c->stream); });
+        EvPair &e = next_ev(c, -2);
+        cudaEventRecord(e.a, c->stream);
+        cudaMemcpyAsync(out + total, c->packed, wave_bytes, cudaMemcpyDeviceToHost, c->stream);
+        cudaEventRecord(e.b, c->stream);
+        c->stats.d2h_bytes += wave_bytes;
+    } else {
+        status = CZG_E_CAPACITY;
+    }
+    total += wave_bytes;
+    if (!cuda_ok(c, cudaStreamSynchronize(c->stream), "wave copy-out")) return CZG_E_DEVICE;
+    collect_events(c);
+    return CZG_OK;
 }
 
 int compress_impl(czg_ctx *c, const uint32_t *tokens, bool device_tokens, const uint64_t *starts,
@@ -706,36 +763,7 @@ int compress_impl(czg_ctx *c, const uint32_t *tokens, bool device_tokens, const 
         }
         int st = run_wave(c, d_tok, starts, w.c0, w.c1, nullptr);
         if (st) return st;
-        const int nc = (int)(w.c1 - w.c0);
-        // lengths -> packed offsets on the host, then pack and copy out
-        int err = 0;
-        cudaMemcpyAsync(out_lens + w.c0, c->lens, sizeof(uint32_t) * nc, cudaMemcpyDeviceToHost, c->stream);
-        cudaMemcpyAsync(&err, c->err_flag, sizeof(int), cudaMemcpyDeviceToHost, c->stream);
-        if (!cuda_ok(c, cudaStreamSynchronize(c->stream), "wave")) return CZG_E_DEVICE;
-        c->stats.d2h_bytes += sizeof(uint32_t) * nc;
-        if (err & kErrToken) return fail(c, CZG_E_TOKEN, "token id >= vocab_size");
-        if (err & kErrOverflow) return fail(c, CZG_E_DEVICE, "encoder slot overflow");
-        if (err & kErrTimeout) return fail(c, CZG_E_TIMEOUT, "a bounded device wait expired");
-        uint64_t *h_pack = reinterpret_cast<uint64_t *>(c->h_meta);
-        h_pack[0] = 0;
-        for (int i = 0; i < nc; i++) h_pack[i + 1] = h_pack[i] + out_lens[w.c0 + i];
-        const uint64_t wave_bytes = h_pack[nc];
-        if (total + wave_bytes <= out_cap) {
-            cudaMemcpyAsync(c->pack_off, h_pack, sizeof(uint64_t) * (nc + 1), cudaMemcpyHostToDevice, c->stream);
-            timed(c, kPack, [&] {
-                launch_pack(c->slots, c->slot_off, c->lens, c->pack_off, nc, c->packed, c->stream);
-            });
-            EvPair &e = next_ev(c, -2);
-            cudaEventRecord(e.a, c->stream);
-            cudaMemcpyAsync(out + total, c->packed, wave_bytes, cudaMemcpyDeviceToHost, c->stream);
-            cudaEventRecord(e.b, c->stream);
-            c->stats.d2h_bytes += wave_bytes;
-        } else {
-            status = CZG_E_CAPACITY;
-        }
-        total += wave_bytes;
-        if (!cuda_ok(c, cudaStreamSynchronize(c->stream), "wave copy-out")) return CZG_E_DEVICE;
-        collect_events(c);
+        if ((st = wave_copy_out(c, w.c0, (int)(w.c1 - w.c0), out, out_cap, out_lens, total, status))) return st;
     }
     stats_end(c);
     if (out_needed) *out_needed = total;
@@ -787,7 +815,7 @@ int decompress_impl(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts
     if (!data_starts || !n_tokens || !out_tokens || (!data && data_starts[n_chunks] > data_starts[0]))
         return fail(c, CZG_E_ARG, "null input pointer");
     const czg_model_info &m = c->info;
-    const int d = m.d_model, dff = m.d_ff, V = m.vocab_size, H = m.n_heads;
+    const int d = m.d_model, dff = c->dff_pad, V = m.vocab_size, H = m.n_heads;
     const int limit = std::min(m.context_length, m.max_seq_len);
     uint64_t total_tok = 0;
     int max_len = 0;
@@ -866,7 +894,7 @@ int decompress_impl(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts
                 const LayerDev &L = c->layers[l];
                 int8_t *kvc = c->kvc + (size_t)l * layer_ld;
                 timed(c, kGemmQkv, [&] {
-                    gemm(c, c->tm_xn, L.tm_qkv, c->xn, L.qkv_w, M, d + 128, d, kEpiRequant, L.qkv_mult, L.qkv_shift,
+                    gemm(c, c->tm_xn, L.tm_qkv, M, d + 128, d, kEpiRequant, L.qkv_mult, L.qkv_shift,
                          c->qkv, d + 128);
                 });
                 timed(c, kKvAppend, [&] {
@@ -882,7 +910,7 @@ int decompress_impl(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts
                                                 c->rope_cos, c->rope_sin, c->lut, c->attn, d, s);
                 });
                 timed(c, kGemmO, [&] {
-                    gemm(c, c->tm_attn, L.tm_out, c->attn, L.out_w, M, d, d, kEpiRequant, L.out_mult, L.out_shift,
+                    gemm(c, c->tm_attn, L.tm_out, M, d, d, kEpiRequant, L.out_mult, L.out_shift,
                          c->o8, d);
                 });
                 timed(c, kResidualNorm, [&] {
@@ -890,11 +918,11 @@ int decompress_impl(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts
                                          l == 0 ? c->embed : nullptr, true, c->x_res, c->res16, c->xn, s);
                 });
                 timed(c, kGemmUp, [&] {
-                    gemm(c, c->tm_xn, L.tm_up, c->xn, L.up_w, M, 2 * dff, d, kEpiReglu, L.up_mult, L.up_shift,
+                    gemm(c, c->tm_xn, L.tm_up, M, 2 * dff, d, kEpiReglu, L.up_mult, L.up_shift,
                          c->hbuf, dff);
                 });
                 timed(c, kGemmDown, [&] {
-                    gemm(c, c->tm_h, L.tm_down, c->hbuf, L.down_w, M, d, dff, kEpiRequant, L.down_mult,
+                    gemm(c, c->tm_h, L.tm_down, M, d, dff, kEpiRequant, L.down_mult,
                          L.down_shift, c->o8, d);
                 });
                 const int8_t *next = l + 1 < m.n_layers ? c->layers[l + 1].attn_norm : c->final_norm;
@@ -904,7 +932,7 @@ int decompress_impl(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts
                 });
             }
             timed(c, kGemmHead, [&] {
-                gemm(c, c->tm_xn, c->tm_head, c->xn, c->head_w, M, c->vpad, d, kEpiInt32, 1, 0, c->logits, c->vpad);
+                gemm(c, c->tm_xn, c->tm_head, M, c->vpad, d, kEpiInt32, 1, 0, c->logits, c->vpad);
             });
             timed(c, kCdfDecode, [&] {
                 launch_cdf_decode(c->logits, V, c->vpad, c->lut, c->lut4k, c->exp0 && c->logit_small, m.coef_q24, m.target_total, M, c->dstate, c->ddata,
@@ -914,6 +942,10 @@ int decompress_impl(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts
                 if (!cuda_ok(c, cudaStreamSynchronize(s), "decode step")) return CZG_E_DEVICE;
                 collect_events(c);
             }
+        }
+        if (c->gemm_failed) {
+            c->gemm_failed = false;
+            return fail(c, CZG_E_DEVICE, "a GEMM launch was refused (output tensor map)");
         }
         if (!cuda_ok(c, cudaGetLastError(), "kernel launch")) return CZG_E_DEVICE;
         // tokens of this wave (stream order) -> caller order
@@ -1066,6 +1098,40 @@ int czg_debug_trace(czg_ctx *c, const uint32_t *tokens, uint32_t n, int32_t *log
     stats_end(c);
     if (err & kErrToken) return fail(c, CZG_E_TOKEN, "token id >= vocab_size");
     if (err & kErrTimeout) return fail(c, CZG_E_TIMEOUT, "a bounded device wait expired");
+    return CZG_OK;
+}
+
+int czg_debug_encode_intervals(czg_ctx *c, const uint32_t *lohi, const uint64_t *starts, uint32_t n_chunks,
+                               uint8_t *out, uint64_t out_cap, uint32_t *out_lens, uint64_t *out_needed) {
+    if (!c) return CZG_E_ARG;
+    if ((!starts && n_chunks) || (n_chunks && !lohi)) return fail(c, CZG_E_ARG, "null input pointer");
+    for (uint32_t i = 0; i < n_chunks; i++)
+        if (starts[i + 1] < starts[i]) return fail(c, CZG_E_ARG, "chunk_starts must be non-decreasing");
+    const uint64_t ntok = n_chunks ? starts[n_chunks] - starts[0] : 0;
+    if (!out) {
+        if (out_needed) *out_needed = czg_compress_bound(ntok, n_chunks);
+        return CZG_OK;
+    }
+    if (!out_lens) return fail(c, CZG_E_ARG, "out_lens is null");
+    if (!cuda_ok(c, cudaSetDevice(c->device), "cudaSetDevice")) return CZG_E_DEVICE;
+    stats_begin(c);
+    if (int st = ensure_workspace(c, ntok)) return st;
+    uint64_t total = 0;
+    int status = CZG_OK;
+    for (const WavePlan &w : plan_waves(c, starts, n_chunks)) {
+        const uint64_t t0 = starts[w.c0], nt = starts[w.c1] - t0;
+        wave_meta(c, starts, w.c0, w.c1);
+        cudaMemcpyAsync(c->lohi, lohi + 2 * (t0 - starts[0]), nt * 8, cudaMemcpyHostToDevice, c->stream);
+        timed(c, kEncode, [&] {
+            launch_encode(c->lohi, c->chunk_row0, c->chunk_len, (int)(w.c1 - w.c0), c->info.target_total, c->slots,
+                          c->slot_off, c->lens, c->err_flag, c->stream);
+        });
+        if (!cuda_ok(c, cudaGetLastError(), "kernel launch")) return CZG_E_DEVICE;
+        if (int st = wave_copy_out(c, w.c0, (int)(w.c1 - w.c0), out, out_cap, out_lens, total, status)) return st;
+    }
+    stats_end(c);
+    if (out_needed) *out_needed = total;
+    if (status == CZG_E_CAPACITY) return fail(c, CZG_E_CAPACITY, "output buffer too small");
     return CZG_OK;
 }
 

@@ -2,7 +2,7 @@
 // cores (tcgen05.mma kind::i8), operands staged by TMA, accumulator in TMEM.
 //
 // Computes the int8 linear layers of rust/src/linear.rs:12-31
-// (out[m, n] = sum_k x[m, k] * W[n, k]) with the epilogues of gemm_mma.cu:
+// (out[m, n] = sum_k x[m, k] * W[n, k]) with one of three epilogues:
 // requantisation (rust/src/model.rs:280-300), requantisation + ReGLU on
 // interleaved gate/up columns (rust/src/reglu.rs:20-46), or raw int32.
 //

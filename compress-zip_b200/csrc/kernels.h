@@ -43,17 +43,14 @@ void launch_kv_prep_split(const int8_t *qkv, int ldq, int d, const int *pos, con
                           const int *chunk_row0, const int *chunk_len, const int16_t *rope_cos,
                           const int16_t *rope_sin, int M, int8_t *kv, cudaStream_t st);
 
-// gemm_mma.cu: C[M,N] = A[M,K] . B[N,K]^T in int8 -> int32 with an epilogue.
-// A must hold ceil(M/128)*128 readable rows; N % 128 == 0; K % 64 == 0.
+// GEMM epilogues (gemm_tc.cu): C[M,N] = A[M,K] . B[N,K]^T in int8 -> int32, then one of
 enum GemmEpilogue {
     kEpiRequant = 0,   // out int8 [M][ldo] = requant(acc)
     kEpiReglu = 1,     // B rows interleaved (gate_j, up_j): out int8 [M][ldo], column j
     kEpiInt32 = 2      // out int32 [M][ldo]
 };
-void launch_gemm(const int8_t *A, const int8_t *B, int M, int N, int K, int epi, int mult,
-                 int shift, void *out, int ldo, cudaStream_t st);
 
-// gemm_tc.cu: the same GEMM on tcgen05 (kind::i8) with TMA-staged operands and
+// gemm_tc.cu: the GEMM on tcgen05 (kind::i8) with TMA-staged operands and
 // TMA stores of the output.  A TcMatrix is a TMA descriptor of a row-major
 // [rows][K] int8 matrix read in boxes of 128 bytes of K by box_rows rows (128 for
 // A, tc_bn_for(N) for B).  Needs K % 128 == 0, N % 128 == 0 (N % 256 == 0 for

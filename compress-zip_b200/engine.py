@@ -23,7 +23,8 @@ MAX_KERNEL_CLASSES = 24
 EXPORTS = ["czg_ctx_create", "czg_ctx_destroy", "czg_last_error", "czg_model_info_get",
            "czg_compress_bound", "czg_compress_chunks", "czg_compress_chunks_device",
            "czg_decompress_chunks", "czg_last_stats", "czg_kernel_name", "czg_debug_trace",
-           "czg_set_stream", "czg_encode_intervals_static", "czg_set_kernel_timing"]
+           "czg_set_stream", "czg_encode_intervals_static", "czg_set_kernel_timing",
+           "czg_debug_encode_intervals"]
 
 
 class CzgError(RuntimeError):
@@ -84,6 +85,8 @@ def lib() -> C.CDLL:
         L.czg_encode_intervals_static.argtypes = [P, P, C.c_uint32, C.c_uint64, C.c_uint32, P,
                                                    C.c_uint64, P, C.POINTER(C.c_uint64), P]
         L.czg_encode_intervals_static.restype = C.c_int
+        L.czg_debug_encode_intervals.argtypes = [P, P, P, C.c_uint32, P, C.c_uint64, P, C.POINTER(C.c_uint64)]
+        L.czg_debug_encode_intervals.restype = C.c_int
         _lib = L
     return _lib
 
@@ -210,3 +213,19 @@ class Engine:
         self._check(lib().czg_debug_trace(self._h, _p(tokens), n, _p(logits), _p(lohi), _p(attn),
                                           _p(fin)))
         return {"logits": logits, "lohi": lohi, "attn": attn, "final_in": fin}
+
+    def debug_encode_intervals(self, lohi: np.ndarray, chunk_starts: np.ndarray) -> list[bytes]:
+        """The compress path's encoder alone on given (sym_low, sym_high) pairs."""
+        lohi = np.ascontiguousarray(lohi, dtype=np.uint32).reshape(-1, 2)
+        starts = np.ascontiguousarray(chunk_starts, dtype=np.uint64)
+        n = len(starts) - 1
+        if n <= 0:
+            return []
+        lens = np.zeros(n, dtype=np.uint32)
+        out = np.empty(max(4 * len(lohi) + 8 * n, 1), dtype=np.uint8)
+        need = C.c_uint64(0)
+        self._check(lib().czg_debug_encode_intervals(self._h, _p(lohi), _p(starts), n, _p(out), len(out),
+                                                     _p(lens), C.byref(need)))
+        offs = np.concatenate([[0], np.cumsum(lens, dtype=np.uint64)]).astype(np.int64)
+        raw = out[: need.value].tobytes()
+        return [raw[offs[i]:offs[i + 1]] for i in range(n)]

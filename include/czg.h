@@ -130,6 +130,15 @@ const char *czg_kernel_name(uint32_t kernel_class);
 int czg_debug_trace(czg_ctx *ctx, const uint32_t *tokens, uint32_t n, int32_t *logits,
                     uint32_t *lohi, int8_t *attn, int8_t *final_in);
 
+/* The encoder of czg_compress_chunks run alone on given coder intervals, for
+ * testing it against the reference's ArithEncoder (rust/src/arith_coder.rs:80-130)
+ * on crafted interval sequences.  lohi: host array of (sym_low, sym_high) pairs,
+ * chunk i taking pairs chunk_starts[i] .. chunk_starts[i+1]; each pair must
+ * satisfy sym_low < sym_high <= target_total.  Output as czg_compress_chunks. */
+int czg_debug_encode_intervals(czg_ctx *ctx, const uint32_t *lohi, const uint64_t *chunk_starts,
+                               uint32_t n_chunks, uint8_t *out, uint64_t out_cap, uint32_t *out_lens,
+                               uint64_t *out_needed);
+
 /* Allocation-free encoder: intervals -> packed chunk bytes.  (No counterpart in
  * the reference; it is the encoder of the compress path, rust/src/arith_coder.rs
  * run per chunk, for callers that may not allocate device memory.)
@@ -143,7 +152,9 @@ int czg_debug_trace(czg_ctx *ctx, const uint32_t *tokens, uint32_t n, int32_t *l
  * the library, held until the process exits).  It calls no allocating routine.
  *
  * d_lohi: device array of n_tokens (sym_low, sym_high) pairs, chunk by chunk;
- * d_chunk_len: device array of n_chunks token counts (summing to n_tokens);
+ * d_chunk_len: device array of n_chunks token counts, which must sum to
+ * n_tokens (checked on the device: otherwise CZG_E_ARG, and nothing is read past
+ * the intervals or written);
  * target_total: the model's target total (czg_model_info.target_total).
  * Encoded chunks are packed back to back into d_out (out_cap bytes), chunk i's
  * length goes to d_out_lens[i], the packed size to *out_bytes.  Runs on
@@ -152,7 +163,9 @@ int czg_debug_trace(czg_ctx *ctx, const uint32_t *tokens, uint32_t n, int32_t *l
  * (else CZG_E_LIMIT); a too small out_cap gives CZG_E_CAPACITY with the needed
  * size in *out_bytes.
  * The first call on a device looks up the array's device address (with that
- * device current); make that first call before any stream capture.  All calls
+ * device current) and keeps it for that device's context; a call after a
+ * cudaDeviceReset looks it up again.  Make the first call on each device, and
+ * the first after a reset, before any stream capture.  All calls
  * share the array and each call clears what must start at zero; calls whose
  * work overlaps on the GPU race on it and must be serialised by the caller. */
 #define CZG_STATIC_MAX_CHUNKS 16384

@@ -312,6 +312,20 @@ def encode_symbols(cum_rows, symbols) -> bytes:
     return buf[: e.len].tobytes()
 
 
+def encode_intervals(pairs, total: int) -> bytes:
+    """Arithmetic-encode (sym_low, sym_high) pairs directly (arith_coder.rs:80-130)."""
+    n = len(pairs)
+    buf = np.zeros(slot_cap(max(n, 1)), dtype=np.uint8)
+    e = Encoder()
+    L = lib()
+    L.czo_enc_init(C.byref(e), ptr(buf), len(buf))
+    for lo, hi in pairs:
+        L.czo_enc_encode_range(C.byref(e), int(lo), int(hi), int(total))
+    L.czo_enc_finish(C.byref(e))
+    assert not e.overflow
+    return buf[: e.len].tobytes()
+
+
 def decode_symbols(data: bytes, cum_rows) -> list[int]:
     arr = np.frombuffer(data + b"\0", dtype=np.uint8).copy()
     d = Decoder()

@@ -353,3 +353,35 @@ def test_requant_forms(shipped_path, tmp_path, oracle_mod, shipped_tokens, proj,
         assert eng.compress_chunks(toks, starts) == oracle_mod.compress_chunks(om, toks, starts)
     finally:
         eng.close()
+
+
+def test_dff_not_multiple_of_128(shipped_path, tmp_path, oracle_mod, shipped_tokens):
+    """d_ff = 960 (a multiple of 64, not of 128): the engine pads the FFN to 1024 hidden
+    units with zero weights for its tcgen05 GEMMs; bytes and intermediates equal the
+    oracle's, which runs the unpadded 960."""
+    from compress_zip_b200 import czm
+    from compress_zip_b200.engine import Engine
+
+    mf = czm.ModelFile.load(shipped_path)
+    t = {k: np.array(v) for k, v in mf.tensors.items()}
+    dff, new = 1024, 960
+    up = t["layers.0.ffn.up.weight"].reshape(2 * dff, -1)
+    t["layers.0.ffn.up.weight"] = np.ascontiguousarray(np.concatenate([up[:new], up[dff:dff + new]]))
+    t["layers.0.ffn.down.weight"] = np.ascontiguousarray(t["layers.0.ffn.down.weight"].reshape(-1, dff)[:, :new])
+    meta = dict(mf.metadata)
+    meta["d_ff"] = str(new)
+    p = tmp_path / "dff960.czm"
+    p.write_bytes(czm.write_safetensors(t, meta))
+    om = oracle_mod.load_model(str(p))
+    assert om.cfg["d_ff"] == new
+    eng = Engine.from_file(str(p), 0)
+    try:
+        assert eng.info["d_ff"] == new
+        _trace_equal(eng, om, oracle_mod, shipped_tokens[:300])
+        toks = shipped_tokens[:2100]
+        starts = _starts(len(toks), 1024)
+        got = eng.compress_chunks(toks, starts)
+        assert got == oracle_mod.compress_chunks(om, toks, starts)
+        assert np.array_equal(eng.decompress_chunks(got, np.diff(starts).astype(np.uint32)), toks)
+    finally:
+        eng.close()

@@ -17,7 +17,7 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 
-def test_static_encoder_matches_compress_entry(shipped_path):
+def test_static_encoder_matches_compress_entry(shipped_path, shipped_oracle, oracle_mod):
     import torch
 
     from compress_zip_b200 import czm, synth
@@ -32,6 +32,8 @@ def test_static_encoder_matches_compress_entry(shipped_path):
             starts = np.array(list(range(0, len(ids), C_len)) + [len(ids)], np.uint64)
             lens = np.diff(starts).astype(np.uint32)
             want_packed, want_lens = eng.compress_packed(ids, starts)
+            # and the CPU oracle's bytes for the same chunks, directly
+            assert want_packed.tobytes() == b"".join(oracle_mod.compress_chunks(shipped_oracle, ids, starts))
             # coder intervals of every chunk from the GPU forward pass
             lohi = np.concatenate([eng.debug_trace(ids[int(a):int(b)])["lohi"]
                                    for a, b in zip(starts[:-1], starts[1:])]).astype(np.uint32)
@@ -52,6 +54,16 @@ def test_static_encoder_matches_compress_entry(shipped_path):
                 got = d_out[: nbytes.value].cpu().numpy()
                 assert np.array_equal(got, want_packed), f"call {call}: bytes differ"
                 assert np.array_equal(d_out_lens.cpu().numpy().view(np.uint32), want_lens)
+        # chunk lengths that do not add up to n_tokens: refused on the device before any
+        # interval is read (CZG_E_ARG), nothing written
+        for n_tok in (len(ids) - 1, len(ids) + 1):
+            d_out.fill_(0xCD)
+            nbytes = C.c_uint64(7)
+            st = E.lib().czg_encode_intervals_static(
+                d_lohi.data_ptr(), d_len.data_ptr(), len(lens), n_tok, eng.info["target_total"],
+                d_out.data_ptr(), cap, d_out_lens.data_ptr(), C.byref(nbytes), C.c_void_p(stream))
+            assert st == 1 and nbytes.value == 0
+            assert bool((d_out == 0xCD).all())
         # beyond the stated limit: a clear status, no work
         nbytes = C.c_uint64(0)
         st = E.lib().czg_encode_intervals_static(
