@@ -90,12 +90,12 @@ __device__ __forceinline__ uint32_t exp_rec(int diff, const uint16_t *lut4k, uin
 
 // score = round_even(round_even(dot / 4) * mult / 2^15) saturated to int32
 // (attention.rs:236-245).  round_even(x / 2^s) = (x + 2^(s-1) - 1 + ((x >> s) & 1)) >> s.
-template <bool WIDE>
+template <bool SAT>
 __device__ __forceinline__ int score_from_dot(int dot, int mult) {
     const int du = (dot + 1 + ((dot >> 2) & 1)) >> 2;
     const long long p = (long long)du * (long long)mult;
     long long s = (p + 16383 + ((p >> 15) & 1)) >> 15;
-    if (WIDE) {   // |mult| >= 2^28: the result may leave the int32 range
+    if (SAT) {   // |mult| >= 2^28: the result may leave the int32 range
         s = s < -2147483648ll ? -2147483648ll : (s > 2147483647ll ? 2147483647ll : s);
     }
     return (int)s;
@@ -111,6 +111,30 @@ __device__ __forceinline__ int score_fast(int dot, int mult16) {
     const long long X = (long long)(du * 8192) * (long long)mult16 + 0x80000000ll;
     const int hi = (int)(X >> 32);
     return (uint32_t)X == 0u ? (hi & ~1) : hi;
+}
+
+// Exact scores and exp indices in FP32 (|mult| < 2^19).  A float in [2^23, 2^24) has
+// spacing 1, and one fused multiply-add rounds its exact result to nearest, ties to
+// even -- the reference's round-half-to-even shift.  With M1 = 1.5 * 2^23 as a bias:
+//   bits(M1) + dot              = M1 + dot                     (|dot| < 2^21)
+//   fma(M1 + dot, 1/4, 0.75 M1)  = M1 + rne(dot / 4)
+//   fma(M1 + du, mult / 2^15, M1 - M1 mult / 2^15) = M1 + rne(du * mult / 2^15)
+// (|du * mult / 2^15| < 2^22; mult / 2^15 and M1 - 384 mult are exact floats), so the
+// bits of the result minus bits(M1) are the score (attention.rs:236-245), and the bits
+// order like the scores.  The exp index t256 = floor((neg * 378194 + 2^23) / 2^24) of a
+// difference neg < 2^23 is fma(neg, 378194 / 2^24, M1) - M1 (no ties below 2^22; above
+// it the index is clamped at 4096 either way).  Checked exhaustively on the host.
+constexpr uint32_t kM1Bits = 0x4B400000u;   // 12582912.0f
+// dot_b: kM1Bits + dot (the QK accumulators start at kM1Bits in MODE 0)
+__device__ __forceinline__ int score_flt(int dot_b, float mf, float c2) {
+    const float ub = __fmaf_rn(__int_as_float(dot_b), 0.25f, 9437184.0f);
+    return __float_as_int(__fmaf_rn(ub, mf, c2));   // biased: kM1Bits + score
+}
+// t256 of a (non-negative) difference of two biased scores, clamped at 4096
+__device__ __forceinline__ uint32_t t256_flt(int pm_b, int sc_b) {
+    const float neg = __fsub_rn(__int_as_float(pm_b), __int_as_float(sc_b));   // exact
+    const uint32_t tb = (uint32_t)__float_as_int(__fmaf_rn(neg, 378194.0f / 16777216.0f, 12582912.0f));
+    return min(tb, kM1Bits + 4096u) - kM1Bits;
 }
 
 // One rescale of a state value by a record's factor e (attention.rs:252-259):
@@ -141,12 +165,46 @@ struct Tile {
 };
 
 // Scores, prefix max, records and weights of row g in one 32-key tile.
-template <bool MASKED, bool WIDE, bool EXP0>
-__device__ __forceinline__ void tile_softmax(const int (&sacc)[4][4], int kb, int prow, int n, int mult, int t,
-                                             int &m, const uint16_t *lut4k, uint32_t c8, Tile &T) {
+// MODE 0: scores in FP32 (|mult| < 2^19), scores and the running max m biased by kM1Bits;
+// MODE 1: |mult| < 2^27 (score_fast); MODE 2: any mult (64-bit, saturating).
+template <bool MASKED, int MODE, bool EXP0>
+__device__ __forceinline__ void tile_softmax(const int (&sacc)[4][4], int kb, int prow, int n, int mult, float mf,
+                                             float c2, int t, int &m, const uint16_t *lut4k, uint32_t c8, Tile &T) {
     int sc[8];
     uint32_t rm = 0;
-    if constexpr (!WIDE) {
+    if constexpr (MODE == 0) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            bool valid = true;
+            if (MASKED) valid = kb + 8 * t + i <= prow && prow < n;
+            sc[i] = valid ? score_flt(sacc[i >> 1][i & 1], mf, c2) : INT32_MIN;
+        }
+        const int x = max(max(max(sc[0], sc[1]), max(sc[2], sc[3])), max(max(sc[4], sc[5]), max(sc[6], sc[7])));
+        const int y1 = __shfl_up_sync(0xffffffffu, x, 1, 4);
+        const int y2 = __shfl_up_sync(0xffffffffu, x, 2, 4);
+        const int y3 = __shfl_up_sync(0xffffffffu, x, 3, 4);
+        const int z1 = max(x, __shfl_xor_sync(0xffffffffu, x, 1));
+        const int run = m;
+        int pm = run;
+        if (t >= 1) pm = max(pm, y1);
+        if (t >= 2) pm = max(pm, y2);
+        if (t >= 3) pm = max(pm, y3);
+        if (pm == INT32_MIN) pm = sc[0];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            bool valid = true;
+            if (MASKED) valid = kb + 8 * t + i <= prow && prow < n;
+            int ef = min(pm - sc[i], 0);
+            if (MASKED) ef = valid ? ef : 0;
+            pm = max(pm, sc[i]);
+            uint32_t w = lut4k[t256_flt(pm, sc[i])];
+            if (!EXP0) w = pm == sc[i] ? 65535u : w;
+            T.w[i] = valid ? w : 0u;
+            T.ef[i] = (uint32_t)ef;
+            rm |= ((uint32_t)ef >> (31 - i)) & (1u << i);
+        }
+        m = max(run, max(z1, __shfl_xor_sync(0xffffffffu, z1, 2)));
+    } else if constexpr (MODE == 1) {
         // |scores| < 2^30, so every difference below fits int32.  The running max is
         // chained from the quad prefix; a record is an entry whose score beats it.
         const int mult16 = mult * 16;
@@ -190,7 +248,7 @@ __device__ __forceinline__ void tile_softmax(const int (&sacc)[4][4], int kb, in
             bool valid = true;
             if (MASKED) valid = kb + 8 * t + i <= prow && prow < n;
             sc[i] = valid ? score_from_dot<true>(sacc[i >> 1][i & 1], mult) : INT32_MIN;
-            L[i] = i ? max(L[i - 1], sc[i]) : sc[i];
+            L[i] = i ? max(L[i - 1], sc[i]) : sc[i];   // MODE 2
         }
         // exclusive prefix max over the quad: three independent shuffles
         const int x = L[7];
@@ -272,7 +330,7 @@ __device__ __forceinline__ void decode_tile_async(uint8_t *stage, const int8_t *
 // each warp copies its task's 32-key tiles (K rows, then the V tile: 4 KB) into a
 // two-stage shared-memory ring with cp.async, the next tile's copy overlapping the
 // current tile's work; the fragments then come from the tile as in the decode kernel.
-template <bool WIDE, bool EXP0, bool STREAM>
+template <int MODE, bool EXP0, bool STREAM>
 __global__ void __launch_bounds__(AM_THREADS, 1)
 k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restrict__ kv_g,
                 const int *__restrict__ chunk_row0, const int *__restrict__ chunk_len, int n_heads,
@@ -335,6 +393,8 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
         const int p_last = min(p0 + AM_ROWS - 1, n - 1);
         const bool full_rows = p0 + AM_ROWS - 1 < n;
         const int mult = score_mult[h];
+        const float mf = __int2float_rn(mult) * (1.0f / 32768.0f);   // exact (MODE 0)
+        const float c2 = __int2float_rn(384 * (32768 - mult));        // M1 - M1 * mf, exact (MODE 0)
 
         // Q fragment of row g with RoPE (attention.rs:53-83); pairs (i, i+32) live in kk = 0 / 1
         uint32_t qa[2][4];
@@ -378,6 +438,7 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
                 mma_s8s8(accs, qa[kk], b0, b1);   // every B column is the sink key
             }
             m = score_from_dot<true>(accs[0], mult);
+            if (MODE == 0) m = (int)(kM1Bits + (uint32_t)m);   // biased like the FP32 scores
             s_state[0] = s_state[1] = 65535u;
         }
         int hiacc[4][4], loacc[4][4];
@@ -404,7 +465,7 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
             int sacc[4][4];
 #pragma unroll
             for (int j = 0; j < 4; j++) {
-                sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0;
+                sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = MODE == 0 ? (int)kM1Bits : 0;
                 const uint4 kw = *reinterpret_cast<const uint4 *>(kst + perm_key(8 * j + g) * 64 + 16 * t);
                 mma_s8s8(sacc[j], qa[0], kw.x, kw.y);
                 mma_s8s8(sacc[j], qa[1], kw.z, kw.w);
@@ -435,9 +496,9 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
 
             Tile T;
             if (!full_rows || kb + 31 > p0)
-                tile_softmax<true, WIDE, EXP0>(sacc, kb, prow, n, mult, t, m, lut4k, c8, T);
+                tile_softmax<true, MODE, EXP0>(sacc, kb, prow, n, mult, mf, c2, t, m, lut4k, c8, T);
             else
-                tile_softmax<false, WIDE, EXP0>(sacc, kb, prow, n, mult, t, m, lut4k, c8, T);
+                tile_softmax<false, MODE, EXP0>(sacc, kb, prow, n, mult, mf, c2, t, m, lut4k, c8, T);
             // P^T B fragments (u8 halves of the weights): word q = entries 4q..4q+3
             uint32_t phi[2], plo[2];
 #pragma unroll
@@ -476,9 +537,9 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
                     if (rem[e] != 0u) {
                         const int key = __ffs(rem[e]) - 1;
                         rem[e] &= rem[e] - 1u;
-                        // saturated (WIDE) scores can wrap the difference to >= 0, where exp gives 65535
+                        // saturated (MODE 2) scores can wrap the difference to >= 0, where exp gives 65535
                         const int rd = (int)rec_e[(2 * t + e) * 32 + key];
-                        const uint32_t ef = WIDE ? exp_attn(rd, lut4k, c8) : exp_rec(rd, lut4k, c8);
+                        const uint32_t ef = MODE == 2 ? exp_attn(rd, lut4k, c8) : exp_rec(rd, lut4k, c8);
                         const uint32_t e16 = ef << 16, e16p1 = e16 + 1u;
                         const uint32_t sa = 256u * (uint32_t)shs[e] + (uint32_t)sls[e];
                         // s + sa >= 0: R(s + sa) is the high word alone
@@ -544,7 +605,7 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
 constexpr int DEC_STAGES = 2;
 constexpr int DEC_SMEM = AM_WARPS * DEC_STAGES * 4096 + AM_LUT * 2;
 
-template <bool WIDE, bool EXP0>
+template <int MODE, bool EXP0>
 __global__ void __launch_bounds__(AM_THREADS, 1)
 k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restrict__ kvc, size_t cache_ld,
                        int M, int p, int n_heads, const int32_t *__restrict__ score_mult,
@@ -572,6 +633,8 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__
     const uint32_t ones[4] = {0x01010101u, 0x01010101u, 0x01010101u, 0x01010101u};
     const bool head = g < n_heads;   // row g of the tile is head g
     const int mult = head ? score_mult[g] : 0;
+    const float mf = __int2float_rn(mult) * (1.0f / 32768.0f);
+    const float c2 = __int2float_rn(384 * (32768 - mult));
     const int ntiles = (p >> 5) + 1;
 
     // the tile sequence (stream fr, tile fk), its next copy going to stage fslot;
@@ -631,6 +694,7 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__
             mma_s8s8(accs, qa[kk], b0, b1);
         }
         m = score_from_dot<true>(accs[0], mult);
+        if (MODE == 0) m = (int)(kM1Bits + (uint32_t)m);
         s_state[0] = s_state[1] = 65535ull;
     }
     int hiacc[4][4], loacc[4][4];
@@ -650,7 +714,7 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__
         int sacc[4][4];
 #pragma unroll
         for (int j = 0; j < 4; j++) {
-            sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0;
+            sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = MODE == 0 ? (int)kM1Bits : 0;
             const uint4 kw = *reinterpret_cast<const uint4 *>(kst + perm_key(8 * j + g) * 64 + 16 * t);
             mma_s8s8(sacc[j], qa[0], kw.x, kw.y);
             mma_s8s8(sacc[j], qa[1], kw.z, kw.w);
@@ -668,9 +732,9 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__
         __syncwarp();   // every lane has its fragments: the stage may be refilled next iteration
         Tile T;
         if (kb + 31 > p)
-            tile_softmax<true, WIDE, EXP0>(sacc, kb, p, p + 1, mult, t, m, lut4k, c8, T);
+            tile_softmax<true, MODE, EXP0>(sacc, kb, p, p + 1, mult, mf, c2, t, m, lut4k, c8, T);
         else
-            tile_softmax<false, WIDE, EXP0>(sacc, kb, p, p + 1, mult, t, m, lut4k, c8, T);
+            tile_softmax<false, MODE, EXP0>(sacc, kb, p, p + 1, mult, mf, c2, t, m, lut4k, c8, T);
         uint32_t phi[2], plo[2];
 #pragma unroll
         for (int q = 0; q < 2; q++) {
@@ -693,9 +757,9 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__
                     if (rem[e] != 0u) {
                         const int key = __ffs(rem[e]) - 1;
                         rem[e] &= rem[e] - 1u;
-                        // saturated (WIDE) scores can wrap the difference to >= 0, where exp gives 65535
+                        // saturated (MODE 2) scores can wrap the difference to >= 0, where exp gives 65535
                         const int rd = (int)rec_e[(2 * t + e) * 32 + key];
-                        const uint32_t ef = WIDE ? exp_attn(rd, lut4k, c8) : exp_rec(rd, lut4k, c8);
+                        const uint32_t ef = MODE == 2 ? exp_attn(rd, lut4k, c8) : exp_rec(rd, lut4k, c8);
                         const uint32_t e16 = ef << 16, e16p1 = e16 + 1u;
                         const unsigned long long sa = 256ull * (uint32_t)shs[e] + (unsigned long long)(uint32_t)sls[e];
                         s_state[e] = (((s_state[e] + sa) * ef + 0x8000ull) >> 16) - sa;
@@ -766,38 +830,55 @@ bool attention_mma_fits(int max_len) { return max_len <= AM_MAX_KEYS; }
 constexpr int AM_STREAM_SMEM = AM_WARPS * AM_WARP_SMEM + AM_LUT * 2 + AM_WARPS * 8192;
 
 void attention_mma_init() {
-    cudaFuncSetAttribute(k_attention_decode_mma<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM);
-    cudaFuncSetAttribute(k_attention_decode_mma<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM);
-    cudaFuncSetAttribute(k_attention_decode_mma<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM);
+    cudaFuncSetAttribute(k_attention_decode_mma<1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM);
+    cudaFuncSetAttribute(k_attention_decode_mma<1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM);
+    cudaFuncSetAttribute(k_attention_decode_mma<0, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM);
+    cudaFuncSetAttribute(k_attention_decode_mma<0, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM);
+    cudaFuncSetAttribute(k_attention_decode_mma<2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM);
     const int smem = (int)attention_mma_smem(AM_MAX_KEYS);
-    cudaFuncSetAttribute(k_attention_mma<false, false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    cudaFuncSetAttribute(k_attention_mma<false, true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    cudaFuncSetAttribute(k_attention_mma<true, false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    cudaFuncSetAttribute(k_attention_mma<false, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(k_attention_mma<1, false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(k_attention_mma<1, true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(k_attention_mma<1, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          AM_STREAM_SMEM);
-    cudaFuncSetAttribute(k_attention_mma<false, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(k_attention_mma<1, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          AM_STREAM_SMEM);
-    cudaFuncSetAttribute(k_attention_mma<true, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(k_attention_mma<0, false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(k_attention_mma<0, true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(k_attention_mma<2, false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(k_attention_mma<0, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         AM_STREAM_SMEM);
+    cudaFuncSetAttribute(k_attention_mma<0, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         AM_STREAM_SMEM);
+    cudaFuncSetAttribute(k_attention_mma<2, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          AM_STREAM_SMEM);
 }
 
 void launch_attention_mma(const int8_t *qkv, int ldq, const int8_t *kv, const int *chunk_row0,
                           const int *chunk_len, int n_chunks, int max_len, int n_heads,
                           const int32_t *score_mult, const int8_t *sink_key, const int16_t *rope_cos,
-                          const int16_t *rope_sin, const uint16_t *lut4k, bool wide_mult, bool exp0, int8_t *out,
+                          const int16_t *rope_sin, const uint16_t *lut4k, int score_mode, bool exp0, int8_t *out,
                           int ldo, cudaStream_t st) {
     if (n_chunks == 0) return;
     const size_t smem = attention_mma_smem(max_len);
-    if (wide_mult)
-        k_attention_mma<true, false, false><<<n_chunks, AM_THREADS, smem, st>>>(
+    if (score_mode == 1) {
+        if (exp0)
+            k_attention_mma<1, true, false><<<n_chunks, AM_THREADS, smem, st>>>(
+                qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
+                lut4k, out, ldo, nullptr);
+        else
+            k_attention_mma<1, false, false><<<n_chunks, AM_THREADS, smem, st>>>(
+                qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
+                lut4k, out, ldo, nullptr);
+    } else if (score_mode == 2)
+        k_attention_mma<2, false, false><<<n_chunks, AM_THREADS, smem, st>>>(
             qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
             lut4k, out, ldo, nullptr);
     else if (exp0)
-        k_attention_mma<false, true, false><<<n_chunks, AM_THREADS, smem, st>>>(
+        k_attention_mma<0, true, false><<<n_chunks, AM_THREADS, smem, st>>>(
             qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
             lut4k, out, ldo, nullptr);
     else
-        k_attention_mma<false, false, false><<<n_chunks, AM_THREADS, smem, st>>>(
+        k_attention_mma<0, false, false><<<n_chunks, AM_THREADS, smem, st>>>(
             qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
             lut4k, out, ldo, nullptr);
 }
@@ -805,19 +886,28 @@ void launch_attention_mma(const int8_t *qkv, int ldq, const int8_t *kv, const in
 void launch_attention_mma_stream(const int8_t *qkv, int ldq, const int8_t *kv, const int *chunk_row0,
                                  const int *chunk_len, const int *chunk_kvoff, int n_chunks, int n_heads,
                                  const int32_t *score_mult, const int8_t *sink_key, const int16_t *rope_cos,
-                                 const int16_t *rope_sin, const uint16_t *lut4k, bool wide_mult, bool exp0,
+                                 const int16_t *rope_sin, const uint16_t *lut4k, int score_mode, bool exp0,
                                  int8_t *out, int ldo, cudaStream_t st) {
     if (n_chunks == 0) return;
-    if (wide_mult)
-        k_attention_mma<true, false, true><<<n_chunks, AM_THREADS, AM_STREAM_SMEM, st>>>(
+    if (score_mode == 1) {
+        if (exp0)
+            k_attention_mma<1, true, true><<<n_chunks, AM_THREADS, AM_STREAM_SMEM, st>>>(
+                qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
+                lut4k, out, ldo, chunk_kvoff);
+        else
+            k_attention_mma<1, false, true><<<n_chunks, AM_THREADS, AM_STREAM_SMEM, st>>>(
+                qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
+                lut4k, out, ldo, chunk_kvoff);
+    } else if (score_mode == 2)
+        k_attention_mma<2, false, true><<<n_chunks, AM_THREADS, AM_STREAM_SMEM, st>>>(
             qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
             lut4k, out, ldo, chunk_kvoff);
     else if (exp0)
-        k_attention_mma<false, true, true><<<n_chunks, AM_THREADS, AM_STREAM_SMEM, st>>>(
+        k_attention_mma<0, true, true><<<n_chunks, AM_THREADS, AM_STREAM_SMEM, st>>>(
             qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
             lut4k, out, ldo, chunk_kvoff);
     else
-        k_attention_mma<false, false, true><<<n_chunks, AM_THREADS, AM_STREAM_SMEM, st>>>(
+        k_attention_mma<0, false, true><<<n_chunks, AM_THREADS, AM_STREAM_SMEM, st>>>(
             qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
             lut4k, out, ldo, chunk_kvoff);
 }
@@ -827,17 +917,24 @@ bool attention_decode_mma_ok(int n_heads) { return n_heads >= 1 && n_heads <= AM
 void launch_attention_decode_mma(const int8_t *qkv, int ldq, const int8_t *kvc, size_t cache_ld, int M, int p,
                                  int n_heads, const int32_t *score_mult, const int8_t *sink_key,
                                  const int16_t *rope_cos, const int16_t *rope_sin, const uint16_t *lut4k,
-                                 bool wide_mult, bool exp0, int8_t *out, int ldo, cudaStream_t st) {
+                                 int score_mode, bool exp0, int8_t *out, int ldo, cudaStream_t st) {
     if (M == 0) return;
     const unsigned grid = (unsigned)std::min<long>((M + AM_WARPS - 1) / AM_WARPS, (long)sm_count());
-    if (wide_mult)
-        launch_k(k_attention_decode_mma<true, false>, grid, AM_THREADS, DEC_SMEM, st, qkv, ldq, kvc, cache_ld, M, p,
+    if (score_mode == 1) {
+        if (exp0)
+            launch_k(k_attention_decode_mma<1, true>, grid, AM_THREADS, DEC_SMEM, st, qkv, ldq, kvc, cache_ld, M, p,
+                     n_heads, score_mult, sink_key, rope_cos, rope_sin, lut4k, out, ldo);
+        else
+            launch_k(k_attention_decode_mma<1, false>, grid, AM_THREADS, DEC_SMEM, st, qkv, ldq, kvc, cache_ld, M, p,
+                     n_heads, score_mult, sink_key, rope_cos, rope_sin, lut4k, out, ldo);
+    } else if (score_mode == 2)
+        launch_k(k_attention_decode_mma<2, false>, grid, AM_THREADS, DEC_SMEM, st, qkv, ldq, kvc, cache_ld, M, p,
                  n_heads, score_mult, sink_key, rope_cos, rope_sin, lut4k, out, ldo);
     else if (exp0)
-        launch_k(k_attention_decode_mma<false, true>, grid, AM_THREADS, DEC_SMEM, st, qkv, ldq, kvc, cache_ld, M, p,
+        launch_k(k_attention_decode_mma<0, true>, grid, AM_THREADS, DEC_SMEM, st, qkv, ldq, kvc, cache_ld, M, p,
                  n_heads, score_mult, sink_key, rope_cos, rope_sin, lut4k, out, ldo);
     else
-        launch_k(k_attention_decode_mma<false, false>, grid, AM_THREADS, DEC_SMEM, st, qkv, ldq, kvc, cache_ld, M, p,
+        launch_k(k_attention_decode_mma<0, false>, grid, AM_THREADS, DEC_SMEM, st, qkv, ldq, kvc, cache_ld, M, p,
                  n_heads, score_mult, sink_key, rope_cos, rope_sin, lut4k, out, ldo);
 }
 

@@ -53,7 +53,9 @@ struct LayerDev {
     int8_t *qkv_w = nullptr, *out_w = nullptr, *up_w = nullptr, *down_w = nullptr;
     int32_t *score_mult = nullptr;
     int8_t *sink_key = nullptr;
-    bool wide_mult = false;   // some |score_mult| >= 2^27: the attention kernels take the general score path
+    // attention score arithmetic: 0 exact FP32 (every |score_mult| < 2^19), 1 32-bit
+    // integer (< 2^27), 2 64-bit with saturation (any)
+    int score_mode = 0;
     int qkv_mult = 1, out_mult = 1, up_mult = 1, down_mult = 1;
     int qkv_shift = 0, out_shift = 0, up_shift = 0, down_shift = 0;
     TcMatrix tm_qkv, tm_out, tm_up, tm_down;   // TMA descriptors of the weights
@@ -392,7 +394,8 @@ int load_model(czg_ctx *c, const uint8_t *bytes, size_t len) {
         for (int hh = 0; hh < H; hh++) {
             int32_t sm;
             memcpy(&sm, t->data + 4 * hh, 4);
-            if (sm >= (1 << 27) || sm <= -(1 << 27)) L.wide_mult = true;
+            const long long am = sm < 0 ? -(long long)sm : (long long)sm;
+            L.score_mode = std::max(L.score_mode, am >= (1ll << 27) ? 2 : (am >= (1ll << 19) ? 1 : 0));
         }
         if (const TensorRef *sk = find(f, p + "attn.sink_key")) {
             if (sk->dtype != "I8" || sk->numel() < 64 || sk->nbytes < 64)
@@ -588,11 +591,11 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
             if (staged)
                 launch_attention_mma(c->qkv, d + 128, c->kv, c->att_row0, c->att_len, nc, max_len, H,
                                      L.score_mult, L.sink_key, c->rope_cos, c->rope_sin, c->lut4k,
-                                     L.wide_mult, c->exp0, c->attn, d, st);
+                                     L.score_mode, c->exp0, c->attn, d, st);
             else if (stream)
                 launch_attention_mma_stream(c->qkv, d + 128, c->kv, c->att_row0, c->att_len, c->att_kvoff, nc, H,
                                             L.score_mult, L.sink_key, c->rope_cos, c->rope_sin, c->lut4k,
-                                            L.wide_mult, c->exp0, c->attn, d, st);
+                                            L.score_mode, c->exp0, c->attn, d, st);
             else
                 launch_attention(c->qkv, d + 128, c->kv, c->att_row0, c->att_len, nc, max_len, H,
                                  L.score_mult, L.sink_key, c->rope_cos, c->rope_sin, c->lut, c->attn, d, st);
@@ -903,7 +906,7 @@ int decompress_impl(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts
                 timed(c, kAttnDecode, [&] {
                     if (split)
                         launch_attention_decode_mma(c->qkv, d + 128, kvc, cache_ld, M, step, H, L.score_mult,
-                                                    L.sink_key, c->rope_cos, c->rope_sin, c->lut4k, L.wide_mult, c->exp0,
+                                                    L.sink_key, c->rope_cos, c->rope_sin, c->lut4k, L.score_mode, c->exp0,
                                                     c->attn, d, s);
                     else
                         launch_attention_decode(c->qkv, d + 128, kvc, cache_ld, M, step, H, L.score_mult, L.sink_key,

@@ -76,7 +76,8 @@ bool launch_gemm_tc(const TcMatrix &A, const TcMatrix &B, int M, int N, int K, i
 void attention_init();
 // attention_mma.cu: tensor-core version, K/V of a chunk staged in shared memory for
 // chunks of at most 1024 positions (launch_attention_mma_stream for longer ones);
-// lut4k = exp_q16 tabulated by t256 <= 4096 (entries from 4096 on are 1); exp0: lut4k[0] == 65535
+// lut4k = exp_q16 tabulated by t256 <= 4096 (entries from 4096 on are 1); exp0: lut4k[0] == 65535;
+// score_mode: 0 exact FP32 scores (all |score_mult| < 2^19), 1 32-bit (< 2^27), 2 64-bit saturating
 bool attention_mma_fits(int max_len);
 void attention_mma_init();
 // Tensor-core decode attention over the split KV layout: one warp per stream, the
@@ -86,18 +87,18 @@ bool attention_decode_mma_ok(int n_heads);
 void launch_attention_decode_mma(const int8_t *qkv, int ldq, const int8_t *kvc, size_t cache_ld, int M, int p,
                                  int n_heads, const int32_t *score_mult, const int8_t *sink_key,
                                  const int16_t *rope_cos, const int16_t *rope_sin, const uint16_t *lut4k,
-                                 bool wide_mult, bool exp0, int8_t *out, int ldo, cudaStream_t st);
+                                 int score_mode, bool exp0, int8_t *out, int ldo, cudaStream_t st);
 void launch_attention_mma(const int8_t *qkv, int ldq, const int8_t *kv, const int *chunk_row0,
                           const int *chunk_len, int n_chunks, int max_len, int n_heads,
                           const int32_t *score_mult, const int8_t *sink_key, const int16_t *rope_cos,
-                          const int16_t *rope_sin, const uint16_t *lut4k, bool wide_mult, bool exp0,
+                          const int16_t *rope_sin, const uint16_t *lut4k, int score_mode, bool exp0,
                           int8_t *out, int ldo, cudaStream_t st);
 // Chunks of any length: K and V in the streaming layout of launch_kv_prep_split,
 // chunk i of the launch at chunk_kvoff[i] * 128 bytes of kv
 void launch_attention_mma_stream(const int8_t *qkv, int ldq, const int8_t *kv, const int *chunk_row0,
                                  const int *chunk_len, const int *chunk_kvoff, int n_chunks, int n_heads,
                                  const int32_t *score_mult, const int8_t *sink_key, const int16_t *rope_cos,
-                                 const int16_t *rope_sin, const uint16_t *lut4k, bool wide_mult, bool exp0,
+                                 const int16_t *rope_sin, const uint16_t *lut4k, int score_mode, bool exp0,
                                  int8_t *out, int ldo, cudaStream_t st);
 // attention.cu: one CTA per chunk; rows of chunk c are chunk_row0[c] ..+chunk_len[c]
 void launch_attention(const int8_t *qkv, int ldq, const int8_t *kv, const int *chunk_row0,
