@@ -124,7 +124,6 @@ __device__ __forceinline__ int score_fast(int dot, int mult16) {
 // order like the scores.  The exp index t256 = floor((neg * 378194 + 2^23) / 2^24) of a
 // difference neg < 2^23 is fma(neg, 378194 / 2^24, M1) - M1 (no ties below 2^22; above
 // it the index is clamped at 4096 either way).  Checked exhaustively on the host.
-constexpr uint32_t kM1Bits = 0x4B400000u;   // 12582912.0f
 // dot_b: kM1Bits + dot (the QK accumulators start at kM1Bits in MODE 0)
 __device__ __forceinline__ int score_flt(int dot_b, float mf, float c2) {
     const float ub = __fmaf_rn(__int_as_float(dot_b), 0.25f, 9437184.0f);

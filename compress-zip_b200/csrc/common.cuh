@@ -17,6 +17,16 @@ constexpr int kHeadDim = 64;
 constexpr int kHalfDim = 32;
 constexpr uint32_t kBos = 1022u;   // rust/src/main.rs:214
 
+// Exact integer arithmetic on the FP32 pipes.  A float in [2^23, 2^24) has spacing 1,
+// and a fused multiply-add rounds its exact result once, to nearest with ties to even,
+// which is the reference's round-half-to-even shift (rust/src/primitives.rs:18-73).
+// With the bias M1 = 1.5 * 2^23 (bits kM1Bits), an integer |x| < 2^22 is the float
+// M1 + x, whose bits are kM1Bits + x, and fma(M1 + x, m, M1 - M1 * m) = M1 + rne(x * m)
+// whenever m and M1 - M1 * m are exact floats and |x * m| < 2^22.  The low byte of
+// the bits of M1 + y is y mod 256, so small results pack into int8 lanes directly.
+constexpr uint32_t kM1Bits = 0x4B400000u;   // 12582912.0f
+constexpr float kM1 = 12582912.0f;
+
 // SMs of the current device (cached per device): persistent grids are sized by it
 inline int sm_count() {
     static int cached[64] = {0};

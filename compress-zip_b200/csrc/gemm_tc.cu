@@ -25,6 +25,9 @@
 // Every mbarrier wait is bounded by a clock budget; on expiry the kernel sets
 // kErrTimeout in the error word, every role stops, and TMEM is freed.
 // No TMA load here uses cluster multicast.
+#include <cmath>
+#include <cstdlib>
+
 #include "kernels.h"
 #include "tc_common.cuh"
 
@@ -36,7 +39,12 @@ constexpr int TC_THREADS = 64 + 32 * TC_EPI_WARPS;
 constexpr int TC_STAGE_OUT = 32 * 64;   // one epilogue warp's staging box: 32 rows x 64 bytes
 
 // Requantisation clamp(round_half_even(acc * mult / 2^shift), +-127) of
-// model.rs:280-300 in three forms (mode):
+// model.rs:280-300 in four forms (mode):
+//  3: mode 2's clamp, then the product and its rounding in one FP32 fused
+//     multiply-add on the biased accumulator (common.cuh, kM1Bits): the result is
+//     the float M1 + requant, whose low byte is the int8 output (chosen when the
+//     clamp bound is below 2^22 and mult / 2^shift, M1 - M1 * mult / 2^shift are
+//     exact floats);
 //  2: |mult| < 2^(shift-1): A = the largest accumulator whose result is <= 127;
 //     clamp(acc, -A, A) * mult fits int32 and lands exactly on +-127 at the clamp
 //     (steps of the result are below 1/2), so no output clamp is needed;
@@ -45,7 +53,14 @@ constexpr int TC_STAGE_OUT = 32 * 64;   // one epilogue warp's staging box: 32 r
 //  0: the 64-bit form.
 struct Requant {
     int mult, shift, clamp_a, bias, mode;   // bias = 2^(shift-1) - 1
+    float mf, c2;                           // mode 3: mult / 2^shift, M1 - M1 * mult / 2^shift
 };
+
+// mode 3: bits of the float M1 + requant(acc)
+__device__ __forceinline__ uint32_t rq_flt(int acc, const Requant &q) {
+    const int a = min(max(acc, -q.clamp_a), q.clamp_a);
+    return __float_as_uint(__fmaf_rn(__int_as_float((int)(kM1Bits + (uint32_t)a)), q.mf, q.c2));
+}
 
 template <int RQ>
 __device__ __forceinline__ int rq(int acc, const Requant &q) {
@@ -252,9 +267,14 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                         if (EPI == kEpiRequant) {   // 32 bytes: chunks 2gi, 2gi+1
                             uint32_t w[8];
 #pragma unroll
-                            for (int j = 0; j < 8; j++)
-                                w[j] = pack4(rq<RQ>((int)v[4 * j], rqp), rq<RQ>((int)v[4 * j + 1], rqp),
-                                             rq<RQ>((int)v[4 * j + 2], rqp), rq<RQ>((int)v[4 * j + 3], rqp));
+                            for (int j = 0; j < 8; j++) {
+                                if (RQ == 3)
+                                    w[j] = pack4(rq_flt((int)v[4 * j], rqp), rq_flt((int)v[4 * j + 1], rqp),
+                                                 rq_flt((int)v[4 * j + 2], rqp), rq_flt((int)v[4 * j + 3], rqp));
+                                else
+                                    w[j] = pack4(rq<RQ>((int)v[4 * j], rqp), rq<RQ>((int)v[4 * j + 1], rqp),
+                                                 rq<RQ>((int)v[4 * j + 2], rqp), rq<RQ>((int)v[4 * j + 3], rqp));
+                            }
 #pragma unroll
                             for (int hh = 0; hh < 2; hh++)
                                 *reinterpret_cast<uint4 *>(sb + (((2 * gi + hh) ^ sw) << 4)) =
@@ -263,9 +283,17 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                             int y[16];
 #pragma unroll
                             for (int j = 0; j < 16; j++) {
-                                const int gte = max(rq<RQ>((int)v[2 * j], rqp), 0);
-                                const int x = gte * rq<RQ>((int)v[2 * j + 1], rqp);   // |x| <= 127 * 127
-                                y[j] = (x + 63 + ((x >> 7) & 1)) >> 7;                  // |y| <= 126: no clamp
+                                if (RQ == 3) {   // y = M1 + rne(max(g, 0) * u / 128) in FP32, exact
+                                    const float gb = __uint_as_float(rq_flt((int)v[2 * j], rqp));
+                                    const float ub = __uint_as_float(rq_flt((int)v[2 * j + 1], rqp));
+                                    const float gate = fmaxf(__fsub_rn(gb, kM1), 0.0f);
+                                    const float u128 = __fmaf_rn(ub, 0.0078125f, -98304.0f);   // (ub - M1) / 128
+                                    y[j] = __float_as_int(__fmaf_rn(gate, u128, kM1));
+                                } else {
+                                    const int gte = max(rq<RQ>((int)v[2 * j], rqp), 0);
+                                    const int x = gte * rq<RQ>((int)v[2 * j + 1], rqp);   // |x| <= 127 * 127
+                                    y[j] = (x + 63 + ((x >> 7) & 1)) >> 7;                  // |y| <= 126: no clamp
+                                }
                             }
                             *reinterpret_cast<uint4 *>(sb + ((gi ^ sw) << 4)) =
                                 make_uint4(pack4(y[0], y[1], y[2], y[3]), pack4(y[4], y[5], y[6], y[7]),
@@ -313,7 +341,7 @@ bool make_out_map(CUtensorMap *map, void *base, uint64_t rows, uint64_t cols, ui
 }
 
 Requant make_requant(int mult, int shift) {
-    Requant q{mult, shift, 0, 0, 0};
+    Requant q{mult, shift, 0, 0, 0, 0.0f, 0.0f};
     if (shift >= 1 && shift <= 24 && mult != 0) {
         const long long am = mult < 0 ? -(long long)mult : (long long)mult;
         q.bias = (1 << (shift - 1)) - 1;
@@ -322,6 +350,14 @@ Requant make_requant(int mult, int shift) {
         if (am < (1ll << (shift - 1)) && a2 * am + (1ll << (shift - 1)) < (1ll << 31)) {
             q.clamp_a = (int)a2;
             q.mode = 2;
+            const double mfd = std::ldexp((double)mult, -shift);
+            const double c2d = 12582912.0 - 12582912.0 * mfd;
+            if (a2 < (1ll << 22) && (double)(float)mfd == mfd && (double)(float)c2d == c2d &&
+                std::getenv("CZG_INT_REQUANT") == nullptr) {
+                q.mf = (float)mfd;
+                q.c2 = (float)c2d;
+                q.mode = 3;
+            }
         } else if (a1 * am + (1ll << (shift - 1)) < (1ll << 31)) {
             q.clamp_a = (int)a1;
             q.mode = 1;
@@ -343,7 +379,9 @@ bool launch_tc(const TcMatrix &A, const TcMatrix &B, int M, int N, int K, int mu
     const CUtensorMap &ma = *reinterpret_cast<const CUtensorMap *>(A.map);
     const CUtensorMap &mb = *reinterpret_cast<const CUtensorMap *>(B.map);
     constexpr int S = TcCfg<BN>::kStages;
-    if (EPI == kEpiInt32 || q.mode == 2)
+    if (EPI != kEpiInt32 && q.mode == 3)
+        launch_k(k_gemm_tc<BN, S, EPI, 3>, grid, TC_THREADS, TcCfg<BN>::kSmem, st, ma, mb, omap, M, N, K, q, err);
+    else if (EPI == kEpiInt32 || q.mode == 2)
         launch_k(k_gemm_tc<BN, S, EPI, 2>, grid, TC_THREADS, TcCfg<BN>::kSmem, st, ma, mb, omap, M, N, K, q, err);
     else if (q.mode == 1)
         launch_k(k_gemm_tc<BN, S, EPI, 1>, grid, TC_THREADS, TcCfg<BN>::kSmem, st, ma, mb, omap, M, N, K, q, err);
@@ -354,6 +392,8 @@ bool launch_tc(const TcMatrix &A, const TcMatrix &B, int M, int N, int K, int mu
 
 template <int BN, int EPI>
 void set_attr_epi() {
+    cudaFuncSetAttribute(k_gemm_tc<BN, TcCfg<BN>::kStages, EPI, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)TcCfg<BN>::kSmem);
     cudaFuncSetAttribute(k_gemm_tc<BN, TcCfg<BN>::kStages, EPI, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)TcCfg<BN>::kSmem);
     cudaFuncSetAttribute(k_gemm_tc<BN, TcCfg<BN>::kStages, EPI, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -331,7 +331,9 @@ def test_config4_long_chunks(tmp_path, shipped_path, oracle_mod, monkeypatch):
 @pytest.mark.parametrize("proj,mult,shift", [
     ("ffn.up", 819, 10),          # |mult| >= 2^(shift-1): clamped 32-bit requantisation
     ("ffn.down", 1 << 28, 30),    # product beyond 32 bits: 64-bit requantisation
-    ("attn.qkv", -3000, 16),      # negative multiplier
+    ("attn.qkv", -3000, 16),      # negative multiplier (FP32 form)
+    ("ffn.up", 1, 2),             # tiny multiplier: FP32 form, clamp bound 509
+    ("attn.out", (1 << 23) + 1, 30),   # M1 - M1 * mult / 2^shift not an exact float: 32-bit form
 ])
 def test_requant_forms(shipped_path, tmp_path, oracle_mod, shipped_tokens, proj, mult, shift):
     """Each requantisation form of the GEMM epilogue against the oracle."""
