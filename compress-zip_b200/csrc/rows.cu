@@ -7,6 +7,8 @@
 //
 // Reference: the residual stream and sandwich norms of rust/src/model.rs:362-480,
 // RMSNorm of rust/src/rmsnorm.rs:40-75.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -41,30 +43,46 @@ __global__ void k_inv_table(int eps, uint16_t *__restrict__ tab) {
     if (m < kInvTab) tab[m] = (uint16_t)inv_rms_q15((uint32_t)m, 1, eps);   // floor(m / 1) + eps
 }
 
-// Warp-level RMSNorm of one row held as D/128 words of 4 int8 per lane
-// (lane owns bytes [4*lane + 128*j, +4)).  rmsnorm.rs:40-75.  The sum of squares
-// uses dp4a (exact: at most 4 * 127^2 per call); round_even(t / 2^15) is
-// (t + 2^14 - 1 + ((t >> 15) & 1)) >> 15, exact for |t| <= 127 * 127 * 2^15.
-template <int NW>
-__device__ __forceinline__ void rmsnorm_words(const uint32_t (&x)[NW], const uint32_t (&w)[NW],
-                                              const uint16_t *__restrict__ inv_tab, uint32_t (&y)[NW]) {
-    constexpr int D = NW * 128;
-    int ss = 0;
+// RMSNorm of rmsnorm.rs:40-75, y = clamp(round_half_even(x * w * inv / 2^15), +-127)
+// with inv = inv_rms_q15 of the row (table by floor(sum_sq / d)), in exact FP32
+// (common.cuh, kM1Bits): IMAD gives the bits of M1 + x * w (|x * w| <= 127^2), and
+// fma(M1 + x * w, inv / 2^15, M1 - 384 inv) = M1 + rne(x * w * inv / 2^15), since
+// M1 * inv / 2^15 = 384 inv and inv / 2^15, M1 - 384 inv are exact floats; the clamp
+// is taken on the biased bits, whose low byte is the int8 result.
+struct NormRow {
+    float mf, c;   // inv / 2^15, M1 - 384 inv
+};
+__device__ __forceinline__ NormRow norm_row(int sum_sq, int D, const uint16_t *__restrict__ inv_tab) {
+    const int inv = __ldg(inv_tab + min((uint32_t)sum_sq / (uint32_t)D, (uint32_t)kInvTabEntries - 1u));
+    return NormRow{__int2float_rn(inv) * (1.0f / 32768.0f), __int2float_rn(12582912 - 384 * inv)};
+}
+// biased bits of the clamped norm output of x (an int8 value) with weight w
+__device__ __forceinline__ int norm_b(int x, int w, const NormRow &n) {
+    const float pb = __int_as_float(x * w + (int)kM1Bits);
+    const int yb = __float_as_int(__fmaf_rn(pb, n.mf, n.c));
+    return min(max(yb, (int)kM1Bits - 127), (int)kM1Bits + 127);
+}
+__device__ __forceinline__ int warp_sum(int v) {
 #pragma unroll
-    for (int j = 0; j < NW; j++) ss = __dp4a((int)x[j], (int)x[j], ss);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const int inv = __ldg(inv_tab + min((uint32_t)ss / (uint32_t)D, (uint32_t)kInvTab - 1u));
-#pragma unroll
-    for (int j = 0; j < NW; j++) {
-        int o4[4];
-#pragma unroll
-        for (int b = 0; b < 4; b++) {
-            const int t = (sext8(x[j], b) * sext8(w[j], b)) * inv;
-            o4[b] = clamp127((t + 0x3FFF + ((t >> 15) & 1)) >> 15);
-        }
-        y[j] = __byte_perm(__byte_perm(o4[0], o4[1], 0x0040), __byte_perm(o4[2], o4[3], 0x0040), 0x5410);
-    }
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+// the low bytes of four biased results as one word of int8
+__device__ __forceinline__ uint32_t pack_low4(int a, int b, int c, int d) {
+    return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+}
+// the four int8 of a word, sign-extended: prmt's default mode copies byte b into byte 0
+// (selector nibble b) and the sign of byte b into bytes 1..3 (nibbles 8 | b)
+__device__ __forceinline__ void unpack4(uint32_t w, int (&v)[4]) {
+    uint32_t r0, r1, r2, r3;
+    asm("prmt.b32 %0, %1, 0, 0x8880;" : "=r"(r0) : "r"(w));
+    asm("prmt.b32 %0, %1, 0, 0x9991;" : "=r"(r1) : "r"(w));
+    asm("prmt.b32 %0, %1, 0, 0xAAA2;" : "=r"(r2) : "r"(w));
+    asm("prmt.b32 %0, %1, 0, 0xBBB3;" : "=r"(r3) : "r"(w));
+    v[0] = (int)r0;
+    v[1] = (int)r1;
+    v[2] = (int)r2;
+    v[3] = (int)r3;
 }
 
 // four consecutive residual elements
@@ -80,6 +98,10 @@ __device__ __forceinline__ void store_res4(int16_t *p, int4 v) {
                                                ((uint32_t)v.z & 0xFFFFu) | ((uint32_t)v.w << 16));
 }
 
+// Persistent warps walk the rows (warp w takes rows w, w + W, ...), so each warp
+// unpacks its norm weights once.  A lane owns elements [4*lane + 128*j, +4).
+__device__ __forceinline__ int row_warps() { return (int)(gridDim.x * blockDim.x) >> 5; }
+
 // x_res[r] = embed[tok_in[r]] (residual), xn[r] = norm(clamp(x_res[r])).  STORE
 // false: the residual is not written (the first residual norm then reads the
 // embedding row again, which stays in L2, instead of x_res from HBM).
@@ -90,35 +112,32 @@ __global__ void k_embed_norm(const uint32_t *__restrict__ tok_in, const int8_t *
     pdl_wait();
     pdl_trigger();
     constexpr int D = NW * 128;
-    int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    int lane = threadIdx.x & 31;
-    if (warp >= M) return;
-    const uint32_t *e = reinterpret_cast<const uint32_t *>(embed + (size_t)tok_in[warp] * D);
+    const int lane = threadIdx.x & 31;
     const uint32_t *wv = reinterpret_cast<const uint32_t *>(norm_w);
-    uint32_t x[NW], w[NW], y[NW];
+    int w[NW][4];
 #pragma unroll
-    for (int j = 0; j < NW; j++) {
-        x[j] = __ldg(e + lane + 32 * j);
-        w[j] = __ldg(wv + lane + 32 * j);
-    }
-    if (STORE) {
-        RT *xr = x_res + (size_t)warp * D;
+    for (int j = 0; j < NW; j++) unpack4(__ldg(wv + lane + 32 * j), w[j]);
+    for (int row = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5); row < M; row += row_warps()) {
+        const uint32_t *e = reinterpret_cast<const uint32_t *>(embed + (size_t)tok_in[row] * D);
+        int x[NW][4];
+        int ss = 0;
+#pragma unroll
+        for (int j = 0; j < NW; j++) {
+            unpack4(__ldg(e + lane + 32 * j), x[j]);
+            if (STORE) store_res4(x_res + (size_t)row * D + 4 * (lane + 32 * j), make_int4(x[j][0], x[j][1], x[j][2], x[j][3]));
+#pragma unroll
+            for (int b = 0; b < 4; b++) {
+                x[j][b] = max(x[j][b], -127);   // clamp_i8 before the norm: -128 becomes -127
+                ss += x[j][b] * x[j][b];
+            }
+        }
+        const NormRow nr = norm_row(warp_sum(ss), D, inv_tab);
+        uint32_t *yo = reinterpret_cast<uint32_t *>(xn + (size_t)row * D);
 #pragma unroll
         for (int j = 0; j < NW; j++)
-            store_res4(xr + 4 * (lane + 32 * j),
-                       make_int4(sext8(x[j], 0), sext8(x[j], 1), sext8(x[j], 2), sext8(x[j], 3)));
+            yo[lane + 32 * j] = pack_low4(norm_b(x[j][0], w[j][0], nr), norm_b(x[j][1], w[j][1], nr),
+                                          norm_b(x[j][2], w[j][2], nr), norm_b(x[j][3], w[j][3], nr));
     }
-#pragma unroll
-    for (int j = 0; j < NW; j++) {   // clamp_i8 before the norm: -128 becomes -127
-        uint32_t c = 0;
-#pragma unroll
-        for (int b = 0; b < 4; b++) c |= (uint32_t)(uint8_t)clamp127(sext8(x[j], b)) << (8 * b);
-        x[j] = c;
-    }
-    rmsnorm_words<NW>(x, w, inv_tab, y);
-    uint32_t *yo = reinterpret_cast<uint32_t *>(xn + (size_t)warp * D);
-#pragma unroll
-    for (int j = 0; j < NW; j++) yo[lane + 32 * j] = y[j];
 }
 
 // o_n = norm(o, post_w); x_res += o_n (int32, never clamped: model.rs:432-434);
@@ -137,45 +156,63 @@ __global__ void k_residual_norm(const int8_t *__restrict__ o, const int8_t *__re
     pdl_wait();
     pdl_trigger();
     constexpr int D = NW * 128;
-    int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    int lane = threadIdx.x & 31;
-    if (warp >= M) return;
-    const uint32_t *ov = reinterpret_cast<const uint32_t *>(o + (size_t)warp * D);
+    const int lane = threadIdx.x & 31;
     const uint32_t *pw = reinterpret_cast<const uint32_t *>(post_w);
     const uint32_t *nw = reinterpret_cast<const uint32_t *>(next_w);
-    uint32_t x[NW], w[NW], y[NW], w2[NW];
-    RT *xr = x_res + (size_t)warp * D;
-    const uint32_t *er = MODE == kResFromEmbed ? reinterpret_cast<const uint32_t *>(embed + (size_t)tok_in[warp] * D)
-                                               : nullptr;
-    int4 rv[NW];
-#pragma unroll
-    for (int j = 0; j < NW; j++) {   // every load of the row first
-        x[j] = ov[lane + 32 * j];
-        w[j] = __ldg(pw + lane + 32 * j);
-        w2[j] = __ldg(nw + lane + 32 * j);
-        if (MODE == kResFromEmbed) {
-            const uint32_t ev = __ldg(er + lane + 32 * j);
-            rv[j] = make_int4(sext8(ev, 0), sext8(ev, 1), sext8(ev, 2), sext8(ev, 3));
-        } else {
-            rv[j] = load_res4(xr + 4 * (lane + 32 * j));
-        }
-    }
-    rmsnorm_words<NW>(x, w, inv_tab, y);
+    int w[NW][4], w2[NW][4];
 #pragma unroll
     for (int j = 0; j < NW; j++) {
-        int4 r = rv[j];
-        r.x = (int)((uint32_t)r.x + (uint32_t)sext8(y[j], 0));
-        r.y = (int)((uint32_t)r.y + (uint32_t)sext8(y[j], 1));
-        r.z = (int)((uint32_t)r.z + (uint32_t)sext8(y[j], 2));
-        r.w = (int)((uint32_t)r.w + (uint32_t)sext8(y[j], 3));
-        if (MODE != kResNoStore) store_res4(xr + 4 * (lane + 32 * j), r);
-        x[j] = (uint32_t)(uint8_t)clamp127(r.x) | ((uint32_t)(uint8_t)clamp127(r.y) << 8) |
-               ((uint32_t)(uint8_t)clamp127(r.z) << 16) | ((uint32_t)(uint8_t)clamp127(r.w) << 24);
+        unpack4(__ldg(pw + lane + 32 * j), w[j]);
+        unpack4(__ldg(nw + lane + 32 * j), w2[j]);
     }
-    rmsnorm_words<NW>(x, w2, inv_tab, y);
-    uint32_t *yo = reinterpret_cast<uint32_t *>(xn + (size_t)warp * D);
+    for (int row = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5); row < M; row += row_warps()) {
+        const uint32_t *ov = reinterpret_cast<const uint32_t *>(o + (size_t)row * D);
+        RT *xr = x_res + (size_t)row * D;
+        const uint32_t *er = MODE == kResFromEmbed ? reinterpret_cast<const uint32_t *>(embed + (size_t)tok_in[row] * D)
+                                                   : nullptr;
+        uint32_t x[NW];
+        int4 rv[NW];
+        int ss = 0;
 #pragma unroll
-    for (int j = 0; j < NW; j++) yo[lane + 32 * j] = y[j];
+        for (int j = 0; j < NW; j++) {   // every load of the row first
+            x[j] = ov[lane + 32 * j];
+            if (MODE == kResFromEmbed) {
+                int ev[4];
+                unpack4(__ldg(er + lane + 32 * j), ev);
+                rv[j] = make_int4(ev[0], ev[1], ev[2], ev[3]);
+            } else {
+                rv[j] = load_res4(xr + 4 * (lane + 32 * j));
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < NW; j++) ss = __dp4a((int)x[j], (int)x[j], ss);   // o is already clamped to +-127
+        const NormRow n1 = norm_row(warp_sum(ss), D, inv_tab);
+        int c[NW][4];
+        int ss2 = 0;
+#pragma unroll
+        for (int j = 0; j < NW; j++) {
+            int xo[4];
+            unpack4(x[j], xo);
+            int4 r = rv[j];
+            r.x = (int)((uint32_t)r.x + (uint32_t)norm_b(xo[0], w[j][0], n1) - kM1Bits);
+            r.y = (int)((uint32_t)r.y + (uint32_t)norm_b(xo[1], w[j][1], n1) - kM1Bits);
+            r.z = (int)((uint32_t)r.z + (uint32_t)norm_b(xo[2], w[j][2], n1) - kM1Bits);
+            r.w = (int)((uint32_t)r.w + (uint32_t)norm_b(xo[3], w[j][3], n1) - kM1Bits);
+            if (MODE != kResNoStore) store_res4(xr + 4 * (lane + 32 * j), r);
+            c[j][0] = clamp127(r.x);
+            c[j][1] = clamp127(r.y);
+            c[j][2] = clamp127(r.z);
+            c[j][3] = clamp127(r.w);
+#pragma unroll
+            for (int b = 0; b < 4; b++) ss2 += c[j][b] * c[j][b];
+        }
+        const NormRow n2 = norm_row(warp_sum(ss2), D, inv_tab);
+        uint32_t *yo = reinterpret_cast<uint32_t *>(xn + (size_t)row * D);
+#pragma unroll
+        for (int j = 0; j < NW; j++)
+            yo[lane + 32 * j] = pack_low4(norm_b(c[j][0], w2[j][0], n2), norm_b(c[j][1], w2[j][1], n2),
+                                          norm_b(c[j][2], w2[j][2], n2), norm_b(c[j][3], w2[j][3], n2));
+    }
 }
 
 // K rotated with RoPE at the row's position and V copied, into kv[row] =
@@ -236,10 +273,14 @@ void launch_rows(const uint32_t *tokens, const int *chunk_row0, const int *chunk
                                      tok_out, pos, rowchunk, err);
 }
 
+// row kernels: blocks of 8 warps, at most 8 blocks per SM resident at once (each warp
+// then walks rows with a stride of the whole grid)
+inline int row_blocks(int M) { return std::min((M + 7) / 8, 8 * sm_count()); }
+
 template <typename RT, bool STORE>
 void embed_norm_t(const uint32_t *tok_in, const int8_t *embed, const int8_t *norm_w, int M, int d, const uint16_t *inv_tab,
                   RT *x_res, int8_t *xn, cudaStream_t st) {
-    const int blocks = (M + 7) / 8;
+    const int blocks = row_blocks(M);
     switch (d / 128) {
         case 2: launch_k(k_embed_norm<2, RT, STORE>, blocks, 256, 0, st, tok_in, embed, norm_w, M, inv_tab, x_res, xn); break;
         case 3: launch_k(k_embed_norm<3, RT, STORE>, blocks, 256, 0, st, tok_in, embed, norm_w, M, inv_tab, x_res, xn); break;
@@ -251,7 +292,7 @@ void embed_norm_t(const uint32_t *tok_in, const int8_t *embed, const int8_t *nor
 template <typename RT, int MODE>
 void residual_norm_t(const int8_t *o, const int8_t *post_w, const int8_t *next_w, int M, int d, const uint16_t *inv_tab,
                      const uint32_t *tok_in, const int8_t *embed, RT *x_res, int8_t *xn, cudaStream_t st) {
-    const int blocks = (M + 7) / 8;
+    const int blocks = row_blocks(M);
     switch (d / 128) {
         case 2: launch_k(k_residual_norm<2, RT, MODE>, blocks, 256, 0, st, o, post_w, next_w, M, inv_tab, tok_in, embed, x_res, xn); break;
         case 3: launch_k(k_residual_norm<3, RT, MODE>, blocks, 256, 0, st, o, post_w, next_w, M, inv_tab, tok_in, embed, x_res, xn); break;
