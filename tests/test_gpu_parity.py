@@ -282,11 +282,13 @@ def test_cdf_edge_models(shipped_path, tmp_path, oracle_mod, shipped_tokens, mod
         eng.close()
 
 
-def test_int32_residual_path(shipped_path, shipped_oracle, oracle_mod, shipped_tokens, monkeypatch):
-    """The int32 residual stream (used for models deeper than 128 layers) on the shipped model."""
+@pytest.mark.parametrize("env", ["CZG_RESIDUAL32", "CZG_INT_REQUANT"])
+def test_int32_residual_path(shipped_path, shipped_oracle, oracle_mod, shipped_tokens, monkeypatch, env):
+    """The int32 residual stream (used for models deeper than 128 layers), and the
+    32-bit integer requantisation epilogue in place of the FP32 one, on the shipped model."""
     from compress_zip_b200.engine import Engine
 
-    monkeypatch.setenv("CZG_RESIDUAL32", "1")
+    monkeypatch.setenv(env, "1")
     eng = Engine.from_file(shipped_path, 0)
     try:
         _trace_equal(eng, shipped_oracle, oracle_mod, shipped_tokens[:300])
@@ -333,7 +335,8 @@ def test_config4_long_chunks(tmp_path, shipped_path, oracle_mod, monkeypatch):
     ("ffn.down", 1 << 28, 30),    # product beyond 32 bits: 64-bit requantisation
     ("attn.qkv", -3000, 16),      # negative multiplier (FP32 form)
     ("ffn.up", 1, 2),             # tiny multiplier: FP32 form, clamp bound 509
-    ("attn.out", (1 << 23) + 1, 30),   # M1 - M1 * mult / 2^shift not an exact float: 32-bit form
+    ("attn.out", (1 << 22) + 1, 24),   # M1 - M1 * mult / 2^shift not an exact float: 32-bit clamped form
+    ("attn.out", (1 << 23) + 1, 30),   # clamp bound * mult beyond 32 bits: 64-bit form
 ])
 def test_requant_forms(shipped_path, tmp_path, oracle_mod, shipped_tokens, proj, mult, shift):
     """Each requantisation form of the GEMM epilogue against the oracle."""
