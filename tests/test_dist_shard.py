@@ -25,7 +25,7 @@ def _rank(rank, world, port, q):
 
     seeds = list(bench.shard_seeds(rank, 2))
     mf = bench.czm.ModelFile.load(os.path.join(ROOT, "models", "v001_eng.czm"))
-    tokens, starts, nbytes = bench.workload(mf, seeds, 64)
+    tokens, starts, nbytes, _ = bench.workload(mf, seeds, 64)
     om = O.load_model(os.path.join(ROOT, "models", "v001_eng.czm"))
     chunks = O.compress_chunks(om, tokens[:400], starts[starts <= 400], nthreads=2)
     tmax, nsum = bench.reduce_over_ranks([1.0 + rank], [float(len(tokens))], "cpu")
@@ -57,5 +57,5 @@ def test_two_rank_sharding():
     mf = bench.czm.ModelFile.load(os.path.join(ROOT, "models", "v001_eng.czm"))
     om = O.load_model(os.path.join(ROOT, "models", "v001_eng.czm"))
     for seeds, chunks in (([1, 2], c0), ([3, 4], c1)):
-        tokens, starts, _ = bench.workload(mf, seeds, 64)
+        tokens, starts, _, _ = bench.workload(mf, seeds, 64)
         assert chunks == O.compress_chunks(om, tokens[:400], starts[starts <= 400], nthreads=4)
