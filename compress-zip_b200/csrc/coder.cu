@@ -321,6 +321,45 @@ k_encode(const uint2 *__restrict__ lohi, const int *__restrict__ chunk_row0,
     if (bs.overflow) atomicOr(err, kErrOverflow);
 }
 
+// Exclusive scan of the encoded chunk lengths into packed offsets (pack_off[0..n)),
+// the total at pack_off[n]; one CTA of 1024 threads walking the chunks 1024 at a time.
+__global__ void __launch_bounds__(1024) k_pack_offsets(const uint32_t *__restrict__ lens, int n,
+                                                       uint64_t *__restrict__ pack_off) {
+    __shared__ uint64_t wsum[32];
+    __shared__ uint64_t carry;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (threadIdx.x == 0) carry = 0;
+    __syncthreads();
+    for (int b = 0; b < n; b += 1024) {
+        const int i = b + (int)threadIdx.x;
+        const uint64_t v = i < n ? lens[i] : 0;
+        uint64_t x = v;   // inclusive scan in the warp
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint64_t y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        if (lane == 31) wsum[warp] = x;
+        __syncthreads();
+        if (warp == 0) {   // scan of the warp totals
+            uint64_t w = wsum[lane];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint64_t y = __shfl_up_sync(0xffffffffu, w, o);
+                if (lane >= o) w += y;
+            }
+            wsum[lane] = w;
+        }
+        __syncthreads();
+        const uint64_t before = carry + (warp ? wsum[warp - 1] : 0);
+        if (i < n) pack_off[i] = before + x - v;
+        __syncthreads();
+        if (threadIdx.x == 0) carry += wsum[31];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) pack_off[n] = carry;
+}
+
 // one CTA per chunk: slot bytes -> packed position
 __global__ void k_pack(const uint8_t *__restrict__ slots, const uint64_t *__restrict__ slot_off,
                        const uint32_t *__restrict__ lens, const uint64_t *__restrict__ pack_off,
@@ -364,6 +403,10 @@ void launch_encode(const uint2 *lohi, const int *chunk_row0, const int *chunk_le
     unsigned long long inv = 0xFFFFFFFFFFFFFFFFull / total;
     k_encode<<<(n_chunks + ENC_THREADS - 1) / ENC_THREADS, ENC_THREADS, 0, st>>>(
         lohi, chunk_row0, chunk_len, n_chunks, total, inv, slots, slot_off, lens, err);
+}
+
+void launch_pack_offsets(const uint32_t *lens, int n_chunks, uint64_t *pack_off, cudaStream_t st) {
+    k_pack_offsets<<<1, 1024, 0, st>>>(lens, n_chunks, pack_off);
 }
 
 void launch_pack(const uint8_t *slots, const uint64_t *slot_off, const uint32_t *lens,

@@ -118,10 +118,20 @@ struct czg_ctx {
     uint64_t *d_off = nullptr, *d_len = nullptr, *d_tokoff = nullptr;
     uint32_t *d_outtok = nullptr;
     std::vector<void *> dec_allocs;
-    // pinned host staging
-    uint8_t *h_meta = nullptr;
+    // pinned host staging: chunk tables of the wave being launched (two, so a wave's
+    // tables can be written while the previous wave's copies are still queued), and
+    // per wave parity the error word, packed total and chunk lengths copied back
+    uint8_t *h_meta = nullptr, *h_meta2 = nullptr, *h_meta_cur = nullptr;
+    uint8_t *h_small[2] = {nullptr, nullptr};
     std::vector<int> att_order;
     size_t h_meta_bytes = 0;
+    // copy-out pipeline of compress calls: a second token buffer and packed buffer,
+    // a stream for the copies and the events that order them with the compute stream
+    uint32_t *tokens2 = nullptr;
+    uint8_t *packed2 = nullptr;
+    cudaStream_t copy_stream = nullptr;
+    cudaEvent_t ev_h2d[2] = {nullptr, nullptr}, ev_comp[2] = {nullptr, nullptr};
+    cudaEvent_t ev_small[2] = {nullptr, nullptr}, ev_d2h[2] = {nullptr, nullptr};
 
     // statistics
     czg_stats stats{};
@@ -429,8 +439,11 @@ int alloc_workspace(czg_ctx *c, int rows, int chunks) {
     if (c->stream) cudaStreamSynchronize(c->stream);
     for (void *p : c->ws_allocs) cudaFree(p);
     c->ws_allocs.clear();
-    if (c->h_meta) cudaFreeHost(c->h_meta);
-    c->h_meta = nullptr;
+    if (c->copy_stream) cudaStreamSynchronize(c->copy_stream);
+    for (uint8_t **h : {&c->h_meta, &c->h_meta2, &c->h_small[0], &c->h_small[1]}) {
+        if (*h) cudaFreeHost(*h);
+        *h = nullptr;
+    }
     c->cap_rows = c->cap_chunks = 0;
     size_t R = (size_t)(rows + 127) / 128 * 128 + 128;
     bool ok = dalloc_ws(c, &c->tokens, R) && dalloc_ws(c, &c->tok_in, R) && dalloc_ws(c, &c->tok_out, R) &&
@@ -441,6 +454,7 @@ int alloc_workspace(czg_ctx *c, int rows, int chunks) {
               dalloc_ws(c, &c->hbuf, R * c->dff_pad) && dalloc_ws(c, &c->logits, R * c->vpad) &&
               dalloc_ws(c, &c->lohi, R) && dalloc_ws(c, &c->slots, 4 * R + 8 * (size_t)chunks + 64) &&
               dalloc_ws(c, &c->packed, 4 * R + 8 * (size_t)chunks + 64) &&
+              dalloc_ws(c, &c->packed2, 4 * R + 8 * (size_t)chunks + 64) && dalloc_ws(c, &c->tokens2, R) &&
               dalloc_ws(c, &c->lens, (size_t)chunks) && dalloc_ws(c, &c->slot_off, (size_t)chunks + 1) &&
               dalloc_ws(c, &c->pack_off, (size_t)chunks + 1) && dalloc_ws(c, &c->chunk_tok0, (size_t)chunks) &&
               dalloc_ws(c, &c->chunk_row0, (size_t)chunks) && dalloc_ws(c, &c->chunk_len, (size_t)chunks) &&
@@ -469,7 +483,12 @@ int alloc_workspace(czg_ctx *c, int rows, int chunks) {
     c->head_cdf = !(hc && std::string(hc) == "0") && c->exp0 && c->logit_small &&
                   m.vocab_size == c->vpad && c->vpad % 256 == 0 && m.coef_q24 < (1u << 23) && d % 128 == 0;
     c->h_meta_bytes = (size_t)chunks * 48 + 64;
-    if (!cuda_ok(c, cudaMallocHost(&c->h_meta, c->h_meta_bytes), "cudaMallocHost")) return CZG_E_DEVICE;
+    if (!cuda_ok(c, cudaMallocHost(&c->h_meta, c->h_meta_bytes), "cudaMallocHost") ||
+        !cuda_ok(c, cudaMallocHost(&c->h_meta2, c->h_meta_bytes), "cudaMallocHost") ||
+        !cuda_ok(c, cudaMallocHost(&c->h_small[0], 16 + 4 * (size_t)chunks), "cudaMallocHost") ||
+        !cuda_ok(c, cudaMallocHost(&c->h_small[1], 16 + 4 * (size_t)chunks), "cudaMallocHost"))
+        return CZG_E_DEVICE;
+    c->h_meta_cur = c->h_meta;
     return CZG_OK;
 }
 
@@ -513,7 +532,7 @@ struct Trace {
 int wave_meta(czg_ctx *c, const uint64_t *starts, uint32_t c0, uint32_t c1) {
     const int nc = (int)(c1 - c0);
     cudaStream_t st = c->stream;
-    int *h_row0 = reinterpret_cast<int *>(c->h_meta);
+    int *h_row0 = reinterpret_cast<int *>(c->h_meta_cur);
     int *h_len = h_row0 + nc;
     uint64_t *h_tok0 = reinterpret_cast<uint64_t *>(h_len + nc + (nc & 1));
     uint64_t *h_slot = h_tok0 + nc;
@@ -705,7 +724,7 @@ int wave_copy_out(czg_ctx *c, uint32_t c0, int nc, uint8_t *out, uint64_t out_ca
     if (err & kErrToken) return fail(c, CZG_E_TOKEN, "token id >= vocab_size");
     if (err & kErrOverflow) return fail(c, CZG_E_DEVICE, "encoder slot overflow");
     if (err & kErrTimeout) return fail(c, CZG_E_TIMEOUT, "a bounded device wait expired");
-    uint64_t *h_pack = reinterpret_cast<uint64_t *>(c->h_meta);
+    uint64_t *h_pack = reinterpret_cast<uint64_t *>(c->h_meta_cur);
     h_pack[0] = 0;
     for (int i = 0; i < nc; i++) h_pack[i + 1] = h_pack[i] + out_lens[c0 + i];
     const uint64_t wave_bytes = h_pack[nc];
@@ -748,26 +767,87 @@ int compress_impl(czg_ctx *c, const uint32_t *tokens, bool device_tokens, const 
     stats_begin(c);
     c->stats.n_tokens = ntok;
     c->stats.n_chunks = n_chunks;
+    if (int st = ensure_workspace(c, ntok)) return st;
+    // Waves are pipelined: wave i's tokens go up on the copy stream into buffer i % 2
+    // while wave i-1 computes; its chunks are packed on the device (offsets by a scan)
+    // into packed buffer i % 2, and only its lengths, total and error word come back
+    // before the host launches wave i+1 -- the packed bytes of wave i follow on the
+    // copy stream while wave i+1 computes.
+    const std::vector<WavePlan> waves = plan_waves(c, starts, n_chunks);
     uint64_t total = 0;
     int status = CZG_OK;
-    if (int st = ensure_workspace(c, ntok)) return st;
-    for (const WavePlan &w : plan_waves(c, starts, n_chunks)) {
+    auto enqueue = [&](const WavePlan &w, int b) -> int {
         const uint64_t t0 = starts[w.c0], nt = starts[w.c1] - t0;
-        const uint32_t *d_tok;
-        if (device_tokens) {
-            d_tok = tokens + t0;
-        } else {
+        const int nc = (int)(w.c1 - w.c0);
+        const uint32_t *d_tok = tokens + t0;
+        if (!device_tokens) {
+            uint32_t *buf = b ? c->tokens2 : c->tokens;
+            cudaStreamWaitEvent(c->copy_stream, c->ev_comp[b], 0);   // wave i-2 has read the buffer
             EvPair &e = next_ev(c, -1);
-            cudaEventRecord(e.a, c->stream);
-            cudaMemcpyAsync(c->tokens, tokens + t0, nt * 4, cudaMemcpyHostToDevice, c->stream);
-            cudaEventRecord(e.b, c->stream);
+            cudaEventRecord(e.a, c->copy_stream);
+            cudaMemcpyAsync(buf, tokens + t0, nt * 4, cudaMemcpyHostToDevice, c->copy_stream);
+            cudaEventRecord(e.b, c->copy_stream);
+            cudaEventRecord(c->ev_h2d[b], c->copy_stream);
+            cudaStreamWaitEvent(c->stream, c->ev_h2d[b], 0);
             c->stats.h2d_bytes += nt * 4;
-            d_tok = c->tokens;
+            d_tok = buf;
         }
-        int st = run_wave(c, d_tok, starts, w.c0, w.c1, nullptr);
-        if (st) return st;
-        if ((st = wave_copy_out(c, w.c0, (int)(w.c1 - w.c0), out, out_cap, out_lens, total, status))) return st;
+        c->h_meta_cur = b ? c->h_meta2 : c->h_meta;
+        if (int st = run_wave(c, d_tok, starts, w.c0, w.c1, nullptr)) return st;
+        uint8_t *packed = b ? c->packed2 : c->packed;
+        launch_pack_offsets(c->lens, nc, c->pack_off, c->stream);
+        cudaStreamWaitEvent(c->stream, c->ev_d2h[b], 0);   // wave i-2's bytes have left the buffer
+        timed(c, kPack, [&] { launch_pack(c->slots, c->slot_off, c->lens, c->pack_off, nc, packed, c->stream); });
+        uint8_t *hs = c->h_small[b];
+        cudaMemcpyAsync(hs, c->err_flag, sizeof(int), cudaMemcpyDeviceToHost, c->stream);
+        cudaMemcpyAsync(hs + 8, c->pack_off + nc, sizeof(uint64_t), cudaMemcpyDeviceToHost, c->stream);
+        cudaMemcpyAsync(hs + 16, c->lens, sizeof(uint32_t) * nc, cudaMemcpyDeviceToHost, c->stream);
+        cudaEventRecord(c->ev_small[b], c->stream);
+        cudaEventRecord(c->ev_comp[b], c->stream);
+        if (!cuda_ok(c, cudaGetLastError(), "wave launch")) return CZG_E_DEVICE;
+        return CZG_OK;
+    };
+    auto finish = [&](const WavePlan &w, int b) -> int {
+        const int nc = (int)(w.c1 - w.c0);
+        if (!cuda_ok(c, cudaEventSynchronize(c->ev_small[b]), "wave")) return CZG_E_DEVICE;
+        const uint8_t *hs = c->h_small[b];
+        int err = 0;
+        uint64_t wave_bytes = 0;
+        memcpy(&err, hs, sizeof(int));
+        memcpy(&wave_bytes, hs + 8, sizeof(uint64_t));
+        memcpy(out_lens + w.c0, hs + 16, sizeof(uint32_t) * nc);
+        c->stats.d2h_bytes += 12 + sizeof(uint32_t) * (uint64_t)nc;
+        if (err & kErrToken) return fail(c, CZG_E_TOKEN, "token id >= vocab_size");
+        if (err & kErrOverflow) return fail(c, CZG_E_DEVICE, "encoder slot overflow");
+        if (err & kErrTimeout) return fail(c, CZG_E_TIMEOUT, "a bounded device wait expired");
+        if (total + wave_bytes <= out_cap) {
+            EvPair &e = next_ev(c, -2);
+            cudaEventRecord(e.a, c->copy_stream);
+            cudaMemcpyAsync(out + total, b ? c->packed2 : c->packed, wave_bytes, cudaMemcpyDeviceToHost,
+                            c->copy_stream);
+            cudaEventRecord(e.b, c->copy_stream);
+            cudaEventRecord(c->ev_d2h[b], c->copy_stream);
+            c->stats.d2h_bytes += wave_bytes;
+        } else {
+            status = CZG_E_CAPACITY;
+        }
+        total += wave_bytes;
+        return CZG_OK;
+    };
+    int st = CZG_OK;
+    for (size_t i = 0; i < waves.size() && !st; i++) {
+        st = enqueue(waves[i], (int)(i & 1));
+        if (!st && i >= 1) st = finish(waves[i - 1], (int)((i - 1) & 1));
     }
+    if (!st && !waves.empty()) st = finish(waves.back(), (int)((waves.size() - 1) & 1));
+    // the last copies complete before the call returns (and before its end event)
+    const bool drained = cudaStreamSynchronize(c->copy_stream) == cudaSuccess;
+    if (st) {
+        cudaStreamSynchronize(c->stream);
+        return st;
+    }
+    if (!cuda_ok(c, drained ? cudaSuccess : cudaErrorUnknown, "wave copy-out")) return CZG_E_DEVICE;
+    collect_events(c);
     stats_end(c);
     if (out_needed) *out_needed = total;
     if (status == CZG_E_CAPACITY) return fail(c, CZG_E_CAPACITY, "output buffer too small");
@@ -1005,6 +1085,11 @@ int czg_ctx_create(int device, const uint8_t *czm, size_t czm_len, czg_ctx **out
     if (!st) {
         cudaEventCreate(&c->ev_begin);
         cudaEventCreate(&c->ev_end);
+        bool ok = cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking) == cudaSuccess;
+        for (int b = 0; b < 2 && ok; b++)
+            for (cudaEvent_t *e : {&c->ev_h2d[b], &c->ev_comp[b], &c->ev_small[b], &c->ev_d2h[b]})
+                ok = ok && cudaEventCreateWithFlags(e, cudaEventDisableTiming) == cudaSuccess;
+        if (!ok) st = fail(c, CZG_E_DEVICE, "cannot create the copy stream and its events");
         kernels_init();
         if (!cuda_ok(c, cudaDeviceSynchronize(), "init")) st = CZG_E_DEVICE;
     }
@@ -1025,7 +1110,13 @@ void czg_ctx_destroy(czg_ctx *c) {
     for (void *p : c->allocs) cudaFree(p);
     for (void *p : c->ws_allocs) cudaFree(p);
     for (void *p : c->dec_allocs) cudaFree(p);
-    if (c->h_meta) cudaFreeHost(c->h_meta);
+    if (c->copy_stream) cudaStreamSynchronize(c->copy_stream);
+    for (uint8_t *h : {c->h_meta, c->h_meta2, c->h_small[0], c->h_small[1]})
+        if (h) cudaFreeHost(h);
+    for (int b = 0; b < 2; b++)
+        for (cudaEvent_t e : {c->ev_h2d[b], c->ev_comp[b], c->ev_small[b], c->ev_d2h[b]})
+            if (e) cudaEventDestroy(e);
+    if (c->copy_stream) cudaStreamDestroy(c->copy_stream);
     for (auto &e : c->evs) { cudaEventDestroy(e.a); cudaEventDestroy(e.b); }
     if (c->ev_begin) cudaEventDestroy(c->ev_begin);
     if (c->ev_end) cudaEventDestroy(c->ev_end);

@@ -134,6 +134,8 @@ void launch_cdf_lohi(const int32_t *logits, int V, int ld, const uint32_t *sym, 
 void launch_encode(const uint2 *lohi, const int *chunk_row0, const int *chunk_len, int n_chunks,
                    uint32_t total, uint8_t *slots, const uint64_t *slot_off, uint32_t *lens,
                    int *err, cudaStream_t st);
+// pack_off[i] = lens[0] + ... + lens[i-1] for i <= n_chunks (on the device)
+void launch_pack_offsets(const uint32_t *lens, int n_chunks, uint64_t *pack_off, cudaStream_t st);
 void launch_pack(const uint8_t *slots, const uint64_t *slot_off, const uint32_t *lens,
                  const uint64_t *pack_off, int n_chunks, uint8_t *packed, cudaStream_t st);
 

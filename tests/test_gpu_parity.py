@@ -390,3 +390,42 @@ def test_dff_not_multiple_of_128(shipped_path, tmp_path, oracle_mod, shipped_tok
         assert np.array_equal(eng.decompress_chunks(got, np.diff(starts).astype(np.uint32)), toks)
     finally:
         eng.close()
+
+
+def test_capacity_and_pipelined_waves(shipped_path, shipped_oracle, oracle_mod, shipped_tokens, monkeypatch):
+    """Several pipelined waves (small wave cap): an output buffer one byte short gives
+    CZG_E_CAPACITY with the exact size, the context stays usable, and with room the
+    packed bytes and lengths equal the oracle's; from host and from device tokens."""
+    import ctypes as C
+
+    import torch
+
+    from compress_zip_b200 import engine as E
+
+    monkeypatch.setenv("CZG_WAVE_TOKENS", "16384")
+    toks = np.concatenate([shipped_tokens] * 6)[:60000].astype(np.uint32)
+    starts = _starts(len(toks), 1024)
+    want = oracle_mod.compress_chunks(shipped_oracle, toks, starts)
+    need_total = sum(len(w) for w in want)
+    eng = E.Engine.from_file(shipped_path, 0)
+    try:
+        L = E.lib()
+        n = len(starts) - 1
+        lens = np.zeros(n, np.uint32)
+        need = C.c_uint64(0)
+        out = np.zeros(need_total - 1, np.uint8)
+        st = L.czg_compress_chunks(eng._h, toks.ctypes.data, starts.ctypes.data, n, out.ctypes.data, len(out),
+                                   lens.ctypes.data, C.byref(need))
+        assert st == 4   # CZG_E_CAPACITY
+        assert need.value == need_total
+        out = np.zeros(need_total, np.uint8)
+        st = L.czg_compress_chunks(eng._h, toks.ctypes.data, starts.ctypes.data, n, out.ctypes.data, len(out),
+                                   lens.ctypes.data, C.byref(need))
+        assert st == 0 and need.value == need_total
+        assert out.tobytes() == b"".join(want) and list(lens) == [len(w) for w in want]
+        d_tok = torch.from_numpy(toks.view(np.int32)).cuda()
+        out2 = np.zeros(need_total, np.uint8)
+        assert eng.compress_device(d_tok.data_ptr(), starts, out2, lens) == need_total
+        assert out2.tobytes() == b"".join(want)
+    finally:
+        eng.close()
