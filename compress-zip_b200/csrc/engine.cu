@@ -30,6 +30,7 @@ void czg::kernels_init() {
     attention_init();
     attention_mma_init();
     gemm_tc_init();
+    gemm_norm_init();
     head_cdf_init();
 }
 
@@ -37,13 +38,14 @@ namespace {
 
 enum KernelClass {
     kRows = 0, kEmbedNorm, kGemmQkv, kKvPrep, kAttention, kGemmO, kResidualNorm, kGemmUp,
-    kGemmDown, kGemmHead, kCdf, kEncode, kPack, kKvAppend, kAttnDecode, kCdfDecode, kHeadCdf, kNumClasses
+    kGemmDown, kGemmHead, kCdf, kEncode, kPack, kKvAppend, kAttnDecode, kCdfDecode, kHeadCdf,
+    kGemmONorm, kGemmDownNorm, kNumClasses
 };
 static_assert(kNumClasses <= CZG_MAX_KERNEL_CLASSES, "too many kernel classes");
 const char *kClassNames[kNumClasses] = {
     "rows", "embed_norm", "gemm_qkv", "kv_prep", "attention", "gemm_o", "residual_norm",
     "gemm_up_reglu", "gemm_down", "gemm_head", "cdf", "encode", "pack", "kv_append",
-    "attention_decode", "cdf_decode", "head_cdf"};
+    "attention_decode", "cdf_decode", "head_cdf", "gemm_o_norm", "gemm_down_norm"};
 
 thread_local std::string g_create_error;
 
@@ -59,6 +61,12 @@ struct LayerDev {
     int qkv_mult = 1, out_mult = 1, up_mult = 1, down_mult = 1;
     int qkv_shift = 0, out_shift = 0, up_shift = 0, down_shift = 0;
     TcMatrix tm_qkv, tm_out, tm_up, tm_down;   // TMA descriptors of the weights
+    // O / down projection with the residual norm in the epilogue (gemm_norm.cu): the
+    // weights read in boxes of d/2 rows; chosen at model load when the projection has
+    // the FP32 requantisation form and d is 256, 384 or 512 (else the GEMM and
+    // k_residual_norm run apart)
+    TcMatrix tm_out_h, tm_down_h;
+    bool fused_o = false, fused_down = false;
 };
 
 struct EvPair {
@@ -420,6 +428,12 @@ int load_model(czg_ctx *c, const uint8_t *bytes, size_t len) {
         if ((st = scalar_i8(c, f, p + "attn.out.shift", 0, &L.out_shift))) return st;
         if ((st = scalar_i8(c, f, p + "ffn.up.shift", 0, &L.up_shift))) return st;
         if ((st = scalar_i8(c, f, p + "ffn.down.shift", 0, &L.down_shift))) return st;
+        const char *fn = getenv("CZG_FUSED_NORM");
+        const bool fuse = gemm_norm_supported(d) && !(fn && std::string(fn) == "0");
+        float mf, c2;
+        int ca;
+        L.fused_o = fuse && requant_fp32(L.out_mult, L.out_shift, &mf, &c2, &ca);
+        L.fused_down = fuse && requant_fp32(L.down_mult, L.down_shift, &mf, &c2, &ca);
     }
     return CZG_OK;
 }
@@ -474,6 +488,7 @@ int alloc_workspace(czg_ctx *c, int rows, int chunks) {
     for (auto &L : c->layers) {
         maps = maps && tc_make_matrix(L.tm_qkv, L.qkv_w, d + 128, d, tc_bn_for(d + 128)) &&
                tc_make_matrix(L.tm_out, L.out_w, d, d, tc_bn_for(d)) &&
+               tc_make_matrix(L.tm_out_h, L.out_w, d, d, d / 2) && tc_make_matrix(L.tm_down_h, L.down_w, d, dffp, d / 2) &&
                tc_make_matrix(L.tm_up, L.up_w, 2 * dffp, d, tc_bn_for(2 * dffp)) &&
                tc_make_matrix(L.tm_down, L.down_w, d, dffp, tc_bn_for(d));
     }
@@ -517,6 +532,53 @@ bool gemm(czg_ctx *c, const TcMatrix &ta, const TcMatrix &tb, int M, int N, int 
     if (launch_gemm_tc(ta, tb, M, N, K, epi, mult, shift, out, ldo, c->err_flag, c->stream)) return true;
     c->gemm_failed = true;
     return false;
+}
+
+// Attention output -> O projection -> post-attention norm, residual add (layer 0:
+// from the embedding row) and the FFN pre-norm into xn (model.rs:418-438): one
+// fused kernel, or the GEMM and k_residual_norm.
+void o_norm(czg_ctx *c, const LayerDev &L, int l, int M, cudaStream_t st) {
+    const int d = c->info.d_model;
+    const int8_t *embed = l == 0 ? c->embed : nullptr;
+    if (L.fused_o) {
+        timed(c, kGemmONorm, [&] {
+            if (!launch_gemm_norm(c->tm_attn, L.tm_out_h, M, d, d, L.out_mult, L.out_shift, L.ffn_norm,
+                                  L.post_attn_norm, c->inv_tab, c->tok_in, embed, true, c->x_res, c->res16, c->xn,
+                                  c->err_flag, st))
+                c->gemm_failed = true;
+        });
+        return;
+    }
+    timed(c, kGemmO, [&] { gemm(c, c->tm_attn, L.tm_out, M, d, d, kEpiRequant, L.out_mult, L.out_shift, c->o8, d); });
+    timed(c, kResidualNorm, [&] {
+        launch_residual_norm(c->o8, L.ffn_norm, L.post_attn_norm, M, d, c->inv_tab, c->tok_in, embed, true,
+                             c->x_res, c->res16, c->xn, st);
+    });
+}
+
+// FFN hidden -> down projection -> post-FFN norm, residual add and the next layer's
+// pre-norm (or the final norm; the residual is then not stored) (model.rs:455-475).
+void down_norm(czg_ctx *c, const LayerDev &L, int l, int M, cudaStream_t st) {
+    const czg_model_info &m = c->info;
+    const int d = m.d_model;
+    const int8_t *next = l + 1 < m.n_layers ? c->layers[l + 1].attn_norm : c->final_norm;
+    const bool store = l + 1 < m.n_layers;
+    if (L.fused_down) {
+        timed(c, kGemmDownNorm, [&] {
+            if (!launch_gemm_norm(c->tm_h, L.tm_down_h, M, d, c->dff_pad, L.down_mult, L.down_shift,
+                                  L.post_ffn_norm, next, c->inv_tab, c->tok_in, nullptr, store, c->x_res, c->res16,
+                                  c->xn, c->err_flag, st))
+                c->gemm_failed = true;
+        });
+        return;
+    }
+    timed(c, kGemmDown, [&] {
+        gemm(c, c->tm_h, L.tm_down, M, d, c->dff_pad, kEpiRequant, L.down_mult, L.down_shift, c->o8, d);
+    });
+    timed(c, kResidualNorm, [&] {
+        launch_residual_norm(c->o8, L.post_ffn_norm, next, M, d, c->inv_tab, c->tok_in, nullptr, store, c->x_res,
+                             c->res16, c->xn, st);
+    });
 }
 
 struct Trace {
@@ -622,27 +684,12 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
         if (tr && tr->attn)
             cudaMemcpy2DAsync(tr->attn + (size_t)l * d, (size_t)m.n_layers * d, c->attn, d, d, M,
                               cudaMemcpyDeviceToHost, st);
-        timed(c, kGemmO, [&] {
-            gemm(c, c->tm_attn, L.tm_out, M, d, d, kEpiRequant, L.out_mult, L.out_shift,
-                 c->o8, d);
-        });
-        timed(c, kResidualNorm, [&] {
-            launch_residual_norm(c->o8, L.ffn_norm, L.post_attn_norm, M, d, c->inv_tab, c->tok_in,
-                                 l == 0 ? c->embed : nullptr, true, c->x_res, c->res16, c->xn, st);
-        });
+        o_norm(c, L, l, M, st);
         timed(c, kGemmUp, [&] {
             gemm(c, c->tm_xn, L.tm_up, M, 2 * dff, d, kEpiReglu, L.up_mult, L.up_shift,
                  c->hbuf, dff);
         });
-        timed(c, kGemmDown, [&] {
-            gemm(c, c->tm_h, L.tm_down, M, d, dff, kEpiRequant, L.down_mult,
-                 L.down_shift, c->o8, d);
-        });
-        const int8_t *next = l + 1 < m.n_layers ? c->layers[l + 1].attn_norm : c->final_norm;
-        timed(c, kResidualNorm, [&] {
-            launch_residual_norm(c->o8, L.post_ffn_norm, next, M, d, c->inv_tab, c->tok_in, nullptr,
-                                 l + 1 < m.n_layers, c->x_res, c->res16, c->xn, st);
-        });
+        down_norm(c, L, l, M, st);
     }
     if (tr && tr->final_in)
         cudaMemcpyAsync(tr->final_in, c->xn, (size_t)M * d, cudaMemcpyDeviceToHost, st);
@@ -992,27 +1039,12 @@ int decompress_impl(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts
                         launch_attention_decode(c->qkv, d + 128, kvc, cache_ld, M, step, H, L.score_mult, L.sink_key,
                                                 c->rope_cos, c->rope_sin, c->lut, c->attn, d, s);
                 });
-                timed(c, kGemmO, [&] {
-                    gemm(c, c->tm_attn, L.tm_out, M, d, d, kEpiRequant, L.out_mult, L.out_shift,
-                         c->o8, d);
-                });
-                timed(c, kResidualNorm, [&] {
-                    launch_residual_norm(c->o8, L.ffn_norm, L.post_attn_norm, M, d, c->inv_tab, c->tok_in,
-                                         l == 0 ? c->embed : nullptr, true, c->x_res, c->res16, c->xn, s);
-                });
+                o_norm(c, L, l, M, s);
                 timed(c, kGemmUp, [&] {
                     gemm(c, c->tm_xn, L.tm_up, M, 2 * dff, d, kEpiReglu, L.up_mult, L.up_shift,
                          c->hbuf, dff);
                 });
-                timed(c, kGemmDown, [&] {
-                    gemm(c, c->tm_h, L.tm_down, M, d, dff, kEpiRequant, L.down_mult,
-                         L.down_shift, c->o8, d);
-                });
-                const int8_t *next = l + 1 < m.n_layers ? c->layers[l + 1].attn_norm : c->final_norm;
-                timed(c, kResidualNorm, [&] {
-                    launch_residual_norm(c->o8, L.post_ffn_norm, next, M, d, c->inv_tab, c->tok_in, nullptr,
-                                         l + 1 < m.n_layers, c->x_res, c->res16, c->xn, s);
-                });
+                down_norm(c, L, l, M, s);
             }
             timed(c, kGemmHead, [&] {
                 gemm(c, c->tm_xn, c->tm_head, M, c->vpad, d, kEpiInt32, 1, 0, c->logits, c->vpad);

@@ -435,6 +435,15 @@ bool tc_make_matrix(TcMatrix &m, const int8_t *base, uint64_t rows, uint64_t K, 
     return r == CUDA_SUCCESS;
 }
 
+bool requant_fp32(int mult, int shift, float *mf, float *c2, int *clamp_a) {
+    const Requant q = make_requant(mult, shift);
+    if (q.mode != 3) return false;
+    *mf = q.mf;
+    *c2 = q.c2;
+    *clamp_a = q.clamp_a;
+    return true;
+}
+
 void gemm_tc_init() {
     set_attr<128>();
     set_attr<256>();

@@ -73,6 +73,20 @@ bool launch_head_cdf(const TcMatrix &A, const TcMatrix &B, int M, int V, int K, 
 bool launch_gemm_tc(const TcMatrix &A, const TcMatrix &B, int M, int N, int K, int epi, int mult, int shift,
                     void *out, int ldo, int *err, cudaStream_t st);
 
+// the FP32 requantisation form (gemm_tc.cu, mode 3) of (mult, shift), or false
+bool requant_fp32(int mult, int shift, float *mf, float *c2, int *clamp_a);
+// gemm_norm.cu: O / down projection (x . W^T, FP32 requantisation) with the post norm,
+// residual add and next pre-norm in the epilogue (rows.cu's k_residual_norm fused):
+// B = the weight as a TcMatrix read in boxes of d/2 rows; embed != nullptr: the
+// residual is embed[tok_in[r]] (written to x_res); store_res false: not written back.
+// false: unsupported (d not 256/384/512, or no FP32 requantisation form), nothing launched.
+void gemm_norm_init();
+bool gemm_norm_supported(int d);
+bool launch_gemm_norm(const TcMatrix &A, const TcMatrix &B, int M, int d, int K, int mult, int shift,
+                      const int8_t *post_w, const int8_t *next_w, const uint16_t *inv_tab, const uint32_t *tok_in,
+                      const int8_t *embed, bool store_res, void *x_res, bool res16, int8_t *xn, int *err,
+                      cudaStream_t st);
+
 void attention_init();
 // attention_mma.cu: tensor-core version, K/V of a chunk staged in shared memory for
 // chunks of at most 1024 positions (launch_attention_mma_stream for longer ones);
