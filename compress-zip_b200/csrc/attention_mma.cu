@@ -597,6 +597,10 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
 // the stream's keys 0..p in the split cache layout (K rows of 64 permuted dims,
 // then V in 2 KB tiles of 32 keys as [8 key groups][64 dims][4 keys]).  The heads are the 8 rows of the attention tile (A rows
 // n_heads..15 are zero); everything else is the chunk kernel's tile step.
+// The warp also appends the stream's key p (RoPE) and value p, from columns kd..kd+127
+// of its qkv row, to the cache (the layout of k_kv_append, decode.cu) and patches
+// them into the stage of the last tile once that tile's copy has landed: the copy may
+// have been issued before the row was written.
 // Persistent: one CTA per SM, warp w takes streams w, w + W, w + 2W, ... (W the
 // warps of the grid).  A warp's tiles, stream after stream, flow through a ring of
 // DEC_STAGES 4 KB shared-memory stages with DEC_STAGES - 1 tile copies in flight,
@@ -606,7 +610,7 @@ constexpr int DEC_SMEM = AM_WARPS * DEC_STAGES * 4096 + AM_LUT * 2;
 
 template <int MODE, bool EXP0>
 __global__ void __launch_bounds__(AM_THREADS, 1)
-k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restrict__ kvc, size_t cache_ld,
+k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, int kd, int8_t *kvc, size_t cache_ld,
                        int M, int p, int n_heads, const int32_t *__restrict__ score_mult,
                        const int8_t *__restrict__ sink_key, const int16_t *__restrict__ rope_cos,
                        const int16_t *__restrict__ rope_sin, const uint16_t *__restrict__ lut4k_g,
@@ -682,6 +686,25 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__
         qa[1][2] = hi[1];
         qa[0][1] = qa[0][3] = qa[1][1] = qa[1][3] = 0u;
     }
+    // key p rotated (attention.rs:29-50) and value p: lane l holds dims l, l + 32 of the
+    // key and dims 2l, 2l + 1 of the value, written to the cache now and kept (one word
+    // per lane, in the output staging area, free until the output) for the last tile
+    {
+        const int8_t *kq = qkv + (size_t)r * ldq + kd;
+        const int x = kq[lane], y = kq[lane + kHalfDim];
+        const int cs = rope_cos[p * kHalfDim + lane], sn = rope_sin[p * kHalfDim + lane];
+        const int kx = clamp127(sra_rne32(x * cs - y * sn, 15));
+        const int ky = clamp127(sra_rne32(x * sn + y * cs, 15));
+        const uint32_t v2 = *reinterpret_cast<const uint16_t *>(kq + 64 + 2 * lane);
+        reinterpret_cast<uint32_t *>(ostage)[lane] = (uint32_t)(uint8_t)kx | ((uint32_t)(uint8_t)ky << 8) | (v2 << 16);
+        int8_t *base = kvc + (size_t)r * cache_ld;
+        const int l2 = lane + kHalfDim;
+        base[(size_t)p * 64 + 16 * ((lane >> 2) & 3) + 4 * (lane >> 4) + (lane & 3)] = (int8_t)kx;
+        base[(size_t)p * 64 + 16 * ((l2 >> 2) & 3) + 4 * (l2 >> 4) + (l2 & 3)] = (int8_t)ky;
+        int8_t *vt = base + len * 64 + (size_t)(p >> 5) * 2048 + ((p & 31) >> 2) * 256 + (p & 3);
+        vt[(2 * lane) * 4] = (int8_t)(v2 & 0xFFu);
+        vt[(2 * lane + 1) * 4] = (int8_t)(v2 >> 8);
+    }
     int m = INT32_MIN;
     unsigned long long s_state[2] = {0, 0};
     if (sink_key != nullptr) {   // attention.rs:211-224
@@ -708,8 +731,18 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__
         fetch();
         asm volatile("cp.async.wait_group %0;" ::"n"(DEC_STAGES - 1) : "memory");
         __syncwarp();
-        const uint8_t *kst = stages + cslot * 4096;   // K rows of the tile, then the V tile
+        uint8_t *kst = stages + cslot * 4096;   // K rows of the tile, then the V tile
         cslot = cslot + 1 == DEC_STAGES ? 0 : cslot + 1;
+        if (kb + 32 > p) {   // the last tile: key p and value p from this step
+            const uint32_t kvw = reinterpret_cast<const uint32_t *>(ostage)[lane];
+            const int l2 = lane + kHalfDim, kp = p & 31;
+            kst[kp * 64 + 16 * ((lane >> 2) & 3) + 4 * (lane >> 4) + (lane & 3)] = (uint8_t)kvw;
+            kst[kp * 64 + 16 * ((l2 >> 2) & 3) + 4 * (l2 >> 4) + (l2 & 3)] = (uint8_t)(kvw >> 8);
+            uint8_t *vs = kst + 2048 + (kp >> 2) * 256 + (kp & 3);
+            vs[(2 * lane) * 4] = (uint8_t)(kvw >> 16);
+            vs[(2 * lane + 1) * 4] = (uint8_t)(kvw >> 24);
+            __syncwarp();
+        }
         int sacc[4][4];
 #pragma unroll
         for (int j = 0; j < 4; j++) {
@@ -913,7 +946,7 @@ void launch_attention_mma_stream(const int8_t *qkv, int ldq, const int8_t *kv, c
 
 bool attention_decode_mma_ok(int n_heads) { return n_heads >= 1 && n_heads <= AM_ROWS; }
 
-void launch_attention_decode_mma(const int8_t *qkv, int ldq, const int8_t *kvc, size_t cache_ld, int M, int p,
+void launch_attention_decode_mma(const int8_t *qkv, int ldq, int kd, int8_t *kvc, size_t cache_ld, int M, int p,
                                  int n_heads, const int32_t *score_mult, const int8_t *sink_key,
                                  const int16_t *rope_cos, const int16_t *rope_sin, const uint16_t *lut4k,
                                  int score_mode, bool exp0, int8_t *out, int ldo, cudaStream_t st) {
@@ -921,19 +954,19 @@ void launch_attention_decode_mma(const int8_t *qkv, int ldq, const int8_t *kvc, 
     const unsigned grid = (unsigned)std::min<long>((M + AM_WARPS - 1) / AM_WARPS, (long)sm_count());
     if (score_mode == 1) {
         if (exp0)
-            launch_k(k_attention_decode_mma<1, true>, grid, AM_THREADS, DEC_SMEM, st, qkv, ldq, kvc, cache_ld, M, p,
+            launch_k(k_attention_decode_mma<1, true>, grid, AM_THREADS, DEC_SMEM, st, qkv, ldq, kd, kvc, cache_ld, M, p,
                      n_heads, score_mult, sink_key, rope_cos, rope_sin, lut4k, out, ldo);
         else
-            launch_k(k_attention_decode_mma<1, false>, grid, AM_THREADS, DEC_SMEM, st, qkv, ldq, kvc, cache_ld, M, p,
+            launch_k(k_attention_decode_mma<1, false>, grid, AM_THREADS, DEC_SMEM, st, qkv, ldq, kd, kvc, cache_ld, M, p,
                      n_heads, score_mult, sink_key, rope_cos, rope_sin, lut4k, out, ldo);
     } else if (score_mode == 2)
-        launch_k(k_attention_decode_mma<2, false>, grid, AM_THREADS, DEC_SMEM, st, qkv, ldq, kvc, cache_ld, M, p,
+        launch_k(k_attention_decode_mma<2, false>, grid, AM_THREADS, DEC_SMEM, st, qkv, ldq, kd, kvc, cache_ld, M, p,
                  n_heads, score_mult, sink_key, rope_cos, rope_sin, lut4k, out, ldo);
     else if (exp0)
-        launch_k(k_attention_decode_mma<0, true>, grid, AM_THREADS, DEC_SMEM, st, qkv, ldq, kvc, cache_ld, M, p,
+        launch_k(k_attention_decode_mma<0, true>, grid, AM_THREADS, DEC_SMEM, st, qkv, ldq, kd, kvc, cache_ld, M, p,
                  n_heads, score_mult, sink_key, rope_cos, rope_sin, lut4k, out, ldo);
     else
-        launch_k(k_attention_decode_mma<0, false>, grid, AM_THREADS, DEC_SMEM, st, qkv, ldq, kvc, cache_ld, M, p,
+        launch_k(k_attention_decode_mma<0, false>, grid, AM_THREADS, DEC_SMEM, st, qkv, ldq, kd, kvc, cache_ld, M, p,
                  n_heads, score_mult, sink_key, rope_cos, rope_sin, lut4k, out, ldo);
 }
 

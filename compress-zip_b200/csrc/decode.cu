@@ -19,6 +19,65 @@ __device__ __forceinline__ uint32_t read_bit(const uint8_t *data, uint64_t len, 
     return (uint32_t)(data[byte] >> (7 - (bit & 7))) & 1u;
 }
 
+// Byte `lane` (< 9) of the chunk from the byte holding bit `bit` on, 0 past the end;
+// window() assembles the warp's nine bytes into the 64 bits from `bit` on, MSB first.
+__device__ __forceinline__ uint32_t window_byte(const uint8_t *data, uint64_t len, uint64_t bit, int lane) {
+    const uint64_t byte = (bit >> 3) + (uint64_t)lane;
+    return (lane < 9 && byte < len) ? (uint32_t)data[byte] : 0u;
+}
+__device__ __forceinline__ unsigned long long window(uint32_t b, uint64_t bit, int lane) {
+    const uint32_t hi = __reduce_or_sync(0xffffffffu, lane < 4 ? b << (24 - 8 * lane) : 0u);
+    const uint32_t lo = __reduce_or_sync(0xffffffffu, lane >= 4 && lane < 8 ? b << (56 - 8 * lane) : 0u);
+    const uint32_t b8 = __shfl_sync(0xffffffffu, b, 8);
+    const unsigned long long w = ((unsigned long long)hi << 32) | lo;
+    const int off = (int)(bit & 7);
+    return off ? (w << off) | (b8 >> (8 - off)) : w;
+}
+
+// ArithDecoder::decode_symbol after the search (arith_coder.rs:244-264): narrow to
+// [lo, hi) of total, then renormalise in closed form.  The loop shifts while the top
+// bits of low and high agree (n1 = clz(low ^ high) times, 32 when equal), and only
+// then takes the E3 steps, while bit 30 is set in low and clear in high: an E3 step
+// leaves the top bits different, so no E1/E2 step follows one.  Over k steps
+//   E1/E2: low << k, (high << k) | (2^k - 1), (code << k) | next k bits;
+//   E3:    (low << k) ^ HALF, (high << k) | HALF | (2^k - 1),
+//          (code & HALF) | ((code << k) & (HALF - 1)) | next k bits,
+// with n3 = the run of set bits of low & ~high from bit 30 down.  n1 + n3 <= 63, so
+// the 64-bit window `win` holds every bit read.
+__device__ __forceinline__ void dec_narrow(DecState &s, uint32_t lo, uint32_t hi, uint32_t total,
+                                           unsigned long long inv_total, unsigned long long win) {
+    const unsigned long long range = (unsigned long long)s.high - s.low + 1;
+    uint32_t high = (uint32_t)(s.low + udiv_by_inv((unsigned long long)hi * range, total, inv_total) - 1);
+    uint32_t low = (uint32_t)(s.low + udiv_by_inv((unsigned long long)lo * range, total, inv_total));
+    uint32_t code = s.code;
+    const int n1 = __clz((int)(low ^ high));
+    if (n1 > 0) {
+        low = (uint32_t)((unsigned long long)low << n1);
+        high = (uint32_t)(((unsigned long long)high << n1) | ((1ull << n1) - 1ull));
+        code = (uint32_t)(((unsigned long long)code << n1) | (win >> (64 - n1)));
+        win <<= n1;
+    }
+    const int n3 = __clz((int)~((low & ~high) << 1));
+    if (n3 > 0) {
+        low = (low << n3) ^ 0x80000000u;
+        high = (high << n3) | 0x80000000u | ((1u << n3) - 1u);
+        code = (code & 0x80000000u) | ((code << n3) & 0x7FFFFFFFu) | (uint32_t)(win >> (64 - n3));
+    }
+    s.low = low;
+    s.high = high;
+    s.code = code;
+    s.bit += (uint64_t)(n1 + n3);
+}
+
+// The next step's first pre-norm output of a stream decoded to `sym`: row sym of the
+// normalised embedding table (the first norm of a row depends on its token alone).
+__device__ __forceinline__ void copy_xn_row(const int8_t *__restrict__ xn_tab, int8_t *__restrict__ xn, int d,
+                                            uint32_t sym, int r, int lane) {
+    const uint32_t *src = reinterpret_cast<const uint32_t *>(xn_tab + (size_t)sym * d);
+    uint32_t *dst = reinterpret_cast<uint32_t *>(xn + (size_t)r * d);
+    for (int j = lane; j < d / 4; j += 32) dst[j] = __ldg(src + j);
+}
+
 // ArithDecoder::new: code = the first 32 bits (arith_coder.rs:153-174)
 __global__ void k_dec_init(const uint8_t *__restrict__ data, const uint64_t *__restrict__ data_off,
                            const uint64_t *__restrict__ data_len, int M, DecState *__restrict__ st,
@@ -85,7 +144,8 @@ __global__ void k_cdf_decode(const int32_t *__restrict__ logits, int V, int ld, 
                              DecState *__restrict__ st, const uint8_t *__restrict__ data,
                              const uint64_t *__restrict__ data_off, const uint64_t *__restrict__ data_len,
                              const uint64_t *__restrict__ tok_off, int step, uint32_t *__restrict__ out_tok,
-                             uint32_t *__restrict__ tok_in) {
+                             uint32_t *__restrict__ tok_in, const int8_t *__restrict__ xn_tab,
+                             int8_t *__restrict__ xn, int d) {
     __shared__ uint16_t lut[256];
     for (int i = threadIdx.x; i < 256; i += blockDim.x) lut[i] = lut_g[i];   // model constant
     pdl_wait();
@@ -193,6 +253,7 @@ __global__ void k_cdf_decode(const int32_t *__restrict__ logits, int V, int ld, 
         out_tok[tok_off[r] + step] = sym;
         tok_in[r] = sym;
     }
+    if (xn != nullptr) copy_xn_row(xn_tab, xn, d, sym, r, lane);
 }
 
 // Register-resident version for V == 32 * E (E in {8, 16, 32}): lane l holds the
@@ -212,7 +273,8 @@ __global__ void __launch_bounds__(256, CDF_BLOCKS_PER_SM) k_cdf_decode_reg(
     const int32_t *__restrict__ logits, int ld, const uint16_t *__restrict__ lut4k_g, uint32_t c8, uint32_t total,
     unsigned long long inv_total, int M, DecState *__restrict__ st, const uint8_t *__restrict__ data,
     const uint64_t *__restrict__ data_off, const uint64_t *__restrict__ data_len, const uint64_t *__restrict__ tok_off,
-    int step, uint32_t *__restrict__ out_tok, uint32_t *__restrict__ tok_in) {
+    int step, uint32_t *__restrict__ out_tok, uint32_t *__restrict__ tok_in, const int8_t *__restrict__ xn_tab,
+    int8_t *__restrict__ xn, int d) {
     constexpr int V = 32 * E;
     __shared__ uint32_t ebuf[8][E / 2];
     __shared__ uint32_t lut_w[CDF_LUT_WORDS];
@@ -231,6 +293,9 @@ __global__ void __launch_bounds__(256, CDF_BLOCKS_PER_SM) k_cdf_decode_reg(
         const int4 v = __ldcs(src + k);
         x[4 * k] = v.x; x[4 * k + 1] = v.y; x[4 * k + 2] = v.z; x[4 * k + 3] = v.w;
     }
+    // the coder state and the next 9 bytes of the chunk, loaded while the CDF is built
+    DecState s = st[r];
+    const uint32_t wb = window_byte(data + data_off[r], data_len[r], s.bit, lane);
     // max and first argmax (primitives.rs:278-295)
     int mx = INT32_MIN, am = 0x7fffffff;
 #pragma unroll
@@ -273,7 +338,6 @@ __global__ void __launch_bounds__(256, CDF_BLOCKS_PER_SM) k_cdf_decode_reg(
     }
     const uint32_t base = inc - F;
 
-    DecState s = st[r];
     const unsigned long long range = (unsigned long long)s.high - s.low + 1;
     // value = ((code - low + 1) * T - 1) / range  (arith_coder.rs:195-200)
     const unsigned long long value = (((unsigned long long)s.code - s.low + 1) * total - 1) / range;
@@ -306,36 +370,15 @@ __global__ void __launch_bounds__(256, CDF_BLOCKS_PER_SM) k_cdf_decode_reg(
     const int sl = past_end ? E - 1 : __ffs(hit) - 1;   // hit != 0 unless past the end
     const uint32_t hi = __shfl_sync(0xffffffffu, cum, sl);
     const uint32_t lo = hi - __shfl_sync(0xffffffffu, f, sl);
+    const unsigned long long win = window(wb, s.bit, lane);
+    const uint32_t sym = (uint32_t)(owner * E + sl);
     if (lane == 0) {
-        const uint32_t sym = (uint32_t)(owner * E + sl);
-        const unsigned long long HALF = 1ull << 31, QUARTER = 1ull << 30, MASK = 0xFFFFFFFFull;
-        unsigned long long low = s.low, high = s.high, code = s.code;
-        uint64_t bit = s.bit;
-        const uint8_t *d = data + data_off[r];
-        const uint64_t len = data_len[r];
-        high = low + udiv_by_inv((unsigned long long)hi * range, total, inv_total) - 1;
-        low = low + udiv_by_inv((unsigned long long)lo * range, total, inv_total);
-        for (;;) {   // arith_coder.rs:244-264
-            if (((low ^ high) & HALF) == 0) {
-                low = (low << 1) & MASK;
-                high = ((high << 1) & MASK) | 1ull;
-                code = ((code << 1) & MASK) | read_bit(d, len, bit++);
-            } else if ((low & ~high & QUARTER) != 0) {
-                low = ((low << 1) ^ HALF) & MASK;
-                high = (((high ^ HALF) << 1) | HALF | 1ull) & MASK;
-                code = (code & HALF) | ((code << 1) & (MASK >> 1)) | read_bit(d, len, bit++);
-            } else {
-                break;
-            }
-        }
-        s.low = (uint32_t)low;
-        s.high = (uint32_t)high;
-        s.code = (uint32_t)code;
-        s.bit = bit;
+        dec_narrow(s, lo, hi, total, inv_total, win);
         st[r] = s;
         out_tok[tok_off[r] + step] = sym;
         tok_in[r] = sym;
     }
+    if (xn != nullptr) copy_xn_row(xn_tab, xn, d, sym, r, lane);
     __syncwarp();   // ebuf is rewritten for the warp's next stream
     }
 }
@@ -359,7 +402,8 @@ void launch_kv_append(const int8_t *qkv, int ldq, int d, int pos, const int16_t 
 void launch_cdf_decode(const int32_t *logits, int V, int ld, const uint16_t *lut, const uint16_t *lut4k, bool exp0,
                        uint32_t coef, uint32_t total, int M, DecState *st, const uint8_t *data,
                        const uint64_t *data_off, const uint64_t *data_len, const uint64_t *tok_off, int step,
-                       uint32_t *out_tok, uint32_t *tok_in, cudaStream_t stream) {
+                       uint32_t *out_tok, uint32_t *tok_in, const int8_t *xn_tab, int8_t *xn, int d,
+                       cudaStream_t stream) {
     if (M == 0) return;
     const unsigned long long inv = 0xFFFFFFFFFFFFFFFFull / total;
     const unsigned grid = (unsigned)((M + 7) / 8);
@@ -370,10 +414,10 @@ void launch_cdf_decode(const int32_t *logits, int V, int ld, const uint16_t *lut
     do {                                                                                                       \
         if (exp0)                                                                                              \
             launch_k(k_cdf_decode_reg<EE, true>, pgrid, 256, 0, stream, logits, ld, lut4k, c8, total, inv, M, st,  \
-                     data, data_off, data_len, tok_off, step, out_tok, tok_in);                                \
+                     data, data_off, data_len, tok_off, step, out_tok, tok_in, xn_tab, xn, d);                \
         else                                                                                                   \
             launch_k(k_cdf_decode_reg<EE, false>, pgrid, 256, 0, stream, logits, ld, lut4k, c8, total, inv, M, st, \
-                     data, data_off, data_len, tok_off, step, out_tok, tok_in);                                \
+                     data, data_off, data_len, tok_off, step, out_tok, tok_in, xn_tab, xn, d);                \
     } while (0)
         if (V == 1024) CZG_CDF_DEC(32);
         else if (V == 512) CZG_CDF_DEC(16);
@@ -382,7 +426,7 @@ void launch_cdf_decode(const int32_t *logits, int V, int ld, const uint16_t *lut
         return;
     }
     launch_k(k_cdf_decode, grid, 256, 0, stream, logits, V, ld, lut, coef, total, inv, M, st, data, data_off, data_len,
-             tok_off, step, out_tok, tok_in);
+             tok_off, step, out_tok, tok_in, xn_tab, xn, d);
 }
 
 }  // namespace czg

@@ -88,6 +88,7 @@ struct czg_ctx {
     int vpad = 0;           // vocab rounded up to the GEMM tile (extra head rows are zero)
     int dff_pad = 0;        // d_ff rounded up to the GEMM tile (extra hidden units are zero)
     int8_t *embed = nullptr, *final_norm = nullptr, *head_w = nullptr;
+    int8_t *xn_tab = nullptr;   // [V][d]: the first pre-norm of every token's embedding row
     uint16_t *lut = nullptr;
     uint16_t *lut4k = nullptr;   // exp_q16 by t256 <= 4096 (lut.rs:213-235 unrolled over ip)
     uint16_t *inv_tab = nullptr;   // inv_rms_q15 by floor(sum_sq / d), eps folded in
@@ -434,6 +435,16 @@ int load_model(czg_ctx *c, const uint8_t *bytes, size_t len) {
         int ca;
         L.fused_o = fuse && requant_fp32(L.out_mult, L.out_shift, &mf, &c2, &ca);
         L.fused_down = fuse && requant_fp32(L.down_mult, L.down_shift, &mf, &c2, &ca);
+    }
+    {   // the first pre-norm depends on the token alone: one row per vocabulary entry
+        std::vector<uint32_t> iota(V);
+        for (int v = 0; v < V; v++) iota[v] = (uint32_t)v;
+        uint32_t *d_iota = nullptr;
+        if (!upload(c, &d_iota, iota.data(), (size_t)V * 4) || !dalloc(c, &c->xn_tab, (size_t)V * d))
+            return CZG_E_DEVICE;
+        launch_embed_norm(d_iota, c->embed, c->layers[0].attn_norm, V, d, c->inv_tab, nullptr, c->res16, false,
+                          c->xn_tab, c->stream);
+        if (!cuda_ok(c, cudaStreamSynchronize(c->stream), "normalised embedding table")) return CZG_E_DEVICE;
     }
     return CZG_OK;
 }
@@ -1016,10 +1027,12 @@ int decompress_impl(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts
         for (int step = 0; step < wmax; step++) {
             while (active > 0 && (int)n_tokens[order[w0 + active - 1]] <= step) active--;
             const int M = active;
-            timed(c, kEmbedNorm, [&] {
-                launch_embed_norm(c->tok_in, c->embed, c->layers[0].attn_norm, M, d, c->inv_tab, c->x_res, c->res16,
-                                  false, c->xn, s);
-            });
+            // later steps find their first pre-norm output written by the previous step's decoder
+            if (step == 0)
+                timed(c, kEmbedNorm, [&] {
+                    launch_embed_norm(c->tok_in, c->embed, c->layers[0].attn_norm, M, d, c->inv_tab, c->x_res,
+                                      c->res16, false, c->xn, s);
+                });
             for (int l = 0; l < m.n_layers; l++) {
                 const LayerDev &L = c->layers[l];
                 int8_t *kvc = c->kvc + (size_t)l * layer_ld;
@@ -1027,12 +1040,14 @@ int decompress_impl(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts
                     gemm(c, c->tm_xn, L.tm_qkv, M, d + 128, d, kEpiRequant, L.qkv_mult, L.qkv_shift,
                          c->qkv, d + 128);
                 });
-                timed(c, kKvAppend, [&] {
-                    launch_kv_append(c->qkv, d + 128, d, step, c->rope_cos, c->rope_sin, M, kvc, cache_ld, split, s);
-                });
+                if (!split)   // the tensor-core decode kernel appends the step's K/V row itself
+                    timed(c, kKvAppend, [&] {
+                        launch_kv_append(c->qkv, d + 128, d, step, c->rope_cos, c->rope_sin, M, kvc, cache_ld, split,
+                                         s);
+                    });
                 timed(c, kAttnDecode, [&] {
                     if (split)
-                        launch_attention_decode_mma(c->qkv, d + 128, kvc, cache_ld, M, step, H, L.score_mult,
+                        launch_attention_decode_mma(c->qkv, d + 128, d, kvc, cache_ld, M, step, H, L.score_mult,
                                                     L.sink_key, c->rope_cos, c->rope_sin, c->lut4k, L.score_mode, c->exp0,
                                                     c->attn, d, s);
                     else
@@ -1051,7 +1066,8 @@ int decompress_impl(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts
             });
             timed(c, kCdfDecode, [&] {
                 launch_cdf_decode(c->logits, V, c->vpad, c->lut, c->lut4k, c->exp0 && c->logit_small, m.coef_q24, m.target_total, M, c->dstate, c->ddata,
-                                  c->d_off, c->d_len, c->d_tokoff, step, c->d_outtok, c->tok_in, s);
+                                  c->d_off, c->d_len, c->d_tokoff, step, c->d_outtok, c->tok_in, c->xn_tab,
+                                  step + 1 < wmax ? c->xn : nullptr, d, s);
             });
             if (c->ev_used > 4096) {   // keep the event pool bounded on long chunks
                 if (!cuda_ok(c, cudaStreamSynchronize(s), "decode step")) return CZG_E_DEVICE;

@@ -98,7 +98,8 @@ void attention_mma_init();
 // heads as the rows of the attention tile (n_heads <= 8); cache_ld = 128 * len,
 // len % 32 == 0.
 bool attention_decode_mma_ok(int n_heads);
-void launch_attention_decode_mma(const int8_t *qkv, int ldq, const int8_t *kvc, size_t cache_ld, int M, int p,
+// also appends key p and value p (columns kd..kd+127 of each qkv row) to the cache
+void launch_attention_decode_mma(const int8_t *qkv, int ldq, int kd, int8_t *kvc, size_t cache_ld, int M, int p,
                                  int n_heads, const int32_t *score_mult, const int8_t *sink_key,
                                  const int16_t *rope_cos, const int16_t *rope_sin, const uint16_t *lut4k,
                                  int score_mode, bool exp0, int8_t *out, int ldo, cudaStream_t st);
@@ -134,7 +135,8 @@ void launch_kv_append(const int8_t *qkv, int ldq, int d, int pos, const int16_t 
 void launch_cdf_decode(const int32_t *logits, int V, int ld, const uint16_t *lut, const uint16_t *lut4k, bool exp0,
                        uint32_t coef, uint32_t total, int M, DecState *st, const uint8_t *data,
                        const uint64_t *data_off, const uint64_t *data_len, const uint64_t *tok_off, int step,
-                       uint32_t *out_tok, uint32_t *tok_in, cudaStream_t stream);
+                       uint32_t *out_tok, uint32_t *tok_in, const int8_t *xn_tab, int8_t *xn, int d,
+                       cudaStream_t stream);
 void launch_attention_decode(const int8_t *qkv, int ldq, const int8_t *kvc, size_t cache_ld, int M, int p,
                              int n_heads, const int32_t *score_mult, const int8_t *sink_key,
                              const int16_t *rope_cos, const int16_t *rope_sin, const uint16_t *lut,
