@@ -257,7 +257,8 @@ __global__ void k_cdf_decode(const int32_t *__restrict__ logits, int V, int ld, 
 }
 
 // Register-resident version for V == 32 * E (E in {8, 16, 32}): lane l holds the
-// E consecutive logits [l*E, (l+1)*E) in registers, the weights come from the
+// E consecutive logits [l*E, (l+1)*E) in registers (each warp copies its next
+// stream's row into shared memory while it decodes the current one), the weights come from the
 // t256-indexed table lut4k (needs coef < 2^24), the division by S uses
 // freq_of.  The interval search is done by the whole warp: the owner
 // lane's weights go through shared memory, one element per lane, and an
@@ -278,6 +279,7 @@ __global__ void __launch_bounds__(256, CDF_BLOCKS_PER_SM) k_cdf_decode_reg(
     constexpr int V = 32 * E;
     __shared__ uint32_t ebuf[8][E / 2];
     __shared__ uint32_t lut_w[CDF_LUT_WORDS];
+    __shared__ __align__(16) int4 rowbuf[8][V / 4];   // per warp: its next stream's logits
     for (int i = threadIdx.x; i < CDF_LUT_WORDS; i += blockDim.x)   // model constant: before the wait
         lut_w[i] = __ldg(reinterpret_cast<const uint32_t *>(lut4k_g) + i);
     pdl_wait();
@@ -285,14 +287,35 @@ __global__ void __launch_bounds__(256, CDF_BLOCKS_PER_SM) k_cdf_decode_reg(
     __syncthreads();
     const uint16_t *lut4k = reinterpret_cast<const uint16_t *>(lut_w);
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-    for (int r = blockIdx.x * 8 + wib; r < M; r += gridDim.x * 8) {
-    const int4 *src = reinterpret_cast<const int4 *>(logits + (size_t)r * ld + lane * E);
+    const int stride = gridDim.x * 8;
+    // the logits row of stream r into rowbuf with cp.async, 16-byte chunk c at c ^ ((c >> 3) & 7):
+    // lane l later reads its chunks l * E / 4 + k, and the eight lanes of each phase of a
+    // 16-byte shared load then fall on eight different bank groups
+    auto fetch_row = [&](int r) {
+        if (r < M) {
+            const int4 *src = reinterpret_cast<const int4 *>(logits + (size_t)r * ld);
+#pragma unroll
+            for (int c = lane; c < V / 4; c += 32)
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                                 (uint32_t)__cvta_generic_to_shared(&rowbuf[wib][c ^ ((c >> 3) & 7)])),
+                             "l"(src + c)
+                             : "memory");
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    fetch_row(blockIdx.x * 8 + wib);
+    for (int r = blockIdx.x * 8 + wib; r < M; r += stride) {
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncwarp();
     int x[E];
 #pragma unroll
     for (int k = 0; k < E / 4; k++) {
-        const int4 v = __ldcs(src + k);
+        const int c = lane * (E / 4) + k;
+        const int4 v = rowbuf[wib][c ^ ((c >> 3) & 7)];
         x[4 * k] = v.x; x[4 * k + 1] = v.y; x[4 * k + 2] = v.z; x[4 * k + 3] = v.w;
     }
+    __syncwarp();   // the buffer takes the warp's next stream while this one is decoded
+    fetch_row(r + stride);
     // the coder state and the next 9 bytes of the chunk, loaded while the CDF is built
     DecState s = st[r];
     const uint32_t wb = window_byte(data + data_off[r], data_len[r], s.bit, lane);
@@ -381,6 +404,7 @@ __global__ void __launch_bounds__(256, CDF_BLOCKS_PER_SM) k_cdf_decode_reg(
     if (xn != nullptr) copy_xn_row(xn_tab, xn, d, sym, r, lane);
     __syncwarp();   // ebuf is rewritten for the warp's next stream
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
 }  // namespace

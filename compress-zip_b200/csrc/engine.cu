@@ -539,8 +539,8 @@ int ensure_workspace(czg_ctx *c, size_t rows) {
 // One projection on the tcgen05 GEMM.  A shape it cannot take or an output map
 // that cannot be encoded is an error of the call (there is no other GEMM).
 bool gemm(czg_ctx *c, const TcMatrix &ta, const TcMatrix &tb, int M, int N, int K, int epi, int mult, int shift,
-          void *out, int ldo) {
-    if (launch_gemm_tc(ta, tb, M, N, K, epi, mult, shift, out, ldo, c->err_flag, c->stream)) return true;
+          void *out, int ldo, const KvSplit *kvs = nullptr) {
+    if (launch_gemm_tc(ta, tb, M, N, K, epi, mult, shift, out, ldo, c->err_flag, c->stream, kvs)) return true;
     c->gemm_failed = true;
     return false;
 }
@@ -661,24 +661,40 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
         launch_embed_norm(c->tok_in, c->embed, c->layers[0].attn_norm, M, d, c->inv_tab, c->x_res, c->res16, false,
                           c->xn, st);
     });
+    // tensor-core attention, K/V tiles streamed per warp from a per-chunk layout (at
+    // 1024 keys 129.6 ms per configuration-1 step against 136.0 with the chunk's
+    // K/V^T staged in shared memory, which CZG_ATTN_STAGED=1 selects up to 1024 keys)
+    const bool staged = c->staged_attention && attention_mma_fits(max_len) && !c->scalar_attention;
+    const bool stream = !staged && !c->scalar_attention;
+    // the streamed layout's K (rotated) and V come out of the QKV GEMM's epilogue
+    // (CZG_KV_EPILOGUE=0: k_kv_prep_split after a plain requantising GEMM)
+    const char *kve = getenv("CZG_KV_EPILOGUE");
+    const bool kv_epi = stream && !(kve && kve[0] == '0');
+    KvSplit kvs;
+    kvs.rowchunk = c->rowchunk;
+    kvs.chunk_row0 = c->chunk_row0;
+    kvs.chunk_len = c->chunk_len;
+    kvs.rope_cos = c->rope_cos;
+    kvs.rope_sin = c->rope_sin;
+    kvs.kv = c->kv;
+    kvs.d = d;
     for (int l = 0; l < m.n_layers; l++) {
         const LayerDev &L = c->layers[l];
         timed(c, kGemmQkv, [&] {
-            gemm(c, c->tm_xn, L.tm_qkv, M, d + 128, d, kEpiRequant, L.qkv_mult, L.qkv_shift,
-                 c->qkv, d + 128);
-        });
-        // tensor-core attention, K/V tiles streamed per warp from a per-chunk layout (at
-        // 1024 keys 129.6 ms per configuration-1 step against 136.0 with the chunk's
-        // K/V^T staged in shared memory, which CZG_ATTN_STAGED=1 selects up to 1024 keys)
-        const bool staged = c->staged_attention && attention_mma_fits(max_len) && !c->scalar_attention;
-        const bool stream = !staged && !c->scalar_attention;
-        timed(c, kKvPrep, [&] {
-            if (stream)
-                launch_kv_prep_split(c->qkv, d + 128, d, c->pos, c->rowchunk, c->chunk_row0, c->chunk_len,
-                                     c->rope_cos, c->rope_sin, M, c->kv, st);
+            if (kv_epi)
+                gemm(c, c->tm_xn, L.tm_qkv, M, d + 128, d, kEpiRequantKv, L.qkv_mult, L.qkv_shift, c->qkv, d + 128,
+                     &kvs);
             else
-                launch_kv_prep(c->qkv, d + 128, d, c->pos, c->rope_cos, c->rope_sin, M, c->kv, st);
+                gemm(c, c->tm_xn, L.tm_qkv, M, d + 128, d, kEpiRequant, L.qkv_mult, L.qkv_shift, c->qkv, d + 128);
         });
+        if (!kv_epi)
+            timed(c, kKvPrep, [&] {
+                if (stream)
+                    launch_kv_prep_split(c->qkv, d + 128, d, c->pos, c->rowchunk, c->chunk_row0, c->chunk_len,
+                                         c->rope_cos, c->rope_sin, M, c->kv, st);
+                else
+                    launch_kv_prep(c->qkv, d + 128, d, c->pos, c->rope_cos, c->rope_sin, M, c->kv, st);
+            });
         timed(c, kAttention, [&] {
             if (staged)
                 launch_attention_mma(c->qkv, d + 128, c->kv, c->att_row0, c->att_len, nc, max_len, H,

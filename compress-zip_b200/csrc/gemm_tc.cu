@@ -2,9 +2,11 @@
 // cores (tcgen05.mma kind::i8), operands staged by TMA, accumulator in TMEM.
 //
 // Computes the int8 linear layers of rust/src/linear.rs:12-31
-// (out[m, n] = sum_k x[m, k] * W[n, k]) with one of three epilogues:
+// (out[m, n] = sum_k x[m, k] * W[n, k]) with one of four epilogues:
 // requantisation (rust/src/model.rs:280-300), requantisation + ReGLU on
-// interleaved gate/up columns (rust/src/reglu.rs:20-46), or raw int32.
+// interleaved gate/up columns (rust/src/reglu.rs:20-46), raw int32, or the QKV
+// projection's requantisation with the key rotated (rust/src/attention.rs:29-50)
+// and the key and value written straight into the attention's per-chunk layout.
 //
 // Persistent, warp-specialised kernel: one CTA per SM walks the 128 x BN output
 // tiles (BN = 128 or 256) in a strided order.
@@ -87,10 +89,49 @@ struct EpiShape {
     static constexpr int kOutCols = EPI == kEpiInt32 ? 16 : 64;
 };
 
+// kEpiRequantKv, key slice: the row's 64 key bytes (staged, 64B-swizzled) rotated
+// (attention.rs:29-50, as k_kv_prep_split) and stored as the split layout's K row
+// (word W = dims 4W..4W+3 at word 4 (W % 4) + W / 4) with four 16-byte stores.
+__device__ __forceinline__ void kv_store_key(const uint8_t *srow, int sw, const int16_t *__restrict__ rc,
+                                             const int16_t *__restrict__ rs, int8_t *dst) {
+    uint32_t kw[16];
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+        const uint4 v = *reinterpret_cast<const uint4 *>(srow + ((c ^ sw) << 4));
+        kw[4 * c] = v.x; kw[4 * c + 1] = v.y; kw[4 * c + 2] = v.z; kw[4 * c + 3] = v.w;
+    }
+    uint32_t cw[16], sn[16];   // the position's 32 cos and 32 sin values, two per word
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+        const uint4 a = __ldg(reinterpret_cast<const uint4 *>(rc) + c), b = __ldg(reinterpret_cast<const uint4 *>(rs) + c);
+        cw[4 * c] = a.x; cw[4 * c + 1] = a.y; cw[4 * c + 2] = a.z; cw[4 * c + 3] = a.w;
+        sn[4 * c] = b.x; sn[4 * c + 1] = b.y; sn[4 * c + 2] = b.z; sn[4 * c + 3] = b.w;
+    }
+    uint32_t ow[16];
+#pragma unroll
+    for (int W = 0; W < 8; W++) {   // dims 4W..4W+3 and their partners + 32
+        uint32_t xw = 0, yw = 0;
+#pragma unroll
+        for (int b = 0; b < 4; b++) {
+            const int i = 4 * W + b;
+            const int x = sext8(kw[W], b), y = sext8(kw[W + 8], b);
+            const int c = (int)(int16_t)(cw[i >> 1] >> (16 * (i & 1))), s = (int)(int16_t)(sn[i >> 1] >> (16 * (i & 1)));
+            xw |= (uint32_t)(uint8_t)clamp127(sra_rne32(x * c - y * s, 15)) << (8 * b);
+            yw |= (uint32_t)(uint8_t)clamp127(sra_rne32(x * s + y * c, 15)) << (8 * b);
+        }
+        ow[4 * (W & 3) + (W >> 2)] = xw;
+        ow[4 * ((W + 8) & 3) + ((W + 8) >> 2)] = yw;
+    }
+    uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+#pragma unroll
+    for (int c = 0; c < 4; c++) d4[c] = make_uint4(ow[4 * c], ow[4 * c + 1], ow[4 * c + 2], ow[4 * c + 3]);
+}
+
 template <int BN, int STAGES, int EPI, int RQ>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-          const __grid_constant__ CUtensorMap map_o, int M, int N, int K, Requant rqp, int *__restrict__ err) {
+          const __grid_constant__ CUtensorMap map_o, int M, int N, int K, Requant rqp, int *__restrict__ err,
+          KvSplit kvs) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     constexpr int A_BYTES = TC_BM * TC_BK;
@@ -264,7 +305,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                             __syncwarp();
                             if (lane == 0) mbar_arrive(&tempty[b]);
                         }
-                        if (EPI == kEpiRequant) {   // 32 bytes: chunks 2gi, 2gi+1
+                        if (EPI == kEpiRequant || EPI == kEpiRequantKv) {   // 32 bytes: chunks 2gi, 2gi+1
                             uint32_t w[8];
 #pragma unroll
                             for (int j = 0; j < 8; j++) {
@@ -300,6 +341,42 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                                            pack4(y[8], y[9], y[10], y[11]), pack4(y[12], y[13], y[14], y[15]));
                         }
                     }
+                }
+                if (EPI == kEpiRequantKv && n0 + ch * EpiShape<EPI>::kAccCols == kvs.d) {
+                    // the key (hf 0) and value (hf 1) columns go to the split layout instead
+                    // of the output; each warp reads only its own staging buffer, so the two
+                    // need no barrier (splitting the key between them behind one was slower)
+                    __syncwarp();
+                    const int row = m0 + 32 * q + lane;
+                    uint32_t voff = 0;   // byte offset in kv of this row's value bytes (dim 0)
+                    if (row < M) {
+                        const int c = kvs.rowchunk[row], r0 = kvs.chunk_row0[c];
+                        const int p = row - r0;
+                        const size_t base = ((size_t)r0 + 32 * (size_t)c) * 128;
+                        if (hf == 0) {
+                            kv_store_key(sbuf0 + nb * TC_STAGE_OUT + lane * 64, (lane >> 1) & 3,
+                                         kvs.rope_cos + p * kHalfDim, kvs.rope_sin + p * kHalfDim,
+                                         kvs.kv + base + (size_t)p * 64);
+                        } else {
+                            const int npad = (kvs.chunk_len[c] + 31) & ~31;
+                            voff = (uint32_t)(base + (size_t)npad * 64 + (size_t)(p >> 5) * 2048 +
+                                              ((p & 31) >> 2) * 256 + (p & 3));
+                        }
+                    }
+                    if (hf == 1) {   // value dims 2l, 2l + 1 of each row to bytes 8l, 8l + 4 of its group
+                        const uint8_t *sv = sbuf0 + nb * TC_STAGE_OUT;
+                        const int nrow = min(32, M - (m0 + 32 * q));
+#pragma unroll 4
+                        for (int r = 0; r < nrow; r++) {
+                            const uint32_t o = __shfl_sync(0xffffffffu, voff, r);
+                            const uint16_t v2 = *reinterpret_cast<const uint16_t *>(
+                                sv + r * 64 + (((lane >> 3) ^ ((r >> 1) & 3)) << 4) + 2 * (lane & 7));
+                            kvs.kv[o + 8 * lane] = (int8_t)(v2 & 0xFFu);
+                            kvs.kv[o + 8 * lane + 4] = (int8_t)(v2 >> 8);
+                        }
+                    }
+                    __syncwarp();   // the staging buffer stays this warp's: no store was issued
+                    continue;
                 }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
@@ -368,7 +445,7 @@ Requant make_requant(int mult, int shift) {
 
 template <int BN, int EPI>
 bool launch_tc(const TcMatrix &A, const TcMatrix &B, int M, int N, int K, int mult, int shift, void *out,
-               int ldo, int *err, cudaStream_t st) {
+               int ldo, int *err, cudaStream_t st, const KvSplit &kvs = KvSplit{}) {
     alignas(64) CUtensorMap omap;
     const int eb = EPI == kEpiInt32 ? 4 : 1;
     const uint64_t cols = EPI == kEpiReglu ? (uint64_t)N / 2 : (uint64_t)N;
@@ -380,13 +457,13 @@ bool launch_tc(const TcMatrix &A, const TcMatrix &B, int M, int N, int K, int mu
     const CUtensorMap &mb = *reinterpret_cast<const CUtensorMap *>(B.map);
     constexpr int S = TcCfg<BN>::kStages;
     if (EPI != kEpiInt32 && q.mode == 3)
-        launch_k(k_gemm_tc<BN, S, EPI, 3>, grid, TC_THREADS, TcCfg<BN>::kSmem, st, ma, mb, omap, M, N, K, q, err);
+        launch_k(k_gemm_tc<BN, S, EPI, 3>, grid, TC_THREADS, TcCfg<BN>::kSmem, st, ma, mb, omap, M, N, K, q, err, kvs);
     else if (EPI == kEpiInt32 || q.mode == 2)
-        launch_k(k_gemm_tc<BN, S, EPI, 2>, grid, TC_THREADS, TcCfg<BN>::kSmem, st, ma, mb, omap, M, N, K, q, err);
+        launch_k(k_gemm_tc<BN, S, EPI, 2>, grid, TC_THREADS, TcCfg<BN>::kSmem, st, ma, mb, omap, M, N, K, q, err, kvs);
     else if (q.mode == 1)
-        launch_k(k_gemm_tc<BN, S, EPI, 1>, grid, TC_THREADS, TcCfg<BN>::kSmem, st, ma, mb, omap, M, N, K, q, err);
+        launch_k(k_gemm_tc<BN, S, EPI, 1>, grid, TC_THREADS, TcCfg<BN>::kSmem, st, ma, mb, omap, M, N, K, q, err, kvs);
     else
-        launch_k(k_gemm_tc<BN, S, EPI, 0>, grid, TC_THREADS, TcCfg<BN>::kSmem, st, ma, mb, omap, M, N, K, q, err);
+        launch_k(k_gemm_tc<BN, S, EPI, 0>, grid, TC_THREADS, TcCfg<BN>::kSmem, st, ma, mb, omap, M, N, K, q, err, kvs);
     return true;
 }
 
@@ -407,6 +484,7 @@ void set_attr() {
     set_attr_epi<BN, kEpiRequant>();
     set_attr_epi<BN, kEpiReglu>();
     set_attr_epi<BN, kEpiInt32>();
+    set_attr_epi<BN, kEpiRequantKv>();
 }
 
 }  // namespace
@@ -450,10 +528,15 @@ void gemm_tc_init() {
 }
 
 bool launch_gemm_tc(const TcMatrix &A, const TcMatrix &B, int M, int N, int K, int epi, int mult, int shift,
-                    void *out, int ldo, int *err, cudaStream_t st) {
+                    void *out, int ldo, int *err, cudaStream_t st, const KvSplit *kvs) {
     if (M <= 0) return true;
     const int bn = tc_bn_for(N);
     if (bn == 0 || (epi == kEpiReglu && bn != 256)) return false;
+    if (epi == kEpiRequantKv) {   // the key/value slice must be one whole 128-column slice
+        if (kvs == nullptr || kvs->d % 128 != 0 || N != kvs->d + 128) return false;
+        return bn == 256 ? launch_tc<256, kEpiRequantKv>(A, B, M, N, K, mult, shift, out, ldo, err, st, *kvs)
+                         : launch_tc<128, kEpiRequantKv>(A, B, M, N, K, mult, shift, out, ldo, err, st, *kvs);
+    }
     if (bn == 256) {
         if (epi == kEpiRequant) return launch_tc<256, kEpiRequant>(A, B, M, N, K, mult, shift, out, ldo, err, st);
         if (epi == kEpiReglu) return launch_tc<256, kEpiReglu>(A, B, M, N, K, mult, shift, out, ldo, err, st);

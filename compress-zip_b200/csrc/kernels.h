@@ -47,7 +47,19 @@ void launch_kv_prep_split(const int8_t *qkv, int ldq, int d, const int *pos, con
 enum GemmEpilogue {
     kEpiRequant = 0,   // out int8 [M][ldo] = requant(acc)
     kEpiReglu = 1,     // B rows interleaved (gate_j, up_j): out int8 [M][ldo], column j
-    kEpiInt32 = 2      // out int32 [M][ldo]
+    kEpiInt32 = 2,     // out int32 [M][ldo]
+    kEpiRequantKv = 3  // the QKV projection: requant as kEpiRequant for the query columns
+                       // [0, d); the key and value columns [d, d + 128) go, the key
+                       // rotated, to the per-chunk split layout of k_kv_prep_split (KvSplit)
+};
+
+// Where kEpiRequantKv writes the keys and values: row r is position r - chunk_row0[c]
+// of chunk c = rowchunk[r]; the layout is k_kv_prep_split's (rows.cu).
+struct KvSplit {
+    const int *rowchunk = nullptr, *chunk_row0 = nullptr, *chunk_len = nullptr;
+    const int16_t *rope_cos = nullptr, *rope_sin = nullptr;
+    int8_t *kv = nullptr;
+    int d = 0;
 };
 
 // gemm_tc.cu: the GEMM on tcgen05 (kind::i8) with TMA-staged operands and
@@ -71,7 +83,7 @@ void head_cdf_init();
 bool launch_head_cdf(const TcMatrix &A, const TcMatrix &B, int M, int V, int K, const uint32_t *sym,
                      const uint16_t *lut4k, uint32_t c8, uint32_t total, uint2 *lohi, int *err, cudaStream_t st);
 bool launch_gemm_tc(const TcMatrix &A, const TcMatrix &B, int M, int N, int K, int epi, int mult, int shift,
-                    void *out, int ldo, int *err, cudaStream_t st);
+                    void *out, int ldo, int *err, cudaStream_t st, const KvSplit *kvs = nullptr);
 
 // the FP32 requantisation form (gemm_tc.cu, mode 3) of (mult, shift), or false
 bool requant_fp32(int mult, int shift, float *mf, float *c2, int *clamp_a);

@@ -252,6 +252,23 @@ def test_other_attention_kernels(shipped_path, shipped_oracle, oracle_mod, shipp
         eng.close()
 
 
+def test_kv_prep_kernel_path(shipped_path, shipped_oracle, oracle_mod, shipped_tokens, monkeypatch):
+    """The key rotation and the per-chunk K/V layout from k_kv_prep_split after a plain
+    requantising QKV GEMM (CZG_KV_EPILOGUE=0), in place of the QKV epilogue that writes
+    them (the default, which every other test runs), against the oracle."""
+    from compress_zip_b200.engine import Engine
+
+    monkeypatch.setenv("CZG_KV_EPILOGUE", "0")
+    eng = Engine.from_file(shipped_path, 0)
+    try:
+        _trace_equal(eng, shipped_oracle, oracle_mod, shipped_tokens[:300])
+        starts = _starts(len(shipped_tokens), 1024)
+        assert eng.compress_chunks(shipped_tokens, starts) == \
+            oracle_mod.compress_chunks(shipped_oracle, shipped_tokens, starts)
+    finally:
+        eng.close()
+
+
 @pytest.mark.parametrize("mode", ["ties", "flat", "extreme"])
 def test_cdf_edge_models(shipped_path, tmp_path, oracle_mod, shipped_tokens, mode):
     """CDF corner cases through real logits: tied maxima (first index wins),
