@@ -433,8 +433,10 @@ int load_model(czg_ctx *c, const uint8_t *bytes, size_t len) {
         const bool fuse = gemm_norm_supported(d) && !(fn && std::string(fn) == "0");
         float mf, c2;
         int ca;
-        L.fused_o = fuse && requant_fp32(L.out_mult, L.out_shift, &mf, &c2, &ca);
-        L.fused_down = fuse && requant_fp32(L.down_mult, L.down_shift, &mf, &c2, &ca);
+        // (the fused kernels use the FP32 requantisation, which needs |acc| < 2^29)
+        L.fused_o = fuse && (long long)d * 16256 < (1ll << 29) && requant_fp32(L.out_mult, L.out_shift, &mf, &c2, &ca);
+        L.fused_down = fuse && (long long)dffp * 16256 < (1ll << 29) &&
+                       requant_fp32(L.down_mult, L.down_shift, &mf, &c2, &ca);
     }
     {   // the first pre-norm depends on the token alone: one row per vocabulary entry
         std::vector<uint32_t> iota(V);

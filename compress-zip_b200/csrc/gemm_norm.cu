@@ -66,8 +66,8 @@ __device__ __forceinline__ void bar_quadrant(int q) {   // the 4 epilogue warps 
 
 // biased bits of the FP32 requantisation of an accumulator (gemm_tc.cu, rq_flt)
 __device__ __forceinline__ int rq_bits(int acc, const GnArgs &a) {
-    const int x = min(max(acc, -a.clamp_a), a.clamp_a);
-    return __float_as_int(__fmaf_rn(__int_as_float((int)(kM1Bits + (uint32_t)x)), a.mf, a.c2));
+    const int b = min(__viaddmax_s32(acc, (int)kM1Bits, (int)kM1Bits - a.clamp_a), (int)kM1Bits + a.clamp_a);
+    return __float_as_int(__fmaf_rn(__int_as_float(b), a.mf, a.c2));
 }
 
 struct GnNorm {
@@ -429,7 +429,7 @@ bool launch_gemm_norm(const TcMatrix &A, const TcMatrix &B, int M, int d, int K,
     if (M <= 0) return true;
     GnArgs ga{};
     if (!gemm_norm_supported(d) || B.box_rows != d / 2 || A.box_rows != TC_BM || K % TC_BK != 0 ||
-        !requant_fp32(mult, shift, &ga.mf, &ga.c2, &ga.clamp_a))
+        (long long)K * 16256 >= (1ll << 29) || !requant_fp32(mult, shift, &ga.mf, &ga.c2, &ga.clamp_a))
         return false;
     ga.post_w = post_w;
     ga.next_w = next_w;

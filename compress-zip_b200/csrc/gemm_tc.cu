@@ -59,9 +59,17 @@ struct Requant {
 };
 
 // mode 3: bits of the float M1 + requant(acc)
+// (the clamp to +-A and the bias as max(acc + bits(M1), bits(M1) - A), one fused
+// add-max, then min(., bits(M1) + A); |acc| < 2^29 keeps the sum inside int32)
 __device__ __forceinline__ uint32_t rq_flt(int acc, const Requant &q) {
-    const int a = min(max(acc, -q.clamp_a), q.clamp_a);
-    return __float_as_uint(__fmaf_rn(__int_as_float((int)(kM1Bits + (uint32_t)a)), q.mf, q.c2));
+    const int b = min(__viaddmax_s32(acc, (int)kM1Bits, (int)kM1Bits - q.clamp_a), (int)kM1Bits + q.clamp_a);
+    return __float_as_uint(__fmaf_rn(__int_as_float(b), q.mf, q.c2));
+}
+// mode 3 with mult > 0, a ReGLU gate: the float M1 + max(requant(acc), 0), which is
+// M1 + requant(max(acc, 0)) since requant is then non-decreasing with requant(0) = 0
+__device__ __forceinline__ float rq_gate_pos(int acc, const Requant &q) {
+    const int b = min(__viaddmax_s32(acc, (int)kM1Bits, (int)kM1Bits), (int)kM1Bits + q.clamp_a);
+    return __fmaf_rn(__int_as_float(b), q.mf, q.c2);
 }
 
 template <int RQ>
@@ -322,18 +330,28 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                                     make_uint4(w[4 * hh], w[4 * hh + 1], w[4 * hh + 2], w[4 * hh + 3]);
                         } else {   // ReGLU on (gate_j, up_j) = columns (2j, 2j+1) (reglu.rs:20-46): 16 bytes, chunk gi
                             int y[16];
+                            if (RQ == 3 && rqp.mult > 0) {   // y = M1 + rne(g * u / 128), g = max(gate, 0), in FP32, exact
 #pragma unroll
-                            for (int j = 0; j < 16; j++) {
-                                if (RQ == 3) {   // y = M1 + rne(max(g, 0) * u / 128) in FP32, exact
-                                    const float gb = __uint_as_float(rq_flt((int)v[2 * j], rqp));
+                                for (int j = 0; j < 16; j++) {
+                                    const float gate = __fsub_rn(rq_gate_pos((int)v[2 * j], rqp), kM1);
                                     const float ub = __uint_as_float(rq_flt((int)v[2 * j + 1], rqp));
-                                    const float gate = fmaxf(__fsub_rn(gb, kM1), 0.0f);
                                     const float u128 = __fmaf_rn(ub, 0.0078125f, -98304.0f);   // (ub - M1) / 128
                                     y[j] = __float_as_int(__fmaf_rn(gate, u128, kM1));
-                                } else {
-                                    const int gte = max(rq<RQ>((int)v[2 * j], rqp), 0);
-                                    const int x = gte * rq<RQ>((int)v[2 * j + 1], rqp);   // |x| <= 127 * 127
-                                    y[j] = (x + 63 + ((x >> 7) & 1)) >> 7;                  // |y| <= 126: no clamp
+                                }
+                            } else {
+#pragma unroll
+                                for (int j = 0; j < 16; j++) {
+                                    if (RQ == 3) {
+                                        const float gb = __uint_as_float(rq_flt((int)v[2 * j], rqp));
+                                        const float ub = __uint_as_float(rq_flt((int)v[2 * j + 1], rqp));
+                                        const float gate = fmaxf(__fsub_rn(gb, kM1), 0.0f);
+                                        const float u128 = __fmaf_rn(ub, 0.0078125f, -98304.0f);
+                                        y[j] = __float_as_int(__fmaf_rn(gate, u128, kM1));
+                                    } else {
+                                        const int gte = max(rq<RQ>((int)v[2 * j], rqp), 0);
+                                        const int x = gte * rq<RQ>((int)v[2 * j + 1], rqp);   // |x| <= 127 * 127
+                                        y[j] = (x + 63 + ((x >> 7) & 1)) >> 7;                  // |y| <= 126: no clamp
+                                    }
                                 }
                             }
                             *reinterpret_cast<uint4 *>(sb + ((gi ^ sw) << 4)) =
@@ -456,9 +474,11 @@ bool launch_tc(const TcMatrix &A, const TcMatrix &B, int M, int N, int K, int mu
     const CUtensorMap &ma = *reinterpret_cast<const CUtensorMap *>(A.map);
     const CUtensorMap &mb = *reinterpret_cast<const CUtensorMap *>(B.map);
     constexpr int S = TcCfg<BN>::kStages;
-    if (EPI != kEpiInt32 && q.mode == 3)
+    // the FP32 form adds bits(M1) to the raw accumulator: |acc| <= K * 128 * 127 < 2^29
+    const bool fp32 = q.mode == 3 && (long long)K * 16256 < (1ll << 29);
+    if (EPI != kEpiInt32 && fp32)
         launch_k(k_gemm_tc<BN, S, EPI, 3>, grid, TC_THREADS, TcCfg<BN>::kSmem, st, ma, mb, omap, M, N, K, q, err, kvs);
-    else if (EPI == kEpiInt32 || q.mode == 2)
+    else if (EPI == kEpiInt32 || q.mode == 2 || q.mode == 3)
         launch_k(k_gemm_tc<BN, S, EPI, 2>, grid, TC_THREADS, TcCfg<BN>::kSmem, st, ma, mb, omap, M, N, K, q, err, kvs);
     else if (q.mode == 1)
         launch_k(k_gemm_tc<BN, S, EPI, 1>, grid, TC_THREADS, TcCfg<BN>::kSmem, st, ma, mb, omap, M, N, K, q, err, kvs);
