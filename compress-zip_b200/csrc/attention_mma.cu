@@ -129,11 +129,12 @@ __device__ __forceinline__ int score_flt(int dot_b, float mf, float c2) {
     const float ub = __fmaf_rn(__int_as_float(dot_b), 0.25f, 9437184.0f);
     return __float_as_int(__fmaf_rn(ub, mf, c2));   // biased: kM1Bits + score
 }
-// t256 of a (non-negative) difference of two biased scores, clamped at 4096
+// t256 of a (non-negative) difference of two biased scores, clamped at 4096 (the
+// bias removal and the clamp as one fused add-min)
 __device__ __forceinline__ uint32_t t256_flt(int pm_b, int sc_b) {
     const float neg = __fsub_rn(__int_as_float(pm_b), __int_as_float(sc_b));   // exact
-    const uint32_t tb = (uint32_t)__float_as_int(__fmaf_rn(neg, 378194.0f / 16777216.0f, 12582912.0f));
-    return min(tb, kM1Bits + 4096u) - kM1Bits;
+    const int tb = __float_as_int(__fmaf_rn(neg, 378194.0f / 16777216.0f, 12582912.0f));
+    return (uint32_t)__viaddmin_s32(tb, -(int)kM1Bits, 4096);
 }
 
 // One rescale of a state value by a record's factor e (attention.rs:252-259):
@@ -158,7 +159,8 @@ __device__ __forceinline__ int perm_key(int n) {
 
 struct Tile {
     uint32_t w[8];    // weights of the row's 8 entries (keys kb + 8t + i)
-    uint32_t ef[8];   // 0, or (previous max - score) of a record (never 0)
+    uint32_t ef[8];   // (previous max - score) of a record (never 0); other entries: not read
+                      // (MODE 0 keeps the difference there, the other modes 0)
     uint32_t rm;      // records among this thread's entries (bit i = entry i)
     uint32_t rowmask; // records of the row in this tile (bit k = key kb + k)
 };
@@ -178,7 +180,8 @@ __device__ __forceinline__ void tile_softmax(const int (&sacc)[4][4], int kb, in
             if (MASKED) valid = kb + 8 * t + i <= prow && prow < n;
             sc[i] = valid ? score_flt(sacc[i >> 1][i & 1], mf, c2) : INT32_MIN;
         }
-        const int x = max(max(max(sc[0], sc[1]), max(sc[2], sc[3])), max(max(sc[4], sc[5]), max(sc[6], sc[7])));
+        const int x = __vimax3_s32(__vimax3_s32(sc[0], sc[1], sc[2]), __vimax3_s32(sc[3], sc[4], sc[5]),
+                                   max(sc[6], sc[7]));
         const int y1 = __shfl_up_sync(0xffffffffu, x, 1, 4);
         const int y2 = __shfl_up_sync(0xffffffffu, x, 2, 4);
         const int y3 = __shfl_up_sync(0xffffffffu, x, 3, 4);
@@ -189,19 +192,23 @@ __device__ __forceinline__ void tile_softmax(const int (&sacc)[4][4], int kb, in
         if (t >= 2) pm = max(pm, y2);
         if (t >= 3) pm = max(pm, y3);
         if (pm == INT32_MIN) pm = sc[0];
+        // an entry is a record iff (prefix max - score) < 0; its sign bits are shifted into
+        // rm in entry order (a funnel shift each), reversed once at the end.  The
+        // difference itself is kept for every entry: only records' values are read.
 #pragma unroll
         for (int i = 0; i < 8; i++) {
             bool valid = true;
             if (MASKED) valid = kb + 8 * t + i <= prow && prow < n;
-            int ef = min(pm - sc[i], 0);
+            int ef = pm - sc[i];
             if (MASKED) ef = valid ? ef : 0;
             pm = max(pm, sc[i]);
             uint32_t w = lut4k[t256_flt(pm, sc[i])];
             if (!EXP0) w = pm == sc[i] ? 65535u : w;
             T.w[i] = valid ? w : 0u;
             T.ef[i] = (uint32_t)ef;
-            rm |= ((uint32_t)ef >> (31 - i)) & (1u << i);
+            rm = __funnelshift_l((uint32_t)ef, rm, 1);
         }
+        rm = __brev(rm) >> 24;
         m = max(run, max(z1, __shfl_xor_sync(0xffffffffu, z1, 2)));
     } else if constexpr (MODE == 1) {
         // |scores| < 2^30, so every difference below fits int32.  The running max is
