@@ -659,10 +659,9 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
         launch_rows(d_tok, c->chunk_row0, c->chunk_len, c->chunk_tok0, nc, V, c->tok_in, c->tok_out,
                     c->pos, c->rowchunk, c->err_flag, st);
     });
-    timed(c, kEmbedNorm, [&] {
-        launch_embed_norm(c->tok_in, c->embed, c->layers[0].attn_norm, M, d, c->inv_tab, c->x_res, c->res16, false,
-                          c->xn, st);
-    });
+    // the first pre-norm from the per-token table (the residual of layer 0 is re-read
+    // from the embedding by the first residual norm)
+    timed(c, kEmbedNorm, [&] { launch_xn_gather(c->tok_in, c->xn_tab, M, d, c->xn, st); });
     // tensor-core attention, K/V tiles streamed per warp from a per-chunk layout (at
     // 1024 keys 129.6 ms per configuration-1 step against 136.0 with the chunk's
     // K/V^T staged in shared memory, which CZG_ATTN_STAGED=1 selects up to 1024 keys)
@@ -1046,11 +1045,7 @@ int decompress_impl(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts
             while (active > 0 && (int)n_tokens[order[w0 + active - 1]] <= step) active--;
             const int M = active;
             // later steps find their first pre-norm output written by the previous step's decoder
-            if (step == 0)
-                timed(c, kEmbedNorm, [&] {
-                    launch_embed_norm(c->tok_in, c->embed, c->layers[0].attn_norm, M, d, c->inv_tab, c->x_res,
-                                      c->res16, false, c->xn, s);
-                });
+            if (step == 0) timed(c, kEmbedNorm, [&] { launch_xn_gather(c->tok_in, c->xn_tab, M, d, c->xn, s); });
             for (int l = 0; l < m.n_layers; l++) {
                 const LayerDev &L = c->layers[l];
                 int8_t *kvc = c->kvc + (size_t)l * layer_ld;

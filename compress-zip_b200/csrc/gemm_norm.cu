@@ -82,6 +82,15 @@ __device__ __forceinline__ int gn_norm_b(int x, int w, const GnNorm &n) {
     const int yb = __float_as_int(__fmaf_rn(__int_as_float(x * w + (int)kM1Bits), n.mf, n.c));
     return min(max(yb, (int)kM1Bits - 127), (int)kM1Bits + 127);
 }
+// the same without the clamp: the biased bits, whose low 16 bits are the int16 y, since
+// |y| <= 127 * 128 * 65535 / 2^15 < 2^15 (inv_tab entries are 16-bit)
+__device__ __forceinline__ int gn_norm_f(int x, int w, const GnNorm &n) {
+    return __float_as_int(__fmaf_rn(__int_as_float(x * w + (int)kM1Bits), n.mf, n.c));
+}
+// two such results as an int16 pair clamped to +-127
+__device__ __forceinline__ uint32_t gn_pair127(int f0, int f1) {
+    return __vmaxs2(__vmins2(__byte_perm(f0, f1, 0x5410), 0x007F007Fu), 0xFF81FF81u);
+}
 // byte b of w sign-extended: prmt's default mode copies byte b and replicates its sign
 __device__ __forceinline__ int sx8(uint32_t w, int b) {
     uint32_t r;
@@ -348,6 +357,49 @@ k_gemm_norm(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ C
                 const uint8_t *srow = o_s + (32 * q + rl) * C::PITCH;
                 RT *xr = reinterpret_cast<RT *>(ga.x_res) + (size_t)grow * D;
                 const bool live = grow < M && alive;
+                int8_t *xo = ga.xn + (size_t)grow * D;
+                if constexpr (sizeof(RT) == 2 && D <= 384) {
+                    // int16 residual: the adds and clamps on int16 pairs (vadd as a 16x2
+                    // add-max against -32768, vmin / vmax), the clamped row as bytes for a
+                    // dp4a sum of squares and the next norm (-8% at d = 384; at d = 512 the
+                    // O projection's kernel measured 9% slower this way, so it keeps the
+                    // per-element form)
+                    uint32_t cb[NW];
+                    int ss2 = 0;
+#pragma unroll
+                    for (int j = 0; j < NW; j++) {
+                        const int col = 4 * lane + 128 * j;
+                        const uint32_t ov = *reinterpret_cast<const uint32_t *>(srow + col);
+                        uint32_t r01, r23;
+                        if constexpr (MODE == kGnFromEmbed) {   // embedding bytes to int16 pairs (prmt
+                            // with sign replication; __byte_perm would ignore the selectors' top bits)
+                            asm("prmt.b32 %0, %1, 0, 0x9180;" : "=r"(r01) : "r"((uint32_t)cur[j]));
+                            asm("prmt.b32 %0, %1, 0, 0xB3A2;" : "=r"(r23) : "r"((uint32_t)cur[j]));
+                        } else {
+                            r01 = cur[j].x;
+                            r23 = cur[j].y;
+                        }
+                        const uint32_t y01 = gn_pair127(gn_norm_f(sx8(ov, 0), w1[j][0], n1), gn_norm_f(sx8(ov, 1), w1[j][1], n1));
+                        const uint32_t y23 = gn_pair127(gn_norm_f(sx8(ov, 2), w1[j][2], n1), gn_norm_f(sx8(ov, 3), w1[j][3], n1));
+                        r01 = (uint32_t)__viaddmax_s16x2((int)r01, (int)y01, (int)0x80008000u);   // exact: |res| < 2^15
+                        r23 = (uint32_t)__viaddmax_s16x2((int)r23, (int)y23, (int)0x80008000u);
+                        if (MODE != kGnNoStore && live) *reinterpret_cast<uint2 *>(xr + col) = make_uint2(r01, r23);
+                        const uint32_t c01 = __vmaxs2(__vmins2(r01, 0x007F007Fu), 0xFF81FF81u);
+                        const uint32_t c23 = __vmaxs2(__vmins2(r23, 0x007F007Fu), 0xFF81FF81u);
+                        cb[j] = __byte_perm(c01, c23, 0x6420);
+                        ss2 = __dp4a((int)cb[j], (int)cb[j], ss2);
+                    }
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) ss2 += __shfl_xor_sync(0xffffffffu, ss2, o);
+                    const GnNorm n2 = gn_norm(ss2, ga.inv_tab, D);
+#pragma unroll
+                    for (int j = 0; j < NW; j++) {
+                        const uint32_t g01 = gn_pair127(gn_norm_f(sx8(cb[j], 0), w2[j][0], n2), gn_norm_f(sx8(cb[j], 1), w2[j][1], n2));
+                        const uint32_t g23 = gn_pair127(gn_norm_f(sx8(cb[j], 2), w2[j][2], n2), gn_norm_f(sx8(cb[j], 3), w2[j][3], n2));
+                        if (live) *reinterpret_cast<uint32_t *>(xo + 4 * lane + 128 * j) = __byte_perm(g01, g23, 0x6420);
+                    }
+                    continue;
+                }
                 int cr[NW][4];
                 int ss2 = 0;
 #pragma unroll
@@ -368,7 +420,6 @@ k_gemm_norm(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ C
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) ss2 += __shfl_xor_sync(0xffffffffu, ss2, o);
                 const GnNorm n2 = gn_norm(ss2, ga.inv_tab, D);
-                int8_t *xo = ga.xn + (size_t)grow * D;
 #pragma unroll
                 for (int j = 0; j < NW; j++) {
                     const uint32_t yw = pk4(gn_norm_b(cr[j][0], w2[j][0], n2), gn_norm_b(cr[j][1], w2[j][1], n2),

@@ -30,6 +30,9 @@ void launch_inv_table(int eps, uint16_t *tab, cudaStream_t st);
 void launch_embed_norm(const uint32_t *tok_in, const int8_t *embed, const int8_t *norm_w, int M,
                        int d, const uint16_t *inv_tab, void *x_res, bool res16, bool store_res, int8_t *xn,
                        cudaStream_t st);
+// xn[r] = xn_tab[tok_in[r]]: the first pre-norm output from the per-token table of
+// normalised embedding rows (d % 16 == 0)
+void launch_xn_gather(const uint32_t *tok_in, const int8_t *xn_tab, int M, int d, int8_t *xn, cudaStream_t st);
 // embed != nullptr: the residual input is embed[tok_in[r]] instead of x_res;
 // store_res false: the updated residual is not written back (the model's last norm)
 void launch_residual_norm(const int8_t *o, const int8_t *post_w, const int8_t *next_w, int M, int d,

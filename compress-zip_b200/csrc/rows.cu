@@ -263,6 +263,18 @@ __global__ void k_kv_prep_split(const int8_t *__restrict__ qkv, int ldq, int d, 
     vt[(2 * i + 1) * 4] = k[64 + 2 * i + 1];
 }
 
+// xn[r] = xn_tab[tok_in[r]], 16 bytes per thread (the table, V x d bytes, stays in L2)
+__global__ void k_xn_gather(const uint32_t *__restrict__ tok_in, const int8_t *__restrict__ xn_tab, int M,
+                            int chunks, int8_t *__restrict__ xn) {
+    pdl_wait();
+    pdl_trigger();
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)M * chunks) return;
+    const int row = (int)(i / chunks), c = (int)(i % chunks);
+    const uint4 *src = reinterpret_cast<const uint4 *>(xn_tab) + (size_t)tok_in[row] * chunks + c;
+    reinterpret_cast<uint4 *>(xn)[(size_t)row * chunks + c] = __ldg(src);
+}
+
 // ---- host launchers -------------------------------------------------------
 
 void launch_rows(const uint32_t *tokens, const int *chunk_row0, const int *chunk_len,
@@ -328,6 +340,13 @@ void launch_embed_norm(const uint32_t *tok_in, const int8_t *embed, const int8_t
         if (store_res) embed_norm_t<int32_t, true>(tok_in, embed, norm_w, M, d, inv_tab, static_cast<int32_t *>(x_res), xn, st);
         else embed_norm_t<int32_t, false>(tok_in, embed, norm_w, M, d, inv_tab, static_cast<int32_t *>(x_res), xn, st);
     }
+}
+
+void launch_xn_gather(const uint32_t *tok_in, const int8_t *xn_tab, int M, int d, int8_t *xn, cudaStream_t st) {
+    if (M == 0) return;
+    const int chunks = d / 16;
+    const long long n = (long long)M * chunks;
+    launch_k(k_xn_gather, (unsigned)((n + 255) / 256), 256, 0, st, tok_in, xn_tab, M, chunks, xn);
 }
 
 void launch_residual_norm(const int8_t *o, const int8_t *post_w, const int8_t *next_w, int M, int d,
