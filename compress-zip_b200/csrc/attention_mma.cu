@@ -45,6 +45,7 @@ constexpr int AM_THREADS = 512;
 constexpr int AM_WARPS = AM_THREADS / 32;
 constexpr int AM_MAX_KEYS = 1024;
 constexpr int AM_ROWS = 8;   // query rows per warp task
+constexpr int AM_TASK_BATCH = 4;   // streamed kernel: consecutive tasks per counter increment
 constexpr int AM_LUT = 4104;   // exp table entries (t256 0..4096, padded)
 // per warp: record differences by key [8][32], output staging [8][64]
 constexpr int AM_WARP_SMEM = AM_ROWS * 32 * 4 + AM_ROWS * 64;
@@ -336,6 +337,14 @@ __device__ __forceinline__ void decode_tile_async(uint8_t *stage, const int8_t *
 // each warp copies its task's 32-key tiles (K rows, then the V tile: 4 KB) into a
 // two-stage shared-memory ring with cp.async, the next tile's copy overlapping the
 // current tile's work; the fragments then come from the tile as in the decode kernel.
+// Nothing of a chunk is staged per CTA, so with gtask given the STREAM kernel is
+// persistent: every warp of the grid takes tasks from one counter in global memory
+// (gtask, zero at launch), chunk by chunk (longest chunks first) and in each chunk
+// longest rows first, task t = (chunk t / (rb_max H), row block rb_max - 1 -
+// (t mod rb_max H) / H, head t mod H); row blocks beyond a shorter chunk's end are
+// empty tasks.  Only the two or three chunks the warps are on are read at a time, so
+// their K/V stay in L2, and no SM idles in a last round of CTAs.  Without gtask, one
+// CTA per chunk as the staged kernel.
 template <int MODE, bool EXP0, bool STREAM>
 __global__ void __launch_bounds__(AM_THREADS, 1)
 k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restrict__ kv_g,
@@ -343,12 +352,13 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
                 const int32_t *__restrict__ score_mult, const int8_t *__restrict__ sink_key,
                 const int16_t *__restrict__ rope_cos, const int16_t *__restrict__ rope_sin,
                 const uint16_t *__restrict__ lut4k_g, int8_t *__restrict__ out, int ldo,
-                const int *__restrict__ chunk_kvoff) {
+                const int *__restrict__ chunk_kvoff, int *__restrict__ gtask, int n_chunks, int rb_max) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ int task_ctr;
-    const int c = blockIdx.x;
-    const int r0 = chunk_row0[c], n = chunk_len[c];
-    const int npad = (n + 31) & ~31;
+    const bool queue = STREAM && gtask != nullptr;   // persistent, global task queue
+    int c = queue ? 0 : blockIdx.x;
+    int r0 = chunk_row0[c], n = chunk_len[c];
+    int npad = (n + 31) & ~31;
     const int vt_ld = ((npad + 127) & ~127) + 32;   // 8 dims of a fragment land on distinct banks
     uint8_t *ks = smem;                              // [npad][64], dims permuted per thread quarter
     uint8_t *vt = ks + npad * 64;                    // [64][vt_ld], keys in order
@@ -364,6 +374,8 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
     uint8_t *ring = reinterpret_cast<uint8_t *>(lut_s + AM_LUT) + warp * 8192;
     const int8_t *kg = STREAM ? kv_g + (size_t)chunk_kvoff[c] * 128 : nullptr;
     const int8_t *vg = STREAM ? kg + (size_t)npad * 64 : nullptr;
+    const int per_chunk = rb_max * n_heads;   // STREAM: tasks per chunk in the global order
+    const int g_tasks = n_chunks * per_chunk;
 
     // K row layout: bytes [16t' + 4k + b] = dim 16k + 4t' + b, so thread t reads its
     // four B words (dims 4t, 16+4t, 32+4t, 48+4t) as one 16-byte load.
@@ -387,13 +399,38 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
     const uint32_t ones[4] = {0x01010101u, 0x01010101u, 0x01010101u, 0x01010101u};
     const int n_rb = (n + AM_ROWS - 1) / AM_ROWS;
     const int n_tasks = n_rb * n_heads;
+    // STREAM: the warp takes AM_TASK_BATCH consecutive tasks per atomic (fewer round
+    // trips to one counter), and lane 0 reserves its next batch while the current one runs
+    int base = 0, sub = AM_TASK_BATCH;
+    int next = (queue && lane == 0) ? atomicAdd(gtask, AM_TASK_BATCH) : 0;
     for (;;) {
-        int task = 0;
-        if (lane == 0) task = atomicAdd(&task_ctr, 1);
-        task = __shfl_sync(0xffffffffu, task, 0);
-        if (task >= n_tasks) break;
-        const int rb = n_rb - 1 - task / n_heads;   // longest rows first
-        const int h = task % n_heads;
+        int task = 0, rb, h;
+        if (queue) {
+            if (sub == AM_TASK_BATCH) {
+                base = __shfl_sync(0xffffffffu, next, 0);
+                sub = 0;
+                if (lane == 0) next = atomicAdd(gtask, AM_TASK_BATCH);
+            }
+            task = base + sub++;
+            if (task >= g_tasks) break;
+            c = task / per_chunk;
+            const int u = task - c * per_chunk;
+            n = chunk_len[c];
+            r0 = chunk_row0[c];
+            const int kvoff = chunk_kvoff[c];
+            rb = rb_max - 1 - u / n_heads;   // longest rows first
+            if (rb >= (n + AM_ROWS - 1) / AM_ROWS) continue;   // beyond this chunk's end
+            h = u % n_heads;
+            npad = (n + 31) & ~31;
+            kg = kv_g + (size_t)kvoff * 128;
+            vg = kg + (size_t)npad * 64;
+        } else {
+            if (lane == 0) task = atomicAdd(&task_ctr, 1);
+            task = __shfl_sync(0xffffffffu, task, 0);
+            if (task >= n_tasks) break;
+            rb = n_rb - 1 - task / n_heads;   // longest rows first
+            h = task % n_heads;
+        }
         const int p0 = rb * AM_ROWS;
         const int prow = p0 + g;                     // the QK / softmax row of this thread
         const int p_last = min(p0 + AM_ROWS - 1, n - 1);
@@ -903,52 +940,66 @@ void launch_attention_mma(const int8_t *qkv, int ldq, const int8_t *kv, const in
         if (exp0)
             k_attention_mma<1, true, false><<<n_chunks, AM_THREADS, smem, st>>>(
                 qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
-                lut4k, out, ldo, nullptr);
+                lut4k, out, ldo, nullptr, nullptr, n_chunks, 0);
         else
             k_attention_mma<1, false, false><<<n_chunks, AM_THREADS, smem, st>>>(
                 qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
-                lut4k, out, ldo, nullptr);
+                lut4k, out, ldo, nullptr, nullptr, n_chunks, 0);
     } else if (score_mode == 2)
         k_attention_mma<2, false, false><<<n_chunks, AM_THREADS, smem, st>>>(
             qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
-            lut4k, out, ldo, nullptr);
+            lut4k, out, ldo, nullptr, nullptr, n_chunks, 0);
     else if (exp0)
         k_attention_mma<0, true, false><<<n_chunks, AM_THREADS, smem, st>>>(
             qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
-            lut4k, out, ldo, nullptr);
+            lut4k, out, ldo, nullptr, nullptr, n_chunks, 0);
     else
         k_attention_mma<0, false, false><<<n_chunks, AM_THREADS, smem, st>>>(
             qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
-            lut4k, out, ldo, nullptr);
+            lut4k, out, ldo, nullptr, nullptr, n_chunks, 0);
 }
 
 void launch_attention_mma_stream(const int8_t *qkv, int ldq, const int8_t *kv, const int *chunk_row0,
-                                 const int *chunk_len, const int *chunk_kvoff, int n_chunks, int n_heads,
+                                 const int *chunk_len, const int *chunk_kvoff, int n_chunks, int max_len, int n_heads,
                                  const int32_t *score_mult, const int8_t *sink_key, const int16_t *rope_cos,
                                  const int16_t *rope_sin, const uint16_t *lut4k, int score_mode, bool exp0,
-                                 int8_t *out, int ldo, cudaStream_t st) {
-    if (n_chunks == 0) return;
+                                 int8_t *out, int ldo, int *task_ctr, cudaStream_t st) {
+    if (n_chunks == 0 || max_len <= 0) return;
+    const int rb_max = (max_len + AM_ROWS - 1) / AM_ROWS;
+    // the global queue from chunks of 1024 keys on (per 3 M-token sample: ctx 1024
+    // -1.9%, ctx 4096 -27%); at ctx 512 its short tasks ran 2-3% slower than one CTA
+    // per chunk, whose last round is then a small part of ~20 (CZG_ATTN_QUEUE=0 / 1)
+    const char *qe = getenv("CZG_ATTN_QUEUE");
+    const bool queue = qe ? qe[0] != '0' : max_len >= 1024;
+    int grid = n_chunks;
+    if (queue) {
+        cudaMemsetAsync(task_ctr, 0, sizeof(int), st);
+        const long long tasks = (long long)n_chunks * rb_max * n_heads;
+        grid = (int)std::min<long long>((tasks + AM_WARPS - 1) / AM_WARPS, (long long)sm_count());
+    } else {
+        task_ctr = nullptr;
+    }
     if (score_mode == 1) {
         if (exp0)
-            k_attention_mma<1, true, true><<<n_chunks, AM_THREADS, AM_STREAM_SMEM, st>>>(
+            k_attention_mma<1, true, true><<<grid, AM_THREADS, AM_STREAM_SMEM, st>>>(
                 qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
-                lut4k, out, ldo, chunk_kvoff);
+                lut4k, out, ldo, chunk_kvoff, task_ctr, n_chunks, rb_max);
         else
-            k_attention_mma<1, false, true><<<n_chunks, AM_THREADS, AM_STREAM_SMEM, st>>>(
+            k_attention_mma<1, false, true><<<grid, AM_THREADS, AM_STREAM_SMEM, st>>>(
                 qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
-                lut4k, out, ldo, chunk_kvoff);
+                lut4k, out, ldo, chunk_kvoff, task_ctr, n_chunks, rb_max);
     } else if (score_mode == 2)
-        k_attention_mma<2, false, true><<<n_chunks, AM_THREADS, AM_STREAM_SMEM, st>>>(
+        k_attention_mma<2, false, true><<<grid, AM_THREADS, AM_STREAM_SMEM, st>>>(
             qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
-            lut4k, out, ldo, chunk_kvoff);
+            lut4k, out, ldo, chunk_kvoff, task_ctr, n_chunks, rb_max);
     else if (exp0)
-        k_attention_mma<0, true, true><<<n_chunks, AM_THREADS, AM_STREAM_SMEM, st>>>(
+        k_attention_mma<0, true, true><<<grid, AM_THREADS, AM_STREAM_SMEM, st>>>(
             qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
-            lut4k, out, ldo, chunk_kvoff);
+            lut4k, out, ldo, chunk_kvoff, task_ctr, n_chunks, rb_max);
     else
-        k_attention_mma<0, false, true><<<n_chunks, AM_THREADS, AM_STREAM_SMEM, st>>>(
+        k_attention_mma<0, false, true><<<grid, AM_THREADS, AM_STREAM_SMEM, st>>>(
             qkv, ldq, kv, chunk_row0, chunk_len, n_heads, score_mult, sink_key, rope_cos, rope_sin,
-            lut4k, out, ldo, chunk_kvoff);
+            lut4k, out, ldo, chunk_kvoff, task_ctr, n_chunks, rb_max);
 }
 
 bool attention_decode_mma_ok(int n_heads) { return n_heads >= 1 && n_heads <= AM_ROWS; }

@@ -106,6 +106,7 @@ struct czg_ctx {
     std::vector<void *> ws_allocs;
     uint32_t *tokens = nullptr, *tok_in = nullptr, *tok_out = nullptr;
     int *pos = nullptr, *x_res = nullptr, *err_flag = nullptr;
+    int *task_ctr = nullptr;   // the streamed attention's global task counter
     bool res16 = false;   // residual stream stored as int16 (exact for n_layers <= 128)
     int8_t *xn = nullptr, *qkv = nullptr, *kv = nullptr, *attn = nullptr, *o8 = nullptr, *hbuf = nullptr;
     int32_t *logits = nullptr;
@@ -487,7 +488,7 @@ int alloc_workspace(czg_ctx *c, int rows, int chunks) {
               dalloc_ws(c, &c->chunk_row0, (size_t)chunks) && dalloc_ws(c, &c->chunk_len, (size_t)chunks) &&
               dalloc_ws(c, &c->att_row0, (size_t)chunks) && dalloc_ws(c, &c->att_len, (size_t)chunks) &&
               dalloc_ws(c, &c->att_kvoff, (size_t)chunks) &&
-              dalloc_ws(c, &c->err_flag, 1);
+              dalloc_ws(c, &c->err_flag, 1) && dalloc_ws(c, &c->task_ctr, 1);
     if (!ok) return CZG_E_DEVICE;
     cudaMemsetAsync(c->err_flag, 0, sizeof(int), c->stream);
     c->cap_rows = rows;
@@ -702,9 +703,9 @@ int run_wave(czg_ctx *c, const uint32_t *d_tok, const uint64_t *starts, uint32_t
                                      L.score_mult, L.sink_key, c->rope_cos, c->rope_sin, c->lut4k,
                                      L.score_mode, c->exp0, c->attn, d, st);
             else if (stream)
-                launch_attention_mma_stream(c->qkv, d + 128, c->kv, c->att_row0, c->att_len, c->att_kvoff, nc, H,
-                                            L.score_mult, L.sink_key, c->rope_cos, c->rope_sin, c->lut4k,
-                                            L.score_mode, c->exp0, c->attn, d, st);
+                launch_attention_mma_stream(c->qkv, d + 128, c->kv, c->att_row0, c->att_len, c->att_kvoff, nc,
+                                            max_len, H, L.score_mult, L.sink_key, c->rope_cos, c->rope_sin,
+                                            c->lut4k, L.score_mode, c->exp0, c->attn, d, c->task_ctr, st);
             else
                 launch_attention(c->qkv, d + 128, c->kv, c->att_row0, c->att_len, nc, max_len, H,
                                  L.score_mult, L.sink_key, c->rope_cos, c->rope_sin, c->lut, c->attn, d, st);

@@ -124,12 +124,14 @@ void launch_attention_mma(const int8_t *qkv, int ldq, const int8_t *kv, const in
                           const int16_t *rope_sin, const uint16_t *lut4k, int score_mode, bool exp0,
                           int8_t *out, int ldo, cudaStream_t st);
 // Chunks of any length: K and V in the streaming layout of launch_kv_prep_split,
-// chunk i of the launch at chunk_kvoff[i] * 128 bytes of kv
+// chunk i of the launch at chunk_kvoff[i] * 128 bytes of kv; chunks longest first
+// (max_len = chunk 0's length); a persistent grid takes tasks from task_ctr (one
+// device int, zeroed here on the stream)
 void launch_attention_mma_stream(const int8_t *qkv, int ldq, const int8_t *kv, const int *chunk_row0,
-                                 const int *chunk_len, const int *chunk_kvoff, int n_chunks, int n_heads,
+                                 const int *chunk_len, const int *chunk_kvoff, int n_chunks, int max_len, int n_heads,
                                  const int32_t *score_mult, const int8_t *sink_key, const int16_t *rope_cos,
                                  const int16_t *rope_sin, const uint16_t *lut4k, int score_mode, bool exp0,
-                                 int8_t *out, int ldo, cudaStream_t st);
+                                 int8_t *out, int ldo, int *task_ctr, cudaStream_t st);
 // attention.cu: one CTA per chunk; rows of chunk c are chunk_row0[c] ..+chunk_len[c]
 void launch_attention(const int8_t *qkv, int ldq, const int8_t *kv, const int *chunk_row0,
                       const int *chunk_len, int n_chunks, int max_len, int n_heads,

@@ -252,6 +252,24 @@ def test_other_attention_kernels(shipped_path, shipped_oracle, oracle_mod, shipp
         eng.close()
 
 
+@pytest.mark.parametrize("queue", ["0", "1"])
+def test_streamed_attention_schedules(shipped_path, shipped_oracle, oracle_mod, shipped_tokens, monkeypatch, queue):
+    """The streamed chunk attention with one CTA per chunk (CZG_ATTN_QUEUE=0) and as a
+    persistent grid over a global task queue (CZG_ATTN_QUEUE=1; the default from
+    1024-key chunks on), on full and ragged chunks, against the oracle."""
+    from compress_zip_b200.engine import Engine
+
+    monkeypatch.setenv("CZG_ATTN_QUEUE", queue)
+    eng = Engine.from_file(shipped_path, 0)
+    try:
+        for C in (1024, 300):
+            starts = _starts(len(shipped_tokens), C)
+            assert eng.compress_chunks(shipped_tokens, starts) == \
+                oracle_mod.compress_chunks(shipped_oracle, shipped_tokens, starts)
+    finally:
+        eng.close()
+
+
 def test_kv_prep_kernel_path(shipped_path, shipped_oracle, oracle_mod, shipped_tokens, monkeypatch):
     """The key rotation and the per-chunk K/V layout from k_kv_prep_split after a plain
     requantising QKV GEMM (CZG_KV_EPILOGUE=0), in place of the QKV epilogue that writes
