@@ -515,14 +515,12 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
             }
             // V^T A fragments: dims 16mi+g / +8; K 4t.. (word 0) and 16+4t.. (word 1) = keys 8t..8t+7
             uint32_t va[4][4];
-            if (STREAM) {   // V tile [8 key groups][64 dims][4 keys]: words of groups 2t, 2t+1
-                const uint32_t *vtile = reinterpret_cast<const uint32_t *>(kst + 2048) + 2 * t * 64;
+            if (STREAM) {   // V tile, lane-major (vt_byte): the lane's 16 words as four 16-byte loads
+                const uint4 *vl = reinterpret_cast<const uint4 *>(kst + 2048) + 4 * lane;
 #pragma unroll
                 for (int mi = 0; mi < 4; mi++) {
-                    va[mi][0] = vtile[16 * mi + g];
-                    va[mi][1] = vtile[16 * mi + g + 8];
-                    va[mi][2] = vtile[64 + 16 * mi + g];
-                    va[mi][3] = vtile[64 + 16 * mi + g + 8];
+                    const uint4 v = vl[mi ^ ((lane >> 1) & 3)];
+                    va[mi][0] = v.x; va[mi][1] = v.y; va[mi][2] = v.z; va[mi][3] = v.w;
                 }
                 __syncwarp();   // every lane has its fragments: the stage may be refilled next tile
             } else {
@@ -639,7 +637,7 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
 
 // Decode: one warp per stream r, the query of every head at position p against
 // the stream's keys 0..p in the split cache layout (K rows of 64 permuted dims,
-// then V in 2 KB tiles of 32 keys as [8 key groups][64 dims][4 keys]).  The heads are the 8 rows of the attention tile (A rows
+// then V in 2 KB tiles of 32 keys in the lane-major layout of vt_byte, common.cuh).  The heads are the 8 rows of the attention tile (A rows
 // n_heads..15 are zero); everything else is the chunk kernel's tile step.
 // The warp also appends the stream's key p (RoPE) and value p, from columns kd..kd+127
 // of its qkv row, to the cache (the layout of k_kv_append, decode.cu) and patches
@@ -745,9 +743,9 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, int kd, int8_t *
         const int l2 = lane + kHalfDim;
         base[(size_t)p * 64 + 16 * ((lane >> 2) & 3) + 4 * (lane >> 4) + (lane & 3)] = (int8_t)kx;
         base[(size_t)p * 64 + 16 * ((l2 >> 2) & 3) + 4 * (l2 >> 4) + (l2 & 3)] = (int8_t)ky;
-        int8_t *vt = base + len * 64 + (size_t)(p >> 5) * 2048 + ((p & 31) >> 2) * 256 + (p & 3);
-        vt[(2 * lane) * 4] = (int8_t)(v2 & 0xFFu);
-        vt[(2 * lane + 1) * 4] = (int8_t)(v2 >> 8);
+        int8_t *vt = base + len * 64 + (size_t)(p >> 5) * 2048;   // the V tile of key p
+        vt[vt_byte(p & 31, 2 * lane)] = (int8_t)(v2 & 0xFFu);
+        vt[vt_byte(p & 31, 2 * lane + 1)] = (int8_t)(v2 >> 8);
     }
     int m = INT32_MIN;
     unsigned long long s_state[2] = {0, 0};
@@ -782,9 +780,9 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, int kd, int8_t *
             const int l2 = lane + kHalfDim, kp = p & 31;
             kst[kp * 64 + 16 * ((lane >> 2) & 3) + 4 * (lane >> 4) + (lane & 3)] = (uint8_t)kvw;
             kst[kp * 64 + 16 * ((l2 >> 2) & 3) + 4 * (l2 >> 4) + (l2 & 3)] = (uint8_t)(kvw >> 8);
-            uint8_t *vs = kst + 2048 + (kp >> 2) * 256 + (kp & 3);
-            vs[(2 * lane) * 4] = (uint8_t)(kvw >> 16);
-            vs[(2 * lane + 1) * 4] = (uint8_t)(kvw >> 24);
+            uint8_t *vs = kst + 2048;
+            vs[vt_byte(kp, 2 * lane)] = (uint8_t)(kvw >> 16);
+            vs[vt_byte(kp, 2 * lane + 1)] = (uint8_t)(kvw >> 24);
             __syncwarp();
         }
         int sacc[4][4];
@@ -797,13 +795,11 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, int kd, int8_t *
         }
         // V^T A fragments: word (group 2t or 2t+1 = keys 8t..8t+3 / 8t+4..8t+7, dim)
         uint32_t va[4][4];
-        const uint32_t *vtile = reinterpret_cast<const uint32_t *>(kst + 2048) + 2 * t * 64;
+        const uint4 *vl = reinterpret_cast<const uint4 *>(kst + 2048) + 4 * lane;   // lane-major (vt_byte)
 #pragma unroll
         for (int mi = 0; mi < 4; mi++) {
-            va[mi][0] = vtile[16 * mi + g];
-            va[mi][1] = vtile[16 * mi + g + 8];
-            va[mi][2] = vtile[64 + 16 * mi + g];
-            va[mi][3] = vtile[64 + 16 * mi + g + 8];
+            const uint4 v = vl[mi ^ ((lane >> 1) & 3)];
+            va[mi][0] = v.x; va[mi][1] = v.y; va[mi][2] = v.z; va[mi][3] = v.w;
         }
         __syncwarp();   // every lane has its fragments: the stage may be refilled next iteration
         Tile T;

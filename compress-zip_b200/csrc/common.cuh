@@ -252,4 +252,18 @@ __device__ __forceinline__ int sext8(uint32_t w, int byte) {
     return (int)(int8_t)((w >> (8 * byte)) & 0xFFu);
 }
 
+// V tile of 32 keys x 64 dims (2 KB) in the attention kernels' streamed and decode
+// layouts, lane-major: the P.V A fragment of lane l = 4g + t (mma m16n8k32, V^T as A)
+// is 16 words va[mi][k] = 4 bytes of keys 8t + 4(k >> 1) .. +3 at dim
+// 16 mi + g + 8 (k & 1), stored as the 16-byte chunk mi at chunk position
+// mi ^ ((l >> 1) & 3) of the lane's 64 bytes, so a lane loads its fragments with four
+// 16-byte loads and the eight lanes of each load phase hit eight bank groups.
+// Returns the byte of (key, dim) in the tile.
+__device__ __forceinline__ int vt_byte(int key, int dim) {
+    const int t = key >> 3, kb = (key >> 2) & 1, b = key & 3;
+    const int mi = dim >> 4, g = dim & 7, h = (dim >> 3) & 1;
+    const int lane = 4 * g + t;
+    return 64 * lane + 16 * (mi ^ ((lane >> 1) & 3)) + 4 * (2 * kb + h) + b;
+}
+
 }  // namespace czg

@@ -102,8 +102,8 @@ __global__ void k_dec_init(const uint8_t *__restrict__ data, const uint64_t *__r
 // split == false: the row is [k_rot 64 | v 64] at pos * 128.  split == true (the
 // tensor-core decode attention): K at pos * 64 with its dims permuted as
 // bytes [16t' + 4k + b] = dim 16k + 4t' + b, and V from len * 64 on in 32-key tiles
-// of 2 KB, byte (key, dim) at tile * 2048 + (key % 32 / 4) * 256 + dim * 4 + key % 4,
-// where len = cache_ld / 128.
+// of 2 KB, byte (key, dim) at tile * 2048 + vt_byte(key % 32, dim) (lane-major,
+// common.cuh), where len = cache_ld / 128.
 __global__ void k_kv_append(const int8_t *__restrict__ qkv, int ldq, int d, int pos,
                             const int16_t *__restrict__ rope_cos, const int16_t *__restrict__ rope_sin,
                             int M, int8_t *__restrict__ kvc, size_t cache_ld, bool split) {
@@ -129,11 +129,9 @@ __global__ void k_kv_append(const int8_t *__restrict__ qkv, int ldq, int d, int 
         const int i2 = i + kHalfDim;
         kr[16 * ((i >> 2) & 3) + 4 * (i >> 4) + (i & 3)] = kx;
         kr[16 * ((i2 >> 2) & 3) + 4 * (i2 >> 4) + (i2 & 3)] = ky;
-        // V in 32-key tiles of [8 groups of 4 keys][64 dims][4 keys]: the 64 bytes of one
-        // key fall into 256 contiguous bytes, and 4 consecutive keys of a dim form one word
-        int8_t *vt = base + len * 64 + (size_t)(pos >> 5) * 2048 + ((pos & 31) >> 2) * 256 + (pos & 3);
-        vt[(2 * i) * 4] = k[64 + 2 * i];
-        vt[(2 * i + 1) * 4] = k[64 + 2 * i + 1];
+        int8_t *vt = base + len * 64 + (size_t)(pos >> 5) * 2048;   // the V tile of key pos
+        vt[vt_byte(pos & 31, 2 * i)] = k[64 + 2 * i];
+        vt[vt_byte(pos & 31, 2 * i + 1)] = k[64 + 2 * i + 1];
     }
 }
 

@@ -377,20 +377,22 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                                          kvs.kv + base + (size_t)p * 64);
                         } else {
                             const int npad = (kvs.chunk_len[c] + 31) & ~31;
-                            voff = (uint32_t)(base + (size_t)npad * 64 + (size_t)(p >> 5) * 2048 +
-                                              ((p & 31) >> 2) * 256 + (p & 3));
+                            // the V tile of key p (a multiple of 128 bytes) with p % 32 in the low bits
+                            voff = (uint32_t)(base + (size_t)npad * 64 + (size_t)(p >> 5) * 2048) | (uint32_t)(p & 31);
                         }
                     }
-                    if (hf == 1) {   // value dims 2l, 2l + 1 of each row to bytes 8l, 8l + 4 of its group
+                    if (hf == 1) {   // value dims 2l, 2l + 1 of each row into its V tile (vt_byte, common.cuh)
                         const uint8_t *sv = sbuf0 + nb * TC_STAGE_OUT;
                         const int nrow = min(32, M - (m0 + 32 * q));
 #pragma unroll 4
                         for (int r = 0; r < nrow; r++) {
                             const uint32_t o = __shfl_sync(0xffffffffu, voff, r);
+                            const int kp = (int)(o & 31u);
+                            int8_t *vt = kvs.kv + (o & ~31u);
                             const uint16_t v2 = *reinterpret_cast<const uint16_t *>(
                                 sv + r * 64 + (((lane >> 3) ^ ((r >> 1) & 3)) << 4) + 2 * (lane & 7));
-                            kvs.kv[o + 8 * lane] = (int8_t)(v2 & 0xFFu);
-                            kvs.kv[o + 8 * lane + 4] = (int8_t)(v2 >> 8);
+                            vt[vt_byte(kp, 2 * lane)] = (int8_t)(v2 & 0xFFu);
+                            vt[vt_byte(kp, 2 * lane + 1)] = (int8_t)(v2 >> 8);
                         }
                     }
                     __syncwarp();   // the staging buffer stays this warp's: no store was issued

@@ -239,7 +239,7 @@ __global__ void k_kv_prep(const int8_t *__restrict__ qkv, int ldq, int d, const 
 // holds): chunk c at kv + (chunk_row0[c] + 32 c) * 128 bytes, its keys' K rows of
 // 64 permuted dims (bytes [16t' + 4k + b] = dim 16k + 4t' + b) first, then V in
 // 32-key tiles of 2 KB from npad * 64 on (npad = len rounded up to 32), byte
-// (key, dim) at tile * 2048 + (key % 32 / 4) * 256 + dim * 4 + key % 4 -- the
+// (key, dim) at tile * 2048 + vt_byte(key % 32, dim) (lane-major, common.cuh) -- the
 // decode cache layout of k_kv_append, per chunk.  One warp per row.
 __global__ void k_kv_prep_split(const int8_t *__restrict__ qkv, int ldq, int d, const int *__restrict__ pos,
                                 const int *__restrict__ rowchunk, const int *__restrict__ chunk_row0,
@@ -258,9 +258,9 @@ __global__ void k_kv_prep_split(const int8_t *__restrict__ qkv, int ldq, int d, 
     const int i2 = i + kHalfDim;
     kr[16 * ((i >> 2) & 3) + 4 * (i >> 4) + (i & 3)] = (int8_t)clamp127(sra_rne32(x * cs - y * sn, 15));
     kr[16 * ((i2 >> 2) & 3) + 4 * (i2 >> 4) + (i2 & 3)] = (int8_t)clamp127(sra_rne32(x * sn + y * cs, 15));
-    int8_t *vt = base + (size_t)npad * 64 + (size_t)(p >> 5) * 2048 + ((p & 31) >> 2) * 256 + (p & 3);
-    vt[(2 * i) * 4] = k[64 + 2 * i];
-    vt[(2 * i + 1) * 4] = k[64 + 2 * i + 1];
+    int8_t *vt = base + (size_t)npad * 64 + (size_t)(p >> 5) * 2048;   // the V tile of key p (vt_byte)
+    vt[vt_byte(p & 31, 2 * i)] = k[64 + 2 * i];
+    vt[vt_byte(p & 31, 2 * i + 1)] = k[64 + 2 * i + 1];
 }
 
 // xn[r] = xn_tab[tok_in[r]], 16 bytes per thread (the table, V x d bytes, stays in L2)
