@@ -246,8 +246,8 @@ struct WordSink {
 };
 
 // One lane per chunk: the 32 chunks of a warp are encoded side by side, each lane
-// walking its own chunk's (sym_low, sym_high) pairs with the next pair loaded a
-// step ahead.  The reference's renormalisation loop (arith_coder.rs:101-119) in
+// walking its own chunk's (sym_low, sym_high) pairs, the next 8 loaded while the
+// current 8 are coded.  The reference's renormalisation loop (arith_coder.rs:101-119) in
 // closed form, one pass per symbol:
 //  * E1/E2: the k = clz(low ^ high) leading bits that agree leave at once -- the
 //    first, then the pending bits (its complement), then the other k - 1 -- and
@@ -260,6 +260,7 @@ struct WordSink {
 // Output leaves in 32-bit words; a pending run that does not fit one push (over
 // 32 bits together with the symbol's agreeing bits) goes out in pieces.
 constexpr int ENC_THREADS = 128;
+constexpr int ENC_AHEAD = 8;   // interval pairs loaded ahead of the coding (an L2 round trip is several steps)
 
 __global__ void __launch_bounds__(ENC_THREADS)
 k_encode(const uint2 *__restrict__ lohi, const int *__restrict__ chunk_row0,
@@ -276,10 +277,18 @@ k_encode(const uint2 *__restrict__ lohi, const int *__restrict__ chunk_row0,
     bs.len = 0; bs.acc = 0; bs.n = 0; bs.overflow = false;
     uint32_t low = 0, high = 0xFFFFFFFFu, pending = 0;
     const uint2 *src = lohi + r0;
-    uint2 nxt = n > 0 ? src[0] : make_uint2(0, 0);
-    for (int i = 0; i < n; i++) {
-        const uint2 lh = nxt;
-        if (i + 1 < n) nxt = src[i + 1];   // in flight during this step
+    // the pairs in blocks of ENC_AHEAD: the next block is in flight while this one is coded
+    uint2 cur[ENC_AHEAD];
+#pragma unroll
+    for (int k = 0; k < ENC_AHEAD; k++) cur[k] = k < n ? src[k] : make_uint2(0, 0);
+    for (int i0 = 0; i0 < n; i0 += ENC_AHEAD) {
+    uint2 nxt[ENC_AHEAD];
+#pragma unroll
+    for (int k = 0; k < ENC_AHEAD; k++) nxt[k] = i0 + ENC_AHEAD + k < n ? src[i0 + ENC_AHEAD + k] : make_uint2(0, 0);
+#pragma unroll
+    for (int k = 0; k < ENC_AHEAD; k++) {   // unrolled, so cur[k] stays in registers
+        if (i0 + k >= n) break;
+        const uint2 lh = cur[k];
         // interval update (arith_coder.rs:86-97); both ends stay inside [low, high]
         const unsigned long long range = (unsigned long long)high - low + 1ull;
         const uint32_t nh = low + (uint32_t)udiv_by_inv((unsigned long long)lh.y * range, total, inv_total) - 1u;
@@ -315,6 +324,9 @@ k_encode(const uint2 *__restrict__ lohi, const int *__restrict__ chunk_row0,
             low = (low << j) & 0x7FFFFFFFu;
             high = (high << j) | 0x80000000u | ((1u << j) - 1u);
         }
+    }
+#pragma unroll
+    for (int k = 0; k < ENC_AHEAD; k++) cur[k] = nxt[k];
     }
     bs.finish();
     lens[c] = bs.len;
