@@ -256,7 +256,8 @@ __global__ void k_cdf_decode(const int32_t *__restrict__ logits, int V, int ld, 
 
 // Register-resident version for V == 32 * E (E in {8, 16, 32}): lane l holds the
 // E consecutive logits [l*E, (l+1)*E) in registers (each warp copies its next
-// stream's row into shared memory while it decodes the current one), the weights come from the
+// stream's row, coder state and offsets into shared memory while it decodes the
+// current one), the weights come from the
 // t256-indexed table lut4k (needs coef < 2^24), the division by S uses
 // freq_of.  The interval search is done by the whole warp: the owner
 // lane's weights go through shared memory, one element per lane, and an
@@ -278,6 +279,8 @@ __global__ void __launch_bounds__(256, CDF_BLOCKS_PER_SM) k_cdf_decode_reg(
     __shared__ uint32_t ebuf[8][E / 2];
     __shared__ uint32_t lut_w[CDF_LUT_WORDS];
     __shared__ __align__(16) int4 rowbuf[8][V / 4];   // per warp: its next stream's logits
+    // and that stream's coder state (3 words of 8 bytes), chunk offset, length and token offset
+    __shared__ __align__(16) unsigned long long mbuf[8][8];
     for (int i = threadIdx.x; i < CDF_LUT_WORDS; i += blockDim.x)   // model constant: before the wait
         lut_w[i] = __ldg(reinterpret_cast<const uint32_t *>(lut4k_g) + i);
     pdl_wait();
@@ -298,6 +301,16 @@ __global__ void __launch_bounds__(256, CDF_BLOCKS_PER_SM) k_cdf_decode_reg(
                                  (uint32_t)__cvta_generic_to_shared(&rowbuf[wib][c ^ ((c >> 3) & 7)])),
                              "l"(src + c)
                              : "memory");
+            if (lane < 6) {
+                const void *m8 = lane < 3 ? static_cast<const void *>(reinterpret_cast<const uint64_t *>(st + r) + lane)
+                                 : lane == 3 ? static_cast<const void *>(data_off + r)
+                                 : lane == 4 ? static_cast<const void *>(data_len + r)
+                                             : static_cast<const void *>(tok_off + r);
+                asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(
+                                 (uint32_t)__cvta_generic_to_shared(&mbuf[wib][lane])),
+                             "l"(m8)
+                             : "memory");
+            }
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
@@ -312,11 +325,12 @@ __global__ void __launch_bounds__(256, CDF_BLOCKS_PER_SM) k_cdf_decode_reg(
         const int4 v = rowbuf[wib][c ^ ((c >> 3) & 7)];
         x[4 * k] = v.x; x[4 * k + 1] = v.y; x[4 * k + 2] = v.z; x[4 * k + 3] = v.w;
     }
-    __syncwarp();   // the buffer takes the warp's next stream while this one is decoded
+    DecState s = *reinterpret_cast<const DecState *>(&mbuf[wib][0]);
+    const unsigned long long doff = mbuf[wib][3], dlen = mbuf[wib][4], toff = mbuf[wib][5];
+    __syncwarp();   // the buffers take the warp's next stream while this one is decoded
     fetch_row(r + stride);
-    // the coder state and the next 9 bytes of the chunk, loaded while the CDF is built
-    DecState s = st[r];
-    const uint32_t wb = window_byte(data + data_off[r], data_len[r], s.bit, lane);
+    // the next 9 bytes of the chunk, loaded while the CDF is built
+    const uint32_t wb = window_byte(data + doff, dlen, s.bit, lane);
     // max and first argmax (primitives.rs:278-295)
     int mx = INT32_MIN, am = 0x7fffffff;
 #pragma unroll
@@ -396,7 +410,7 @@ __global__ void __launch_bounds__(256, CDF_BLOCKS_PER_SM) k_cdf_decode_reg(
     if (lane == 0) {
         dec_narrow(s, lo, hi, total, inv_total, win);
         st[r] = s;
-        out_tok[tok_off[r] + step] = sym;
+        out_tok[toff + step] = sym;
         tok_in[r] = sym;
     }
     if (xn != nullptr) copy_xn_row(xn_tab, xn, d, sym, r, lane);
