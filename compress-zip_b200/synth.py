@@ -98,12 +98,13 @@ ARCH2 = dict(vocab_size=1024, n_layers=8, n_heads=8, n_kv_heads=2, d_model=512, 
              head_dim=64)
 
 
-def arch2_model(shipped: czm.ModelFile, ctx: int, seed: int = 7) -> bytes:
+def arch2_model(shipped: czm.ModelFile, ctx: int, seed: int = 7, arch: dict | None = None) -> bytes:
     """Config-2/4 model bytes: int8 tensors = clamp(round(N(0, 24^2)), +-127) drawn from
     ``seed`` in the fixed order written below; mult/shift, exp LUT, softmax constants
     and tokenizer copied from the shipped model; score_mult = the shipped six values
-    followed by its first two."""
-    a = ARCH2
+    followed by its first two.  ``arch`` (keys as ARCH2) builds another shape the same
+    way, for tests."""
+    a = ARCH2 if arch is None else arch
     d, dff, V, L = a["d_model"], a["d_ff"], a["vocab_size"], a["n_layers"]
     kvd = a["n_kv_heads"] * 64
     rng = np.random.Generator(np.random.PCG64(seed))

@@ -192,6 +192,34 @@ def test_arch2_trace_and_bytes(arch2, oracle_mod, shipped_tokens):
     assert eng.compress_chunks(toks, starts) == oracle_mod.compress_chunks(om, toks, starts)
 
 
+@pytest.mark.parametrize("queue", ["0", "1"])
+def test_four_head_model(shipped_path, tmp_path, oracle_mod, shipped_tokens, monkeypatch, queue):
+    """A synthetic 4-head model (d 256, 1 KV head, d_ff 512, 2 layers, ctx 1024): the
+    d = 256 forms of the QKV K/V epilogue (128-column tiles), the fused norm GEMMs
+    and the streamed attention in both schedules; trace and bytes against the oracle,
+    and the GPU decodes the oracle's streams."""
+    from compress_zip_b200 import czm, synth
+    from compress_zip_b200.engine import Engine
+
+    arch = dict(vocab_size=1024, n_layers=2, n_heads=4, n_kv_heads=1, d_model=256, d_ff=512, head_dim=64)
+    data = synth.arch2_model(czm.ModelFile.load(shipped_path), 1024, seed=11, arch=arch)
+    p = tmp_path / "four_head.czm"
+    p.write_bytes(data)
+    om = oracle_mod.load_model(str(p))
+    assert om.check() == 0
+    monkeypatch.setenv("CZG_ATTN_QUEUE", queue)
+    eng = Engine(data, 0)
+    try:
+        _trace_equal(eng, om, oracle_mod, shipped_tokens[:300])
+        toks = shipped_tokens[:2500]
+        starts = _starts(len(toks), 1024)
+        chunks = oracle_mod.compress_chunks(om, toks, starts)
+        assert eng.compress_chunks(toks, starts) == chunks
+        assert np.array_equal(eng.decompress_chunks(chunks, np.diff(starts)), toks)
+    finally:
+        eng.close()
+
+
 def _variant_model(shipped_path, tmp_path, sink=False, score_mult=None):
     """The shipped model with an attention sink key and/or other score multipliers."""
     from compress_zip_b200 import czm
