@@ -66,6 +66,15 @@ __device__ __forceinline__ void mma_s8u8(int (&c)[4], const uint32_t (&a)[4], ui
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// c = A * B from a zero accumulator (the previous contents of c are not read)
+__device__ __forceinline__ void mma_s8u8_z(int (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};\n"
+        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
+}
+
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
     uint32_t d;
     asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
@@ -316,6 +325,56 @@ __device__ __forceinline__ uint32_t bytes_equal(uint32_t x, uint32_t q) {
     return prmt(~nz & 0x80808080u, 0u, 0xBA98u);                    // replicate bit 7 over the byte
 }
 
+// One record pass of a tile (attention.rs:248-263): the rows with a pass-th record
+// rescale their state by that record's factor, then every row adds its entries of
+// segment `pass` (a row with fewer records has none there).  A row's state is
+// 256 * hiacc + loacc (mod 2^32) and s_state + 256 * shs + sls: the pass first folds
+// every hiacc into its loacc, so the rescale reads one word and the pass's high-byte
+// products start from a zero accumulator.  s < 2^32 holds for up to 65,536 keys and a
+// sink (65,537 weights <= 65,535: 2^32 - 1), so its rescale is the high word of one
+// 64-bit product.
+template <int MODE>
+__device__ __forceinline__ void record_pass(int pass, int t, uint32_t (&rem)[2], const uint32_t *rec_e,
+                                            const uint16_t *lut4k, uint32_t c8, uint32_t (&s_state)[2],
+                                            int (&shs)[4], int (&sls)[4], int (&hiacc)[4][4], int (&loacc)[4][4],
+                                            const uint32_t (&segw)[2], const uint32_t (&phi)[2],
+                                            const uint32_t (&plo)[2], const uint32_t (&va)[4][4],
+                                            const uint32_t (&ones)[4]) {
+#pragma unroll
+    for (int mi = 0; mi < 4; mi++)
+#pragma unroll
+        for (int k = 0; k < 4; k++) loacc[mi][k] = (int)(((uint32_t)hiacc[mi][k] << 8) + (uint32_t)loacc[mi][k]);
+#pragma unroll
+    for (int e = 0; e < 2; e++) {
+        if (rem[e] != 0u) {
+            const int key = __ffs(rem[e]) - 1;
+            rem[e] &= rem[e] - 1u;
+            // saturated (MODE 2) scores can wrap the difference to >= 0, where exp gives 65535
+            const int rd = (int)rec_e[(2 * t + e) * 32 + key];
+            const uint32_t ef = MODE == 2 ? exp_attn(rd, lut4k, c8) : exp_rec(rd, lut4k, c8);
+            const uint32_t e16 = ef << 16, e16p1 = e16 + 1u;
+            const uint32_t sa = 256u * (uint32_t)shs[e] + (uint32_t)sls[e];
+            // s + sa >= 0: R(s + sa) is the high word alone
+            s_state[e] = (uint32_t)(((unsigned long long)(s_state[e] + sa) * e16 + 0x80000000ull) >> 32) - sa;
+#pragma unroll
+            for (int mi = 0; mi < 4; mi++)
+#pragma unroll
+                for (int k = e; k < 4; k += 2) loacc[mi][k] = (int)rescale_rec((uint32_t)loacc[mi][k], e16, e16p1);
+        }
+    }
+    // P^T of this pass: bytes of entries in segment `pass`
+    const uint32_t m0 = bytes_equal(segw[0], (uint32_t)pass);
+    const uint32_t m1 = bytes_equal(segw[1], (uint32_t)pass);
+    const uint32_t bh0 = phi[0] & m0, bl0 = plo[0] & m0, bh1 = phi[1] & m1, bl1 = plo[1] & m1;
+    mma_s8u8(shs, ones, bh0, bh1);
+    mma_s8u8(sls, ones, bl0, bl1);
+#pragma unroll
+    for (int mi = 0; mi < 4; mi++) {
+        mma_s8u8_z(hiacc[mi], va[mi], bh0, bh1);
+        mma_s8u8(loacc[mi], va[mi], bl0, bl1);
+    }
+}
+
 __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
                  : "memory");
@@ -471,7 +530,7 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
 
         int m = INT32_MIN;   // running max of row g
         // PV layout: thread (g, t) holds rows 2t + e, dims 16*mi + g + 8*dh at [mi][2*dh + e]
-        uint32_t s_state[2] = {0u, 0u};   // s < 65535 * 1025 < 2^27 for chunks of <= 1024 keys
+        uint32_t s_state[2] = {0u, 0u};   // exact in 32 bits (record_pass)
         if (sink_key != nullptr) {   // attention.rs:211-224
             int accs[4] = {0, 0, 0, 0};
 #pragma unroll
@@ -572,40 +631,8 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
                 }
             }
             for (int pass = 1; pass <= maxrec; pass++) {
-                // rows with a pass-th record fold their state (attention.rs:248-263)
-#pragma unroll
-                for (int e = 0; e < 2; e++) {
-                    if (rem[e] != 0u) {
-                        const int key = __ffs(rem[e]) - 1;
-                        rem[e] &= rem[e] - 1u;
-                        // saturated (MODE 2) scores can wrap the difference to >= 0, where exp gives 65535
-                        const int rd = (int)rec_e[(2 * t + e) * 32 + key];
-                        const uint32_t ef = MODE == 2 ? exp_attn(rd, lut4k, c8) : exp_rec(rd, lut4k, c8);
-                        const uint32_t e16 = ef << 16, e16p1 = e16 + 1u;
-                        const uint32_t sa = 256u * (uint32_t)shs[e] + (uint32_t)sls[e];
-                        // s + sa >= 0: R(s + sa) is the high word alone
-                        s_state[e] = (uint32_t)(((unsigned long long)(s_state[e] + sa) * e16 + 0x80000000ull) >> 32) - sa;
-#pragma unroll
-                        for (int mi = 0; mi < 4; mi++)
-#pragma unroll
-                            for (int k = e; k < 4; k += 2) {
-                                const uint32_t x = ((uint32_t)hiacc[mi][k] << 8) + (uint32_t)loacc[mi][k];
-                                loacc[mi][k] = (int)rescale_rec(x, e16, e16p1);
-                                hiacc[mi][k] = 0;
-                            }
-                    }
-                }
-                // P^T of this pass: bytes of entries in segment `pass`
-                const uint32_t m0 = bytes_equal(segw[0], (uint32_t)pass);
-                const uint32_t m1 = bytes_equal(segw[1], (uint32_t)pass);
-                const uint32_t bh0 = phi[0] & m0, bl0 = plo[0] & m0, bh1 = phi[1] & m1, bl1 = plo[1] & m1;
-                mma_s8u8(shs, ones, bh0, bh1);
-                mma_s8u8(sls, ones, bl0, bl1);
-#pragma unroll
-                for (int mi = 0; mi < 4; mi++) {
-                    mma_s8u8(hiacc[mi], va[mi], bh0, bh1);
-                    mma_s8u8(loacc[mi], va[mi], bl0, bl1);
-                }
+                record_pass<MODE>(pass, t, rem, rec_e, lut4k, c8, s_state, shs, sls, hiacc, loacc, segw, phi, plo,
+                                  va, ones);
             }
         }
 
@@ -748,7 +775,7 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, int kd, int8_t *
         vt[vt_byte(p & 31, 2 * lane + 1)] = (int8_t)(v2 >> 8);
     }
     int m = INT32_MIN;
-    unsigned long long s_state[2] = {0, 0};
+    uint32_t s_state[2] = {0u, 0u};   // exact in 32 bits (record_pass)
     if (sink_key != nullptr) {   // attention.rs:211-224
         int accs[4] = {0, 0, 0, 0};
 #pragma unroll
@@ -759,7 +786,7 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, int kd, int8_t *
         }
         m = score_from_dot<true>(accs[0], mult);
         if (MODE == 0) m = (int)(kM1Bits + (uint32_t)m);
-        s_state[0] = s_state[1] = 65535ull;
+        s_state[0] = s_state[1] = 65535u;
     }
     int hiacc[4][4], loacc[4][4];
 #pragma unroll
@@ -822,34 +849,11 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, int kd, int8_t *
             tile_records(T, t, g, rec_e, segw, rem);
             __syncwarp();
         }
-        for (int pass = 0; pass <= maxrec; pass++) {
-            if (pass > 0) {
-#pragma unroll
-                for (int e = 0; e < 2; e++) {
-                    if (rem[e] != 0u) {
-                        const int key = __ffs(rem[e]) - 1;
-                        rem[e] &= rem[e] - 1u;
-                        // saturated (MODE 2) scores can wrap the difference to >= 0, where exp gives 65535
-                        const int rd = (int)rec_e[(2 * t + e) * 32 + key];
-                        const uint32_t ef = MODE == 2 ? exp_attn(rd, lut4k, c8) : exp_rec(rd, lut4k, c8);
-                        const uint32_t e16 = ef << 16, e16p1 = e16 + 1u;
-                        const unsigned long long sa = 256ull * (uint32_t)shs[e] + (unsigned long long)(uint32_t)sls[e];
-                        s_state[e] = (((s_state[e] + sa) * ef + 0x8000ull) >> 16) - sa;
-#pragma unroll
-                        for (int mi = 0; mi < 4; mi++)
-#pragma unroll
-                            for (int k = e; k < 4; k += 2) {
-                                const uint32_t x = ((uint32_t)hiacc[mi][k] << 8) + (uint32_t)loacc[mi][k];
-                                loacc[mi][k] = (int)rescale_rec(x, e16, e16p1);
-                                hiacc[mi][k] = 0;
-                            }
-                    }
-                }
-            }
+        {   // pass 0: the whole tile, or segment 0 of each row
             uint32_t bh0 = phi[0], bh1 = phi[1], bl0 = plo[0], bl1 = plo[1];
             if (maxrec > 0) {
-                const uint32_t m0 = bytes_equal(segw[0], (uint32_t)pass);
-                const uint32_t m1 = bytes_equal(segw[1], (uint32_t)pass);
+                const uint32_t m0 = bytes_equal(segw[0], 0u);
+                const uint32_t m1 = bytes_equal(segw[1], 0u);
                 bh0 &= m0; bl0 &= m0; bh1 &= m1; bl1 &= m1;
             }
             mma_s8u8(shs, ones, bh0, bh1);
@@ -860,12 +864,15 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, int kd, int8_t *
                 mma_s8u8(loacc[mi], va[mi], bl0, bl1);
             }
         }
+        for (int pass = 1; pass <= maxrec; pass++)
+            record_pass<MODE>(pass, t, rem, rec_e, lut4k, c8, s_state, shs, sls, hiacc, loacc, segw, phi, plo, va,
+                              ones);
     }
 
     // output of heads 2t, 2t+1 (attention.rs:279-284)
 #pragma unroll
     for (int e = 0; e < 2; e++) {
-        const unsigned long long sv = s_state[e] + 256ull * (uint32_t)shs[e] + (unsigned long long)(uint32_t)sls[e];
+        const uint32_t sv = s_state[e] + 256u * (uint32_t)shs[e] + (uint32_t)sls[e];
         const RneDiv dv = make_rne_div(sv == 0 ? 1ull : sv);
         uint8_t *orow = ostage + (2 * t + e) * 64;
 #pragma unroll
