@@ -58,8 +58,8 @@ __device__ __forceinline__ void attend_query(const int8_t *__restrict__ qr, int 
     {
         int x = qr[lane], y = qr[lane + 32];
         int cs = rope_cos[p * kHalfDim + lane], sn = rope_sin[p * kHalfDim + lane];
-        qb[lane] = (int8_t)clamp127(sra_rne32(sra_rne32(x * cs - y * sn, 15), 1));
-        qb[lane + 32] = (int8_t)clamp127(sra_rne32(sra_rne32(x * sn + y * cs, 15), 1));
+        qb[lane] = (int8_t)rope_q_round(x * cs - y * sn);
+        qb[lane + 32] = (int8_t)rope_q_round(x * sn + y * cs);
     }
     __syncwarp();
     uint32_t q[16];

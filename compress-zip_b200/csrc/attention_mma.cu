@@ -516,8 +516,8 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
                     int x = sext8(raw[k], b), y = sext8(raw[k + 2], b);
                     int cs = 0, sn = 0;
                     if (prow < n) { cs = rope_cos[prow * kHalfDim + i]; sn = rope_sin[prow * kHalfDim + i]; }
-                    int xr = clamp127(sra_rne32(sra_rne32(x * cs - y * sn, 15), 1));
-                    int yr = clamp127(sra_rne32(sra_rne32(x * sn + y * cs, 15), 1));
+                    int xr = rope_q_round(x * cs - y * sn);
+                    int yr = rope_q_round(x * sn + y * cs);
                     lo[k] |= (uint32_t)(uint8_t)xr << (8 * b);
                     hi[k] |= (uint32_t)(uint8_t)yr << (8 * b);
                 }
@@ -744,8 +744,8 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, int kd, int8_t *
                 const int i = 16 * k + 4 * t + b;
                 int x = sext8(raw[k], b), y = sext8(raw[k + 2], b);
                 const int cs = rope_cos[p * kHalfDim + i], sn = rope_sin[p * kHalfDim + i];
-                int xr = clamp127(sra_rne32(sra_rne32(x * cs - y * sn, 15), 1));
-                int yr = clamp127(sra_rne32(sra_rne32(x * sn + y * cs, 15), 1));
+                int xr = rope_q_round(x * cs - y * sn);
+                int yr = rope_q_round(x * sn + y * cs);
                 lo[k] |= (uint32_t)(uint8_t)xr << (8 * b);
                 hi[k] |= (uint32_t)(uint8_t)yr << (8 * b);
             }
@@ -762,8 +762,8 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, int kd, int8_t *
         const int8_t *kq = qkv + (size_t)r * ldq + kd;
         const int x = kq[lane], y = kq[lane + kHalfDim];
         const int cs = rope_cos[p * kHalfDim + lane], sn = rope_sin[p * kHalfDim + lane];
-        const int kx = clamp127(sra_rne32(x * cs - y * sn, 15));
-        const int ky = clamp127(sra_rne32(x * sn + y * cs, 15));
+        const int kx = rope_k_round(x * cs - y * sn);
+        const int ky = rope_k_round(x * sn + y * cs);
         const uint32_t v2 = *reinterpret_cast<const uint16_t *>(kq + 64 + 2 * lane);
         reinterpret_cast<uint32_t *>(ostage)[lane] = (uint32_t)(uint8_t)kx | ((uint32_t)(uint8_t)ky << 8) | (v2 << 16);
         int8_t *base = kvc + (size_t)r * cache_ld;

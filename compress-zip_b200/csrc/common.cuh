@@ -83,6 +83,23 @@ __device__ __forceinline__ int sra_rne32(int v, int sh) {
     return q;
 }
 
+// The RoPE roundings (attention.rs:29-83) of v = x*cos -/+ y*sin, |v| <= 2^23 (int8 x, y;
+// int16 cos, sin): clamp127(rne(v / 2^15)) for keys and clamp127(rne(rne(v / 2^15) / 2))
+// for queries, in FP32.  v converts exactly; with M1 = 1.5 * 2^23, fma(v, 2^-15, M1) is
+// M1 + v / 2^15 (|v / 2^15| <= 256) rounded once to spacing 1, ties to even: M1 +
+// rne(v / 2^15), and fma(that, 1/2, M1/2) = M1 + rne(rne(v / 2^15) / 2) likewise; the
+// bias comes off inside the clamp.  Checked against the integer forms for every v in
+// [-2^23, 2^23] (tests/rope_round_fp32.c).
+__device__ __forceinline__ int rope_k_round(int v) {
+    const int b = __float_as_int(__fmaf_rn(__int2float_rn(v), 1.0f / 32768.0f, 12582912.0f));
+    return min(__viaddmax_s32(b, -(int)kM1Bits, -127), 127);
+}
+__device__ __forceinline__ int rope_q_round(int v) {
+    const float r1 = __fmaf_rn(__int2float_rn(v), 1.0f / 32768.0f, 12582912.0f);
+    const int b = __float_as_int(__fmaf_rn(r1, 0.5f, 6291456.0f));
+    return min(__viaddmax_s32(b, -(int)kM1Bits, -127), 127);
+}
+
 // primitives.rs:49-73 (result saturated to the int32 range)
 __device__ __forceinline__ int sra_rne64_to32(long long v, int sh) {
     long long q = v;

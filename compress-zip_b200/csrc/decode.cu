@@ -115,8 +115,8 @@ __global__ void k_kv_append(const int8_t *__restrict__ qkv, int ldq, int d, int 
     const int8_t *k = qkv + (size_t)r * ldq + d;
     const int x = k[i], y = k[i + kHalfDim];
     const int c = rope_cos[pos * kHalfDim + i], s = rope_sin[pos * kHalfDim + i];
-    const int8_t kx = (int8_t)clamp127(sra_rne32(x * c - y * s, 15));
-    const int8_t ky = (int8_t)clamp127(sra_rne32(x * s + y * c, 15));
+    const int8_t kx = (int8_t)rope_k_round(x * c - y * s);
+    const int8_t ky = (int8_t)rope_k_round(x * s + y * c);
     int8_t *base = kvc + (size_t)r * cache_ld;
     if (!split) {
         int8_t *dst = base + (size_t)pos * 128;

@@ -124,8 +124,8 @@ __device__ __forceinline__ void kv_store_key(const uint8_t *srow, int sw, const 
             const int i = 4 * W + b;
             const int x = sext8(kw[W], b), y = sext8(kw[W + 8], b);
             const int c = (int)(int16_t)(cw[i >> 1] >> (16 * (i & 1))), s = (int)(int16_t)(sn[i >> 1] >> (16 * (i & 1)));
-            xw |= (uint32_t)(uint8_t)clamp127(sra_rne32(x * c - y * s, 15)) << (8 * b);
-            yw |= (uint32_t)(uint8_t)clamp127(sra_rne32(x * s + y * c, 15)) << (8 * b);
+            xw |= (uint32_t)(uint8_t)rope_k_round(x * c - y * s) << (8 * b);
+            yw |= (uint32_t)(uint8_t)rope_k_round(x * s + y * c) << (8 * b);
         }
         ow[4 * (W & 3) + (W >> 2)] = xw;
         ow[4 * ((W + 8) & 3) + ((W + 8) >> 2)] = yw;

@@ -229,8 +229,8 @@ __global__ void k_kv_prep(const int8_t *__restrict__ qkv, int ldq, int d, const 
     int x = k[i], y = k[i + kHalfDim];
     int c = rope_cos[p * kHalfDim + i], s = rope_sin[p * kHalfDim + i];
     int8_t *dst = kv + (size_t)row * 128;
-    dst[i] = (int8_t)clamp127(sra_rne32(x * c - y * s, 15));            // attention.rs:29-50
-    dst[i + kHalfDim] = (int8_t)clamp127(sra_rne32(x * s + y * c, 15));
+    dst[i] = (int8_t)rope_k_round(x * c - y * s);            // attention.rs:29-50
+    dst[i + kHalfDim] = (int8_t)rope_k_round(x * s + y * c);
     reinterpret_cast<uint16_t *>(dst + 64)[i] = reinterpret_cast<const uint16_t *>(k + 64)[i];
 }
 
@@ -256,8 +256,8 @@ __global__ void k_kv_prep_split(const int8_t *__restrict__ qkv, int ldq, int d, 
     const int cs = rope_cos[p * kHalfDim + i], sn = rope_sin[p * kHalfDim + i];
     int8_t *kr = base + (size_t)p * 64;
     const int i2 = i + kHalfDim;
-    kr[16 * ((i >> 2) & 3) + 4 * (i >> 4) + (i & 3)] = (int8_t)clamp127(sra_rne32(x * cs - y * sn, 15));
-    kr[16 * ((i2 >> 2) & 3) + 4 * (i2 >> 4) + (i2 & 3)] = (int8_t)clamp127(sra_rne32(x * sn + y * cs, 15));
+    kr[16 * ((i >> 2) & 3) + 4 * (i >> 4) + (i & 3)] = (int8_t)rope_k_round(x * cs - y * sn);
+    kr[16 * ((i2 >> 2) & 3) + 4 * (i2 >> 4) + (i2 & 3)] = (int8_t)rope_k_round(x * sn + y * cs);
     int8_t *vt = base + (size_t)npad * 64 + (size_t)(p >> 5) * 2048;   // the V tile of key p (vt_byte)
     vt[vt_byte(p & 31, 2 * i)] = k[64 + 2 * i];
     vt[vt_byte(p & 31, 2 * i + 1)] = k[64 + 2 * i + 1];
