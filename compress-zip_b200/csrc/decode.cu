@@ -374,11 +374,18 @@ __global__ void __launch_bounds__(256, CDF_BLOCKS_PER_SM) k_cdf_decode_reg(
     const uint32_t base = inc - F;
 
     const unsigned long long range = (unsigned long long)s.high - s.low + 1;
-    // value = ((code - low + 1) * T - 1) / range  (arith_coder.rs:195-200)
-    const unsigned long long value = (((unsigned long long)s.code - s.low + 1) * total - 1) / range;
-    // smallest i with v32 < cum[i], else the last symbol (arith_coder.rs:203, 225-241)
-    const uint32_t v32 = (uint32_t)value;
-    const uint32_t bal = __ballot_sync(0xffffffffu, v32 >= base && v32 < base + F);
+    // value = ((code - low + 1) * T - 1) / range  (arith_coder.rs:195-200), and the search
+    // takes the smallest i with v32 < cum[i], else the last symbol (arith_coder.rs:203,
+    // 225-241), v32 = value mod 2^32.  With code >= low (every stream the encoder wrote),
+    // c = code - low + 1 <= range, so value < T < 2^30 is v32 and, for X < 2^31,
+    // v32 < X  <=>  c * T - 1 < X * range  (both sides < 2^63): no division.  A corrupt
+    // state (code < low) wraps c and takes the division.
+    const unsigned long long cN = (unsigned long long)s.code - s.low + 1;
+    const bool direct = cN <= range;   // the same for the whole warp
+    const unsigned long long num = cN * total - 1;
+    const uint32_t v32 = direct ? 0u : (uint32_t)(num / range);
+    auto below = [&](uint32_t X) { return direct ? num < (unsigned long long)X * range : v32 < X; };
+    const uint32_t bal = __ballot_sync(0xffffffffu, !below(base) && below(base + F));
     const bool past_end = bal == 0;
     const int owner = past_end ? 31 : __ffs(bal) - 1;
     if (lane == owner) {
@@ -401,7 +408,7 @@ __global__ void __launch_bounds__(256, CDF_BLOCKS_PER_SM) k_cdf_decode_reg(
         if (lane >= o) cum += u;
     }
     cum += obase;
-    const uint32_t hit = __ballot_sync(0xffffffffu, lane < E && v32 < cum);
+    const uint32_t hit = __ballot_sync(0xffffffffu, lane < E && below(cum));
     const int sl = past_end ? E - 1 : __ffs(hit) - 1;   // hit != 0 unless past the end
     const uint32_t hi = __shfl_sync(0xffffffffu, cum, sl);
     const uint32_t lo = hi - __shfl_sync(0xffffffffu, f, sl);

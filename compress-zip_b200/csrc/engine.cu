@@ -1019,13 +1019,11 @@ int decompress_impl(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts
         h_off.resize(ns);
         h_len.resize(ns);
         h_tok.resize(ns);
-        uint64_t wtok = 0;
-        for (int r = 0; r < ns; r++) {
+        for (int r = 0; r < ns; r++) {   // each stream's tokens go straight to its place in the caller's order
             const uint32_t ch = order[w0 + r];
             h_off[r] = data_starts[ch] - data_starts[0];
             h_len[r] = data_starts[ch + 1] - data_starts[ch];
-            h_tok[r] = wtok;
-            wtok += n_tokens[ch];
+            h_tok[r] = tok_base[ch];
         }
         cudaMemcpyAsync(c->d_off, h_off.data(), 8 * ns, cudaMemcpyHostToDevice, s);
         cudaMemcpyAsync(c->d_len, h_len.data(), 8 * ns, cudaMemcpyHostToDevice, s);
@@ -1093,22 +1091,26 @@ int decompress_impl(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts
             return fail(c, CZG_E_DEVICE, "a GEMM launch was refused (output tensor map)");
         }
         if (!cuda_ok(c, cudaGetLastError(), "kernel launch")) return CZG_E_DEVICE;
-        // tokens of this wave (stream order) -> caller order
-        std::vector<uint32_t> wt(wtok);
+        if (w1 < n_chunks) {   // the next wave reuses the per-stream buffers: end this one
+            int err = 0;
+            cudaMemcpyAsync(&err, c->err_flag, sizeof(int), cudaMemcpyDeviceToHost, s);
+            if (!cuda_ok(c, cudaStreamSynchronize(s), "decode wave")) return CZG_E_DEVICE;
+            collect_events(c);
+            if (err & kErrTimeout) return fail(c, CZG_E_TIMEOUT, "a bounded device wait expired");
+        }
+    }
+    // every token is in caller order on the device: one copy
+    {
         EvPair &e = next_ev(c, -2);
         cudaEventRecord(e.a, s);
-        if (wtok) cudaMemcpyAsync(wt.data(), c->d_outtok, wtok * 4, cudaMemcpyDeviceToHost, s);
+        if (total_tok) cudaMemcpyAsync(out_tokens, c->d_outtok, total_tok * 4, cudaMemcpyDeviceToHost, s);
         cudaEventRecord(e.b, s);
         int err = 0;
         cudaMemcpyAsync(&err, c->err_flag, sizeof(int), cudaMemcpyDeviceToHost, s);
-        if (!cuda_ok(c, cudaStreamSynchronize(s), "decode wave")) return CZG_E_DEVICE;
+        if (!cuda_ok(c, cudaStreamSynchronize(s), "decode")) return CZG_E_DEVICE;
         collect_events(c);
-        c->stats.d2h_bytes += wtok * 4;
+        c->stats.d2h_bytes += total_tok * 4;
         if (err & kErrTimeout) return fail(c, CZG_E_TIMEOUT, "a bounded device wait expired");
-        for (int r = 0; r < ns; r++) {
-            const uint32_t ch = order[w0 + r];
-            memcpy(out_tokens + tok_base[ch], wt.data() + h_tok[r], 4ull * n_tokens[ch]);
-        }
     }
     stats_end(c);
     return CZG_OK;
