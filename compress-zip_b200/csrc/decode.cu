@@ -268,7 +268,10 @@ __global__ void k_cdf_decode(const int32_t *__restrict__ logits, int V, int ld, 
 constexpr int CDF_LUT_WORDS = 4104 / 2;   // lut4k: t256 0..4096, padded
 constexpr int CDF_BLOCKS_PER_SM = 4;
 
-template <int E, bool EXP0>
+// KEY: every logit is below 2^26 in magnitude (d * 127 * 128 < 2^26), so
+// logit * 32 + (31 - k) orders the lane's entries by value, then by first index, in
+// one int32 and the lane's max with its first index is a three-input max tree.
+template <int E, bool EXP0, bool KEY>
 __global__ void __launch_bounds__(256, CDF_BLOCKS_PER_SM) k_cdf_decode_reg(
     const int32_t *__restrict__ logits, int ld, const uint16_t *__restrict__ lut4k_g, uint32_t c8, uint32_t total,
     unsigned long long inv_total, int M, DecState *__restrict__ st, const uint8_t *__restrict__ data,
@@ -333,14 +336,26 @@ __global__ void __launch_bounds__(256, CDF_BLOCKS_PER_SM) k_cdf_decode_reg(
     const uint32_t wb = window_byte(data + doff, dlen, s.bit, lane);
     // max and first argmax (primitives.rs:278-295)
     int mx = INT32_MIN, am = 0x7fffffff;
+    if constexpr (KEY) {
+        int key = INT32_MIN;
 #pragma unroll
-    for (int k = 0; k < E; k++)
-        if (x[k] > mx) { mx = x[k]; am = lane * E + k; }
+        for (int k = 0; k < E; k += 2) key = __vimax3_s32(key, x[k] * 32 + (31 - k), x[k + 1] * 32 + (30 - k));
+        const int lmx = key >> 5;
+        mx = lmx;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const int om = __shfl_xor_sync(0xffffffffu, mx, o);
-        const int oa = __shfl_xor_sync(0xffffffffu, am, o);
-        if (om > mx || (om == mx && oa < am)) { mx = om; am = oa; }
+        for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const int first = __ffs(__ballot_sync(0xffffffffu, lmx == mx)) - 1;   // lowest lane holding the max
+        am = first * E + 31 - (__shfl_sync(0xffffffffu, key, first) & 31);
+    } else {
+#pragma unroll
+        for (int k = 0; k < E; k++)
+            if (x[k] > mx) { mx = x[k]; am = lane * E + k; }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const int om = __shfl_xor_sync(0xffffffffu, mx, o);
+            const int oa = __shfl_xor_sync(0xffffffffu, am, o);
+            if (om > mx || (om == mx && oa < am)) { mx = om; am = oa; }
+        }
     }
     uint32_t ew[E / 2];
     uint32_t S = 0;
@@ -453,19 +468,22 @@ void launch_cdf_decode(const int32_t *logits, int V, int ld, const uint16_t *lut
     if (coef < (1u << 24) && ld % 4 == 0 && (V == 1024 || V == 512 || V == 256)) {
         const unsigned pgrid = std::min<unsigned>(grid, (unsigned)(CDF_BLOCKS_PER_SM * sm_count()));
         const uint32_t c8 = coef << 8;
-#define CZG_CDF_DEC(EE)                                                                                       \
-    do {                                                                                                       \
-        if (exp0)                                                                                              \
-            launch_k(k_cdf_decode_reg<EE, true>, pgrid, 256, 0, stream, logits, ld, lut4k, c8, total, inv, M, st,  \
-                     data, data_off, data_len, tok_off, step, out_tok, tok_in, xn_tab, xn, d);                \
-        else                                                                                                   \
-            launch_k(k_cdf_decode_reg<EE, false>, pgrid, 256, 0, stream, logits, ld, lut4k, c8, total, inv, M, st, \
-                     data, data_off, data_len, tok_off, step, out_tok, tok_in, xn_tab, xn, d);                \
+        const bool key = (long long)d * 16256 < (1ll << 26);   // |logit| <= d * 127 * 128
+#define CZG_CDF_DEC1(EE, X0, KY)                                                                                  \
+    launch_k(k_cdf_decode_reg<EE, X0, KY>, pgrid, 256, 0, stream, logits, ld, lut4k, c8, total, inv, M, st, data, \
+             data_off, data_len, tok_off, step, out_tok, tok_in, xn_tab, xn, d)
+#define CZG_CDF_DEC(EE)                                                                                          \
+    do {                                                                                                          \
+        if (exp0 && key) CZG_CDF_DEC1(EE, true, true);                                                           \
+        else if (exp0) CZG_CDF_DEC1(EE, true, false);                                                            \
+        else if (key) CZG_CDF_DEC1(EE, false, true);                                                             \
+        else CZG_CDF_DEC1(EE, false, false);                                                                     \
     } while (0)
         if (V == 1024) CZG_CDF_DEC(32);
         else if (V == 512) CZG_CDF_DEC(16);
         else CZG_CDF_DEC(8);
 #undef CZG_CDF_DEC
+#undef CZG_CDF_DEC1
         return;
     }
     launch_k(k_cdf_decode, grid, 256, 0, stream, logits, V, ld, lut, coef, total, inv, M, st, data, data_off, data_len,
