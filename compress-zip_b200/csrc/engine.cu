@@ -18,6 +18,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "czg.h"
@@ -128,6 +129,9 @@ struct czg_ctx {
     uint64_t *d_off = nullptr, *d_len = nullptr, *d_tokoff = nullptr;
     uint32_t *d_outtok = nullptr;
     std::vector<void *> dec_allocs;
+    // pinned staging of the decoded tokens (grown on demand)
+    uint8_t *h_out = nullptr;
+    size_t h_out_bytes = 0;
     // pinned host staging: chunk tables of the wave being launched (two, so a wave's
     // tables can be written while the previous wave's copies are still queued), and
     // per wave parity the error word, packed total and chunk lengths copied back
@@ -965,6 +969,40 @@ int dec_reserve(czg_ctx *c, size_t streams, size_t len, size_t bytes, size_t tok
     return CZG_OK;
 }
 
+// Device memory to a caller's (pageable) host buffer: one DMA into pinned staging at
+// full PCIe / C2C speed, then host threads copy it on (a direct copy to pageable
+// memory goes through the driver's staging at a few GB/s).  Small copies, or no
+// pinned memory to be had, take the direct copy.  Returns false on a CUDA error.
+bool copy_out(czg_ctx *c, void *dst, const void *src, size_t n, cudaStream_t s) {
+    if (n == 0) return true;
+    if (n >= ((size_t)1 << 22) && n > c->h_out_bytes) {
+        if (c->h_out) {
+            cudaFreeHost(c->h_out);
+            c->h_out = nullptr;
+            c->h_out_bytes = 0;
+        }
+        if (cudaMallocHost(&c->h_out, n) == cudaSuccess) c->h_out_bytes = n;
+        else { c->h_out = nullptr; cudaGetLastError(); }
+    }
+    if (n < ((size_t)1 << 22) || n > c->h_out_bytes) {
+        cudaMemcpyAsync(dst, src, n, cudaMemcpyDeviceToHost, s);
+        return cudaStreamSynchronize(s) == cudaSuccess;
+    }
+    cudaMemcpyAsync(c->h_out, src, n, cudaMemcpyDeviceToHost, s);
+    if (cudaStreamSynchronize(s) != cudaSuccess) return false;
+    const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+    const size_t nt = std::min<size_t>(std::min(8u, hw), n >> 22);   // >= 4 MB per thread
+    const size_t per = (n / nt + 63) & ~(size_t)63;
+    std::vector<std::thread> pool;
+    for (size_t i = 1; i < nt; i++) {
+        const size_t a = std::min(n, i * per), b = std::min(n, a + per);
+        if (a < b) pool.emplace_back([=] { memcpy((uint8_t *)dst + a, c->h_out + a, b - a); });
+    }
+    memcpy(dst, c->h_out, std::min(n, per));
+    for (auto &t : pool) t.join();
+    return true;
+}
+
 // Decompress: all chunks of a wave decode in lockstep, longest first, so the
 // active streams at step i are a prefix of the rows.
 int decompress_impl(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts, const uint32_t *n_tokens,
@@ -1101,13 +1139,13 @@ int decompress_impl(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts
     }
     // every token is in caller order on the device: one copy
     {
-        EvPair &e = next_ev(c, -2);
-        cudaEventRecord(e.a, s);
-        if (total_tok) cudaMemcpyAsync(out_tokens, c->d_outtok, total_tok * 4, cudaMemcpyDeviceToHost, s);
-        cudaEventRecord(e.b, s);
         int err = 0;
         cudaMemcpyAsync(&err, c->err_flag, sizeof(int), cudaMemcpyDeviceToHost, s);
-        if (!cuda_ok(c, cudaStreamSynchronize(s), "decode")) return CZG_E_DEVICE;
+        EvPair &e = next_ev(c, -2);
+        cudaEventRecord(e.a, s);
+        const bool ok = copy_out(c, out_tokens, c->d_outtok, total_tok * 4, s);
+        cudaEventRecord(e.b, s);
+        if (!ok || !cuda_ok(c, cudaStreamSynchronize(s), "decode")) return CZG_E_DEVICE;
         collect_events(c);
         c->stats.d2h_bytes += total_tok * 4;
         if (err & kErrTimeout) return fail(c, CZG_E_TIMEOUT, "a bounded device wait expired");
@@ -1175,7 +1213,7 @@ void czg_ctx_destroy(czg_ctx *c) {
     for (void *p : c->ws_allocs) cudaFree(p);
     for (void *p : c->dec_allocs) cudaFree(p);
     if (c->copy_stream) cudaStreamSynchronize(c->copy_stream);
-    for (uint8_t *h : {c->h_meta, c->h_meta2, c->h_small[0], c->h_small[1]})
+    for (uint8_t *h : {c->h_meta, c->h_meta2, c->h_small[0], c->h_small[1], c->h_out})
         if (h) cudaFreeHost(h);
     for (int b = 0; b < 2; b++)
         for (cudaEvent_t e : {c->ev_h2d[b], c->ev_comp[b], c->ev_small[b], c->ev_d2h[b]})
