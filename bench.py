@@ -646,6 +646,25 @@ def decode_bench(eng, mf, rank, args, stream, world, parity):
             "kernel_split": "from one more, untimed run with per-kernel CUDA events"}
 
 
+def _corpus_docs(bounds):
+    """Documents of seeds [lo, hi) (a worker of corpus_bench's generation pool)."""
+    lo, hi = bounds
+    return synth.documents(range(lo, hi), 65536)
+
+
+def corpus_documents(lo, hi, workers):
+    """synth.documents over seeds [lo, hi), split over a pool of spawned processes
+    (untimed setup: a 1 GB corpus takes minutes in one process)."""
+    if workers <= 1 or hi - lo < 256:
+        return synth.documents(range(lo, hi), 65536)
+    import multiprocessing as mp
+
+    cuts = [lo + (hi - lo) * i // workers for i in range(workers + 1)]
+    with mp.get_context("spawn").Pool(workers) as pool:
+        parts = pool.map(_corpus_docs, [(cuts[i], cuts[i + 1]) for i in range(workers)])
+    return [d for part in parts for d in part]
+
+
 def corpus_bench(args, mf, rank, world, local):
     """Configuration 4 proper: a corpus of args.corpus_mb MB of 64 KiB documents
     (seeds 10000..) split by document over the ranks (strong scaling: the corpus is
@@ -662,7 +681,7 @@ def corpus_bench(args, mf, rank, world, local):
     lo, hi = rank * n_docs // world, (rank + 1) * n_docs // world
     model = synth.arch2_model(mf, 4096)
     tok = mf.tokenizer()
-    docs = synth.documents(range(10000 + lo, 10000 + hi), 65536)
+    docs = corpus_documents(10000 + lo, 10000 + hi, max(1, min(16, (os.cpu_count() or 1) // world)))
     ids = tok.encode_batch_arrays(docs, num_threads=min(16, os.cpu_count() or 1))
     tokens, starts, doc_chunk0 = chunked(ids, 4096)
     n_tok, n_chunks, nbytes = int(len(tokens)), int(len(starts) - 1), sum(len(d.encode()) for d in docs)
