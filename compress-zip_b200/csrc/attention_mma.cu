@@ -303,14 +303,16 @@ __device__ __forceinline__ void tile_softmax(const int (&sacc)[4][4], int kb, in
 __device__ __forceinline__ uint32_t spread4(uint32_t x) { return ((x & 0xFu) * 0x00204081u) & 0x01010101u; }
 
 // Record bookkeeping of a tile with records.  Segment of each entry (records of
-// its row at or before it in key order), one byte per entry: word q holds entries
-// 4q..4q+3.  The entries' (previous max - score) go to rec_e[row][key] (0 where no
-// record); rem[e] = the record mask of PV row 2t+e, which the folds walk.
-__device__ __forceinline__ void tile_records(const Tile &T, int t, int g, uint32_t *rec_e, uint32_t (&segw)[2],
+// its row at or before it in key order, at most 32), one byte per entry plus 0x80:
+// word q holds entries 4q..4q+3.  The entries' (previous max - score) go to
+// rec_e[row][key] (0 where no record); rem[e] = the record mask of PV row 2t+e,
+// which the folds walk.
+__device__ __forceinline__ void tile_records(const Tile &T, int t, int g, uint32_t *rec_e, uint32_t (&segb)[2],
                                              uint32_t (&rem)[2]) {
     const uint32_t before = (uint32_t)__popc(T.rowmask & ((1u << (8 * t)) - 1u));
-    segw[0] = (spread4(T.rm) + before) * 0x01010101u;
-    segw[1] = (spread4(T.rm >> 4) + (segw[0] >> 24)) * 0x01010101u;
+    const uint32_t s0 = (spread4(T.rm) + before) * 0x01010101u;
+    segb[0] = s0 + 0x80808080u;
+    segb[1] = (spread4(T.rm >> 4) + (s0 >> 24)) * 0x01010101u + 0x80808080u;
     uint4 *dst = reinterpret_cast<uint4 *>(rec_e + g * 32 + 8 * t);
     dst[0] = make_uint4(T.ef[0], T.ef[1], T.ef[2], T.ef[3]);
     dst[1] = make_uint4(T.ef[4], T.ef[5], T.ef[6], T.ef[7]);
@@ -318,11 +320,12 @@ __device__ __forceinline__ void tile_records(const Tile &T, int t, int g, uint32
     rem[1] = __shfl_sync(0xffffffffu, T.rowmask, 8 * t + 4);   // row 2t+1
 }
 
-// 0xFF in each byte of x equal to q, else 0
-__device__ __forceinline__ uint32_t bytes_equal(uint32_t x, uint32_t q) {
-    const uint32_t y = x ^ (q * 0x01010101u);
-    const uint32_t nz = ((y & 0x7F7F7F7Fu) + 0x7F7F7F7Fu) | y;   // bit 7 set in non-zero bytes
-    return prmt(~nz & 0x80808080u, 0u, 0xBA98u);                    // replicate bit 7 over the byte
+// 0xFF in each byte whose segment is >= p, else 0 (segb as tile_records writes it,
+// p <= 64): each byte 0x80 + seg - p stays in 64..192, so no borrow crosses bytes and
+// bit 7 is set exactly when seg >= p; prmt replicates it over the byte.  The entries
+// of segment p are then seg_ge(p) & ~seg_ge(p + 1).
+__device__ __forceinline__ uint32_t seg_ge(uint32_t segb, uint32_t p) {
+    return prmt(segb - p * 0x01010101u, 0u, 0xBA98u);
 }
 
 // One record pass of a tile (attention.rs:248-263): the rows with a pass-th record
@@ -337,9 +340,9 @@ template <int MODE>
 __device__ __forceinline__ void record_pass(int pass, int t, uint32_t (&rem)[2], const uint32_t *rec_e,
                                             const uint16_t *lut4k, uint32_t c8, uint32_t (&s_state)[2],
                                             int (&shs)[4], int (&sls)[4], int (&hiacc)[4][4], int (&loacc)[4][4],
-                                            const uint32_t (&segw)[2], const uint32_t (&phi)[2],
-                                            const uint32_t (&plo)[2], const uint32_t (&va)[4][4],
-                                            const uint32_t (&ones)[4]) {
+                                            const uint32_t (&segb)[2], uint32_t (&geq)[2],
+                                            const uint32_t (&phi)[2], const uint32_t (&plo)[2],
+                                            const uint32_t (&va)[4][4], const uint32_t (&ones)[4]) {
 #pragma unroll
     for (int mi = 0; mi < 4; mi++)
 #pragma unroll
@@ -362,10 +365,12 @@ __device__ __forceinline__ void record_pass(int pass, int t, uint32_t (&rem)[2],
                 for (int k = e; k < 4; k += 2) loacc[mi][k] = (int)rescale_rec((uint32_t)loacc[mi][k], e16, e16p1);
         }
     }
-    // P^T of this pass: bytes of entries in segment `pass`
-    const uint32_t m0 = bytes_equal(segw[0], (uint32_t)pass);
-    const uint32_t m1 = bytes_equal(segw[1], (uint32_t)pass);
-    const uint32_t bh0 = phi[0] & m0, bl0 = plo[0] & m0, bh1 = phi[1] & m1, bl1 = plo[1] & m1;
+    // P^T of this pass: bytes of entries in segment `pass` (geq: segment >= pass)
+    const uint32_t n0 = seg_ge(segb[0], (uint32_t)pass + 1u), n1 = seg_ge(segb[1], (uint32_t)pass + 1u);
+    const uint32_t bh0 = phi[0] & geq[0] & ~n0, bl0 = plo[0] & geq[0] & ~n0;
+    const uint32_t bh1 = phi[1] & geq[1] & ~n1, bl1 = plo[1] & geq[1] & ~n1;
+    geq[0] = n0;
+    geq[1] = n1;
     mma_s8u8(shs, ones, bh0, bh1);
     mma_s8u8(sls, ones, bl0, bl1);
 #pragma unroll
@@ -609,18 +614,18 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
                 phi[q] = prmt(x01, x23, 0x7632u);
             }
             const int maxrec = (int)__reduce_max_sync(0xffffffffu, (unsigned)__popc(T.rowmask));
-            uint32_t segw[2] = {0, 0};
+            uint32_t segb[2] = {0, 0}, geq[2] = {0, 0};
             uint32_t rem[2] = {0, 0};   // records of the PV rows 2t, 2t+1 not yet folded
             if (maxrec > 0) {
-                tile_records(T, t, g, rec_e, segw, rem);
+                tile_records(T, t, g, rec_e, segb, rem);
                 __syncwarp();
             }
             {   // pass 0: the whole tile, or segment 0 of each row
                 uint32_t bh0 = phi[0], bh1 = phi[1], bl0 = plo[0], bl1 = plo[1];
                 if (maxrec > 0) {
-                    const uint32_t m0 = bytes_equal(segw[0], 0u);
-                    const uint32_t m1 = bytes_equal(segw[1], 0u);
-                    bh0 &= m0; bl0 &= m0; bh1 &= m1; bl1 &= m1;
+                    geq[0] = seg_ge(segb[0], 1u);
+                    geq[1] = seg_ge(segb[1], 1u);
+                    bh0 &= ~geq[0]; bl0 &= ~geq[0]; bh1 &= ~geq[1]; bl1 &= ~geq[1];
                 }
                 mma_s8u8(shs, ones, bh0, bh1);   // weight sums (all-ones rows)
                 mma_s8u8(sls, ones, bl0, bl1);
@@ -631,8 +636,8 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
                 }
             }
             for (int pass = 1; pass <= maxrec; pass++) {
-                record_pass<MODE>(pass, t, rem, rec_e, lut4k, c8, s_state, shs, sls, hiacc, loacc, segw, phi, plo,
-                                  va, ones);
+                record_pass<MODE>(pass, t, rem, rec_e, lut4k, c8, s_state, shs, sls, hiacc, loacc, segb, geq, phi,
+                                  plo, va, ones);
             }
         }
 
@@ -843,18 +848,18 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, int kd, int8_t *
             phi[q] = prmt(x01, x23, 0x7632u);
         }
         const int maxrec = (int)__reduce_max_sync(0xffffffffu, (unsigned)__popc(T.rowmask));
-        uint32_t segw[2] = {0, 0};
+        uint32_t segb[2] = {0, 0}, geq[2] = {0, 0};
         uint32_t rem[2] = {0, 0};
         if (maxrec > 0) {
-            tile_records(T, t, g, rec_e, segw, rem);
+            tile_records(T, t, g, rec_e, segb, rem);
             __syncwarp();
         }
         {   // pass 0: the whole tile, or segment 0 of each row
             uint32_t bh0 = phi[0], bh1 = phi[1], bl0 = plo[0], bl1 = plo[1];
             if (maxrec > 0) {
-                const uint32_t m0 = bytes_equal(segw[0], 0u);
-                const uint32_t m1 = bytes_equal(segw[1], 0u);
-                bh0 &= m0; bl0 &= m0; bh1 &= m1; bl1 &= m1;
+                geq[0] = seg_ge(segb[0], 1u);
+                geq[1] = seg_ge(segb[1], 1u);
+                bh0 &= ~geq[0]; bl0 &= ~geq[0]; bh1 &= ~geq[1]; bl1 &= ~geq[1];
             }
             mma_s8u8(shs, ones, bh0, bh1);
             mma_s8u8(sls, ones, bl0, bl1);
@@ -865,8 +870,8 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, int kd, int8_t *
             }
         }
         for (int pass = 1; pass <= maxrec; pass++)
-            record_pass<MODE>(pass, t, rem, rec_e, lut4k, c8, s_state, shs, sls, hiacc, loacc, segw, phi, plo, va,
-                              ones);
+            record_pass<MODE>(pass, t, rem, rec_e, lut4k, c8, s_state, shs, sls, hiacc, loacc, segb, geq, phi, plo,
+                              va, ones);
     }
 
     // output of heads 2t, 2t+1 (attention.rs:279-284)
