@@ -992,13 +992,21 @@ bool copy_out(czg_ctx *c, void *dst, const void *src, size_t n, cudaStream_t s) 
     if (cudaStreamSynchronize(s) != cudaSuccess) return false;
     const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
     const size_t nt = std::min<size_t>(std::min(8u, hw), n >> 22);   // >= 4 MB per thread
-    const size_t per = (n / nt + 63) & ~(size_t)63;
+    const size_t per = ((n + nt - 1) / nt + 63) & ~(size_t)63;   // slices of 64-byte multiples covering n
     std::vector<std::thread> pool;
+    size_t done = std::min(n, per);   // [0, done) is this thread's; a slice no thread took is copied here too
     for (size_t i = 1; i < nt; i++) {
         const size_t a = std::min(n, i * per), b = std::min(n, a + per);
-        if (a < b) pool.emplace_back([=] { memcpy((uint8_t *)dst + a, c->h_out + a, b - a); });
+        if (a >= b) break;
+        try {
+            pool.emplace_back([=] { memcpy((uint8_t *)dst + a, c->h_out + a, b - a); });
+        } catch (...) {   // no thread to be had: the rest in this one
+            break;
+        }
+        done = b;
     }
     memcpy(dst, c->h_out, std::min(n, per));
+    if (done < n) memcpy((uint8_t *)dst + done, c->h_out + done, n - done);
     for (auto &t : pool) t.join();
     return true;
 }
