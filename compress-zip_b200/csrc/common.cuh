@@ -254,6 +254,21 @@ __device__ __forceinline__ int div_rne_s32_by(int num, RneDiv v) {
     return (int)(neg ? 0u - q : q);
 }
 
+// clamp127(rne(x / d)) for d >= 1 (d < 2^32), with rcp = the correctly rounded float
+// of 1 / float(d): the float product of float(x) and rcp is within a relative 2^-22 of
+// x / d, so within 2^-15 wherever the quotient is below 128 in magnitude (beyond it
+// the clamp decides).  Unless it lies within 2^-14 of a half, its nearest integer is
+// then the nearest integer of x / d (ties cannot be that close to a non-tie: they are
+// 1 / (2d) >= 2^-33 apart); the rest take the exact integer division.
+__device__ __forceinline__ int div_rne_clamp127(int x, uint32_t d, float rcp) {
+    const float qf = __fmul_rn(__int2float_rn(x), rcp);
+    const float kf = rintf(qf);
+    int q;
+    if (fabsf(__fsub_rn(qf, kf)) <= 0.5f - 1.0f / 16384.0f) q = __float2int_rn(kf);
+    else q = div_rne_s32_by(x, make_rne_div(d));
+    return clamp127(q);
+}
+
 // floor(a / d) for a < 2^62 and d > 0 given inv = floor((2^64 - 1) / d):
 // the estimate umulhi(a, inv) is at most one below the quotient.
 __device__ __forceinline__ unsigned long long udiv_by_inv(unsigned long long a,
