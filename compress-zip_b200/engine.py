@@ -172,15 +172,16 @@ class Engine:
     def decompress_chunks(self, chunks: list[bytes], n_tokens) -> np.ndarray:
         n = len(chunks)
         nt = np.ascontiguousarray(n_tokens, dtype=np.uint32)
+        total = int(nt.sum(dtype=np.uint64))
         # every token of every chunk is written by the call (no zero fill needed)
-        out = np.empty(max(int(nt.sum()), 1), dtype=np.uint32)
+        out = np.empty(max(total, 1), dtype=np.uint32)
         if n == 0:
             return out[:0]
         data = np.frombuffer(b"".join(chunks) or b"\0", dtype=np.uint8)   # read only
         starts = np.zeros(n + 1, dtype=np.uint64)
-        starts[1:] = np.cumsum([len(c) for c in chunks])
+        np.cumsum(np.fromiter(map(len, chunks), dtype=np.uint64, count=n), out=starts[1:])
         self._check(lib().czg_decompress_chunks(self._h, _p(data), _p(starts), _p(nt), n, _p(out)))
-        return out[: int(nt.sum())]
+        return out[:total]
 
     def set_stream(self, stream_handle: int | None) -> None:
         """Run subsequent work on a caller's cudaStream_t (None: the own stream)."""
