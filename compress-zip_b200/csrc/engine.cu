@@ -1035,10 +1035,19 @@ int decompress_impl(czg_ctx *c, const uint8_t *data, const uint64_t *data_starts
     stats_begin(c);
     c->stats.n_tokens = total_tok;
     c->stats.n_chunks = n_chunks;
-    // stream order: longest first (stable)
+    // stream order: longest first, stable (a counting sort: lengths are at most the context)
     std::vector<uint32_t> order(n_chunks);
-    for (uint32_t i = 0; i < n_chunks; i++) order[i] = i;
-    std::stable_sort(order.begin(), order.end(), [&](uint32_t a, uint32_t b) { return n_tokens[a] > n_tokens[b]; });
+    {
+        std::vector<uint32_t> at((size_t)max_len + 2, 0);   // at[l]: first slot of length l
+        for (uint32_t i = 0; i < n_chunks; i++) at[n_tokens[i]]++;
+        uint32_t pos = 0;
+        for (int l = max_len; l >= 0; l--) {
+            const uint32_t k = at[l];
+            at[l] = pos;
+            pos += k;
+        }
+        for (uint32_t i = 0; i < n_chunks; i++) order[at[n_tokens[i]]++] = i;
+    }
     std::vector<uint64_t> tok_base(n_chunks + 1, 0);
     for (uint32_t i = 0; i < n_chunks; i++) tok_base[i + 1] = tok_base[i] + n_tokens[i];
     // streams per wave: the activation rows and a KV-cache budget
