@@ -582,8 +582,9 @@ def decode_bench(eng, mf, rank, args, stream, world, parity):
     """decompression of 4,096 independent streams, each
     the chunks of a 4 KB document at L4 (ctx 512), seeds 2000.. (rank r: +r*4096).
     The chunks are produced by the engine itself (untimed); the timed region is
-    czg_decompress_chunks from host bytes to host tokens (H2D/D2H inside), CUDA
-    events on the engine's stream; the tokens must equal the originals.  Rank 0
+    czg_decompress_chunks from host bytes to host tokens (H2D/D2H inside) into one
+    reused host buffer, CUDA events on the engine's stream; the tokens must equal
+    the originals.  Rank 0
     then encodes the first and last 32 documents with the CPU oracle: its bytes
     must equal the GPU's, and the GPU must decode the oracle's streams back to the
     tokens (parity["config3"])."""
@@ -600,14 +601,19 @@ def decode_bench(eng, mf, rank, args, stream, world, parity):
     # the timed runs go without per-kernel events (thousands of small launches: the
     # events would cost ~15%); one more run with them gives the kernel split
     eng.set_kernel_timing(False)
-    got = eng.decompress_chunks(chunks, counts)   # warm-up
+    # the decoded tokens land in one host buffer reused by every run (as a streaming
+    # caller would); it is overwritten with 0xFFFFFFFF before each run, untimed, so a
+    # token a run fails to write cannot pass the check
+    dec_out = np.empty(max(len(tokens), 1), dtype=np.uint32)
+    got = eng.decompress_chunks(chunks, counts, out=dec_out)   # warm-up
     exact = bool(np.array_equal(got, tokens))
     steps = max(1, min(args.steps, 3))
     times, launches = [], 0
     for _ in range(steps):
+        dec_out.fill(0xFFFFFFFF)
         torch.cuda.synchronize()
         ev0.record(stream)
-        got = eng.decompress_chunks(chunks, counts)
+        got = eng.decompress_chunks(chunks, counts, out=dec_out)
         ev1.record(stream)
         torch.cuda.synchronize()
         times.append(ev0.elapsed_time(ev1))

@@ -169,12 +169,18 @@ class Engine:
         return need.value
 
     # ---- decompress ----------------------------------------------------------
-    def decompress_chunks(self, chunks: list[bytes], n_tokens) -> np.ndarray:
+    def decompress_chunks(self, chunks: list[bytes], n_tokens, out: np.ndarray | None = None) -> np.ndarray:
+        """Tokens of every chunk, chunk after chunk.  ``out`` (optional): a contiguous
+        uint32 buffer of at least sum(n_tokens) entries to decode into, reused across
+        calls (a fresh buffer's pages are first touched by the copy); the result is a
+        view of it."""
         n = len(chunks)
         nt = np.ascontiguousarray(n_tokens, dtype=np.uint32)
         total = int(nt.sum(dtype=np.uint64))
-        # every token of every chunk is written by the call (no zero fill needed)
-        out = np.empty(max(total, 1), dtype=np.uint32)
+        if out is None:   # every token of every chunk is written by the call (no zero fill needed)
+            out = np.empty(max(total, 1), dtype=np.uint32)
+        elif out.dtype != np.uint32 or not out.flags["C_CONTIGUOUS"] or out.ndim != 1 or len(out) < max(total, 1):
+            raise ValueError("out must be a contiguous 1-D uint32 array of at least sum(n_tokens) entries")
         if n == 0:
             return out[:0]
         data = np.frombuffer(b"".join(chunks) or b"\0", dtype=np.uint8)   # read only

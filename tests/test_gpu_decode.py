@@ -46,6 +46,24 @@ def test_decode_oracle_streams(eng, shipped_oracle, oracle_mod, doc_tokens, C):
     assert np.array_equal(got, tokens)
 
 
+def test_decode_into_caller_buffer(eng, shipped_oracle, oracle_mod, doc_tokens):
+    """decompress_chunks(out=...): the tokens land in the caller's buffer (reused
+    across calls, entries past the result untouched), and a buffer of the wrong
+    type or size is refused before any device work."""
+    tokens, starts = _chunked(doc_tokens, 256)
+    chunks = oracle_mod.compress_chunks(shipped_oracle, tokens, starts)
+    buf = np.full(len(tokens) + 5, 0xFFFFFFFF, dtype=np.uint32)
+    for _ in range(2):
+        got = eng.decompress_chunks(chunks, np.diff(starts), out=buf)
+        assert np.shares_memory(got, buf) and np.array_equal(got, tokens)
+        assert (buf[len(tokens):] == 0xFFFFFFFF).all()
+        buf[: len(tokens)] = 0xFFFFFFFF
+    with pytest.raises(ValueError):
+        eng.decompress_chunks(chunks, np.diff(starts), out=np.empty(len(tokens) - 1, np.uint32))
+    with pytest.raises(ValueError):
+        eng.decompress_chunks(chunks, np.diff(starts), out=np.empty(len(tokens), np.int64))
+
+
 def test_gpu_roundtrip_ragged(eng, doc_tokens):
     tokens, starts = _chunked(doc_tokens, 512)
     # an empty chunk and one-token chunks in the middle
