@@ -679,9 +679,12 @@ k_attention_mma(const int8_t *__restrict__ qkv, int ldq, const int8_t *__restric
 // Persistent: one CTA per SM, warp w takes streams w, w + W, w + 2W, ... (W the
 // warps of the grid).  A warp's tiles, stream after stream, flow through a ring of
 // DEC_STAGES 4 KB shared-memory stages with DEC_STAGES - 1 tile copies in flight,
-// so the first tiles of the next stream load while the current one finishes.
+// so the first tiles of the next stream load while the current one finishes; the
+// stream's qkv row (its queries and the step's key and value) rides in the copy
+// group of its first tile, and the position's RoPE values sit in shared memory.
 constexpr int DEC_STAGES = 2;
-constexpr int DEC_SMEM = AM_WARPS * DEC_STAGES * 4096 + AM_LUT * 2;
+constexpr int DEC_ROW = 640;   // a stream's qkv row (d + 128 bytes, d <= 512 with at most 8 heads)
+constexpr int DEC_SMEM = AM_WARPS * DEC_STAGES * 4096 + AM_LUT * 2 + 128 + AM_WARPS * DEC_ROW;
 
 template <int MODE, bool EXP0>
 __global__ void __launch_bounds__(AM_THREADS, 1)
@@ -696,6 +699,9 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, int kd, int8_t *
     const int g = lane >> 2, t = lane & 3;
     uint16_t *lut_s = reinterpret_cast<uint16_t *>(dsm + AM_WARPS * DEC_STAGES * 4096);
     for (int i = tid; i < AM_LUT; i += AM_THREADS) lut_s[i] = lut4k_g[i];   // model constant
+    // the RoPE values of position p (model constants): cos at [0, 32), sin at [32, 64)
+    int16_t *rope_s = reinterpret_cast<int16_t *>(lut_s + AM_LUT);
+    if (tid < 2 * kHalfDim) rope_s[tid] = tid < kHalfDim ? rope_cos[p * kHalfDim + tid] : rope_sin[p * kHalfDim + tid - kHalfDim];
     pdl_wait();
     pdl_trigger();
     __syncthreads();
@@ -704,6 +710,9 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, int kd, int8_t *
     int r = blockIdx.x * AM_WARPS + warp;
     if (r >= M) return;
     uint8_t *stages = dsm + warp * (DEC_STAGES * 4096);
+    // this warp's copy of its current stream's qkv row, loaded with the stream's first tile
+    uint8_t *qrow = reinterpret_cast<uint8_t *>(rope_s + 2 * kHalfDim) + warp * DEC_ROW;
+    const int row_chunks = ldq >> 4;   // ldq = d + 128 <= DEC_ROW, a multiple of 16
     uint32_t *rec_e = reinterpret_cast<uint32_t *>(wsm + warp * AM_WARP_SMEM);   // [8][32]
     uint8_t *ostage = reinterpret_cast<uint8_t *>(rec_e + AM_ROWS * 32);         // [8][64]
     const size_t len = cache_ld / 128;
@@ -721,6 +730,8 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, int kd, int8_t *
     auto fetch = [&]() {
         if (fr < M) {
             const int8_t *k0 = kvc + (size_t)fr * cache_ld;   // [len][64] K rows, then the V tiles
+            if (fk == 0)   // the stream's qkv row joins its first tile's copy group
+                for (int c = lane; c < row_chunks; c += 32) cp_async16(qrow + 16 * c, qkv + (size_t)fr * ldq + 16 * c);
             decode_tile_async(stages + fslot * 4096, k0, k0 + len * 64, 32 * fk, lane);
             if (++fk == ntiles) { fk = 0; fr += stride; }
         } else {
@@ -733,12 +744,15 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, int kd, int8_t *
 
     for (; r < M; r += stride) {
 
+    // this stream's qkv row (and first tile) have landed: the only copy group in flight
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncwarp();
     // Q fragment of head g at position p with RoPE (attention.rs:53-83)
     uint32_t qa[2][4];
     {
         uint32_t raw[4] = {0, 0, 0, 0};
         if (head) {
-            const int8_t *qr = qkv + (size_t)r * ldq + g * 64;
+            const uint8_t *qr = qrow + g * 64;
 #pragma unroll
             for (int k = 0; k < 4; k++) raw[k] = *reinterpret_cast<const uint32_t *>(qr + 16 * k + 4 * t);
         }
@@ -749,7 +763,7 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, int kd, int8_t *
             for (int b = 0; b < 4; b++) {
                 const int i = 16 * k + 4 * t + b;
                 int x = sext8(raw[k], b), y = sext8(raw[k + 2], b);
-                const int cs = rope_cos[p * kHalfDim + i], sn = rope_sin[p * kHalfDim + i];
+                const int cs = rope_s[i], sn = rope_s[kHalfDim + i];
                 int xr = rope_q_round(x * cs - y * sn);
                 int yr = rope_q_round(x * sn + y * cs);
                 lo[k] |= (uint32_t)(uint8_t)xr << (8 * b);
@@ -765,9 +779,9 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, int kd, int8_t *
     // key and dims 2l, 2l + 1 of the value, written to the cache now and kept (one word
     // per lane, in the output staging area, free until the output) for the last tile
     {
-        const int8_t *kq = qkv + (size_t)r * ldq + kd;
+        const int8_t *kq = reinterpret_cast<const int8_t *>(qrow) + kd;
         const int x = kq[lane], y = kq[lane + kHalfDim];
-        const int cs = rope_cos[p * kHalfDim + lane], sn = rope_sin[p * kHalfDim + lane];
+        const int cs = rope_s[lane], sn = rope_s[kHalfDim + lane];
         const int kx = rope_k_round(x * cs - y * sn);
         const int ky = rope_k_round(x * sn + y * cs);
         const uint32_t v2 = *reinterpret_cast<const uint16_t *>(kq + 64 + 2 * lane);
@@ -780,6 +794,7 @@ k_attention_decode_mma(const int8_t *__restrict__ qkv, int ldq, int kd, int8_t *
         vt[vt_byte(p & 31, 2 * lane)] = (int8_t)(v2 & 0xFFu);
         vt[vt_byte(p & 31, 2 * lane + 1)] = (int8_t)(v2 >> 8);
     }
+    __syncwarp();   // every lane has read the row: the next stream's copy may overwrite it
     int m = INT32_MIN;
     uint32_t s_state[2] = {0u, 0u};   // exact in 32 bits (record_pass)
     if (sink_key != nullptr) {   // attention.rs:211-224
