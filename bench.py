@@ -658,6 +658,11 @@ def _corpus_docs(bounds):
     return synth.documents(range(lo, hi), 65536)
 
 
+def corpus_range(rank, world, n_docs):
+    """Rank `rank`'s contiguous share [lo, hi) of n_docs documents (strong scaling)."""
+    return rank * n_docs // world, (rank + 1) * n_docs // world
+
+
 def corpus_documents(lo, hi, workers):
     """synth.documents over seeds [lo, hi), split over a pool of spawned processes
     (untimed setup: a 1 GB corpus takes minutes in one process)."""
@@ -684,7 +689,7 @@ def corpus_bench(args, mf, rank, world, local):
     from compress_zip_b200.engine import Engine
 
     n_docs = args.corpus_mb * (1 << 20) // 65536
-    lo, hi = rank * n_docs // world, (rank + 1) * n_docs // world
+    lo, hi = corpus_range(rank, world, n_docs)
     model = synth.arch2_model(mf, 4096)
     tok = mf.tokenizer()
     docs = corpus_documents(10000 + lo, 10000 + hi, max(1, min(16, (os.cpu_count() or 1) // world)))
