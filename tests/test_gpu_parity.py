@@ -318,7 +318,9 @@ def test_kv_prep_kernel_path(shipped_path, shipped_oracle, oracle_mod, shipped_t
 @pytest.mark.parametrize("mode", ["ties", "flat", "extreme"])
 def test_cdf_edge_models(shipped_path, tmp_path, oracle_mod, shipped_tokens, mode):
     """CDF corner cases through real logits: tied maxima (first index wins),
-    a flat row (every weight 65535), and logits far apart (most weights 1)."""
+    a flat row (every weight 65535), and logits far apart (most weights 1); the
+    GPU decoder (its own max and first-argmax search) decodes the oracle's bytes
+    back to the tokens."""
     from compress_zip_b200 import czm
     from compress_zip_b200.engine import Engine
 
@@ -340,7 +342,9 @@ def test_cdf_edge_models(shipped_path, tmp_path, oracle_mod, shipped_tokens, mod
         _trace_equal(eng, om, oracle_mod, shipped_tokens[:400])
         toks = shipped_tokens[:1500]
         starts = _starts(len(toks), 512)
-        assert eng.compress_chunks(toks, starts) == oracle_mod.compress_chunks(om, toks, starts)
+        want = oracle_mod.compress_chunks(om, toks, starts)
+        assert eng.compress_chunks(toks, starts) == want
+        assert np.array_equal(eng.decompress_chunks(want, np.diff(starts).astype(np.uint32)), toks)
     finally:
         eng.close()
 
