@@ -969,45 +969,59 @@ int dec_reserve(czg_ctx *c, size_t streams, size_t len, size_t bytes, size_t tok
     return CZG_OK;
 }
 
-// Device memory to a caller's (pageable) host buffer: one DMA into pinned staging at
-// full PCIe / C2C speed, then host threads copy it on (a direct copy to pageable
-// memory goes through the driver's staging at a few GB/s).  Small copies, or no
-// pinned memory to be had, take the direct copy.  Returns false on a CUDA error.
-bool copy_out(czg_ctx *c, void *dst, const void *src, size_t n, cudaStream_t s) {
-    if (n == 0) return true;
-    if (n >= ((size_t)1 << 22) && n > c->h_out_bytes) {
-        if (c->h_out) {
-            cudaFreeHost(c->h_out);
-            c->h_out = nullptr;
-            c->h_out_bytes = 0;
-        }
-        if (cudaMallocHost(&c->h_out, n) == cudaSuccess) c->h_out_bytes = n;
-        else { c->h_out = nullptr; cudaGetLastError(); }
-    }
-    if (n < ((size_t)1 << 22) || n > c->h_out_bytes) {
-        cudaMemcpyAsync(dst, src, n, cudaMemcpyDeviceToHost, s);
-        return cudaStreamSynchronize(s) == cudaSuccess;
-    }
-    cudaMemcpyAsync(c->h_out, src, n, cudaMemcpyDeviceToHost, s);
-    if (cudaStreamSynchronize(s) != cudaSuccess) return false;
+// n bytes of host memory copied by up to eight threads (the calling one included);
+// a thread that cannot be started leaves its slices to the calling thread
+void parallel_memcpy(uint8_t *dst, const uint8_t *src, size_t n) {
     const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
-    const size_t nt = std::min<size_t>(std::min(8u, hw), n >> 22);   // >= 4 MB per thread
+    const size_t nt = std::max<size_t>(1, std::min<size_t>(std::min(8u, hw), n >> 22));   // >= 4 MB per thread
     const size_t per = ((n + nt - 1) / nt + 63) & ~(size_t)63;   // slices of 64-byte multiples covering n
     std::vector<std::thread> pool;
-    size_t done = std::min(n, per);   // [0, done) is this thread's; a slice no thread took is copied here too
+    size_t done = std::min(n, per);   // [0, done) is this thread's or a started thread's
     for (size_t i = 1; i < nt; i++) {
         const size_t a = std::min(n, i * per), b = std::min(n, a + per);
         if (a >= b) break;
         try {
-            pool.emplace_back([=] { memcpy((uint8_t *)dst + a, c->h_out + a, b - a); });
+            pool.emplace_back([=] { memcpy(dst + a, src + a, b - a); });
         } catch (...) {   // no thread to be had: the rest in this one
             break;
         }
         done = b;
     }
-    memcpy(dst, c->h_out, std::min(n, per));
-    if (done < n) memcpy((uint8_t *)dst + done, c->h_out + done, n - done);
+    memcpy(dst, src, std::min(n, per));
+    if (done < n) memcpy(dst + done, src + done, n - done);
     for (auto &t : pool) t.join();
+}
+
+// Device memory to a caller's (pageable) host buffer: DMAs into pinned staging at
+// full PCIe / C2C speed, then host threads copy it on (a direct copy to pageable
+// memory goes through the driver's staging at a few GB/s).  The staging buffer is
+// at most CZG_COPY_STAGING_BYTES (default 256 MB; larger results go through it in
+// pieces).  Small copies, or no pinned memory to be had, take the direct copy.
+// Returns false on a CUDA error.
+bool copy_out(czg_ctx *c, void *dst, const void *src, size_t n, cudaStream_t s) {
+    if (n == 0) return true;
+    size_t cap = (size_t)256 << 20;
+    if (const char *ev = getenv("CZG_COPY_STAGING_BYTES")) cap = std::max<size_t>((size_t)1 << 22, strtoull(ev, nullptr, 10));
+    const size_t want = std::min(n, cap);
+    if (n >= ((size_t)1 << 22) && want > c->h_out_bytes) {
+        if (c->h_out) {
+            cudaFreeHost(c->h_out);
+            c->h_out = nullptr;
+            c->h_out_bytes = 0;
+        }
+        if (cudaMallocHost(&c->h_out, want) == cudaSuccess) c->h_out_bytes = want;
+        else { c->h_out = nullptr; cudaGetLastError(); }
+    }
+    if (n < ((size_t)1 << 22) || c->h_out_bytes == 0) {
+        cudaMemcpyAsync(dst, src, n, cudaMemcpyDeviceToHost, s);
+        return cudaStreamSynchronize(s) == cudaSuccess;
+    }
+    for (size_t off = 0; off < n; off += c->h_out_bytes) {
+        const size_t len = std::min(c->h_out_bytes, n - off);
+        cudaMemcpyAsync(c->h_out, (const uint8_t *)src + off, len, cudaMemcpyDeviceToHost, s);
+        if (cudaStreamSynchronize(s) != cudaSuccess) return false;
+        parallel_memcpy((uint8_t *)dst + off, c->h_out, len);
+    }
     return true;
 }
 

@@ -104,7 +104,8 @@ int czg_compress_chunks_device(czg_ctx *ctx, const uint32_t *d_tokens,
  * rust/src/arith_coder.rs:176-190).  Tokens of chunk i land at
  * out_tokens + sum(n_tokens[0..i)).  Results of 4 MB and more leave the device
  * through a page-locked staging buffer that the context keeps (grown to the
- * largest such result, freed by czg_ctx_destroy) and host threads copy on. */
+ * largest such result up to CZG_COPY_STAGING_BYTES, default 256 MB, larger ones in
+ * pieces; freed by czg_ctx_destroy) and host threads copy on. */
 int czg_decompress_chunks(czg_ctx *ctx, const uint8_t *data, const uint64_t *data_starts,
                           const uint32_t *n_tokens, uint32_t n_chunks, uint32_t *out_tokens);
 
